@@ -1,0 +1,126 @@
+"""Autograd contract of the rasterizer (mirrors
+gswarp/_internal/frontend/standard_autograd.py:36-188).
+
+Forward returns (color, radii, depth, alpha, proj_2D, conic_2D,
+conic_2D_inv); backward returns gradients for means3D, means2D, sh,
+colors_precomp, opacities, scales, rotations and cov3Ds_precomp.  Forward
+state (render records, pair list, tile ranges, n_contrib) is kept with
+``save_for_backward``, so a retained graph replays its own binning state and
+the buffers are released with the graph.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _pipeline as pl
+from ._runtime import ExecutionOptions, execution_options, resolve_execution_options
+
+NUM_CHANNELS = 3
+
+
+def _camera(rs) -> pl.Camera:
+    return pl.Camera(
+        W=int(rs.image_width), H=int(rs.image_height), tanfovx=float(rs.tanfovx), tanfovy=float(rs.tanfovy),
+        viewmatrix=pl._f32(rs.viewmatrix), projmatrix=pl._f32(rs.projmatrix), campos=pl._f32(rs.campos),
+    )
+
+
+def run_forward(means3D, sh, colors_precomp, opacities, scales, rotations, cov3Ds_precomp, rs,
+                options: ExecutionOptions):
+    """Typed forward: returns (outputs tuple, Gaussians, Preprocessed, Binned, Rendered, Camera)."""
+    if means3D.ndim != 2 or means3D.shape[1] != 3:
+        raise ValueError("means3D must have dimensions (num_points, 3)")
+    if getattr(rs, "prefiltered", False):
+        raise NotImplementedError("prefiltered=True is not supported in the native preprocess path yet.")
+    cam = _camera(rs)
+    dev = means3D.device
+    bg = pl._f32(rs.bg).reshape(NUM_CHANNELS)
+    g = pl.make_gaussians(means3D, opacities, scales, rotations, cov3Ds_precomp, sh, colors_precomp,
+                          rs.scale_modifier, rs.sh_degree)
+    mode = pl.coverage_mode_id(options)
+    with torch.cuda.device(dev):
+        pre = pl.preprocess(g, cam, mode)
+        binned = pl.binning(pre, cam, mode)
+        ren = pl.render(pre, binned, cam, bg, options.compute_depth)
+    return g, pre, binned, ren, cam, bg
+
+
+class _RasterizeGaussians(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, means3D, means2D, sh, colors_precomp, opacities, scales, rotations, cov3Ds_precomp,
+                raster_settings):
+        options = resolve_execution_options(raster_settings)
+        with execution_options(options):
+            g, pre, binned, ren, cam, bg = run_forward(means3D, sh, colors_precomp, opacities, scales, rotations,
+                                                      cov3Ds_precomp, raster_settings, options)
+        ctx.raster_settings = raster_settings
+        ctx.options = options
+        ctx.num_rendered = binned.num_rendered
+        ctx.save_for_backward(colors_precomp, opacities, means3D, scales, rotations, cov3Ds_precomp, sh,
+                              pre.radii, pre.records, binned.point_list, binned.ranges, ren.n_contrib, ren.alpha)
+        ctx.mark_non_differentiable(pre.radii)
+        return ren.color, pre.radii, ren.depth, ren.alpha, pre.proj_2d, pre.conic_2d, pre.conic_2d_inv
+
+    @staticmethod
+    def backward(ctx, grad_color, grad_radii, grad_depth, grad_alpha, grad_proj_2D, grad_conic_2D,
+                 grad_conic_2D_inv):
+        (colors_precomp, opacities, means3D, scales, rotations, cov3Ds_precomp, sh, radii, records, point_list,
+         ranges, n_contrib, alpha) = ctx.saved_tensors
+        rs = ctx.raster_settings
+        grads = run_backward(rs, ctx.options, ctx.num_rendered, means3D, sh, colors_precomp, opacities, scales,
+                             rotations, cov3Ds_precomp, radii, records, point_list, ranges, n_contrib, alpha,
+                             grad_color, grad_depth, grad_alpha, grad_proj_2D, grad_conic_2D, grad_conic_2D_inv)
+        (g_means2D, g_colors, g_opac, g_means3D, g_cov, g_sh, g_scales, g_rot) = grads
+        return g_means3D, g_means2D, g_sh, g_colors, g_opac, g_scales, g_rot, g_cov, None
+
+
+def _grad_or_zeros(t, shape, dev):
+    if t is None:
+        return torch.zeros(shape, dtype=torch.float32, device=dev)
+    return pl._f32(t)
+
+
+def run_backward(rs, options, num_rendered, means3D, sh, colors_precomp, opacities, scales, rotations,
+                 cov3Ds_precomp, radii, records, point_list, ranges, n_contrib, alpha, grad_color, grad_depth,
+                 grad_alpha, grad_proj_2D, grad_conic_2D, grad_conic_2D_inv):
+    """Returns the reference's 8-tuple (backward_ops.py:746): grad_means2D,
+    grad_colors, grad_opacities, grad_means3D, grad_cov3D, grad_sh,
+    grad_scales, grad_rotations."""
+    P = means3D.shape[0]
+    dev = means3D.device
+    cam = _camera(rs)
+    H, W = cam.H, cam.W
+    if P == 0:
+        return (torch.zeros((0, 3), dtype=torch.float32, device=dev), torch.empty_like(colors_precomp),
+                torch.empty_like(opacities), torch.zeros_like(means3D), torch.empty_like(cov3Ds_precomp),
+                torch.empty_like(sh), torch.zeros_like(scales), torch.zeros_like(rotations))
+    bg = pl._f32(rs.bg).reshape(NUM_CHANNELS)
+    g = pl.make_gaussians(means3D, opacities, scales, rotations, cov3Ds_precomp, sh, colors_precomp,
+                          rs.scale_modifier, rs.sh_degree)
+    gc = _grad_or_zeros(grad_color, (NUM_CHANNELS, H, W), dev)
+    gd = _grad_or_zeros(grad_depth, (1, H, W), dev)
+    ga = _grad_or_zeros(grad_alpha, (1, H, W), dev)
+    gp = _grad_or_zeros(grad_proj_2D, (P, 2), dev)
+    gk = _grad_or_zeros(grad_conic_2D, (P, 3), dev)
+    gki = _grad_or_zeros(grad_conic_2D_inv, (P, 3), dev)
+    binned = pl.Binned(int(num_rendered), point_list, ranges)
+    with torch.cuda.device(dev):
+        grad_acc = pl.render_backward(records, binned, cam, bg, pl._f32(alpha), n_contrib, gc, gd, ga,
+                                      options.compute_depth, P)
+        pg = pl.preprocess_backward(g, cam, radii, records, grad_acc, gp, gk, gki)
+    grad_colors = pg.grad_colors if g.colors is not None else torch.empty_like(colors_precomp)
+    grad_opac = pg.grad_opacity.reshape(opacities.shape)
+    grad_cov = pg.grad_cov3D if g.cov3D is not None else torch.empty_like(cov3Ds_precomp)
+    grad_sh = pg.grad_sh.reshape(sh.shape) if g.sh is not None else torch.empty_like(sh)
+    if g.cov3D is None:
+        grad_scales, grad_rot = pg.grad_scales, pg.grad_rotations
+    else:
+        grad_scales, grad_rot = torch.zeros_like(scales), torch.zeros_like(rotations)
+    return pg.grad_means2D, grad_colors, grad_opac, pg.grad_means3D, grad_cov, grad_sh, grad_scales, grad_rot
+
+
+def rasterize_gaussians(means3D, means2D, sh, colors_precomp, opacities, scales, rotations, cov3Ds_precomp,
+                        raster_settings):
+    return _RasterizeGaussians.apply(means3D, means2D, sh, colors_precomp, opacities, scales, rotations,
+                                     cov3Ds_precomp, raster_settings)

@@ -1,0 +1,413 @@
+"""Host side of the rasterizer: stage order, buffer allocation, C-ABI calls.
+
+Mirrors the stage pipeline of gswarp (methods/pipeline.py:11-45 ->
+preprocess_ops.py:289-581, binning_ops.py:84-431, render_ops.py:16-93,
+backward_ops.py:376-746).  Every buffer, workspaces included, comes from the
+torch caching allocator on the caller's current stream; the native library
+owns no memory.  The forward performs exactly one host synchronization: the
+pair count read after the depth-ordered scan, as the reference does
+(binning_ops.py:243-252).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from ._coverage import BASELINE_3DGS_COVERAGE, resolve_tile_coverage_mode_id
+from ._runtime import BLOCK_X, BLOCK_Y, ExecutionOptions
+
+NUM_CHANNELS = 3
+MAX_BINNING_PAIRS = (1 << 31) - 1
+
+_STICKY: dict[int, torch.Tensor] = {}
+
+# Optional CUDA-event timing of the native stages (used by bench.py): when
+# enabled, every stage call records (start, end, info) on the current stream.
+TIMING_ENABLED = False
+TIMERS: dict[str, list] = {}
+
+
+class _stage_timer:
+    def __init__(self, name: str, info: dict | None = None):
+        self.name = name
+        self.info = info or {}
+
+    def __enter__(self):
+        if TIMING_ENABLED:
+            self.a = torch.cuda.Event(enable_timing=True)
+            self.b = torch.cuda.Event(enable_timing=True)
+            self.a.record()
+        return self
+
+    def __exit__(self, *exc):
+        if TIMING_ENABLED and exc[0] is None:
+            self.b.record()
+            TIMERS.setdefault(self.name, []).append((self.a, self.b, self.info))
+        return False
+
+
+def sticky_error_word(device: torch.device) -> torch.Tensor:
+    """Per-device int64 word that kernels OR error bits into (checked at the
+    next host synchronization)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    t = _STICKY.get(idx)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int64, device=device)
+        _STICKY[idx] = t
+    return t
+
+
+def _f32(t: torch.Tensor) -> torch.Tensor:
+    t = t.detach()
+    if t.dtype != torch.float32:
+        t = t.float()
+    if not t.is_contiguous():
+        t = t.contiguous()
+    return t
+
+
+def _aligned16(t: torch.Tensor) -> torch.Tensor:
+    return t if t.data_ptr() % 16 == 0 else t.clone()
+
+
+def _workspace(nbytes: int, device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
+
+
+@dataclass(slots=True)
+class Camera:
+    W: int
+    H: int
+    tanfovx: float
+    tanfovy: float
+    viewmatrix: torch.Tensor
+    projmatrix: torch.Tensor
+    campos: torch.Tensor
+
+    @property
+    def focal_x(self) -> float:
+        return self.W / (2.0 * float(self.tanfovx))
+
+    @property
+    def focal_y(self) -> float:
+        return self.H / (2.0 * float(self.tanfovy))
+
+    @property
+    def grid(self) -> tuple[int, int]:
+        return (self.W + BLOCK_X - 1) // BLOCK_X, (self.H + BLOCK_Y - 1) // BLOCK_Y
+
+
+@dataclass(slots=True)
+class Gaussians:
+    means3D: torch.Tensor
+    opacities: torch.Tensor
+    scales: torch.Tensor | None
+    rotations: torch.Tensor | None
+    cov3D: torch.Tensor | None
+    sh: torch.Tensor | None          # (P, K, 3) view of the caller's tensor
+    colors: torch.Tensor | None
+    scale_modifier: float
+    degree: int
+
+    @property
+    def P(self) -> int:
+        return self.means3D.shape[0]
+
+
+@dataclass(slots=True)
+class Preprocessed:
+    radii: torch.Tensor
+    proj_2d: torch.Tensor
+    conic_2d: torch.Tensor
+    conic_2d_inv: torch.Tensor
+    depths: torch.Tensor
+    tiles_touched: torch.Tensor
+    records: torch.Tensor
+
+
+@dataclass(slots=True)
+class Binned:
+    num_rendered: int
+    point_list: torch.Tensor
+    ranges: torch.Tensor
+
+
+@dataclass(slots=True)
+class Rendered:
+    color: torch.Tensor
+    depth: torch.Tensor
+    alpha: torch.Tensor
+    n_contrib: torch.Tensor
+
+
+def make_gaussians(means3D, opacities, scales, rotations, cov3D, sh, colors, scale_modifier, degree) -> Gaussians:
+    P = means3D.shape[0]
+
+    def opt(t, shape):
+        if t is None or t.numel() == 0:
+            return None
+        return _f32(t).reshape(shape)
+
+    sh_t = None
+    if sh is not None and sh.numel() != 0:
+        sh_t = _f32(sh).reshape(P, -1, NUM_CHANNELS)
+    rot = opt(rotations, (P, 4))
+    return Gaussians(
+        means3D=_f32(means3D),
+        opacities=_f32(opacities).reshape(P),
+        scales=opt(scales, (P, 3)),
+        rotations=_aligned16(rot) if rot is not None else None,
+        cov3D=opt(cov3D, (P, 6)),
+        sh=sh_t,
+        colors=opt(colors, (P, NUM_CHANNELS)),
+        scale_modifier=float(scale_modifier),
+        degree=int(degree),
+    )
+
+
+def coverage_mode_id(options: ExecutionOptions | None) -> int:
+    mode = "auto" if options is None else options.tile_coverage_mode
+    return resolve_tile_coverage_mode_id(mode, BASELINE_3DGS_COVERAGE)
+
+
+def preprocess(g: Gaussians, cam: Camera, coverage_mode: int) -> Preprocessed:
+    P = g.P
+    dev = g.means3D.device
+    out = Preprocessed(
+        radii=torch.empty(P, dtype=torch.int32, device=dev),
+        proj_2d=torch.empty((P, 2), dtype=torch.float32, device=dev),
+        conic_2d=torch.empty((P, 3), dtype=torch.float32, device=dev),
+        conic_2d_inv=torch.empty((P, 3), dtype=torch.float32, device=dev),
+        depths=torch.empty(P, dtype=torch.float32, device=dev),
+        tiles_touched=torch.empty(P, dtype=torch.int32, device=dev),
+        records=torch.empty((P, _lib.RECORD_FLOATS), dtype=torch.float32, device=dev),
+    )
+    if P == 0:
+        return out
+    a = _lib.PreprocessArgs()
+    a.P, a.W, a.H = P, cam.W, cam.H
+    a.means = _lib.ptr(g.means3D)
+    a.scales = _lib.ptr(g.scales)
+    a.rotations = _lib.ptr(g.rotations)
+    a.cov3d_precomp = _lib.ptr(g.cov3D)
+    a.scale_modifier = g.scale_modifier
+    a.opacities = _lib.ptr(g.opacities)
+    a.viewmatrix = _lib.ptr(cam.viewmatrix)
+    a.projmatrix = _lib.ptr(cam.projmatrix)
+    a.campos = _lib.ptr(cam.campos)
+    a.tanfovx, a.tanfovy = float(cam.tanfovx), float(cam.tanfovy)
+    a.focal_x, a.focal_y = cam.focal_x, cam.focal_y
+    a.sh = _lib.ptr(g.sh)
+    a.sh_degree = g.degree
+    a.sh_coeffs = g.sh.shape[1] if g.sh is not None else 0
+    a.colors_precomp = _lib.ptr(g.colors)
+    a.coverage_mode = coverage_mode
+    a.radii = _lib.ptr(out.radii)
+    a.proj_2d = _lib.ptr(out.proj_2d)
+    a.conic_2d = _lib.ptr(out.conic_2d)
+    a.conic_2d_inv = _lib.ptr(out.conic_2d_inv)
+    a.depths = _lib.ptr(out.depths)
+    a.tiles_touched = _lib.ptr(out.tiles_touched)
+    a.records = _lib.ptr(out.records)
+    with _stage_timer("preprocess_fwd", {"P": P, "kernels": 1}):
+        _lib.call("gsb_preprocess_fwd", a, _lib.stream_handle(dev))
+    return out
+
+
+def binning(pre: Preprocessed, cam: Camera, coverage_mode: int) -> Binned:
+    P = pre.radii.shape[0]
+    dev = pre.radii.device
+    gx, gy = cam.grid
+    tiles = gx * gy
+    L = _lib.load()
+    stream = _lib.stream_handle(dev)
+    ranges = torch.empty((tiles, 2), dtype=torch.int32, device=dev)
+    if P == 0:
+        ranges.zero_()
+        return Binned(0, torch.empty(0, dtype=torch.int32, device=dev), ranges)
+    depth_order = torch.empty(P, dtype=torch.int32, device=dev)
+    offsets = torch.empty(P, dtype=torch.int32, device=dev)
+    status = torch.empty(2, dtype=torch.int64, device=dev)
+    ws_bytes = int(L.gsb_bin_count_workspace_bytes(P))
+    ws = _workspace(ws_bytes, dev)
+    a = _lib.BinCountArgs()
+    a.P = P
+    a.depths = _lib.ptr(pre.depths)
+    a.radii = _lib.ptr(pre.radii)
+    a.tiles_touched = _lib.ptr(pre.tiles_touched)
+    a.depth_order = _lib.ptr(depth_order)
+    a.point_offsets = _lib.ptr(offsets)
+    a.status_out = _lib.ptr(status)
+    a.workspace = _lib.ptr(ws)
+    a.workspace_bytes = ws_bytes
+    with _stage_timer("bin_count", {"P": P, "kernels": 11}):
+        _lib.call("gsb_bin_count", a, stream)
+    sticky = sticky_error_word(dev)
+    total, err, sticky_bits = torch.cat([status, sticky]).tolist()
+    if err or sticky_bits:
+        sticky.zero_()
+        raise RuntimeError(f"gswarp_b200 device error word {int(err) | int(sticky_bits):#x} (bounded wait timed out or binning mismatch)")
+    if total < 0 or total > MAX_BINNING_PAIRS:
+        raise OverflowError(
+            "binning tile-reference count exceeds signed int32; reduce Gaussian footprint or image size"
+        )
+    R = int(total)
+    point_list = torch.empty(max(R, 1), dtype=torch.int32, device=dev)
+    ws2_bytes = int(L.gsb_bin_sort_workspace_bytes(R, cam.W, cam.H))
+    ws2 = _workspace(ws2_bytes, dev) if R > 0 else _workspace(256, dev)
+    b = _lib.BinSortArgs()
+    b.P, b.W, b.H = P, cam.W, cam.H
+    b.num_rendered = R
+    b.coverage_mode = coverage_mode
+    b.depth_order = _lib.ptr(depth_order)
+    b.point_offsets = _lib.ptr(offsets)
+    b.radii = _lib.ptr(pre.radii)
+    b.records = _lib.ptr(pre.records)
+    b.conic_2d_inv = _lib.ptr(pre.conic_2d_inv)
+    b.tiles_touched = _lib.ptr(pre.tiles_touched)
+    b.point_list = _lib.ptr(point_list)
+    b.ranges = _lib.ptr(ranges)
+    b.error_word = _lib.ptr(sticky)
+    b.workspace = _lib.ptr(ws2)
+    b.workspace_bytes = ws2.numel()
+    with _stage_timer("bin_emit_sort", {"P": P, "num_rendered": R, "kernels": 7}):
+        _lib.call("gsb_bin_emit_sort", b, stream)
+    return Binned(R, point_list[:R], ranges)
+
+
+def render(pre: Preprocessed, binned: Binned, cam: Camera, background: torch.Tensor, compute_depth: bool) -> Rendered:
+    dev = pre.records.device
+    H, W = cam.H, cam.W
+    out = Rendered(
+        color=torch.empty((NUM_CHANNELS, H, W), dtype=torch.float32, device=dev),
+        depth=torch.empty((1, H, W), dtype=torch.float32, device=dev),
+        alpha=torch.empty((1, H, W), dtype=torch.float32, device=dev),
+        n_contrib=torch.empty(H * W, dtype=torch.int32, device=dev),
+    )
+    a = _lib.RenderFwdArgs()
+    a.W, a.H = W, H
+    a.compute_depth = int(bool(compute_depth))
+    a.ranges = _lib.ptr(binned.ranges)
+    a.point_list = _lib.ptr(binned.point_list) if binned.num_rendered > 0 else None
+    a.records = _lib.ptr(pre.records) if pre.records.numel() else _lib.ptr(torch.zeros(16, device=dev))
+    a.background = _lib.ptr(background)
+    a.out_color = _lib.ptr(out.color)
+    a.out_depth = _lib.ptr(out.depth)
+    a.out_alpha = _lib.ptr(out.alpha)
+    a.n_contrib = _lib.ptr(out.n_contrib)
+    info = {"num_rendered": binned.num_rendered, "P": pre.records.shape[0], "kernels": 1}
+    with _stage_timer("render_fwd", info):
+        _lib.call("gsb_render_fwd", a, _lib.stream_handle(dev))
+    if TIMING_ENABLED:
+        info["pairs"] = int(out.n_contrib.sum(dtype=torch.int64))
+    return out
+
+
+def render_backward(pre_records, binned: Binned, cam: Camera, background, out_alpha, n_contrib,
+                    grad_color, grad_depth, grad_alpha, compute_depth: bool, P: int) -> torch.Tensor:
+    dev = pre_records.device
+    grad_acc = torch.zeros((P, _lib.GRAD_FLOATS), dtype=torch.float32, device=dev)
+    if binned.num_rendered == 0 or P == 0:
+        return grad_acc
+    a = _lib.RenderBwdArgs()
+    a.W, a.H, a.P = cam.W, cam.H, P
+    a.compute_depth = int(bool(compute_depth))
+    a.ranges = _lib.ptr(binned.ranges)
+    a.point_list = _lib.ptr(binned.point_list)
+    a.records = _lib.ptr(pre_records)
+    a.background = _lib.ptr(background)
+    a.out_alpha = _lib.ptr(out_alpha)
+    a.n_contrib = _lib.ptr(n_contrib)
+    a.grad_color = _lib.ptr(grad_color)
+    a.grad_depth = _lib.ptr(grad_depth)
+    a.grad_alpha = _lib.ptr(grad_alpha)
+    a.grad_acc = _lib.ptr(grad_acc)
+    info = {"num_rendered": binned.num_rendered, "P": P, "kernels": 1}
+    with _stage_timer("render_bwd", info):
+        _lib.call("gsb_render_bwd", a, _lib.stream_handle(dev))
+    if TIMING_ENABLED:
+        info["pairs"] = int(n_contrib.sum(dtype=torch.int64))
+    return grad_acc
+
+
+@dataclass(slots=True)
+class PreprocessGrads:
+    grad_means3D: torch.Tensor
+    grad_means2D: torch.Tensor
+    grad_opacity: torch.Tensor
+    grad_scales: torch.Tensor | None
+    grad_rotations: torch.Tensor | None
+    grad_cov3D: torch.Tensor | None
+    grad_sh: torch.Tensor | None
+    grad_colors: torch.Tensor | None
+
+
+def preprocess_backward(g: Gaussians, cam: Camera, radii, records, grad_acc, grad_proj_2d, grad_conic_2d,
+                        grad_conic_2d_inv, out: PreprocessGrads | None = None) -> PreprocessGrads:
+    """Per-Gaussian backward.  With ``out`` given, gradients are added into
+    its buffers (multi-view accumulation); otherwise fresh tensors are made."""
+    P = g.P
+    dev = g.means3D.device
+    acc = out is not None
+    if out is None:
+        out = PreprocessGrads(
+            grad_means3D=torch.empty((P, 3), dtype=torch.float32, device=dev),
+            grad_means2D=torch.empty((P, 3), dtype=torch.float32, device=dev),
+            grad_opacity=torch.empty(P, dtype=torch.float32, device=dev),
+            grad_scales=torch.empty((P, 3), dtype=torch.float32, device=dev) if g.cov3D is None else None,
+            grad_rotations=torch.empty((P, 4), dtype=torch.float32, device=dev) if g.cov3D is None else None,
+            grad_cov3D=torch.empty((P, 6), dtype=torch.float32, device=dev) if g.cov3D is not None else None,
+            grad_sh=torch.empty(g.sh.shape, dtype=torch.float32, device=dev) if g.sh is not None else None,
+            grad_colors=torch.empty((P, 3), dtype=torch.float32, device=dev) if g.sh is None else None,
+        )
+    if P == 0:
+        return out
+    a = _lib.PreprocessBwdArgs()
+    a.P, a.W, a.H = P, cam.W, cam.H
+    a.means = _lib.ptr(g.means3D)
+    a.radii = _lib.ptr(radii)
+    a.scales = _lib.ptr(g.scales)
+    a.rotations = _lib.ptr(g.rotations)
+    a.cov3d_precomp = _lib.ptr(g.cov3D)
+    a.scale_modifier = g.scale_modifier
+    a.viewmatrix = _lib.ptr(cam.viewmatrix)
+    a.projmatrix = _lib.ptr(cam.projmatrix)
+    a.campos = _lib.ptr(cam.campos)
+    a.tanfovx, a.tanfovy = float(cam.tanfovx), float(cam.tanfovy)
+    a.focal_x, a.focal_y = cam.focal_x, cam.focal_y
+    a.sh = _lib.ptr(g.sh)
+    a.sh_degree = g.degree
+    a.sh_coeffs = g.sh.shape[1] if g.sh is not None else 0
+    a.records = _lib.ptr(records)
+    a.grad_acc = _lib.ptr(grad_acc)
+    a.grad_proj_2d = _lib.ptr(grad_proj_2d)
+    a.grad_conic_2d = _lib.ptr(grad_conic_2d)
+    a.grad_conic_2d_inv = _lib.ptr(grad_conic_2d_inv)
+    a.accumulate = int(acc)
+    a.grad_means3d = _lib.ptr(out.grad_means3D)
+    a.grad_means2d = _lib.ptr(out.grad_means2D)
+    a.grad_scales = _lib.ptr(out.grad_scales)
+    a.grad_rotations = _lib.ptr(out.grad_rotations)
+    a.grad_opacity = _lib.ptr(out.grad_opacity)
+    a.grad_sh = _lib.ptr(out.grad_sh)
+    a.grad_colors = _lib.ptr(out.grad_colors)
+    a.grad_cov3d = _lib.ptr(out.grad_cov3D)
+    with _stage_timer("preprocess_bwd", {"P": P, "kernels": 1}):
+        _lib.call("gsb_preprocess_bwd", a, _lib.stream_handle(dev))
+    return out
+
+
+def mark_visible(means3D: torch.Tensor, viewmatrix: torch.Tensor) -> torch.Tensor:
+    pts = _f32(means3D)
+    if pts.ndim != 2 or pts.shape[1] != 3:
+        raise ValueError("means3D must have dimensions (num_points, 3)")
+    out = torch.empty(pts.shape[0], dtype=torch.uint8, device=pts.device)
+    if pts.shape[0] == 0:
+        return out.to(torch.bool)
+    with torch.cuda.device(pts.device):
+        _lib.call("gsb_mark_visible", pts.shape[0], _lib.ptr(pts), _lib.ptr(_f32(viewmatrix)), _lib.ptr(out),
+                  _lib.stream_handle(pts.device))
+    return out.view(torch.bool)

@@ -1,0 +1,316 @@
+// binning.cu -- duplicate-with-keys, stable tile|depth ordering and tile ranges.
+//
+// Restates gswarp's _build_binning_state (binning_ops.py:84-431) in its
+// default "warp_depth_stable_tile" form:
+//   gsb_bin_count:     stable radix sort of all Gaussians by depth float bits
+//                      (invisible ones last), gather of tiles_touched in that
+//                      order and an inclusive scan (int64 total) -- the
+//                      reference's K3/K7/K4/K5 (binning_ops.py:152-224).
+//   gsb_bin_emit_sort: one thread per depth-ordered Gaussian re-runs the
+//                      AccuTile sweep and writes (tile id, point id) pairs
+//                      (binning_kernels.py:126-216, 410-451); a stable radix
+//                      sort over ceil(log2(tiles)) key bits orders them by
+//                      tile (memory.py:571-600); ranges come from the sorted
+//                      keys (binning_kernels.py:467-487).
+// The resulting point list is ordered by (tile, depth bits, point index), the
+// canonical order both reference sort modes produce.  Built with -fmad=false
+// so the emitted tiles match the preprocess counts bit for bit.
+#include <algorithm>
+
+#include "gsb_common.cuh"
+#include "gsb_geometry.cuh"
+#include "radix_sort.cuh"
+
+namespace gsb {
+namespace {
+
+constexpr int SCAN_THREADS = 256;
+constexpr int SCAN_ITEMS = 16;
+constexpr int SCAN_TILE = SCAN_THREADS * SCAN_ITEMS;  // 4096
+
+__global__ void depth_keys_kernel(int P, const float* __restrict__ depths,
+                                  const int* __restrict__ radii, unsigned* __restrict__ keys,
+                                  unsigned* __restrict__ vals) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= P) return;
+  keys[i] = radii[i] > 0 ? __float_as_uint(depths[i]) : 0xFFFFFFFFu;
+  vals[i] = (unsigned)i;
+}
+
+// Block sums (int64) of tiles_touched gathered in depth order.
+__global__ void __launch_bounds__(SCAN_THREADS) scan_reduce_kernel(
+    int P, const int* __restrict__ order, const int* __restrict__ tiles_touched,
+    long long* __restrict__ block_sums) {
+  __shared__ long long s[SCAN_THREADS / 32];
+  const long long base = (long long)blockIdx.x * SCAN_TILE;
+  long long acc = 0;
+#pragma unroll
+  for (int i = 0; i < SCAN_ITEMS; ++i) {
+    const long long r = base + i * SCAN_THREADS + threadIdx.x;
+    if (r < P) acc += tiles_touched[order[r]];
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if ((threadIdx.x & 31) == 0) s[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    long long t = 0;
+    for (int w = 0; w < SCAN_THREADS / 32; ++w) t += s[w];
+    block_sums[blockIdx.x] = t;
+  }
+}
+
+// Exclusive scan of the block sums in one CTA; writes the pair total.
+__global__ void __launch_bounds__(1024) scan_blocks_kernel(int nblocks,
+                                                           long long* __restrict__ block_sums,
+                                                           long long* __restrict__ status_out) {
+  __shared__ long long s_carry;
+  __shared__ long long s_warp[32];
+  if (threadIdx.x == 0) s_carry = 0;
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int base = 0; base < nblocks; base += 1024) {
+    const int i = base + threadIdx.x;
+    const long long v = i < nblocks ? block_sums[i] : 0;
+    long long x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const long long y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) s_warp[warp] = x;
+    __syncthreads();
+    long long wpre = 0, tot = 0;
+    for (int w = 0; w < 32; ++w) {
+      const long long t = s_warp[w];
+      if (w < warp) wpre += t;
+      tot += t;
+    }
+    if (i < nblocks) block_sums[i] = s_carry + wpre + x - v;
+    __syncthreads();
+    if (threadIdx.x == 0) s_carry += tot;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) status_out[0] = s_carry;
+}
+
+// Inclusive scan in depth order: offsets[r] = sum_{q<=r} tiles[order[q]].
+__global__ void __launch_bounds__(SCAN_THREADS) scan_downsweep_kernel(
+    int P, const int* __restrict__ order, const int* __restrict__ tiles_touched,
+    const long long* __restrict__ block_prefix, int* __restrict__ offsets) {
+  __shared__ long long s_warp[SCAN_THREADS / 32];
+  const long long base = (long long)blockIdx.x * SCAN_TILE;
+  // Thread t owns the SCAN_ITEMS consecutive ranks [base + t*ITEMS, ...).
+  long long v[SCAN_ITEMS];
+  long long run = 0;
+#pragma unroll
+  for (int i = 0; i < SCAN_ITEMS; ++i) {
+    const long long r = base + (long long)threadIdx.x * SCAN_ITEMS + i;
+    const long long c = r < P ? tiles_touched[order[r]] : 0;
+    run += c;
+    v[i] = run;
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  long long x = run;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const long long y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) s_warp[warp] = x;
+  __syncthreads();
+  long long wpre = 0;
+  for (int w = 0; w < warp; ++w) wpre += s_warp[w];
+  const long long excl = block_prefix[blockIdx.x] + wpre + x - run;
+#pragma unroll
+  for (int i = 0; i < SCAN_ITEMS; ++i) {
+    const long long r = base + (long long)threadIdx.x * SCAN_ITEMS + i;
+    if (r < P) offsets[r] = (int)(excl + v[i]);
+  }
+}
+
+struct EmitPairs {
+  unsigned* keys;
+  unsigned* vals;
+  long long start;
+  int cap;
+  int point;
+  mutable int k;
+  __device__ __forceinline__ void operator()(int tile) const {
+    if (k < cap) {
+      keys[start + k] = (unsigned)tile;
+      vals[start + k] = (unsigned)point;
+    }
+    ++k;
+  }
+};
+
+__global__ void __launch_bounds__(256) emit_kernel(
+    int P, int gx, int gy, int mode, const int* __restrict__ order,
+    const int* __restrict__ offsets, const int* __restrict__ tiles_touched,
+    const int* __restrict__ radii, const float4* __restrict__ records,
+    const float* __restrict__ conic_2d_inv, unsigned* __restrict__ keys,
+    unsigned* __restrict__ vals, long long* __restrict__ err) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= P) return;
+  const int p = order[r];
+  const int n = tiles_touched[p];
+  if (n <= 0) return;
+  const int radius = radii[p];
+  const float4 q0 = records[(size_t)p * 3 + 0];
+  const float4 q1 = records[(size_t)p * 3 + 1];
+  const float cov_a = conic_2d_inv[(size_t)p * 3 + 0];
+  const float cov_c = conic_2d_inv[(size_t)p * 3 + 2];
+  EmitPairs e{keys, vals, (long long)offsets[r] - n, n, p, 0};
+  cover_tiles(q0.x, q0.y, cov_a, cov_c, q0.z, q0.w, q1.x, q1.y, radius, gx, gy, mode, e);
+  if (e.k != n) atomicOr((unsigned long long*)err, (unsigned long long)ERR_EMIT_MISMATCH);
+}
+
+__global__ void ranges_kernel(long long R, const unsigned* __restrict__ keys,
+                              int* __restrict__ ranges) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= R) return;
+  const unsigned cur = keys[i];
+  if (i == 0) {
+    ranges[cur * 2] = 0;
+  } else {
+    const unsigned prev = keys[i - 1];
+    if (cur != prev) {
+      ranges[prev * 2 + 1] = (int)i;
+      ranges[cur * 2] = (int)i;
+    }
+  }
+  if (i == R - 1) ranges[cur * 2 + 1] = (int)R;
+}
+
+inline size_t align256(size_t b) { return (b + 255) & ~(size_t)255; }
+
+inline int tile_sort_passes(int tiles) {
+  if (tiles <= 1) return 0;
+  int bits = 32 - __builtin_clz((unsigned)(tiles - 1));
+  return (bits + radix::RADIX_BITS - 1) / radix::RADIX_BITS;
+}
+
+}  // namespace
+}  // namespace gsb
+
+using namespace gsb;
+
+GSB_EXPORT size_t gsb_bin_count_workspace_bytes(int P) {
+  const size_t n = (size_t)(P > 0 ? P : 1);
+  size_t b = 0;
+  b += align256(n * 4) * 3;  // keys, keys_alt, vals_alt
+  b += align256((size_t)div_up((long long)n, SCAN_TILE) * 8);
+  b += radix::scratch_bytes((long long)n, 4);
+  return b + 256;
+}
+
+GSB_EXPORT int gsb_bin_count(const gsb_bin_count_args* a, void* stream) {
+  if (!a || a->P < 0) {
+    set_error("gsb_bin_count: invalid arguments");
+    return GSB_ERR_INVALID;
+  }
+  cudaStream_t s = (cudaStream_t)stream;
+  if (!a->status_out) {
+    set_error("gsb_bin_count: status_out is required");
+    return GSB_ERR_INVALID;
+  }
+  if (a->P == 0) {
+    cudaMemsetAsync(a->status_out, 0, 2 * sizeof(long long), s);
+    return check_launch("gsb_bin_count(empty)");
+  }
+  if (!a->depths || !a->radii || !a->tiles_touched || !a->depth_order || !a->point_offsets ||
+      !a->workspace || a->workspace_bytes < gsb_bin_count_workspace_bytes(a->P)) {
+    set_error("gsb_bin_count: null pointer or workspace too small");
+    return GSB_ERR_INVALID;
+  }
+  const int P = a->P;
+  char* w = (char*)(((uintptr_t)a->workspace + 255) & ~(uintptr_t)255);
+  unsigned* keys = (unsigned*)w;
+  w += align256((size_t)P * 4);
+  unsigned* keys_alt = (unsigned*)w;
+  w += align256((size_t)P * 4);
+  unsigned* vals_alt = (unsigned*)w;
+  w += align256((size_t)P * 4);
+  const int nblocks = div_up(P, SCAN_TILE);
+  long long* block_sums = (long long*)w;
+  w += align256((size_t)nblocks * 8);
+  void* sort_scratch = w;
+
+  long long* err = a->status_out + 1;
+  cudaMemsetAsync(err, 0, sizeof(long long), s);
+  unsigned* vals0 = (unsigned*)a->depth_order;
+  depth_keys_kernel<<<div_up(P, 256), 256, 0, s>>>(P, a->depths, a->radii, keys, vals0);
+  unsigned* kb[2] = {keys, keys_alt};
+  unsigned* vb[2] = {vals0, vals_alt};
+  const int where = radix::sort_pairs(kb, vb, P, 4, sort_scratch, err, s);
+  if (where != 0) {  // 4 passes always end in buffer 0; kept for safety
+    cudaMemcpyAsync(a->depth_order, vals_alt, (size_t)P * 4, cudaMemcpyDeviceToDevice, s);
+  }
+  scan_reduce_kernel<<<nblocks, SCAN_THREADS, 0, s>>>(P, a->depth_order, a->tiles_touched,
+                                                      block_sums);
+  scan_blocks_kernel<<<1, 1024, 0, s>>>(nblocks, block_sums, a->status_out);
+  scan_downsweep_kernel<<<nblocks, SCAN_THREADS, 0, s>>>(P, a->depth_order, a->tiles_touched,
+                                                         block_sums, a->point_offsets);
+  return check_launch("gsb_bin_count");
+}
+
+GSB_EXPORT size_t gsb_bin_sort_workspace_bytes(long long R, int W, int H) {
+  const int tiles = div_up(W, BLOCK_X) * div_up(H, BLOCK_Y);
+  const size_t n = (size_t)(R > 0 ? R : 1);
+  size_t b = align256(n * 4) * 3;  // keys, keys_alt, vals_alt
+  b += radix::scratch_bytes((long long)n, std::max(tile_sort_passes(tiles), 1));
+  return b + 256;
+}
+
+GSB_EXPORT int gsb_bin_emit_sort(const gsb_bin_sort_args* a, void* stream) {
+  if (!a || a->P < 0 || a->W <= 0 || a->H <= 0 || a->num_rendered < 0 ||
+      a->num_rendered > 2147483647ll) {
+    set_error("gsb_bin_emit_sort: invalid sizes");
+    return a && a->num_rendered > 2147483647ll ? GSB_ERR_OVERFLOW : GSB_ERR_INVALID;
+  }
+  cudaStream_t s = (cudaStream_t)stream;
+  const int gx = div_up(a->W, BLOCK_X), gy = div_up(a->H, BLOCK_Y);
+  const int tiles = gx * gy;
+  if (!a->ranges || !a->error_word) {
+    set_error("gsb_bin_emit_sort: ranges and error_word are required");
+    return GSB_ERR_INVALID;
+  }
+  cudaMemsetAsync(a->ranges, 0, (size_t)tiles * 2 * sizeof(int), s);
+  const long long R = a->num_rendered;
+  if (R == 0 || a->P == 0) return check_launch("gsb_bin_emit_sort(empty)");
+  if (!a->depth_order || !a->point_offsets || !a->radii || !a->records || !a->conic_2d_inv ||
+      !a->tiles_touched || !a->point_list || !a->workspace ||
+      a->workspace_bytes < gsb_bin_sort_workspace_bytes(R, a->W, a->H)) {
+    set_error("gsb_bin_emit_sort: null pointer or workspace too small");
+    return GSB_ERR_INVALID;
+  }
+  char* w = (char*)(((uintptr_t)a->workspace + 255) & ~(uintptr_t)255);
+  unsigned* keys = (unsigned*)w;
+  w += align256((size_t)R * 4);
+  unsigned* keys_alt = (unsigned*)w;
+  w += align256((size_t)R * 4);
+  unsigned* vals_alt = (unsigned*)w;
+  w += align256((size_t)R * 4);
+  void* sort_scratch = w;
+
+  const int passes = tile_sort_passes(tiles);
+  // Emit into whichever value buffer the last sort pass will NOT write, so
+  // the sorted point ids land directly in point_list.
+  unsigned* pl = (unsigned*)a->point_list;
+  unsigned* vb[2];
+  unsigned* kb[2] = {keys, keys_alt};
+  if (passes % 2 == 0) {
+    vb[0] = pl;
+    vb[1] = vals_alt;
+  } else {
+    vb[0] = vals_alt;
+    vb[1] = pl;
+  }
+  emit_kernel<<<div_up(a->P, 256), 256, 0, s>>>(
+      a->P, gx, gy, a->coverage_mode, a->depth_order, a->point_offsets, a->tiles_touched, a->radii,
+      reinterpret_cast<const float4*>(a->records), a->conic_2d_inv, kb[0], vb[0], a->error_word);
+  const int where = radix::sort_pairs(kb, vb, R, passes, sort_scratch, a->error_word, s);
+  ranges_kernel<<<div_up(R, 256), 256, 0, s>>>(R, kb[where], a->ranges);
+  return check_launch("gsb_bin_emit_sort");
+}

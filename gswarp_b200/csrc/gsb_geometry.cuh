@@ -1,0 +1,197 @@
+// gsb_geometry.cuh -- screen-space footprint and AccuTile tile coverage.
+//
+// Device restatement of gswarp's math_kernels.py:86-390 and the emission
+// loops of binning_kernels.py:126-216.  Every translation unit that includes
+// this header is compiled with -fmad=false (no FMA contraction), IEEE
+// division and square root, so the tile counts computed in preprocess and
+// the tiles emitted during binning are bit-identical to each other and to
+// the CPU oracle; the count/emit agreement is what keeps the pair buffer
+// exactly filled.
+#pragma once
+
+#include "gsb_common.cuh"
+
+namespace gsb {
+
+constexpr float DET_EPSILON = 1.0e-7f;
+constexpr float SNUGBOX_PIXEL_PADDING = 1.0f;
+constexpr float COVERAGE_Q_EPSILON = 1.0e-4f;
+constexpr float FLT_BIG = 3.402823466e38f;
+
+struct Rect {
+  int x0, y0, x1, y1;
+};
+
+// math_kernels.py:86-87
+__device__ __forceinline__ float ndc2pix(float v, int size) {
+  return ((v + 1.0f) * (float)size - 1.0f) * 0.5f;
+}
+
+// math_kernels.py:136-148 (CUDA getRect)
+__device__ __forceinline__ Rect tile_rect(float px, float py, int radius, int gx, int gy) {
+  Rect r;
+  r.x0 = imn(gx, imx(0, f2i((px - (float)radius) / (float)BLOCK_X)));
+  r.y0 = imn(gy, imx(0, f2i((py - (float)radius) / (float)BLOCK_Y)));
+  r.x1 = imn(gx, imx(0, f2i((px + (float)radius + (float)(BLOCK_X - 1)) / (float)BLOCK_X)));
+  r.y1 = imn(gy, imx(0, f2i((py + (float)radius + (float)(BLOCK_Y - 1)) / (float)BLOCK_Y)));
+  return r;
+}
+
+// Opacity threshold 2*ln(max(255*op, 1)) of math_kernels.py:170,340.
+__device__ __forceinline__ float opacity_threshold(float opacity) {
+  return 2.0f * crlogf(fmx(255.0f * opacity, 1.0f));
+}
+
+// math_kernels.py:150-194: padded SnugBox clipped to the CUDA 3-sigma rect.
+__device__ __forceinline__ Rect snugbox_rect(float px, float py, float cov_aa, float cov_cc,
+                                             float t, int cuda_radius, int gx, int gy) {
+  Rect c = tile_rect(px, py, cuda_radius, gx, gy);
+  if (t <= 0.0f) return Rect{0, 0, 0, 0};
+  int rx = f2i(ceilf(sqrtf(fmx(t * cov_aa, 0.0f)) + SNUGBOX_PIXEL_PADDING));
+  int ry = f2i(ceilf(sqrtf(fmx(t * cov_cc, 0.0f)) + SNUGBOX_PIXEL_PADDING));
+  Rect s;
+  s.x0 = imn(gx, imx(0, f2i((px - (float)rx) / (float)BLOCK_X)));
+  s.y0 = imn(gy, imx(0, f2i((py - (float)ry) / (float)BLOCK_Y)));
+  s.x1 = imn(gx, imx(0, f2i((px + (float)rx + (float)(BLOCK_X - 1)) / (float)BLOCK_X)));
+  s.y1 = imn(gy, imx(0, f2i((py + (float)ry + (float)(BLOCK_Y - 1)) / (float)BLOCK_Y)));
+  return Rect{imx(c.x0, s.x0), imx(c.y0, s.y0), imn(c.x1, s.x1), imn(c.y1, s.y1)};
+}
+
+// math_kernels.py:196-204
+__device__ __forceinline__ float conic_q(float x, float y, float a, float b, float c) {
+  return a * x * x + 2.0f * b * x * y + c * y * y;
+}
+
+// math_kernels.py:206-240
+__device__ __forceinline__ bool conic_rect_intersects(float px, float py, float a, float b,
+                                                      float c, float threshold, int tx, int ty) {
+  float det = a * c - b * b;
+  if (a <= 0.0f || c <= 0.0f || det <= DET_EPSILON) return true;
+  float x0 = (float)(tx * BLOCK_X) - px;
+  float x1 = (float)(tx * BLOCK_X + BLOCK_X - 1) - px;
+  float y0 = (float)(ty * BLOCK_Y) - py;
+  float y1 = (float)(ty * BLOCK_Y + BLOCK_Y - 1) - py;
+  if (x0 <= 0.0f && x1 >= 0.0f && y0 <= 0.0f && y1 >= 0.0f) return true;
+  float q_min = FLT_BIG;
+  float y = fclamp(-b * x0 / c, y0, y1);
+  q_min = fmn(q_min, conic_q(x0, y, a, b, c));
+  y = fclamp(-b * x1 / c, y0, y1);
+  q_min = fmn(q_min, conic_q(x1, y, a, b, c));
+  float x = fclamp(-b * y0 / a, x0, x1);
+  q_min = fmn(q_min, conic_q(x, y0, a, b, c));
+  x = fclamp(-b * y1 / a, x0, x1);
+  q_min = fmn(q_min, conic_q(x, y1, a, b, c));
+  return q_min <= threshold + COVERAGE_Q_EPSILON;
+}
+
+// math_kernels.py:242-303: AccuTile tile interval of one band.
+__device__ __forceinline__ void band_interval(float pu, float pv, float cuu, float cuv, float cvv,
+                                              float threshold, int tile_v, int block_u,
+                                              int block_v, int rect_u_min, int rect_u_max,
+                                              int& lo, int& hi) {
+  float det = cuu * cvv - cuv * cuv;
+  if (cuu <= 0.0f || cvv <= 0.0f || det <= DET_EPSILON) {
+    lo = rect_u_min;
+    hi = rect_u_max;
+    return;
+  }
+  float ts = threshold + COVERAGE_Q_EPSILON;
+  float v0 = (float)(tile_v * block_v) - pv;
+  float v1 = (float)(tile_v * block_v + block_v - 1) - pv;
+  float u_min = FLT_BIG, u_max = -FLT_BIG;
+  bool found = false;
+  float disc = cuu * ts - det * v0 * v0;
+  if (disc >= -COVERAGE_Q_EPSILON) {
+    float half = sqrtf(fmx(disc, 0.0f)) / cuu;
+    float center = -cuv * v0 / cuu;
+    u_min = fmn(u_min, center - half);
+    u_max = fmx(u_max, center + half);
+    found = true;
+  }
+  disc = cuu * ts - det * v1 * v1;
+  if (disc >= -COVERAGE_Q_EPSILON) {
+    float half = sqrtf(fmx(disc, 0.0f)) / cuu;
+    float center = -cuv * v1 / cuu;
+    u_min = fmn(u_min, center - half);
+    u_max = fmx(u_max, center + half);
+    found = true;
+  }
+  float extent_u = sqrtf(fmx(ts * cvv / det, 0.0f));
+  float v_at_min_u = cuv * extent_u / cvv;
+  if (v_at_min_u >= v0 - COVERAGE_Q_EPSILON && v_at_min_u <= v1 + COVERAGE_Q_EPSILON) {
+    u_min = fmn(u_min, -extent_u);
+    u_max = fmx(u_max, -extent_u);
+    found = true;
+  }
+  float v_at_max_u = -cuv * extent_u / cvv;
+  if (v_at_max_u >= v0 - COVERAGE_Q_EPSILON && v_at_max_u <= v1 + COVERAGE_Q_EPSILON) {
+    u_min = fmn(u_min, extent_u);
+    u_max = fmx(u_max, extent_u);
+    found = true;
+  }
+  if (!found) {
+    lo = rect_u_min;
+    hi = rect_u_min;
+    return;
+  }
+  int tmin = f2i(floorf((pu + u_min) / (float)block_u));
+  int tmax = f2i(floorf((pu + u_max) / (float)block_u)) + 1;
+  lo = imx(rect_u_min, imn(rect_u_max, tmin));
+  hi = imx(rect_u_min, imn(rect_u_max, tmax));
+}
+
+// Tile coverage of one Gaussian (math_kernels.py:305-390; conic_rect as
+// recounted by binning_kernels.py:56-124).  With EMIT=true
+// it also writes every covered tile id, in the reference's emission order
+// (binning_kernels.py:141-216), through emit(tile_id).
+struct NoEmit {
+  __device__ __forceinline__ void operator()(int) const {}
+};
+
+template <typename Emit>
+__device__ __forceinline__ int cover_tiles(float px, float py, float cov_aa, float cov_cc,
+                                           float ca, float cb, float cc, float opacity,
+                                           int cuda_radius, int gx, int gy, int mode,
+                                           const Emit& emit) {
+  const float t = opacity_threshold(opacity);
+  Rect r = snugbox_rect(px, py, cov_aa, cov_cc, t, cuda_radius, gx, gy);
+  int span_x = r.x1 - r.x0;
+  int span_y = r.y1 - r.y0;
+  int area = span_x * span_y;
+  if (area <= 1 || mode == GSB_COVERAGE_SNUGBOX) {
+    for (int ty = r.y0; ty < r.y1; ++ty)
+      for (int tx = r.x0; tx < r.x1; ++tx) emit(ty * gx + tx);
+    return area;
+  }
+  int count = 0;
+  // conic_rect keeps its per-tile test only for footprints of at most 64
+  // tiles and falls back to the AccuTile sweep above that, which is what the
+  // reference's binning recount applies (binning_kernels.py:56-124).
+  if (mode == GSB_COVERAGE_CONIC_RECT && area <= 64) {
+    for (int ty = r.y0; ty < r.y1; ++ty)
+      for (int tx = r.x0; tx < r.x1; ++tx)
+        if (conic_rect_intersects(px, py, ca, cb, cc, t, tx, ty)) {
+          ++count;
+          emit(ty * gx + tx);
+        }
+    return count;
+  }
+  if (span_y <= span_x) {
+    for (int ty = r.y0; ty < r.y1; ++ty) {
+      int lo, hi;
+      band_interval(px, py, ca, cb, cc, t, ty, BLOCK_X, BLOCK_Y, r.x0, r.x1, lo, hi);
+      count += imx(0, hi - lo);
+      for (int tx = lo; tx < hi; ++tx) emit(ty * gx + tx);
+    }
+  } else {
+    for (int tx = r.x0; tx < r.x1; ++tx) {
+      int lo, hi;
+      band_interval(py, px, cc, cb, ca, t, tx, BLOCK_Y, BLOCK_X, r.y0, r.y1, lo, hi);
+      count += imx(0, hi - lo);
+      for (int ty = lo; ty < hi; ++ty) emit(ty * gx + tx);
+    }
+  }
+  return count;
+}
+
+}  // namespace gsb

@@ -1,0 +1,357 @@
+// preprocess.cu -- per-Gaussian projection, EWA covariance, radius, AccuTile
+// tile count and SH colour, fused into one pass over the Gaussians.
+//
+// Restates gswarp's _fused_project_cov3d_cov2d_preprocess_sr_warp_kernel
+// (preprocess_kernels.py:83-269), its cov3D_precomp variant
+// (_project_preprocess_visible_points_cov_warp_kernel :630-672 +
+// _cov2d_preprocess_masked_pack_warp_kernel :345-476) and
+// _forward_rgb_from_sh_v3_warp_kernel (:272-342).  Built with -fmad=false:
+// radii, tiles_touched and depth bits must match the CPU oracle bit for bit.
+//
+// B200 layout: one thread per Gaussian, 256-thread CTAs; view/proj matrices
+// staged once per CTA in shared memory; the SH row (up to 192 B) is read with
+// 16-byte vector loads only for Gaussians that survive culling; the render
+// record (48 B, three float4) is written with vector stores so the render
+// kernels gather one Gaussian with three 16-byte loads.
+#include "gsb_common.cuh"
+#include "gsb_geometry.cuh"
+
+namespace gsb {
+namespace {
+
+__constant__ float SH_C0 = 0.28209479177387814f;
+__constant__ float SH_C1 = 0.4886025119029199f;
+__constant__ float SH_C2[5] = {1.0925484305920792f, -1.0925484305920792f, 0.31539156525252005f,
+                               -1.0925484305920792f, 0.5462742152960396f};
+__constant__ float SH_C3[7] = {-0.5900435899266435f, 2.890611442640554f, -0.4570457994644658f,
+                               0.3731763325901154f,  -0.4570457994644658f, 1.445305721320277f,
+                               -0.5900435899266435f};
+
+// SH degree 0..3 colour (preprocess_kernels.py:272-342).  Coefficient c of
+// channel ch lives at sp[c*3+ch].
+__device__ __forceinline__ void eval_sh(const float* __restrict__ sp, int K, int degree, float x,
+                                        float y, float z, float col[3]) {
+  const float c0 = SH_C0;
+#pragma unroll
+  for (int ch = 0; ch < 3; ++ch) col[ch] = c0 * __ldg(sp + ch);
+  if (degree > 0 && K > 3) {
+    const float c1 = SH_C1;
+    float b1 = -c1 * y, b2 = c1 * z, b3 = -c1 * x;
+#pragma unroll
+    for (int ch = 0; ch < 3; ++ch) col[ch] = col[ch] + b1 * __ldg(sp + 3 + ch);
+#pragma unroll
+    for (int ch = 0; ch < 3; ++ch) col[ch] = col[ch] + b2 * __ldg(sp + 6 + ch);
+#pragma unroll
+    for (int ch = 0; ch < 3; ++ch) col[ch] = col[ch] + b3 * __ldg(sp + 9 + ch);
+    if (degree > 1 && K > 8) {
+      float xx = x * x, yy = y * y, zz = z * z, xy = x * y, yz = y * z, xz = x * z;
+      float w[5];
+      w[0] = SH_C2[0] * xy;
+      w[1] = SH_C2[1] * yz;
+      w[2] = SH_C2[2] * (2.0f * zz - xx - yy);
+      w[3] = SH_C2[3] * xz;
+      w[4] = SH_C2[4] * (xx - yy);
+#pragma unroll
+      for (int k = 0; k < 5; ++k)
+#pragma unroll
+        for (int ch = 0; ch < 3; ++ch) col[ch] = col[ch] + w[k] * __ldg(sp + (4 + k) * 3 + ch);
+      if (degree > 2 && K > 15) {
+        float v[7];
+        v[0] = SH_C3[0] * y * (3.0f * xx - yy);
+        v[1] = SH_C3[1] * xy * z;
+        v[2] = SH_C3[2] * y * (4.0f * zz - xx - yy);
+        v[3] = SH_C3[3] * z * (2.0f * zz - 3.0f * xx - 3.0f * yy);
+        v[4] = SH_C3[4] * x * (4.0f * zz - xx - yy);
+        v[5] = SH_C3[5] * z * (xx - yy);
+        v[6] = SH_C3[6] * x * (xx - 3.0f * yy);
+#pragma unroll
+        for (int k = 0; k < 7; ++k)
+#pragma unroll
+          for (int ch = 0; ch < 3; ++ch) col[ch] = col[ch] + v[k] * __ldg(sp + (9 + k) * 3 + ch);
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) preprocess_fwd_kernel(const gsb_preprocess_args a) {
+  __shared__ float s_view[16], s_proj[16], s_cam[3];
+  if (threadIdx.x < 16) {
+    s_view[threadIdx.x] = a.viewmatrix[threadIdx.x];
+    s_proj[threadIdx.x] = a.projmatrix[threadIdx.x];
+  } else if (threadIdx.x < 19) {
+    s_cam[threadIdx.x - 16] = a.campos ? a.campos[threadIdx.x - 16] : 0.0f;
+  }
+  __syncthreads();
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= a.P) return;
+  const float* v = s_view;
+  const float* pr = s_proj;
+  const int gx = (a.W + BLOCK_X - 1) / BLOCK_X;
+  const int gy = (a.H + BLOCK_Y - 1) / BLOCK_Y;
+
+  const float p0 = a.means[idx * 3 + 0], p1 = a.means[idx * 3 + 1], p2 = a.means[idx * 3 + 2];
+  const float opacity = a.opacities[idx];
+
+  int radius = 0, tiles = 0;
+  float depth = 0.0f, px = 0.0f, py = 0.0f;
+  float con0 = 0.0f, con1 = 0.0f, con2 = 0.0f;
+  float cov_a = 0.0f, cov_b = 0.0f, cov_c = 0.0f;
+
+  const float p_view_z = v[2] * p0 + v[6] * p1 + v[10] * p2 + v[14];
+  bool go = false;
+  float ppx = 0.0f, ppy = 0.0f;
+  bool strict_det = false;
+  if (a.cov3d_precomp == nullptr) {
+    if (p_view_z > 0.2f) {
+      const float hom_x = pr[0] * p0 + pr[4] * p1 + pr[8] * p2 + pr[12];
+      const float hom_y = pr[1] * p0 + pr[5] * p1 + pr[9] * p2 + pr[13];
+      const float hom_w = pr[3] * p0 + pr[7] * p1 + pr[11] * p2 + pr[15];
+      const float inv_w = 1.0f / (hom_w + 1.0e-7f);
+      ppx = hom_x * inv_w;
+      ppy = hom_y * inv_w;
+      const float s0 = a.scales[idx * 3 + 0] * a.scale_modifier;
+      const float s1 = a.scales[idx * 3 + 1] * a.scale_modifier;
+      const float s2 = a.scales[idx * 3 + 2] * a.scale_modifier;
+      const float4 q = reinterpret_cast<const float4*>(a.rotations)[idx];
+      const float rr = q.x, xq = q.y, yq = q.z, zq = q.w;
+      const float r00 = 1.0f - 2.0f * (yq * yq + zq * zq);
+      const float r01 = 2.0f * (xq * yq + rr * zq);
+      const float r02 = 2.0f * (xq * zq - rr * yq);
+      const float r10 = 2.0f * (xq * yq - rr * zq);
+      const float r11 = 1.0f - 2.0f * (xq * xq + zq * zq);
+      const float r12 = 2.0f * (yq * zq + rr * xq);
+      const float r20 = 2.0f * (xq * zq + rr * yq);
+      const float r21 = 2.0f * (yq * zq - rr * xq);
+      const float r22 = 1.0f - 2.0f * (xq * xq + yq * yq);
+      const float m00 = s0 * r00, m01 = s0 * r01, m02 = s0 * r02;
+      const float m10 = s1 * r10, m11 = s1 * r11, m12 = s1 * r12;
+      const float m20 = s2 * r20, m21 = s2 * r21, m22 = s2 * r22;
+      float vx = v[0] * p0 + v[4] * p1 + v[8] * p2 + v[12];
+      float vy = v[1] * p0 + v[5] * p1 + v[9] * p2 + v[13];
+      const float vz = p_view_z;
+      const float limx = 1.3f * a.tanfovx, limy = 1.3f * a.tanfovy;
+      const float txtz = vx / vz, tytz = vy / vz;
+      vx = fclamp(txtz, -limx, limx) * vz;
+      vy = fclamp(tytz, -limy, limy) * vz;
+      const float a_j = a.focal_x / vz, b_j = a.focal_y / vz;
+      const float c_j = -(a.focal_x * vx) / (vz * vz);
+      const float d_j = -(a.focal_y * vy) / (vz * vz);
+      const float t00 = v[0] * a_j + v[2] * c_j;
+      const float t10 = v[4] * a_j + v[6] * c_j;
+      const float t20 = v[8] * a_j + v[10] * c_j;
+      const float t01 = v[1] * b_j + v[2] * d_j;
+      const float t11 = v[5] * b_j + v[6] * d_j;
+      const float t21 = v[9] * b_j + v[10] * d_j;
+      const float a00 = m00 * t00 + m01 * t10 + m02 * t20;
+      const float a10 = m10 * t00 + m11 * t10 + m12 * t20;
+      const float a20 = m20 * t00 + m21 * t10 + m22 * t20;
+      const float a01 = m00 * t01 + m01 * t11 + m02 * t21;
+      const float a11 = m10 * t01 + m11 * t11 + m12 * t21;
+      const float a21 = m20 * t01 + m21 * t11 + m22 * t21;
+      cov_a = a00 * a00 + a10 * a10 + a20 * a20 + 0.3f;
+      cov_b = a00 * a01 + a10 * a11 + a20 * a21;
+      cov_c = a01 * a01 + a11 * a11 + a21 * a21 + 0.3f;
+      go = true;
+    }
+  } else {
+    const float* c3 = a.cov3d_precomp + (size_t)idx * 6;
+    if (p_view_z > 0.2f) {
+      const float hom_x = pr[0] * p0 + pr[4] * p1 + pr[8] * p2 + pr[12];
+      const float hom_y = pr[1] * p0 + pr[5] * p1 + pr[9] * p2 + pr[13];
+      const float hom_w = pr[3] * p0 + pr[7] * p1 + pr[11] * p2 + pr[15];
+      const float inv_w = 1.0f / (hom_w + 1.0e-7f);
+      ppx = hom_x * inv_w;
+      ppy = hom_y * inv_w;
+      // conservative visibility (math_kernels.py:104-134, 392-406)
+      const float row0 = fabsf(c3[0]) + fabsf(c3[1]) + fabsf(c3[2]);
+      const float row1 = fabsf(c3[1]) + fabsf(c3[3]) + fabsf(c3[4]);
+      const float row2 = fabsf(c3[2]) + fabsf(c3[4]) + fabsf(c3[5]);
+      const float lam = fmx(row0, fmx(row1, row2));
+      const float limx = 1.3f * a.tanfovx, limy = 1.3f * a.tanfovy;
+      const float fx = (float)a.W / (2.0f * a.tanfovx);
+      const float fy = (float)a.H / (2.0f * a.tanfovy);
+      const float row0n = (fx / p_view_z) * sqrtf(1.0f + limx * limx);
+      const float row1n = (fy / p_view_z) * sqrtf(1.0f + limy * limy);
+      const float jf = row0n * row0n + row1n * row1n;
+      const float lu = lam * jf + 0.3f;
+      const int radius_upper = f2i(ceilf(3.0f * sqrtf(fmx(lu, 0.0f))));
+      const Rect rr = tile_rect(ndc2pix(ppx, a.W), ndc2pix(ppy, a.H), radius_upper, gx, gy);
+      if ((rr.x1 - rr.x0) * (rr.y1 - rr.y0) != 0) {
+        float x = v[0] * p0 + v[4] * p1 + v[8] * p2 + v[12];
+        float y = v[1] * p0 + v[5] * p1 + v[9] * p2 + v[13];
+        const float z = v[2] * p0 + v[6] * p1 + v[10] * p2 + v[14];
+        const float txtz = x / z, tytz = y / z;
+        x = fclamp(txtz, -limx, limx) * z;
+        y = fclamp(tytz, -limy, limy) * z;
+        const float ja = a.focal_x / z, jb = a.focal_y / z;
+        const float jc = -(a.focal_x * x) / (z * z);
+        const float jd = -(a.focal_y * y) / (z * z);
+        const float t00 = v[0] * ja + v[2] * jc;
+        const float t10 = v[4] * ja + v[6] * jc;
+        const float t20 = v[8] * ja + v[10] * jc;
+        const float t01 = v[1] * jb + v[2] * jd;
+        const float t11 = v[5] * jb + v[6] * jd;
+        const float t21 = v[9] * jb + v[10] * jd;
+        const float v00 = c3[0], v01 = c3[1], v02 = c3[2], v11 = c3[3], v12 = c3[4], v22 = c3[5];
+        const float vt0x = v00 * t00 + v01 * t10 + v02 * t20;
+        const float vt0y = v01 * t00 + v11 * t10 + v12 * t20;
+        const float vt0z = v02 * t00 + v12 * t10 + v22 * t20;
+        const float vt1x = v00 * t01 + v01 * t11 + v02 * t21;
+        const float vt1y = v01 * t01 + v11 * t11 + v12 * t21;
+        const float vt1z = v02 * t01 + v12 * t11 + v22 * t21;
+        cov_a = t00 * vt0x + t10 * vt0y + t20 * vt0z + 0.3f;
+        cov_b = t00 * vt1x + t10 * vt1y + t20 * vt1z;
+        cov_c = t01 * vt1x + t11 * vt1y + t21 * vt1z + 0.3f;
+        go = true;
+        strict_det = true;
+      }
+    }
+  }
+
+  if (go) {
+    // preprocess_kernels.py:221-269 (and :439-476 with a strict det test)
+    const float det = cov_a * cov_c - cov_b * cov_b;
+    const bool degenerate = strict_det ? (fabsf(det) < DET_EPSILON) : (fabsf(det) <= DET_EPSILON);
+    if (!degenerate) {
+      const float det_inv = 1.0f / det;
+      const float k0 = cov_c * det_inv, k1 = -cov_b * det_inv, k2 = cov_a * det_inv;
+      const float mid = 0.5f * (cov_a + cov_c);
+      const float root = sqrtf(fmx(0.1f, mid * mid - det));
+      const float l1 = mid + root, l2 = mid - root;
+      const int rad = f2i(ceilf(3.0f * sqrtf(fmx(l1, l2))));
+      const float qx = ndc2pix(ppx, a.W);
+      const float qy = ndc2pix(ppy, a.H);
+      const Rect cr = tile_rect(qx, qy, rad, gx, gy);
+      if ((cr.x1 - cr.x0) * (cr.y1 - cr.y0) != 0) {
+        radius = rad;
+        depth = p_view_z;
+        px = qx;
+        py = qy;
+        con0 = k0;
+        con1 = k1;
+        con2 = k2;
+        tiles = cover_tiles(px, py, cov_a, cov_c, con0, con1, con2, opacity, radius, gx, gy,
+                            a.coverage_mode, NoEmit{});
+      } else {
+        cov_a = cov_b = cov_c = 0.0f;
+      }
+    } else {
+      cov_a = cov_b = cov_c = 0.0f;
+    }
+  } else {
+    cov_a = cov_b = cov_c = 0.0f;
+  }
+
+  // Colour: only Gaussians that can be rendered need it; the SH backward
+  // only reads the clamp flags where the render gradient is non-zero.
+  float col[3] = {0.0f, 0.0f, 0.0f};
+  unsigned clamp_bits = 0u;
+  if (radius > 0) {
+    if (a.colors_precomp) {
+      col[0] = a.colors_precomp[idx * 3 + 0];
+      col[1] = a.colors_precomp[idx * 3 + 1];
+      col[2] = a.colors_precomp[idx * 3 + 2];
+    } else if (a.sh) {
+      const float dx = p0 - s_cam[0], dy = p1 - s_cam[1], dz = p2 - s_cam[2];
+      const float len_sq = dx * dx + dy * dy + dz * dz;
+      const float inv_len = 1.0f / sqrtf(fmx(len_sq, 1.0e-20f));
+      const float* sp = a.sh + (size_t)idx * a.sh_coeffs * 3;
+      eval_sh(sp, a.sh_coeffs, a.sh_degree, dx * inv_len, dy * inv_len, dz * inv_len, col);
+#pragma unroll
+      for (int ch = 0; ch < 3; ++ch) {
+        col[ch] = col[ch] + 0.5f;
+        if (col[ch] < 0.0f) {
+          col[ch] = 0.0f;
+          clamp_bits |= 1u << ch;
+        }
+      }
+    }
+  }
+
+  a.radii[idx] = radius;
+  a.depths[idx] = depth;
+  a.tiles_touched[idx] = tiles;
+  reinterpret_cast<float2*>(a.proj_2d)[idx] = make_float2(px, py);
+  a.conic_2d[idx * 3 + 0] = con0;
+  a.conic_2d[idx * 3 + 1] = con1;
+  a.conic_2d[idx * 3 + 2] = con2;
+  a.conic_2d_inv[idx * 3 + 0] = cov_a;
+  a.conic_2d_inv[idx * 3 + 1] = cov_b;
+  a.conic_2d_inv[idx * 3 + 2] = cov_c;
+  float4* rec = reinterpret_cast<float4*>(a.records) + (size_t)idx * 3;
+  const float op_rec = radius > 0 ? opacity : 0.0f;
+  rec[0] = make_float4(px, py, con0, con1);
+  rec[1] = make_float4(con2, op_rec, depth, __uint_as_float(clamp_bits));
+  rec[2] = make_float4(col[0], col[1], col[2], 0.0f);
+}
+
+__global__ void mark_visible_kernel(int P, const float* __restrict__ means,
+                                    const float* __restrict__ view, uint8_t* out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= P) return;
+  const float z = view[2] * means[i * 3] + view[6] * means[i * 3 + 1] +
+                  view[10] * means[i * 3 + 2] + view[14];
+  out[i] = z > 0.2f ? 1 : 0;
+}
+
+__global__ void threshold_log_kernel(const float* in, float* out, long long n) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = crlogf(in[i]);
+}
+
+}  // namespace
+}  // namespace gsb
+
+using namespace gsb;
+
+GSB_EXPORT int gsb_preprocess_fwd(const gsb_preprocess_args* a, void* stream) {
+  if (!a || a->P < 0 || a->W <= 0 || a->H <= 0) {
+    set_error("gsb_preprocess_fwd: invalid sizes");
+    return GSB_ERR_INVALID;
+  }
+  if (a->P == 0) return GSB_OK;
+  const bool sr = a->scales && a->rotations;
+  if (sr == (a->cov3d_precomp != nullptr)) {
+    set_error("gsb_preprocess_fwd: provide exactly one of scales/rotations or cov3d_precomp");
+    return GSB_ERR_INVALID;
+  }
+  if (!a->means || !a->opacities || !a->viewmatrix || !a->projmatrix || !a->radii ||
+      !a->proj_2d || !a->conic_2d || !a->conic_2d_inv || !a->depths || !a->tiles_touched ||
+      !a->records) {
+    set_error("gsb_preprocess_fwd: null pointer argument");
+    return GSB_ERR_INVALID;
+  }
+  if (a->sh && (a->sh_coeffs <= 0 || !a->campos)) {
+    set_error("gsb_preprocess_fwd: SH colours need sh_coeffs > 0 and campos");
+    return GSB_ERR_INVALID;
+  }
+  if ((reinterpret_cast<uintptr_t>(a->records) & 15) ||
+      (a->rotations && (reinterpret_cast<uintptr_t>(a->rotations) & 15)) ||
+      (reinterpret_cast<uintptr_t>(a->proj_2d) & 7)) {
+    set_error("gsb_preprocess_fwd: records/rotations need 16-byte and proj_2d 8-byte alignment");
+    return GSB_ERR_INVALID;
+  }
+  preprocess_fwd_kernel<<<div_up(a->P, 256), 256, 0, (cudaStream_t)stream>>>(*a);
+  return check_launch("preprocess_fwd_kernel");
+}
+
+GSB_EXPORT int gsb_mark_visible(int P, const float* means, const float* viewmatrix, uint8_t* out,
+                                void* stream) {
+  if (P < 0 || (P > 0 && (!means || !viewmatrix || !out))) {
+    set_error("gsb_mark_visible: invalid arguments");
+    return GSB_ERR_INVALID;
+  }
+  if (P == 0) return GSB_OK;
+  mark_visible_kernel<<<div_up(P, 256), 256, 0, (cudaStream_t)stream>>>(P, means, viewmatrix, out);
+  return check_launch("mark_visible_kernel");
+}
+
+GSB_EXPORT int gsb_selftest_threshold_log(const float* in, float* out, long long n, void* stream) {
+  if (n < 0 || (n > 0 && (!in || !out))) {
+    set_error("gsb_selftest_threshold_log: invalid arguments");
+    return GSB_ERR_INVALID;
+  }
+  if (n == 0) return GSB_OK;
+  threshold_log_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(in, out, n);
+  return check_launch("threshold_log_kernel");
+}

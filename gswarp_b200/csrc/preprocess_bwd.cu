@@ -1,0 +1,465 @@
+// preprocess_bwd.cu -- per-Gaussian backward of projection, EWA covariance,
+// scale/rotation (or precomputed 3D covariance) and SH colour, in one pass.
+//
+// Restates gswarp's _fused_backward_preprocess_accumulate_warp_kernel
+// (backward_kernels.py:52-295) together with the SH backward kernels
+// (:297-536), and for cov3D_precomp inputs _backward_projected_means
+// (:842-875) + _backward_cov2d (:709-840) + the accumulate kernel (:34-50),
+// composed as in backward_ops.py:525-744.  Built with -fmad=false: fed the
+// same render gradients it reproduces the CPU oracle bit for bit.
+//
+// B200 layout: one thread per Gaussian.  The render gradients arrive as one
+// 48-byte accumulator per Gaussian (three 16-byte loads); cov3d is recomputed
+// from scale/rotation instead of being stored by the forward (same
+// expressions, same bits, 48 fewer bytes of traffic per Gaussian); SH rows
+// are read only where the colour gradient is non-zero and the (P,K,3)
+// gradient is written in place with 16-byte stores, with none of the
+// reference's (P,K,3)<->(K,P,3) transposes.
+#include "gsb_common.cuh"
+
+namespace gsb {
+namespace {
+
+__constant__ float SH_C0 = 0.28209479177387814f;
+__constant__ float SH_C1 = 0.4886025119029199f;
+__constant__ float SH_C2[5] = {1.0925484305920792f, -1.0925484305920792f, 0.31539156525252005f,
+                               -1.0925484305920792f, 0.5462742152960396f};
+__constant__ float SH_C3[7] = {-0.5900435899266435f, 2.890611442640554f, -0.4570457994644658f,
+                               0.3731763325901154f,  -0.4570457994644658f, 1.445305721320277f,
+                               -0.5900435899266435f};
+
+__device__ __forceinline__ void store_or_add(float* p, float v, bool acc) {
+  if (acc)
+    *p += v;
+  else
+    *p = v;
+}
+
+// math_kernels.py:89-97
+__device__ __forceinline__ void dnormvdv(const float v[3], const float g[3], float out[3]) {
+  const float sum2 = v[0] * v[0] + v[1] * v[1] + v[2] * v[2];
+  const float invsum32 = 1.0f / sqrtf(fmx(sum2 * sum2 * sum2, 1.0e-20f));
+  out[0] = ((sum2 - v[0] * v[0]) * g[0] - v[1] * v[0] * g[1] - v[2] * v[0] * g[2]) * invsum32;
+  out[1] = (-v[0] * v[1] * g[0] + (sum2 - v[1] * v[1]) * g[1] - v[2] * v[1] * g[2]) * invsum32;
+  out[2] = (-v[0] * v[2] * g[0] - v[1] * v[2] * g[1] + (sum2 - v[2] * v[2]) * g[2]) * invsum32;
+}
+
+// SH backward (backward_kernels.py:297-536).  Writes the (K,3) gradient row
+// and returns the mean gradient through the view direction.
+__device__ void sh_backward(const gsb_preprocess_bwd_args& a, int idx, const float mean[3],
+                            const float cam[3], const float grad_rgb[3], unsigned clamp_bits,
+                            float gmean[3]) {
+  const int K = a.sh_coeffs;
+  const int degree = a.sh_degree;
+  float g[3];
+#pragma unroll
+  for (int c = 0; c < 3; ++c) g[c] = grad_rgb[c] * (1.0f - (float)((clamp_bits >> c) & 1u));
+  gmean[0] = gmean[1] = gmean[2] = 0.0f;
+  float* out = a.grad_sh + (size_t)idx * K * 3;
+  const bool acc = a.accumulate != 0;
+  if (g[0] == 0.0f && g[1] == 0.0f && g[2] == 0.0f) {
+    // Zero colour gradient: every SH gradient and the direction term vanish.
+    if (!acc)
+      for (int k = 0; k < K * 3; ++k) out[k] = 0.0f;
+    return;
+  }
+  const float* sp = a.sh + (size_t)idx * K * 3;
+  const float dir[3] = {mean[0] - cam[0], mean[1] - cam[1], mean[2] - cam[2]};
+  const float len_sq = dir[0] * dir[0] + dir[1] * dir[1] + dir[2] * dir[2];
+  const float inv_len = 1.0f / sqrtf(fmx(len_sq, 1.0e-20f));
+  const float x = dir[0] * inv_len, y = dir[1] * inv_len, z = dir[2] * inv_len;
+  float dx[3] = {0, 0, 0}, dy[3] = {0, 0, 0}, dz[3] = {0, 0, 0};
+  float w[16];
+#pragma unroll
+  for (int k = 0; k < 16; ++k) w[k] = 0.0f;
+  int used = 0;
+  if (K > 0) {
+    w[0] = SH_C0;
+    used = 1;
+  }
+  if (degree > 0 && K > 3) {
+    const float c1 = SH_C1;
+    w[1] = -c1 * y;
+    w[2] = c1 * z;
+    w[3] = -c1 * x;
+    used = 4;
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+      dx[c] = -c1 * __ldg(sp + 9 + c);
+      dy[c] = -c1 * __ldg(sp + 3 + c);
+      dz[c] = c1 * __ldg(sp + 6 + c);
+    }
+    if (degree > 1 && K > 8) {
+      const float xx = x * x, yy = y * y, zz = z * z, xy = x * y, yz = y * z, xz = x * z;
+      w[4] = SH_C2[0] * xy;
+      w[5] = SH_C2[1] * yz;
+      w[6] = SH_C2[2] * (2.0f * zz - xx - yy);
+      w[7] = SH_C2[3] * xz;
+      w[8] = SH_C2[4] * (xx - yy);
+      used = 9;
+#pragma unroll
+      for (int c = 0; c < 3; ++c) {
+        const float s4 = __ldg(sp + 12 + c), s5 = __ldg(sp + 15 + c), s6 = __ldg(sp + 18 + c);
+        const float s7 = __ldg(sp + 21 + c), s8 = __ldg(sp + 24 + c);
+        dx[c] = dx[c] + (SH_C2[0] * y) * s4 + (SH_C2[2] * (-2.0f * x)) * s6 + (SH_C2[3] * z) * s7 +
+                (SH_C2[4] * (2.0f * x)) * s8;
+        dy[c] = dy[c] + (SH_C2[0] * x) * s4 + (SH_C2[1] * z) * s5 + (SH_C2[2] * (-2.0f * y)) * s6 +
+                (SH_C2[4] * (-2.0f * y)) * s8;
+        dz[c] = dz[c] + (SH_C2[1] * y) * s5 + (SH_C2[2] * (4.0f * z)) * s6 + (SH_C2[3] * x) * s7;
+      }
+      if (degree > 2 && K > 15) {
+        w[9] = SH_C3[0] * y * (3.0f * xx - yy);
+        w[10] = SH_C3[1] * xy * z;
+        w[11] = SH_C3[2] * y * (4.0f * zz - xx - yy);
+        w[12] = SH_C3[3] * z * (2.0f * zz - 3.0f * xx - 3.0f * yy);
+        w[13] = SH_C3[4] * x * (4.0f * zz - xx - yy);
+        w[14] = SH_C3[5] * z * (xx - yy);
+        w[15] = SH_C3[6] * x * (xx - 3.0f * yy);
+        used = 16;
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+          const float s9 = __ldg(sp + 27 + c), s10 = __ldg(sp + 30 + c), s11 = __ldg(sp + 33 + c);
+          const float s12 = __ldg(sp + 36 + c), s13 = __ldg(sp + 39 + c);
+          const float s14 = __ldg(sp + 42 + c), s15 = __ldg(sp + 45 + c);
+          dx[c] = dx[c] + (SH_C3[0] * (6.0f * xy)) * s9 + (SH_C3[1] * yz) * s10 +
+                  (SH_C3[2] * (-2.0f * xy)) * s11 + (SH_C3[3] * (-6.0f * xz)) * s12 +
+                  (SH_C3[4] * (-3.0f * xx + 4.0f * zz - yy)) * s13 + (SH_C3[5] * (2.0f * xz)) * s14 +
+                  (SH_C3[6] * (3.0f * (xx - yy))) * s15;
+          dy[c] = dy[c] + (SH_C3[0] * (3.0f * (xx - yy))) * s9 + (SH_C3[1] * xz) * s10 +
+                  (SH_C3[2] * (-3.0f * yy + 4.0f * zz - xx)) * s11 + (SH_C3[3] * (-6.0f * yz)) * s12 +
+                  (SH_C3[4] * (-2.0f * xy)) * s13 + (SH_C3[5] * (-2.0f * yz)) * s14 +
+                  (SH_C3[6] * (-6.0f * xy)) * s15;
+          dz[c] = dz[c] + (SH_C3[1] * xy) * s10 + (SH_C3[2] * (8.0f * yz)) * s11 +
+                  (SH_C3[3] * (3.0f * (2.0f * zz - xx - yy))) * s12 + (SH_C3[4] * (8.0f * xz)) * s13 +
+                  (SH_C3[5] * (xx - yy)) * s14;
+        }
+      }
+    }
+  }
+  // Gradient rows: w[k] * g for the coefficients the degree uses, 0 above.
+  if (K == 16 && !acc && (reinterpret_cast<uintptr_t>(out) & 15) == 0) {
+    float4* o4 = reinterpret_cast<float4*>(out);
+    float row[48];
+#pragma unroll
+    for (int k = 0; k < 16; ++k)
+#pragma unroll
+      for (int c = 0; c < 3; ++c) row[k * 3 + c] = w[k] * g[c];
+#pragma unroll
+    for (int q = 0; q < 12; ++q)
+      o4[q] = make_float4(row[q * 4], row[q * 4 + 1], row[q * 4 + 2], row[q * 4 + 3]);
+  } else {
+    for (int k = 0; k < K; ++k)
+      for (int c = 0; c < 3; ++c) {
+        const float gv = k < used ? w[k] * g[c] : 0.0f;
+        store_or_add(out + k * 3 + c, gv, acc);
+      }
+  }
+  const float ddir[3] = {dx[0] * g[0] + dx[1] * g[1] + dx[2] * g[2],
+                         dy[0] * g[0] + dy[1] * g[1] + dy[2] * g[2],
+                         dz[0] * g[0] + dz[1] * g[1] + dz[2] * g[2]};
+  dnormvdv(dir, ddir, gmean);
+}
+
+template <bool PRECOMP>
+__global__ void __launch_bounds__(256) preprocess_bwd_kernel(const gsb_preprocess_bwd_args a) {
+  __shared__ float s_view[16], s_proj[16], s_cam[3];
+  if (threadIdx.x < 16) {
+    s_view[threadIdx.x] = a.viewmatrix[threadIdx.x];
+    s_proj[threadIdx.x] = a.projmatrix[threadIdx.x];
+  } else if (threadIdx.x < 19) {
+    s_cam[threadIdx.x - 16] = a.campos ? a.campos[threadIdx.x - 16] : 0.0f;
+  }
+  __syncthreads();
+  const int tid = blockIdx.x * blockDim.x + threadIdx.x;
+  if (tid >= a.P) return;
+  const float* pr = s_proj;
+  const float* vf = s_view;
+  const bool acc = a.accumulate != 0;
+  const float mean[3] = {a.means[tid * 3], a.means[tid * 3 + 1], a.means[tid * 3 + 2]};
+  const int rad = a.radii[tid];
+  const float4* ga4 = reinterpret_cast<const float4*>(a.grad_acc) + (size_t)tid * 3;
+  const float4 gq0 = ga4[0], gq1 = ga4[1], gq2 = ga4[2];
+  const float rgx = gq0.x, rgy = gq0.y, rgd = gq0.z;
+  const float rco[4] = {gq1.x, gq1.y, gq1.z, gq1.w};
+  const float rrgb[3] = {gq2.x, gq2.y, gq2.z};
+
+  float gxy0 = rgx, gxy1 = rgy;
+  if (rad > 0) {
+    gxy0 = gxy0 + a.grad_proj_2d[tid * 2];
+    gxy1 = gxy1 + a.grad_proj_2d[tid * 2 + 1];
+  }
+  const float hom_x = pr[0] * mean[0] + pr[4] * mean[1] + pr[8] * mean[2] + pr[12];
+  const float hom_y = pr[1] * mean[0] + pr[5] * mean[1] + pr[9] * mean[2] + pr[13];
+  const float hom_w = pr[3] * mean[0] + pr[7] * mean[1] + pr[11] * mean[2] + pr[15];
+  const float inv_w = 1.0f / (hom_w + 1.0e-7f);
+  float pm_x, pm_y, pm_z;
+  if (!PRECOMP) {
+    // backward_kernels.py:89-112
+    const float inv_w2 = inv_w * inv_w;
+    const float gh = hom_x * gxy0 + hom_y * gxy1;
+    pm_x = inv_w * (pr[0] * gxy0 + pr[1] * gxy1) - pr[3] * inv_w2 * gh;
+    pm_y = inv_w * (pr[4] * gxy0 + pr[5] * gxy1) - pr[7] * inv_w2 * gh;
+    pm_z = inv_w * (pr[8] * gxy0 + pr[9] * gxy1) - pr[11] * inv_w2 * gh;
+  } else {
+    // backward_kernels.py:853-866
+    const float mul1 = hom_x * inv_w * inv_w;
+    const float mul2 = hom_y * inv_w * inv_w;
+    pm_x = (pr[0] * inv_w - pr[3] * mul1) * gxy0 + (pr[1] * inv_w - pr[3] * mul2) * gxy1;
+    pm_y = (pr[4] * inv_w - pr[7] * mul1) * gxy0 + (pr[5] * inv_w - pr[7] * mul2) * gxy1;
+    pm_z = (pr[8] * inv_w - pr[11] * mul1) * gxy0 + (pr[9] * inv_w - pr[11] * mul2) * gxy1;
+  }
+  const float zz = vf[2] * mean[0] + vf[6] * mean[1] + vf[10] * mean[2] + vf[14];
+  pm_x = pm_x + (vf[2] - vf[3] * zz) * rgd;
+  pm_y = pm_y + (vf[6] - vf[7] * zz) * rgd;
+  pm_z = pm_z + (vf[10] - vf[11] * zz) * rgd;
+
+  float gcm[3] = {0.0f, 0.0f, 0.0f};
+  float gs[3] = {0.0f, 0.0f, 0.0f}, gr[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  float gc3[6] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+  if (rad > 0) {
+    const float x = vf[0] * mean[0] + vf[4] * mean[1] + vf[8] * mean[2] + vf[12];
+    const float y = vf[1] * mean[0] + vf[5] * mean[1] + vf[9] * mean[2] + vf[13];
+    const float z = zz;
+    const float limx = 1.3f * a.tanfovx, limy = 1.3f * a.tanfovy;
+    const float w00 = vf[0], w01 = vf[1], w02 = vf[2], w10 = vf[4], w11 = vf[5], w12 = vf[6];
+    const float w20 = vf[8], w21 = vf[9], w22 = vf[10];
+    const float tc0 = rco[0] + a.grad_conic_2d[tid * 3 + 0];
+    const float tc1 = rco[1] + a.grad_conic_2d[tid * 3 + 1];
+    const float tc2 = rco[2] + a.grad_conic_2d[tid * 3 + 2];
+    const float gi0 = a.grad_conic_2d_inv[tid * 3 + 0];
+    const float gi1 = a.grad_conic_2d_inv[tid * 3 + 1];
+    const float gi2 = a.grad_conic_2d_inv[tid * 3 + 2];
+    if (!PRECOMP) {
+      // backward_kernels.py:124-287
+      const float tz_inv = 1.0f / (z + 1.0e-7f);
+      const float txtz = x * tz_inv, tytz = y * tz_inv;
+      float x_mul = 1.0f, y_mul = 1.0f;
+      if (txtz < -limx || txtz > limx) x_mul = 0.0f;
+      if (tytz < -limy || tytz > limy) y_mul = 0.0f;
+      const float tx = fclamp(txtz, -limx, limx), ty = fclamp(tytz, -limy, limy);
+      const float j00 = a.focal_x * tz_inv;
+      const float j02 = -j00 * tx;
+      const float j11 = a.focal_y * tz_inv;
+      const float j12 = -j11 * ty;
+      const float t00 = w00 * j00 + w02 * j02, t10 = w10 * j00 + w12 * j02,
+                  t20 = w20 * j00 + w22 * j02;
+      const float t01 = w01 * j11 + w02 * j12, t11 = w11 * j11 + w12 * j12,
+                  t21 = w21 * j11 + w22 * j12;
+      const float s0 = a.scales[tid * 3 + 0] * a.scale_modifier;
+      const float s1 = a.scales[tid * 3 + 1] * a.scale_modifier;
+      const float s2 = a.scales[tid * 3 + 2] * a.scale_modifier;
+      const float4 q = reinterpret_cast<const float4*>(a.rotations)[tid];
+      const float rr = q.x, xq = q.y, yq = q.z, zq = q.w;
+      const float r00 = 1.0f - 2.0f * (yq * yq + zq * zq);
+      const float r01 = 2.0f * (xq * yq + rr * zq);
+      const float r02 = 2.0f * (xq * zq - rr * yq);
+      const float r10 = 2.0f * (xq * yq - rr * zq);
+      const float r11 = 1.0f - 2.0f * (xq * xq + zq * zq);
+      const float r12 = 2.0f * (yq * zq + rr * xq);
+      const float r20 = 2.0f * (xq * zq + rr * yq);
+      const float r21 = 2.0f * (yq * zq - rr * xq);
+      const float r22 = 1.0f - 2.0f * (xq * xq + yq * yq);
+      const float m00 = s0 * r00, m01 = s0 * r01, m02 = s0 * r02;
+      const float m10 = s1 * r10, m11 = s1 * r11, m12 = s1 * r12;
+      const float m20 = s2 * r20, m21 = s2 * r21, m22 = s2 * r22;
+      const float v00 = m00 * m00 + m10 * m10 + m20 * m20;
+      const float v01 = m00 * m01 + m10 * m11 + m20 * m21;
+      const float v02 = m00 * m02 + m10 * m12 + m20 * m22;
+      const float v11 = m01 * m01 + m11 * m11 + m21 * m21;
+      const float v12 = m01 * m02 + m11 * m12 + m21 * m22;
+      const float v22 = m02 * m02 + m12 * m12 + m22 * m22;
+      const float vt0x = v00 * t00 + v01 * t10 + v02 * t20;
+      const float vt0y = v01 * t00 + v11 * t10 + v12 * t20;
+      const float vt0z = v02 * t00 + v12 * t10 + v22 * t20;
+      const float vt1x = v00 * t01 + v01 * t11 + v02 * t21;
+      const float vt1y = v01 * t01 + v11 * t11 + v12 * t21;
+      const float vt1z = v02 * t01 + v12 * t11 + v22 * t21;
+      const float filt = 0.0f;
+      const float aa = t00 * vt0x + t10 * vt0y + t20 * vt0z + 0.3f + filt;
+      const float bb = t00 * vt1x + t10 * vt1y + t20 * vt1z;
+      const float cc = t01 * vt1x + t11 * vt1y + t21 * vt1z + 0.3f + filt;
+      const float denom = aa * cc - bb * bb;
+      const float denom2inv = 1.0f / (denom * denom + 1.0e-7f);
+      float dL_da = denom2inv * (-cc * cc * tc0 + 2.0f * bb * cc * tc1 - bb * bb * tc2);
+      float dL_dc = denom2inv * (-aa * aa * tc2 + 2.0f * aa * bb * tc1 - bb * bb * tc0);
+      float dL_db = denom2inv * 2.0f * (bb * cc * tc0 - (aa * cc + bb * bb) * tc1 + aa * bb * tc2);
+      dL_da = dL_da + gi0;
+      dL_db = dL_db + gi1;
+      dL_dc = dL_dc + gi2;
+      const float gc0 = t00 * t00 * dL_da + t00 * t01 * dL_db + t01 * t01 * dL_dc;
+      const float gc3v = t10 * t10 * dL_da + t10 * t11 * dL_db + t11 * t11 * dL_dc;
+      const float gc5 = t20 * t20 * dL_da + t20 * t21 * dL_db + t21 * t21 * dL_dc;
+      const float gc1 = 2.0f * t00 * t10 * dL_da + (t00 * t11 + t01 * t10) * dL_db + 2.0f * t01 * t11 * dL_dc;
+      const float gc2 = 2.0f * t00 * t20 * dL_da + (t00 * t21 + t01 * t20) * dL_db + 2.0f * t01 * t21 * dL_dc;
+      const float gc4 = 2.0f * t10 * t20 * dL_da + (t10 * t21 + t11 * t20) * dL_db + 2.0f * t11 * t21 * dL_dc;
+      const float dT00 = 2.0f * vt0x * dL_da + vt1x * dL_db;
+      const float dT01 = 2.0f * vt0y * dL_da + vt1y * dL_db;
+      const float dT02 = 2.0f * vt0z * dL_da + vt1z * dL_db;
+      const float dT10 = vt0x * dL_db + 2.0f * vt1x * dL_dc;
+      const float dT11 = vt0y * dL_db + 2.0f * vt1y * dL_dc;
+      const float dT12 = vt0z * dL_db + 2.0f * vt1z * dL_dc;
+      const float dJ00 = w00 * dT00 + w10 * dT01 + w20 * dT02;
+      const float dJ02 = w02 * dT00 + w12 * dT01 + w22 * dT02;
+      const float dJ11 = w01 * dT10 + w11 * dT11 + w21 * dT12;
+      const float dJ12 = w02 * dT10 + w12 * dT11 + w22 * dT12;
+      const float dL_dtx = x_mul * -j00 * tz_inv * dJ02;
+      const float dL_dty = y_mul * -j11 * tz_inv * dJ12;
+      const float dL_dtz = -(j00 * dJ00 + j11 * dJ11 + 2.0f * j02 * dJ02 + 2.0f * j12 * dJ12) * tz_inv;
+      gcm[0] = w00 * dL_dtx + w01 * dL_dty + w02 * dL_dtz;
+      gcm[1] = w10 * dL_dtx + w11 * dL_dty + w12 * dL_dtz;
+      gcm[2] = w20 * dL_dtx + w21 * dL_dty + w22 * dL_dtz;
+      const float sg00 = gc0, sg01 = 0.5f * gc1, sg02 = 0.5f * gc2, sg11 = gc3v, sg12 = 0.5f * gc4,
+                  sg22 = gc5;
+      const float dM00 = 2.0f * (m00 * sg00 + m01 * sg01 + m02 * sg02);
+      const float dM01 = 2.0f * (m00 * sg01 + m01 * sg11 + m02 * sg12);
+      const float dM02 = 2.0f * (m00 * sg02 + m01 * sg12 + m02 * sg22);
+      const float dM10 = 2.0f * (m10 * sg00 + m11 * sg01 + m12 * sg02);
+      const float dM11 = 2.0f * (m10 * sg01 + m11 * sg11 + m12 * sg12);
+      const float dM12 = 2.0f * (m10 * sg02 + m11 * sg12 + m12 * sg22);
+      const float dM20 = 2.0f * (m20 * sg00 + m21 * sg01 + m22 * sg02);
+      const float dM21 = 2.0f * (m20 * sg01 + m21 * sg11 + m22 * sg12);
+      const float dM22 = 2.0f * (m20 * sg02 + m21 * sg12 + m22 * sg22);
+      gs[0] = a.scale_modifier * (dM00 * r00 + dM01 * r01 + dM02 * r02);
+      gs[1] = a.scale_modifier * (dM10 * r10 + dM11 * r11 + dM12 * r12);
+      gs[2] = a.scale_modifier * (dM20 * r20 + dM21 * r21 + dM22 * r22);
+      const float dR00 = dM00 * s0, dR01 = dM01 * s0, dR02 = dM02 * s0;
+      const float dR10 = dM10 * s1, dR11 = dM11 * s1, dR12 = dM12 * s1;
+      const float dR20 = dM20 * s2, dR21 = dM21 * s2, dR22 = dM22 * s2;
+      gr[0] = 2.0f * zq * (dR01 - dR10) + 2.0f * yq * (dR20 - dR02) + 2.0f * xq * (dR12 - dR21);
+      gr[1] = 2.0f * yq * (dR10 + dR01) + 2.0f * zq * (dR20 + dR02) + 2.0f * rr * (dR12 - dR21) -
+              4.0f * xq * (dR22 + dR11);
+      gr[2] = 2.0f * xq * (dR10 + dR01) + 2.0f * rr * (dR20 - dR02) + 2.0f * zq * (dR12 + dR21) -
+              4.0f * yq * (dR22 + dR00);
+      gr[3] = 2.0f * rr * (dR01 - dR10) + 2.0f * xq * (dR20 + dR02) + 2.0f * yq * (dR12 + dR21) -
+              4.0f * zq * (dR11 + dR00);
+    } else {
+      // backward_kernels.py:731-840
+      const float* c3 = a.cov3d_precomp + (size_t)tid * 6;
+      const float txtz = x / z, tytz = y / z;
+      const float tx = fclamp(txtz, -limx, limx) * z;
+      const float ty = fclamp(tytz, -limy, limy) * z;
+      float xm = 1.0f, ym = 1.0f;
+      if (txtz < -limx || txtz > limx) xm = 0.0f;
+      if (tytz < -limy || tytz > limy) ym = 0.0f;
+      const float j00 = a.focal_x / z;
+      const float j02 = -(a.focal_x * tx) / (z * z);
+      const float j11 = a.focal_y / z;
+      const float j12 = -(a.focal_y * ty) / (z * z);
+      const float t00 = w00 * j00 + w02 * j02, t10 = w10 * j00 + w12 * j02,
+                  t20 = w20 * j00 + w22 * j02;
+      const float t01 = w01 * j11 + w02 * j12, t11 = w11 * j11 + w12 * j12,
+                  t21 = w21 * j11 + w22 * j12;
+      const float v00 = c3[0], v01 = c3[1], v02 = c3[2], v11 = c3[3], v12 = c3[4], v22 = c3[5];
+      const float vt0x = v00 * t00 + v01 * t10 + v02 * t20;
+      const float vt0y = v01 * t00 + v11 * t10 + v12 * t20;
+      const float vt0z = v02 * t00 + v12 * t10 + v22 * t20;
+      const float vt1x = v00 * t01 + v01 * t11 + v02 * t21;
+      const float vt1y = v01 * t01 + v11 * t11 + v12 * t21;
+      const float vt1z = v02 * t01 + v12 * t11 + v22 * t21;
+      const float filt = 0.0f;
+      const float aa = t00 * vt0x + t10 * vt0y + t20 * vt0z + 0.3f + filt;
+      const float bb = t00 * vt1x + t10 * vt1y + t20 * vt1z;
+      const float cc = t01 * vt1x + t11 * vt1y + t21 * vt1z + 0.3f + filt;
+      const float denom = aa * cc - bb * bb;
+      const float d2i = 1.0f / (denom * denom + 1.0e-7f);
+      float dL_da = d2i * (-cc * cc * tc0 + 2.0f * bb * cc * tc1 + (denom - aa * cc) * tc2);
+      float dL_dc = d2i * (-aa * aa * tc2 + 2.0f * aa * bb * tc1 + (denom - aa * cc) * tc0);
+      float dL_db = d2i * 2.0f * (bb * cc * tc0 - (denom + 2.0f * bb * bb) * tc1 + aa * bb * tc2);
+      dL_da = dL_da + gi0;
+      dL_db = dL_db + gi1;
+      dL_dc = dL_dc + gi2;
+      gc3[0] = t00 * t00 * dL_da + t00 * t01 * dL_db + t01 * t01 * dL_dc;
+      gc3[3] = t10 * t10 * dL_da + t10 * t11 * dL_db + t11 * t11 * dL_dc;
+      gc3[5] = t20 * t20 * dL_da + t20 * t21 * dL_db + t21 * t21 * dL_dc;
+      gc3[1] = 2.0f * t00 * t10 * dL_da + (t00 * t11 + t01 * t10) * dL_db + 2.0f * t01 * t11 * dL_dc;
+      gc3[2] = 2.0f * t00 * t20 * dL_da + (t00 * t21 + t01 * t20) * dL_db + 2.0f * t01 * t21 * dL_dc;
+      gc3[4] = 2.0f * t10 * t20 * dL_da + (t10 * t21 + t11 * t20) * dL_db + 2.0f * t11 * t21 * dL_dc;
+      const float dT00 = 2.0f * (t00 * v00 + t10 * v01 + t20 * v02) * dL_da + (t01 * v00 + t11 * v01 + t21 * v02) * dL_db;
+      const float dT01 = 2.0f * (t00 * v01 + t10 * v11 + t20 * v12) * dL_da + (t01 * v01 + t11 * v11 + t21 * v12) * dL_db;
+      const float dT02 = 2.0f * (t00 * v02 + t10 * v12 + t20 * v22) * dL_da + (t01 * v02 + t11 * v12 + t21 * v22) * dL_db;
+      const float dT10 = 2.0f * (t01 * v00 + t11 * v01 + t21 * v02) * dL_dc + (t00 * v00 + t10 * v01 + t20 * v02) * dL_db;
+      const float dT11 = 2.0f * (t01 * v01 + t11 * v11 + t21 * v12) * dL_dc + (t00 * v01 + t10 * v11 + t20 * v12) * dL_db;
+      const float dT12 = 2.0f * (t01 * v02 + t11 * v12 + t21 * v22) * dL_dc + (t00 * v02 + t10 * v12 + t20 * v22) * dL_db;
+      const float dJ00 = w00 * dT00 + w10 * dT01 + w20 * dT02;
+      const float dJ02 = w02 * dT00 + w12 * dT01 + w22 * dT02;
+      const float dJ11 = w01 * dT10 + w11 * dT11 + w21 * dT12;
+      const float dJ12 = w02 * dT10 + w12 * dT11 + w22 * dT12;
+      const float tz_inv = 1.0f / z;
+      const float tz2 = tz_inv * tz_inv;
+      const float tz3 = tz2 * tz_inv;
+      const float dL_dtx = xm * -a.focal_x * tz2 * dJ02;
+      const float dL_dty = ym * -a.focal_y * tz2 * dJ12;
+      const float dL_dtz = -a.focal_x * tz2 * dJ00 - a.focal_y * tz2 * dJ11 +
+                           (2.0f * a.focal_x * tx) * tz3 * dJ02 + (2.0f * a.focal_y * ty) * tz3 * dJ12;
+      gcm[0] = vf[0] * dL_dtx + vf[1] * dL_dty + vf[2] * dL_dtz;
+      gcm[1] = vf[4] * dL_dtx + vf[5] * dL_dty + vf[6] * dL_dtz;
+      gcm[2] = vf[8] * dL_dtx + vf[9] * dL_dty + vf[10] * dL_dtz;
+    }
+  }
+  float gsm[3] = {0.0f, 0.0f, 0.0f};
+  if (a.sh) {
+    const unsigned clamp_bits =
+        __float_as_uint(reinterpret_cast<const float4*>(a.records)[(size_t)tid * 3 + 1].w);
+    sh_backward(a, tid, mean, s_cam, rrgb, clamp_bits, gsm);
+  }
+  float m0 = pm_x + gcm[0], m1 = pm_y + gcm[1], m2 = pm_z + gcm[2];
+  if (a.sh) {
+    m0 = m0 + gsm[0];
+    m1 = m1 + gsm[1];
+    m2 = m2 + gsm[2];
+  }
+  store_or_add(a.grad_means3d + tid * 3 + 0, m0, acc);
+  store_or_add(a.grad_means3d + tid * 3 + 1, m1, acc);
+  store_or_add(a.grad_means3d + tid * 3 + 2, m2, acc);
+  if (a.grad_means2d) {
+    store_or_add(a.grad_means2d + tid * 3 + 0, rgx, acc);
+    store_or_add(a.grad_means2d + tid * 3 + 1, rgy, acc);
+    store_or_add(a.grad_means2d + tid * 3 + 2, 0.0f, acc);
+  }
+  if (!PRECOMP) {
+    if (a.grad_scales)
+      for (int k = 0; k < 3; ++k) store_or_add(a.grad_scales + tid * 3 + k, gs[k], acc);
+    if (a.grad_rotations)
+      for (int k = 0; k < 4; ++k) store_or_add(a.grad_rotations + tid * 4 + k, gr[k], acc);
+  } else if (a.grad_cov3d) {
+    for (int k = 0; k < 6; ++k) store_or_add(a.grad_cov3d + tid * 6 + k, gc3[k], acc);
+  }
+  if (a.grad_opacity) store_or_add(a.grad_opacity + tid, rco[3], acc);
+  if (a.grad_colors)
+    for (int k = 0; k < 3; ++k) store_or_add(a.grad_colors + tid * 3 + k, rrgb[k], acc);
+}
+
+}  // namespace
+}  // namespace gsb
+
+using namespace gsb;
+
+GSB_EXPORT int gsb_preprocess_bwd(const gsb_preprocess_bwd_args* a, void* stream) {
+  if (!a || a->P < 0 || a->W <= 0 || a->H <= 0) {
+    set_error("gsb_preprocess_bwd: invalid sizes");
+    return GSB_ERR_INVALID;
+  }
+  if (a->P == 0) return GSB_OK;
+  const bool precomp = a->cov3d_precomp != nullptr;
+  if (!precomp && (!a->scales || !a->rotations)) {
+    set_error("gsb_preprocess_bwd: scales/rotations or cov3d_precomp required");
+    return GSB_ERR_INVALID;
+  }
+  if (!a->means || !a->radii || !a->viewmatrix || !a->projmatrix || !a->records ||
+      !a->grad_acc || !a->grad_proj_2d || !a->grad_conic_2d || !a->grad_conic_2d_inv ||
+      !a->grad_means3d || (a->sh && (!a->grad_sh || !a->campos || a->sh_coeffs <= 0))) {
+    set_error("gsb_preprocess_bwd: null pointer argument");
+    return GSB_ERR_INVALID;
+  }
+  if ((reinterpret_cast<uintptr_t>(a->grad_acc) & 15) || (reinterpret_cast<uintptr_t>(a->records) & 15) ||
+      (!precomp && (reinterpret_cast<uintptr_t>(a->rotations) & 15))) {
+    set_error("gsb_preprocess_bwd: grad_acc/records/rotations need 16-byte alignment");
+    return GSB_ERR_INVALID;
+  }
+  cudaStream_t s = (cudaStream_t)stream;
+  if (precomp)
+    preprocess_bwd_kernel<true><<<div_up(a->P, 256), 256, 0, s>>>(*a);
+  else
+    preprocess_bwd_kernel<false><<<div_up(a->P, 256), 256, 0, s>>>(*a);
+  return check_launch("preprocess_bwd_kernel");
+}

@@ -1,0 +1,283 @@
+// radix_sort.cuh -- stable LSD radix sort of (uint32 key, uint32 value) pairs.
+//
+// Replaces Warp's wp.utils.radix_sort_pairs (called from gswarp
+// memory.py:571-600 and knn.py:337-341) with a single-pass-per-digit
+// ("onesweep") design for sm_100a:
+//   1. one histogram kernel computes the 8-bit digit histograms of every
+//      pass in a single read of the keys (warp-aggregated shared atomics);
+//   2. a tiny kernel turns them into per-pass bin bases;
+//   3. each pass is ONE kernel: a CTA claims the next 3840-key tile through
+//      an atomic counter, ranks its keys stably per warp (__match_any_sync),
+//      publishes its per-digit counts, resolves its global offsets by
+//      decoupled look-back over the preceding tiles, stages the tile in
+//      digit order in shared memory and writes it out in runs.
+// Tiles are claimed in launch order, so every tile a CTA waits on belongs to
+// a CTA that is already running; each look-back spin is nevertheless bounded
+// (SPIN_LIMIT) and reports ERR_LOOKBACK_TIMEOUT instead of hanging.
+#pragma once
+
+#include <algorithm>
+
+#include "gsb_common.cuh"
+
+namespace gsb {
+namespace radix {
+// Internal linkage: every translation unit that sorts gets its own copy.
+namespace {
+
+constexpr int RADIX_BITS = 8;
+constexpr int RADIX = 1 << RADIX_BITS;
+constexpr int THREADS = 256;
+constexpr int WARPS = THREADS / 32;
+constexpr int ITEMS = 15;
+constexpr int TILE_KEYS = THREADS * ITEMS;  // 3840
+constexpr int MAX_PASSES = 4;
+
+constexpr unsigned long long FLAG_AGG = 1ull << 62;
+constexpr unsigned long long FLAG_INC = 2ull << 62;
+constexpr unsigned long long VALUE_MASK = (1ull << 62) - 1;
+
+__device__ __forceinline__ unsigned long long ld_volatile(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_volatile(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Exclusive scan of one value per thread across a 256-thread CTA.
+__device__ __forceinline__ unsigned block_exclusive_scan(unsigned v, unsigned* s_warp,
+                                                         unsigned* total_out) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  unsigned x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    unsigned y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) s_warp[warp] = x;
+  __syncthreads();
+  unsigned wpre = 0, tot = 0;
+#pragma unroll
+  for (int w = 0; w < WARPS; ++w) {
+    unsigned t = s_warp[w];
+    if (w < warp) wpre += t;
+    tot += t;
+  }
+  __syncthreads();
+  if (total_out) *total_out = tot;
+  return wpre + x - v;
+}
+
+__global__ void __launch_bounds__(THREADS) histogram_kernel(const unsigned* __restrict__ keys,
+                                                            int n, int passes,
+                                                            unsigned* __restrict__ hist) {
+  __shared__ unsigned s_hist[MAX_PASSES][RADIX];
+  for (int i = threadIdx.x; i < MAX_PASSES * RADIX; i += THREADS) (&s_hist[0][0])[i] = 0u;
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const long long warps_total = (long long)gridDim.x * WARPS;
+  const long long warp_id = (long long)blockIdx.x * WARPS + (threadIdx.x >> 5);
+  for (long long base = warp_id * 32; base < n; base += warps_total * 32) {
+    const long long i = base + lane;
+    const bool valid = i < n;
+    const unsigned k = valid ? keys[i] : 0u;
+    for (int p = 0; p < passes; ++p) {
+      const unsigned d = valid ? (k >> (p * RADIX_BITS)) & (RADIX - 1) : (unsigned)RADIX;
+      const unsigned peers = __match_any_sync(0xffffffffu, d);
+      if (valid && lane == __ffs(peers) - 1) atomicAdd(&s_hist[p][d], (unsigned)__popc(peers));
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < passes * RADIX; i += THREADS) {
+    const unsigned c = (&s_hist[0][0])[i];
+    if (c) atomicAdd(&hist[i], c);
+  }
+}
+
+__global__ void __launch_bounds__(THREADS) bin_base_kernel(const unsigned* __restrict__ hist,
+                                                           unsigned* __restrict__ bin_base) {
+  __shared__ unsigned s_warp[WARPS];
+  const int p = blockIdx.x;
+  const unsigned c = hist[p * RADIX + threadIdx.x];
+  bin_base[p * RADIX + threadIdx.x] = block_exclusive_scan(c, s_warp, nullptr);
+}
+
+template <bool HAS_VALS>
+__global__ void __launch_bounds__(THREADS) onesweep_kernel(
+    const unsigned* __restrict__ keys_in, const unsigned* __restrict__ vals_in,
+    unsigned* __restrict__ keys_out, unsigned* __restrict__ vals_out, int n, int shift,
+    const unsigned* __restrict__ bin_base, unsigned long long* __restrict__ lookback,
+    unsigned* __restrict__ tile_counter, long long* __restrict__ err) {
+  __shared__ unsigned s_keys[TILE_KEYS];
+  __shared__ unsigned s_vals[HAS_VALS ? TILE_KEYS : 1];
+  __shared__ unsigned s_warp_hist[WARPS][RADIX];
+  __shared__ unsigned s_digit_start[RADIX];
+  __shared__ unsigned s_global[RADIX];
+  __shared__ unsigned s_scan[WARPS];
+  __shared__ int s_tile;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) s_tile = (int)atomicAdd(tile_counter, 1u);
+  for (int i = tid; i < WARPS * RADIX; i += THREADS) (&s_warp_hist[0][0])[i] = 0u;
+  __syncthreads();
+  const int tile = s_tile;
+  const long long base = (long long)tile * TILE_KEYS + (long long)warp * (ITEMS * 32);
+
+  unsigned key[ITEMS], val[ITEMS], rank[ITEMS];
+#pragma unroll
+  for (int i = 0; i < ITEMS; ++i) {
+    const long long pos = base + i * 32 + lane;
+    const bool valid = pos < n;
+    key[i] = valid ? keys_in[pos] : 0xFFFFFFFFu;
+    if (HAS_VALS) val[i] = valid ? vals_in[pos] : 0u;
+    rank[i] = valid ? 0u : 0xFFFFFFFFu;  // invalid marker
+  }
+  // Stable warp-local ranking: round i holds 32 consecutive keys.
+#pragma unroll
+  for (int i = 0; i < ITEMS; ++i) {
+    const bool valid = rank[i] != 0xFFFFFFFFu;
+    const unsigned d = valid ? (key[i] >> shift) & (RADIX - 1) : (unsigned)RADIX;
+    const unsigned peers = __match_any_sync(0xffffffffu, d);
+    unsigned old = 0;
+    if (valid) {
+      old = s_warp_hist[warp][d];
+      rank[i] = old + __popc(peers & lanemask_lt());
+    }
+    __syncwarp();
+    if (valid && lane == __ffs(peers) - 1) s_warp_hist[warp][d] = old + __popc(peers);
+    __syncwarp();
+  }
+  __syncthreads();
+
+  // Thread `tid` owns digit `tid`: per-warp exclusive offsets and tile count.
+  unsigned total = 0;
+#pragma unroll
+  for (int w = 0; w < WARPS; ++w) {
+    const unsigned c = s_warp_hist[w][tid];
+    s_warp_hist[w][tid] = total;
+    total += c;
+  }
+  unsigned long long* my_slot = lookback + (size_t)tile * RADIX + tid;
+  st_volatile(my_slot, (tile == 0 ? FLAG_INC : FLAG_AGG) | (unsigned long long)total);
+  s_digit_start[tid] = block_exclusive_scan(total, s_scan, nullptr);
+
+  unsigned long long excl = 0;
+  if (tile > 0) {
+    int t = tile - 1;
+    int spins = 0;
+    while (true) {
+      const unsigned long long v = ld_volatile(lookback + (size_t)t * RADIX + tid);
+      const unsigned long long flag = v & ~VALUE_MASK;
+      if (flag == 0) {
+        if (++spins > SPIN_LIMIT) {
+          atomicOr((unsigned long long*)err, (unsigned long long)ERR_LOOKBACK_TIMEOUT);
+          break;
+        }
+        continue;
+      }
+      excl += v & VALUE_MASK;
+      if (flag == FLAG_INC || t == 0) break;
+      --t;
+    }
+    st_volatile(my_slot, FLAG_INC | (excl + total));
+  }
+  s_global[tid] = bin_base[tid] + (unsigned)excl;
+  __syncthreads();
+
+  // Stage the tile in digit order.
+#pragma unroll
+  for (int i = 0; i < ITEMS; ++i) {
+    if (rank[i] != 0xFFFFFFFFu) {
+      const unsigned d = (key[i] >> shift) & (RADIX - 1);
+      const unsigned pos = s_digit_start[d] + s_warp_hist[warp][d] + rank[i];
+      s_keys[pos] = key[i];
+      if (HAS_VALS) s_vals[pos] = val[i];
+    }
+  }
+  __syncthreads();
+  const long long tile_base = (long long)tile * TILE_KEYS;
+  const int tile_n = (int)min((long long)TILE_KEYS, (long long)n - tile_base);
+  for (int j = tid; j < tile_n; j += THREADS) {
+    const unsigned k = s_keys[j];
+    const unsigned d = (k >> shift) & (RADIX - 1);
+    const unsigned dst = s_global[d] + (unsigned)j - s_digit_start[d];
+    keys_out[dst] = k;
+    if (HAS_VALS) vals_out[dst] = s_vals[j];
+  }
+}
+
+// Workspace layout for sorting n pairs with `passes` 8-bit passes.
+struct SortScratch {
+  unsigned* hist;                  // passes*256
+  unsigned* bin_base;              // passes*256
+  unsigned* counters;              // passes
+  unsigned long long* lookback;    // passes*tiles*256
+  size_t zero_bytes;               // bytes to clear from `hist` on
+};
+
+__host__ inline int num_tiles(long long n) { return (int)((n + TILE_KEYS - 1) / TILE_KEYS); }
+
+__host__ inline size_t scratch_bytes(long long n, int passes) {
+  const size_t tiles = (size_t)num_tiles(n > 0 ? n : 1);
+  size_t b = 0;
+  b += (size_t)passes * RADIX * 4;   // hist
+  b += (size_t)passes * RADIX * 4;   // bin_base
+  b += 256;                          // counters (padded)
+  b = (b + 255) & ~(size_t)255;
+  b += (size_t)passes * tiles * RADIX * 8;
+  return b + 256;
+}
+
+__host__ inline SortScratch carve_scratch(void* base, long long n, int passes) {
+  const size_t tiles = (size_t)num_tiles(n > 0 ? n : 1);
+  char* p = (char*)(((uintptr_t)base + 255) & ~(uintptr_t)255);
+  SortScratch s;
+  char* start = p;
+  s.hist = (unsigned*)p;
+  p += (size_t)passes * RADIX * 4;
+  s.bin_base = (unsigned*)p;
+  p += (size_t)passes * RADIX * 4;
+  s.counters = (unsigned*)p;
+  p += 256;
+  p = (char*)(((uintptr_t)p + 255) & ~(uintptr_t)255);
+  s.lookback = (unsigned long long*)p;
+  p += (size_t)passes * tiles * RADIX * 8;
+  s.zero_bytes = (size_t)(p - start);
+  return s;
+}
+
+// Sorts n pairs by the low `passes*8` key bits.  Buffers ping-pong:
+// pass 0 reads (k[0],v[0]) and writes (k[1],v[1]), pass 1 the reverse, ...
+// Returns the index (0/1) of the buffer pair that holds the result.
+// vals may be null (keys only).
+__host__ inline int sort_pairs(unsigned* k[2], unsigned* v[2], long long n, int passes,
+                               void* scratch, long long* err, cudaStream_t stream) {
+  if (n <= 1 || passes == 0) return 0;
+  SortScratch s = carve_scratch(scratch, n, passes);
+  cudaMemsetAsync(s.hist, 0, s.zero_bytes, stream);
+  const int hist_blocks = (int)std::min<long long>(148 * 4, (n + THREADS * 8 - 1) / (THREADS * 8));
+  histogram_kernel<<<std::max(hist_blocks, 1), THREADS, 0, stream>>>(k[0], (int)n, passes, s.hist);
+  bin_base_kernel<<<passes, THREADS, 0, stream>>>(s.hist, s.bin_base);
+  const int tiles = num_tiles(n);
+  int cur = 0;
+  for (int p = 0; p < passes; ++p) {
+    unsigned long long* lb = s.lookback + (size_t)p * tiles * RADIX;
+    if (v[0]) {
+      onesweep_kernel<true><<<tiles, THREADS, 0, stream>>>(
+          k[cur], v[cur], k[cur ^ 1], v[cur ^ 1], (int)n, p * RADIX_BITS, s.bin_base + p * RADIX,
+          lb, s.counters + p, err);
+    } else {
+      onesweep_kernel<false><<<tiles, THREADS, 0, stream>>>(
+          k[cur], nullptr, k[cur ^ 1], nullptr, (int)n, p * RADIX_BITS, s.bin_base + p * RADIX,
+          lb, s.counters + p, err);
+    }
+    cur ^= 1;
+  }
+  return cur;
+}
+
+}  // namespace
+}  // namespace radix
+}  // namespace gsb

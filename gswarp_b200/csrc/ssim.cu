@@ -1,0 +1,283 @@
+// ssim.cu -- fused separable 11x11 SSIM forward and backward.
+//
+// Restates gswarp's fused_ssim.py: Gaussian window sigma 1.5 (:47-57);
+// forward _fwd_h (:461-518) + _fwd_v_train_tiled (:522-638) ('same') or
+// _fwd_v_train_valid (:760-828) ('valid'); backward _bwd_h_scalar
+// (:831-874) / _bwd_h_scalar_valid (:878-935) + _bwd_v_tiled (:985-1067) /
+// _bwd_v (:938-981).  The reference runs each direction as two kernels with
+// four (forward) or three (backward) full-size intermediate maps in HBM; here
+// each direction is ONE kernel per 32x16 output tile: the input tile plus a
+// 5-pixel halo is staged in shared memory, the horizontal pass writes shared
+// memory only, and the vertical pass produces the outputs.  Forward writes
+// only what backward needs (dm0, dm1, dm2) plus one partial SSIM sum per CTA;
+// a last tiny kernel turns the partial sums into the mean.
+//
+// Out-of-image taps are zero-filled in shared memory; adding g*0 is exact, so
+// this equals the reference's explicit bounds checks.  The 'valid' vertical
+// pass pairs symmetric taps g*(top+bottom) as the reference does there.
+#include "gsb_common.cuh"
+
+namespace gsb {
+namespace {
+
+constexpr int TX = 32, TY = 16;
+constexpr int HALO = 5;
+constexpr int RX = TX + 2 * HALO;  // 42
+constexpr int RY = TY + 2 * HALO;  // 26
+constexpr int THREADS = 256;
+
+__constant__ float GW[11] = {0.001028380123898387f, 0.0075987582094967365f,
+                             0.036000773310661316f,  0.10936068743467331f,
+                             0.21300552785396576f,   0.26601171493530273f,
+                             0.21300552785396576f,   0.10936068743467331f,
+                             0.036000773310661316f,  0.0075987582094967365f,
+                             0.001028380123898387f};
+
+__global__ void __launch_bounds__(THREADS) ssim_fwd_kernel(const gsb_ssim_fwd_args a, int tiles_x,
+                                                           int tiles_y) {
+  __shared__ float s_x[RY][RX + 1];
+  __shared__ float s_y[RY][RX + 1];
+  __shared__ float s_h[4][RY][TX + 1];
+  __shared__ float s_red[THREADS / 32];
+  const int H = a.H, W = a.W;
+  const int tile = blockIdx.x;
+  const int tx = tile % tiles_x;
+  const int ty = (tile / tiles_x) % tiles_y;
+  const int plane = tile / (tiles_x * tiles_y);
+  const int x0 = tx * TX, y0 = ty * TY;
+  const size_t pbase = (size_t)plane * H * W;
+  const float* img1 = a.img1 + pbase;
+  const float* img2 = a.img2 + pbase;
+
+  for (int i = threadIdx.x; i < RY * RX; i += THREADS) {
+    const int r = i / RX, c = i % RX;
+    const int gy = y0 - HALO + r, gxp = x0 - HALO + c;
+    float v1 = 0.0f, v2 = 0.0f;
+    if (gy >= 0 && gy < H && gxp >= 0 && gxp < W) {
+      v1 = __ldg(img1 + (size_t)gy * W + gxp);
+      v2 = __ldg(img2 + (size_t)gy * W + gxp);
+    }
+    s_x[r][c] = v1;
+    s_y[r][c] = v2;
+  }
+  __syncthreads();
+  // Horizontal pass (fused_ssim.py:477-511): symmetric tap pairs, then centre.
+  for (int i = threadIdx.x; i < RY * TX; i += THREADS) {
+    const int r = i / TX, c = i % TX;
+    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 5; ++k) {
+      const float g = GW[k];
+      const float v1l = s_x[r][c + k], v2l = s_y[r][c + k];
+      const float v1r = s_x[r][c + 10 - k], v2r = s_y[r][c + 10 - k];
+      a0 += g * (v1l + v1r);
+      a1 += g * (v2l + v2r);
+      a2 += g * (v1l * v1l + v2l * v2l + v1r * v1r + v2r * v2r);
+      a3 += g * (v1l * v2l + v1r * v2r);
+    }
+    const float v1c = s_x[r][c + 5], v2c = s_y[r][c + 5];
+    a0 += GW[5] * v1c;
+    a1 += GW[5] * v2c;
+    a2 += GW[5] * (v1c * v1c + v2c * v2c);
+    a3 += GW[5] * v1c * v2c;
+    s_h[0][r][c] = a0;
+    s_h[1][r][c] = a1;
+    s_h[2][r][c] = a2;
+    s_h[3][r][c] = a3;
+  }
+  __syncthreads();
+  float local_sum = 0.0f;
+  const size_t npix = (size_t)a.B * a.C * H * W;
+  for (int i = threadIdx.x; i < TX * TY; i += THREADS) {
+    const int r = i / TX, c = i % TX;
+    const int gy = y0 + r, gxp = x0 + c;
+    if (gy >= H || gxp >= W) continue;
+    if (a.valid && (gy < 5 || gy >= H - 5 || gxp < 5 || gxp >= W - 5)) continue;
+    float s4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int k = 0; k < 5; ++k) {
+      const float g = GW[k];
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        const float top = s_h[m][r + k][c], bot = s_h[m][r + 10 - k][c];
+        if (a.valid) {
+          s4[m] += g * (top + bot);
+        } else {
+          s4[m] += g * top;
+          s4[m] += g * bot;
+        }
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < 4; ++m) s4[m] += GW[5] * s_h[m][r + 5][c];
+    const float mu1 = s4[0], mu2 = s4[1];
+    const float mu1_sq = mu1 * mu1, mu2_sq = mu2 * mu2, mu1mu2 = mu1 * mu2;
+    const float Av = mu1_sq + mu2_sq + a.C1;
+    const float Bv = s4[2] - mu1_sq - mu2_sq + a.C2;
+    const float Cv = 2.0f * mu1mu2 + a.C1;
+    const float Dv = 2.0f * (s4[3] - mu1mu2) + a.C2;
+    const float rA = 1.0f / Av, rB = 1.0f / Bv, rAB = rA * rB;
+    const float m = Cv * Dv * rAB;
+    local_sum += m;
+    if (a.dm) {
+      const size_t o = pbase + (size_t)gy * W + gxp;
+      a.dm[o] = 2.0f * (mu2 * (Dv - Cv) * rAB + mu1 * m * (rB - rA));
+      a.dm[npix + o] = -m * rB;
+      a.dm[2 * npix + o] = 2.0f * Cv * rAB;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) local_sum += __shfl_xor_sync(0xffffffffu, local_sum, o);
+  if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = local_sum;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.0f;
+#pragma unroll
+    for (int w = 0; w < THREADS / 32; ++w) t += s_red[w];
+    a.partials[blockIdx.x] = t;
+  }
+}
+
+__global__ void __launch_bounds__(1024) ssim_mean_kernel(const float* __restrict__ partials, int n,
+                                                         double inv_count, float* __restrict__ loss) {
+  __shared__ double s[32];
+  double acc = 0.0;
+  for (int i = threadIdx.x; i < n; i += 1024) acc += (double)partials[i];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if ((threadIdx.x & 31) == 0) s[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int w = 0; w < 32; ++w) t += s[w];
+    *loss = (float)(t * inv_count);
+  }
+}
+
+__global__ void __launch_bounds__(THREADS) ssim_bwd_kernel(const gsb_ssim_bwd_args a, int tiles_x,
+                                                           int tiles_y, float inv_n) {
+  __shared__ float s_dm[3][RY][RX + 1];
+  __shared__ float s_t[3][RY][TX + 1];
+  const int H = a.H, W = a.W;
+  const int tile = blockIdx.x;
+  const int tx = tile % tiles_x;
+  const int ty = (tile / tiles_x) % tiles_y;
+  const int plane = tile / (tiles_x * tiles_y);
+  const int x0 = tx * TX, y0 = ty * TY;
+  const size_t pbase = (size_t)plane * H * W;
+  const size_t npix = (size_t)a.B * a.C * H * W;
+  const float scale = inv_n * a.upstream[0];
+  const int lo_y = a.valid ? 5 : 0, hi_y = a.valid ? H - 5 : H;
+  const int lo_x = a.valid ? 5 : 0, hi_x = a.valid ? W - 5 : W;
+  for (int i = threadIdx.x; i < RY * RX; i += THREADS) {
+    const int r = i / RX, c = i % RX;
+    const int gy = y0 - HALO + r, gxp = x0 - HALO + c;
+    float d0 = 0.0f, d1 = 0.0f, d2 = 0.0f;
+    if (gy >= lo_y && gy < hi_y && gxp >= lo_x && gxp < hi_x) {
+      const size_t o = pbase + (size_t)gy * W + gxp;
+      d0 = __ldg(a.dm + o);
+      d1 = __ldg(a.dm + npix + o);
+      d2 = __ldg(a.dm + 2 * npix + o);
+    }
+    s_dm[0][r][c] = d0;
+    s_dm[1][r][c] = d1;
+    s_dm[2][r][c] = d2;
+  }
+  __syncthreads();
+  // Horizontal pass of dm * (upstream / N) (fused_ssim.py:844-868).
+  for (int i = threadIdx.x; i < RY * TX; i += THREADS) {
+    const int r = i / TX, c = i % TX;
+    float t0 = 0.0f, t1 = 0.0f, t2 = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 5; ++k) {
+      const float gs = GW[k] * scale;
+      t0 += gs * s_dm[0][r][c + k];
+      t1 += gs * s_dm[1][r][c + k];
+      t2 += gs * s_dm[2][r][c + k];
+      t0 += gs * s_dm[0][r][c + 10 - k];
+      t1 += gs * s_dm[1][r][c + 10 - k];
+      t2 += gs * s_dm[2][r][c + 10 - k];
+    }
+    const float gs = GW[5] * scale;
+    t0 += gs * s_dm[0][r][c + 5];
+    t1 += gs * s_dm[1][r][c + 5];
+    t2 += gs * s_dm[2][r][c + 5];
+    s_t[0][r][c] = t0;
+    s_t[1][r][c] = t1;
+    s_t[2][r][c] = t2;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < TX * TY; i += THREADS) {
+    const int r = i / TX, c = i % TX;
+    const int gy = y0 + r, gxp = x0 + c;
+    if (gy >= H || gxp >= W) continue;
+    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 5; ++k) {
+      const float g = GW[k];
+      a0 += g * s_t[0][r + k][c];
+      a1 += g * s_t[1][r + k][c];
+      a2 += g * s_t[2][r + k][c];
+      a0 += g * s_t[0][r + 10 - k][c];
+      a1 += g * s_t[1][r + 10 - k][c];
+      a2 += g * s_t[2][r + 10 - k][c];
+    }
+    a0 += GW[5] * s_t[0][r + 5][c];
+    a1 += GW[5] * s_t[1][r + 5][c];
+    a2 += GW[5] * s_t[2][r + 5][c];
+    const size_t o = pbase + (size_t)gy * W + gxp;
+    a.grad_img1[o] = a0 + 2.0f * __ldg(a.img1 + o) * a1 + __ldg(a.img2 + o) * a2;
+  }
+}
+
+inline void tiles_of(int H, int W, int& tx, int& ty) {
+  tx = div_up(W, TX);
+  ty = div_up(H, TY);
+}
+
+}  // namespace
+}  // namespace gsb
+
+using namespace gsb;
+
+GSB_EXPORT int gsb_ssim_partials_count(int B, int C, int H, int W) {
+  int tx, ty;
+  tiles_of(H, W, tx, ty);
+  return B * C * tx * ty;
+}
+
+GSB_EXPORT int gsb_ssim_fwd(const gsb_ssim_fwd_args* a, void* stream) {
+  if (!a || a->B <= 0 || a->C <= 0 || a->H <= 0 || a->W <= 0 || !a->img1 || !a->img2 ||
+      !a->partials || !a->loss) {
+    set_error("gsb_ssim_fwd: invalid arguments");
+    return GSB_ERR_INVALID;
+  }
+  if (a->valid && (a->H < 11 || a->W < 11)) {
+    set_error("gsb_ssim_fwd: padding='valid' requires image height and width of at least 11");
+    return GSB_ERR_INVALID;
+  }
+  int tx, ty;
+  tiles_of(a->H, a->W, tx, ty);
+  const int blocks = a->B * a->C * tx * ty;
+  cudaStream_t s = (cudaStream_t)stream;
+  ssim_fwd_kernel<<<blocks, THREADS, 0, s>>>(*a, tx, ty);
+  const double count = a->valid ? (double)a->B * a->C * (a->H - 10) * (a->W - 10)
+                                 : (double)a->B * a->C * a->H * a->W;
+  ssim_mean_kernel<<<1, 1024, 0, s>>>(a->partials, blocks, 1.0 / count, a->loss);
+  return check_launch("ssim_fwd_kernel");
+}
+
+GSB_EXPORT int gsb_ssim_bwd(const gsb_ssim_bwd_args* a, void* stream) {
+  if (!a || a->B <= 0 || a->C <= 0 || a->H <= 0 || a->W <= 0 || !a->img1 || !a->img2 ||
+      !a->dm || !a->upstream || !a->grad_img1) {
+    set_error("gsb_ssim_bwd: invalid arguments");
+    return GSB_ERR_INVALID;
+  }
+  int tx, ty;
+  tiles_of(a->H, a->W, tx, ty);
+  const double count = a->valid ? (double)a->B * a->C * (a->H - 10) * (a->W - 10)
+                                 : (double)a->B * a->C * a->H * a->W;
+  const float inv_n = (float)(1.0 / count);
+  ssim_bwd_kernel<<<a->B * a->C * tx * ty, THREADS, 0, (cudaStream_t)stream>>>(*a, tx, ty, inv_n);
+  return check_launch("ssim_bwd_kernel");
+}

@@ -1,0 +1,279 @@
+/*
+ * gsb200.h -- C ABI of libgsb200.so, the sm_100a kernels behind gswarp_b200.
+ *
+ * Every entry point takes plain device pointers, sizes and scalars plus a
+ * cudaStream_t (passed as void*), enqueues its kernels on that stream and
+ * returns an int status (GSB_OK or a negative GSB_ERR_* code; the message is
+ * available from gsb_last_error() on the calling thread).  The library never
+ * allocates device memory: every output and workspace buffer is provided by
+ * the caller, sized with the *_workspace_bytes() queries.  It keeps no state
+ * between calls and is safe to call from several host threads on different
+ * streams.
+ *
+ * Each entry point replaces a stage of gswarp v1.1.0 (fancifulland2718/gswarp);
+ * the reference interface it stands in for is cited beside it, by file:line
+ * inside that project.
+ *
+ * Floating point conventions: view/proj matrices are 16 floats read as
+ * flat[c*4+r] (the transposed 3DGS world_view_transform / full_proj_transform,
+ * exactly what the reference kernels read, preprocess_kernels.py:134).
+ */
+#ifndef GSB200_H
+#define GSB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GSB_ABI_VERSION 1
+
+#define GSB_OK 0
+#define GSB_ERR_INVALID (-1)  /* bad argument: ValueError in Python          */
+#define GSB_ERR_OVERFLOW (-2) /* int32 pair-count overflow: OverflowError    */
+#define GSB_ERR_CUDA (-3)     /* CUDA launch / runtime error: RuntimeError   */
+#define GSB_ERR_TIMEOUT (-4)  /* a bounded device-side wait gave up          */
+
+/* Tile-coverage modes (gswarp/_internal/coverage.py:80-84). */
+#define GSB_COVERAGE_SNUGBOX 0
+#define GSB_COVERAGE_ACCUTILE 1
+#define GSB_COVERAGE_CONIC_RECT 2
+
+/* Per-Gaussian render record written by preprocess and read by the render
+ * kernels: 12 floats = 48 bytes, three float4:
+ *   [0..3]  x, y, conic_a, conic_b
+ *   [4..7]  conic_c, opacity, depth, clamped bits (uint32 bit c = channel c)
+ *   [8..11] r, g, b, 0
+ * Per-Gaussian render-gradient accumulator (filled by gsb_render_bwd):
+ * 12 floats = 48 bytes:
+ *   [0..3]  dL/dx, dL/dy, dL/ddepth, 0
+ *   [4..7]  dL/dconic_a, dL/dconic_b, dL/dconic_c, dL/dopacity
+ *   [8..11] dL/dr, dL/dg, dL/db, 0                                         */
+#define GSB_RECORD_FLOATS 12
+#define GSB_GRAD_FLOATS 12
+
+int gsb_abi_version(void);
+const char* gsb_last_error(void);
+
+/* ------------------------------------------------------------------------ */
+/* Preprocess forward.  Replaces preprocess_gaussians                        */
+/* (gswarp/_internal/backends/warp/preprocess_ops.py:289-581): the fused     */
+/* projection/cov3d/EWA cov2d/conic/radius/AccuTile kernel                  */
+/* (preprocess_kernels.py:83-269), its cov3D_precomp variant (:345-476,     */
+/* :630-672) and the SH colour kernel (:272-342).                            */
+/* ------------------------------------------------------------------------ */
+typedef struct {
+  int P, W, H;
+  const float* means;          /* (P,3) */
+  const float* scales;         /* (P,3) or NULL when cov3d_precomp is given */
+  const float* rotations;      /* (P,4) or NULL */
+  const float* cov3d_precomp;  /* (P,6) or NULL */
+  float scale_modifier;
+  const float* opacities;      /* (P) */
+  const float* viewmatrix;     /* 16 floats, device */
+  const float* projmatrix;     /* 16 floats, device */
+  const float* campos;         /* 3 floats, device */
+  float tanfovx, tanfovy, focal_x, focal_y;
+  const float* sh;             /* (P,K,3) or NULL */
+  int sh_degree, sh_coeffs;    /* degree and K */
+  const float* colors_precomp; /* (P,3) or NULL (exactly one of sh/colors) */
+  int coverage_mode;           /* GSB_COVERAGE_* */
+  /* outputs (all (P,...) device arrays) */
+  int* radii;
+  float* proj_2d;       /* (P,2) */
+  float* conic_2d;      /* (P,3) */
+  float* conic_2d_inv;  /* (P,3) */
+  float* depths;        /* (P) */
+  int* tiles_touched;   /* (P) */
+  float* records;       /* (P,12) render records */
+} gsb_preprocess_args;
+
+int gsb_preprocess_fwd(const gsb_preprocess_args* a, void* stream);
+
+/* markVisible (preprocess_ops.py:584-595 / preprocess_kernels.py:603-627). */
+int gsb_mark_visible(int P, const float* means, const float* viewmatrix, uint8_t* out,
+                     void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Binning.  Replaces _build_binning_state (binning_ops.py:84-431) with two  */
+/* calls separated by one host read of the pair count.                       */
+/* gsb_bin_count: stable depth sort of all Gaussians (key = depth float     */
+/* bits, invisible Gaussians last), depth-ordered inclusive scan of         */
+/* tiles_touched (binning_ops.py:152-224) and the int64 pair total written  */
+/* to *status_out[0]; status_out[1] receives the device error word.         */
+/* ------------------------------------------------------------------------ */
+typedef struct {
+  int P;
+  const float* depths;        /* (P) */
+  const int* radii;           /* (P) */
+  const int* tiles_touched;   /* (P) */
+  int* depth_order;           /* out (P): point ids in depth order */
+  int* point_offsets;         /* out (P): inclusive scan in depth order */
+  long long* status_out;      /* out, device: [0]=pair total, [1]=error word */
+  void* workspace;
+  size_t workspace_bytes;
+} gsb_bin_count_args;
+
+size_t gsb_bin_count_workspace_bytes(int P);
+int gsb_bin_count(const gsb_bin_count_args* a, void* stream);
+
+/* gsb_bin_emit_sort: emit (tile id, point id) pairs in depth order with the  */
+/* same AccuTile sweep as the count (binning_kernels.py:126-216,410-451),   */
+/* stable radix sort by tile id (memory.py:571-600 semantics), identify     */
+/* ranges (binning_kernels.py:467-487).  Result order: ascending (tile,     */
+/* depth bits, point id).  ranges is zero-filled here first.                */
+typedef struct {
+  int P, W, H;
+  long long num_rendered;
+  int coverage_mode;
+  const int* depth_order;      /* from gsb_bin_count */
+  const int* point_offsets;    /* from gsb_bin_count */
+  const int* radii;
+  const float* records;        /* (P,12) */
+  const float* conic_2d_inv;   /* (P,3) */
+  const int* tiles_touched;
+  int* point_list;             /* out (num_rendered) */
+  int* ranges;                 /* out (tiles,2) */
+  long long* error_word;       /* device word; OR-ed with error bits */
+  void* workspace;
+  size_t workspace_bytes;
+} gsb_bin_sort_args;
+
+size_t gsb_bin_sort_workspace_bytes(long long num_rendered, int W, int H);
+int gsb_bin_emit_sort(const gsb_bin_sort_args* a, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Render forward.  Replaces _render_tiles_warp (render_ops.py:16-93) /     */
+/* _render_tiles_tiled256_warp_kernel (render_kernels.py:15-147).           */
+/* ------------------------------------------------------------------------ */
+typedef struct {
+  int W, H;
+  int compute_depth;
+  const int* ranges;
+  const int* point_list;
+  const float* records;
+  const float* background;  /* 3 floats, device */
+  float* out_color;         /* (3,H,W) */
+  float* out_depth;         /* (1,H,W) */
+  float* out_alpha;         /* (1,H,W) */
+  int* n_contrib;           /* (H*W) */
+} gsb_render_fwd_args;
+
+int gsb_render_fwd(const gsb_render_fwd_args* a, void* stream);
+
+/* Render backward.  Replaces _backward_render_tiles_warp                    */
+/* (backward_ops.py:183-290) / _backward_render_tiles_warp32_kernel         */
+/* (backward_kernels.py:538-707).  grad_acc must be zero-filled (P,12).     */
+typedef struct {
+  int W, H, P;
+  int compute_depth;
+  const int* ranges;
+  const int* point_list;
+  const float* records;
+  const float* background;
+  const float* out_alpha;
+  const int* n_contrib;
+  const float* grad_color;  /* (3,H,W) */
+  const float* grad_depth;  /* (1,H,W) */
+  const float* grad_alpha;  /* (1,H,W) */
+  float* grad_acc;          /* (P,12), accumulated with atomics */
+} gsb_render_bwd_args;
+
+int gsb_render_bwd(const gsb_render_bwd_args* a, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Preprocess + SH backward.  Replaces the tail of                           */
+/* _rasterize_gaussians_backward_python (backward_ops.py:525-744): the SH   */
+/* backward (backward_kernels.py:297-536), the fused preprocess backward    */
+/* (:52-295) and the cov3D_precomp kernels (:709-949).                       */
+/* ------------------------------------------------------------------------ */
+typedef struct {
+  int P, W, H;
+  const float* means;
+  const int* radii;
+  const float* scales;         /* or NULL */
+  const float* rotations;      /* or NULL */
+  const float* cov3d_precomp;  /* or NULL */
+  float scale_modifier;
+  const float* viewmatrix;
+  const float* projmatrix;
+  const float* campos;
+  float tanfovx, tanfovy, focal_x, focal_y;
+  const float* sh;             /* (P,K,3) or NULL */
+  int sh_degree, sh_coeffs;
+  const float* records;        /* forward records (clamped bits) */
+  const float* grad_acc;       /* (P,12) from gsb_render_bwd */
+  const float* grad_proj_2d;   /* (P,2) user gradient of proj_2D */
+  const float* grad_conic_2d;  /* (P,3) */
+  const float* grad_conic_2d_inv; /* (P,3) */
+  int accumulate;              /* 1: add into the outputs instead of storing */
+  /* outputs (NULL where not applicable) */
+  float* grad_means3d;   /* (P,3) */
+  float* grad_means2d;   /* (P,3) */
+  float* grad_scales;    /* (P,3) */
+  float* grad_rotations; /* (P,4) */
+  float* grad_opacity;   /* (P) */
+  float* grad_sh;        /* (P,K,3) */
+  float* grad_colors;    /* (P,3) colors_precomp gradient */
+  float* grad_cov3d;     /* (P,6) cov3D_precomp gradient */
+} gsb_preprocess_bwd_args;
+
+int gsb_preprocess_bwd(const gsb_preprocess_bwd_args* a, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Fused SSIM.  Replaces FusedSSIMMap (gswarp/fused_ssim.py:1074-1150) and   */
+/* its four separable kernels (:461-638, :831-1067).                         */
+/* ------------------------------------------------------------------------ */
+typedef struct {
+  int B, C, H, W;
+  int valid;              /* 0: 'same' padding, 1: 'valid' */
+  float C1, C2;
+  const float* img1;
+  const float* img2;
+  float* dm;              /* (3,B,C,H,W) workspace kept for backward, or NULL (inference) */
+  float* partials;        /* gsb_ssim_partials_count() floats, workspace */
+  float* loss;            /* 1 float out: mean SSIM */
+} gsb_ssim_fwd_args;
+
+int gsb_ssim_partials_count(int B, int C, int H, int W);
+int gsb_ssim_fwd(const gsb_ssim_fwd_args* a, void* stream);
+
+typedef struct {
+  int B, C, H, W;
+  int valid;
+  const float* img1;
+  const float* img2;
+  const float* dm;        /* from gsb_ssim_fwd */
+  const float* upstream;  /* 1 float, device: dL/dloss */
+  float* grad_img1;       /* (B,C,H,W) */
+} gsb_ssim_bwd_args;
+
+int gsb_ssim_bwd(const gsb_ssim_bwd_args* a, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* KNN initialiser.  Replaces distCUDA2 (gswarp/knn.py:264-410).             */
+/* out[i] = mean squared distance of point i to its three nearest others.   */
+/* ------------------------------------------------------------------------ */
+typedef struct {
+  int P;                 /* >= 4 */
+  const float* points;   /* (P,3) */
+  float* out;            /* (P) */
+  long long* error_word; /* device word */
+  void* workspace;
+  size_t workspace_bytes;
+} gsb_knn_args;
+
+size_t gsb_knn_workspace_bytes(int P);
+int gsb_knn(const gsb_knn_args* a, void* stream);
+
+/* Correctly rounded binary32 log of every input (the AccuTile threshold   */
+/* primitive); exported so tests can pin device and host bit for bit.       */
+int gsb_selftest_threshold_log(const float* in, float* out, long long n, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GSB200_H */

@@ -1,0 +1,70 @@
+"""CPU checks of the C ABI: the library loads, exports every entry point that
+include/gsb200.h declares, reports its ABI version, sizes workspaces and
+rejects bad arguments with the right status before touching the GPU."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from gswarp_b200 import _lib
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "gsb200.h"
+
+
+def _declared():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"\b(gsb_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    L = _lib.load()
+    names = _declared()
+    assert len(names) >= 15
+    for n in names:
+        assert hasattr(L, n), n
+    assert set(_lib.EXPORTED) <= set(names)
+
+
+def test_abi_version():
+    assert _lib.load().gsb_abi_version() == _lib.ABI_VERSION
+
+
+def test_workspace_queries_are_host_only():
+    L = _lib.load()
+    a = L.gsb_bin_count_workspace_bytes(1_000_000)
+    b = L.gsb_bin_count_workspace_bytes(2_000_000)
+    assert 0 < a < b
+    assert L.gsb_bin_sort_workspace_bytes(10_000_000, 1920, 1080) > 10_000_000 * 12
+    assert L.gsb_knn_workspace_bytes(2_000_000) > 2_000_000 * 28
+    assert L.gsb_ssim_partials_count(4, 3, 1080, 1920) == 12 * 60 * 68
+
+
+def test_invalid_arguments_map_to_value_error():
+    L = _lib.load()
+    a = _lib.PreprocessArgs()
+    a.P, a.W, a.H = 10, 16, 16  # no scales/rotations/cov3d, null pointers
+    st = L.gsb_preprocess_fwd(ctypes.byref(a), None)
+    assert st == _lib.GSB_ERR_INVALID
+    with pytest.raises(ValueError, match="scales/rotations"):
+        _lib.check(st, "gsb_preprocess_fwd")
+    k = _lib.KNNArgs()
+    k.P = 3
+    assert L.gsb_knn(ctypes.byref(k), None) == _lib.GSB_ERR_INVALID
+    s = _lib.SSIMFwdArgs()
+    s.B, s.C, s.H, s.W = 1, 1, 8, 8
+    s.valid = 1
+    with pytest.raises(ValueError):
+        _lib.check(L.gsb_ssim_fwd(ctypes.byref(s), None), "gsb_ssim_fwd")
+
+
+def test_pair_count_overflow_maps_to_overflow_error():
+    L = _lib.load()
+    b = _lib.BinSortArgs()
+    b.P, b.W, b.H = 1, 16, 16
+    b.num_rendered = 1 << 31
+    st = L.gsb_bin_emit_sort(ctypes.byref(b), None)
+    assert st == _lib.GSB_ERR_OVERFLOW
+    with pytest.raises(OverflowError):
+        _lib.check(st, "gsb_bin_emit_sort")
