@@ -203,8 +203,12 @@ __global__ void __launch_bounds__(THREADS) onesweep_kernel(
     const unsigned k = s_keys[j];
     const unsigned d = (k >> shift) & (RADIX - 1);
     const unsigned dst = s_global[d] + (unsigned)j - s_digit_start[d];
-    keys_out[dst] = k;
-    if (HAS_VALS) vals_out[dst] = s_vals[j];
+    // dst < n whenever the histogram and look-back agree; the test keeps a
+    // timed-out look-back (flagged above) from writing out of bounds.
+    if (dst < (unsigned)n) {
+      keys_out[dst] = k;
+      if (HAS_VALS) vals_out[dst] = s_vals[j];
+    }
   }
 }
 

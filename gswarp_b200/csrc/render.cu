@@ -187,7 +187,8 @@ __global__ void __launch_bounds__(THREADS) render_bwd_kernel(const gsb_render_bw
   int cta_max = 0;
 #pragma unroll
   for (int w = 0; w < THREADS / 32; ++w) cta_max = max(cta_max, s_max[w]);
-  if (cta_max == 0) return;
+  cta_max = min(cta_max, n);  // n_contrib never exceeds the tile's list
+  if (cta_max <= 0) return;
 
   const float ddelx_dx = 0.5f * (float)a.W;
   const float ddely_dy = 0.5f * (float)a.H;
