@@ -281,3 +281,107 @@ GSB_EXPORT int gsb_ssim_bwd(const gsb_ssim_bwd_args* a, void* stream) {
   ssim_bwd_kernel<<<a->B * a->C * tx * ty, THREADS, 0, (cudaStream_t)stream>>>(*a, tx, ty, inv_n);
   return check_launch("ssim_bwd_kernel");
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free SSIM forward.
+//
+// Some callers cannot hand this library a workspace: a host process whose
+// device memory is reserved up front by another allocator (a framework's
+// caching pool that owns the whole device), a plain C / FFI caller with no
+// device allocator of its own, or a latency-critical loop in which a
+// cudaMalloc/cudaFree round trip (cudaFree synchronizes the device) is not
+// acceptable.  This entry point computes the same mean SSIM (and, if `dm` is
+// given, the same dm maps) as gsb_ssim_fwd but keeps its only scratch -- one
+// partial sum per 32x16 output tile -- in a fixed device array that lives in
+// this library for as long as it is loaded (256 KiB on every GPU that loads
+// it), so it allocates nothing.
+//
+// Limits and sharing rules:
+//  * at most GSB_SSIM_NOALLOC_MAX_PARTIALS tiles, i.e. B*C*ceil(H/16)*
+//    ceil(W/32) <= 65536 (four 3x1080x1920 images need 48,960); larger
+//    inputs are rejected with GSB_ERR_INVALID;
+//  * every call on a device shares the one array and it keeps the last
+//    call's partial sums; each call writes every slot it later reads, so
+//    nothing has to start at zero, but two calls whose kernels overlap on
+//    the GPU (different streams without ordering) race on the array;
+//  * the array's device address is looked up once per device, on the first
+//    call made with that device current; make that first call before any
+//    stream capture begins.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+namespace gsb {
+namespace {
+constexpr int NOALLOC_MAX_PARTIALS = GSB_SSIM_NOALLOC_MAX_PARTIALS;
+static __device__ __align__(256) float g_noalloc_partials[NOALLOC_MAX_PARTIALS];
+constexpr int NOALLOC_MAX_DEVICES = 64;
+float* g_noalloc_ptr[NOALLOC_MAX_DEVICES] = {};
+std::mutex g_noalloc_mutex;
+
+// Device address of the fixed scratch array on the current device (looked
+// up once per device).
+int noalloc_scratch(float** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= NOALLOC_MAX_DEVICES) {
+    set_error("gsb_ssim_fwd_noalloc: no usable current device (%s)", cudaGetErrorString(e));
+    return GSB_ERR_CUDA;
+  }
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_partials);
+    if (e != cudaSuccess || !p) {
+      set_error("gsb_ssim_fwd_noalloc: cudaGetSymbolAddress failed (%s)", cudaGetErrorString(e));
+      return GSB_ERR_CUDA;
+    }
+    g_noalloc_ptr[dev] = (float*)p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return GSB_OK;
+}
+}  // namespace
+}  // namespace gsb
+
+GSB_EXPORT int gsb_ssim_fwd_noalloc(int B, int C, int H, int W, int valid, float C1, float C2,
+                                    const float* img1, const float* img2, float* dm, float* loss,
+                                    void* stream) {
+  if (B <= 0 || C <= 0 || H <= 0 || W <= 0 || !img1 || !img2 || !loss) {
+    set_error("gsb_ssim_fwd_noalloc: invalid arguments");
+    return GSB_ERR_INVALID;
+  }
+  if (valid && (H < 11 || W < 11)) {
+    set_error("gsb_ssim_fwd_noalloc: padding='valid' requires image height and width of at least 11");
+    return GSB_ERR_INVALID;
+  }
+  int tx, ty;
+  tiles_of(H, W, tx, ty);
+  const long long blocks = (long long)B * C * tx * ty;
+  if (blocks > NOALLOC_MAX_PARTIALS) {
+    set_error("gsb_ssim_fwd_noalloc: %lld output tiles exceed the fixed scratch of %d "
+              "(B*C*ceil(H/16)*ceil(W/32) must be <= %d); use gsb_ssim_fwd with a workspace",
+              blocks, NOALLOC_MAX_PARTIALS, NOALLOC_MAX_PARTIALS);
+    return GSB_ERR_INVALID;
+  }
+  float* partials = nullptr;
+  const int st = noalloc_scratch(&partials);
+  if (st != GSB_OK) return st;
+  gsb_ssim_fwd_args a{};
+  a.B = B;
+  a.C = C;
+  a.H = H;
+  a.W = W;
+  a.valid = valid;
+  a.C1 = C1;
+  a.C2 = C2;
+  a.img1 = img1;
+  a.img2 = img2;
+  a.dm = dm;
+  a.partials = partials;
+  a.loss = loss;
+  cudaStream_t s = (cudaStream_t)stream;
+  ssim_fwd_kernel<<<(int)blocks, THREADS, 0, s>>>(a, tx, ty);
+  const double count = valid ? (double)B * C * (H - 10) * (W - 10) : (double)B * C * H * W;
+  ssim_mean_kernel<<<1, 1024, 0, s>>>(partials, (int)blocks, 1.0 / count, loss);
+  return check_launch("gsb_ssim_fwd_noalloc");
+}

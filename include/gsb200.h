@@ -252,6 +252,22 @@ typedef struct {
 
 int gsb_ssim_bwd(const gsb_ssim_bwd_args* a, void* stream);
 
+/* Allocation-free SSIM forward.  No counterpart in the reference: it exists
+ * for callers that cannot provide device memory (a process whose device
+ * memory is reserved up front by another allocator, a plain C/FFI caller
+ * without a device allocator, or a loop that cannot afford a cudaMalloc /
+ * cudaFree round trip).  Same result as gsb_ssim_fwd (mean SSIM into *loss,
+ * dm maps if dm is non-NULL), but its scratch is a fixed 256 KiB device array
+ * inside the library, so B*C*ceil(H/16)*ceil(W/32) must not exceed
+ * GSB_SSIM_NOALLOC_MAX_PARTIALS (larger inputs return GSB_ERR_INVALID).
+ * All calls on a device share that array: calls whose kernels overlap on the
+ * GPU race.  The first call on a device looks up the array's address; make
+ * it before any stream capture begins. */
+#define GSB_SSIM_NOALLOC_MAX_PARTIALS 65536
+int gsb_ssim_fwd_noalloc(int B, int C, int H, int W, int valid, float C1, float C2,
+                         const float* img1, const float* img2, float* dm, float* loss,
+                         void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* KNN initialiser.  Replaces distCUDA2 (gswarp/knn.py:264-410).             */
 /* out[i] = mean squared distance of point i to its three nearest others.   */
