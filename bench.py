@@ -127,32 +127,28 @@ def make_scene(args, device, rank):
 
 
 class Trainer:
-    """Parameters, flat gradient buffer and one data-parallel step."""
+    """Parameters, the flat gradient buffer and one data-parallel step
+    (gswarp_b200.view_sharding) rendering this rank's views through the
+    public API."""
 
     def __init__(self, scene, views, targets_dev, targets_host, world, device):
         import torch
 
         import gswarp_b200 as gs
+        from gswarp_b200.view_sharding import ViewShardedStep
 
         self.gs = gs
         self.torch = torch
-        N = scene.n
-        self.N = N
+        self.N = scene.n
         self.device = device
         self.world = world
-        # parameters (rasterizer inputs) and one flat SoA gradient buffer
+        # parameters (rasterizer inputs); their .grad are views of one flat buffer
         self.means = scene.means.contiguous().requires_grad_(True)
         self.scales = scene.scales.contiguous().requires_grad_(True)
         self.rots = scene.rotations.contiguous().requires_grad_(True)
         self.opac = scene.opacities.contiguous().requires_grad_(True)
         self.sh = scene.sh.contiguous().requires_grad_(True)
         self.params = [self.means, self.scales, self.rots, self.opac, self.sh]
-        self.flat = torch.zeros(N * FLOATS_PER_GAUSSIAN, dtype=torch.float32, device=device)
-        off = 0
-        for p in self.params:
-            n = p.numel()
-            p.grad = self.flat[off:off + n].view_as(p)
-            off += n
         self.views = views
         self.targets_dev = targets_dev
         self.targets_host = targets_host
@@ -166,31 +162,30 @@ class Trainer:
         self.means2d = torch.zeros_like(self.means, requires_grad=True)
         self.loss_host = torch.zeros(len(views), dtype=torch.float32).pin_memory() if targets_host else None
         self.stage_tgt = [torch.empty_like(t) for t in targets_dev] if targets_host else None
+        self.e2e = False
+        self.dp = ViewShardedStep(self.params, range(len(views)), self._view_loss)
+        self.flat = self.dp.grads.flat
+
+    def _view_loss(self, i):
+        gs = self.gs
+        if self.e2e:
+            tgt = self.stage_tgt[i]
+            tgt.copy_(self.targets_host[i], non_blocking=True)
+        else:
+            tgt = self.targets_dev[i]
+        self.means2d.grad = None
+        color, radii, meta = gs.GaussianRasterizer(self.settings[i])(
+            self.means, self.means2d, self.opac, shs=self.sh, scales=self.scales, rotations=self.rots)
+        l1 = (color - tgt).abs().mean()
+        ssim = gs.fused_ssim(color.unsqueeze(0), tgt.unsqueeze(0))
+        return l1 + 0.2 * (1.0 - ssim)
 
     def step(self, e2e: bool = False):
-        torch = self.torch
-        gs = self.gs
-        self.flat.zero_()
-        self.means2d.grad = None
-        losses = []
-        for i, s in enumerate(self.settings):
-            if e2e:
-                tgt = self.stage_tgt[i]
-                tgt.copy_(self.targets_host[i], non_blocking=True)
-            else:
-                tgt = self.targets_dev[i]
-            color, radii, meta = gs.GaussianRasterizer(s)(
-                self.means, self.means2d, self.opac, shs=self.sh, scales=self.scales, rotations=self.rots)
-            l1 = (color - tgt).abs().mean()
-            ssim = gs.fused_ssim(color.unsqueeze(0), tgt.unsqueeze(0))
-            loss = l1 + 0.2 * (1.0 - ssim)
-            loss.backward()
-            losses.append(loss.detach())
-        if self.world > 1:
-            torch.distributed.all_reduce(self.flat)
+        self.e2e = e2e
+        res = self.dp.step()
         if e2e:
-            self.loss_host.copy_(torch.stack(losses), non_blocking=True)
-        return losses
+            self.loss_host.copy_(self.torch.stack(res.losses), non_blocking=True)
+        return res.losses
 
 
 def timed(fn, steps, warmup, world):

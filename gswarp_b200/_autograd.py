@@ -60,6 +60,9 @@ class _RasterizeGaussians(torch.autograd.Function):
         ctx.save_for_backward(colors_precomp, opacities, means3D, scales, rotations, cov3Ds_precomp, sh,
                               pre.radii, pre.records, binned.point_list, binned.ranges, ren.n_contrib, ren.alpha)
         ctx.mark_non_differentiable(pre.radii)
+        # Unused outputs arrive as None in backward instead of zero tensors;
+        # the kernels treat a missing gradient as zero without reading it.
+        ctx.set_materialize_grads(False)
         return ren.color, pre.radii, ren.depth, ren.alpha, pre.proj_2d, pre.conic_2d, pre.conic_2d_inv
 
     @staticmethod
@@ -75,10 +78,8 @@ class _RasterizeGaussians(torch.autograd.Function):
         return g_means3D, g_means2D, g_sh, g_colors, g_opac, g_scales, g_rot, g_cov, None
 
 
-def _grad_or_zeros(t, shape, dev):
-    if t is None:
-        return torch.zeros(shape, dtype=torch.float32, device=dev)
-    return pl._f32(t)
+def _grad_or_none(t):
+    return None if t is None else pl._f32(t)
 
 
 def run_backward(rs, options, num_rendered, means3D, sh, colors_precomp, opacities, scales, rotations,
@@ -98,16 +99,21 @@ def run_backward(rs, options, num_rendered, means3D, sh, colors_precomp, opaciti
     bg = pl._f32(rs.bg).reshape(NUM_CHANNELS)
     g = pl.make_gaussians(means3D, opacities, scales, rotations, cov3Ds_precomp, sh, colors_precomp,
                           rs.scale_modifier, rs.sh_degree)
-    gc = _grad_or_zeros(grad_color, (NUM_CHANNELS, H, W), dev)
-    gd = _grad_or_zeros(grad_depth, (1, H, W), dev)
-    ga = _grad_or_zeros(grad_alpha, (1, H, W), dev)
-    gp = _grad_or_zeros(grad_proj_2D, (P, 2), dev)
-    gk = _grad_or_zeros(grad_conic_2D, (P, 3), dev)
-    gki = _grad_or_zeros(grad_conic_2D_inv, (P, 3), dev)
+    gc = _grad_or_none(grad_color)
+    gd = _grad_or_none(grad_depth)
+    ga = _grad_or_none(grad_alpha)
+    gp = _grad_or_none(grad_proj_2D)
+    gk = _grad_or_none(grad_conic_2D)
+    gki = _grad_or_none(grad_conic_2D_inv)
     binned = pl.Binned(int(num_rendered), point_list, ranges)
     with torch.cuda.device(dev):
-        grad_acc = pl.render_backward(records, binned, cam, bg, pl._f32(alpha), n_contrib, gc, gd, ga,
-                                      options.compute_depth, P)
+        if gc is None and gd is None and ga is None:
+            grad_acc = torch.zeros((P, pl._lib.GRAD_FLOATS), dtype=torch.float32, device=dev)
+        else:
+            if gc is None:
+                gc = torch.zeros((NUM_CHANNELS, H, W), dtype=torch.float32, device=dev)
+            grad_acc = pl.render_backward(records, binned, cam, bg, pl._f32(alpha), n_contrib, gc, gd, ga,
+                                          options.compute_depth, P)
         pg = pl.preprocess_backward(g, cam, radii, records, grad_acc, gp, gk, gki)
     grad_colors = pg.grad_colors if g.colors is not None else torch.empty_like(colors_precomp)
     grad_opac = pg.grad_opacity.reshape(opacities.shape)

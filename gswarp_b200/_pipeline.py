@@ -126,6 +126,7 @@ class Preprocessed:
     depths: torch.Tensor
     tiles_touched: torch.Tensor
     records: torch.Tensor
+    cov3d: torch.Tensor | None = None
 
 
 @dataclass(slots=True)
@@ -173,10 +174,14 @@ def coverage_mode_id(options: ExecutionOptions | None) -> int:
     return resolve_tile_coverage_mode_id(mode, BASELINE_3DGS_COVERAGE)
 
 
-def preprocess(g: Gaussians, cam: Camera, coverage_mode: int) -> Preprocessed:
+def preprocess(g: Gaussians, cam: Camera, coverage_mode: int, want_cov3d: bool = False) -> Preprocessed:
     P = g.P
     dev = g.means3D.device
+    cov3d = None
+    if want_cov3d:
+        cov3d = g.cov3D if g.cov3D is not None else torch.empty((P, 6), dtype=torch.float32, device=dev)
     out = Preprocessed(
+        cov3d=cov3d,
         radii=torch.empty(P, dtype=torch.int32, device=dev),
         proj_2d=torch.empty((P, 2), dtype=torch.float32, device=dev),
         conic_2d=torch.empty((P, 3), dtype=torch.float32, device=dev),
@@ -212,6 +217,7 @@ def preprocess(g: Gaussians, cam: Camera, coverage_mode: int) -> Preprocessed:
     a.depths = _lib.ptr(out.depths)
     a.tiles_touched = _lib.ptr(out.tiles_touched)
     a.records = _lib.ptr(out.records)
+    a.cov3d_out = _lib.ptr(cov3d) if (cov3d is not None and g.cov3D is None) else None
     with _stage_timer("preprocess_fwd", {"P": P, "kernels": 1}):
         _lib.call("gsb_preprocess_fwd", a, _lib.stream_handle(dev))
     return out

@@ -29,20 +29,20 @@ __constant__ float SH_C3[7] = {-0.5900435899266435f, 2.890611442640554f, -0.4570
 
 // SH degree 0..3 colour (preprocess_kernels.py:272-342).  Coefficient c of
 // channel ch lives at sp[c*3+ch].
-__device__ __forceinline__ void eval_sh(const float* __restrict__ sp, int K, int degree, float x,
+__device__ __forceinline__ void eval_sh(const float (&sp)[48], int K, int degree, float x,
                                         float y, float z, float col[3]) {
   const float c0 = SH_C0;
 #pragma unroll
-  for (int ch = 0; ch < 3; ++ch) col[ch] = c0 * __ldg(sp + ch);
+  for (int ch = 0; ch < 3; ++ch) col[ch] = c0 * sp[ch];
   if (degree > 0 && K > 3) {
     const float c1 = SH_C1;
     float b1 = -c1 * y, b2 = c1 * z, b3 = -c1 * x;
 #pragma unroll
-    for (int ch = 0; ch < 3; ++ch) col[ch] = col[ch] + b1 * __ldg(sp + 3 + ch);
+    for (int ch = 0; ch < 3; ++ch) col[ch] = col[ch] + b1 * sp[3 + ch];
 #pragma unroll
-    for (int ch = 0; ch < 3; ++ch) col[ch] = col[ch] + b2 * __ldg(sp + 6 + ch);
+    for (int ch = 0; ch < 3; ++ch) col[ch] = col[ch] + b2 * sp[6 + ch];
 #pragma unroll
-    for (int ch = 0; ch < 3; ++ch) col[ch] = col[ch] + b3 * __ldg(sp + 9 + ch);
+    for (int ch = 0; ch < 3; ++ch) col[ch] = col[ch] + b3 * sp[9 + ch];
     if (degree > 1 && K > 8) {
       float xx = x * x, yy = y * y, zz = z * z, xy = x * y, yz = y * z, xz = x * z;
       float w[5];
@@ -54,7 +54,7 @@ __device__ __forceinline__ void eval_sh(const float* __restrict__ sp, int K, int
 #pragma unroll
       for (int k = 0; k < 5; ++k)
 #pragma unroll
-        for (int ch = 0; ch < 3; ++ch) col[ch] = col[ch] + w[k] * __ldg(sp + (4 + k) * 3 + ch);
+        for (int ch = 0; ch < 3; ++ch) col[ch] = col[ch] + w[k] * sp[(4 + k) * 3 + ch];
       if (degree > 2 && K > 15) {
         float v[7];
         v[0] = SH_C3[0] * y * (3.0f * xx - yy);
@@ -67,7 +67,7 @@ __device__ __forceinline__ void eval_sh(const float* __restrict__ sp, int K, int
 #pragma unroll
         for (int k = 0; k < 7; ++k)
 #pragma unroll
-          for (int ch = 0; ch < 3; ++ch) col[ch] = col[ch] + v[k] * __ldg(sp + (9 + k) * 3 + ch);
+          for (int ch = 0; ch < 3; ++ch) col[ch] = col[ch] + v[k] * sp[(9 + k) * 3 + ch];
       }
     }
   }
@@ -102,6 +102,10 @@ __global__ void __launch_bounds__(256) preprocess_fwd_kernel(const gsb_preproces
   float ppx = 0.0f, ppy = 0.0f;
   bool strict_det = false;
   if (a.cov3d_precomp == nullptr) {
+    if (a.cov3d_out && !(p_view_z > 0.2f)) {
+      float* c3 = a.cov3d_out + (size_t)idx * 6;
+      for (int k = 0; k < 6; ++k) c3[k] = 0.0f;  // near-culled: zero (preprocess_kernels.py:116-121)
+    }
     if (p_view_z > 0.2f) {
       const float hom_x = pr[0] * p0 + pr[4] * p1 + pr[8] * p2 + pr[12];
       const float hom_y = pr[1] * p0 + pr[5] * p1 + pr[9] * p2 + pr[13];
@@ -126,6 +130,16 @@ __global__ void __launch_bounds__(256) preprocess_fwd_kernel(const gsb_preproces
       const float m00 = s0 * r00, m01 = s0 * r01, m02 = s0 * r02;
       const float m10 = s1 * r10, m11 = s1 * r11, m12 = s1 * r12;
       const float m20 = s2 * r20, m21 = s2 * r21, m22 = s2 * r22;
+      if (a.cov3d_out) {
+        // preprocess_kernels.py:177-182 (cov3d = M^T M, upper triangle)
+        float* c3 = a.cov3d_out + (size_t)idx * 6;
+        c3[0] = m00 * m00 + m10 * m10 + m20 * m20;
+        c3[1] = m00 * m01 + m10 * m11 + m20 * m21;
+        c3[2] = m00 * m02 + m10 * m12 + m20 * m22;
+        c3[3] = m01 * m01 + m11 * m11 + m21 * m21;
+        c3[4] = m01 * m02 + m11 * m12 + m21 * m22;
+        c3[5] = m02 * m02 + m12 * m12 + m22 * m22;
+      }
       float vx = v[0] * p0 + v[4] * p1 + v[8] * p2 + v[12];
       float vy = v[1] * p0 + v[5] * p1 + v[9] * p2 + v[13];
       const float vz = p_view_z;
@@ -256,7 +270,25 @@ __global__ void __launch_bounds__(256) preprocess_fwd_kernel(const gsb_preproces
       const float len_sq = dx * dx + dy * dy + dz * dz;
       const float inv_len = 1.0f / sqrtf(fmx(len_sq, 1.0e-20f));
       const float* sp = a.sh + (size_t)idx * a.sh_coeffs * 3;
-      eval_sh(sp, a.sh_coeffs, a.sh_degree, dx * inv_len, dy * inv_len, dz * inv_len, col);
+      // The first 16 coefficients of the row, with 16-byte loads when the row
+      // is an aligned 48-float record (SH degree 3).
+      float shv[48];
+      if (a.sh_coeffs == 16 && (reinterpret_cast<uintptr_t>(sp) & 15) == 0) {
+        const float4* s4p = reinterpret_cast<const float4*>(sp);
+#pragma unroll
+        for (int q = 0; q < 12; ++q) {
+          const float4 v = __ldg(s4p + q);
+          shv[q * 4 + 0] = v.x;
+          shv[q * 4 + 1] = v.y;
+          shv[q * 4 + 2] = v.z;
+          shv[q * 4 + 3] = v.w;
+        }
+      } else {
+        const int nsh = (a.sh_coeffs < 16 ? a.sh_coeffs : 16) * 3;
+#pragma unroll
+        for (int k = 0; k < 48; ++k) shv[k] = k < nsh ? __ldg(sp + k) : 0.0f;
+      }
+      eval_sh(shv, a.sh_coeffs, a.sh_degree, dx * inv_len, dy * inv_len, dz * inv_len, col);
 #pragma unroll
       for (int ch = 0; ch < 3; ++ch) {
         col[ch] = col[ch] + 0.5f;

@@ -64,6 +64,24 @@ __device__ void sh_backward(const gsb_preprocess_bwd_args& a, int idx, const flo
     return;
   }
   const float* sp = a.sh + (size_t)idx * K * 3;
+  // The row's coefficients (up to 16 x 3); 16-byte loads when the row is a
+  // whole, aligned 48-float record.
+  float shv[48];
+  if (K == 16 && (reinterpret_cast<uintptr_t>(sp) & 15) == 0) {
+    const float4* s4p = reinterpret_cast<const float4*>(sp);
+#pragma unroll
+    for (int q = 0; q < 12; ++q) {
+      const float4 v = __ldg(s4p + q);
+      shv[q * 4 + 0] = v.x;
+      shv[q * 4 + 1] = v.y;
+      shv[q * 4 + 2] = v.z;
+      shv[q * 4 + 3] = v.w;
+    }
+  } else {
+    const int n = (K < 16 ? K : 16) * 3;
+#pragma unroll
+    for (int k = 0; k < 48; ++k) shv[k] = k < n ? __ldg(sp + k) : 0.0f;
+  }
   const float dir[3] = {mean[0] - cam[0], mean[1] - cam[1], mean[2] - cam[2]};
   const float len_sq = dir[0] * dir[0] + dir[1] * dir[1] + dir[2] * dir[2];
   const float inv_len = 1.0f / sqrtf(fmx(len_sq, 1.0e-20f));
@@ -85,9 +103,9 @@ __device__ void sh_backward(const gsb_preprocess_bwd_args& a, int idx, const flo
     used = 4;
 #pragma unroll
     for (int c = 0; c < 3; ++c) {
-      dx[c] = -c1 * __ldg(sp + 9 + c);
-      dy[c] = -c1 * __ldg(sp + 3 + c);
-      dz[c] = c1 * __ldg(sp + 6 + c);
+      dx[c] = -c1 * shv[9 + c];
+      dy[c] = -c1 * shv[3 + c];
+      dz[c] = c1 * shv[6 + c];
     }
     if (degree > 1 && K > 8) {
       const float xx = x * x, yy = y * y, zz = z * z, xy = x * y, yz = y * z, xz = x * z;
@@ -99,8 +117,8 @@ __device__ void sh_backward(const gsb_preprocess_bwd_args& a, int idx, const flo
       used = 9;
 #pragma unroll
       for (int c = 0; c < 3; ++c) {
-        const float s4 = __ldg(sp + 12 + c), s5 = __ldg(sp + 15 + c), s6 = __ldg(sp + 18 + c);
-        const float s7 = __ldg(sp + 21 + c), s8 = __ldg(sp + 24 + c);
+        const float s4 = shv[12 + c], s5 = shv[15 + c], s6 = shv[18 + c];
+        const float s7 = shv[21 + c], s8 = shv[24 + c];
         dx[c] = dx[c] + (SH_C2[0] * y) * s4 + (SH_C2[2] * (-2.0f * x)) * s6 + (SH_C2[3] * z) * s7 +
                 (SH_C2[4] * (2.0f * x)) * s8;
         dy[c] = dy[c] + (SH_C2[0] * x) * s4 + (SH_C2[1] * z) * s5 + (SH_C2[2] * (-2.0f * y)) * s6 +
@@ -118,9 +136,9 @@ __device__ void sh_backward(const gsb_preprocess_bwd_args& a, int idx, const flo
         used = 16;
 #pragma unroll
         for (int c = 0; c < 3; ++c) {
-          const float s9 = __ldg(sp + 27 + c), s10 = __ldg(sp + 30 + c), s11 = __ldg(sp + 33 + c);
-          const float s12 = __ldg(sp + 36 + c), s13 = __ldg(sp + 39 + c);
-          const float s14 = __ldg(sp + 42 + c), s15 = __ldg(sp + 45 + c);
+          const float s9 = shv[27 + c], s10 = shv[30 + c], s11 = shv[33 + c];
+          const float s12 = shv[36 + c], s13 = shv[39 + c];
+          const float s14 = shv[42 + c], s15 = shv[45 + c];
           dx[c] = dx[c] + (SH_C3[0] * (6.0f * xy)) * s9 + (SH_C3[1] * yz) * s10 +
                   (SH_C3[2] * (-2.0f * xy)) * s11 + (SH_C3[3] * (-6.0f * xz)) * s12 +
                   (SH_C3[4] * (-3.0f * xx + 4.0f * zz - yy)) * s13 + (SH_C3[5] * (2.0f * xz)) * s14 +
@@ -139,20 +157,23 @@ __device__ void sh_backward(const gsb_preprocess_bwd_args& a, int idx, const flo
   // Gradient rows: w[k] * g for the coefficients the degree uses, 0 above.
   if (K == 16 && !acc && (reinterpret_cast<uintptr_t>(out) & 15) == 0) {
     float4* o4 = reinterpret_cast<float4*>(out);
-    float row[48];
 #pragma unroll
-    for (int k = 0; k < 16; ++k)
-#pragma unroll
-      for (int c = 0; c < 3; ++c) row[k * 3 + c] = w[k] * g[c];
-#pragma unroll
-    for (int q = 0; q < 12; ++q)
-      o4[q] = make_float4(row[q * 4], row[q * 4 + 1], row[q * 4 + 2], row[q * 4 + 3]);
+    for (int q = 0; q < 12; ++q) {
+      const int e = q * 4;
+      o4[q] = make_float4(w[(e + 0) / 3] * g[(e + 0) % 3], w[(e + 1) / 3] * g[(e + 1) % 3],
+                          w[(e + 2) / 3] * g[(e + 2) % 3], w[(e + 3) / 3] * g[(e + 3) % 3]);
+    }
   } else {
-    for (int k = 0; k < K; ++k)
+    for (int k = 0; k < K; ++k) {
+      float wk = 0.0f;  // w[k] without dynamic register indexing
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (j == k) wk = w[j];
       for (int c = 0; c < 3; ++c) {
-        const float gv = k < used ? w[k] * g[c] : 0.0f;
+        const float gv = k < used ? wk * g[c] : 0.0f;
         store_or_add(out + k * 3 + c, gv, acc);
       }
+    }
   }
   const float ddir[3] = {dx[0] * g[0] + dx[1] * g[1] + dx[2] * g[2],
                          dy[0] * g[0] + dy[1] * g[1] + dy[2] * g[2],
@@ -184,7 +205,7 @@ __global__ void __launch_bounds__(256) preprocess_bwd_kernel(const gsb_preproces
   const float rrgb[3] = {gq2.x, gq2.y, gq2.z};
 
   float gxy0 = rgx, gxy1 = rgy;
-  if (rad > 0) {
+  if (rad > 0 && a.grad_proj_2d) {
     gxy0 = gxy0 + a.grad_proj_2d[tid * 2];
     gxy1 = gxy1 + a.grad_proj_2d[tid * 2 + 1];
   }
@@ -223,12 +244,15 @@ __global__ void __launch_bounds__(256) preprocess_bwd_kernel(const gsb_preproces
     const float limx = 1.3f * a.tanfovx, limy = 1.3f * a.tanfovy;
     const float w00 = vf[0], w01 = vf[1], w02 = vf[2], w10 = vf[4], w11 = vf[5], w12 = vf[6];
     const float w20 = vf[8], w21 = vf[9], w22 = vf[10];
-    const float tc0 = rco[0] + a.grad_conic_2d[tid * 3 + 0];
-    const float tc1 = rco[1] + a.grad_conic_2d[tid * 3 + 1];
-    const float tc2 = rco[2] + a.grad_conic_2d[tid * 3 + 2];
-    const float gi0 = a.grad_conic_2d_inv[tid * 3 + 0];
-    const float gi1 = a.grad_conic_2d_inv[tid * 3 + 1];
-    const float gi2 = a.grad_conic_2d_inv[tid * 3 + 2];
+    // A NULL user gradient is a zero gradient (x + 0 == x).
+    const float* gk = a.grad_conic_2d ? a.grad_conic_2d + tid * 3 : nullptr;
+    const float* gkv = a.grad_conic_2d_inv ? a.grad_conic_2d_inv + tid * 3 : nullptr;
+    const float tc0 = gk ? rco[0] + gk[0] : rco[0];
+    const float tc1 = gk ? rco[1] + gk[1] : rco[1];
+    const float tc2 = gk ? rco[2] + gk[2] : rco[2];
+    const float gi0 = gkv ? gkv[0] : 0.0f;
+    const float gi1 = gkv ? gkv[1] : 0.0f;
+    const float gi2 = gkv ? gkv[2] : 0.0f;
     if (!PRECOMP) {
       // backward_kernels.py:124-287
       const float tz_inv = 1.0f / (z + 1.0e-7f);
@@ -446,7 +470,7 @@ GSB_EXPORT int gsb_preprocess_bwd(const gsb_preprocess_bwd_args* a, void* stream
     return GSB_ERR_INVALID;
   }
   if (!a->means || !a->radii || !a->viewmatrix || !a->projmatrix || !a->records ||
-      !a->grad_acc || !a->grad_proj_2d || !a->grad_conic_2d || !a->grad_conic_2d_inv ||
+      !a->grad_acc ||
       !a->grad_means3d || (a->sh && (!a->grad_sh || !a->campos || a->sh_coeffs <= 0))) {
     set_error("gsb_preprocess_bwd: null pointer argument");
     return GSB_ERR_INVALID;

@@ -1,7 +1,7 @@
 // render.cu -- 16x16-tile front-to-back alpha blending and its backward.
 //
 // Forward restates _render_tiles_tiled256_warp_kernel
-// (render_kernels.py:15-147): integer pixel coordinates, 256-Gaussian rounds
+// (render_kernels.py:15-147): integer pixel coordinates, Gaussian rounds
 // with a CTA-wide done vote, alpha = min(0.99, op*exp(power)), skip below
 // 1/255, stop (without adding the pair) once T*(1-alpha) < 1e-4.
 // Backward restates _backward_render_tiles_warp32_kernel
@@ -10,51 +10,67 @@
 // last_color (and depth) terms, gradients of xy (scaled by W/2, H/2), conic,
 // opacity, colour and depth.
 //
-// B200 design (both directions): one 256-thread CTA per tile; each warp owns
-// an 8x4 pixel block (squarer than the reference's 16x2 rows, so a small
-// Gaussian touches fewer warps); Gaussians are staged per batch in shared
-// memory from the 48-byte render records (three 16-byte loads per Gaussian);
-// exp is one MUFU.EX2.  Backward: the CTA walks its list from the CTA-wide
-// maximum contributor down, each warp skips positions above its own maximum,
-// a warp vote skips Gaussians no lane of the warp uses, and the ten gradient
-// terms are reduced across the warp with a 12-shuffle transpose reduction
-// (instead of 10 x 5 butterfly shuffles); 10 lanes then issue one float
-// atomic each into the per-Gaussian accumulator.
+// B200 design (both directions): one 128-thread CTA per 16x16 tile; each
+// thread owns TWO pixels (rows y and y+4 of its warp's 8x8 block), so every
+// Gaussian staged in shared memory is read once per two pixels and the
+// per-(warp, Gaussian) control work covers 64 pixels.  Gaussians are staged
+// per batch from the 48-byte render records (three 16-byte loads per
+// Gaussian); exp is one MUFU.EX2, 1/(1-alpha) one MUFU.RCP.  Backward: the
+// CTA walks its list from the CTA-wide maximum contributor down, each warp
+// skips positions above its own maximum, a warp vote skips Gaussians no lane
+// uses, and the ten gradient terms (already summed over the thread's two
+// pixels) are reduced across the warp with a 12-shuffle transpose reduction
+// (instead of 10 x 5 butterfly shuffles); 10 lanes then issue one float atomic
+// each into the per-Gaussian accumulator.
 #include "gsb_common.cuh"
 
 namespace gsb {
 namespace {
 
-constexpr int THREADS = 256;
-constexpr int FWD_BATCH = 256;
-constexpr int BWD_BATCH = 128;
+constexpr int THREADS = 128;
+constexpr int BATCH = 128;
 constexpr unsigned FULL = 0xffffffffu;
 
-__device__ __forceinline__ void pixel_of(int tile, int gx, int& px, int& py) {
+// Pixel coordinates of the thread's two pixels.
+__device__ __forceinline__ void pixels_of(int tile, int gx, int& px, int& py0) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tx = tile % gx, ty = tile / gx;
   px = tx * BLOCK_X + (warp & 1) * 8 + (lane & 7);
-  py = ty * BLOCK_Y + (warp >> 1) * 4 + (lane >> 3);
+  py0 = ty * BLOCK_Y + (warp >> 1) * 8 + (lane >> 3);
+}
+
+__device__ __forceinline__ float fast_rcp(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 template <bool DEPTH>
 __global__ void __launch_bounds__(THREADS) render_fwd_kernel(const gsb_render_fwd_args a, int gx) {
-  __shared__ float2 s_xy[FWD_BATCH];
-  __shared__ float4 s_cop[FWD_BATCH];   // conic a, b, c, opacity
-  __shared__ float4 s_rgbd[FWD_BATCH];  // r, g, b, depth
+  __shared__ float2 s_xy[BATCH];
+  __shared__ float4 s_cop[BATCH];   // conic a, b, c, opacity
+  __shared__ float4 s_rgbd[BATCH];  // r, g, b, depth
   const int tile = blockIdx.x;
-  int pxi, pyi;
-  pixel_of(tile, gx, pxi, pyi);
-  const bool inside = pxi < a.W && pyi < a.H;
+  int pxi, py0;
+  pixels_of(tile, gx, pxi, py0);
   const int2 range = reinterpret_cast<const int2*>(a.ranges)[tile];
   const float4* rec = reinterpret_cast<const float4*>(a.records);
-  const float fx = (float)pxi, fy = (float)pyi;
-
-  float T = 1.0f, c0 = 0.0f, c1 = 0.0f, c2 = 0.0f, wsum = 0.0f, dacc = 0.0f;
-  int last = 0;
-  bool done = !inside;
-  for (int b = range.x; b < range.y; b += FWD_BATCH) {
-    if (__syncthreads_count(done) == THREADS) break;
+  const float fx = (float)pxi;
+  float fy[2], T[2], c0[2], c1[2], c2[2], wsum[2], dacc[2];
+  int last[2];
+  bool inside[2], done[2];
+#pragma unroll
+  for (int p = 0; p < 2; ++p) {
+    const int py = py0 + 4 * p;
+    fy[p] = (float)py;
+    inside[p] = pxi < a.W && py < a.H;
+    done[p] = !inside[p];
+    T[p] = 1.0f;
+    c0[p] = c1[p] = c2[p] = wsum[p] = dacc[p] = 0.0f;
+    last[p] = 0;
+  }
+  for (int b = range.x; b < range.y; b += BATCH) {
+    if (__syncthreads_count(done[0] && done[1]) == THREADS) break;
     const int i = b + threadIdx.x;
     if (i < range.y) {
       const int id = a.point_list[i];
@@ -66,42 +82,49 @@ __global__ void __launch_bounds__(THREADS) render_fwd_kernel(const gsb_render_fw
       s_rgbd[threadIdx.x] = make_float4(q2.x, q2.y, q2.z, q1.z);
     }
     __syncthreads();
-    const int cnt = min(FWD_BATCH, range.y - b);
-    if (!done) {
-      for (int j = 0; j < cnt; ++j) {
-        const float2 xy = s_xy[j];
-        const float4 co = s_cop[j];
-        const float dx = xy.x - fx, dy = xy.y - fy;
-        const float power = -0.5f * (co.x * dx * dx + co.z * dy * dy) - co.y * dx * dy;
+    const int cnt = min(BATCH, range.y - b);
+    for (int j = 0; j < cnt; ++j) {
+      if (done[0] && done[1]) break;
+      const float2 xy = s_xy[j];
+      const float4 co = s_cop[j];
+      const float dx = xy.x - fx;
+      const float adx2 = co.x * dx * dx;
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        if (done[p]) continue;
+        const float dy = xy.y - fy[p];
+        const float power = -0.5f * (adx2 + co.z * dy * dy) - co.y * dx * dy;
         if (power > 0.0f) continue;
         const float alpha = fminf(0.99f, co.w * fast_exp(power));
         if (alpha < (1.0f / 255.0f)) continue;
-        const float test_T = T * (1.0f - alpha);
+        const float test_T = T[p] * (1.0f - alpha);
         if (test_T < 0.0001f) {
-          done = true;
-          break;
+          done[p] = true;
+          continue;
         }
-        const float contrib = alpha * T;
+        const float contrib = alpha * T[p];
         const float4 cd = s_rgbd[j];
-        c0 += cd.x * contrib;
-        c1 += cd.y * contrib;
-        c2 += cd.z * contrib;
-        wsum += contrib;
-        if (DEPTH) dacc += cd.w * contrib;
-        T = test_T;
-        last = b - range.x + j + 1;
+        c0[p] += cd.x * contrib;
+        c1[p] += cd.y * contrib;
+        c2[p] += cd.z * contrib;
+        wsum[p] += contrib;
+        if (DEPTH) dacc[p] += cd.w * contrib;
+        T[p] = test_T;
+        last[p] = b - range.x + j + 1;
       }
     }
   }
-  if (inside) {
-    const long long npix = (long long)a.W * a.H;
-    const long long pix = (long long)pyi * a.W + pxi;
-    a.n_contrib[pix] = last;
-    a.out_color[pix] = c0 + T * a.background[0];
-    a.out_color[npix + pix] = c1 + T * a.background[1];
-    a.out_color[2 * npix + pix] = c2 + T * a.background[2];
-    a.out_alpha[pix] = wsum;
-    a.out_depth[pix] = dacc;
+  const long long npix = (long long)a.W * a.H;
+#pragma unroll
+  for (int p = 0; p < 2; ++p) {
+    if (!inside[p]) continue;
+    const long long pix = (long long)(py0 + 4 * p) * a.W + pxi;
+    a.n_contrib[pix] = last[p];
+    a.out_color[pix] = c0[p] + T[p] * a.background[0];
+    a.out_color[npix + pix] = c1[p] + T[p] * a.background[1];
+    a.out_color[2 * npix + pix] = c2[p] + T[p] * a.background[2];
+    a.out_alpha[pix] = wsum[p];
+    a.out_depth[pix] = dacc[p];
   }
 }
 
@@ -151,37 +174,102 @@ __device__ __forceinline__ int warp_reduce10(const float (&v)[10], float& out) {
   return off < 0 ? -1 : (b4 ? 5 : 0) + off;
 }
 
+// Back-to-front state of one pixel (backward_kernels.py:606-625).
+struct BwdPixel {
+  int lc;
+  float fy, T, T_final, g0, g1, g2, gd, ga, bg_dot;
+  float ar0, ar1, ar2, adr, aar, la, lc0, lc1, lc2, ld;
+};
+
+// One pixel's contribution of the Gaussian at this position, added to v[]
+// (backward_kernels.py:637-685).  Returns whether the pixel contributed.
+template <bool DEPTH>
+__device__ __forceinline__ bool bwd_pixel(BwdPixel& s, float dx, float adx2, const float2 xy,
+                                          const float4 co, const float4 cd, float ddelx_dx,
+                                          float ddely_dy, float (&v)[10]) {
+  const float dy = xy.y - s.fy;
+  const float power = -0.5f * (adx2 + co.z * dy * dy) - co.y * dx * dy;
+  if (power > 0.0f) return false;
+  const float G = fast_exp(power);
+  const float alpha = fminf(0.99f, co.w * G);
+  if (alpha < (1.0f / 255.0f)) return false;
+  const float oma = fmaxf(1.0f - alpha, 1.0e-5f);
+  const float inv_oma = fast_rcp(oma);
+  s.T = s.T * inv_oma;
+  const float dchannel = alpha * s.T;
+  s.ar0 = s.la * s.lc0 + (1.0f - s.la) * s.ar0;
+  s.ar1 = s.la * s.lc1 + (1.0f - s.la) * s.ar1;
+  s.ar2 = s.la * s.lc2 + (1.0f - s.la) * s.ar2;
+  s.lc0 = cd.x;
+  s.lc1 = cd.y;
+  s.lc2 = cd.z;
+  float dL_dopa = (cd.x - s.ar0) * s.g0 + (cd.y - s.ar1) * s.g1 + (cd.z - s.ar2) * s.g2;
+  v[7] += dchannel * s.g0;
+  v[8] += dchannel * s.g1;
+  v[9] += dchannel * s.g2;
+  if (DEPTH) {
+    s.adr = s.la * s.ld + (1.0f - s.la) * s.adr;
+    s.ld = cd.w;
+    dL_dopa += (cd.w - s.adr) * s.gd;
+    v[2] += dchannel * s.gd;
+  }
+  s.aar = s.la + (1.0f - s.la) * s.aar;
+  dL_dopa += (1.0f - s.aar) * s.ga;
+  dL_dopa *= s.T;
+  s.la = alpha;
+  dL_dopa += (-s.T_final * inv_oma) * s.bg_dot;
+  const float dL_dG = co.w * dL_dopa;
+  const float gdx = G * dx, gdy = G * dy;
+  const float dG_ddelx = -gdx * co.x - gdy * co.y;
+  const float dG_ddely = -gdy * co.z - gdx * co.y;
+  v[0] += dL_dG * dG_ddelx * ddelx_dx;
+  v[1] += dL_dG * dG_ddely * ddely_dy;
+  v[3] += -0.5f * gdx * dx * dL_dG;
+  v[4] += -0.5f * gdx * dy * dL_dG;
+  v[5] += -0.5f * gdy * dy * dL_dG;
+  v[6] += G * dL_dopa;
+  return true;
+}
+
 template <bool DEPTH>
 __global__ void __launch_bounds__(THREADS) render_bwd_kernel(const gsb_render_bwd_args a, int gx) {
-  __shared__ int s_id[BWD_BATCH];
-  __shared__ float2 s_xy[BWD_BATCH];
-  __shared__ float4 s_cop[BWD_BATCH];
-  __shared__ float4 s_rgbd[BWD_BATCH];
+  __shared__ int s_id[BATCH];
+  __shared__ float2 s_xy[BATCH];
+  __shared__ float4 s_cop[BATCH];
+  __shared__ float4 s_rgbd[BATCH];
   __shared__ int s_max[THREADS / 32];
   const int tile = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  int pxi, pyi;
-  pixel_of(tile, gx, pxi, pyi);
-  const bool inside = pxi < a.W && pyi < a.H;
+  int pxi, py0;
+  pixels_of(tile, gx, pxi, py0);
   const int2 range = reinterpret_cast<const int2*>(a.ranges)[tile];
   const int n = range.y - range.x;
   const float4* rec = reinterpret_cast<const float4*>(a.records);
-
   const long long npix = (long long)a.W * a.H;
-  const long long pix = (long long)pyi * a.W + pxi;
-  int lc = 0;
-  float T_final = 0.0f, g0 = 0.0f, g1 = 0.0f, g2 = 0.0f, gd = 0.0f, ga = 0.0f, bg_dot = 0.0f;
-  if (inside && n > 0) {
-    lc = a.n_contrib[pix];
-    T_final = 1.0f - a.out_alpha[pix];
-    g0 = a.grad_color[pix];
-    g1 = a.grad_color[npix + pix];
-    g2 = a.grad_color[2 * npix + pix];
-    if (DEPTH) gd = a.grad_depth[pix];
-    ga = a.grad_alpha[pix];
-    bg_dot = a.background[0] * g0 + a.background[1] * g1 + a.background[2] * g2;
+
+  BwdPixel px[2];
+#pragma unroll
+  for (int p = 0; p < 2; ++p) {
+    BwdPixel& s = px[p];
+    const int py = py0 + 4 * p;
+    s.fy = (float)py;
+    s.lc = 0;
+    s.T_final = s.g0 = s.g1 = s.g2 = s.gd = s.ga = s.bg_dot = 0.0f;
+    if (pxi < a.W && py < a.H && n > 0) {
+      const long long pix = (long long)py * a.W + pxi;
+      s.lc = a.n_contrib[pix];
+      s.T_final = 1.0f - a.out_alpha[pix];
+      s.g0 = a.grad_color[pix];
+      s.g1 = a.grad_color[npix + pix];
+      s.g2 = a.grad_color[2 * npix + pix];
+      if (DEPTH && a.grad_depth) s.gd = a.grad_depth[pix];
+      if (a.grad_alpha) s.ga = a.grad_alpha[pix];
+      s.bg_dot = a.background[0] * s.g0 + a.background[1] * s.g1 + a.background[2] * s.g2;
+    }
+    s.T = s.T_final;
+    s.ar0 = s.ar1 = s.ar2 = s.adr = s.aar = s.la = s.lc0 = s.lc1 = s.lc2 = s.ld = 0.0f;
   }
-  const int warp_max = __reduce_max_sync(FULL, lc);
+  const int warp_max = __reduce_max_sync(FULL, max(px[0].lc, px[1].lc));
   if (lane == 0) s_max[warp] = warp_max;
   __syncthreads();
   int cta_max = 0;
@@ -192,13 +280,10 @@ __global__ void __launch_bounds__(THREADS) render_bwd_kernel(const gsb_render_bw
 
   const float ddelx_dx = 0.5f * (float)a.W;
   const float ddely_dy = 0.5f * (float)a.H;
-  const float fx = (float)pxi, fy = (float)pyi;
-  float T = T_final;
-  float ar0 = 0.0f, ar1 = 0.0f, ar2 = 0.0f, adr = 0.0f, aar = 0.0f;
-  float la = 0.0f, lc0 = 0.0f, lc1 = 0.0f, lc2 = 0.0f, ld = 0.0f;
+  const float fx = (float)pxi;
 
-  for (int hi = cta_max; hi > 0; hi -= BWD_BATCH) {
-    const int lo = max(0, hi - BWD_BATCH);
+  for (int hi = cta_max; hi > 0; hi -= BATCH) {
+    const int lo = max(0, hi - BATCH);
     __syncthreads();
     for (int k = threadIdx.x; k < hi - lo; k += THREADS) {
       const int id = a.point_list[range.x + lo + k];
@@ -218,54 +303,14 @@ __global__ void __launch_bounds__(THREADS) render_bwd_kernel(const gsb_render_bw
 #pragma unroll
       for (int k = 0; k < 10; ++k) v[k] = 0.0f;
       bool contrib = false;
-      if (pos < lc) {
+      if (pos < px[0].lc || pos < px[1].lc) {
         const float2 xy = s_xy[j];
         const float4 co = s_cop[j];
-        const float dx = xy.x - fx, dy = xy.y - fy;
-        const float power = -0.5f * (co.x * dx * dx + co.z * dy * dy) - co.y * dx * dy;
-        if (power <= 0.0f) {
-          const float G = fast_exp(power);
-          const float alpha = fminf(0.99f, co.w * G);
-          if (alpha >= (1.0f / 255.0f)) {
-            contrib = true;
-            const float oma = fmaxf(1.0f - alpha, 1.0e-5f);
-            const float inv_oma = __frcp_rn(oma);
-            T = T * inv_oma;
-            const float dchannel = alpha * T;
-            const float4 cd = s_rgbd[j];
-            ar0 = la * lc0 + (1.0f - la) * ar0;
-            ar1 = la * lc1 + (1.0f - la) * ar1;
-            ar2 = la * lc2 + (1.0f - la) * ar2;
-            lc0 = cd.x;
-            lc1 = cd.y;
-            lc2 = cd.z;
-            float dL_dopa = (cd.x - ar0) * g0 + (cd.y - ar1) * g1 + (cd.z - ar2) * g2;
-            v[7] = dchannel * g0;
-            v[8] = dchannel * g1;
-            v[9] = dchannel * g2;
-            if (DEPTH) {
-              adr = la * ld + (1.0f - la) * adr;
-              ld = cd.w;
-              dL_dopa += (cd.w - adr) * gd;
-              v[2] = dchannel * gd;
-            }
-            aar = la + (1.0f - la) * aar;
-            dL_dopa += (1.0f - aar) * ga;
-            dL_dopa *= T;
-            la = alpha;
-            dL_dopa += (-T_final * inv_oma) * bg_dot;
-            const float dL_dG = co.w * dL_dopa;
-            const float gdx = G * dx, gdy = G * dy;
-            const float dG_ddelx = -gdx * co.x - gdy * co.y;
-            const float dG_ddely = -gdy * co.z - gdx * co.y;
-            v[0] = dL_dG * dG_ddelx * ddelx_dx;
-            v[1] = dL_dG * dG_ddely * ddely_dy;
-            v[3] = -0.5f * gdx * dx * dL_dG;
-            v[4] = -0.5f * gdx * dy * dL_dG;
-            v[5] = -0.5f * gdy * dy * dL_dG;
-            v[6] = G * dL_dopa;
-          }
-        }
+        const float4 cd = s_rgbd[j];
+        const float dx = xy.x - fx;
+        const float adx2 = co.x * dx * dx;
+        if (pos < px[0].lc) contrib |= bwd_pixel<DEPTH>(px[0], dx, adx2, xy, co, cd, ddelx_dx, ddely_dy, v);
+        if (pos < px[1].lc) contrib |= bwd_pixel<DEPTH>(px[1], dx, adx2, xy, co, cd, ddelx_dx, ddely_dy, v);
       }
       if (__any_sync(FULL, contrib)) {
         float sum;
@@ -301,8 +346,7 @@ GSB_EXPORT int gsb_render_fwd(const gsb_render_fwd_args* a, void* stream) {
 
 GSB_EXPORT int gsb_render_bwd(const gsb_render_bwd_args* a, void* stream) {
   if (!a || a->W <= 0 || a->H <= 0 || a->P < 0 || !a->ranges || !a->records ||
-      !a->background || !a->out_alpha || !a->n_contrib || !a->grad_color || !a->grad_alpha ||
-      (a->compute_depth && !a->grad_depth) || !a->grad_acc) {
+      !a->background || !a->out_alpha || !a->n_contrib || !a->grad_color || !a->grad_acc) {
     set_error("gsb_render_bwd: invalid arguments");
     return GSB_ERR_INVALID;
   }

@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define GSB_ABI_VERSION 1
+#define GSB_ABI_VERSION 2
 
 #define GSB_OK 0
 #define GSB_ERR_INVALID (-1)  /* bad argument: ValueError in Python          */
@@ -88,6 +88,8 @@ typedef struct {
   float* depths;        /* (P) */
   int* tiles_touched;   /* (P) */
   float* records;       /* (P,12) render records */
+  float* cov3d_out;     /* (P,6) 3D covariance of the scale/rotation path, or NULL
+                           (only the packed raw-compat geometry buffer needs it) */
 } gsb_preprocess_args;
 
 int gsb_preprocess_fwd(const gsb_preprocess_args* a, void* stream);
@@ -176,8 +178,8 @@ typedef struct {
   const float* out_alpha;
   const int* n_contrib;
   const float* grad_color;  /* (3,H,W) */
-  const float* grad_depth;  /* (1,H,W) */
-  const float* grad_alpha;  /* (1,H,W) */
+  const float* grad_depth;  /* (1,H,W) or NULL (zero gradient) */
+  const float* grad_alpha;  /* (1,H,W) or NULL (zero gradient) */
   float* grad_acc;          /* (P,12), accumulated with atomics */
 } gsb_render_bwd_args;
 
@@ -205,9 +207,9 @@ typedef struct {
   int sh_degree, sh_coeffs;
   const float* records;        /* forward records (clamped bits) */
   const float* grad_acc;       /* (P,12) from gsb_render_bwd */
-  const float* grad_proj_2d;   /* (P,2) user gradient of proj_2D */
-  const float* grad_conic_2d;  /* (P,3) */
-  const float* grad_conic_2d_inv; /* (P,3) */
+  const float* grad_proj_2d;   /* (P,2) user gradient of proj_2D, or NULL (zero) */
+  const float* grad_conic_2d;  /* (P,3) or NULL */
+  const float* grad_conic_2d_inv; /* (P,3) or NULL */
   int accumulate;              /* 1: add into the outputs instead of storing */
   /* outputs (NULL where not applicable) */
   float* grad_means3d;   /* (P,3) */
