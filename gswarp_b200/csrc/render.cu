@@ -45,17 +45,45 @@ __device__ __forceinline__ float fast_rcp(float x) {
   return y;
 }
 
+// Conservative screen box of the pixels where this Gaussian can reach
+// alpha >= 1/255: op*exp(-q/2) >= 1/255  <=>  q = d^T conic d <= t with
+// t = 2 ln(255 op); the ellipse {q <= t} has half-extents sqrt(t*cov_xx),
+// sqrt(t*cov_yy) (cov = conic^-1).  Widened by 1% + 0.5 px so rounding in
+// the per-pixel test can never reach outside it.  A conic that is not
+// positive definite gets an unbounded box (never culled); t <= 0 (opacity
+// below 1/255) an empty one.
+__device__ __forceinline__ float4 alpha_box(float x, float y, float a, float b, float c, float op) {
+  const float det = a * c - b * b;
+  const float inf = __int_as_float(0x7f800000);
+  if (!(a > 0.0f) || !(det > 0.0f)) return make_float4(-inf, inf, -inf, inf);
+  const float t = 2.0f * __logf(255.0f * op);
+  if (!(t > 0.0f)) return make_float4(inf, -inf, inf, -inf);
+  const float inv = 1.0f / det;
+  const float ex = sqrtf(t * c * inv) * 1.01f + 0.5f;
+  const float ey = sqrtf(t * a * inv) * 1.01f + 0.5f;
+  return make_float4(x - ex, x + ex, y - ey, y + ey);
+}
+
+__device__ __forceinline__ bool box_hits(const float4 b, float x0, float x1, float y0, float y1) {
+  return b.x <= x1 && b.y >= x0 && b.z <= y1 && b.w >= y0;
+}
+
 template <bool DEPTH>
 __global__ void __launch_bounds__(THREADS) render_fwd_kernel(const gsb_render_fwd_args a, int gx) {
   __shared__ float2 s_xy[BATCH];
   __shared__ float4 s_cop[BATCH];   // conic a, b, c, opacity
   __shared__ float4 s_rgbd[BATCH];  // r, g, b, depth
+  __shared__ float4 s_box[BATCH];   // alpha_box
   const int tile = blockIdx.x;
+  const int lane = threadIdx.x & 31;
   int pxi, py0;
   pixels_of(tile, gx, pxi, py0);
   const int2 range = reinterpret_cast<const int2*>(a.ranges)[tile];
   const float4* rec = reinterpret_cast<const float4*>(a.records);
   const float fx = (float)pxi;
+  // the warp's 8x8 pixel block
+  const float bx0 = (float)(__shfl_sync(FULL, pxi, 0)), by0 = (float)(__shfl_sync(FULL, py0, 0));
+  const float bx1 = bx0 + 7.0f, by1 = by0 + 7.0f;
   float fy[2], T[2], c0[2], c1[2], c2[2], wsum[2], dacc[2];
   int last[2];
   bool inside[2], done[2];
@@ -80,11 +108,20 @@ __global__ void __launch_bounds__(THREADS) render_fwd_kernel(const gsb_render_fw
       s_xy[threadIdx.x] = make_float2(q0.x, q0.y);
       s_cop[threadIdx.x] = make_float4(q0.z, q0.w, q1.x, q1.y);
       s_rgbd[threadIdx.x] = make_float4(q2.x, q2.y, q2.z, q1.z);
+      s_box[threadIdx.x] = alpha_box(q0.x, q0.y, q0.z, q0.w, q1.x, q1.y);
     }
     __syncthreads();
     const int cnt = min(BATCH, range.y - b);
-    for (int j = 0; j < cnt; ++j) {
-      if (done[0] && done[1]) break;
+    // Each lane tests one staged Gaussian against the warp's block; the warp
+    // then visits only the hits, in front-to-back order.
+    for (int cb = 0; cb < cnt; cb += 32) {
+      if (__all_sync(FULL, done[0] && done[1])) break;
+      const int g = cb + lane;
+      unsigned hits = __ballot_sync(FULL, g < cnt && box_hits(s_box[g], bx0, bx1, by0, by1));
+      while (hits) {
+      const int j = cb + __ffs(hits) - 1;
+      hits &= hits - 1;
+      if (done[0] && done[1]) continue;
       const float2 xy = s_xy[j];
       const float4 co = s_cop[j];
       const float dx = xy.x - fx;
@@ -111,6 +148,7 @@ __global__ void __launch_bounds__(THREADS) render_fwd_kernel(const gsb_render_fw
         if (DEPTH) dacc[p] += cd.w * contrib;
         T[p] = test_T;
         last[p] = b - range.x + j + 1;
+      }
       }
     }
   }
@@ -237,6 +275,7 @@ __global__ void __launch_bounds__(THREADS) render_bwd_kernel(const gsb_render_bw
   __shared__ float2 s_xy[BATCH];
   __shared__ float4 s_cop[BATCH];
   __shared__ float4 s_rgbd[BATCH];
+  __shared__ float4 s_box[BATCH];
   __shared__ int s_max[THREADS / 32];
   const int tile = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -281,6 +320,8 @@ __global__ void __launch_bounds__(THREADS) render_bwd_kernel(const gsb_render_bw
   const float ddelx_dx = 0.5f * (float)a.W;
   const float ddely_dy = 0.5f * (float)a.H;
   const float fx = (float)pxi;
+  const float bx0 = (float)(__shfl_sync(FULL, pxi, 0)), by0 = (float)(__shfl_sync(FULL, py0, 0));
+  const float bx1 = bx0 + 7.0f, by1 = by0 + 7.0f;
 
   for (int hi = cta_max; hi > 0; hi -= BATCH) {
     const int lo = max(0, hi - BATCH);
@@ -294,11 +335,19 @@ __global__ void __launch_bounds__(THREADS) render_bwd_kernel(const gsb_render_bw
       s_xy[k] = make_float2(q0.x, q0.y);
       s_cop[k] = make_float4(q0.z, q0.w, q1.x, q1.y);
       s_rgbd[k] = make_float4(q2.x, q2.y, q2.z, q1.z);
+      s_box[k] = alpha_box(q0.x, q0.y, q0.z, q0.w, q1.x, q1.y);
     }
     __syncthreads();
     const int top = min(hi, warp_max);
-    for (int pos = top - 1; pos >= lo; --pos) {
-      const int j = pos - lo;
+    // Lanes test staged Gaussians against the warp's 8x8 block; the warp
+    // visits only the hits below its own maximum, back to front.
+    for (int cb = ((top - lo - 1) >> 5) << 5; cb >= 0 && top > lo; cb -= 32) {
+      const int g = cb + lane;
+      unsigned hits = __ballot_sync(FULL, g < top - lo && box_hits(s_box[g], bx0, bx1, by0, by1));
+      while (hits) {
+      const int j = cb + 31 - __clz(hits);
+      hits &= ~(1u << (j - cb));
+      const int pos = lo + j;
       float v[10];
 #pragma unroll
       for (int k = 0; k < 10; ++k) v[k] = 0.0f;
@@ -319,6 +368,7 @@ __global__ void __launch_bounds__(THREADS) render_bwd_kernel(const gsb_render_bw
           const int off = slot < 3 ? slot : slot + 1;
           atomicAdd(a.grad_acc + (size_t)s_id[j] * GSB_GRAD_FLOATS + off, sum);
         }
+      }
       }
     }
   }
