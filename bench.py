@@ -127,22 +127,29 @@ def make_scene(args, device, rank):
 
 
 class Trainer:
-    """Parameters, the flat gradient buffer and one data-parallel step
-    (gswarp_b200.view_sharding) rendering this rank's views through the
-    public API."""
+    """Parameters, the flat gradient buffer and one data-parallel step over
+    this rank's views, through one of two public paths:
 
-    def __init__(self, scene, views, targets_dev, targets_host, world, device):
+    * ``fused``    -- gswarp_b200.training.FusedViewStep: the C ABI stage by
+      stage with the photometric loss kernels and preprocess backward
+      accumulating into the flat gradient buffer (no autograd);
+    * ``autograd`` -- the drop-in path: gswarp_b200.GaussianRasterizer +
+      fused_ssim under autograd (gswarp_b200.view_sharding.ViewShardedStep).
+    """
+
+    def __init__(self, scene, views, targets_dev, targets_host, world, device, path="fused"):
         import torch
 
         import gswarp_b200 as gs
+        from gswarp_b200.training import FusedViewStep
         from gswarp_b200.view_sharding import ViewShardedStep
 
         self.gs = gs
         self.torch = torch
+        self.path = path
         self.N = scene.n
         self.device = device
         self.world = world
-        # parameters (rasterizer inputs); their .grad are views of one flat buffer
         self.means = scene.means.contiguous().requires_grad_(True)
         self.scales = scene.scales.contiguous().requires_grad_(True)
         self.rots = scene.rotations.contiguous().requires_grad_(True)
@@ -159,12 +166,16 @@ class Trainer:
                 scale_modifier=1.0, viewmatrix=v.viewmatrix, projmatrix=v.projmatrix, sh_degree=3,
                 campos=v.campos, prefiltered=False)
             for v in views]
-        self.means2d = torch.zeros_like(self.means, requires_grad=True)
         self.loss_host = torch.zeros(len(views), dtype=torch.float32).pin_memory() if targets_host else None
-        self.stage_tgt = [torch.empty_like(t) for t in targets_dev] if targets_host else None
-        self.e2e = False
-        self.dp = ViewShardedStep(self.params, range(len(views)), self._view_loss)
-        self.flat = self.dp.grads.flat
+        if path == "fused":
+            self.fused = FusedViewStep(self.params, self.settings, l1_weight=1.0, ssim_weight=0.2)
+            self.flat = self.fused.grads.flat
+        else:
+            self.means2d = torch.zeros_like(self.means, requires_grad=True)
+            self.stage_tgt = [torch.empty_like(t) for t in targets_dev] if targets_host else None
+            self.e2e = False
+            self.dp = ViewShardedStep(self.params, range(len(views)), self._view_loss)
+            self.flat = self.dp.grads.flat
 
     def _view_loss(self, i):
         gs = self.gs
@@ -181,11 +192,14 @@ class Trainer:
         return l1 + 0.2 * (1.0 - ssim)
 
     def step(self, e2e: bool = False):
-        self.e2e = e2e
-        res = self.dp.step()
+        if self.path == "fused":
+            losses = self.fused.step(self.targets_host if e2e else self.targets_dev)[:, 0]
+        else:
+            self.e2e = e2e
+            losses = self.torch.stack(self.dp.step().losses)
         if e2e:
-            self.loss_host.copy_(self.torch.stack(res.losses), non_blocking=True)
-        return res.losses
+            self.loss_host.copy_(losses, non_blocking=True)
+        return losses
 
 
 def timed(fn, steps, warmup, world):
@@ -230,8 +244,8 @@ def kernel_profile(trainer, steps=2):
     out = {}
     for name, evs in _pipeline.TIMERS.items():
         ts = [a.elapsed_time(b) for a, b, _ in evs]
-        out[name] = {"launches": len(ts), "total_ms": sum(ts), "mean_ms": sum(ts) / max(len(ts), 1),
-                     "extra": [x for _, _, x in evs]}
+        out[name] = {"launches": len(ts), "kernels": sum(x.get("kernels", 1) for _, _, x in evs),
+                     "total_ms": sum(ts), "mean_ms": sum(ts) / max(len(ts), 1), "extra": [x for _, _, x in evs]}
     _pipeline.TIMERS.clear()
     return out
 
@@ -246,10 +260,14 @@ def measure_cfg2(device, steps, warmup):
     scene = wl.config2_scene(seed=0, n=1_000_000).to(device)
     view = wl.config2_view(seed=0).to(device)
     tgt = wl.target_image(0).to(device)
-    tr = Trainer(scene, [view], [tgt], None, 1, device)
-    ms = timed(tr.step, steps, warmup, 1)
-    return {"views_per_s": 1000.0 * steps / ms, "ms_per_view": ms / steps, "gaussians": 1_000_000,
-            "width": 1920, "height": 1080}
+    out = {"gaussians": 1_000_000, "width": 1920, "height": 1080, "loss": "L1 + 0.2 (1 - SSIM)"}
+    for path in ("fused", "autograd"):
+        tr = Trainer(scene, [view], [tgt], None, 1, device, path=path)
+        ms = timed(tr.step, steps, warmup, 1)
+        out[path] = {"views_per_s": 1000.0 * steps / ms, "ms_per_view": ms / steps}
+        del tr
+    out["views_per_s"] = out["fused"]["views_per_s"]
+    return out
 
 
 def cpu_baseline_sample(views, scene_cpu, band_rows=136):
@@ -309,15 +327,16 @@ def roofline(prof, peaks, pixels, N):
     R = extra.get("num_rendered", 0)
     E = extra.get("pairs", 0)
     P = extra.get("P", N)
-    # algorithmic bytes per launch (per-unit figures: see DESIGN.md)
+    # algorithmic bytes per launch: per-unit bytes the stage must move x units
     per_launch = {
         "render_bwd": 44 * R + 28 * pixels + 40 * P,
         "render_fwd": 44 * R + 24 * pixels,
         "preprocess_fwd": 316 * P,
-        "preprocess_bwd": 528 * P,
+        # accumulate mode: 288 B read + 236 B read-modify-written per visible Gaussian, 4 B (radius) otherwise
+        "preprocess_bwd": 760 * extra.get("visible", P) + 4 * (P - extra.get("visible", P)),
         "binning": 8 * P + 12 * R + 24 * R + 8 * R,
-        "ssim_fwd": 20 * pixels,
-        "ssim_bwd": 24 * pixels,
+        "loss_fwd": 60 * pixels,
+        "loss_bwd": 72 * pixels,
     }.get(name, 0)
     peak = peaks.get("hbm_gbs", 6650.0)
     achieved = per_launch / mean_s / 1e9 if mean_s > 0 else 0.0
@@ -407,8 +426,19 @@ def run_ours(args):
         e2e = {"value": 1000.0 * views_total / ms_e2e, "unit": "views/s", "h2d_bytes_per_step": img_bytes,
                "d2h_bytes_per_step": V * 4}
 
+    # the drop-in autograd path on the same workload, for comparison
+    tr_ag = Trainer(scene, views, targets_dev, targets_host, world, device, path="autograd")
+    ms_ag = timed(tr_ag.step, args.steps, args.warmup, world)
+    autograd_api = {"value": 1000.0 * views_total / ms_ag, "unit": "views/s",
+                    "path": "GaussianRasterizer + fused_ssim under autograd, ViewShardedStep"}
+    if not args.no_e2e:
+        ms_ag_e2e = timed(lambda: tr_ag.step(e2e=True), args.steps, 1, world)
+        autograd_api["e2e"] = 1000.0 * views_total / ms_ag_e2e
+    del tr_ag
+    torch.cuda.empty_cache()
+
     prof = kernel_profile(tr, steps=1)
-    launches = sum(v["launches"] for v in prof.values())
+    launches = sum(v["kernels"] for v in prof.values())
     rl = roofline(prof, peaks, args.width * args.height, scene.n)
 
     extra = {}
@@ -433,6 +463,9 @@ def run_ours(args):
                        "l2": "inputs larger than L2 (6M-Gaussian scene, 1.4 GB of parameters)"},
             "clocks": clocks,
             "e2e": e2e,
+            "path": "gswarp_b200.training.FusedViewStep (C ABI stages, fused photometric loss, preprocess "
+                    "backward accumulating into the flat gradient buffer)",
+            "autograd_api": autograd_api,
             "gpu_launches": launches * args.steps,
             "roofline": rl,
             "kernels": {k: {kk: vv for kk, vv in v.items() if kk != "extra"} for k, v in prof.items()},

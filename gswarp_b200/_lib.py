@@ -24,7 +24,7 @@ GSB_ERR_OVERFLOW = -2
 GSB_ERR_CUDA = -3
 GSB_ERR_TIMEOUT = -4
 
-ABI_VERSION = 2
+ABI_VERSION = 3
 RECORD_FLOATS = 12
 GRAD_FLOATS = 12
 
@@ -120,6 +120,22 @@ class SSIMBwdArgs(ctypes.Structure):
     ]
 
 
+class PhotoLossFwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("B", c_int), ("C", c_int), ("H", c_int), ("W", c_int),
+        ("C1", c_float), ("C2", c_float), ("w_l1", c_float), ("w_ssim", c_float),
+        ("img", vp), ("target", vp), ("dm", vp), ("partials", vp), ("loss_out", vp),
+    ]
+
+
+class PhotoLossBwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("B", c_int), ("C", c_int), ("H", c_int), ("W", c_int),
+        ("w_l1", c_float), ("w_ssim", c_float), ("upstream", c_float),
+        ("img", vp), ("target", vp), ("dm", vp), ("grad_img", vp),
+    ]
+
+
 class KNNArgs(ctypes.Structure):
     _fields_ = [
         ("P", c_int), ("points", vp), ("out", vp), ("error_word", vp),
@@ -135,7 +151,8 @@ EXPORTED = (
     "gsb_bin_count_workspace_bytes", "gsb_bin_count", "gsb_bin_sort_workspace_bytes",
     "gsb_bin_emit_sort", "gsb_render_fwd", "gsb_render_bwd", "gsb_preprocess_bwd",
     "gsb_ssim_partials_count", "gsb_ssim_fwd", "gsb_ssim_bwd", "gsb_knn_workspace_bytes",
-    "gsb_knn", "gsb_selftest_threshold_log",
+    "gsb_knn", "gsb_selftest_threshold_log", "gsb_ssim_fwd_noalloc", "gsb_photo_loss_fwd",
+    "gsb_photo_loss_bwd",
 )
 
 
@@ -160,6 +177,8 @@ def _declare(L) -> None:
     fn("gsb_ssim_partials_count", c_int, [c_int, c_int, c_int, c_int])
     fn("gsb_ssim_fwd", c_int, [P(SSIMFwdArgs), vp])
     fn("gsb_ssim_bwd", c_int, [P(SSIMBwdArgs), vp])
+    fn("gsb_photo_loss_fwd", c_int, [P(PhotoLossFwdArgs), vp])
+    fn("gsb_photo_loss_bwd", c_int, [P(PhotoLossBwdArgs), vp])
     fn("gsb_knn_workspace_bytes", ctypes.c_size_t, [c_int])
     fn("gsb_knn", c_int, [P(KNNArgs), vp])
     fn("gsb_selftest_threshold_log", c_int, [vp, vp, c_ll, vp])

@@ -401,8 +401,11 @@ def preprocess_backward(g: Gaussians, cam: Camera, radii, records, grad_acc, gra
     a.grad_sh = _lib.ptr(out.grad_sh)
     a.grad_colors = _lib.ptr(out.grad_colors)
     a.grad_cov3d = _lib.ptr(out.grad_cov3D)
-    with _stage_timer("preprocess_bwd", {"P": P, "kernels": 1}):
+    info = {"P": P, "kernels": 1, "accumulate": acc}
+    with _stage_timer("preprocess_bwd", info):
         _lib.call("gsb_preprocess_bwd", a, _lib.stream_handle(dev))
+    if TIMING_ENABLED:
+        info["visible"] = int((radii > 0).sum())
     return out
 
 

@@ -44,53 +44,21 @@ __device__ __forceinline__ void dnormvdv(const float v[3], const float g[3], flo
   out[2] = (-v[0] * v[2] * g[0] - v[1] * v[2] * g[1] + (sum2 - v[2] * v[2]) * g[2]) * invsum32;
 }
 
-// SH backward (backward_kernels.py:297-536).  Writes the (K,3) gradient row
-// and returns the mean gradient through the view direction.
-__device__ void sh_backward(const gsb_preprocess_bwd_args& a, int idx, const float mean[3],
-                            const float cam[3], const float grad_rgb[3], unsigned clamp_bits,
-                            float gmean[3]) {
-  const int K = a.sh_coeffs;
-  const int degree = a.sh_degree;
-  float g[3];
-#pragma unroll
-  for (int c = 0; c < 3; ++c) g[c] = grad_rgb[c] * (1.0f - (float)((clamp_bits >> c) & 1u));
-  gmean[0] = gmean[1] = gmean[2] = 0.0f;
-  float* out = a.grad_sh + (size_t)idx * K * 3;
-  const bool acc = a.accumulate != 0;
-  if (g[0] == 0.0f && g[1] == 0.0f && g[2] == 0.0f) {
-    // Zero colour gradient: every SH gradient and the direction term vanish.
-    if (!acc)
-      for (int k = 0; k < K * 3; ++k) out[k] = 0.0f;
-    return;
-  }
-  const float* sp = a.sh + (size_t)idx * K * 3;
-  // The row's coefficients (up to 16 x 3); 16-byte loads when the row is a
-  // whole, aligned 48-float record.
-  float shv[48];
-  if (K == 16 && (reinterpret_cast<uintptr_t>(sp) & 15) == 0) {
-    const float4* s4p = reinterpret_cast<const float4*>(sp);
-#pragma unroll
-    for (int q = 0; q < 12; ++q) {
-      const float4 v = __ldg(s4p + q);
-      shv[q * 4 + 0] = v.x;
-      shv[q * 4 + 1] = v.y;
-      shv[q * 4 + 2] = v.z;
-      shv[q * 4 + 3] = v.w;
-    }
-  } else {
-    const int n = (K < 16 ? K : 16) * 3;
-#pragma unroll
-    for (int k = 0; k < 48; ++k) shv[k] = k < n ? __ldg(sp + k) : 0.0f;
-  }
+// SH backward (backward_kernels.py:297-536), direction-dependent part:
+// basis weights w[k] (0 above the degree), the number of coefficients the
+// degree uses, and the gradient through the view direction from the row's
+// coefficients shv[0..47] (zero-padded past K).
+__device__ __forceinline__ void sh_core(int K, int degree, const float shv[48], const float mean[3],
+                                        const float cam[3], const float g[3], float w[16], int& used,
+                                        float gmean[3]) {
   const float dir[3] = {mean[0] - cam[0], mean[1] - cam[1], mean[2] - cam[2]};
   const float len_sq = dir[0] * dir[0] + dir[1] * dir[1] + dir[2] * dir[2];
   const float inv_len = 1.0f / sqrtf(fmx(len_sq, 1.0e-20f));
   const float x = dir[0] * inv_len, y = dir[1] * inv_len, z = dir[2] * inv_len;
   float dx[3] = {0, 0, 0}, dy[3] = {0, 0, 0}, dz[3] = {0, 0, 0};
-  float w[16];
 #pragma unroll
   for (int k = 0; k < 16; ++k) w[k] = 0.0f;
-  int used = 0;
+  used = 0;
   if (K > 0) {
     w[0] = SH_C0;
     used = 1;
@@ -154,31 +122,56 @@ __device__ void sh_backward(const gsb_preprocess_bwd_args& a, int idx, const flo
       }
     }
   }
-  // Gradient rows: w[k] * g for the coefficients the degree uses, 0 above.
-  if (K == 16 && !acc && (reinterpret_cast<uintptr_t>(out) & 15) == 0) {
-    float4* o4 = reinterpret_cast<float4*>(out);
-#pragma unroll
-    for (int q = 0; q < 12; ++q) {
-      const int e = q * 4;
-      o4[q] = make_float4(w[(e + 0) / 3] * g[(e + 0) % 3], w[(e + 1) / 3] * g[(e + 1) % 3],
-                          w[(e + 2) / 3] * g[(e + 2) % 3], w[(e + 3) / 3] * g[(e + 3) % 3]);
-    }
-  } else {
-    for (int k = 0; k < K; ++k) {
-      float wk = 0.0f;  // w[k] without dynamic register indexing
-#pragma unroll
-      for (int j = 0; j < 16; ++j)
-        if (j == k) wk = w[j];
-      for (int c = 0; c < 3; ++c) {
-        const float gv = k < used ? wk * g[c] : 0.0f;
-        store_or_add(out + k * 3 + c, gv, acc);
-      }
-    }
-  }
   const float ddir[3] = {dx[0] * g[0] + dx[1] * g[1] + dx[2] * g[2],
                          dy[0] * g[0] + dy[1] * g[1] + dy[2] * g[2],
                          dz[0] * g[0] + dz[1] * g[1] + dz[2] * g[2]};
   dnormvdv(dir, ddir, gmean);
+}
+
+
+// Colour gradient through the clamp flags; zero when the channel was clamped.
+__device__ __forceinline__ bool sh_color_grad(const float grad_rgb[3], unsigned clamp_bits, float g[3]) {
+#pragma unroll
+  for (int c = 0; c < 3; ++c) g[c] = grad_rgb[c] * (1.0f - (float)((clamp_bits >> c) & 1u));
+  return !(g[0] == 0.0f && g[1] == 0.0f && g[2] == 0.0f);
+}
+
+// Per-thread SH backward for any K: reads the row from global memory,
+// writes (or adds) the (K,3) gradient row, returns the mean gradient.
+__device__ void sh_backward(const gsb_preprocess_bwd_args& a, int idx, const float mean[3],
+                            const float cam[3], const float grad_rgb[3], unsigned clamp_bits,
+                            float gmean[3]) {
+  const int K = a.sh_coeffs;
+  float g[3];
+  gmean[0] = gmean[1] = gmean[2] = 0.0f;
+  float* out = a.grad_sh + (size_t)idx * K * 3;
+  const bool acc = a.accumulate != 0;
+  if (!sh_color_grad(grad_rgb, clamp_bits, g)) {
+    // Zero colour gradient: every SH gradient and the direction term vanish.
+    if (!acc)
+      for (int k = 0; k < K * 3; ++k) out[k] = 0.0f;
+    return;
+  }
+  const float* sp = a.sh + (size_t)idx * K * 3;
+  float shv[48];
+  {
+    const int n = (K < 16 ? K : 16) * 3;
+#pragma unroll
+    for (int k = 0; k < 48; ++k) shv[k] = k < n ? __ldg(sp + k) : 0.0f;
+  }
+  float w[16];
+  int used = 0;
+  sh_core(K, a.sh_degree, shv, mean, cam, g, w, used, gmean);
+  for (int k = 0; k < K; ++k) {
+    float wk = 0.0f;  // w[k] without dynamic register indexing
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (j == k) wk = w[j];
+    for (int c = 0; c < 3; ++c) {
+      const float gv = k < used ? wk * g[c] : 0.0f;
+      store_or_add(out + k * 3 + c, gv, acc);
+    }
+  }
 }
 
 template <bool PRECOMP>

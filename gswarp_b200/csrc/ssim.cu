@@ -33,12 +33,16 @@ __constant__ float GW[11] = {0.001028380123898387f, 0.0075987582094967365f,
                              0.036000773310661316f,  0.0075987582094967365f,
                              0.001028380123898387f};
 
+// WITH_L1 also sums |img1 - img2| over the tile's pixels into
+// partials[gridDim.x + blockIdx.x] (the photometric training loss).
+template <bool WITH_L1>
 __global__ void __launch_bounds__(THREADS) ssim_fwd_kernel(const gsb_ssim_fwd_args a, int tiles_x,
                                                            int tiles_y) {
   __shared__ float s_x[RY][RX + 1];
   __shared__ float s_y[RY][RX + 1];
   __shared__ float s_h[4][RY][TX + 1];
   __shared__ float s_red[THREADS / 32];
+  __shared__ float s_red_l1[THREADS / 32];
   const int H = a.H, W = a.W;
   const int tile = blockIdx.x;
   const int tx = tile % tiles_x;
@@ -86,7 +90,7 @@ __global__ void __launch_bounds__(THREADS) ssim_fwd_kernel(const gsb_ssim_fwd_ar
     s_h[3][r][c] = a3;
   }
   __syncthreads();
-  float local_sum = 0.0f;
+  float local_sum = 0.0f, local_l1 = 0.0f;
   const size_t npix = (size_t)a.B * a.C * H * W;
   for (int i = threadIdx.x; i < TX * TY; i += THREADS) {
     const int r = i / TX, c = i % TX;
@@ -119,6 +123,7 @@ __global__ void __launch_bounds__(THREADS) ssim_fwd_kernel(const gsb_ssim_fwd_ar
     const float rA = 1.0f / Av, rB = 1.0f / Bv, rAB = rA * rB;
     const float m = Cv * Dv * rAB;
     local_sum += m;
+    if (WITH_L1) local_l1 += fabsf(s_x[r + HALO][c + HALO] - s_y[r + HALO][c + HALO]);
     if (a.dm) {
       const size_t o = pbase + (size_t)gy * W + gxp;
       a.dm[o] = 2.0f * (mu2 * (Dv - Cv) * rAB + mu1 * m * (rB - rA));
@@ -129,12 +134,23 @@ __global__ void __launch_bounds__(THREADS) ssim_fwd_kernel(const gsb_ssim_fwd_ar
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) local_sum += __shfl_xor_sync(0xffffffffu, local_sum, o);
   if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = local_sum;
+  if (WITH_L1) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) local_l1 += __shfl_xor_sync(0xffffffffu, local_l1, o);
+    if ((threadIdx.x & 31) == 0) s_red_l1[threadIdx.x >> 5] = local_l1;
+  }
   __syncthreads();
   if (threadIdx.x == 0) {
     float t = 0.0f;
 #pragma unroll
     for (int w = 0; w < THREADS / 32; ++w) t += s_red[w];
     a.partials[blockIdx.x] = t;
+    if (WITH_L1) {
+      float u = 0.0f;
+#pragma unroll
+      for (int w = 0; w < THREADS / 32; ++w) u += s_red_l1[w];
+      a.partials[gridDim.x + blockIdx.x] = u;
+    }
   }
 }
 
@@ -154,8 +170,12 @@ __global__ void __launch_bounds__(1024) ssim_mean_kernel(const float* __restrict
   }
 }
 
+// upstream_host != 0 replaces the device upstream scalar (the photometric
+// loss passes -w_ssim); WITH_L1 adds l1_scale * sign(img1 - img2).
+template <bool WITH_L1>
 __global__ void __launch_bounds__(THREADS) ssim_bwd_kernel(const gsb_ssim_bwd_args a, int tiles_x,
-                                                           int tiles_y, float inv_n) {
+                                                           int tiles_y, float inv_n, float upstream_host,
+                                                           float l1_scale) {
   __shared__ float s_dm[3][RY][RX + 1];
   __shared__ float s_t[3][RY][TX + 1];
   const int H = a.H, W = a.W;
@@ -166,7 +186,7 @@ __global__ void __launch_bounds__(THREADS) ssim_bwd_kernel(const gsb_ssim_bwd_ar
   const int x0 = tx * TX, y0 = ty * TY;
   const size_t pbase = (size_t)plane * H * W;
   const size_t npix = (size_t)a.B * a.C * H * W;
-  const float scale = inv_n * a.upstream[0];
+  const float scale = inv_n * (WITH_L1 ? upstream_host : a.upstream[0]);
   const int lo_y = a.valid ? 5 : 0, hi_y = a.valid ? H - 5 : H;
   const int lo_x = a.valid ? 5 : 0, hi_x = a.valid ? W - 5 : W;
   for (int i = threadIdx.x; i < RY * RX; i += THREADS) {
@@ -226,7 +246,46 @@ __global__ void __launch_bounds__(THREADS) ssim_bwd_kernel(const gsb_ssim_bwd_ar
     a1 += GW[5] * s_t[1][r + 5][c];
     a2 += GW[5] * s_t[2][r + 5][c];
     const size_t o = pbase + (size_t)gy * W + gxp;
-    a.grad_img1[o] = a0 + 2.0f * __ldg(a.img1 + o) * a1 + __ldg(a.img2 + o) * a2;
+    const float x1 = __ldg(a.img1 + o), x2 = __ldg(a.img2 + o);
+    float gv = a0 + 2.0f * x1 * a1 + x2 * a2;
+    if (WITH_L1) {
+      const float d = x1 - x2;
+      gv = gv + (d > 0.0f ? l1_scale : (d < 0.0f ? -l1_scale : 0.0f));
+    }
+    a.grad_img1[o] = gv;
+  }
+}
+
+// Photometric loss mean: partials[0,n) hold SSIM sums, [n,2n) |d| sums.
+__global__ void __launch_bounds__(1024) photo_mean_kernel(const float* __restrict__ partials, int n,
+                                                          double inv_count, float w_l1, float w_ssim,
+                                                          float* __restrict__ out) {
+  __shared__ double s[2][32];
+  double acc_s = 0.0, acc_l = 0.0;
+  for (int i = threadIdx.x; i < n; i += 1024) {
+    acc_s += (double)partials[i];
+    acc_l += (double)partials[n + i];
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    acc_s += __shfl_xor_sync(0xffffffffu, acc_s, o);
+    acc_l += __shfl_xor_sync(0xffffffffu, acc_l, o);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    s[0][threadIdx.x >> 5] = acc_s;
+    s[1][threadIdx.x >> 5] = acc_l;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double ts = 0.0, tl = 0.0;
+    for (int w = 0; w < 32; ++w) {
+      ts += s[0][w];
+      tl += s[1][w];
+    }
+    const double ssim = ts * inv_count, l1 = tl * inv_count;
+    out[0] = (float)((double)w_l1 * l1 + (double)w_ssim * (1.0 - ssim));
+    out[1] = (float)l1;
+    out[2] = (float)ssim;
   }
 }
 
@@ -260,7 +319,7 @@ GSB_EXPORT int gsb_ssim_fwd(const gsb_ssim_fwd_args* a, void* stream) {
   tiles_of(a->H, a->W, tx, ty);
   const int blocks = a->B * a->C * tx * ty;
   cudaStream_t s = (cudaStream_t)stream;
-  ssim_fwd_kernel<<<blocks, THREADS, 0, s>>>(*a, tx, ty);
+  ssim_fwd_kernel<false><<<blocks, THREADS, 0, s>>>(*a, tx, ty);
   const double count = a->valid ? (double)a->B * a->C * (a->H - 10) * (a->W - 10)
                                  : (double)a->B * a->C * a->H * a->W;
   ssim_mean_kernel<<<1, 1024, 0, s>>>(a->partials, blocks, 1.0 / count, a->loss);
@@ -278,8 +337,77 @@ GSB_EXPORT int gsb_ssim_bwd(const gsb_ssim_bwd_args* a, void* stream) {
   const double count = a->valid ? (double)a->B * a->C * (a->H - 10) * (a->W - 10)
                                  : (double)a->B * a->C * a->H * a->W;
   const float inv_n = (float)(1.0 / count);
-  ssim_bwd_kernel<<<a->B * a->C * tx * ty, THREADS, 0, (cudaStream_t)stream>>>(*a, tx, ty, inv_n);
+  ssim_bwd_kernel<false><<<a->B * a->C * tx * ty, THREADS, 0, (cudaStream_t)stream>>>(*a, tx, ty, inv_n,
+                                                                                      0.0f, 0.0f);
   return check_launch("ssim_bwd_kernel");
+}
+
+// ---------------------------------------------------------------------------
+// Photometric training loss  L = w_l1 * mean|img - target|
+//                               + w_ssim * (1 - SSIM(img, target))
+// ('same' padding), the loss the reference's SSIM documentation pairs its
+// fused SSIM with (docs/ssim.md:22, :91).  The L1 term rides on the SSIM
+// kernels' tile loads: forward adds one |d| partial per tile, backward adds
+// l1_scale * sign(d) to the SSIM gradient, so the whole loss costs the same
+// two image passes as SSIM alone.
+// ---------------------------------------------------------------------------
+GSB_EXPORT int gsb_photo_loss_fwd(const gsb_photo_loss_fwd_args* a, void* stream) {
+  if (!a || a->B <= 0 || a->C <= 0 || a->H <= 0 || a->W <= 0 || !a->img || !a->target || !a->dm ||
+      !a->partials || !a->loss_out) {
+    set_error("gsb_photo_loss_fwd: invalid arguments");
+    return GSB_ERR_INVALID;
+  }
+  int tx, ty;
+  tiles_of(a->H, a->W, tx, ty);
+  const int blocks = a->B * a->C * tx * ty;
+  gsb_ssim_fwd_args f{};
+  f.B = a->B;
+  f.C = a->C;
+  f.H = a->H;
+  f.W = a->W;
+  f.valid = 0;
+  f.C1 = a->C1;
+  f.C2 = a->C2;
+  f.img1 = a->img;
+  f.img2 = a->target;
+  f.dm = a->dm;
+  f.partials = a->partials;
+  f.loss = a->loss_out;
+  cudaStream_t s = (cudaStream_t)stream;
+  ssim_fwd_kernel<true><<<blocks, THREADS, 0, s>>>(f, tx, ty);
+  const double count = (double)a->B * a->C * a->H * a->W;
+  photo_mean_kernel<<<1, 1024, 0, s>>>(a->partials, blocks, 1.0 / count, a->w_l1, a->w_ssim, a->loss_out);
+  return check_launch("gsb_photo_loss_fwd");
+}
+
+GSB_EXPORT int gsb_photo_loss_bwd(const gsb_photo_loss_bwd_args* a, void* stream) {
+  if (!a || a->B <= 0 || a->C <= 0 || a->H <= 0 || a->W <= 0 || !a->img || !a->target || !a->dm ||
+      !a->grad_img) {
+    set_error("gsb_photo_loss_bwd: invalid arguments");
+    return GSB_ERR_INVALID;
+  }
+  int tx, ty;
+  tiles_of(a->H, a->W, tx, ty);
+  const double count = (double)a->B * a->C * a->H * a->W;
+  const float inv_n = (float)(1.0 / count);
+  gsb_ssim_bwd_args b{};
+  b.B = a->B;
+  b.C = a->C;
+  b.H = a->H;
+  b.W = a->W;
+  b.valid = 0;
+  b.img1 = a->img;
+  b.img2 = a->target;
+  b.dm = a->dm;
+  b.upstream = nullptr;
+  b.grad_img1 = a->grad_img;
+  // Same float products as autograd forms for the two terms:
+  // SSIM: inv_n * (-w_ssim * upstream); L1: (w_l1 * upstream) * inv_n.
+  const float ssim_up = -(a->w_ssim * a->upstream);
+  const float l1_scale = (a->w_l1 * a->upstream) * inv_n;
+  ssim_bwd_kernel<true><<<a->B * a->C * tx * ty, THREADS, 0, (cudaStream_t)stream>>>(b, tx, ty, inv_n,
+                                                                                     ssim_up, l1_scale);
+  return check_launch("gsb_photo_loss_bwd");
 }
 
 // ---------------------------------------------------------------------------
@@ -380,7 +508,7 @@ GSB_EXPORT int gsb_ssim_fwd_noalloc(int B, int C, int H, int W, int valid, float
   a.partials = partials;
   a.loss = loss;
   cudaStream_t s = (cudaStream_t)stream;
-  ssim_fwd_kernel<<<(int)blocks, THREADS, 0, s>>>(a, tx, ty);
+  ssim_fwd_kernel<false><<<(int)blocks, THREADS, 0, s>>>(a, tx, ty);
   const double count = valid ? (double)B * C * (H - 10) * (W - 10) : (double)B * C * H * W;
   ssim_mean_kernel<<<1, 1024, 0, s>>>(partials, (int)blocks, 1.0 / count, loss);
   return check_launch("gsb_ssim_fwd_noalloc");

@@ -1,0 +1,173 @@
+"""Fused multi-view training step: the 3DGS hot path with no autograd glue.
+
+The drop-in path (``GaussianRasterizer`` + ``fused_ssim`` under autograd)
+runs every kernel of the hot path, but autograd adds work between them:
+each view's per-Gaussian gradients come back as fresh tensors that
+``AccumulateGrad`` then adds into the parameters' ``.grad`` (a full extra
+read-read-write of 59 floats per Gaussian per view), unused outputs get
+zero-filled gradients, and the L1 term is a chain of elementwise kernels.
+
+``FusedViewStep`` runs the same stages through the C ABI directly, per view:
+
+    preprocess -> binning -> render -> photometric loss fwd+bwd
+               -> render backward -> preprocess backward
+
+with the loss ``w_l1 * L1 + w_ssim * (1 - SSIM)`` (the loss the reference's
+SSIM documentation pairs its fused SSIM with, gswarp docs/ssim.md:22, :91)
+computed by one forward and one backward kernel pass, and with preprocess
+backward ADDING each view's gradients straight into the flat gradient buffer
+(``accumulate`` mode of ``gsb_preprocess_bwd``), whose SoA blocks are the
+parameters' ``.grad``.  After the rank's views it takes part in one sum
+all-reduce of that buffer, as ``view_sharding.ViewShardedStep`` does.
+
+Gradients equal the autograd path's up to the float summation order of the
+render backward's atomics (tests compare the two).
+"""
+
+from __future__ import annotations
+
+from typing import Sequence
+
+import torch
+
+from . import _lib, _pipeline as pl
+from ._autograd import _camera
+from ._runtime import resolve_execution_options
+from .view_sharding import GradientBuffer
+
+NUM_CHANNELS = 3
+SSIM_C1 = 0.01 ** 2
+SSIM_C2 = 0.03 ** 2
+
+
+def photometric_loss_forward(img: torch.Tensor, target: torch.Tensor, l1_weight: float = 1.0,
+                             ssim_weight: float = 0.2, out: torch.Tensor | None = None):
+    """``(loss3, dm)``: loss3 = [w_l1*L1 + w_ssim*(1-SSIM), L1, SSIM] on the
+    device, dm = the per-pixel maps backward needs.  Images are (C,H,W) or
+    (B,C,H,W) fp32 on one CUDA device; 'same' padding."""
+    x = pl._f32(img)
+    y = pl._f32(target)
+    if x.shape != y.shape or x.ndim not in (3, 4):
+        raise ValueError("img and target must share a (C,H,W) or (B,C,H,W) shape")
+    B, C, H, W = (1, *x.shape) if x.ndim == 3 else x.shape
+    dev = x.device
+    L = _lib.load()
+    dm = torch.empty((3, B, C, H, W), dtype=torch.float32, device=dev)
+    parts = torch.empty(2 * int(L.gsb_ssim_partials_count(B, C, H, W)), dtype=torch.float32, device=dev)
+    loss3 = out if out is not None else torch.empty(3, dtype=torch.float32, device=dev)
+    a = _lib.PhotoLossFwdArgs()
+    a.B, a.C, a.H, a.W = B, C, H, W
+    a.C1, a.C2 = SSIM_C1, SSIM_C2
+    a.w_l1, a.w_ssim = float(l1_weight), float(ssim_weight)
+    a.img, a.target, a.dm, a.partials, a.loss_out = (_lib.ptr(x), _lib.ptr(y), _lib.ptr(dm), _lib.ptr(parts),
+                                                    _lib.ptr(loss3))
+    with torch.cuda.device(dev), pl._stage_timer("loss_fwd", {"kernels": 2}):
+        _lib.call("gsb_photo_loss_fwd", a, _lib.stream_handle(dev))
+    return loss3, dm
+
+
+def photometric_loss_backward(img: torch.Tensor, target: torch.Tensor, dm: torch.Tensor, l1_weight: float = 1.0,
+                              ssim_weight: float = 0.2, upstream: float = 1.0) -> torch.Tensor:
+    """upstream * d(w_l1*L1 + w_ssim*(1-SSIM))/d img, same shape as img."""
+    x = pl._f32(img)
+    y = pl._f32(target)
+    B, C, H, W = (1, *x.shape) if x.ndim == 3 else x.shape
+    if dm.shape != (3, B, C, H, W):
+        raise ValueError("dm does not belong to these images")
+    g = torch.empty_like(x)
+    a = _lib.PhotoLossBwdArgs()
+    a.B, a.C, a.H, a.W = B, C, H, W
+    a.w_l1, a.w_ssim, a.upstream = float(l1_weight), float(ssim_weight), float(upstream)
+    a.img, a.target, a.dm, a.grad_img = _lib.ptr(x), _lib.ptr(y), _lib.ptr(dm), _lib.ptr(g)
+    with torch.cuda.device(x.device), pl._stage_timer("loss_bwd", {"kernels": 1}):
+        _lib.call("gsb_photo_loss_bwd", a, _lib.stream_handle(x.device))
+    return g
+
+
+class FusedViewStep:
+    """One data-parallel training step over this rank's views, fused.
+
+    ``params`` are (means (P,3), scales (P,3), rotations (P,4), opacities
+    (P,1), sh (P,K,3)), the rasterizer's inputs; ``settings`` the
+    ``GaussianRasterizationSettings`` of every view this rank renders.
+    ``step(targets)`` takes one (3,H,W) target per view -- on the device, or
+    in (pinned) host memory, in which case it is copied to the device inside
+    the step -- and returns the per-view [loss, L1, SSIM] rows as a (V,3)
+    device tensor.  Gradients are in ``self.grads`` (one flat buffer; its
+    blocks are the parameters' ``.grad``) and are all-reduced across the
+    process group when one is initialised.
+    """
+
+    def __init__(self, params: Sequence[torch.Tensor], settings: Sequence, l1_weight: float = 1.0,
+                 ssim_weight: float = 0.2, group=None):
+        if len(params) != 5:
+            raise ValueError("params must be (means, scales, rotations, opacities, sh)")
+        means, scales, rots, opac, sh = params
+        P = means.shape[0]
+        for t, shape in ((means, (P, 3)), (scales, (P, 3)), (rots, (P, 4)), (opac, (P, 1))):
+            if tuple(t.shape) != shape or t.dtype != torch.float32 or not t.is_contiguous():
+                raise ValueError(f"parameter of shape {tuple(t.shape)} must be contiguous fp32 {shape}")
+        if sh.ndim != 3 or sh.shape[0] != P or sh.shape[2] != NUM_CHANNELS or sh.dtype != torch.float32 \
+                or not sh.is_contiguous():
+            raise ValueError("sh must be contiguous fp32 (P, K, 3)")
+        if not settings:
+            raise ValueError("no views")
+        self.params = list(params)
+        self.settings = list(settings)
+        self.cams = [_camera(rs) for rs in self.settings]
+        self.modes = [pl.coverage_mode_id(resolve_execution_options(rs)) for rs in self.settings]
+        self.bgs = [pl._f32(rs.bg).reshape(NUM_CHANNELS) for rs in self.settings]
+        self.l1_weight = float(l1_weight)
+        self.ssim_weight = float(ssim_weight)
+        self.group = group
+        self.grads = GradientBuffer(self.params)
+        dev = means.device
+        self.device = dev
+        self.losses = torch.zeros((len(self.settings), 3), dtype=torch.float32, device=dev)
+        self._staging: dict[int, torch.Tensor] = {}
+
+    def _gaussians(self, rs) -> pl.Gaussians:
+        means, scales, rots, opac, sh = self.params
+        return pl.make_gaussians(means, opac, scales, rots, None, sh, None, rs.scale_modifier, rs.sh_degree)
+
+    def _target(self, i: int, t: torch.Tensor) -> torch.Tensor:
+        if t.device == self.device:
+            return pl._f32(t)
+        buf = self._staging.get(i)
+        if buf is None or buf.shape != t.shape:
+            buf = torch.empty(t.shape, dtype=torch.float32, device=self.device)
+            self._staging[i] = buf
+        buf.copy_(t, non_blocking=True)
+        return buf
+
+    def view(self, i: int, target: torch.Tensor) -> None:
+        """Forward + loss + backward of view ``i``; gradients are added into
+        the flat buffer and the view's loss row into ``self.losses[i]``."""
+        rs, cam, mode, bg = self.settings[i], self.cams[i], self.modes[i], self.bgs[i]
+        g = self._gaussians(rs)
+        P = g.P
+        if target.shape != (NUM_CHANNELS, cam.H, cam.W):
+            raise ValueError(f"target {i} must have shape (3, {cam.H}, {cam.W})")
+        tgt = self._target(i, target)
+        pre = pl.preprocess(g, cam, mode)
+        binned = pl.binning(pre, cam, mode)
+        ren = pl.render(pre, binned, cam, bg, False)
+        _, dm = photometric_loss_forward(ren.color, tgt, self.l1_weight, self.ssim_weight, out=self.losses[i])
+        grad_img = photometric_loss_backward(ren.color, tgt, dm, self.l1_weight, self.ssim_weight)
+        grad_acc = pl.render_backward(pre.records, binned, cam, bg, ren.alpha, ren.n_contrib, grad_img, None, None,
+                                      False, P)
+        v_means, v_scales, v_rots, v_opac, v_sh = self.grads.views
+        out = pl.PreprocessGrads(grad_means3D=v_means, grad_means2D=None, grad_opacity=v_opac,
+                                 grad_scales=v_scales, grad_rotations=v_rots, grad_cov3D=None, grad_sh=v_sh,
+                                 grad_colors=None)
+        pl.preprocess_backward(g, cam, pre.radii, pre.records, grad_acc, None, None, None, out=out)
+
+    def step(self, targets: Sequence[torch.Tensor]) -> torch.Tensor:
+        if len(targets) != len(self.settings):
+            raise ValueError(f"expected {len(self.settings)} targets, got {len(targets)}")
+        with torch.cuda.device(self.device):
+            self.grads.zero_()
+            for i, t in enumerate(targets):
+                self.view(i, t)
+            self.grads.all_reduce(self.group)
+        return self.losses

@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define GSB_ABI_VERSION 2
+#define GSB_ABI_VERSION 3
 
 #define GSB_OK 0
 #define GSB_ERR_INVALID (-1)  /* bad argument: ValueError in Python          */
@@ -253,6 +253,37 @@ typedef struct {
 } gsb_ssim_bwd_args;
 
 int gsb_ssim_bwd(const gsb_ssim_bwd_args* a, void* stream);
+
+/* Photometric training loss (B200 addition; the reference composes it in
+ * Python from an L1 term and its fused SSIM, docs/ssim.md:22,91):
+ *   L = w_l1 * mean|img - target| + w_ssim * (1 - SSIM(img, target)),
+ * 'same' padding, 11x11 Gaussian window.  Forward writes loss_out[0] = L,
+ * loss_out[1] = mean L1, loss_out[2] = mean SSIM, and the dm maps backward
+ * needs; backward writes upstream * dL/dimg. */
+typedef struct {
+  int B, C, H, W;
+  float C1, C2;
+  float w_l1, w_ssim;
+  const float* img;       /* (B,C,H,W) rendered */
+  const float* target;    /* (B,C,H,W) */
+  float* dm;              /* (3,B,C,H,W) workspace kept for backward */
+  float* partials;        /* 2 * gsb_ssim_partials_count() floats, workspace */
+  float* loss_out;        /* 3 floats out (device) */
+} gsb_photo_loss_fwd_args;
+
+int gsb_photo_loss_fwd(const gsb_photo_loss_fwd_args* a, void* stream);
+
+typedef struct {
+  int B, C, H, W;
+  float w_l1, w_ssim;
+  float upstream;         /* dTotal/dL, host scalar (1 for a plain training step) */
+  const float* img;
+  const float* target;
+  const float* dm;        /* from gsb_photo_loss_fwd */
+  float* grad_img;        /* (B,C,H,W) */
+} gsb_photo_loss_bwd_args;
+
+int gsb_photo_loss_bwd(const gsb_photo_loss_bwd_args* a, void* stream);
 
 /* Allocation-free SSIM forward.  No counterpart in the reference: it exists
  * for callers that cannot provide device memory (a process whose device

@@ -1,0 +1,143 @@
+"""Fused training step against the drop-in autograd path.
+
+The photometric loss kernels (L1 + SSIM in one forward and one backward
+pass) are checked against the same loss built from ``abs().mean()`` and the
+library's own ``fused_ssim`` under autograd; ``FusedViewStep`` (no autograd,
+preprocess backward accumulating into the flat gradient buffer) is checked
+against ``ViewShardedStep`` driving ``GaussianRasterizer`` + ``fused_ssim``
+through autograd, on the same scene and views."""
+
+import pytest
+import torch
+
+import gswarp_b200 as gs
+from gswarp_b200 import workloads as wl
+from gswarp_b200.training import FusedViewStep, photometric_loss_backward, photometric_loss_forward
+from gswarp_b200.view_sharding import ViewShardedStep
+
+pytestmark = pytest.mark.gpu
+
+
+def _images(seed, shape, dev):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.rand(shape, generator=g)
+    y = (x + 0.05 * torch.randn(shape, generator=g)).clamp(0, 1)
+    y[..., :3, :5] = x[..., :3, :5]  # exact ties: sign(0) = 0 in the L1 gradient
+    return x.to(dev), y.to(dev)
+
+
+@pytest.mark.parametrize("shape", [(3, 37, 53), (3, 128, 96), (2, 3, 40, 70)])
+@pytest.mark.parametrize("weights", [(1.0, 0.2), (0.8, 0.2), (0.0, 1.0), (1.0, 0.0)])
+def test_photometric_loss_matches_autograd_composition(cuda, shape, weights):
+    w1, w2 = weights
+    x, y = _images(7, shape, cuda)
+    loss3, dm = photometric_loss_forward(x, y, w1, w2)
+    grad = photometric_loss_backward(x, y, dm, w1, w2)
+
+    xr = x.clone().requires_grad_(True)
+    batched = xr if xr.ndim == 4 else xr.unsqueeze(0)
+    yb = y if y.ndim == 4 else y.unsqueeze(0)
+    l1 = (xr - y).abs().mean()
+    ssim = gs.fused_ssim(batched, yb)
+    ref = w1 * l1 + w2 * (1.0 - ssim)
+    ref.backward()
+    got = loss3.cpu()
+    torch.testing.assert_close(got[1], l1.detach().cpu(), rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(got[2], ssim.detach().cpu(), rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(got[0], ref.detach().cpu(), rtol=1e-5, atol=1e-6)
+    # Same float products, same terms: equal up to the order of one addition.
+    torch.testing.assert_close(grad, xr.grad, rtol=1e-6, atol=1e-12)
+
+
+def test_photometric_loss_upstream_scales_gradient(cuda):
+    x, y = _images(3, (3, 64, 64), cuda)
+    _, dm = photometric_loss_forward(x, y)
+    g1 = photometric_loss_backward(x, y, dm, upstream=1.0)
+    g3 = photometric_loss_backward(x, y, dm, upstream=0.5)
+    torch.testing.assert_close(g3, 0.5 * g1, rtol=1e-6, atol=1e-12)
+
+
+def test_photometric_loss_rejects_bad_shapes(cuda):
+    x, y = _images(3, (3, 16, 16), cuda)
+    with pytest.raises(ValueError):
+        photometric_loss_forward(x, y[:, :8])
+    _, dm = photometric_loss_forward(x, y)
+    with pytest.raises(ValueError):
+        photometric_loss_backward(x[:, :8], y[:, :8], dm)
+
+
+def _scene(dev, n, views, W, H):
+    sc = wl.config2_scene(seed=5, n=n)
+    cams = wl.ring_views(views, seed=5, width=W, height=H)
+    params = [t.to(dev).contiguous() for t in (sc.means, sc.scales, sc.rotations, sc.opacities, sc.sh)]
+    bg = torch.zeros(3, device=dev)
+    settings = [gs.GaussianRasterizationSettings(
+        image_height=v.height, image_width=v.width, tanfovx=v.tanfovx, tanfovy=v.tanfovy, bg=bg,
+        scale_modifier=1.0, viewmatrix=v.viewmatrix.to(dev), projmatrix=v.projmatrix.to(dev), sh_degree=3,
+        campos=v.campos.to(dev), prefiltered=False) for v in cams]
+    targets = [wl.target_image(100 + i, H, W).to(dev) for i in range(views)]
+    return params, settings, targets
+
+
+def _autograd_step(params, settings, targets, w1, w2):
+    ps = [p.detach().clone().requires_grad_(True) for p in params]
+    means2d = torch.zeros_like(ps[0], requires_grad=True)
+
+    def view_loss(i):
+        color, _, _ = gs.GaussianRasterizer(settings[i])(ps[0], means2d, ps[3], shs=ps[4], scales=ps[1],
+                                                         rotations=ps[2])
+        l1 = (color - targets[i]).abs().mean()
+        return w1 * l1 + w2 * (1.0 - gs.fused_ssim(color.unsqueeze(0), targets[i].unsqueeze(0)))
+
+    step = ViewShardedStep(ps, range(len(settings)), view_loss)
+    res = step.step()
+    return step.grads.flat, torch.stack(res.losses)
+
+
+@pytest.mark.parametrize("n,views,W,H", [(20_000, 3, 320, 192), (200_000, 2, 960, 544)])
+def test_fused_step_matches_autograd_step(cuda, n, views, W, H):
+    params, settings, targets = _scene(cuda, n, views, W, H)
+    ref_flat, ref_losses = _autograd_step(params, settings, targets, 1.0, 0.2)
+    fused = FusedViewStep([p.clone() for p in params], settings, 1.0, 0.2)
+    losses = fused.step(targets)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(losses[:, 0], ref_losses, rtol=1e-5, atol=1e-6)
+    got = fused.grads.flat
+    assert torch.isfinite(got).all()
+    assert float(got.abs().sum()) > 0
+    # render backward sums with float atomics in arbitrary order: compare blocks by norm
+    off = 0
+    for p in params:
+        k = p.numel()
+        a, b = got[off:off + k], ref_flat[off:off + k]
+        assert float((a - b).norm()) <= 1e-4 * float(b.norm()) + 1e-7
+        off += k
+    # a second step re-zeroes and re-accumulates (no doubling)
+    fused.step(targets)
+    assert float((fused.grads.flat - got).norm()) <= 1e-4 * float(got.norm()) + 1e-7
+
+
+def test_fused_step_host_targets_match_device_targets(cuda):
+    params, settings, targets = _scene(cuda, 20_000, 2, 256, 128)
+    host = [t.cpu().pin_memory() for t in targets]
+    a = FusedViewStep([p.clone() for p in params], settings)
+    la = a.step(targets).clone()
+    ga = a.grads.flat.clone()
+    b = FusedViewStep([p.clone() for p in params], settings)
+    lb = b.step(host)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(la, lb, rtol=1e-6, atol=1e-7)
+    assert float((b.grads.flat - ga).norm()) <= 1e-4 * float(ga.norm()) + 1e-7
+
+
+def test_fused_step_parameter_grads_alias_flat_buffer(cuda):
+    params, settings, targets = _scene(cuda, 5_000, 1, 128, 96)
+    ps = [p.clone().requires_grad_(True) for p in params]
+    step = FusedViewStep(ps, settings)
+    step.step(targets)
+    for p, v in zip(ps, step.grads.views):
+        assert p.grad.data_ptr() == v.data_ptr()
+    with pytest.raises(ValueError):
+        step.step(targets + targets)
+    with pytest.raises(ValueError):
+        FusedViewStep(ps[:4], settings)
