@@ -174,9 +174,89 @@ __device__ void sh_backward(const gsb_preprocess_bwd_args& a, int idx, const flo
   }
 }
 
-template <bool PRECOMP>
-__global__ void __launch_bounds__(256) preprocess_bwd_kernel(const gsb_preprocess_bwd_args a) {
+// Warp-cooperative SH backward for (P,16,3) rows.  One thread per Gaussian
+// reads and writes its 48-float row with stride-48 accesses, 32 rows apart
+// across a warp; here the warp moves its 32 consecutive rows (6 KB, one
+// contiguous span) between global and shared memory with coalesced 16-byte
+// accesses, and each thread works on its row in shared memory (rows padded to
+// 52 floats, so the per-thread 16-byte reads and writes are conflict-free).
+// Arithmetic is the same sh_core as the per-thread path.
+constexpr int SH_ROW_F4 = 13;  // 52 floats per staged row
+constexpr int PB_THREADS = 256;
+constexpr int PB_SH16_THREADS = 128;
+
+__device__ __forceinline__ void sh_backward_staged(const gsb_preprocess_bwd_args& a, float4* rows, int idx0,
+                                                   bool work, bool need, const float mean[3],
+                                                   const float cam[3], const float g[3], float gmean[3]) {
+  const int lane = threadIdx.x & 31;
+  const bool acc = a.accumulate != 0;
+  const unsigned need_mask = __ballot_sync(0xffffffffu, need);
+  const unsigned work_mask = __ballot_sync(0xffffffffu, work);
+  gmean[0] = gmean[1] = gmean[2] = 0.0f;
+  if (work_mask == 0u) return;
+  const float4* src = reinterpret_cast<const float4*>(a.sh) + (size_t)idx0 * 12;
+  if (need_mask) {
+#pragma unroll 4
+    for (int j = lane; j < 32 * 12; j += 32) {
+      const int r = j / 12;
+      if ((need_mask >> r) & 1u) rows[r * SH_ROW_F4 + (j - r * 12)] = __ldg(src + j);
+    }
+  }
+  __syncwarp();
+  if (need) {
+    float4* row = rows + lane * SH_ROW_F4;
+    float shv[48];
+#pragma unroll
+    for (int q = 0; q < 12; ++q) {
+      const float4 v = row[q];
+      shv[q * 4 + 0] = v.x;
+      shv[q * 4 + 1] = v.y;
+      shv[q * 4 + 2] = v.z;
+      shv[q * 4 + 3] = v.w;
+    }
+    float w[16];
+    int used = 0;
+    sh_core(16, a.sh_degree, shv, mean, cam, g, w, used, gmean);
+#pragma unroll
+    for (int q = 0; q < 12; ++q) {
+      const int e = q * 4;
+      row[q] = make_float4((e + 0) / 3 < used ? w[(e + 0) / 3] * g[(e + 0) % 3] : 0.0f,
+                           (e + 1) / 3 < used ? w[(e + 1) / 3] * g[(e + 1) % 3] : 0.0f,
+                           (e + 2) / 3 < used ? w[(e + 2) / 3] * g[(e + 2) % 3] : 0.0f,
+                           (e + 3) / 3 < used ? w[(e + 3) / 3] * g[(e + 3) % 3] : 0.0f);
+    }
+  }
+  __syncwarp();
+  float4* dst = reinterpret_cast<float4*>(a.grad_sh) + (size_t)idx0 * 12;
+#pragma unroll 4
+  for (int j = lane; j < 32 * 12; j += 32) {
+    const int r = j / 12;
+    if (!((work_mask >> r) & 1u)) continue;
+    if ((need_mask >> r) & 1u) {
+      float4 v = rows[r * SH_ROW_F4 + (j - r * 12)];
+      if (acc) {
+        const float4 o = dst[j];
+        v = make_float4(o.x + v.x, o.y + v.y, o.z + v.z, o.w + v.w);
+      }
+      dst[j] = v;
+    } else if (!acc) {
+      dst[j] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+  }
+  __syncwarp();
+}
+
+// SH16: SH rows of exactly 16 coefficients, 16-byte aligned, handled by
+// sh_backward_staged (every lane of a warp takes part, so lanes past P or
+// without work stay in the kernel and only skip their loads and stores).
+// In accumulate mode a Gaussian with radius 0 got no render gradient and no
+// user gradient (both only apply where radius > 0), so its contribution is
+// zero and it is skipped without touching memory.
+template <bool PRECOMP, bool SH16>
+__global__ void __launch_bounds__(SH16 ? PB_SH16_THREADS : PB_THREADS)
+    preprocess_bwd_kernel(const gsb_preprocess_bwd_args a) {
   __shared__ float s_view[16], s_proj[16], s_cam[3];
+  __shared__ float4 s_rows[SH16 ? PB_SH16_THREADS * SH_ROW_F4 : 1];
   if (threadIdx.x < 16) {
     s_view[threadIdx.x] = a.viewmatrix[threadIdx.x];
     s_proj[threadIdx.x] = a.projmatrix[threadIdx.x];
@@ -185,14 +265,24 @@ __global__ void __launch_bounds__(256) preprocess_bwd_kernel(const gsb_preproces
   }
   __syncthreads();
   const int tid = blockIdx.x * blockDim.x + threadIdx.x;
-  if (tid >= a.P) return;
+  const bool acc = a.accumulate != 0;
+  const bool live = tid < a.P;
+  const int rad = live ? a.radii[tid] : 0;
+  const bool work = live && (!acc || rad > 0);
+  if (!SH16 && !work) return;
   const float* pr = s_proj;
   const float* vf = s_view;
-  const bool acc = a.accumulate != 0;
-  const float mean[3] = {a.means[tid * 3], a.means[tid * 3 + 1], a.means[tid * 3 + 2]};
-  const int rad = a.radii[tid];
-  const float4* ga4 = reinterpret_cast<const float4*>(a.grad_acc) + (size_t)tid * 3;
-  const float4 gq0 = ga4[0], gq1 = ga4[1], gq2 = ga4[2];
+  float mean[3] = {0.0f, 0.0f, 0.0f};
+  float4 gq0 = make_float4(0.0f, 0.0f, 0.0f, 0.0f), gq1 = gq0, gq2 = gq0;
+  if (work) {
+    mean[0] = a.means[tid * 3];
+    mean[1] = a.means[tid * 3 + 1];
+    mean[2] = a.means[tid * 3 + 2];
+    const float4* ga4 = reinterpret_cast<const float4*>(a.grad_acc) + (size_t)tid * 3;
+    gq0 = ga4[0];
+    gq1 = ga4[1];
+    gq2 = ga4[2];
+  }
   const float rgx = gq0.x, rgy = gq0.y, rgd = gq0.z;
   const float rco[4] = {gq1.x, gq1.y, gq1.z, gq1.w};
   const float rrgb[3] = {gq2.x, gq2.y, gq2.z};
@@ -414,13 +504,24 @@ __global__ void __launch_bounds__(256) preprocess_bwd_kernel(const gsb_preproces
     }
   }
   float gsm[3] = {0.0f, 0.0f, 0.0f};
-  if (a.sh) {
+  if (SH16) {
+    float g[3] = {0.0f, 0.0f, 0.0f};
+    bool need = false;
+    if (work) {
+      const unsigned clamp_bits =
+          __float_as_uint(reinterpret_cast<const float4*>(a.records)[(size_t)tid * 3 + 1].w);
+      need = sh_color_grad(rrgb, clamp_bits, g);
+    }
+    sh_backward_staged(a, s_rows + (threadIdx.x & ~31) * SH_ROW_F4, tid & ~31, work, need, mean, s_cam, g,
+                       gsm);
+    if (!work) return;
+  } else if (a.sh) {
     const unsigned clamp_bits =
         __float_as_uint(reinterpret_cast<const float4*>(a.records)[(size_t)tid * 3 + 1].w);
     sh_backward(a, tid, mean, s_cam, rrgb, clamp_bits, gsm);
   }
   float m0 = pm_x + gcm[0], m1 = pm_y + gcm[1], m2 = pm_z + gcm[2];
-  if (a.sh) {
+  if (SH16 || a.sh) {
     m0 = m0 + gsm[0];
     m1 = m1 + gsm[1];
     m2 = m2 + gsm[2];
@@ -474,9 +575,20 @@ GSB_EXPORT int gsb_preprocess_bwd(const gsb_preprocess_bwd_args* a, void* stream
     return GSB_ERR_INVALID;
   }
   cudaStream_t s = (cudaStream_t)stream;
-  if (precomp)
-    preprocess_bwd_kernel<true><<<div_up(a->P, 256), 256, 0, s>>>(*a);
-  else
-    preprocess_bwd_kernel<false><<<div_up(a->P, 256), 256, 0, s>>>(*a);
+  const bool sh16 = a->sh && a->sh_coeffs == 16 && !(reinterpret_cast<uintptr_t>(a->sh) & 15) &&
+                    !(reinterpret_cast<uintptr_t>(a->grad_sh) & 15);
+  if (sh16) {
+    const int blocks = div_up(a->P, PB_SH16_THREADS);
+    if (precomp)
+      preprocess_bwd_kernel<true, true><<<blocks, PB_SH16_THREADS, 0, s>>>(*a);
+    else
+      preprocess_bwd_kernel<false, true><<<blocks, PB_SH16_THREADS, 0, s>>>(*a);
+  } else {
+    const int blocks = div_up(a->P, PB_THREADS);
+    if (precomp)
+      preprocess_bwd_kernel<true, false><<<blocks, PB_THREADS, 0, s>>>(*a);
+    else
+      preprocess_bwd_kernel<false, false><<<blocks, PB_THREADS, 0, s>>>(*a);
+  }
   return check_launch("preprocess_bwd_kernel");
 }

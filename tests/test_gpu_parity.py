@@ -200,6 +200,57 @@ def test_preprocess_backward_bit_exact(cuda, name):
         np.testing.assert_array_equal(got, ref[k], err_msg=k)
 
 
+@pytest.mark.parametrize("name,unaligned", [("cfg1", False), ("cfg2_200k", False), ("cfg2_200k", True)])
+def test_preprocess_backward_accumulate_adds_exactly(cuda, name, unaligned):
+    """accumulate mode adds each Gaussian's gradients into the given buffers:
+    result == prefill + (the non-accumulating result), bit for bit; Gaussians
+    with radius 0 are left untouched.  cfg2 exercises the warp-staged SH rows
+    (K = 16, 16-byte aligned) and, with an unaligned SH tensor, the
+    per-thread path, which must give the same bits."""
+    scene, view, g, cam, pre, binned, ren, bg, inp = _render_case(name, cuda)
+    W, H, P = view.width, view.height, scene.n
+    if unaligned:
+        buf = torch.empty(g.sh.numel() + 1, device=cuda)
+        buf[1:] = g.sh.reshape(-1)
+        g.sh = buf[1:].view(g.sh.shape)
+        assert g.sh.data_ptr() % 16 != 0
+    gen = torch.Generator().manual_seed(6)
+    grad_acc = pl.render_backward(pre.records, binned, cam, bg, ren.alpha, ren.n_contrib,
+                                  torch.randn(3, H, W, generator=gen).to(cuda), None, None, False, P)
+    fresh = pl.preprocess_backward(g, cam, pre.radii, pre.records, grad_acc, None, None, None)
+    K = g.sh.shape[1]
+    pre_fill = pl.PreprocessGrads(
+        grad_means3D=torch.randn(P, 3, generator=gen).to(cuda), grad_means2D=torch.randn(P, 3, generator=gen).to(cuda),
+        grad_opacity=torch.randn(P, generator=gen).to(cuda), grad_scales=torch.randn(P, 3, generator=gen).to(cuda),
+        grad_rotations=torch.randn(P, 4, generator=gen).to(cuda), grad_cov3D=None,
+        grad_sh=torch.randn(P, K, 3, generator=gen).to(cuda), grad_colors=None)
+    if unaligned:
+        sbuf = torch.empty(P * K * 3 + 1, device=cuda)
+        sbuf[1:] = pre_fill.grad_sh.reshape(-1)
+        pre_fill.grad_sh = sbuf[1:].view(P, K, 3)
+    before = {k: getattr(pre_fill, k).clone() for k in ("grad_means3D", "grad_means2D", "grad_opacity",
+                                                         "grad_scales", "grad_rotations", "grad_sh")}
+    pl.preprocess_backward(g, cam, pre.radii, pre.records, grad_acc, None, None, None, out=pre_fill)
+    torch.cuda.synchronize()
+    vis = pre.radii > 0
+    assert int(vis.sum()) > 0
+    for k, b in before.items():
+        got = getattr(pre_fill, k)
+        want = b + getattr(fresh, k).reshape(b.shape)
+        want[~vis] = b[~vis]
+        assert torch.equal(got, want), k
+    if not unaligned and name == "cfg2_200k":
+        # the staged and per-thread SH paths agree bit for bit (non-accumulating)
+        buf = torch.empty(g.sh.numel() + 1, device=cuda)
+        buf[1:] = g.sh.reshape(-1)
+        g2 = pl.Gaussians(g.means3D, g.opacities, g.scales, g.rotations, None, buf[1:].view(g.sh.shape), None,
+                          g.scale_modifier, g.degree)
+        other = pl.preprocess_backward(g2, cam, pre.radii, pre.records, grad_acc, None, None, None)
+        torch.cuda.synchronize()
+        for k in before:
+            assert torch.equal(getattr(other, k), getattr(fresh, k)), k
+
+
 def test_cov3d_precomp_and_colors_paths(cuda):
     scene, view = _scene("cfg2_small_view", cuda)
     # cov3d from scale/rotation via the oracle's own forward (pinned above)
