@@ -55,6 +55,7 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-cfg2", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-autograd", action="store_true", help="skip the drop-in autograd path comparison")
     return p.parse_args()
 
 
@@ -353,6 +354,22 @@ def roofline(prof, peaks, pixels, N):
     return out
 
 
+def measure_autograd(args, scene, views, targets_dev, targets_host, world, device, views_total):
+    """The drop-in path (GaussianRasterizer + fused_ssim under autograd) on the same workload."""
+    import torch
+
+    tr_ag = Trainer(scene, views, targets_dev, targets_host, world, device, path="autograd")
+    ms_ag = timed(tr_ag.step, args.steps, args.warmup, world)
+    out = {"value": 1000.0 * views_total / ms_ag, "unit": "views/s",
+           "path": "GaussianRasterizer + fused_ssim under autograd, ViewShardedStep"}
+    if not args.no_e2e:
+        ms_ag_e2e = timed(lambda: tr_ag.step(e2e=True), args.steps, 1, world)
+        out["e2e"] = 1000.0 * views_total / ms_ag_e2e
+    del tr_ag
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_reference(args):
     """CPU restatement of the reference's kernels (warp-lang is absent)."""
     rank = int(os.environ.get("RANK", "0"))
@@ -427,15 +444,9 @@ def run_ours(args):
                "d2h_bytes_per_step": V * 4}
 
     # the drop-in autograd path on the same workload, for comparison
-    tr_ag = Trainer(scene, views, targets_dev, targets_host, world, device, path="autograd")
-    ms_ag = timed(tr_ag.step, args.steps, args.warmup, world)
-    autograd_api = {"value": 1000.0 * views_total / ms_ag, "unit": "views/s",
-                    "path": "GaussianRasterizer + fused_ssim under autograd, ViewShardedStep"}
-    if not args.no_e2e:
-        ms_ag_e2e = timed(lambda: tr_ag.step(e2e=True), args.steps, 1, world)
-        autograd_api["e2e"] = 1000.0 * views_total / ms_ag_e2e
-    del tr_ag
-    torch.cuda.empty_cache()
+    autograd_api = None
+    if not args.no_autograd:
+        autograd_api = measure_autograd(args, scene, views, targets_dev, targets_host, world, device, views_total)
 
     prof = kernel_profile(tr, steps=1)
     launches = sum(v["kernels"] for v in prof.values())

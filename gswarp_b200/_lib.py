@@ -24,7 +24,7 @@ GSB_ERR_OVERFLOW = -2
 GSB_ERR_CUDA = -3
 GSB_ERR_TIMEOUT = -4
 
-ABI_VERSION = 3
+ABI_VERSION = 4
 RECORD_FLOATS = 12
 GRAD_FLOATS = 12
 
@@ -45,7 +45,7 @@ class PreprocessArgs(ctypes.Structure):
         ("colors_precomp", vp),
         ("coverage_mode", c_int),
         ("radii", vp), ("proj_2d", vp), ("conic_2d", vp), ("conic_2d_inv", vp), ("depths", vp),
-        ("tiles_touched", vp), ("records", vp), ("cov3d_out", vp),
+        ("tiles_touched", vp), ("records", vp), ("cov3d_out", vp), ("bin_records", vp),
     ]
 
 
@@ -66,7 +66,7 @@ class BinSortArgs(ctypes.Structure):
         ("depth_order", vp), ("point_offsets", vp), ("radii", vp), ("records", vp),
         ("conic_2d_inv", vp), ("tiles_touched", vp),
         ("point_list", vp), ("ranges", vp), ("error_word", vp),
-        ("workspace", vp), ("workspace_bytes", ctypes.c_size_t),
+        ("workspace", vp), ("workspace_bytes", ctypes.c_size_t), ("bin_records", vp),
     ]
 
 

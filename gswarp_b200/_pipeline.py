@@ -127,6 +127,7 @@ class Preprocessed:
     tiles_touched: torch.Tensor
     records: torch.Tensor
     cov3d: torch.Tensor | None = None
+    bin_records: torch.Tensor | None = None
 
 
 @dataclass(slots=True)
@@ -174,7 +175,15 @@ def coverage_mode_id(options: ExecutionOptions | None) -> int:
     return resolve_tile_coverage_mode_id(mode, BASELINE_3DGS_COVERAGE)
 
 
-def preprocess(g: Gaussians, cam: Camera, coverage_mode: int, want_cov3d: bool = False) -> Preprocessed:
+BIN_RECORD_FLOATS = 8
+MAX_TILE_GRID = 65535
+
+
+def preprocess(g: Gaussians, cam: Camera, coverage_mode: int, want_cov3d: bool = False,
+               bin_records: bool = True) -> Preprocessed:
+    """Runs the fused preprocess.  With ``bin_records`` (the default) it also
+    writes the 32-byte per-Gaussian records the binning emit reads instead of
+    gathering radii, render records, conic_2D_inv and tiles_touched."""
     P = g.P
     dev = g.means3D.device
     cov3d = None
@@ -190,6 +199,9 @@ def preprocess(g: Gaussians, cam: Camera, coverage_mode: int, want_cov3d: bool =
         tiles_touched=torch.empty(P, dtype=torch.int32, device=dev),
         records=torch.empty((P, _lib.RECORD_FLOATS), dtype=torch.float32, device=dev),
     )
+    gx, gy = cam.grid
+    if bin_records and P > 0 and gx <= MAX_TILE_GRID and gy <= MAX_TILE_GRID:
+        out.bin_records = torch.empty((P, BIN_RECORD_FLOATS), dtype=torch.float32, device=dev)
     if P == 0:
         return out
     a = _lib.PreprocessArgs()
@@ -218,6 +230,7 @@ def preprocess(g: Gaussians, cam: Camera, coverage_mode: int, want_cov3d: bool =
     a.tiles_touched = _lib.ptr(out.tiles_touched)
     a.records = _lib.ptr(out.records)
     a.cov3d_out = _lib.ptr(cov3d) if (cov3d is not None and g.cov3D is None) else None
+    a.bin_records = _lib.ptr(out.bin_records)
     with _stage_timer("preprocess_fwd", {"P": P, "kernels": 1}):
         _lib.call("gsb_preprocess_fwd", a, _lib.stream_handle(dev))
     return out
@@ -279,6 +292,7 @@ def binning(pre: Preprocessed, cam: Camera, coverage_mode: int) -> Binned:
     b.error_word = _lib.ptr(sticky)
     b.workspace = _lib.ptr(ws2)
     b.workspace_bytes = ws2.numel()
+    b.bin_records = _lib.ptr(pre.bin_records)
     with _stage_timer("bin_emit_sort", {"P": P, "num_rendered": R, "kernels": 7}):
         _lib.call("gsb_bin_emit_sort", b, stream)
     return Binned(R, point_list[:R], ranges)

@@ -145,6 +145,27 @@ struct EmitPairs {
   }
 };
 
+// Emit from the 32-byte binning records written by preprocess: one random
+// 32-byte read per Gaussian; the pair count is the difference of adjacent
+// inclusive offsets (both coalesced).
+__global__ void __launch_bounds__(256) emit_binrec_kernel(
+    int P, int gx, int mode, const int* __restrict__ order, const int* __restrict__ offsets,
+    const float4* __restrict__ bin_records, unsigned* __restrict__ keys, unsigned* __restrict__ vals,
+    long long* __restrict__ err) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= P) return;
+  const int end = offsets[r];
+  const int n = end - (r > 0 ? offsets[r - 1] : 0);
+  if (n <= 0) return;
+  const int p = order[r];
+  float px, py, ca, cb, cc, t;
+  Rect rect;
+  load_bin_record(bin_records + (size_t)p * 2, px, py, ca, cb, cc, t, rect);
+  EmitPairs e{keys, vals, (long long)end - n, n, p, 0};
+  cover_tiles_in_rect(px, py, ca, cb, cc, t, rect, gx, mode, e);
+  if (e.k != n) atomicOr((unsigned long long*)err, (unsigned long long)ERR_EMIT_MISMATCH);
+}
+
 __global__ void __launch_bounds__(256) emit_kernel(
     int P, int gx, int gy, int mode, const int* __restrict__ order,
     const int* __restrict__ offsets, const int* __restrict__ tiles_touched,
@@ -279,10 +300,15 @@ GSB_EXPORT int gsb_bin_emit_sort(const gsb_bin_sort_args* a, void* stream) {
   cudaMemsetAsync(a->ranges, 0, (size_t)tiles * 2 * sizeof(int), s);
   const long long R = a->num_rendered;
   if (R == 0 || a->P == 0) return check_launch("gsb_bin_emit_sort(empty)");
-  if (!a->depth_order || !a->point_offsets || !a->radii || !a->records || !a->conic_2d_inv ||
-      !a->tiles_touched || !a->point_list || !a->workspace ||
+  const bool binrec = a->bin_records != nullptr;
+  if (!a->depth_order || !a->point_offsets || !a->point_list || !a->workspace ||
+      (!binrec && (!a->radii || !a->records || !a->conic_2d_inv || !a->tiles_touched)) ||
       a->workspace_bytes < gsb_bin_sort_workspace_bytes(R, a->W, a->H)) {
     set_error("gsb_bin_emit_sort: null pointer or workspace too small");
+    return GSB_ERR_INVALID;
+  }
+  if (binrec && ((reinterpret_cast<uintptr_t>(a->bin_records) & 15) || gx > 65535 || gy > 65535)) {
+    set_error("gsb_bin_emit_sort: bin_records needs 16-byte alignment and tile grids below 65536");
     return GSB_ERR_INVALID;
   }
   char* w = (char*)(((uintptr_t)a->workspace + 255) & ~(uintptr_t)255);
@@ -307,9 +333,14 @@ GSB_EXPORT int gsb_bin_emit_sort(const gsb_bin_sort_args* a, void* stream) {
     vb[0] = vals_alt;
     vb[1] = pl;
   }
-  emit_kernel<<<div_up(a->P, 256), 256, 0, s>>>(
-      a->P, gx, gy, a->coverage_mode, a->depth_order, a->point_offsets, a->tiles_touched, a->radii,
-      reinterpret_cast<const float4*>(a->records), a->conic_2d_inv, kb[0], vb[0], a->error_word);
+  if (binrec)
+    emit_binrec_kernel<<<div_up(a->P, 256), 256, 0, s>>>(
+        a->P, gx, a->coverage_mode, a->depth_order, a->point_offsets,
+        reinterpret_cast<const float4*>(a->bin_records), kb[0], vb[0], a->error_word);
+  else
+    emit_kernel<<<div_up(a->P, 256), 256, 0, s>>>(
+        a->P, gx, gy, a->coverage_mode, a->depth_order, a->point_offsets, a->tiles_touched, a->radii,
+        reinterpret_cast<const float4*>(a->records), a->conic_2d_inv, kb[0], vb[0], a->error_word);
   const int where = radix::sort_pairs(kb, vb, R, passes, sort_scratch, a->error_word, s);
   ranges_kernel<<<div_up(R, 256), 256, 0, s>>>(R, kb[where], a->ranges);
   return check_launch("gsb_bin_emit_sort");

@@ -148,13 +148,22 @@ struct NoEmit {
   __device__ __forceinline__ void operator()(int) const {}
 };
 
+// The two halves of cover_tiles: the footprint's opacity threshold and
+// clipped SnugBox rect (which need the 2D covariance and the radius), then
+// the tile sweep inside the rect (which needs only the centre, the conic and
+// the threshold).  Preprocess stores (rect, threshold) per Gaussian so the
+// binning emit can run the second half alone, on the same bits.
+__device__ __forceinline__ void coverage_setup(float px, float py, float cov_aa, float cov_cc,
+                                               float opacity, int cuda_radius, int gx, int gy,
+                                               Rect& r, float& t) {
+  t = opacity_threshold(opacity);
+  r = snugbox_rect(px, py, cov_aa, cov_cc, t, cuda_radius, gx, gy);
+}
+
 template <typename Emit>
-__device__ __forceinline__ int cover_tiles(float px, float py, float cov_aa, float cov_cc,
-                                           float ca, float cb, float cc, float opacity,
-                                           int cuda_radius, int gx, int gy, int mode,
-                                           const Emit& emit) {
-  const float t = opacity_threshold(opacity);
-  Rect r = snugbox_rect(px, py, cov_aa, cov_cc, t, cuda_radius, gx, gy);
+__device__ __forceinline__ int cover_tiles_in_rect(float px, float py, float ca, float cb, float cc,
+                                                   float t, const Rect r, int gx, int mode,
+                                                   const Emit& emit) {
   int span_x = r.x1 - r.x0;
   int span_y = r.y1 - r.y0;
   int area = span_x * span_y;
@@ -192,6 +201,42 @@ __device__ __forceinline__ int cover_tiles(float px, float py, float cov_aa, flo
     }
   }
   return count;
+}
+
+template <typename Emit>
+__device__ __forceinline__ int cover_tiles(float px, float py, float cov_aa, float cov_cc,
+                                           float ca, float cb, float cc, float opacity,
+                                           int cuda_radius, int gx, int gy, int mode,
+                                           const Emit& emit) {
+  Rect r;
+  float t;
+  coverage_setup(px, py, cov_aa, cov_cc, opacity, cuda_radius, gx, gy, r, t);
+  return cover_tiles_in_rect(px, py, ca, cb, cc, t, r, gx, mode, emit);
+}
+
+// 32-byte binning record of a Gaussian with tiles: (px, py, conic a, conic b)
+// and (conic c, threshold, rect x0 | y0 << 16, rect x1 | y1 << 16); the rect
+// packing needs tile grids below 65536 in each direction.
+__device__ __forceinline__ void store_bin_record(float4* rec, float px, float py, float ca, float cb,
+                                                 float cc, float t, const Rect r) {
+  rec[0] = make_float4(px, py, ca, cb);
+  rec[1] = make_float4(cc, t, __uint_as_float((unsigned)r.x0 | ((unsigned)r.y0 << 16)),
+                       __uint_as_float((unsigned)r.x1 | ((unsigned)r.y1 << 16)));
+}
+__device__ __forceinline__ void load_bin_record(const float4* rec, float& px, float& py, float& ca,
+                                                float& cb, float& cc, float& t, Rect& r) {
+  const float4 a = __ldg(rec), b = __ldg(rec + 1);
+  px = a.x;
+  py = a.y;
+  ca = a.z;
+  cb = a.w;
+  cc = b.x;
+  t = b.y;
+  const unsigned lo = __float_as_uint(b.z), hi = __float_as_uint(b.w);
+  r.x0 = (int)(lo & 0xFFFFu);
+  r.y0 = (int)(lo >> 16);
+  r.x1 = (int)(hi & 0xFFFFu);
+  r.y1 = (int)(hi >> 16);
 }
 
 }  // namespace gsb

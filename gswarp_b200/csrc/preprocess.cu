@@ -244,8 +244,13 @@ __global__ void __launch_bounds__(256) preprocess_fwd_kernel(const gsb_preproces
         con0 = k0;
         con1 = k1;
         con2 = k2;
-        tiles = cover_tiles(px, py, cov_a, cov_c, con0, con1, con2, opacity, radius, gx, gy,
-                            a.coverage_mode, NoEmit{});
+        Rect br;
+        float bt;
+        coverage_setup(px, py, cov_a, cov_c, opacity, radius, gx, gy, br, bt);
+        tiles = cover_tiles_in_rect(px, py, con0, con1, con2, bt, br, gx, a.coverage_mode, NoEmit{});
+        if (a.bin_records && tiles > 0)
+          store_bin_record(reinterpret_cast<float4*>(a.bin_records) + (size_t)idx * 2, px, py, con0, con1,
+                           con2, bt, br);
       } else {
         cov_a = cov_b = cov_c = 0.0f;
       }
@@ -361,6 +366,11 @@ GSB_EXPORT int gsb_preprocess_fwd(const gsb_preprocess_args* a, void* stream) {
       (a->rotations && (reinterpret_cast<uintptr_t>(a->rotations) & 15)) ||
       (reinterpret_cast<uintptr_t>(a->proj_2d) & 7)) {
     set_error("gsb_preprocess_fwd: records/rotations need 16-byte and proj_2d 8-byte alignment");
+    return GSB_ERR_INVALID;
+  }
+  if (a->bin_records && ((reinterpret_cast<uintptr_t>(a->bin_records) & 15) ||
+                         div_up(a->W, BLOCK_X) > 65535 || div_up(a->H, BLOCK_Y) > 65535)) {
+    set_error("gsb_preprocess_fwd: bin_records needs 16-byte alignment and tile grids below 65536");
     return GSB_ERR_INVALID;
   }
   preprocess_fwd_kernel<<<div_up(a->P, 256), 256, 0, (cudaStream_t)stream>>>(*a);

@@ -7,7 +7,7 @@
 //      pass in a single read of the keys (warp-aggregated shared atomics);
 //   2. a tiny kernel turns them into per-pass bin bases;
 //   3. each pass is ONE kernel: a CTA claims the next 3840-key tile through
-//      an atomic counter, ranks its keys stably per warp (__match_any_sync),
+//      an atomic counter, ranks its keys stably per warp (per-bit ballots),
 //      publishes its per-digit counts, resolves its global offsets by
 //      decoupled look-back over the preceding tiles, stages the tile in
 //      digit order in shared memory and writes it out in runs.
@@ -32,6 +32,8 @@ constexpr int WARPS = THREADS / 32;
 constexpr int ITEMS = 15;
 constexpr int TILE_KEYS = THREADS * ITEMS;  // 3840
 constexpr int MAX_PASSES = 4;
+constexpr int LOOKBACK_WINDOW = 4;
+constexpr int HIST_ITEMS = 8;
 
 constexpr unsigned long long FLAG_AGG = 1ull << 62;
 constexpr unsigned long long FLAG_INC = 2ull << 62;
@@ -44,6 +46,20 @@ __device__ __forceinline__ unsigned long long ld_volatile(const unsigned long lo
 }
 __device__ __forceinline__ void st_volatile(unsigned long long* p, unsigned long long v) {
   asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Lanes of the warp whose 9-bit value d (an 8-bit digit, or RADIX for "no
+// key") equals this lane's: nine ballots, one per bit (cheaper on sm_100a
+// than a match.any over 32 distinct values).
+__device__ __forceinline__ unsigned digit_peers(unsigned d) {
+  unsigned peers = 0xffffffffu;
+#pragma unroll
+  for (int b = 0; b <= RADIX_BITS; ++b) {
+    const bool bit = (d >> b) & 1u;
+    const unsigned m = __ballot_sync(0xffffffffu, bit);
+    peers &= bit ? m : ~m;
+  }
+  return peers;
 }
 
 // Exclusive scan of one value per thread across a 256-thread CTA.
@@ -70,28 +86,40 @@ __device__ __forceinline__ unsigned block_exclusive_scan(unsigned v, unsigned* s
   return wpre + x - v;
 }
 
+// Digit histograms of every pass in one read of the keys.  Each warp counts
+// into its own shared sub-histogram with plain shared atomics (same-digit
+// lanes serialize in hardware; digits of depth bits and tile ids spread well
+// enough that this beats aggregating peers first), HIST_ITEMS keys per lane
+// loaded before any is counted.
 __global__ void __launch_bounds__(THREADS) histogram_kernel(const unsigned* __restrict__ keys,
                                                             int n, int passes,
                                                             unsigned* __restrict__ hist) {
-  __shared__ unsigned s_hist[MAX_PASSES][RADIX];
-  for (int i = threadIdx.x; i < MAX_PASSES * RADIX; i += THREADS) (&s_hist[0][0])[i] = 0u;
+  __shared__ unsigned s_hist[WARPS][MAX_PASSES][RADIX];
+  for (int i = threadIdx.x; i < WARPS * MAX_PASSES * RADIX; i += THREADS) (&s_hist[0][0][0])[i] = 0u;
   __syncthreads();
-  const int lane = threadIdx.x & 31;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const long long warps_total = (long long)gridDim.x * WARPS;
-  const long long warp_id = (long long)blockIdx.x * WARPS + (threadIdx.x >> 5);
-  for (long long base = warp_id * 32; base < n; base += warps_total * 32) {
-    const long long i = base + lane;
-    const bool valid = i < n;
-    const unsigned k = valid ? keys[i] : 0u;
-    for (int p = 0; p < passes; ++p) {
-      const unsigned d = valid ? (k >> (p * RADIX_BITS)) & (RADIX - 1) : (unsigned)RADIX;
-      const unsigned peers = __match_any_sync(0xffffffffu, d);
-      if (valid && lane == __ffs(peers) - 1) atomicAdd(&s_hist[p][d], (unsigned)__popc(peers));
+  const long long warp_id = (long long)blockIdx.x * WARPS + warp;
+  for (long long base = warp_id * 32 * HIST_ITEMS; base < n; base += warps_total * 32 * HIST_ITEMS) {
+    unsigned kv[HIST_ITEMS];
+#pragma unroll
+    for (int it = 0; it < HIST_ITEMS; ++it) {
+      const long long i = base + it * 32 + lane;
+      kv[it] = i < n ? __ldg(keys + i) : 0u;
+    }
+#pragma unroll
+    for (int it = 0; it < HIST_ITEMS; ++it) {
+      if (base + it * 32 + lane < n) {
+        for (int p = 0; p < passes; ++p)
+          atomicAdd(&s_hist[warp][p][(kv[it] >> (p * RADIX_BITS)) & (RADIX - 1)], 1u);
+      }
     }
   }
   __syncthreads();
   for (int i = threadIdx.x; i < passes * RADIX; i += THREADS) {
-    const unsigned c = (&s_hist[0][0])[i];
+    unsigned c = 0;
+#pragma unroll
+    for (int w = 0; w < WARPS; ++w) c += (&s_hist[w][0][0])[i];
     if (c) atomicAdd(&hist[i], c);
   }
 }
@@ -105,7 +133,7 @@ __global__ void __launch_bounds__(THREADS) bin_base_kernel(const unsigned* __res
 }
 
 template <bool HAS_VALS>
-__global__ void __launch_bounds__(THREADS) onesweep_kernel(
+__global__ void __launch_bounds__(THREADS, 4) onesweep_kernel(
     const unsigned* __restrict__ keys_in, const unsigned* __restrict__ vals_in,
     unsigned* __restrict__ keys_out, unsigned* __restrict__ vals_out, int n, int shift,
     const unsigned* __restrict__ bin_base, unsigned long long* __restrict__ lookback,
@@ -125,13 +153,12 @@ __global__ void __launch_bounds__(THREADS) onesweep_kernel(
   const int tile = s_tile;
   const long long base = (long long)tile * TILE_KEYS + (long long)warp * (ITEMS * 32);
 
-  unsigned key[ITEMS], val[ITEMS], rank[ITEMS];
+  unsigned key[ITEMS], rank[ITEMS];
 #pragma unroll
   for (int i = 0; i < ITEMS; ++i) {
     const long long pos = base + i * 32 + lane;
     const bool valid = pos < n;
     key[i] = valid ? keys_in[pos] : 0xFFFFFFFFu;
-    if (HAS_VALS) val[i] = valid ? vals_in[pos] : 0u;
     rank[i] = valid ? 0u : 0xFFFFFFFFu;  // invalid marker
   }
   // Stable warp-local ranking: round i holds 32 consecutive keys.
@@ -139,7 +166,7 @@ __global__ void __launch_bounds__(THREADS) onesweep_kernel(
   for (int i = 0; i < ITEMS; ++i) {
     const bool valid = rank[i] != 0xFFFFFFFFu;
     const unsigned d = valid ? (key[i] >> shift) & (RADIX - 1) : (unsigned)RADIX;
-    const unsigned peers = __match_any_sync(0xffffffffu, d);
+    const unsigned peers = digit_peers(d);
     unsigned old = 0;
     if (valid) {
       old = s_warp_hist[warp][d];
@@ -162,40 +189,68 @@ __global__ void __launch_bounds__(THREADS) onesweep_kernel(
   unsigned long long* my_slot = lookback + (size_t)tile * RADIX + tid;
   st_volatile(my_slot, (tile == 0 ? FLAG_INC : FLAG_AGG) | (unsigned long long)total);
   s_digit_start[tid] = block_exclusive_scan(total, s_scan, nullptr);
-
-  unsigned long long excl = 0;
-  if (tile > 0) {
-    int t = tile - 1;
-    int spins = 0;
-    while (true) {
-      const unsigned long long v = ld_volatile(lookback + (size_t)t * RADIX + tid);
-      const unsigned long long flag = v & ~VALUE_MASK;
-      if (flag == 0) {
-        if (++spins > SPIN_LIMIT) {
-          atomicOr((unsigned long long*)err, (unsigned long long)ERR_LOOKBACK_TIMEOUT);
-          break;
-        }
-        continue;
-      }
-      excl += v & VALUE_MASK;
-      if (flag == FLAG_INC || t == 0) break;
-      --t;
-    }
-    st_volatile(my_slot, FLAG_INC | (excl + total));
-  }
-  s_global[tid] = bin_base[tid] + (unsigned)excl;
   __syncthreads();
 
-  // Stage the tile in digit order.
+  // Stage the tile in digit order (before the look-back, so the key and rank
+  // registers are free while it waits); values are read here, not earlier.
 #pragma unroll
   for (int i = 0; i < ITEMS; ++i) {
     if (rank[i] != 0xFFFFFFFFu) {
       const unsigned d = (key[i] >> shift) & (RADIX - 1);
-      const unsigned pos = s_digit_start[d] + s_warp_hist[warp][d] + rank[i];
-      s_keys[pos] = key[i];
-      if (HAS_VALS) s_vals[pos] = val[i];
+      rank[i] += s_digit_start[d] + s_warp_hist[warp][d];
+      s_keys[rank[i]] = key[i];
     }
   }
+  if (HAS_VALS) {
+    unsigned val[ITEMS];
+#pragma unroll
+    for (int i = 0; i < ITEMS; ++i) {
+      const long long pos = base + i * 32 + lane;
+      val[i] = rank[i] != 0xFFFFFFFFu ? vals_in[pos] : 0u;
+    }
+#pragma unroll
+    for (int i = 0; i < ITEMS; ++i)
+      if (rank[i] != 0xFFFFFFFFu) s_vals[rank[i]] = val[i];
+  }
+
+  // Decoupled look-back over a window of LOOKBACK_WINDOW predecessors at a
+  // time: the window's status words are loaded together (one memory round
+  // trip per window instead of one per tile), then consumed nearest first,
+  // adding aggregates until an inclusive prefix is found.  A slot that is not
+  // published yet is re-read (bounded) before the walk moves past it.
+  unsigned long long excl = 0;
+  if (tile > 0) {
+    int t = tile - 1;
+    int spins = 0;
+    bool done = false;
+    while (!done) {
+      unsigned long long w[LOOKBACK_WINDOW];
+#pragma unroll
+      for (int k = 0; k < LOOKBACK_WINDOW; ++k)
+        w[k] = t - k >= 0 ? ld_volatile(lookback + (size_t)(t - k) * RADIX + tid) : FLAG_INC;
+#pragma unroll
+      for (int k = 0; k < LOOKBACK_WINDOW; ++k) {
+        if (done) break;
+        unsigned long long v = w[k];
+        while ((v & ~VALUE_MASK) == 0) {
+          if (++spins > SPIN_LIMIT) {
+            atomicOr((unsigned long long*)err, (unsigned long long)ERR_LOOKBACK_TIMEOUT);
+            break;
+          }
+          v = ld_volatile(lookback + (size_t)(t - k) * RADIX + tid);
+        }
+        if ((v & ~VALUE_MASK) == 0) {  // timed out: give up, error already flagged
+          done = true;
+          break;
+        }
+        if (t - k >= 0) excl += v & VALUE_MASK;
+        if ((v & ~VALUE_MASK) == FLAG_INC || t - k <= 0) done = true;
+      }
+      t -= LOOKBACK_WINDOW;
+    }
+    st_volatile(my_slot, FLAG_INC | (excl + total));
+  }
+  s_global[tid] = bin_base[tid] + (unsigned)excl;
   __syncthreads();
   const long long tile_base = (long long)tile * TILE_KEYS;
   const int tile_n = (int)min((long long)TILE_KEYS, (long long)n - tile_base);

@@ -68,12 +68,72 @@ __device__ __forceinline__ bool box_hits(const float4 b, float x0, float x1, flo
   return b.x <= x1 && b.y >= x0 && b.z <= y1 && b.w >= y0;
 }
 
+// Ellipse data for the exact block test: conic (a, b, c) and the culling
+// threshold on q = a dx^2 + 2b dx dy + c dy^2.  alpha >= 1/255 needs
+// q <= t = 2 ln(255 op); the test uses t * 1.02 + 0.05 (alpha 2.5% below the
+// cut-off at the edge, far above the rounding of the per-pixel evaluation),
+// and +inf for a conic that is not positive definite (never culled).
+__device__ __forceinline__ float4 cull_ellipse(float a, float b, float c, float op) {
+  const float inf = __int_as_float(0x7f800000);
+  if (!(a > 0.0f) || !(a * c - b * b > 0.0f)) return make_float4(a, b, c, inf);
+  const float t = 2.0f * __logf(255.0f * op);
+  return make_float4(a, b, c, t * 1.02f + 0.05f);
+}
+
+// Whether the ellipse {q <= e.w} around (cx, cy) reaches the pixel block
+// [x0, x1] x [y0, y1] (d = centre - pixel, as in the per-pixel evaluation).
+// Outside the block the minimum of the convex q lies on an edge; each edge
+// minimum is the clamped stationary point.
+__device__ __forceinline__ bool ellipse_hits(float cx, float cy, const float4 e, float x0, float x1,
+                                             float y0, float y1) {
+  if (!(e.w < __int_as_float(0x7f800000))) return true;
+  const float X0 = cx - x1, X1 = cx - x0, Y0 = cy - y1, Y1 = cy - y0;
+  if (X0 <= 0.0f && X1 >= 0.0f && Y0 <= 0.0f && Y1 >= 0.0f) return true;
+  const float ia = fast_rcp(e.x), ic = fast_rcp(e.z);
+  float q = __int_as_float(0x7f800000);
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const float X = k ? X1 : X0;
+    const float dy = fminf(fmaxf(-e.y * X * ic, Y0), Y1);
+    q = fminf(q, e.x * X * X + (2.0f * e.y * X + e.z * dy) * dy);
+    const float Y = k ? Y1 : Y0;
+    const float dx = fminf(fmaxf(-e.y * Y * ia, X0), X1);
+    q = fminf(q, e.z * Y * Y + (2.0f * e.y * Y + e.x * dx) * dx);
+  }
+  return q <= e.w;
+}
+
+// Exponent of a Gaussian at pixel offset (dx, dy) in log2 units, from the
+// staged coefficients cf = (-a/2, -b, -c/2) * log2(e):
+//   power2 = cf.x dx^2 + (cf.z dy + cf.y dx) dy = log2(e) * (-(a dx^2 + c dy^2)/2 - b dx dy),
+// so exp(power) = ex2(power2).  ax = cf.x dx^2 and bx = cf.y dx are shared by
+// the thread's two pixels (same column).  Forward and backward evaluate it
+// through this one function with explicit FMAs, so they make the same
+// alpha decisions bit for bit.
+__device__ __forceinline__ float4 power_coefs(float a, float b, float c) {
+  const float L2E = 1.4426950408889634f;
+  return make_float4(-0.5f * L2E * a, -L2E * b, -0.5f * L2E * c, 0.0f);
+}
+__device__ __forceinline__ void column_terms(const float4 cf, float dx, float& ax, float& bx) {
+  ax = __fmul_rn(__fmul_rn(cf.x, dx), dx);
+  bx = __fmul_rn(cf.y, dx);
+}
+__device__ __forceinline__ float power2_of(const float4 cf, float ax, float bx, float dy) {
+  return __fmaf_rn(__fmaf_rn(cf.z, dy, bx), dy, ax);
+}
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 template <bool DEPTH>
 __global__ void __launch_bounds__(THREADS) render_fwd_kernel(const gsb_render_fwd_args a, int gx) {
   __shared__ float2 s_xy[BATCH];
-  __shared__ float4 s_cop[BATCH];   // conic a, b, c, opacity
+  __shared__ float4 s_cf[BATCH];    // power coefficients, opacity in .w
   __shared__ float4 s_rgbd[BATCH];  // r, g, b, depth
   __shared__ float4 s_box[BATCH];   // alpha_box
+  __shared__ float4 s_el[BATCH];    // cull_ellipse
   const int tile = blockIdx.x;
   const int lane = threadIdx.x & 31;
   int pxi, py0;
@@ -106,9 +166,12 @@ __global__ void __launch_bounds__(THREADS) render_fwd_kernel(const gsb_render_fw
       const float4 q1 = __ldg(rec + (size_t)id * 3 + 1);
       const float4 q2 = __ldg(rec + (size_t)id * 3 + 2);
       s_xy[threadIdx.x] = make_float2(q0.x, q0.y);
-      s_cop[threadIdx.x] = make_float4(q0.z, q0.w, q1.x, q1.y);
+      float4 cf = power_coefs(q0.z, q0.w, q1.x);
+      cf.w = q1.y;
+      s_cf[threadIdx.x] = cf;
       s_rgbd[threadIdx.x] = make_float4(q2.x, q2.y, q2.z, q1.z);
       s_box[threadIdx.x] = alpha_box(q0.x, q0.y, q0.z, q0.w, q1.x, q1.y);
+      s_el[threadIdx.x] = cull_ellipse(q0.z, q0.w, q1.x, q1.y);
     }
     __syncthreads();
     const int cnt = min(BATCH, range.y - b);
@@ -117,22 +180,27 @@ __global__ void __launch_bounds__(THREADS) render_fwd_kernel(const gsb_render_fw
     for (int cb = 0; cb < cnt; cb += 32) {
       if (__all_sync(FULL, done[0] && done[1])) break;
       const int g = cb + lane;
-      unsigned hits = __ballot_sync(FULL, g < cnt && box_hits(s_box[g], bx0, bx1, by0, by1));
+      bool hit = g < cnt && box_hits(s_box[g], bx0, bx1, by0, by1);
+      if (__any_sync(FULL, hit) && hit) {
+        const float2 cxy = s_xy[g];
+        hit = ellipse_hits(cxy.x, cxy.y, s_el[g], bx0, bx1, by0, by1);
+      }
+      unsigned hits = __ballot_sync(FULL, hit);
       while (hits) {
       const int j = cb + __ffs(hits) - 1;
       hits &= hits - 1;
       if (done[0] && done[1]) continue;
       const float2 xy = s_xy[j];
-      const float4 co = s_cop[j];
+      const float4 cf = s_cf[j];
       const float dx = xy.x - fx;
-      const float adx2 = co.x * dx * dx;
+      float ax, bx;
+      column_terms(cf, dx, ax, bx);
 #pragma unroll
       for (int p = 0; p < 2; ++p) {
         if (done[p]) continue;
-        const float dy = xy.y - fy[p];
-        const float power = -0.5f * (adx2 + co.z * dy * dy) - co.y * dx * dy;
-        if (power > 0.0f) continue;
-        const float alpha = fminf(0.99f, co.w * fast_exp(power));
+        const float power2 = power2_of(cf, ax, bx, xy.y - fy[p]);
+        if (power2 > 0.0f) continue;
+        const float alpha = fminf(0.99f, cf.w * ex2_approx(power2));
         if (alpha < (1.0f / 255.0f)) continue;
         const float test_T = T[p] * (1.0f - alpha);
         if (test_T < 0.0001f) {
@@ -213,69 +281,83 @@ __device__ __forceinline__ int warp_reduce10(const float (&v)[10], float& out) {
 }
 
 // Back-to-front state of one pixel (backward_kernels.py:606-625).
+// The colour part of accum_rec only enters dL/dalpha through its dot
+// product with the pixel's colour gradient g, so the state keeps that dot
+// product S = accum_rec . g (same recurrence, S' = la lcg + (1 - la) S with
+// lcg = last_color . g) instead of the three channels.
 struct BwdPixel {
   int lc;
   float fy, T, T_final, g0, g1, g2, gd, ga, bg_dot;
-  float ar0, ar1, ar2, adr, aar, la, lc0, lc1, lc2, ld;
+  float S, lcg, adr, aar, la, ld;
 };
 
-// One pixel's contribution of the Gaussian at this position, added to v[]
-// (backward_kernels.py:637-685).  Returns whether the pixel contributed.
-template <bool DEPTH>
-__device__ __forceinline__ bool bwd_pixel(BwdPixel& s, float dx, float adx2, const float2 xy,
-                                          const float4 co, const float4 cd, float ddelx_dx,
-                                          float ddely_dy, float (&v)[10]) {
-  const float dy = xy.y - s.fy;
-  const float power = -0.5f * (adx2 + co.z * dy * dy) - co.y * dx * dy;
-  if (power > 0.0f) return false;
-  const float G = fast_exp(power);
-  const float alpha = fminf(0.99f, co.w * G);
+// Gradient sums of one Gaussian over the thread's pixels.  The per-pixel
+// terms of backward_kernels.py:637-685 are, with u = G * dL/dalpha,
+//   d/dx   = -op * W/2 * u (a dx + b dy)     d/dconic_a = -op/2 * u dx^2
+//   d/dy   = -op * H/2 * u (c dy + b dx)     d/dconic_b = -op/2 * u dx dy
+//   d/dop  = u                               d/dconic_c = -op/2 * u dy^2
+// so each pixel only accumulates the moments U = sum u, UY = sum u dy,
+// UYY = sum u dy^2 (dx is the thread's column); the Gaussian's constants
+// (op, a, b, c, W/2, H/2, -1/2) are applied once, after the warp reduction.
+struct BwdSums {
+  float U, UY, UYY, dcol0, dcol1, dcol2, ddepth;
+};
+
+// One pixel's contribution of the Gaussian at this position (3DGS
+// recurrences accum_rec / last_alpha / last_color, backward_kernels.py:
+// 637-671).  Returns whether the pixel contributed.
+template <bool DEPTH, bool GA>
+__device__ __forceinline__ bool bwd_pixel(BwdPixel& s, const float4 cf, float ax, float bx, float y,
+                                          const float4 cd, bool has_bg, BwdSums& m) {
+  const float dy = y - s.fy;
+  const float power2 = power2_of(cf, ax, bx, dy);
+  if (power2 > 0.0f) return false;
+  const float G = ex2_approx(power2);
+  const float alpha = fminf(0.99f, cf.w * G);
   if (alpha < (1.0f / 255.0f)) return false;
-  const float oma = fmaxf(1.0f - alpha, 1.0e-5f);
-  const float inv_oma = fast_rcp(oma);
+  // alpha <= 0.99, so 1 - alpha >= 0.01 (the reference's 1e-5 floor never binds)
+  const float inv_oma = fast_rcp(1.0f - alpha);
   s.T = s.T * inv_oma;
   const float dchannel = alpha * s.T;
-  s.ar0 = s.la * s.lc0 + (1.0f - s.la) * s.ar0;
-  s.ar1 = s.la * s.lc1 + (1.0f - s.la) * s.ar1;
-  s.ar2 = s.la * s.lc2 + (1.0f - s.la) * s.ar2;
-  s.lc0 = cd.x;
-  s.lc1 = cd.y;
-  s.lc2 = cd.z;
-  float dL_dopa = (cd.x - s.ar0) * s.g0 + (cd.y - s.ar1) * s.g1 + (cd.z - s.ar2) * s.g2;
-  v[7] += dchannel * s.g0;
-  v[8] += dchannel * s.g1;
-  v[9] += dchannel * s.g2;
+  const float cg = cd.x * s.g0 + cd.y * s.g1 + cd.z * s.g2;
+  s.S = __fmaf_rn(s.la, s.lcg - s.S, s.S);
+  s.lcg = cg;
+  float dL_dopa = cg - s.S;
+  m.dcol0 += dchannel * s.g0;
+  m.dcol1 += dchannel * s.g1;
+  m.dcol2 += dchannel * s.g2;
   if (DEPTH) {
-    s.adr = s.la * s.ld + (1.0f - s.la) * s.adr;
+    s.adr = __fmaf_rn(s.la, s.ld - s.adr, s.adr);
     s.ld = cd.w;
     dL_dopa += (cd.w - s.adr) * s.gd;
-    v[2] += dchannel * s.gd;
+    m.ddepth += dchannel * s.gd;
   }
-  s.aar = s.la + (1.0f - s.la) * s.aar;
-  dL_dopa += (1.0f - s.aar) * s.ga;
+  if (GA) {
+    s.aar = s.la + (1.0f - s.la) * s.aar;
+    dL_dopa += (1.0f - s.aar) * s.ga;
+  }
   dL_dopa *= s.T;
   s.la = alpha;
-  dL_dopa += (-s.T_final * inv_oma) * s.bg_dot;
-  const float dL_dG = co.w * dL_dopa;
-  const float gdx = G * dx, gdy = G * dy;
-  const float dG_ddelx = -gdx * co.x - gdy * co.y;
-  const float dG_ddely = -gdy * co.z - gdx * co.y;
-  v[0] += dL_dG * dG_ddelx * ddelx_dx;
-  v[1] += dL_dG * dG_ddely * ddely_dy;
-  v[3] += -0.5f * gdx * dx * dL_dG;
-  v[4] += -0.5f * gdx * dy * dL_dG;
-  v[5] += -0.5f * gdy * dy * dL_dG;
-  v[6] += G * dL_dopa;
+  if (has_bg) dL_dopa += (-s.T_final * inv_oma) * s.bg_dot;
+  const float u = G * dL_dopa;
+  const float uy = u * dy;
+  m.U += u;
+  m.UY += uy;
+  m.UYY = __fmaf_rn(uy, dy, m.UYY);
   return true;
 }
 
-template <bool DEPTH>
+// DEPTH: compute_depth with a depth gradient given; GA: an alpha gradient
+// given.  Without them those terms are exactly zero and are not evaluated.
+template <bool DEPTH, bool GA>
 __global__ void __launch_bounds__(THREADS) render_bwd_kernel(const gsb_render_bwd_args a, int gx) {
   __shared__ int s_id[BATCH];
   __shared__ float2 s_xy[BATCH];
-  __shared__ float4 s_cop[BATCH];
+  __shared__ float4 s_cf[BATCH];    // power coefficients, opacity in .w
+  __shared__ float4 s_con[BATCH];   // conic a, b, c
   __shared__ float4 s_rgbd[BATCH];
   __shared__ float4 s_box[BATCH];
+  __shared__ float4 s_el[BATCH];
   __shared__ int s_max[THREADS / 32];
   const int tile = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -285,6 +367,7 @@ __global__ void __launch_bounds__(THREADS) render_bwd_kernel(const gsb_render_bw
   const int n = range.y - range.x;
   const float4* rec = reinterpret_cast<const float4*>(a.records);
   const long long npix = (long long)a.W * a.H;
+  const bool has_bg = a.background[0] != 0.0f || a.background[1] != 0.0f || a.background[2] != 0.0f;
 
   BwdPixel px[2];
 #pragma unroll
@@ -301,12 +384,12 @@ __global__ void __launch_bounds__(THREADS) render_bwd_kernel(const gsb_render_bw
       s.g0 = a.grad_color[pix];
       s.g1 = a.grad_color[npix + pix];
       s.g2 = a.grad_color[2 * npix + pix];
-      if (DEPTH && a.grad_depth) s.gd = a.grad_depth[pix];
-      if (a.grad_alpha) s.ga = a.grad_alpha[pix];
+      if (DEPTH) s.gd = a.grad_depth[pix];
+      if (GA) s.ga = a.grad_alpha[pix];
       s.bg_dot = a.background[0] * s.g0 + a.background[1] * s.g1 + a.background[2] * s.g2;
     }
     s.T = s.T_final;
-    s.ar0 = s.ar1 = s.ar2 = s.adr = s.aar = s.la = s.lc0 = s.lc1 = s.lc2 = s.ld = 0.0f;
+    s.S = s.lcg = s.adr = s.aar = s.la = s.ld = 0.0f;
   }
   const int warp_max = __reduce_max_sync(FULL, max(px[0].lc, px[1].lc));
   if (lane == 0) s_max[warp] = warp_max;
@@ -317,8 +400,8 @@ __global__ void __launch_bounds__(THREADS) render_bwd_kernel(const gsb_render_bw
   cta_max = min(cta_max, n);  // n_contrib never exceeds the tile's list
   if (cta_max <= 0) return;
 
-  const float ddelx_dx = 0.5f * (float)a.W;
-  const float ddely_dy = 0.5f * (float)a.H;
+  const float half_w = 0.5f * (float)a.W;
+  const float half_h = 0.5f * (float)a.H;
   const float fx = (float)pxi;
   const float bx0 = (float)(__shfl_sync(FULL, pxi, 0)), by0 = (float)(__shfl_sync(FULL, py0, 0));
   const float bx1 = bx0 + 7.0f, by1 = by0 + 7.0f;
@@ -333,9 +416,13 @@ __global__ void __launch_bounds__(THREADS) render_bwd_kernel(const gsb_render_bw
       const float4 q2 = __ldg(rec + (size_t)id * 3 + 2);
       s_id[k] = id;
       s_xy[k] = make_float2(q0.x, q0.y);
-      s_cop[k] = make_float4(q0.z, q0.w, q1.x, q1.y);
+      float4 cf = power_coefs(q0.z, q0.w, q1.x);
+      cf.w = q1.y;
+      s_cf[k] = cf;
+      s_con[k] = make_float4(q0.z, q0.w, q1.x, 0.0f);
       s_rgbd[k] = make_float4(q2.x, q2.y, q2.z, q1.z);
       s_box[k] = alpha_box(q0.x, q0.y, q0.z, q0.w, q1.x, q1.y);
+      s_el[k] = cull_ellipse(q0.z, q0.w, q1.x, q1.y);
     }
     __syncthreads();
     const int top = min(hi, warp_max);
@@ -343,30 +430,53 @@ __global__ void __launch_bounds__(THREADS) render_bwd_kernel(const gsb_render_bw
     // visits only the hits below its own maximum, back to front.
     for (int cb = ((top - lo - 1) >> 5) << 5; cb >= 0 && top > lo; cb -= 32) {
       const int g = cb + lane;
-      unsigned hits = __ballot_sync(FULL, g < top - lo && box_hits(s_box[g], bx0, bx1, by0, by1));
+      bool hit = g < top - lo && box_hits(s_box[g], bx0, bx1, by0, by1);
+      if (__any_sync(FULL, hit) && hit) {
+        const float2 cxy = s_xy[g];
+        hit = ellipse_hits(cxy.x, cxy.y, s_el[g], bx0, bx1, by0, by1);
+      }
+      unsigned hits = __ballot_sync(FULL, hit);
       while (hits) {
       const int j = cb + 31 - __clz(hits);
       hits &= ~(1u << (j - cb));
       const int pos = lo + j;
-      float v[10];
-#pragma unroll
-      for (int k = 0; k < 10; ++k) v[k] = 0.0f;
+      BwdSums m = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
       bool contrib = false;
+      float dx = 0.0f;
       if (pos < px[0].lc || pos < px[1].lc) {
         const float2 xy = s_xy[j];
-        const float4 co = s_cop[j];
+        const float4 cf = s_cf[j];
         const float4 cd = s_rgbd[j];
-        const float dx = xy.x - fx;
-        const float adx2 = co.x * dx * dx;
-        if (pos < px[0].lc) contrib |= bwd_pixel<DEPTH>(px[0], dx, adx2, xy, co, cd, ddelx_dx, ddely_dy, v);
-        if (pos < px[1].lc) contrib |= bwd_pixel<DEPTH>(px[1], dx, adx2, xy, co, cd, ddelx_dx, ddely_dy, v);
+        dx = xy.x - fx;
+        float ax, bx;
+        column_terms(cf, dx, ax, bx);
+        if (pos < px[0].lc) contrib |= bwd_pixel<DEPTH, GA>(px[0], cf, ax, bx, xy.y, cd, has_bg, m);
+        if (pos < px[1].lc) contrib |= bwd_pixel<DEPTH, GA>(px[1], cf, ax, bx, xy.y, cd, has_bg, m);
       }
       if (__any_sync(FULL, contrib)) {
+        const float4 con = s_con[j];
+        const float dxU = dx * m.U;
+        float v[10];
+        v[0] = con.x * dxU + con.y * m.UY;   // x: times -op W/2
+        v[1] = con.z * m.UY + con.y * dxU;   // y: times -op H/2
+        v[2] = m.ddepth;
+        v[3] = dx * dxU;                     // conic a: times -op/2
+        v[4] = dx * m.UY;                    // conic b: times -op/2
+        v[5] = m.UYY;                        // conic c: times -op/2
+        v[6] = m.U;                          // opacity
+        v[7] = m.dcol0;
+        v[8] = m.dcol1;
+        v[9] = m.dcol2;
         float sum;
         const int slot = warp_reduce10(v, sum);
         if (!(lane & 1) && slot >= 0) {
+          const float op = s_cf[j].w;
+          float scale = 1.0f;
+          if (slot == 0) scale = -op * half_w;
+          else if (slot == 1) scale = -op * half_h;
+          else if (slot >= 3 && slot <= 5) scale = -0.5f * op;
           const int off = slot < 3 ? slot : slot + 1;
-          atomicAdd(a.grad_acc + (size_t)s_id[j] * GSB_GRAD_FLOATS + off, sum);
+          if (DEPTH || slot != 2) atomicAdd(a.grad_acc + (size_t)s_id[j] * GSB_GRAD_FLOATS + off, sum * scale);
         }
       }
       }
@@ -403,9 +513,16 @@ GSB_EXPORT int gsb_render_bwd(const gsb_render_bwd_args* a, void* stream) {
   if (a->P == 0) return GSB_OK;
   const int gx = div_up(a->W, BLOCK_X), gy = div_up(a->H, BLOCK_Y);
   cudaStream_t s = (cudaStream_t)stream;
-  if (a->compute_depth)
-    render_bwd_kernel<true><<<gx * gy, THREADS, 0, s>>>(*a, gx);
+  const bool depth = a->compute_depth && a->grad_depth;
+  const bool ga = a->grad_alpha != nullptr;
+  const int blocks = gx * gy;
+  if (depth && ga)
+    render_bwd_kernel<true, true><<<blocks, THREADS, 0, s>>>(*a, gx);
+  else if (depth)
+    render_bwd_kernel<true, false><<<blocks, THREADS, 0, s>>>(*a, gx);
+  else if (ga)
+    render_bwd_kernel<false, true><<<blocks, THREADS, 0, s>>>(*a, gx);
   else
-    render_bwd_kernel<false><<<gx * gy, THREADS, 0, s>>>(*a, gx);
+    render_bwd_kernel<false, false><<<blocks, THREADS, 0, s>>>(*a, gx);
   return check_launch("render_bwd_kernel");
 }

@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define GSB_ABI_VERSION 3
+#define GSB_ABI_VERSION 4
 
 #define GSB_OK 0
 #define GSB_ERR_INVALID (-1)  /* bad argument: ValueError in Python          */
@@ -90,6 +90,10 @@ typedef struct {
   float* records;       /* (P,12) render records */
   float* cov3d_out;     /* (P,6) 3D covariance of the scale/rotation path, or NULL
                            (only the packed raw-compat geometry buffer needs it) */
+  float* bin_records;   /* (P,8) 16-byte aligned, or NULL: per Gaussian with tiles, the
+                           centre, conic, opacity threshold and clipped tile rect the
+                           binning emit needs (written only where tiles_touched > 0;
+                           needs both tile-grid dimensions below 65536) */
 } gsb_preprocess_args;
 
 int gsb_preprocess_fwd(const gsb_preprocess_args* a, void* stream);
@@ -141,6 +145,9 @@ typedef struct {
   long long* error_word;       /* device word; OR-ed with error bits */
   void* workspace;
   size_t workspace_bytes;
+  const float* bin_records;    /* (P,8) from gsb_preprocess_fwd, or NULL: with it the emit
+                                  reads one 32-byte record per Gaussian (radii, records,
+                                  conic_2d_inv and tiles_touched are then not read) */
 } gsb_bin_sort_args;
 
 size_t gsb_bin_sort_workspace_bytes(long long num_rendered, int W, int H);

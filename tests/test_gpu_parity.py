@@ -98,12 +98,18 @@ def test_preprocess_and_binning_bit_exact(cuda, name, mode):
     np.testing.assert_array_equal(clamp_bits[vis], ref_bits[vis])
     assert vis.sum() > 0 and ref["tiles_touched"].sum() > 0
 
-    binned = pl.binning(pre, cam, mode)
-    torch.cuda.synchronize()
+    assert pre.bin_records is not None
     ref_pl, ref_ranges, _ = oracle.binning(ref, view.width, view.height, mode)
-    assert binned.num_rendered == len(ref_pl)
-    np.testing.assert_array_equal(_np(binned.point_list), ref_pl)
-    np.testing.assert_array_equal(_np(binned.ranges), ref_ranges)
+    # emit from the preprocess binning records, then from the gathered
+    # per-Gaussian arrays (no binning records): both bit-exact
+    for use_binrec in (True, False):
+        if not use_binrec:
+            pre.bin_records = None
+        binned = pl.binning(pre, cam, mode)
+        torch.cuda.synchronize()
+        assert binned.num_rendered == len(ref_pl)
+        np.testing.assert_array_equal(_np(binned.point_list), ref_pl)
+        np.testing.assert_array_equal(_np(binned.ranges), ref_ranges)
 
 
 def _render_case(name, dev):
