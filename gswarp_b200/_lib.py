@@ -24,7 +24,7 @@ GSB_ERR_OVERFLOW = -2
 GSB_ERR_CUDA = -3
 GSB_ERR_TIMEOUT = -4
 
-ABI_VERSION = 4
+ABI_VERSION = 5
 RECORD_FLOATS = 12
 GRAD_FLOATS = 12
 
@@ -67,6 +67,7 @@ class BinSortArgs(ctypes.Structure):
         ("conic_2d_inv", vp), ("tiles_touched", vp),
         ("point_list", vp), ("ranges", vp), ("error_word", vp),
         ("workspace", vp), ("workspace_bytes", ctypes.c_size_t), ("bin_records", vp),
+        ("bin_status", vp),
     ]
 
 

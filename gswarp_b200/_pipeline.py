@@ -249,7 +249,7 @@ def binning(pre: Preprocessed, cam: Camera, coverage_mode: int) -> Binned:
         return Binned(0, torch.empty(0, dtype=torch.int32, device=dev), ranges)
     depth_order = torch.empty(P, dtype=torch.int32, device=dev)
     offsets = torch.empty(P, dtype=torch.int32, device=dev)
-    status = torch.empty(2, dtype=torch.int64, device=dev)
+    status = torch.empty(3, dtype=torch.int64, device=dev)
     ws_bytes = int(L.gsb_bin_count_workspace_bytes(P))
     ws = _workspace(ws_bytes, dev)
     a = _lib.BinCountArgs()
@@ -262,10 +262,10 @@ def binning(pre: Preprocessed, cam: Camera, coverage_mode: int) -> Binned:
     a.status_out = _lib.ptr(status)
     a.workspace = _lib.ptr(ws)
     a.workspace_bytes = ws_bytes
-    with _stage_timer("bin_count", {"P": P, "kernels": 11}):
+    with _stage_timer("bin_count", {"P": P, "kernels": 12}):
         _lib.call("gsb_bin_count", a, stream)
     sticky = sticky_error_word(dev)
-    total, err, sticky_bits = torch.cat([status, sticky]).tolist()
+    total, err, _, sticky_bits = torch.cat([status, sticky]).tolist()
     if err or sticky_bits:
         sticky.zero_()
         raise RuntimeError(f"gswarp_b200 device error word {int(err) | int(sticky_bits):#x} (bounded wait timed out or binning mismatch)")
@@ -293,6 +293,7 @@ def binning(pre: Preprocessed, cam: Camera, coverage_mode: int) -> Binned:
     b.workspace = _lib.ptr(ws2)
     b.workspace_bytes = ws2.numel()
     b.bin_records = _lib.ptr(pre.bin_records)
+    b.bin_status = _lib.ptr(status)
     with _stage_timer("bin_emit_sort", {"P": P, "num_rendered": R, "kernels": 7}):
         _lib.call("gsb_bin_emit_sort", b, stream)
     return Binned(R, point_list[:R], ranges)

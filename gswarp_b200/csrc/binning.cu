@@ -28,20 +28,68 @@ constexpr int SCAN_THREADS = 256;
 constexpr int SCAN_ITEMS = 16;
 constexpr int SCAN_TILE = SCAN_THREADS * SCAN_ITEMS;  // 4096
 
-__global__ void depth_keys_kernel(int P, const float* __restrict__ depths,
-                                  const int* __restrict__ radii, unsigned* __restrict__ keys,
-                                  unsigned* __restrict__ vals) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= P) return;
-  keys[i] = radii[i] > 0 ? __float_as_uint(depths[i]) : 0xFFFFFFFFu;
-  vals[i] = (unsigned)i;
+// Per 4096-Gaussian block: how many have tiles (tiles_touched > 0).
+__global__ void __launch_bounds__(SCAN_THREADS) vis_count_kernel(int P, const int* __restrict__ tiles_touched,
+                                                                 long long* __restrict__ block_sums) {
+  __shared__ int s[SCAN_THREADS / 32];
+  const long long base = (long long)blockIdx.x * SCAN_TILE;
+  int acc = 0;
+#pragma unroll
+  for (int i = 0; i < SCAN_ITEMS; ++i) {
+    const long long r = base + i * SCAN_THREADS + threadIdx.x;
+    if (r < P) acc += tiles_touched[r] > 0;
+  }
+  acc = __reduce_add_sync(0xffffffffu, acc);
+  if ((threadIdx.x & 31) == 0) s[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    long long t = 0;
+    for (int w = 0; w < SCAN_THREADS / 32; ++w) t += s[w];
+    block_sums[blockIdx.x] = t;
+  }
+}
+
+// Order-preserving compaction of the Gaussians with tiles: keys = depth
+// float bits, vals = point index, in index order (so the stable depth sort
+// breaks depth ties by index).  block_prefix = exclusive block offsets.
+__global__ void __launch_bounds__(SCAN_THREADS) vis_compact_kernel(
+    int P, const float* __restrict__ depths, const int* __restrict__ tiles_touched,
+    const long long* __restrict__ block_prefix, unsigned* __restrict__ keys, unsigned* __restrict__ vals) {
+  __shared__ int s_warp[SCAN_THREADS / 32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const long long base = (long long)blockIdx.x * SCAN_TILE;
+  // Chunk i covers SCAN_THREADS consecutive indices; warps take them in order.
+  long long out = block_prefix[blockIdx.x];
+#pragma unroll 1
+  for (int i = 0; i < SCAN_ITEMS; ++i) {
+    const long long r = base + i * SCAN_THREADS + threadIdx.x;
+    const bool keep = r < P && tiles_touched[r] > 0;
+    const unsigned m = __ballot_sync(0xffffffffu, keep);
+    if (lane == 0) s_warp[warp] = __popc(m);
+    __syncthreads();
+    int before = 0, total = 0;
+#pragma unroll
+    for (int w = 0; w < SCAN_THREADS / 32; ++w) {
+      const int c = s_warp[w];
+      before += w < warp ? c : 0;
+      total += c;
+    }
+    if (keep) {
+      const long long o = out + before + __popc(m & lanemask_lt());
+      keys[o] = __float_as_uint(depths[r]);
+      vals[o] = (unsigned)r;
+    }
+    out += total;
+    __syncthreads();
+  }
 }
 
 // Block sums (int64) of tiles_touched gathered in depth order.
 __global__ void __launch_bounds__(SCAN_THREADS) scan_reduce_kernel(
-    int P, const int* __restrict__ order, const int* __restrict__ tiles_touched,
+    const int* __restrict__ n_dev, const int* __restrict__ order, const int* __restrict__ tiles_touched,
     long long* __restrict__ block_sums) {
   __shared__ long long s[SCAN_THREADS / 32];
+  const int P = *n_dev;
   const long long base = (long long)blockIdx.x * SCAN_TILE;
   long long acc = 0;
 #pragma unroll
@@ -60,10 +108,12 @@ __global__ void __launch_bounds__(SCAN_THREADS) scan_reduce_kernel(
   }
 }
 
-// Exclusive scan of the block sums in one CTA; writes the pair total.
+// Exclusive scan of the block sums in one CTA; writes the total (and, if
+// total_int is given, the total as an int for device-side counts).
 __global__ void __launch_bounds__(1024) scan_blocks_kernel(int nblocks,
                                                            long long* __restrict__ block_sums,
-                                                           long long* __restrict__ status_out) {
+                                                           long long* __restrict__ status_out,
+                                                           int* __restrict__ total_int) {
   __shared__ long long s_carry;
   __shared__ long long s_warp[32];
   if (threadIdx.x == 0) s_carry = 0;
@@ -91,14 +141,19 @@ __global__ void __launch_bounds__(1024) scan_blocks_kernel(int nblocks,
     if (threadIdx.x == 0) s_carry += tot;
     __syncthreads();
   }
-  if (threadIdx.x == 0) status_out[0] = s_carry;
+  if (threadIdx.x == 0) {
+    status_out[0] = s_carry;
+    if (total_int) *total_int = (int)s_carry;
+  }
 }
 
 // Inclusive scan in depth order: offsets[r] = sum_{q<=r} tiles[order[q]].
 __global__ void __launch_bounds__(SCAN_THREADS) scan_downsweep_kernel(
-    int P, const int* __restrict__ order, const int* __restrict__ tiles_touched,
+    const int* __restrict__ n_dev, const int* __restrict__ order, const int* __restrict__ tiles_touched,
     const long long* __restrict__ block_prefix, int* __restrict__ offsets) {
   __shared__ long long s_warp[SCAN_THREADS / 32];
+  const int P = *n_dev;
+  if ((long long)blockIdx.x * SCAN_TILE >= P) return;
   const long long base = (long long)blockIdx.x * SCAN_TILE;
   // Thread t owns the SCAN_ITEMS consecutive ranks [base + t*ITEMS, ...).
   long long v[SCAN_ITEMS];
@@ -149,11 +204,11 @@ struct EmitPairs {
 // 32-byte read per Gaussian; the pair count is the difference of adjacent
 // inclusive offsets (both coalesced).
 __global__ void __launch_bounds__(256) emit_binrec_kernel(
-    int P, int gx, int mode, const int* __restrict__ order, const int* __restrict__ offsets,
-    const float4* __restrict__ bin_records, unsigned* __restrict__ keys, unsigned* __restrict__ vals,
-    long long* __restrict__ err) {
+    const long long* __restrict__ n_dev, int gx, int mode, const int* __restrict__ order,
+    const int* __restrict__ offsets, const float4* __restrict__ bin_records, unsigned* __restrict__ keys,
+    unsigned* __restrict__ vals, long long* __restrict__ err) {
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
-  if (r >= P) return;
+  if (r >= *n_dev) return;
   const int end = offsets[r];
   const int n = end - (r > 0 ? offsets[r - 1] : 0);
   if (n <= 0) return;
@@ -167,13 +222,13 @@ __global__ void __launch_bounds__(256) emit_binrec_kernel(
 }
 
 __global__ void __launch_bounds__(256) emit_kernel(
-    int P, int gx, int gy, int mode, const int* __restrict__ order,
+    const long long* __restrict__ n_dev, int gx, int gy, int mode, const int* __restrict__ order,
     const int* __restrict__ offsets, const int* __restrict__ tiles_touched,
     const int* __restrict__ radii, const float4* __restrict__ records,
     const float* __restrict__ conic_2d_inv, unsigned* __restrict__ keys,
     unsigned* __restrict__ vals, long long* __restrict__ err) {
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
-  if (r >= P) return;
+  if (r >= *n_dev) return;
   const int p = order[r];
   const int n = tiles_touched[p];
   if (n <= 0) return;
@@ -222,6 +277,7 @@ GSB_EXPORT size_t gsb_bin_count_workspace_bytes(int P) {
   size_t b = 0;
   b += align256(n * 4) * 3;  // keys, keys_alt, vals_alt
   b += align256((size_t)div_up((long long)n, SCAN_TILE) * 8);
+  b += 256;                  // device count of Gaussians with tiles
   b += radix::scratch_bytes((long long)n, 4);
   return b + 256;
 }
@@ -237,7 +293,7 @@ GSB_EXPORT int gsb_bin_count(const gsb_bin_count_args* a, void* stream) {
     return GSB_ERR_INVALID;
   }
   if (a->P == 0) {
-    cudaMemsetAsync(a->status_out, 0, 2 * sizeof(long long), s);
+    cudaMemsetAsync(a->status_out, 0, 3 * sizeof(long long), s);
     return check_launch("gsb_bin_count(empty)");
   }
   if (!a->depths || !a->radii || !a->tiles_touched || !a->depth_order || !a->point_offsets ||
@@ -256,22 +312,29 @@ GSB_EXPORT int gsb_bin_count(const gsb_bin_count_args* a, void* stream) {
   const int nblocks = div_up(P, SCAN_TILE);
   long long* block_sums = (long long*)w;
   w += align256((size_t)nblocks * 8);
+  int* n_vis = (int*)w;
+  w += 256;
   void* sort_scratch = w;
 
   long long* err = a->status_out + 1;
   cudaMemsetAsync(err, 0, sizeof(long long), s);
+  // 1. order-preserving compaction of the Gaussians with tiles (count V into
+  //    status_out[2] and n_vis); only they take part in the depth sort.
   unsigned* vals0 = (unsigned*)a->depth_order;
-  depth_keys_kernel<<<div_up(P, 256), 256, 0, s>>>(P, a->depths, a->radii, keys, vals0);
+  vis_count_kernel<<<nblocks, SCAN_THREADS, 0, s>>>(P, a->tiles_touched, block_sums);
+  scan_blocks_kernel<<<1, 1024, 0, s>>>(nblocks, block_sums, a->status_out + 2, n_vis);
+  vis_compact_kernel<<<nblocks, SCAN_THREADS, 0, s>>>(P, a->depths, a->tiles_touched, block_sums, keys, vals0);
+  // 2. stable sort of the V (depth bits, index) pairs.
   unsigned* kb[2] = {keys, keys_alt};
   unsigned* vb[2] = {vals0, vals_alt};
-  const int where = radix::sort_pairs(kb, vb, P, 4, sort_scratch, err, s);
+  const int where = radix::sort_pairs(kb, vb, P, n_vis, 4, sort_scratch, err, s);
   if (where != 0) {  // 4 passes always end in buffer 0; kept for safety
     cudaMemcpyAsync(a->depth_order, vals_alt, (size_t)P * 4, cudaMemcpyDeviceToDevice, s);
   }
-  scan_reduce_kernel<<<nblocks, SCAN_THREADS, 0, s>>>(P, a->depth_order, a->tiles_touched,
-                                                      block_sums);
-  scan_blocks_kernel<<<1, 1024, 0, s>>>(nblocks, block_sums, a->status_out);
-  scan_downsweep_kernel<<<nblocks, SCAN_THREADS, 0, s>>>(P, a->depth_order, a->tiles_touched,
+  // 3. inclusive scan of tiles_touched in depth order; pair total -> status_out[0].
+  scan_reduce_kernel<<<nblocks, SCAN_THREADS, 0, s>>>(n_vis, a->depth_order, a->tiles_touched, block_sums);
+  scan_blocks_kernel<<<1, 1024, 0, s>>>(nblocks, block_sums, a->status_out, nullptr);
+  scan_downsweep_kernel<<<nblocks, SCAN_THREADS, 0, s>>>(n_vis, a->depth_order, a->tiles_touched,
                                                          block_sums, a->point_offsets);
   return check_launch("gsb_bin_count");
 }
@@ -293,8 +356,8 @@ GSB_EXPORT int gsb_bin_emit_sort(const gsb_bin_sort_args* a, void* stream) {
   cudaStream_t s = (cudaStream_t)stream;
   const int gx = div_up(a->W, BLOCK_X), gy = div_up(a->H, BLOCK_Y);
   const int tiles = gx * gy;
-  if (!a->ranges || !a->error_word) {
-    set_error("gsb_bin_emit_sort: ranges and error_word are required");
+  if (!a->ranges || !a->error_word || !a->bin_status) {
+    set_error("gsb_bin_emit_sort: ranges, error_word and bin_status are required");
     return GSB_ERR_INVALID;
   }
   cudaMemsetAsync(a->ranges, 0, (size_t)tiles * 2 * sizeof(int), s);
@@ -335,13 +398,13 @@ GSB_EXPORT int gsb_bin_emit_sort(const gsb_bin_sort_args* a, void* stream) {
   }
   if (binrec)
     emit_binrec_kernel<<<div_up(a->P, 256), 256, 0, s>>>(
-        a->P, gx, a->coverage_mode, a->depth_order, a->point_offsets,
+        a->bin_status + 2, gx, a->coverage_mode, a->depth_order, a->point_offsets,
         reinterpret_cast<const float4*>(a->bin_records), kb[0], vb[0], a->error_word);
   else
     emit_kernel<<<div_up(a->P, 256), 256, 0, s>>>(
-        a->P, gx, gy, a->coverage_mode, a->depth_order, a->point_offsets, a->tiles_touched, a->radii,
+        a->bin_status + 2, gx, gy, a->coverage_mode, a->depth_order, a->point_offsets, a->tiles_touched, a->radii,
         reinterpret_cast<const float4*>(a->records), a->conic_2d_inv, kb[0], vb[0], a->error_word);
-  const int where = radix::sort_pairs(kb, vb, R, passes, sort_scratch, a->error_word, s);
+  const int where = radix::sort_pairs(kb, vb, R, nullptr, passes, sort_scratch, a->error_word, s);
   ranges_kernel<<<div_up(R, 256), 256, 0, s>>>(R, kb[where], a->ranges);
   return check_launch("gsb_bin_emit_sort");
 }

@@ -289,7 +289,7 @@ GSB_EXPORT int gsb_knn(const gsb_knn_args* a, void* stream) {
   morton_kernel<<<div_up(P, 256), 256, 0, s>>>(P, a->points, bounds, codes, idx);
   unsigned* kb[2] = {codes, codes_alt};
   unsigned* vb[2] = {idx, idx_alt};
-  const int where = radix::sort_pairs(kb, vb, P, 4, scratch, a->error_word, s);
+  const int where = radix::sort_pairs(kb, vb, P, nullptr, 4, scratch, a->error_word, s);
   const unsigned* order = vb[where];
   gather_box_kernel<<<nb, 256, 0, s>>>(P, a->points, order, sx, sy, sz, boxes);
   const size_t smem = (size_t)nb * 6 * 4;

@@ -92,8 +92,9 @@ __device__ __forceinline__ unsigned block_exclusive_scan(unsigned v, unsigned* s
 // enough that this beats aggregating peers first), HIST_ITEMS keys per lane
 // loaded before any is counted.
 __global__ void __launch_bounds__(THREADS) histogram_kernel(const unsigned* __restrict__ keys,
-                                                            int n, int passes,
-                                                            unsigned* __restrict__ hist) {
+                                                            int n_host, const int* __restrict__ n_dev,
+                                                            int passes, unsigned* __restrict__ hist) {
+  const int n = n_dev ? *n_dev : n_host;
   __shared__ unsigned s_hist[WARPS][MAX_PASSES][RADIX];
   for (int i = threadIdx.x; i < WARPS * MAX_PASSES * RADIX; i += THREADS) (&s_hist[0][0][0])[i] = 0u;
   __syncthreads();
@@ -135,7 +136,8 @@ __global__ void __launch_bounds__(THREADS) bin_base_kernel(const unsigned* __res
 template <bool HAS_VALS>
 __global__ void __launch_bounds__(THREADS, 4) onesweep_kernel(
     const unsigned* __restrict__ keys_in, const unsigned* __restrict__ vals_in,
-    unsigned* __restrict__ keys_out, unsigned* __restrict__ vals_out, int n, int shift,
+    unsigned* __restrict__ keys_out, unsigned* __restrict__ vals_out, int n_host,
+    const int* __restrict__ n_dev, int shift,
     const unsigned* __restrict__ bin_base, unsigned long long* __restrict__ lookback,
     unsigned* __restrict__ tile_counter, long long* __restrict__ err) {
   __shared__ unsigned s_keys[TILE_KEYS];
@@ -147,10 +149,14 @@ __global__ void __launch_bounds__(THREADS, 4) onesweep_kernel(
   __shared__ int s_tile;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // With a device-side count the grid is sized for the upper bound; CTAs
+  // that claim a tile past the end leave (no later tile waits on them).
+  const int n = n_dev ? *n_dev : n_host;
   if (tid == 0) s_tile = (int)atomicAdd(tile_counter, 1u);
   for (int i = tid; i < WARPS * RADIX; i += THREADS) (&s_warp_hist[0][0])[i] = 0u;
   __syncthreads();
   const int tile = s_tile;
+  if ((long long)tile * TILE_KEYS >= n) return;
   const long long base = (long long)tile * TILE_KEYS + (long long)warp * (ITEMS * 32);
 
   unsigned key[ITEMS], rank[ITEMS];
@@ -310,14 +316,15 @@ __host__ inline SortScratch carve_scratch(void* base, long long n, int passes) {
 // Sorts n pairs by the low `passes*8` key bits.  Buffers ping-pong:
 // pass 0 reads (k[0],v[0]) and writes (k[1],v[1]), pass 1 the reverse, ...
 // Returns the index (0/1) of the buffer pair that holds the result.
-// vals may be null (keys only).
-__host__ inline int sort_pairs(unsigned* k[2], unsigned* v[2], long long n, int passes,
+// vals may be null (keys only).  With n_dev non-null the count is read on
+// the device (at most n, which sizes the grids and the scratch).
+__host__ inline int sort_pairs(unsigned* k[2], unsigned* v[2], long long n, const int* n_dev, int passes,
                                void* scratch, long long* err, cudaStream_t stream) {
-  if (n <= 1 || passes == 0) return 0;
+  if ((n <= 1 && !n_dev) || n <= 0 || passes == 0) return 0;
   SortScratch s = carve_scratch(scratch, n, passes);
   cudaMemsetAsync(s.hist, 0, s.zero_bytes, stream);
   const int hist_blocks = (int)std::min<long long>(148 * 4, (n + THREADS * 8 - 1) / (THREADS * 8));
-  histogram_kernel<<<std::max(hist_blocks, 1), THREADS, 0, stream>>>(k[0], (int)n, passes, s.hist);
+  histogram_kernel<<<std::max(hist_blocks, 1), THREADS, 0, stream>>>(k[0], (int)n, n_dev, passes, s.hist);
   bin_base_kernel<<<passes, THREADS, 0, stream>>>(s.hist, s.bin_base);
   const int tiles = num_tiles(n);
   int cur = 0;
@@ -325,11 +332,11 @@ __host__ inline int sort_pairs(unsigned* k[2], unsigned* v[2], long long n, int 
     unsigned long long* lb = s.lookback + (size_t)p * tiles * RADIX;
     if (v[0]) {
       onesweep_kernel<true><<<tiles, THREADS, 0, stream>>>(
-          k[cur], v[cur], k[cur ^ 1], v[cur ^ 1], (int)n, p * RADIX_BITS, s.bin_base + p * RADIX,
+          k[cur], v[cur], k[cur ^ 1], v[cur ^ 1], (int)n, n_dev, p * RADIX_BITS, s.bin_base + p * RADIX,
           lb, s.counters + p, err);
     } else {
       onesweep_kernel<false><<<tiles, THREADS, 0, stream>>>(
-          k[cur], nullptr, k[cur ^ 1], nullptr, (int)n, p * RADIX_BITS, s.bin_base + p * RADIX,
+          k[cur], nullptr, k[cur ^ 1], nullptr, (int)n, n_dev, p * RADIX_BITS, s.bin_base + p * RADIX,
           lb, s.counters + p, err);
     }
     cur ^= 1;

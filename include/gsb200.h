@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define GSB_ABI_VERSION 4
+#define GSB_ABI_VERSION 5
 
 #define GSB_OK 0
 #define GSB_ERR_INVALID (-1)  /* bad argument: ValueError in Python          */
@@ -105,19 +105,19 @@ int gsb_mark_visible(int P, const float* means, const float* viewmatrix, uint8_t
 /* ------------------------------------------------------------------------ */
 /* Binning.  Replaces _build_binning_state (binning_ops.py:84-431) with two  */
 /* calls separated by one host read of the pair count.                       */
-/* gsb_bin_count: stable depth sort of all Gaussians (key = depth float     */
-/* bits, invisible Gaussians last), depth-ordered inclusive scan of         */
-/* tiles_touched (binning_ops.py:152-224) and the int64 pair total written  */
-/* to *status_out[0]; status_out[1] receives the device error word.         */
+/* gsb_bin_count: order-preserving compaction of the V Gaussians with      */
+/* tiles, stable sort of them by depth float bits (ties by index), depth-   */
+/* ordered inclusive scan of tiles_touched (binning_ops.py:152-224).        */
+/* status_out[0] = int64 pair total, [1] = device error word, [2] = V.       */
 /* ------------------------------------------------------------------------ */
 typedef struct {
   int P;
   const float* depths;        /* (P) */
   const int* radii;           /* (P) */
   const int* tiles_touched;   /* (P) */
-  int* depth_order;           /* out (P): point ids in depth order */
-  int* point_offsets;         /* out (P): inclusive scan in depth order */
-  long long* status_out;      /* out, device: [0]=pair total, [1]=error word */
+  int* depth_order;           /* out (P): first V entries = ids with tiles, in depth order */
+  int* point_offsets;         /* out (P): first V entries = inclusive scan in depth order */
+  long long* status_out;      /* out, device, 3 words: [0]=pair total, [1]=error word, [2]=V */
   void* workspace;
   size_t workspace_bytes;
 } gsb_bin_count_args;
@@ -148,6 +148,7 @@ typedef struct {
   const float* bin_records;    /* (P,8) from gsb_preprocess_fwd, or NULL: with it the emit
                                   reads one 32-byte record per Gaussian (radii, records,
                                   conic_2d_inv and tiles_touched are then not read) */
+  const long long* bin_status; /* status_out of gsb_bin_count (device; V is read from [2]) */
 } gsb_bin_sort_args;
 
 size_t gsb_bin_sort_workspace_bytes(long long num_rendered, int W, int H);
