@@ -24,7 +24,7 @@ GSB_ERR_OVERFLOW = -2
 GSB_ERR_CUDA = -3
 GSB_ERR_TIMEOUT = -4
 
-ABI_VERSION = 5
+ABI_VERSION = 6
 RECORD_FLOATS = 12
 GRAD_FLOATS = 12
 
@@ -53,7 +53,7 @@ class BinCountArgs(ctypes.Structure):
     _fields_ = [
         ("P", c_int),
         ("depths", vp), ("radii", vp), ("tiles_touched", vp),
-        ("depth_order", vp), ("point_offsets", vp), ("status_out", vp),
+        ("depth_order", vp), ("point_offsets", vp), ("binned_ids", vp), ("status_out", vp),
         ("workspace", vp), ("workspace_bytes", ctypes.c_size_t),
     ]
 
@@ -102,6 +102,7 @@ class PreprocessBwdArgs(ctypes.Structure):
         ("accumulate", c_int),
         ("grad_means3d", vp), ("grad_means2d", vp), ("grad_scales", vp), ("grad_rotations", vp),
         ("grad_opacity", vp), ("grad_sh", vp), ("grad_colors", vp), ("grad_cov3d", vp),
+        ("ids", vp), ("num_ids", c_int),
     ]
 
 

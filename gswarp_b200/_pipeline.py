@@ -135,6 +135,7 @@ class Binned:
     num_rendered: int
     point_list: torch.Tensor
     ranges: torch.Tensor
+    ids: torch.Tensor | None = None   # ascending ids of the Gaussians with tiles (if requested)
 
 
 @dataclass(slots=True)
@@ -236,7 +237,10 @@ def preprocess(g: Gaussians, cam: Camera, coverage_mode: int, want_cov3d: bool =
     return out
 
 
-def binning(pre: Preprocessed, cam: Camera, coverage_mode: int) -> Binned:
+def binning(pre: Preprocessed, cam: Camera, coverage_mode: int, want_ids: bool = False) -> Binned:
+    """Binning.  With ``want_ids`` the result also lists, in ascending order,
+    the Gaussians that touch at least one tile (the only ones the render
+    backward gives a gradient)."""
     P = pre.radii.shape[0]
     dev = pre.radii.device
     gx, gy = cam.grid
@@ -246,7 +250,8 @@ def binning(pre: Preprocessed, cam: Camera, coverage_mode: int) -> Binned:
     ranges = torch.empty((tiles, 2), dtype=torch.int32, device=dev)
     if P == 0:
         ranges.zero_()
-        return Binned(0, torch.empty(0, dtype=torch.int32, device=dev), ranges)
+        empty = torch.empty(0, dtype=torch.int32, device=dev)
+        return Binned(0, empty, ranges, empty if want_ids else None)
     depth_order = torch.empty(P, dtype=torch.int32, device=dev)
     offsets = torch.empty(P, dtype=torch.int32, device=dev)
     status = torch.empty(3, dtype=torch.int64, device=dev)
@@ -259,13 +264,15 @@ def binning(pre: Preprocessed, cam: Camera, coverage_mode: int) -> Binned:
     a.tiles_touched = _lib.ptr(pre.tiles_touched)
     a.depth_order = _lib.ptr(depth_order)
     a.point_offsets = _lib.ptr(offsets)
+    ids = torch.empty(P, dtype=torch.int32, device=dev) if want_ids else None
+    a.binned_ids = _lib.ptr(ids)
     a.status_out = _lib.ptr(status)
     a.workspace = _lib.ptr(ws)
     a.workspace_bytes = ws_bytes
     with _stage_timer("bin_count", {"P": P, "kernels": 12}):
         _lib.call("gsb_bin_count", a, stream)
     sticky = sticky_error_word(dev)
-    total, err, _, sticky_bits = torch.cat([status, sticky]).tolist()
+    total, err, num_binned, sticky_bits = torch.cat([status, sticky]).tolist()
     if err or sticky_bits:
         sticky.zero_()
         raise RuntimeError(f"gswarp_b200 device error word {int(err) | int(sticky_bits):#x} (bounded wait timed out or binning mismatch)")
@@ -296,7 +303,7 @@ def binning(pre: Preprocessed, cam: Camera, coverage_mode: int) -> Binned:
     b.bin_status = _lib.ptr(status)
     with _stage_timer("bin_emit_sort", {"P": P, "num_rendered": R, "kernels": 7}):
         _lib.call("gsb_bin_emit_sort", b, stream)
-    return Binned(R, point_list[:R], ranges)
+    return Binned(R, point_list[:R], ranges, ids[:int(num_binned)] if ids is not None else None)
 
 
 def render(pre: Preprocessed, binned: Binned, cam: Camera, background: torch.Tensor, compute_depth: bool) -> Rendered:
@@ -367,9 +374,14 @@ class PreprocessGrads:
 
 
 def preprocess_backward(g: Gaussians, cam: Camera, radii, records, grad_acc, grad_proj_2d, grad_conic_2d,
-                        grad_conic_2d_inv, out: PreprocessGrads | None = None) -> PreprocessGrads:
+                        grad_conic_2d_inv, out: PreprocessGrads | None = None,
+                        ids: torch.Tensor | None = None) -> PreprocessGrads:
     """Per-Gaussian backward.  With ``out`` given, gradients are added into
-    its buffers (multi-view accumulation); otherwise fresh tensors are made."""
+    its buffers (multi-view accumulation); otherwise fresh tensors are made.
+    ``ids`` (accumulate mode only) restricts the work to those Gaussians --
+    the binned ids, when the only gradients are the render's."""
+    if ids is not None and out is None:
+        raise ValueError("an id list needs accumulation buffers (out=...)")
     P = g.P
     dev = g.means3D.device
     acc = out is not None
@@ -408,6 +420,10 @@ def preprocess_backward(g: Gaussians, cam: Camera, radii, records, grad_acc, gra
     a.grad_conic_2d = _lib.ptr(grad_conic_2d)
     a.grad_conic_2d_inv = _lib.ptr(grad_conic_2d_inv)
     a.accumulate = int(acc)
+    a.ids = _lib.ptr(ids) if ids is not None and ids.numel() else None
+    a.num_ids = int(ids.numel()) if ids is not None else 0
+    if ids is not None and ids.numel() == 0:
+        return out
     a.grad_means3d = _lib.ptr(out.grad_means3D)
     a.grad_means2d = _lib.ptr(out.grad_means2D)
     a.grad_scales = _lib.ptr(out.grad_scales)
@@ -420,7 +436,7 @@ def preprocess_backward(g: Gaussians, cam: Camera, radii, records, grad_acc, gra
     with _stage_timer("preprocess_bwd", info):
         _lib.call("gsb_preprocess_bwd", a, _lib.stream_handle(dev))
     if TIMING_ENABLED:
-        info["visible"] = int((radii > 0).sum())
+        info["visible"] = int(ids.numel()) if ids is not None else int((radii > 0).sum())
     return out
 
 

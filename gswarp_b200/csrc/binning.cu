@@ -54,7 +54,8 @@ __global__ void __launch_bounds__(SCAN_THREADS) vis_count_kernel(int P, const in
 // breaks depth ties by index).  block_prefix = exclusive block offsets.
 __global__ void __launch_bounds__(SCAN_THREADS) vis_compact_kernel(
     int P, const float* __restrict__ depths, const int* __restrict__ tiles_touched,
-    const long long* __restrict__ block_prefix, unsigned* __restrict__ keys, unsigned* __restrict__ vals) {
+    const long long* __restrict__ block_prefix, unsigned* __restrict__ keys, unsigned* __restrict__ vals,
+    int* __restrict__ ids_out) {
   __shared__ int s_warp[SCAN_THREADS / 32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const long long base = (long long)blockIdx.x * SCAN_TILE;
@@ -78,6 +79,7 @@ __global__ void __launch_bounds__(SCAN_THREADS) vis_compact_kernel(
       const long long o = out + before + __popc(m & lanemask_lt());
       keys[o] = __float_as_uint(depths[r]);
       vals[o] = (unsigned)r;
+      if (ids_out) ids_out[o] = (int)r;
     }
     out += total;
     __syncthreads();
@@ -323,7 +325,8 @@ GSB_EXPORT int gsb_bin_count(const gsb_bin_count_args* a, void* stream) {
   unsigned* vals0 = (unsigned*)a->depth_order;
   vis_count_kernel<<<nblocks, SCAN_THREADS, 0, s>>>(P, a->tiles_touched, block_sums);
   scan_blocks_kernel<<<1, 1024, 0, s>>>(nblocks, block_sums, a->status_out + 2, n_vis);
-  vis_compact_kernel<<<nblocks, SCAN_THREADS, 0, s>>>(P, a->depths, a->tiles_touched, block_sums, keys, vals0);
+  vis_compact_kernel<<<nblocks, SCAN_THREADS, 0, s>>>(P, a->depths, a->tiles_touched, block_sums, keys, vals0,
+                                                      a->binned_ids);
   // 2. stable sort of the V (depth bits, index) pairs.
   unsigned* kb[2] = {keys, keys_alt};
   unsigned* vb[2] = {vals0, vals_alt};

@@ -185,7 +185,7 @@ constexpr int SH_ROW_F4 = 13;  // 52 floats per staged row
 constexpr int PB_THREADS = 256;
 constexpr int PB_SH16_THREADS = 128;
 
-__device__ __forceinline__ void sh_backward_staged(const gsb_preprocess_bwd_args& a, float4* rows, int idx0,
+__device__ __forceinline__ void sh_backward_staged(const gsb_preprocess_bwd_args& a, float4* rows, int my_idx,
                                                    bool work, bool need, const float mean[3],
                                                    const float cam[3], const float g[3], float gmean[3]) {
   const int lane = threadIdx.x & 31;
@@ -194,12 +194,15 @@ __device__ __forceinline__ void sh_backward_staged(const gsb_preprocess_bwd_args
   const unsigned work_mask = __ballot_sync(0xffffffffu, work);
   gmean[0] = gmean[1] = gmean[2] = 0.0f;
   if (work_mask == 0u) return;
-  const float4* src = reinterpret_cast<const float4*>(a.sh) + (size_t)idx0 * 12;
+  // Row r belongs to lane r's Gaussian (consecutive Gaussians, or the
+  // Gaussians of an id list); its 12 float4 are contiguous in memory.
+  const float4* src = reinterpret_cast<const float4*>(a.sh);
   if (need_mask) {
 #pragma unroll 4
     for (int j = lane; j < 32 * 12; j += 32) {
       const int r = j / 12;
-      if ((need_mask >> r) & 1u) rows[r * SH_ROW_F4 + (j - r * 12)] = __ldg(src + j);
+      const int row_idx = __shfl_sync(0xffffffffu, my_idx, r);
+      if ((need_mask >> r) & 1u) rows[r * SH_ROW_F4 + (j - r * 12)] = __ldg(src + (size_t)row_idx * 12 + (j - r * 12));
     }
   }
   __syncwarp();
@@ -227,20 +230,22 @@ __device__ __forceinline__ void sh_backward_staged(const gsb_preprocess_bwd_args
     }
   }
   __syncwarp();
-  float4* dst = reinterpret_cast<float4*>(a.grad_sh) + (size_t)idx0 * 12;
+  float4* dst_base = reinterpret_cast<float4*>(a.grad_sh);
 #pragma unroll 4
   for (int j = lane; j < 32 * 12; j += 32) {
     const int r = j / 12;
+    const int row_idx = __shfl_sync(0xffffffffu, my_idx, r);
     if (!((work_mask >> r) & 1u)) continue;
+    float4* dst = dst_base + (size_t)row_idx * 12 + (j - r * 12);
     if ((need_mask >> r) & 1u) {
       float4 v = rows[r * SH_ROW_F4 + (j - r * 12)];
       if (acc) {
-        const float4 o = dst[j];
+        const float4 o = *dst;
         v = make_float4(o.x + v.x, o.y + v.y, o.z + v.z, o.w + v.w);
       }
-      dst[j] = v;
+      *dst = v;
     } else if (!acc) {
-      dst[j] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      *dst = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     }
   }
   __syncwarp();
@@ -266,8 +271,11 @@ __global__ void __launch_bounds__(SH16 ? PB_SH16_THREADS : PB_THREADS)
   __syncthreads();
   const int tid = blockIdx.x * blockDim.x + threadIdx.x;
   const bool acc = a.accumulate != 0;
-  const bool live = tid < a.P;
-  const int rad = live ? a.radii[tid] : 0;
+  // With an id list, thread t handles Gaussian ids[t] (t < num_ids);
+  // otherwise thread t handles Gaussian t.
+  const bool live = a.ids ? tid < a.num_ids : tid < a.P;
+  const int gid = a.ids ? (live ? a.ids[tid] : 0) : tid;
+  const int rad = live ? a.radii[gid] : 0;
   const bool work = live && (!acc || rad > 0);
   if (!SH16 && !work) return;
   const float* pr = s_proj;
@@ -275,10 +283,10 @@ __global__ void __launch_bounds__(SH16 ? PB_SH16_THREADS : PB_THREADS)
   float mean[3] = {0.0f, 0.0f, 0.0f};
   float4 gq0 = make_float4(0.0f, 0.0f, 0.0f, 0.0f), gq1 = gq0, gq2 = gq0;
   if (work) {
-    mean[0] = a.means[tid * 3];
-    mean[1] = a.means[tid * 3 + 1];
-    mean[2] = a.means[tid * 3 + 2];
-    const float4* ga4 = reinterpret_cast<const float4*>(a.grad_acc) + (size_t)tid * 3;
+    mean[0] = a.means[gid * 3];
+    mean[1] = a.means[gid * 3 + 1];
+    mean[2] = a.means[gid * 3 + 2];
+    const float4* ga4 = reinterpret_cast<const float4*>(a.grad_acc) + (size_t)gid * 3;
     gq0 = ga4[0];
     gq1 = ga4[1];
     gq2 = ga4[2];
@@ -289,8 +297,8 @@ __global__ void __launch_bounds__(SH16 ? PB_SH16_THREADS : PB_THREADS)
 
   float gxy0 = rgx, gxy1 = rgy;
   if (rad > 0 && a.grad_proj_2d) {
-    gxy0 = gxy0 + a.grad_proj_2d[tid * 2];
-    gxy1 = gxy1 + a.grad_proj_2d[tid * 2 + 1];
+    gxy0 = gxy0 + a.grad_proj_2d[gid * 2];
+    gxy1 = gxy1 + a.grad_proj_2d[gid * 2 + 1];
   }
   const float hom_x = pr[0] * mean[0] + pr[4] * mean[1] + pr[8] * mean[2] + pr[12];
   const float hom_y = pr[1] * mean[0] + pr[5] * mean[1] + pr[9] * mean[2] + pr[13];
@@ -328,8 +336,8 @@ __global__ void __launch_bounds__(SH16 ? PB_SH16_THREADS : PB_THREADS)
     const float w00 = vf[0], w01 = vf[1], w02 = vf[2], w10 = vf[4], w11 = vf[5], w12 = vf[6];
     const float w20 = vf[8], w21 = vf[9], w22 = vf[10];
     // A NULL user gradient is a zero gradient (x + 0 == x).
-    const float* gk = a.grad_conic_2d ? a.grad_conic_2d + tid * 3 : nullptr;
-    const float* gkv = a.grad_conic_2d_inv ? a.grad_conic_2d_inv + tid * 3 : nullptr;
+    const float* gk = a.grad_conic_2d ? a.grad_conic_2d + gid * 3 : nullptr;
+    const float* gkv = a.grad_conic_2d_inv ? a.grad_conic_2d_inv + gid * 3 : nullptr;
     const float tc0 = gk ? rco[0] + gk[0] : rco[0];
     const float tc1 = gk ? rco[1] + gk[1] : rco[1];
     const float tc2 = gk ? rco[2] + gk[2] : rco[2];
@@ -352,10 +360,10 @@ __global__ void __launch_bounds__(SH16 ? PB_SH16_THREADS : PB_THREADS)
                   t20 = w20 * j00 + w22 * j02;
       const float t01 = w01 * j11 + w02 * j12, t11 = w11 * j11 + w12 * j12,
                   t21 = w21 * j11 + w22 * j12;
-      const float s0 = a.scales[tid * 3 + 0] * a.scale_modifier;
-      const float s1 = a.scales[tid * 3 + 1] * a.scale_modifier;
-      const float s2 = a.scales[tid * 3 + 2] * a.scale_modifier;
-      const float4 q = reinterpret_cast<const float4*>(a.rotations)[tid];
+      const float s0 = a.scales[gid * 3 + 0] * a.scale_modifier;
+      const float s1 = a.scales[gid * 3 + 1] * a.scale_modifier;
+      const float s2 = a.scales[gid * 3 + 2] * a.scale_modifier;
+      const float4 q = reinterpret_cast<const float4*>(a.rotations)[gid];
       const float rr = q.x, xq = q.y, yq = q.z, zq = q.w;
       const float r00 = 1.0f - 2.0f * (yq * yq + zq * zq);
       const float r01 = 2.0f * (xq * yq + rr * zq);
@@ -441,7 +449,7 @@ __global__ void __launch_bounds__(SH16 ? PB_SH16_THREADS : PB_THREADS)
               4.0f * zq * (dR11 + dR00);
     } else {
       // backward_kernels.py:731-840
-      const float* c3 = a.cov3d_precomp + (size_t)tid * 6;
+      const float* c3 = a.cov3d_precomp + (size_t)gid * 6;
       const float txtz = x / z, tytz = y / z;
       const float tx = fclamp(txtz, -limx, limx) * z;
       const float ty = fclamp(tytz, -limy, limy) * z;
@@ -509,16 +517,16 @@ __global__ void __launch_bounds__(SH16 ? PB_SH16_THREADS : PB_THREADS)
     bool need = false;
     if (work) {
       const unsigned clamp_bits =
-          __float_as_uint(reinterpret_cast<const float4*>(a.records)[(size_t)tid * 3 + 1].w);
+          __float_as_uint(reinterpret_cast<const float4*>(a.records)[(size_t)gid * 3 + 1].w);
       need = sh_color_grad(rrgb, clamp_bits, g);
     }
-    sh_backward_staged(a, s_rows + (threadIdx.x & ~31) * SH_ROW_F4, tid & ~31, work, need, mean, s_cam, g,
+    sh_backward_staged(a, s_rows + (threadIdx.x & ~31) * SH_ROW_F4, gid, work, need, mean, s_cam, g,
                        gsm);
     if (!work) return;
   } else if (a.sh) {
     const unsigned clamp_bits =
-        __float_as_uint(reinterpret_cast<const float4*>(a.records)[(size_t)tid * 3 + 1].w);
-    sh_backward(a, tid, mean, s_cam, rrgb, clamp_bits, gsm);
+        __float_as_uint(reinterpret_cast<const float4*>(a.records)[(size_t)gid * 3 + 1].w);
+    sh_backward(a, gid, mean, s_cam, rrgb, clamp_bits, gsm);
   }
   float m0 = pm_x + gcm[0], m1 = pm_y + gcm[1], m2 = pm_z + gcm[2];
   if (SH16 || a.sh) {
@@ -526,25 +534,25 @@ __global__ void __launch_bounds__(SH16 ? PB_SH16_THREADS : PB_THREADS)
     m1 = m1 + gsm[1];
     m2 = m2 + gsm[2];
   }
-  store_or_add(a.grad_means3d + tid * 3 + 0, m0, acc);
-  store_or_add(a.grad_means3d + tid * 3 + 1, m1, acc);
-  store_or_add(a.grad_means3d + tid * 3 + 2, m2, acc);
+  store_or_add(a.grad_means3d + gid * 3 + 0, m0, acc);
+  store_or_add(a.grad_means3d + gid * 3 + 1, m1, acc);
+  store_or_add(a.grad_means3d + gid * 3 + 2, m2, acc);
   if (a.grad_means2d) {
-    store_or_add(a.grad_means2d + tid * 3 + 0, rgx, acc);
-    store_or_add(a.grad_means2d + tid * 3 + 1, rgy, acc);
-    store_or_add(a.grad_means2d + tid * 3 + 2, 0.0f, acc);
+    store_or_add(a.grad_means2d + gid * 3 + 0, rgx, acc);
+    store_or_add(a.grad_means2d + gid * 3 + 1, rgy, acc);
+    store_or_add(a.grad_means2d + gid * 3 + 2, 0.0f, acc);
   }
   if (!PRECOMP) {
     if (a.grad_scales)
-      for (int k = 0; k < 3; ++k) store_or_add(a.grad_scales + tid * 3 + k, gs[k], acc);
+      for (int k = 0; k < 3; ++k) store_or_add(a.grad_scales + gid * 3 + k, gs[k], acc);
     if (a.grad_rotations)
-      for (int k = 0; k < 4; ++k) store_or_add(a.grad_rotations + tid * 4 + k, gr[k], acc);
+      for (int k = 0; k < 4; ++k) store_or_add(a.grad_rotations + gid * 4 + k, gr[k], acc);
   } else if (a.grad_cov3d) {
-    for (int k = 0; k < 6; ++k) store_or_add(a.grad_cov3d + tid * 6 + k, gc3[k], acc);
+    for (int k = 0; k < 6; ++k) store_or_add(a.grad_cov3d + gid * 6 + k, gc3[k], acc);
   }
-  if (a.grad_opacity) store_or_add(a.grad_opacity + tid, rco[3], acc);
+  if (a.grad_opacity) store_or_add(a.grad_opacity + gid, rco[3], acc);
   if (a.grad_colors)
-    for (int k = 0; k < 3; ++k) store_or_add(a.grad_colors + tid * 3 + k, rrgb[k], acc);
+    for (int k = 0; k < 3; ++k) store_or_add(a.grad_colors + gid * 3 + k, rrgb[k], acc);
 }
 
 }  // namespace
@@ -558,6 +566,12 @@ GSB_EXPORT int gsb_preprocess_bwd(const gsb_preprocess_bwd_args* a, void* stream
     return GSB_ERR_INVALID;
   }
   if (a->P == 0) return GSB_OK;
+  if (a->ids && (!a->accumulate || a->num_ids < 0 || a->num_ids > a->P)) {
+    set_error("gsb_preprocess_bwd: an id list needs accumulate mode and 0 <= num_ids <= P");
+    return GSB_ERR_INVALID;
+  }
+  const int threads_needed = a->ids ? a->num_ids : a->P;
+  if (threads_needed == 0) return GSB_OK;
   const bool precomp = a->cov3d_precomp != nullptr;
   if (!precomp && (!a->scales || !a->rotations)) {
     set_error("gsb_preprocess_bwd: scales/rotations or cov3d_precomp required");
@@ -578,13 +592,13 @@ GSB_EXPORT int gsb_preprocess_bwd(const gsb_preprocess_bwd_args* a, void* stream
   const bool sh16 = a->sh && a->sh_coeffs == 16 && !(reinterpret_cast<uintptr_t>(a->sh) & 15) &&
                     !(reinterpret_cast<uintptr_t>(a->grad_sh) & 15);
   if (sh16) {
-    const int blocks = div_up(a->P, PB_SH16_THREADS);
+    const int blocks = div_up(threads_needed, PB_SH16_THREADS);
     if (precomp)
       preprocess_bwd_kernel<true, true><<<blocks, PB_SH16_THREADS, 0, s>>>(*a);
     else
       preprocess_bwd_kernel<false, true><<<blocks, PB_SH16_THREADS, 0, s>>>(*a);
   } else {
-    const int blocks = div_up(a->P, PB_THREADS);
+    const int blocks = div_up(threads_needed, PB_THREADS);
     if (precomp)
       preprocess_bwd_kernel<true, false><<<blocks, PB_THREADS, 0, s>>>(*a);
     else

@@ -150,7 +150,7 @@ class FusedViewStep:
             raise ValueError(f"target {i} must have shape (3, {cam.H}, {cam.W})")
         tgt = self._target(i, target)
         pre = pl.preprocess(g, cam, mode)
-        binned = pl.binning(pre, cam, mode)
+        binned = pl.binning(pre, cam, mode, want_ids=True)
         ren = pl.render(pre, binned, cam, bg, False)
         _, dm = photometric_loss_forward(ren.color, tgt, self.l1_weight, self.ssim_weight, out=self.losses[i])
         grad_img = photometric_loss_backward(ren.color, tgt, dm, self.l1_weight, self.ssim_weight)
@@ -160,7 +160,7 @@ class FusedViewStep:
         out = pl.PreprocessGrads(grad_means3D=v_means, grad_means2D=None, grad_opacity=v_opac,
                                  grad_scales=v_scales, grad_rotations=v_rots, grad_cov3D=None, grad_sh=v_sh,
                                  grad_colors=None)
-        pl.preprocess_backward(g, cam, pre.radii, pre.records, grad_acc, None, None, None, out=out)
+        pl.preprocess_backward(g, cam, pre.radii, pre.records, grad_acc, None, None, None, out=out, ids=binned.ids)
 
     def step(self, targets: Sequence[torch.Tensor]) -> torch.Tensor:
         if len(targets) != len(self.settings):

@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define GSB_ABI_VERSION 5
+#define GSB_ABI_VERSION 6
 
 #define GSB_OK 0
 #define GSB_ERR_INVALID (-1)  /* bad argument: ValueError in Python          */
@@ -117,6 +117,7 @@ typedef struct {
   const int* tiles_touched;   /* (P) */
   int* depth_order;           /* out (P): first V entries = ids with tiles, in depth order */
   int* point_offsets;         /* out (P): first V entries = inclusive scan in depth order */
+  int* binned_ids;            /* optional out (P): first V entries = ids with tiles, ascending */
   long long* status_out;      /* out, device, 3 words: [0]=pair total, [1]=error word, [2]=V */
   void* workspace;
   size_t workspace_bytes;
@@ -228,6 +229,10 @@ typedef struct {
   float* grad_sh;        /* (P,K,3) */
   float* grad_colors;    /* (P,3) colors_precomp gradient */
   float* grad_cov3d;     /* (P,6) cov3D_precomp gradient */
+  const int* ids;        /* optional (accumulate mode only): process just these Gaussians,
+                            e.g. the binned_ids of gsb_bin_count (the others get no
+                            render gradient and are left untouched); NULL = all P */
+  int num_ids;
 } gsb_preprocess_bwd_args;
 
 int gsb_preprocess_bwd(const gsb_preprocess_bwd_args* a, void* stream);

@@ -245,6 +245,24 @@ def test_preprocess_backward_accumulate_adds_exactly(cuda, name, unaligned):
         want = b + getattr(fresh, k).reshape(b.shape)
         want[~vis] = b[~vis]
         assert torch.equal(got, want), k
+    # restricted to the binned ids (the Gaussians with tiles), the
+    # accumulation gives the same bits
+    with_ids = pl.binning(pre, cam, 1, want_ids=True)
+    want_ids = torch.nonzero(pre.tiles_touched > 0).flatten().to(torch.int32)
+    assert torch.equal(with_ids.ids, want_ids)
+    pre_fill2 = pl.PreprocessGrads(**{k: getattr(pre_fill, k) for k in pre_fill.__slots__})
+    for k, b in before.items():
+        fresh_buf = b.clone()
+        if k == "grad_sh" and unaligned:
+            sbuf2 = torch.empty(b.numel() + 1, device=cuda)
+            sbuf2[1:] = b.reshape(-1)
+            fresh_buf = sbuf2[1:].view(b.shape)
+        setattr(pre_fill2, k, fresh_buf)
+    pl.preprocess_backward(g, cam, pre.radii, pre.records, grad_acc, None, None, None, out=pre_fill2,
+                           ids=with_ids.ids)
+    torch.cuda.synchronize()
+    for k in before:
+        assert torch.equal(getattr(pre_fill2, k), getattr(pre_fill, k)), k
     if not unaligned and name == "cfg2_200k":
         # the staged and per-thread SH paths agree bit for bit (non-accumulating)
         buf = torch.empty(g.sh.numel() + 1, device=cuda)
