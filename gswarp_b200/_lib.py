@@ -24,7 +24,7 @@ GSB_ERR_OVERFLOW = -2
 GSB_ERR_CUDA = -3
 GSB_ERR_TIMEOUT = -4
 
-ABI_VERSION = 6
+ABI_VERSION = 7
 RECORD_FLOATS = 12
 GRAD_FLOATS = 12
 
@@ -46,6 +46,7 @@ class PreprocessArgs(ctypes.Structure):
         ("coverage_mode", c_int),
         ("radii", vp), ("proj_2d", vp), ("conic_2d", vp), ("conic_2d_inv", vp), ("depths", vp),
         ("tiles_touched", vp), ("records", vp), ("cov3d_out", vp), ("bin_records", vp),
+        ("sparse_records", c_int),
     ]
 
 

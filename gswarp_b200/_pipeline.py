@@ -120,9 +120,9 @@ class Gaussians:
 @dataclass(slots=True)
 class Preprocessed:
     radii: torch.Tensor
-    proj_2d: torch.Tensor
-    conic_2d: torch.Tensor
-    conic_2d_inv: torch.Tensor
+    proj_2d: torch.Tensor | None
+    conic_2d: torch.Tensor | None
+    conic_2d_inv: torch.Tensor | None
     depths: torch.Tensor
     tiles_touched: torch.Tensor
     records: torch.Tensor
@@ -181,10 +181,13 @@ MAX_TILE_GRID = 65535
 
 
 def preprocess(g: Gaussians, cam: Camera, coverage_mode: int, want_cov3d: bool = False,
-               bin_records: bool = True) -> Preprocessed:
+               bin_records: bool = True, sparse: bool = False) -> Preprocessed:
     """Runs the fused preprocess.  With ``bin_records`` (the default) it also
     writes the 32-byte per-Gaussian records the binning emit reads instead of
-    gathering radii, render records, conic_2D_inv and tiles_touched."""
+    gathering radii, render records, conic_2D_inv and tiles_touched.
+    ``sparse`` (internal training step) skips what only the autograd outputs
+    need: proj_2D / conic_2D / conic_2D_inv are not produced and render
+    records are written only for Gaussians with a radius."""
     P = g.P
     dev = g.means3D.device
     cov3d = None
@@ -193,9 +196,9 @@ def preprocess(g: Gaussians, cam: Camera, coverage_mode: int, want_cov3d: bool =
     out = Preprocessed(
         cov3d=cov3d,
         radii=torch.empty(P, dtype=torch.int32, device=dev),
-        proj_2d=torch.empty((P, 2), dtype=torch.float32, device=dev),
-        conic_2d=torch.empty((P, 3), dtype=torch.float32, device=dev),
-        conic_2d_inv=torch.empty((P, 3), dtype=torch.float32, device=dev),
+        proj_2d=None if sparse else torch.empty((P, 2), dtype=torch.float32, device=dev),
+        conic_2d=None if sparse else torch.empty((P, 3), dtype=torch.float32, device=dev),
+        conic_2d_inv=None if sparse else torch.empty((P, 3), dtype=torch.float32, device=dev),
         depths=torch.empty(P, dtype=torch.float32, device=dev),
         tiles_touched=torch.empty(P, dtype=torch.int32, device=dev),
         records=torch.empty((P, _lib.RECORD_FLOATS), dtype=torch.float32, device=dev),
@@ -203,6 +206,8 @@ def preprocess(g: Gaussians, cam: Camera, coverage_mode: int, want_cov3d: bool =
     gx, gy = cam.grid
     if bin_records and P > 0 and gx <= MAX_TILE_GRID and gy <= MAX_TILE_GRID:
         out.bin_records = torch.empty((P, BIN_RECORD_FLOATS), dtype=torch.float32, device=dev)
+    elif sparse:
+        out.conic_2d_inv = torch.empty((P, 3), dtype=torch.float32, device=dev)  # the gathering emit needs it
     if P == 0:
         return out
     a = _lib.PreprocessArgs()
@@ -232,6 +237,7 @@ def preprocess(g: Gaussians, cam: Camera, coverage_mode: int, want_cov3d: bool =
     a.records = _lib.ptr(out.records)
     a.cov3d_out = _lib.ptr(cov3d) if (cov3d is not None and g.cov3D is None) else None
     a.bin_records = _lib.ptr(out.bin_records)
+    a.sparse_records = int(sparse)
     with _stage_timer("preprocess_fwd", {"P": P, "kernels": 1}):
         _lib.call("gsb_preprocess_fwd", a, _lib.stream_handle(dev))
     return out

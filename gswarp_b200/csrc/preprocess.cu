@@ -73,8 +73,21 @@ __device__ __forceinline__ void eval_sh(const float (&sp)[48], int K, int degree
   }
 }
 
-__global__ void __launch_bounds__(256) preprocess_fwd_kernel(const gsb_preprocess_args a) {
+constexpr int PF_THREADS = 256;
+constexpr int PF_SH16_THREADS = 128;
+constexpr int SH_ROW_F4 = 13;  // staged SH row: 48 floats padded to 52
+
+// SH16: (P,16,3) SH rows, 16-byte aligned.  Each warp then moves the SH rows
+// of its 32 consecutive Gaussians (one contiguous 6 KB span) into shared
+// memory with coalesced 16-byte loads -- only the rows of Gaussians that
+// survive culling -- and each thread evaluates its row from there (rows
+// padded to 52 floats: conflict-free 16-byte reads).  Every lane of the warp
+// takes part, so threads past P stay in the kernel with nothing to do.
+template <bool SH16>
+__global__ void __launch_bounds__(SH16 ? PF_SH16_THREADS : PF_THREADS)
+    preprocess_fwd_kernel(const gsb_preprocess_args a) {
   __shared__ float s_view[16], s_proj[16], s_cam[3];
+  __shared__ float4 s_rows[SH16 ? PF_SH16_THREADS * SH_ROW_F4 : 1];
   if (threadIdx.x < 16) {
     s_view[threadIdx.x] = a.viewmatrix[threadIdx.x];
     s_proj[threadIdx.x] = a.projmatrix[threadIdx.x];
@@ -83,26 +96,29 @@ __global__ void __launch_bounds__(256) preprocess_fwd_kernel(const gsb_preproces
   }
   __syncthreads();
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= a.P) return;
+  const bool live = idx < a.P;
+  if (!SH16 && !live) return;
+  const int li = live ? idx : 0;  // in-bounds index for the loads of lanes past P
   const float* v = s_view;
   const float* pr = s_proj;
   const int gx = (a.W + BLOCK_X - 1) / BLOCK_X;
   const int gy = (a.H + BLOCK_Y - 1) / BLOCK_Y;
 
-  const float p0 = a.means[idx * 3 + 0], p1 = a.means[idx * 3 + 1], p2 = a.means[idx * 3 + 2];
-  const float opacity = a.opacities[idx];
+  const float p0 = a.means[li * 3 + 0], p1 = a.means[li * 3 + 1], p2 = a.means[li * 3 + 2];
+  const float opacity = a.opacities[li];
 
   int radius = 0, tiles = 0;
   float depth = 0.0f, px = 0.0f, py = 0.0f;
   float con0 = 0.0f, con1 = 0.0f, con2 = 0.0f;
   float cov_a = 0.0f, cov_b = 0.0f, cov_c = 0.0f;
 
-  const float p_view_z = v[2] * p0 + v[6] * p1 + v[10] * p2 + v[14];
+  // lanes past P take the near-plane-culled path and store nothing
+  const float p_view_z = live ? v[2] * p0 + v[6] * p1 + v[10] * p2 + v[14] : 0.0f;
   bool go = false;
   float ppx = 0.0f, ppy = 0.0f;
   bool strict_det = false;
   if (a.cov3d_precomp == nullptr) {
-    if (a.cov3d_out && !(p_view_z > 0.2f)) {
+    if (live && a.cov3d_out && !(p_view_z > 0.2f)) {
       float* c3 = a.cov3d_out + (size_t)idx * 6;
       for (int k = 0; k < 6; ++k) c3[k] = 0.0f;  // near-culled: zero (preprocess_kernels.py:116-121)
     }
@@ -265,7 +281,46 @@ __global__ void __launch_bounds__(256) preprocess_fwd_kernel(const gsb_preproces
   // only reads the clamp flags where the render gradient is non-zero.
   float col[3] = {0.0f, 0.0f, 0.0f};
   unsigned clamp_bits = 0u;
-  if (radius > 0) {
+  if (SH16) {
+    const bool need = radius > 0 && a.colors_precomp == nullptr;
+    const unsigned need_mask = __ballot_sync(0xffffffffu, need);
+    float4* rows = s_rows + (threadIdx.x & ~31) * SH_ROW_F4;
+    const int lane = threadIdx.x & 31;
+    if (need_mask) {
+      const float4* src = reinterpret_cast<const float4*>(a.sh) + (size_t)(idx & ~31) * 12;
+#pragma unroll 4
+      for (int j = lane; j < 32 * 12; j += 32) {
+        const int r = j / 12;
+        if ((need_mask >> r) & 1u) rows[r * SH_ROW_F4 + (j - r * 12)] = __ldg(src + j);
+      }
+    }
+    __syncwarp();
+    if (need) {
+      const float dx = p0 - s_cam[0], dy = p1 - s_cam[1], dz = p2 - s_cam[2];
+      const float len_sq = dx * dx + dy * dy + dz * dz;
+      const float inv_len = 1.0f / sqrtf(fmx(len_sq, 1.0e-20f));
+      float shv[48];
+      const float4* row = rows + lane * SH_ROW_F4;
+#pragma unroll
+      for (int q = 0; q < 12; ++q) {
+        const float4 t = row[q];
+        shv[q * 4 + 0] = t.x;
+        shv[q * 4 + 1] = t.y;
+        shv[q * 4 + 2] = t.z;
+        shv[q * 4 + 3] = t.w;
+      }
+      eval_sh(shv, 16, a.sh_degree, dx * inv_len, dy * inv_len, dz * inv_len, col);
+#pragma unroll
+      for (int ch = 0; ch < 3; ++ch) {
+        col[ch] = col[ch] + 0.5f;
+        if (col[ch] < 0.0f) {
+          col[ch] = 0.0f;
+          clamp_bits |= 1u << ch;
+        }
+      }
+    }
+    if (!live) return;
+  } else if (radius > 0) {
     if (a.colors_precomp) {
       col[0] = a.colors_precomp[idx * 3 + 0];
       col[1] = a.colors_precomp[idx * 3 + 1];
@@ -308,18 +363,24 @@ __global__ void __launch_bounds__(256) preprocess_fwd_kernel(const gsb_preproces
   a.radii[idx] = radius;
   a.depths[idx] = depth;
   a.tiles_touched[idx] = tiles;
-  reinterpret_cast<float2*>(a.proj_2d)[idx] = make_float2(px, py);
-  a.conic_2d[idx * 3 + 0] = con0;
-  a.conic_2d[idx * 3 + 1] = con1;
-  a.conic_2d[idx * 3 + 2] = con2;
-  a.conic_2d_inv[idx * 3 + 0] = cov_a;
-  a.conic_2d_inv[idx * 3 + 1] = cov_b;
-  a.conic_2d_inv[idx * 3 + 2] = cov_c;
-  float4* rec = reinterpret_cast<float4*>(a.records) + (size_t)idx * 3;
-  const float op_rec = radius > 0 ? opacity : 0.0f;
-  rec[0] = make_float4(px, py, con0, con1);
-  rec[1] = make_float4(con2, op_rec, depth, __uint_as_float(clamp_bits));
-  rec[2] = make_float4(col[0], col[1], col[2], 0.0f);
+  if (a.proj_2d) reinterpret_cast<float2*>(a.proj_2d)[idx] = make_float2(px, py);
+  if (a.conic_2d) {
+    a.conic_2d[idx * 3 + 0] = con0;
+    a.conic_2d[idx * 3 + 1] = con1;
+    a.conic_2d[idx * 3 + 2] = con2;
+  }
+  if (a.conic_2d_inv) {
+    a.conic_2d_inv[idx * 3 + 0] = cov_a;
+    a.conic_2d_inv[idx * 3 + 1] = cov_b;
+    a.conic_2d_inv[idx * 3 + 2] = cov_c;
+  }
+  if (radius > 0 || !a.sparse_records) {
+    float4* rec = reinterpret_cast<float4*>(a.records) + (size_t)idx * 3;
+    const float op_rec = radius > 0 ? opacity : 0.0f;
+    rec[0] = make_float4(px, py, con0, con1);
+    rec[1] = make_float4(con2, op_rec, depth, __uint_as_float(clamp_bits));
+    rec[2] = make_float4(col[0], col[1], col[2], 0.0f);
+  }
 }
 
 __global__ void mark_visible_kernel(int P, const float* __restrict__ means,
@@ -353,8 +414,7 @@ GSB_EXPORT int gsb_preprocess_fwd(const gsb_preprocess_args* a, void* stream) {
     return GSB_ERR_INVALID;
   }
   if (!a->means || !a->opacities || !a->viewmatrix || !a->projmatrix || !a->radii ||
-      !a->proj_2d || !a->conic_2d || !a->conic_2d_inv || !a->depths || !a->tiles_touched ||
-      !a->records) {
+      !a->depths || !a->tiles_touched || !a->records) {
     set_error("gsb_preprocess_fwd: null pointer argument");
     return GSB_ERR_INVALID;
   }
@@ -373,7 +433,12 @@ GSB_EXPORT int gsb_preprocess_fwd(const gsb_preprocess_args* a, void* stream) {
     set_error("gsb_preprocess_fwd: bin_records needs 16-byte alignment and tile grids below 65536");
     return GSB_ERR_INVALID;
   }
-  preprocess_fwd_kernel<<<div_up(a->P, 256), 256, 0, (cudaStream_t)stream>>>(*a);
+  const bool sh16 = a->sh && !a->colors_precomp && a->sh_coeffs == 16 &&
+                    !(reinterpret_cast<uintptr_t>(a->sh) & 15);
+  if (sh16)
+    preprocess_fwd_kernel<true><<<div_up(a->P, PF_SH16_THREADS), PF_SH16_THREADS, 0, (cudaStream_t)stream>>>(*a);
+  else
+    preprocess_fwd_kernel<false><<<div_up(a->P, PF_THREADS), PF_THREADS, 0, (cudaStream_t)stream>>>(*a);
   return check_launch("preprocess_fwd_kernel");
 }
 

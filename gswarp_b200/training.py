@@ -149,7 +149,7 @@ class FusedViewStep:
         if target.shape != (NUM_CHANNELS, cam.H, cam.W):
             raise ValueError(f"target {i} must have shape (3, {cam.H}, {cam.W})")
         tgt = self._target(i, target)
-        pre = pl.preprocess(g, cam, mode)
+        pre = pl.preprocess(g, cam, mode, sparse=True)
         binned = pl.binning(pre, cam, mode, want_ids=True)
         ren = pl.render(pre, binned, cam, bg, False)
         _, dm = photometric_loss_forward(ren.color, tgt, self.l1_weight, self.ssim_weight, out=self.losses[i])

@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define GSB_ABI_VERSION 6
+#define GSB_ABI_VERSION 7
 
 #define GSB_OK 0
 #define GSB_ERR_INVALID (-1)  /* bad argument: ValueError in Python          */
@@ -82,9 +82,10 @@ typedef struct {
   int coverage_mode;           /* GSB_COVERAGE_* */
   /* outputs (all (P,...) device arrays) */
   int* radii;
-  float* proj_2d;       /* (P,2) */
-  float* conic_2d;      /* (P,3) */
-  float* conic_2d_inv;  /* (P,3) */
+  float* proj_2d;       /* (P,2), or NULL (not written) */
+  float* conic_2d;      /* (P,3), or NULL (not written) */
+  float* conic_2d_inv;  /* (P,3), or NULL (not written; the binning emit needs it
+                           unless bin_records are used) */
   float* depths;        /* (P) */
   int* tiles_touched;   /* (P) */
   float* records;       /* (P,12) render records */
@@ -94,6 +95,8 @@ typedef struct {
                            centre, conic, opacity threshold and clipped tile rect the
                            binning emit needs (written only where tiles_touched > 0;
                            needs both tile-grid dimensions below 65536) */
+  int sparse_records;   /* 1: write render records only where radius > 0 (nothing reads
+                           the others: render and the id-list backward skip them) */
 } gsb_preprocess_args;
 
 int gsb_preprocess_fwd(const gsb_preprocess_args* a, void* stream);

@@ -112,6 +112,27 @@ def test_preprocess_and_binning_bit_exact(cuda, name, mode):
         np.testing.assert_array_equal(_np(binned.ranges), ref_ranges)
 
 
+def test_sparse_preprocess_matches_dense(cuda):
+    """The training step's sparse preprocess gives the same radii, counts,
+    depths, binning records and (where radius > 0) render records."""
+    scene, view = _scene("cfg2_200k", cuda)
+    g, cam, dense = _gpu_pre(scene, view, cuda)
+    sparse = pl.preprocess(g, cam, 1, sparse=True)
+    torch.cuda.synchronize()
+    assert sparse.proj_2d is None and sparse.conic_2d is None and sparse.conic_2d_inv is None
+    for k in ("radii", "tiles_touched", "depths"):
+        assert torch.equal(getattr(sparse, k), getattr(dense, k)), k
+    vis = dense.radii > 0
+    assert torch.equal(sparse.records[vis].view(torch.int32), dense.records[vis].view(torch.int32))
+    withtiles = dense.tiles_touched > 0
+    assert torch.equal(sparse.bin_records[withtiles].view(torch.int32),
+                       dense.bin_records[withtiles].view(torch.int32))
+    a = pl.binning(dense, cam, 1)
+    b = pl.binning(sparse, cam, 1)
+    assert a.num_rendered == b.num_rendered
+    assert torch.equal(a.point_list, b.point_list) and torch.equal(a.ranges, b.ranges)
+
+
 def _render_case(name, dev):
     scene, view = _scene(name, dev)
     g, cam, pre = _gpu_pre(scene, view, dev)
