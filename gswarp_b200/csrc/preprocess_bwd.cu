@@ -44,11 +44,24 @@ __device__ __forceinline__ void dnormvdv(const float v[3], const float g[3], flo
   out[2] = (-v[0] * v[2] * g[0] - v[1] * v[2] * g[1] + (sum2 - v[2] * v[2]) * g[2]) * invsum32;
 }
 
+// Coefficient e (= 3 * coefficient + channel) of one SH row: from a
+// register copy, or from the row staged in shared memory (read where used,
+// which keeps the 48 coefficients out of registers).
+struct RegRow {
+  const float* v;
+  __device__ __forceinline__ float operator()(int e) const { return v[e]; }
+};
+struct SmemRow {
+  const float* p;
+  __device__ __forceinline__ float operator()(int e) const { return p[e]; }
+};
+
 // SH backward (backward_kernels.py:297-536), direction-dependent part:
 // basis weights w[k] (0 above the degree), the number of coefficients the
 // degree uses, and the gradient through the view direction from the row's
 // coefficients shv[0..47] (zero-padded past K).
-__device__ __forceinline__ void sh_core(int K, int degree, const float shv[48], const float mean[3],
+template <class Src>
+__device__ __forceinline__ void sh_core(int K, int degree, const Src& shv, const float mean[3],
                                         const float cam[3], const float g[3], float w[16], int& used,
                                         float gmean[3]) {
   const float dir[3] = {mean[0] - cam[0], mean[1] - cam[1], mean[2] - cam[2]};
@@ -71,9 +84,9 @@ __device__ __forceinline__ void sh_core(int K, int degree, const float shv[48], 
     used = 4;
 #pragma unroll
     for (int c = 0; c < 3; ++c) {
-      dx[c] = -c1 * shv[9 + c];
-      dy[c] = -c1 * shv[3 + c];
-      dz[c] = c1 * shv[6 + c];
+      dx[c] = -c1 * shv(9 + c);
+      dy[c] = -c1 * shv(3 + c);
+      dz[c] = c1 * shv(6 + c);
     }
     if (degree > 1 && K > 8) {
       const float xx = x * x, yy = y * y, zz = z * z, xy = x * y, yz = y * z, xz = x * z;
@@ -85,8 +98,8 @@ __device__ __forceinline__ void sh_core(int K, int degree, const float shv[48], 
       used = 9;
 #pragma unroll
       for (int c = 0; c < 3; ++c) {
-        const float s4 = shv[12 + c], s5 = shv[15 + c], s6 = shv[18 + c];
-        const float s7 = shv[21 + c], s8 = shv[24 + c];
+        const float s4 = shv(12 + c), s5 = shv(15 + c), s6 = shv(18 + c);
+        const float s7 = shv(21 + c), s8 = shv(24 + c);
         dx[c] = dx[c] + (SH_C2[0] * y) * s4 + (SH_C2[2] * (-2.0f * x)) * s6 + (SH_C2[3] * z) * s7 +
                 (SH_C2[4] * (2.0f * x)) * s8;
         dy[c] = dy[c] + (SH_C2[0] * x) * s4 + (SH_C2[1] * z) * s5 + (SH_C2[2] * (-2.0f * y)) * s6 +
@@ -104,9 +117,9 @@ __device__ __forceinline__ void sh_core(int K, int degree, const float shv[48], 
         used = 16;
 #pragma unroll
         for (int c = 0; c < 3; ++c) {
-          const float s9 = shv[27 + c], s10 = shv[30 + c], s11 = shv[33 + c];
-          const float s12 = shv[36 + c], s13 = shv[39 + c];
-          const float s14 = shv[42 + c], s15 = shv[45 + c];
+          const float s9 = shv(27 + c), s10 = shv(30 + c), s11 = shv(33 + c);
+          const float s12 = shv(36 + c), s13 = shv(39 + c);
+          const float s14 = shv(42 + c), s15 = shv(45 + c);
           dx[c] = dx[c] + (SH_C3[0] * (6.0f * xy)) * s9 + (SH_C3[1] * yz) * s10 +
                   (SH_C3[2] * (-2.0f * xy)) * s11 + (SH_C3[3] * (-6.0f * xz)) * s12 +
                   (SH_C3[4] * (-3.0f * xx + 4.0f * zz - yy)) * s13 + (SH_C3[5] * (2.0f * xz)) * s14 +
@@ -161,7 +174,7 @@ __device__ void sh_backward(const gsb_preprocess_bwd_args& a, int idx, const flo
   }
   float w[16];
   int used = 0;
-  sh_core(K, a.sh_degree, shv, mean, cam, g, w, used, gmean);
+  sh_core(K, a.sh_degree, RegRow{shv}, mean, cam, g, w, used, gmean);
   for (int k = 0; k < K; ++k) {
     float wk = 0.0f;  // w[k] without dynamic register indexing
 #pragma unroll
@@ -176,16 +189,17 @@ __device__ void sh_backward(const gsb_preprocess_bwd_args& a, int idx, const flo
 
 // Warp-cooperative SH backward for (P,16,3) rows.  One thread per Gaussian
 // reads and writes its 48-float row with stride-48 accesses, 32 rows apart
-// across a warp; here the warp moves its 32 consecutive rows (6 KB, one
-// contiguous span) between global and shared memory with coalesced 16-byte
-// accesses, and each thread works on its row in shared memory (rows padded to
-// 52 floats, so the per-thread 16-byte reads and writes are conflict-free).
-// Arithmetic is the same sh_core as the per-thread path.
-constexpr int SH_ROW_F4 = 13;  // 52 floats per staged row
+// across a warp; here the warp moves its 32 rows (each 192 contiguous bytes)
+// between global and shared memory with coalesced 16-byte global accesses,
+// and each thread works on its row in shared memory, reading coefficients
+// where they are used (rows padded to 49 floats: the per-thread scalar
+// accesses of a warp hit 32 different banks).  Arithmetic is the same
+// sh_core as the per-thread path.
+constexpr int SH_ROW_F = 49;
 constexpr int PB_THREADS = 256;
 constexpr int PB_SH16_THREADS = 128;
 
-__device__ __forceinline__ void sh_backward_staged(const gsb_preprocess_bwd_args& a, float4* rows, int my_idx,
+__device__ __forceinline__ void sh_backward_staged(const gsb_preprocess_bwd_args& a, float* rows, int my_idx,
                                                    bool work, bool need, const float mean[3],
                                                    const float cam[3], const float g[3], float gmean[3]) {
   const int lane = threadIdx.x & 31;
@@ -200,45 +214,38 @@ __device__ __forceinline__ void sh_backward_staged(const gsb_preprocess_bwd_args
   if (need_mask) {
 #pragma unroll 4
     for (int j = lane; j < 32 * 12; j += 32) {
-      const int r = j / 12;
+      const int r = j / 12, q = j - r * 12;
       const int row_idx = __shfl_sync(0xffffffffu, my_idx, r);
-      if ((need_mask >> r) & 1u) rows[r * SH_ROW_F4 + (j - r * 12)] = __ldg(src + (size_t)row_idx * 12 + (j - r * 12));
+      if ((need_mask >> r) & 1u) {
+        const float4 v = __ldg(src + (size_t)row_idx * 12 + q);
+        float* d = rows + r * SH_ROW_F + q * 4;
+        d[0] = v.x;
+        d[1] = v.y;
+        d[2] = v.z;
+        d[3] = v.w;
+      }
     }
   }
   __syncwarp();
   if (need) {
-    float4* row = rows + lane * SH_ROW_F4;
-    float shv[48];
-#pragma unroll
-    for (int q = 0; q < 12; ++q) {
-      const float4 v = row[q];
-      shv[q * 4 + 0] = v.x;
-      shv[q * 4 + 1] = v.y;
-      shv[q * 4 + 2] = v.z;
-      shv[q * 4 + 3] = v.w;
-    }
+    float* row = rows + lane * SH_ROW_F;
     float w[16];
     int used = 0;
-    sh_core(16, a.sh_degree, shv, mean, cam, g, w, used, gmean);
+    sh_core(16, a.sh_degree, SmemRow{row}, mean, cam, g, w, used, gmean);
 #pragma unroll
-    for (int q = 0; q < 12; ++q) {
-      const int e = q * 4;
-      row[q] = make_float4((e + 0) / 3 < used ? w[(e + 0) / 3] * g[(e + 0) % 3] : 0.0f,
-                           (e + 1) / 3 < used ? w[(e + 1) / 3] * g[(e + 1) % 3] : 0.0f,
-                           (e + 2) / 3 < used ? w[(e + 2) / 3] * g[(e + 2) % 3] : 0.0f,
-                           (e + 3) / 3 < used ? w[(e + 3) / 3] * g[(e + 3) % 3] : 0.0f);
-    }
+    for (int e = 0; e < 48; ++e) row[e] = e / 3 < used ? w[e / 3] * g[e % 3] : 0.0f;
   }
   __syncwarp();
   float4* dst_base = reinterpret_cast<float4*>(a.grad_sh);
 #pragma unroll 4
   for (int j = lane; j < 32 * 12; j += 32) {
-    const int r = j / 12;
+    const int r = j / 12, q = j - r * 12;
     const int row_idx = __shfl_sync(0xffffffffu, my_idx, r);
     if (!((work_mask >> r) & 1u)) continue;
-    float4* dst = dst_base + (size_t)row_idx * 12 + (j - r * 12);
+    float4* dst = dst_base + (size_t)row_idx * 12 + q;
     if ((need_mask >> r) & 1u) {
-      float4 v = rows[r * SH_ROW_F4 + (j - r * 12)];
+      const float* sr = rows + r * SH_ROW_F + q * 4;
+      float4 v = make_float4(sr[0], sr[1], sr[2], sr[3]);
       if (acc) {
         const float4 o = *dst;
         v = make_float4(o.x + v.x, o.y + v.y, o.z + v.z, o.w + v.w);
@@ -261,7 +268,7 @@ template <bool PRECOMP, bool SH16>
 __global__ void __launch_bounds__(SH16 ? PB_SH16_THREADS : PB_THREADS)
     preprocess_bwd_kernel(const gsb_preprocess_bwd_args a) {
   __shared__ float s_view[16], s_proj[16], s_cam[3];
-  __shared__ float4 s_rows[SH16 ? PB_SH16_THREADS * SH_ROW_F4 : 1];
+  __shared__ float s_rows[SH16 ? PB_SH16_THREADS * SH_ROW_F : 1];
   if (threadIdx.x < 16) {
     s_view[threadIdx.x] = a.viewmatrix[threadIdx.x];
     s_proj[threadIdx.x] = a.projmatrix[threadIdx.x];
@@ -282,18 +289,38 @@ __global__ void __launch_bounds__(SH16 ? PB_SH16_THREADS : PB_THREADS)
   const float* vf = s_view;
   float mean[3] = {0.0f, 0.0f, 0.0f};
   float4 gq0 = make_float4(0.0f, 0.0f, 0.0f, 0.0f), gq1 = gq0, gq2 = gq0;
+  const float4* ga4 = reinterpret_cast<const float4*>(a.grad_acc) + (size_t)gid * 3;
   if (work) {
     mean[0] = a.means[gid * 3];
     mean[1] = a.means[gid * 3 + 1];
     mean[2] = a.means[gid * 3 + 2];
-    const float4* ga4 = reinterpret_cast<const float4*>(a.grad_acc) + (size_t)gid * 3;
     gq0 = ga4[0];
     gq1 = ga4[1];
     gq2 = ga4[2];
   }
+  const float rrgb[3] = {gq2.x, gq2.y, gq2.z};
+
+  // SH first: only its mean gradient (3 floats) stays live through the
+  // projection / covariance part below, which keeps the register peak down.
+  float gsm[3] = {0.0f, 0.0f, 0.0f};
+  if (SH16) {
+    float g[3] = {0.0f, 0.0f, 0.0f};
+    bool need = false;
+    if (work) {
+      const unsigned clamp_bits =
+          __float_as_uint(reinterpret_cast<const float4*>(a.records)[(size_t)gid * 3 + 1].w);
+      need = sh_color_grad(rrgb, clamp_bits, g);
+    }
+    sh_backward_staged(a, s_rows + (threadIdx.x & ~31) * SH_ROW_F, gid, work, need, mean, s_cam, g,
+                       gsm);
+    if (!work) return;
+  } else if (a.sh) {
+    const unsigned clamp_bits =
+        __float_as_uint(reinterpret_cast<const float4*>(a.records)[(size_t)gid * 3 + 1].w);
+    sh_backward(a, gid, mean, s_cam, rrgb, clamp_bits, gsm);
+  }
   const float rgx = gq0.x, rgy = gq0.y, rgd = gq0.z;
   const float rco[4] = {gq1.x, gq1.y, gq1.z, gq1.w};
-  const float rrgb[3] = {gq2.x, gq2.y, gq2.z};
 
   float gxy0 = rgx, gxy1 = rgy;
   if (rad > 0 && a.grad_proj_2d) {
@@ -510,23 +537,6 @@ __global__ void __launch_bounds__(SH16 ? PB_SH16_THREADS : PB_THREADS)
       gcm[1] = vf[4] * dL_dtx + vf[5] * dL_dty + vf[6] * dL_dtz;
       gcm[2] = vf[8] * dL_dtx + vf[9] * dL_dty + vf[10] * dL_dtz;
     }
-  }
-  float gsm[3] = {0.0f, 0.0f, 0.0f};
-  if (SH16) {
-    float g[3] = {0.0f, 0.0f, 0.0f};
-    bool need = false;
-    if (work) {
-      const unsigned clamp_bits =
-          __float_as_uint(reinterpret_cast<const float4*>(a.records)[(size_t)gid * 3 + 1].w);
-      need = sh_color_grad(rrgb, clamp_bits, g);
-    }
-    sh_backward_staged(a, s_rows + (threadIdx.x & ~31) * SH_ROW_F4, gid, work, need, mean, s_cam, g,
-                       gsm);
-    if (!work) return;
-  } else if (a.sh) {
-    const unsigned clamp_bits =
-        __float_as_uint(reinterpret_cast<const float4*>(a.records)[(size_t)gid * 3 + 1].w);
-    sh_backward(a, gid, mean, s_cam, rrgb, clamp_bits, gsm);
   }
   float m0 = pm_x + gcm[0], m1 = pm_y + gcm[1], m2 = pm_z + gcm[2];
   if (SH16 || a.sh) {
