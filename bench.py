@@ -318,7 +318,18 @@ def cpu_baseline_sample(views, scene_cpu, band_rows=136):
                       f"{dt:.2f} s wall"}
 
 
-def roofline(prof, peaks, pixels, N):
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of each kernel at the default
+# workload (6M Gaussians, 1920x1080, first view), from a 1-pass ncu capture of
+# `python bench.py --steps 1 --warmup 1 --no-e2e --no-cfg2 --no-cpu-baseline --no-autograd`.
+MEASURED_TRAFFIC = {
+    "render_bwd": 262.66e6 + 32.25e6,
+    "render_fwd": 163.15e6 + 31.17e6,
+    "preprocess_bwd": 1.43e9 + 348.69e6,
+    "preprocess_fwd": 1.06e9 + 349.14e6,
+}
+
+
+def roofline(prof, peaks, pixels, N, workload_is_default=False):
     """Roofline of the dominant native kernel (by total time)."""
     if not prof:
         return None
@@ -329,9 +340,13 @@ def roofline(prof, peaks, pixels, N):
     E = extra.get("pairs", 0)
     P = extra.get("P", N)
     # algorithmic bytes per launch: per-unit bytes the stage must move x units
+    V = extra.get("binned", P)
     per_launch = {
-        "render_bwd": 44 * R + 28 * pixels + 40 * P,
-        "render_fwd": 44 * R + 24 * pixels,
+        # pair id + 48-B record per pair; n_contrib, final alpha, colour grad per pixel; 48-B accumulator per
+        # binned Gaussian, read and written
+        "render_bwd": 52 * R + 20 * pixels + 96 * V,
+        # pair id + record per pair; colour, alpha, depth, n_contrib per pixel
+        "render_fwd": 52 * R + 24 * pixels,
         "preprocess_fwd": 316 * P,
         # accumulate mode: 288 B read + 236 B read-modify-written per visible Gaussian, 4 B (radius) otherwise
         "preprocess_bwd": 760 * extra.get("visible", P) + 4 * (P - extra.get("visible", P)),
@@ -341,8 +356,9 @@ def roofline(prof, peaks, pixels, N):
     }.get(name, 0)
     peak = peaks.get("hbm_gbs", 6650.0)
     achieved = per_launch / mean_s / 1e9 if mean_s > 0 else 0.0
+    traffic = MEASURED_TRAFFIC.get(name) if workload_is_default else None
     out = {"kernel": name, "bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
-           "frac": round(achieved / peak, 4) if peak else None, "traffic": None,
+           "frac": round(achieved / peak, 4) if peak else None, "traffic": traffic,
            "mean_launch_ms": round(rec["mean_ms"], 4), "algorithmic_bytes_per_launch": per_launch,
            "peak_source": peaks.get("_source", "measured")}
     if name in ("render_bwd", "render_fwd") and E:
@@ -450,7 +466,8 @@ def run_ours(args):
 
     prof = kernel_profile(tr, steps=1)
     launches = sum(v["kernels"] for v in prof.values())
-    rl = roofline(prof, peaks, args.width * args.height, scene.n)
+    default = (args.gaussians, args.width, args.height) == (6_000_000, 1920, 1080)
+    rl = roofline(prof, peaks, args.width * args.height, scene.n, workload_is_default=default)
 
     extra = {}
     if rank == 0 and world == 1:

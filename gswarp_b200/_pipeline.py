@@ -364,6 +364,8 @@ def render_backward(pre_records, binned: Binned, cam: Camera, background, out_al
         _lib.call("gsb_render_bwd", a, _lib.stream_handle(dev))
     if TIMING_ENABLED:
         info["pairs"] = int(n_contrib.sum(dtype=torch.int64))
+        info["binned"] = int(binned.ids.numel()) if binned.ids is not None else \
+            int(torch.unique(binned.point_list).numel())
     return grad_acc
 
 
