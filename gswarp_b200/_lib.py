@@ -24,7 +24,7 @@ GSB_ERR_OVERFLOW = -2
 GSB_ERR_CUDA = -3
 GSB_ERR_TIMEOUT = -4
 
-ABI_VERSION = 7
+ABI_VERSION = 8
 RECORD_FLOATS = 12
 GRAD_FLOATS = 12
 
@@ -103,7 +103,7 @@ class PreprocessBwdArgs(ctypes.Structure):
         ("accumulate", c_int),
         ("grad_means3d", vp), ("grad_means2d", vp), ("grad_scales", vp), ("grad_rotations", vp),
         ("grad_opacity", vp), ("grad_sh", vp), ("grad_colors", vp), ("grad_cov3d", vp),
-        ("ids", vp), ("num_ids", c_int),
+        ("ids", vp), ("num_ids", c_int), ("clear_grad_acc", c_int),
     ]
 
 

@@ -341,9 +341,14 @@ def render(pre: Preprocessed, binned: Binned, cam: Camera, background: torch.Ten
 
 
 def render_backward(pre_records, binned: Binned, cam: Camera, background, out_alpha, n_contrib,
-                    grad_color, grad_depth, grad_alpha, compute_depth: bool, P: int) -> torch.Tensor:
+                    grad_color, grad_depth, grad_alpha, compute_depth: bool, P: int,
+                    grad_acc: torch.Tensor | None = None) -> torch.Tensor:
+    """Render backward into ``grad_acc`` (P,12) -- a fresh zero-filled tensor,
+    or the caller's, which must be zero (e.g. kept zero by preprocess
+    backward's clear_grad_acc)."""
     dev = pre_records.device
-    grad_acc = torch.zeros((P, _lib.GRAD_FLOATS), dtype=torch.float32, device=dev)
+    if grad_acc is None:
+        grad_acc = torch.zeros((P, _lib.GRAD_FLOATS), dtype=torch.float32, device=dev)
     if binned.num_rendered == 0 or P == 0:
         return grad_acc
     a = _lib.RenderBwdArgs()
@@ -383,7 +388,7 @@ class PreprocessGrads:
 
 def preprocess_backward(g: Gaussians, cam: Camera, radii, records, grad_acc, grad_proj_2d, grad_conic_2d,
                         grad_conic_2d_inv, out: PreprocessGrads | None = None,
-                        ids: torch.Tensor | None = None) -> PreprocessGrads:
+                        ids: torch.Tensor | None = None, clear_grad_acc: bool = False) -> PreprocessGrads:
     """Per-Gaussian backward.  With ``out`` given, gradients are added into
     its buffers (multi-view accumulation); otherwise fresh tensors are made.
     ``ids`` (accumulate mode only) restricts the work to those Gaussians --
@@ -430,6 +435,7 @@ def preprocess_backward(g: Gaussians, cam: Camera, radii, records, grad_acc, gra
     a.accumulate = int(acc)
     a.ids = _lib.ptr(ids) if ids is not None and ids.numel() else None
     a.num_ids = int(ids.numel()) if ids is not None else 0
+    a.clear_grad_acc = int(clear_grad_acc)
     if ids is not None and ids.numel() == 0:
         return out
     a.grad_means3d = _lib.ptr(out.grad_means3D)

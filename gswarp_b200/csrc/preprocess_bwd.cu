@@ -236,23 +236,40 @@ __device__ __forceinline__ void sh_backward_staged(const gsb_preprocess_bwd_args
     for (int e = 0; e < 48; ++e) row[e] = e / 3 < used ? w[e / 3] * g[e % 3] : 0.0f;
   }
   __syncwarp();
+  // Written back in chunks of SH_CHUNK float4 per lane; in accumulate mode a
+  // chunk's old values are all loaded before its stores (as above, so the
+  // loads do not wait on earlier stores).
   float4* dst_base = reinterpret_cast<float4*>(a.grad_sh);
-#pragma unroll 4
-  for (int j = lane; j < 32 * 12; j += 32) {
-    const int r = j / 12, q = j - r * 12;
-    const int row_idx = __shfl_sync(0xffffffffu, my_idx, r);
-    if (!((work_mask >> r) & 1u)) continue;
-    float4* dst = dst_base + (size_t)row_idx * 12 + q;
-    if ((need_mask >> r) & 1u) {
-      const float* sr = rows + r * SH_ROW_F + q * 4;
-      float4 v = make_float4(sr[0], sr[1], sr[2], sr[3]);
-      if (acc) {
-        const float4 o = *dst;
-        v = make_float4(o.x + v.x, o.y + v.y, o.z + v.z, o.w + v.w);
+  constexpr int SH_CHUNK = 4;
+#pragma unroll 1
+  for (int j0 = 0; j0 < 12; j0 += SH_CHUNK) {
+    float4 old[SH_CHUNK];
+    float4* dst[SH_CHUNK];
+    bool wr[SH_CHUNK], nd[SH_CHUNK];
+#pragma unroll
+    for (int c = 0; c < SH_CHUNK; ++c) {
+      const int j = (j0 + c) * 32 + lane;
+      const int r = j / 12, q = j - r * 12;
+      const int row_idx = __shfl_sync(0xffffffffu, my_idx, r);
+      wr[c] = (work_mask >> r) & 1u;
+      nd[c] = (need_mask >> r) & 1u;
+      dst[c] = dst_base + (size_t)row_idx * 12 + q;
+      old[c] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      if (acc && wr[c] && nd[c]) old[c] = *dst[c];
+    }
+#pragma unroll
+    for (int c = 0; c < SH_CHUNK; ++c) {
+      const int j = (j0 + c) * 32 + lane;
+      const int r = j / 12, q = j - r * 12;
+      if (!wr[c]) continue;
+      if (nd[c]) {
+        const float* sr = rows + r * SH_ROW_F + q * 4;
+        float4 v = make_float4(sr[0], sr[1], sr[2], sr[3]);
+        if (acc) v = make_float4(old[c].x + v.x, old[c].y + v.y, old[c].z + v.z, old[c].w + v.w);
+        *dst[c] = v;
+      } else if (!acc) {
+        *dst[c] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       }
-      *dst = v;
-    } else if (!acc) {
-      *dst = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     }
   }
   __syncwarp();
@@ -297,6 +314,16 @@ __global__ void __launch_bounds__(SH16 ? PB_SH16_THREADS : PB_THREADS)
     gq0 = ga4[0];
     gq1 = ga4[1];
     gq2 = ga4[2];
+  }
+  // Scale/rotation inputs are loaded here, ahead of the SH stage's stores
+  // (loads placed after those stores could not be moved above them).
+  float sc_in[3] = {0.0f, 0.0f, 0.0f};
+  float4 rot_in = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  if (!PRECOMP && work && rad > 0) {
+    sc_in[0] = a.scales[gid * 3 + 0];
+    sc_in[1] = a.scales[gid * 3 + 1];
+    sc_in[2] = a.scales[gid * 3 + 2];
+    rot_in = reinterpret_cast<const float4*>(a.rotations)[gid];
   }
   const float rrgb[3] = {gq2.x, gq2.y, gq2.z};
 
@@ -387,10 +414,10 @@ __global__ void __launch_bounds__(SH16 ? PB_SH16_THREADS : PB_THREADS)
                   t20 = w20 * j00 + w22 * j02;
       const float t01 = w01 * j11 + w02 * j12, t11 = w11 * j11 + w12 * j12,
                   t21 = w21 * j11 + w22 * j12;
-      const float s0 = a.scales[gid * 3 + 0] * a.scale_modifier;
-      const float s1 = a.scales[gid * 3 + 1] * a.scale_modifier;
-      const float s2 = a.scales[gid * 3 + 2] * a.scale_modifier;
-      const float4 q = reinterpret_cast<const float4*>(a.rotations)[gid];
+      const float s0 = sc_in[0] * a.scale_modifier;
+      const float s1 = sc_in[1] * a.scale_modifier;
+      const float s2 = sc_in[2] * a.scale_modifier;
+      const float4 q = rot_in;
       const float rr = q.x, xq = q.y, yq = q.z, zq = q.w;
       const float r00 = 1.0f - 2.0f * (yq * yq + zq * zq);
       const float r01 = 2.0f * (xq * yq + rr * zq);
@@ -544,23 +571,60 @@ __global__ void __launch_bounds__(SH16 ? PB_SH16_THREADS : PB_THREADS)
     m1 = m1 + gsm[1];
     m2 = m2 + gsm[2];
   }
-  store_or_add(a.grad_means3d + gid * 3 + 0, m0, acc);
-  store_or_add(a.grad_means3d + gid * 3 + 1, m1, acc);
-  store_or_add(a.grad_means3d + gid * 3 + 2, m2, acc);
-  if (a.grad_means2d) {
-    store_or_add(a.grad_means2d + gid * 3 + 0, rgx, acc);
-    store_or_add(a.grad_means2d + gid * 3 + 1, rgy, acc);
-    store_or_add(a.grad_means2d + gid * 3 + 2, 0.0f, acc);
+  // Accumulate mode: every old value is loaded before any store.  The output
+  // pointers may alias as far as the compiler knows, so interleaved
+  // read-modify-writes would each wait for the previous store to retire.
+  const bool has2 = a.grad_means2d != nullptr;
+  const bool hass = !PRECOMP && a.grad_scales != nullptr;
+  const bool hasr = !PRECOMP && a.grad_rotations != nullptr;
+  const bool hasc = PRECOMP && a.grad_cov3d != nullptr;
+  const bool haso = a.grad_opacity != nullptr;
+  float om[3] = {0.0f, 0.0f, 0.0f}, o2[3] = {0.0f, 0.0f, 0.0f}, os[3] = {0.0f, 0.0f, 0.0f};
+  float orr[4] = {0.0f, 0.0f, 0.0f, 0.0f}, oc[6] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f}, oo = 0.0f;
+  if (acc) {
+#pragma unroll
+    for (int k = 0; k < 3; ++k) om[k] = a.grad_means3d[gid * 3 + k];
+    if (has2)
+#pragma unroll
+      for (int k = 0; k < 3; ++k) o2[k] = a.grad_means2d[gid * 3 + k];
+    if (hass)
+#pragma unroll
+      for (int k = 0; k < 3; ++k) os[k] = a.grad_scales[gid * 3 + k];
+    if (hasr)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) orr[k] = a.grad_rotations[gid * 4 + k];
+    if (hasc)
+#pragma unroll
+      for (int k = 0; k < 6; ++k) oc[k] = a.grad_cov3d[gid * 6 + k];
+    if (haso) oo = a.grad_opacity[gid];
   }
-  if (!PRECOMP) {
-    if (a.grad_scales)
-      for (int k = 0; k < 3; ++k) store_or_add(a.grad_scales + gid * 3 + k, gs[k], acc);
-    if (a.grad_rotations)
-      for (int k = 0; k < 4; ++k) store_or_add(a.grad_rotations + gid * 4 + k, gr[k], acc);
-  } else if (a.grad_cov3d) {
-    for (int k = 0; k < 6; ++k) store_or_add(a.grad_cov3d + gid * 6 + k, gc3[k], acc);
+  // *p += v is *p = *p + v: the same sum in the same order.
+  const float mv[3] = {m0, m1, m2};
+#pragma unroll
+  for (int k = 0; k < 3; ++k) a.grad_means3d[gid * 3 + k] = acc ? om[k] + mv[k] : mv[k];
+  if (has2) {
+    const float v2[3] = {rgx, rgy, 0.0f};
+#pragma unroll
+    for (int k = 0; k < 3; ++k) a.grad_means2d[gid * 3 + k] = acc ? o2[k] + v2[k] : v2[k];
   }
-  if (a.grad_opacity) store_or_add(a.grad_opacity + gid, rco[3], acc);
+  if (hass)
+#pragma unroll
+    for (int k = 0; k < 3; ++k) a.grad_scales[gid * 3 + k] = acc ? os[k] + gs[k] : gs[k];
+  if (hasr)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) a.grad_rotations[gid * 4 + k] = acc ? orr[k] + gr[k] : gr[k];
+  if (hasc)
+#pragma unroll
+    for (int k = 0; k < 6; ++k) a.grad_cov3d[gid * 6 + k] = acc ? oc[k] + gc3[k] : gc3[k];
+  if (haso) a.grad_opacity[gid] = acc ? oo + rco[3] : rco[3];
+  if (a.clear_grad_acc) {
+    // last, so the zero stores do not hold back any load above
+    float4* w4 = const_cast<float4*>(ga4);
+    const float4 z = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    w4[0] = z;
+    w4[1] = z;
+    w4[2] = z;
+  }
   if (a.grad_colors)
     for (int k = 0; k < 3; ++k) store_or_add(a.grad_colors + gid * 3 + k, rrgb[k], acc);
 }

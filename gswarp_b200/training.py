@@ -125,6 +125,7 @@ class FusedViewStep:
         self.device = dev
         self.losses = torch.zeros((len(self.settings), 3), dtype=torch.float32, device=dev)
         self._staging: dict[int, torch.Tensor] = {}
+        self._grad_acc: torch.Tensor | None = None
 
     def _gaussians(self, rs) -> pl.Gaussians:
         means, scales, rots, opac, sh = self.params
@@ -154,13 +155,18 @@ class FusedViewStep:
         ren = pl.render(pre, binned, cam, bg, False)
         _, dm = photometric_loss_forward(ren.color, tgt, self.l1_weight, self.ssim_weight, out=self.losses[i])
         grad_img = photometric_loss_backward(ren.color, tgt, dm, self.l1_weight, self.ssim_weight)
+        if self._grad_acc is None or self._grad_acc.shape[0] != P:
+            self._grad_acc = torch.zeros((P, _lib.GRAD_FLOATS), dtype=torch.float32, device=self.device)
         grad_acc = pl.render_backward(pre.records, binned, cam, bg, ren.alpha, ren.n_contrib, grad_img, None, None,
-                                      False, P)
+                                      False, P, grad_acc=self._grad_acc)
         v_means, v_scales, v_rots, v_opac, v_sh = self.grads.views
         out = pl.PreprocessGrads(grad_means3D=v_means, grad_means2D=None, grad_opacity=v_opac,
                                  grad_scales=v_scales, grad_rotations=v_rots, grad_cov3D=None, grad_sh=v_sh,
                                  grad_colors=None)
-        pl.preprocess_backward(g, cam, pre.radii, pre.records, grad_acc, None, None, None, out=out, ids=binned.ids)
+        # reads each binned Gaussian's accumulator entry and zeroes it: the accumulator is all zero again
+        # for the next view (render backward only touches binned Gaussians)
+        pl.preprocess_backward(g, cam, pre.radii, pre.records, grad_acc, None, None, None, out=out, ids=binned.ids,
+                               clear_grad_acc=True)
 
     def step(self, targets: Sequence[torch.Tensor]) -> torch.Tensor:
         if len(targets) != len(self.settings):

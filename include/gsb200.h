@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define GSB_ABI_VERSION 7
+#define GSB_ABI_VERSION 8
 
 #define GSB_OK 0
 #define GSB_ERR_INVALID (-1)  /* bad argument: ValueError in Python          */
@@ -236,6 +236,9 @@ typedef struct {
                             e.g. the binned_ids of gsb_bin_count (the others get no
                             render gradient and are left untouched); NULL = all P */
   int num_ids;
+  int clear_grad_acc;    /* 1: zero each processed Gaussian's grad_acc entry after reading it,
+                            so a persistent accumulator is ready for the next view without a
+                            full memset (the render backward only touches binned Gaussians) */
 } gsb_preprocess_bwd_args;
 
 int gsb_preprocess_bwd(const gsb_preprocess_bwd_args* a, void* stream);
