@@ -271,6 +271,65 @@ def measure_cfg2(device, steps, warmup):
     return out
 
 
+def _event_ms(fn, reps, warmup):
+    import torch
+
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / reps
+
+
+def measure_small_configs(device):
+    """BASELINE configs 1, 3 and 4 through the public API (device-resident
+    inputs, CUDA events, mean over repetitions after warm-up)."""
+    import torch
+
+    import gswarp_b200 as gs
+    from gswarp_b200 import workloads as wl
+
+    out = {}
+    # config 1: 10K Gaussians SH0 at 256x256, forward + backward with dL/dcolor ~ N(0,1)
+    sc, view = wl.config1_scene(seed=0)
+    sc = sc.to(device)
+    v = view.to(device)
+    rs = gs.GaussianRasterizationSettings(
+        image_height=v.height, image_width=v.width, tanfovx=v.tanfovx, tanfovy=v.tanfovy,
+        bg=torch.zeros(3, device=device), scale_modifier=1.0, viewmatrix=v.viewmatrix, projmatrix=v.projmatrix,
+        sh_degree=0, campos=v.campos, prefiltered=False)
+    ps = [t.clone().requires_grad_(True) for t in (sc.means, sc.opacities, sc.sh, sc.scales, sc.rotations)]
+    m2d = torch.zeros_like(ps[0], requires_grad=True)
+    gcol = torch.randn(3, v.height, v.width, generator=torch.Generator().manual_seed(0)).to(device)
+
+    def cfg1():
+        color, _, _ = gs.GaussianRasterizer(rs)(ps[0], m2d, ps[1], shs=ps[2], scales=ps[3], rotations=ps[4])
+        color.backward(gcol)
+
+    out["config1_ms"] = _event_ms(cfg1, 50, 5)
+    # config 3: fused SSIM forward + backward on 4 x 3 x 1080 x 1920
+    img, tgt = wl.config3_images(seed=0)
+    img = img.to(device).requires_grad_(True)
+    tgt = tgt.to(device)
+
+    def cfg3():
+        img.grad = None
+        gs.fused_ssim(img, tgt).backward()
+
+    out["config3_ssim_fwd_bwd_ms"] = _event_ms(cfg3, 20, 3)
+    del img, tgt
+    # config 4: KNN initialiser on 2M clustered points
+    pts = wl.config4_points(seed=0).to(device)
+    out["config4_knn_ms"] = _event_ms(lambda: gs.distCUDA2(pts), 10, 2)
+    return out
+
+
 def cpu_baseline_sample(views, scene_cpu, band_rows=136):
     """Times the CPU oracle (all host threads) on one view of the workload:
     preprocess + binning of every Gaussian, then render, render backward, SSIM
@@ -475,6 +534,7 @@ def run_ours(args):
         torch.cuda.empty_cache()
         if not args.no_cfg2:
             extra["config2_single_view"] = measure_cfg2(device, max(3, args.steps), max(3, args.warmup))
+            extra["other_configs"] = measure_small_configs(device)
         if not args.no_cpu_baseline:
             scene_cpu = wl.config2_scene(seed=0, n=args.gaussians)
             extra["cpu_baseline"] = cpu_baseline_sample([views[0]], scene_cpu)
