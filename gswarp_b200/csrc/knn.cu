@@ -4,19 +4,24 @@
 // degenerate-extent widening (done here on the device in fp64, without the
 // reference's six .item() host syncs), 30-bit Morton codes (:48-67,
 // :108-119), stable radix sort of (code, index) (:334-341), gather into
-// sorted SoA, per-1024-point box AABBs (:137-162) and the box-pruned 3-NN
-// search seeded from the +-3 sorted neighbours (:165-256).
+// sorted SoA, and a box-pruned 3-NN search (:137-256).
 //
-// The pruning is exact (a box is skipped only when its lower-bound distance
-// exceeds the current third-best), so the result is the mean of the three
-// smallest squared distances whatever order boxes are visited in; this
-// kernel visits the point's own box first, which tightens the bound early.
-// Built with -fmad=false so distances match the CPU oracle bit for bit.
+// The pruning is exact: a group of candidates is skipped only when a lower
+// bound of its squared distance exceeds the current third-best, and every
+// bound is computed with the same monotone float operations (no FMA
+// contraction, -fmad=false) as the point distances it bounds, so the result
+// is the mean of the three smallest squared distances whatever order
+// candidates are visited in -- bit for bit the reference's value.
 //
-// B200 layout: box AABBs are computed with one CTA per box (block min/max
-// reductions instead of the reference's 6 float atomics per point) and are
-// staged in shared memory by every search CTA (24 bytes per box: up to 9,000
-// boxes = 9.2M points fit in 227 KB; larger inputs read them from L2).
+// B200 layout: the sorted points are grouped into leaves of 32 (one per
+// lane), parents of 32 leaves (the reference's 1024-point boxes) and
+// grandparents of 32 parents, each with an AABB.  One warp searches for the
+// 32 consecutive sorted points of a leaf: it scans its own leaf, then walks
+// grandparents -> parents -> leaves, testing 32 boxes per step (one per
+// lane) against the warp's query AABB and its largest third-best, and scans
+// a surviving leaf by broadcasting its 32 points with shuffles to every lane
+// that still needs it (the reference instead tests every 1024-point box per
+// point and scans boxes point by point).
 #include <algorithm>
 
 #include "gsb_common.cuh"
@@ -25,7 +30,6 @@
 namespace gsb {
 namespace {
 
-constexpr int BOX = 1024;
 constexpr int BOUNDS_BLOCKS = 296;
 constexpr float FLT_BIG_K = 3.402823466e38f;
 
@@ -110,53 +114,73 @@ __global__ void morton_kernel(int P, const float* __restrict__ pts,
   idx[i] = (unsigned)i;
 }
 
-// One CTA per 1024-point box: gather sorted SoA and the box AABB.
-__global__ void __launch_bounds__(256) gather_box_kernel(int P, const float* __restrict__ pts,
-                                                         const unsigned* __restrict__ order,
-                                                         float* __restrict__ sx,
-                                                         float* __restrict__ sy,
-                                                         float* __restrict__ sz,
-                                                         float* __restrict__ boxes) {
-  const int b = blockIdx.x;
-  float lo[3] = {INFINITY, INFINITY, INFINITY}, hi[3] = {-INFINITY, -INFINITY, -INFINITY};
-  for (int k = threadIdx.x; k < BOX; k += 256) {
-    const int i = b * BOX + k;
-    if (i >= P) break;
+constexpr int LEAF = 32;  // points per leaf (one per lane); 32 leaves per parent, 32 parents per grandparent
+
+// Thread per sorted point: gather the sorted SoA; each warp (= one leaf of
+// 32 consecutive sorted points) reduces its AABB.
+__global__ void __launch_bounds__(256) gather_leaf_kernel(int P, const float* __restrict__ pts,
+                                                          const unsigned* __restrict__ order,
+                                                          float* __restrict__ sx, float* __restrict__ sy,
+                                                          float* __restrict__ sz, float* __restrict__ leaf_boxes) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  const int leaf = i / LEAF;
+  if (leaf * LEAF >= P) return;  // whole warp past the end
+  float v[3] = {0.0f, 0.0f, 0.0f};
+  const bool valid = i < P;
+  if (valid) {
     const unsigned o = order[i];
-    const float v[3] = {pts[(size_t)o * 3], pts[(size_t)o * 3 + 1], pts[(size_t)o * 3 + 2]};
+    v[0] = pts[(size_t)o * 3];
+    v[1] = pts[(size_t)o * 3 + 1];
+    v[2] = pts[(size_t)o * 3 + 2];
     sx[i] = v[0];
     sy[i] = v[1];
     sz[i] = v[2];
-#pragma unroll
-    for (int c = 0; c < 3; ++c) {
-      lo[c] = fminf(lo[c], v[c]);
-      hi[c] = fmaxf(hi[c], v[c]);
-    }
   }
-  __shared__ float s[6][8];
+  float lo[3], hi[3];
 #pragma unroll
   for (int c = 0; c < 3; ++c) {
+    lo[c] = valid ? v[c] : INFINITY;
+    hi[c] = valid ? v[c] : -INFINITY;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       lo[c] = fminf(lo[c], __shfl_xor_sync(0xffffffffu, lo[c], o));
       hi[c] = fmaxf(hi[c], __shfl_xor_sync(0xffffffffu, hi[c], o));
     }
   }
-  if ((threadIdx.x & 31) == 0)
-    for (int c = 0; c < 3; ++c) {
-      s[c][threadIdx.x >> 5] = lo[c];
-      s[3 + c][threadIdx.x >> 5] = hi[c];
-    }
-  __syncthreads();
-  if (threadIdx.x < 6) {
-    float r = s[threadIdx.x][0];
-    for (int w = 1; w < 8; ++w)
-      r = threadIdx.x < 3 ? fminf(r, s[threadIdx.x][w]) : fmaxf(r, s[threadIdx.x][w]);
-    boxes[(size_t)b * 6 + threadIdx.x] = r;  // minx,miny,minz,maxx,maxy,maxz
+  if ((threadIdx.x & 31) == 0) {
+    float* b = leaf_boxes + (size_t)leaf * 6;
+    b[0] = lo[0]; b[1] = lo[1]; b[2] = lo[2];
+    b[3] = hi[0]; b[4] = hi[1]; b[5] = hi[2];
   }
 }
 
-// knn.py:71-100
+// Warp per parent box: AABB of up to 32 child boxes.
+__global__ void __launch_bounds__(256) reduce_boxes_kernel(int nchild, const float* __restrict__ child,
+                                                           float* __restrict__ parent) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  const int par = t / 32, lane = threadIdx.x & 31;
+  if (par * 32 >= nchild) return;
+  const int c = par * 32 + lane;
+  const bool valid = c < nchild;
+  float lo[3], hi[3];
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    lo[k] = valid ? child[(size_t)c * 6 + k] : INFINITY;
+    hi[k] = valid ? child[(size_t)c * 6 + 3 + k] : -INFINITY;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      lo[k] = fminf(lo[k], __shfl_xor_sync(0xffffffffu, lo[k], o));
+      hi[k] = fmaxf(hi[k], __shfl_xor_sync(0xffffffffu, hi[k], o));
+    }
+  }
+  if (lane == 0) {
+    float* b = parent + (size_t)par * 6;
+    b[0] = lo[0]; b[1] = lo[1]; b[2] = lo[2];
+    b[3] = hi[0]; b[4] = hi[1]; b[5] = hi[2];
+  }
+}
+
+// knn.py:71-100: squared distance from a point to an AABB (0 inside).
 __device__ __forceinline__ float box_dist(const float* bx, float px, float py, float pz) {
   float dx = 0.0f, dy = 0.0f, dz = 0.0f;
   if (px < bx[0] || px > bx[3]) {
@@ -174,6 +198,20 @@ __device__ __forceinline__ float box_dist(const float* bx, float px, float py, f
   return dx * dx + dy * dy + dz * dz;
 }
 
+// Squared distance between two AABBs (0 when they overlap): a lower bound
+// of every point-to-point distance between them, computed with the same
+// rounding-monotone operations as those distances.
+__device__ __forceinline__ float boxbox_dist(const float* a, const float* b) {
+  float d[3];
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    d[k] = 0.0f;
+    if (a[k] > b[3 + k]) d[k] = a[k] - b[3 + k];
+    else if (b[k] > a[3 + k]) d[k] = b[k] - a[3 + k];
+  }
+  return d[0] * d[0] + d[1] * d[1] + d[2] * d[2];
+}
+
 __device__ __forceinline__ void push3(float d, float& b0, float& b1, float& b2) {
   if (d < b0) {
     b2 = b1;
@@ -187,56 +225,74 @@ __device__ __forceinline__ void push3(float d, float& b0, float& b1, float& b2) 
   }
 }
 
-__device__ __forceinline__ void scan_box(int b, int P, int idx, float px, float py, float pz,
-                                         const float* __restrict__ sx, const float* __restrict__ sy,
-                                         const float* __restrict__ sz, float& b0, float& b1,
-                                         float& b2) {
-  const int e = min(P, (b + 1) * BOX);
-  for (int i = b * BOX; i < e; ++i) {
-    if (i == idx) continue;
-    const float dx = px - __ldg(sx + i), dy = py - __ldg(sy + i), dz = pz - __ldg(sz + i);
-    push3(dx * dx + dy * dy + dz * dz, b0, b1, b2);
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Scan leaf L for the lanes with `need`: lane j holds the leaf's point j and
+// broadcasts it; the query's own index is skipped.
+__device__ __forceinline__ void scan_leaf(int L, int P, int my_idx, bool need, float px, float py, float pz,
+                                          const float* __restrict__ sx, const float* __restrict__ sy,
+                                          const float* __restrict__ sz, float& b0, float& b1, float& b2) {
+  const int lane = threadIdx.x & 31;
+  const int c = L * LEAF + lane;
+  const bool cv = c < P;
+  const float cx = cv ? sx[c] : 0.0f, cy = cv ? sy[c] : 0.0f, cz = cv ? sz[c] : 0.0f;
+  const int n = min(LEAF, P - L * LEAF);
+  for (int k = 0; k < n; ++k) {
+    const float qx = __shfl_sync(0xffffffffu, cx, k);
+    const float qy = __shfl_sync(0xffffffffu, cy, k);
+    const float qz = __shfl_sync(0xffffffffu, cz, k);
+    if (need && L * LEAF + k != my_idx) {
+      const float dx = px - qx, dy = py - qy, dz = pz - qz;
+      push3(dx * dx + dy * dy + dz * dz, b0, b1, b2);
+    }
   }
 }
 
-template <bool SMEM_BOXES>
-__global__ void __launch_bounds__(256) search_kernel(int P, int nb, const float* __restrict__ sx,
-                                                     const float* __restrict__ sy,
-                                                     const float* __restrict__ sz,
-                                                     const float* __restrict__ boxes_g,
-                                                     const unsigned* __restrict__ order,
-                                                     float* __restrict__ out) {
-  extern __shared__ float s_boxes[];
-  const float* boxes = boxes_g;
-  if (SMEM_BOXES) {
-    for (int i = threadIdx.x; i < nb * 6; i += blockDim.x) s_boxes[i] = boxes_g[i];
-    __syncthreads();
-    boxes = s_boxes;
-  }
-  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= P) return;
-  const float px = sx[idx], py = sy[idx], pz = sz[idx];
+// One warp per query leaf.  Boxes: leaves (nl), parents (np), grandparents (ng).
+__global__ void __launch_bounds__(256) search_kernel(int P, int nl, int np, int ng, const float* __restrict__ sx,
+                                                     const float* __restrict__ sy, const float* __restrict__ sz,
+                                                     const float* __restrict__ leaf_b, const float* __restrict__ par_b,
+                                                     const float* __restrict__ gp_b,
+                                                     const unsigned* __restrict__ order, float* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int qleaf = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  if (qleaf >= nl) return;  // whole warp
+  const int my_idx = qleaf * LEAF + lane;
+  const bool valid = my_idx < P;
+  const float px = valid ? sx[my_idx] : 0.0f, py = valid ? sy[my_idx] : 0.0f, pz = valid ? sz[my_idx] : 0.0f;
   float b0 = FLT_BIG_K, b1 = FLT_BIG_K, b2 = FLT_BIG_K;
-  const int lo = max(0, idx - 3), hi = min(P - 1, idx + 3);
-  for (int i = lo; i <= hi; ++i) {
-    if (i == idx) continue;
-    const float dx = px - sx[i], dy = py - sy[i], dz = pz - sz[i];
-    push3(dx * dx + dy * dy + dz * dz, b0, b1, b2);
+  // 1. the query's own leaf (its Morton neighbours): a first third-best.
+  scan_leaf(qleaf, P, my_idx, valid, px, py, pz, sx, sy, sz, b0, b1, b2);
+  const float* qb = leaf_b + (size_t)qleaf * 6;  // the warp's query AABB
+  const int own_par = qleaf / 32, own_gp = own_par / 32;
+  // 2. grandparents, own first; parents and leaves below them, tested 32 at a time.
+  for (int gi = 0; gi < ng; ++gi) {
+    const int g = gi == 0 ? own_gp : (gi <= own_gp ? gi - 1 : gi);
+    float mb2 = warp_max(valid ? b2 : 0.0f);
+    if (boxbox_dist(qb, gp_b + (size_t)g * 6) > mb2) continue;
+    const int pidx = g * 32 + lane;
+    unsigned pmask = __ballot_sync(0xffffffffu, pidx < np && boxbox_dist(qb, par_b + (size_t)pidx * 6) <= mb2);
+    while (pmask) {
+      const int pp = g * 32 + __ffs(pmask) - 1;
+      pmask &= pmask - 1;
+      mb2 = warp_max(valid ? b2 : 0.0f);
+      const int lidx = pp * 32 + lane;
+      unsigned lmask = __ballot_sync(0xffffffffu, lidx < nl && lidx != qleaf &&
+                                                      boxbox_dist(qb, leaf_b + (size_t)lidx * 6) <= mb2);
+      while (lmask) {
+        const int L = pp * 32 + __ffs(lmask) - 1;
+        lmask &= lmask - 1;
+        const bool need = valid && !(box_dist(leaf_b + (size_t)L * 6, px, py, pz) > b2);
+        if (!__any_sync(0xffffffffu, need)) continue;
+        scan_leaf(L, P, my_idx, need, px, py, pz, sx, sy, sz, b0, b1, b2);
+      }
+    }
   }
-  const float reject = b2;
-  b0 = b1 = b2 = FLT_BIG_K;
-  const int own = idx / BOX;
-  {
-    const float bd = box_dist(boxes + own * 6, px, py, pz);
-    if (!(bd > reject || bd > b2)) scan_box(own, P, idx, px, py, pz, sx, sy, sz, b0, b1, b2);
-  }
-  for (int b = 0; b < nb; ++b) {
-    if (b == own) continue;
-    const float bd = box_dist(boxes + b * 6, px, py, pz);
-    if (bd > reject || bd > b2) continue;
-    scan_box(b, P, idx, px, py, pz, sx, sy, sz, b0, b1, b2);
-  }
-  out[order[idx]] = (b0 + b1 + b2) / 3.0f;
+  if (valid) out[order[my_idx]] = (b0 + b1 + b2) / 3.0f;
 }
 
 inline size_t a256(size_t b) { return (b + 255) & ~(size_t)255; }
@@ -248,10 +304,10 @@ using namespace gsb;
 
 GSB_EXPORT size_t gsb_knn_workspace_bytes(int P) {
   const size_t n = (size_t)(P > 0 ? P : 1);
-  const size_t nb = (n + BOX - 1) / BOX;
+  const size_t nl = (n + LEAF - 1) / LEAF, np = (nl + 31) / 32, ng = (np + 31) / 32;
   size_t b = a256(n * 4) * 4;        // codes, codes_alt, idx, idx_alt
   b += a256(n * 4) * 3;              // sx, sy, sz
-  b += a256(nb * 6 * 4);             // boxes
+  b += a256(nl * 6 * 4) + a256(np * 6 * 4) + a256(ng * 6 * 4);  // leaf, parent, grandparent boxes
   b += a256((size_t)BOUNDS_BLOCKS * 6 * 4) + 256;  // partials + bounds
   b += radix::scratch_bytes((long long)n, 4);
   return b + 256;
@@ -264,7 +320,7 @@ GSB_EXPORT int gsb_knn(const gsb_knn_args* a, void* stream) {
     return GSB_ERR_INVALID;
   }
   const int P = a->P;
-  const int nb = (P + BOX - 1) / BOX;
+  const int nl = (P + LEAF - 1) / LEAF, np = (nl + 31) / 32, ng = (np + 31) / 32;
   cudaStream_t s = (cudaStream_t)stream;
   char* w = (char*)(((uintptr_t)a->workspace + 255) & ~(uintptr_t)255);
   auto take = [&](size_t bytes) {
@@ -279,7 +335,9 @@ GSB_EXPORT int gsb_knn(const gsb_knn_args* a, void* stream) {
   float* sx = (float*)take((size_t)P * 4);
   float* sy = (float*)take((size_t)P * 4);
   float* sz = (float*)take((size_t)P * 4);
-  float* boxes = (float*)take((size_t)nb * 6 * 4);
+  float* leaf_b = (float*)take((size_t)nl * 6 * 4);
+  float* par_b = (float*)take((size_t)np * 6 * 4);
+  float* gp_b = (float*)take((size_t)ng * 6 * 4);
   float* part = (float*)take((size_t)BOUNDS_BLOCKS * 6 * 4);
   float* bounds = (float*)take(256);
   void* scratch = w;
@@ -291,14 +349,10 @@ GSB_EXPORT int gsb_knn(const gsb_knn_args* a, void* stream) {
   unsigned* vb[2] = {idx, idx_alt};
   const int where = radix::sort_pairs(kb, vb, P, nullptr, 4, scratch, a->error_word, s);
   const unsigned* order = vb[where];
-  gather_box_kernel<<<nb, 256, 0, s>>>(P, a->points, order, sx, sy, sz, boxes);
-  const size_t smem = (size_t)nb * 6 * 4;
-  if (smem <= 200 * 1024) {
-    cudaFuncSetAttribute(search_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem);
-    search_kernel<true><<<div_up(P, 256), 256, smem, s>>>(P, nb, sx, sy, sz, boxes, order, a->out);
-  } else {
-    search_kernel<false><<<div_up(P, 256), 256, 0, s>>>(P, nb, sx, sy, sz, boxes, order, a->out);
-  }
+  gather_leaf_kernel<<<div_up((long long)nl * LEAF, 256), 256, 0, s>>>(P, a->points, order, sx, sy, sz, leaf_b);
+  reduce_boxes_kernel<<<div_up((long long)np * 32, 256), 256, 0, s>>>(nl, leaf_b, par_b);
+  reduce_boxes_kernel<<<div_up((long long)ng * 32, 256), 256, 0, s>>>(np, par_b, gp_b);
+  search_kernel<<<div_up((long long)nl * 32, 256), 256, 0, s>>>(P, nl, np, ng, sx, sy, sz, leaf_b, par_b, gp_b,
+                                                                order, a->out);
   return check_launch("gsb_knn");
 }

@@ -90,3 +90,11 @@ def test_knn_config4_subset(cuda):
     got = gs.distCUDA2(pts.to(cuda)).cpu().numpy()
     want, _ = oracle.knn(pts.numpy())
     np.testing.assert_array_equal(got, want)
+
+
+def test_knn_config4_full(cuda):
+    """The full config-4 input (2M clustered points): bit-exact against the oracle."""
+    pts = wl.config4_points(seed=0)
+    got = gs.distCUDA2(pts.to(cuda)).cpu().numpy()
+    want, _ = oracle.knn(pts.numpy())
+    np.testing.assert_array_equal(got, want)
