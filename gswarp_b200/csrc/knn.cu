@@ -268,27 +268,39 @@ __global__ void __launch_bounds__(256) search_kernel(int P, int nl, int np, int 
   // 1. the query's own leaf (its Morton neighbours): a first third-best.
   scan_leaf(qleaf, P, my_idx, valid, px, py, pz, sx, sy, sz, b0, b1, b2);
   const float* qb = leaf_b + (size_t)qleaf * 6;  // the warp's query AABB
+  // 2. two walks over grandparents -> parents -> leaves, 32 boxes tested at a
+  // time against the warp's query AABB: the first visits only leaves whose
+  // box overlaps the query AABB (the local neighbourhood, which brings every
+  // lane's third-best down quickly), the second every other leaf that its
+  // lower bound does not rule out.  A leaf is scanned at most once: the
+  // second walk skips exactly the leaves the first one visited.
   const int own_par = qleaf / 32, own_gp = own_par / 32;
-  // 2. grandparents, own first; parents and leaves below them, tested 32 at a time.
-  for (int gi = 0; gi < ng; ++gi) {
-    const int g = gi == 0 ? own_gp : (gi <= own_gp ? gi - 1 : gi);
-    float mb2 = warp_max(valid ? b2 : 0.0f);
-    if (boxbox_dist(qb, gp_b + (size_t)g * 6) > mb2) continue;
-    const int pidx = g * 32 + lane;
-    unsigned pmask = __ballot_sync(0xffffffffu, pidx < np && boxbox_dist(qb, par_b + (size_t)pidx * 6) <= mb2);
-    while (pmask) {
-      const int pp = g * 32 + __ffs(pmask) - 1;
-      pmask &= pmask - 1;
-      mb2 = warp_max(valid ? b2 : 0.0f);
-      const int lidx = pp * 32 + lane;
-      unsigned lmask = __ballot_sync(0xffffffffu, lidx < nl && lidx != qleaf &&
-                                                      boxbox_dist(qb, leaf_b + (size_t)lidx * 6) <= mb2);
-      while (lmask) {
-        const int L = pp * 32 + __ffs(lmask) - 1;
-        lmask &= lmask - 1;
-        const bool need = valid && !(box_dist(leaf_b + (size_t)L * 6, px, py, pz) > b2);
-        if (!__any_sync(0xffffffffu, need)) continue;
-        scan_leaf(L, P, my_idx, need, px, py, pz, sx, sy, sz, b0, b1, b2);
+  for (int pass = 0; pass < 2; ++pass) {
+    for (int gi = 0; gi < ng; ++gi) {
+      const int g = gi == 0 ? own_gp : (gi <= own_gp ? gi - 1 : gi);
+      float mb2 = pass == 0 ? 0.0f : warp_max(valid ? b2 : 0.0f);
+      if (boxbox_dist(qb, gp_b + (size_t)g * 6) > mb2) continue;
+      const int pidx = g * 32 + lane;
+      unsigned pmask =
+          __ballot_sync(0xffffffffu, pidx < np && boxbox_dist(qb, par_b + (size_t)pidx * 6) <= mb2);
+      while (pmask) {
+        const int pp = g * 32 + __ffs(pmask) - 1;
+        pmask &= pmask - 1;
+        if (pass == 1) mb2 = warp_max(valid ? b2 : 0.0f);
+        const int lidx = pp * 32 + lane;
+        bool lneed = false;
+        if (lidx < nl && lidx != qleaf) {
+          const float d = boxbox_dist(qb, leaf_b + (size_t)lidx * 6);
+          lneed = pass == 0 ? d == 0.0f : (d > 0.0f && d <= mb2);
+        }
+        unsigned lmask = __ballot_sync(0xffffffffu, lneed);
+        while (lmask) {
+          const int L = pp * 32 + __ffs(lmask) - 1;
+          lmask &= lmask - 1;
+          const bool need = valid && !(box_dist(leaf_b + (size_t)L * 6, px, py, pz) > b2);
+          if (!__any_sync(0xffffffffu, need)) continue;
+          scan_leaf(L, P, my_idx, need, px, py, pz, sx, sy, sz, b0, b1, b2);
+        }
       }
     }
   }
