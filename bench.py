@@ -236,12 +236,17 @@ def kernel_profile(trainer, steps=2):
 
     _pipeline.TIMERS.clear()
     _pipeline.TIMING_ENABLED = True
+    fused = getattr(trainer, "fused", None)
+    if fused is not None:
+        fused.concurrent_views = False  # stage events measure one kernel at a time
     try:
         for _ in range(steps):
             trainer.step()
         torch.cuda.synchronize()
     finally:
         _pipeline.TIMING_ENABLED = False
+        if fused is not None:
+            fused.concurrent_views = True
     out = {}
     for name, evs in _pipeline.TIMERS.items():
         ts = [a.elapsed_time(b) for a, b, _ in evs]

@@ -125,7 +125,10 @@ class FusedViewStep:
         self.device = dev
         self.losses = torch.zeros((len(self.settings), 3), dtype=torch.float32, device=dev)
         self._staging: dict[int, torch.Tensor] = {}
-        self._grad_acc: torch.Tensor | None = None
+        self._grad_acc: list[torch.Tensor | None] = [None, None]
+        self._side: torch.cuda.Stream | None = None
+        # two streams in turn (overlapping consecutive views); False = one stream
+        self.concurrent_views = True
 
     def _gaussians(self, rs) -> pl.Gaussians:
         means, scales, rots, opac, sh = self.params
@@ -141,9 +144,13 @@ class FusedViewStep:
         buf.copy_(t, non_blocking=True)
         return buf
 
-    def view(self, i: int, target: torch.Tensor) -> None:
-        """Forward + loss + backward of view ``i``; gradients are added into
-        the flat buffer and the view's loss row into ``self.losses[i]``."""
+    def view(self, i: int, target: torch.Tensor, before_accumulate: torch.cuda.Event | None = None,
+             lane: int = 0) -> None:
+        """Forward + loss + backward of view ``i`` on the current stream;
+        gradients are added into the flat buffer and the view's loss row
+        into ``self.losses[i]``.  ``before_accumulate`` (if given) is waited
+        for just before the accumulation into the flat buffer; ``lane``
+        picks the render-gradient accumulator (one per concurrent stream)."""
         rs, cam, mode, bg = self.settings[i], self.cams[i], self.modes[i], self.bgs[i]
         g = self._gaussians(rs)
         P = g.P
@@ -155,25 +162,47 @@ class FusedViewStep:
         ren = pl.render(pre, binned, cam, bg, False)
         _, dm = photometric_loss_forward(ren.color, tgt, self.l1_weight, self.ssim_weight, out=self.losses[i])
         grad_img = photometric_loss_backward(ren.color, tgt, dm, self.l1_weight, self.ssim_weight)
-        if self._grad_acc is None or self._grad_acc.shape[0] != P:
-            self._grad_acc = torch.zeros((P, _lib.GRAD_FLOATS), dtype=torch.float32, device=self.device)
+        acc_buf = self._grad_acc[lane]
+        if acc_buf is None or acc_buf.shape[0] != P:
+            acc_buf = torch.zeros((P, _lib.GRAD_FLOATS), dtype=torch.float32, device=self.device)
+            self._grad_acc[lane] = acc_buf
         grad_acc = pl.render_backward(pre.records, binned, cam, bg, ren.alpha, ren.n_contrib, grad_img, None, None,
-                                      False, P, grad_acc=self._grad_acc)
+                                      False, P, grad_acc=acc_buf)
         v_means, v_scales, v_rots, v_opac, v_sh = self.grads.views
         out = pl.PreprocessGrads(grad_means3D=v_means, grad_means2D=None, grad_opacity=v_opac,
                                  grad_scales=v_scales, grad_rotations=v_rots, grad_cov3D=None, grad_sh=v_sh,
                                  grad_colors=None)
+        if before_accumulate is not None:
+            torch.cuda.current_stream(self.device).wait_event(before_accumulate)
         # reads each binned Gaussian's accumulator entry and zeroes it: the accumulator is all zero again
         # for the next view (render backward only touches binned Gaussians)
         pl.preprocess_backward(g, cam, pre.radii, pre.records, grad_acc, None, None, None, out=out, ids=binned.ids,
                                clear_grad_acc=True)
 
     def step(self, targets: Sequence[torch.Tensor]) -> torch.Tensor:
+        """Runs every view, then the all-reduce.  Consecutive views go to two
+        streams in turn, so one view's compute-bound render kernels overlap
+        the next view's memory- and latency-bound preprocess and binning;
+        the accumulations into the flat gradient buffer stay in view order
+        (each waits for the previous one)."""
         if len(targets) != len(self.settings):
             raise ValueError(f"expected {len(self.settings)} targets, got {len(targets)}")
         with torch.cuda.device(self.device):
+            main = torch.cuda.current_stream(self.device)
+            if self._side is None:
+                self._side = torch.cuda.Stream(self.device)
+            streams = (main, self._side) if self.concurrent_views else (main, main)
             self.grads.zero_()
+            ready = torch.cuda.Event()
+            ready.record(main)
+            self._side.wait_event(ready)  # zeroed buffer, targets and parameters visible to both streams
+            prev = None
             for i, t in enumerate(targets):
-                self.view(i, t)
+                s = streams[i % 2]
+                with torch.cuda.stream(s):
+                    self.view(i, t, before_accumulate=prev, lane=i % 2)
+                    prev = torch.cuda.Event()
+                    prev.record(s)
+            main.wait_event(prev)
             self.grads.all_reduce(self.group)
         return self.losses
