@@ -350,7 +350,7 @@ __device__ __forceinline__ bool bwd_pixel(BwdPixel& s, const float4 cf, float ax
 // DEPTH: compute_depth with a depth gradient given; GA: an alpha gradient
 // given.  Without them those terms are exactly zero and are not evaluated.
 template <bool DEPTH, bool GA>
-__global__ void __launch_bounds__(THREADS) render_bwd_kernel(const gsb_render_bwd_args a, int gx) {
+__global__ void __launch_bounds__(THREADS, 6) render_bwd_kernel(const gsb_render_bwd_args a, int gx) {
   __shared__ int s_id[BATCH];
   __shared__ float2 s_xy[BATCH];
   __shared__ float4 s_cf[BATCH];    // power coefficients, opacity in .w
@@ -402,6 +402,21 @@ __global__ void __launch_bounds__(THREADS) render_bwd_kernel(const gsb_render_bw
 
   const float half_w = 0.5f * (float)a.W;
   const float half_h = 0.5f * (float)a.H;
+  // Which reduced term this lane writes (a lane constant): its accumulator
+  // offset and the Gaussian-constant factor op * my_mul_op + my_mul_one
+  // (-op W/2 for x, -op H/2 for y, -op/2 for the conic, 1 otherwise).
+  bool my_writer;
+  int my_off;
+  float my_mul_op, my_mul_one;
+  {
+    float dummy[10] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+    float unused;
+    const int slot = warp_reduce10(dummy, unused);
+    my_writer = !(lane & 1) && slot >= 0 && (DEPTH || slot != 2);
+    my_off = slot < 3 ? slot : slot + 1;
+    my_mul_op = slot == 0 ? -half_w : slot == 1 ? -half_h : (slot >= 3 && slot <= 5) ? -0.5f : 0.0f;
+    my_mul_one = (slot == 2 || slot >= 6) ? 1.0f : 0.0f;
+  }
   const float fx = (float)pxi;
   const float bx0 = (float)(__shfl_sync(FULL, pxi, 0)), by0 = (float)(__shfl_sync(FULL, py0, 0));
   const float bx1 = bx0 + 7.0f, by1 = by0 + 7.0f;
@@ -468,15 +483,10 @@ __global__ void __launch_bounds__(THREADS) render_bwd_kernel(const gsb_render_bw
         v[8] = m.dcol1;
         v[9] = m.dcol2;
         float sum;
-        const int slot = warp_reduce10(v, sum);
-        if (!(lane & 1) && slot >= 0) {
-          const float op = s_cf[j].w;
-          float scale = 1.0f;
-          if (slot == 0) scale = -op * half_w;
-          else if (slot == 1) scale = -op * half_h;
-          else if (slot >= 3 && slot <= 5) scale = -0.5f * op;
-          const int off = slot < 3 ? slot : slot + 1;
-          if (DEPTH || slot != 2) atomicAdd(a.grad_acc + (size_t)s_id[j] * GSB_GRAD_FLOATS + off, sum * scale);
+        warp_reduce10(v, sum);
+        if (my_writer) {
+          const float scale = fmaf(s_cf[j].w, my_mul_op, my_mul_one);
+          atomicAdd(a.grad_acc + (size_t)s_id[j] * GSB_GRAD_FLOATS + my_off, sum * scale);
         }
       }
       }

@@ -144,3 +144,17 @@ def test_fused_step_parameter_grads_alias_flat_buffer(cuda):
         step.step(targets + targets)
     with pytest.raises(ValueError):
         FusedViewStep(ps[:4], settings)
+
+
+def test_fused_step_concurrent_views_match_serial(cuda):
+    """Two streams in turn give the same losses and (up to atomic order) the same gradients as one stream."""
+    params, settings, targets = _scene(cuda, 50_000, 5, 320, 192)
+    a = FusedViewStep([p.clone() for p in params], settings)
+    a.concurrent_views = False
+    la = a.step(targets).clone()
+    ga = a.grads.flat.clone()
+    b = FusedViewStep([p.clone() for p in params], settings)
+    lb = b.step(targets)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(la, lb, rtol=1e-6, atol=1e-7)
+    assert float((b.grads.flat - ga).norm()) <= 1e-4 * float(ga.norm()) + 1e-7
