@@ -203,23 +203,35 @@ struct EmitPairs {
 };
 
 // Emit from the 32-byte binning records written by preprocess: one random
-// 32-byte read per Gaussian; the pair count is the difference of adjacent
-// inclusive offsets (both coalesced).
+// 32-byte read per Gaussian, then the recorded tiles are written out (the
+// AccuTile arithmetic is not repeated, except for the rare records with more
+// than BINREC_MAX_BANDS bands, which re-run the sweep from the render
+// record).  The pair count is the difference of adjacent inclusive offsets
+// (both coalesced).
 __global__ void __launch_bounds__(256) emit_binrec_kernel(
     const long long* __restrict__ n_dev, int gx, int mode, const int* __restrict__ order,
-    const int* __restrict__ offsets, const float4* __restrict__ bin_records, unsigned* __restrict__ keys,
-    unsigned* __restrict__ vals, long long* __restrict__ err) {
+    const int* __restrict__ offsets, const uint4* __restrict__ bin_records, const float4* __restrict__ records,
+    unsigned* __restrict__ keys, unsigned* __restrict__ vals, long long* __restrict__ err) {
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= *n_dev) return;
   const int end = offsets[r];
   const int n = end - (r > 0 ? offsets[r - 1] : 0);
   if (n <= 0) return;
   const int p = order[r];
-  float px, py, ca, cb, cc, t;
-  Rect rect;
-  load_bin_record(bin_records + (size_t)p * 2, px, py, ca, cb, cc, t, rect);
+  const uint4 a = __ldg(bin_records + (size_t)p * 2), b = __ldg(bin_records + (size_t)p * 2 + 1);
+  const unsigned w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+  float px = 0.0f, py = 0.0f, ca = 0.0f, cb = 0.0f, cc = 0.0f, t = 0.0f;
+  if ((w[2] & 3u) == BINREC_SWEEP) {
+    const float4 q0 = __ldg(records + (size_t)p * 3), q1 = __ldg(records + (size_t)p * 3 + 1);
+    px = q0.x;
+    py = q0.y;
+    ca = q0.z;
+    cb = q0.w;
+    cc = q1.x;
+    t = opacity_threshold(q1.y);
+  }
   EmitPairs e{keys, vals, (long long)end - n, n, p, 0};
-  cover_tiles_in_rect(px, py, ca, cb, cc, t, rect, gx, mode, e);
+  emit_record(w, gx, mode, px, py, ca, cb, cc, t, e);
   if (e.k != n) atomicOr((unsigned long long*)err, (unsigned long long)ERR_EMIT_MISMATCH);
 }
 
@@ -368,7 +380,7 @@ GSB_EXPORT int gsb_bin_emit_sort(const gsb_bin_sort_args* a, void* stream) {
   if (R == 0 || a->P == 0) return check_launch("gsb_bin_emit_sort(empty)");
   const bool binrec = a->bin_records != nullptr;
   if (!a->depth_order || !a->point_offsets || !a->point_list || !a->workspace ||
-      (!binrec && (!a->radii || !a->records || !a->conic_2d_inv || !a->tiles_touched)) ||
+      !a->records || (!binrec && (!a->radii || !a->conic_2d_inv || !a->tiles_touched)) ||
       a->workspace_bytes < gsb_bin_sort_workspace_bytes(R, a->W, a->H)) {
     set_error("gsb_bin_emit_sort: null pointer or workspace too small");
     return GSB_ERR_INVALID;
@@ -402,7 +414,8 @@ GSB_EXPORT int gsb_bin_emit_sort(const gsb_bin_sort_args* a, void* stream) {
   if (binrec)
     emit_binrec_kernel<<<div_up(a->P, 256), 256, 0, s>>>(
         a->bin_status + 2, gx, a->coverage_mode, a->depth_order, a->point_offsets,
-        reinterpret_cast<const float4*>(a->bin_records), kb[0], vb[0], a->error_word);
+        reinterpret_cast<const uint4*>(a->bin_records), reinterpret_cast<const float4*>(a->records), kb[0],
+        vb[0], a->error_word);
   else
     emit_kernel<<<div_up(a->P, 256), 256, 0, s>>>(
         a->bin_status + 2, gx, gy, a->coverage_mode, a->depth_order, a->point_offsets, a->tiles_touched, a->radii,

@@ -214,29 +214,99 @@ __device__ __forceinline__ int cover_tiles(float px, float py, float cov_aa, flo
   return cover_tiles_in_rect(px, py, ca, cb, cc, t, r, gx, mode, emit);
 }
 
-// 32-byte binning record of a Gaussian with tiles: (px, py, conic a, conic b)
-// and (conic c, threshold, rect x0 | y0 << 16, rect x1 | y1 << 16); the rect
-// packing needs tile grids below 65536 in each direction.
-__device__ __forceinline__ void store_bin_record(float4* rec, float px, float py, float ca, float cb,
-                                                 float cc, float t, const Rect r) {
-  rec[0] = make_float4(px, py, ca, cb);
-  rec[1] = make_float4(cc, t, __uint_as_float((unsigned)r.x0 | ((unsigned)r.y0 << 16)),
-                       __uint_as_float((unsigned)r.x1 | ((unsigned)r.y1 << 16)));
+// 32-byte binning record of a Gaussian with tiles, written by preprocess
+// while it counts the tiles, so that the binning emit only replays the
+// result: words 0-1 hold the clipped rect (x0 | y0 << 16, x1 | y1 << 16;
+// tile grids below 65536), word 2 the kind (bits 0-1), the band direction
+// (bit 2: bands are tile columns) and the band count (bits 8-15), words 3-7
+// the payload:
+//   BINREC_RECT  every tile of the rect (area <= 1, or SnugBox mode);
+//   BINREC_BANDS the AccuTile [lo, hi) of each band, lo | hi << 16, up to 5;
+//   BINREC_MASK  conic_rect per-tile results for rects of <= 64 tiles,
+//                row-major bits in words 3-4;
+//   BINREC_SWEEP more than 5 bands: the emit re-runs the sweep from the
+//                render record (same inputs, same bits).
+constexpr unsigned BINREC_RECT = 0, BINREC_BANDS = 1, BINREC_MASK = 2, BINREC_SWEEP = 3;
+constexpr int BINREC_MAX_BANDS = 5;
+
+// Counts the tiles of cover_tiles_in_rect and fills the record; the count
+// is the one cover_tiles_in_rect returns (same calls, same order).
+__device__ __forceinline__ int coverage_record(float px, float py, float ca, float cb, float cc, float t,
+                                               const Rect r, int mode, unsigned (&w)[8]) {
+  w[0] = (unsigned)r.x0 | ((unsigned)r.y0 << 16);
+  w[1] = (unsigned)r.x1 | ((unsigned)r.y1 << 16);
+  w[2] = w[3] = w[4] = w[5] = w[6] = w[7] = 0u;
+  const int span_x = r.x1 - r.x0, span_y = r.y1 - r.y0;
+  const int area = span_x * span_y;
+  if (area <= 1 || mode == GSB_COVERAGE_SNUGBOX) {
+    w[2] = BINREC_RECT;
+    return area;
+  }
+  int count = 0;
+  if (mode == GSB_COVERAGE_CONIC_RECT && area <= 64) {
+    unsigned long long mask = 0ull;
+    int bit = 0;
+    for (int ty = r.y0; ty < r.y1; ++ty)
+      for (int tx = r.x0; tx < r.x1; ++tx, ++bit)
+        if (conic_rect_intersects(px, py, ca, cb, cc, t, tx, ty)) {
+          ++count;
+          mask |= 1ull << bit;
+        }
+    w[2] = BINREC_MASK;
+    w[3] = (unsigned)mask;
+    w[4] = (unsigned)(mask >> 32);
+    return count;
+  }
+  const bool vertical = span_y > span_x;
+  const int nb = vertical ? span_x : span_y;
+  const bool fits = nb <= BINREC_MAX_BANDS;
+  w[2] = (fits ? BINREC_BANDS : BINREC_SWEEP) | (vertical ? 4u : 0u) | ((unsigned)nb << 8);
+  for (int b = 0; b < nb; ++b) {
+    int lo, hi;
+    if (!vertical)
+      band_interval(px, py, ca, cb, cc, t, r.y0 + b, BLOCK_X, BLOCK_Y, r.x0, r.x1, lo, hi);
+    else
+      band_interval(py, px, cc, cb, ca, t, r.x0 + b, BLOCK_Y, BLOCK_X, r.y0, r.y1, lo, hi);
+    count += imx(0, hi - lo);
+    if (fits && b < BINREC_MAX_BANDS) w[3 + b] = (unsigned)lo | ((unsigned)hi << 16);
+  }
+  return count;
 }
-__device__ __forceinline__ void load_bin_record(const float4* rec, float& px, float& py, float& ca,
-                                                float& cb, float& cc, float& t, Rect& r) {
-  const float4 a = __ldg(rec), b = __ldg(rec + 1);
-  px = a.x;
-  py = a.y;
-  ca = a.z;
-  cb = a.w;
-  cc = b.x;
-  t = b.y;
-  const unsigned lo = __float_as_uint(b.z), hi = __float_as_uint(b.w);
-  r.x0 = (int)(lo & 0xFFFFu);
-  r.y0 = (int)(lo >> 16);
-  r.x1 = (int)(hi & 0xFFFFu);
-  r.y1 = (int)(hi >> 16);
+
+// Emits the tiles of a binning record in cover_tiles_in_rect's order.
+// BINREC_SWEEP records need the sweep inputs, passed in by the caller.
+template <typename Emit>
+__device__ __forceinline__ void emit_record(const unsigned (&w)[8], int gx, int mode, float px, float py, float ca,
+                                            float cb, float cc, float t, const Emit& emit) {
+  Rect r;
+  r.x0 = (int)(w[0] & 0xFFFFu);
+  r.y0 = (int)(w[0] >> 16);
+  r.x1 = (int)(w[1] & 0xFFFFu);
+  r.y1 = (int)(w[1] >> 16);
+  const unsigned kind = w[2] & 3u;
+  const bool vertical = (w[2] >> 2) & 1u;
+  const int nb = (int)((w[2] >> 8) & 0xFFu);
+  if (kind == BINREC_RECT) {
+    for (int ty = r.y0; ty < r.y1; ++ty)
+      for (int tx = r.x0; tx < r.x1; ++tx) emit(ty * gx + tx);
+  } else if (kind == BINREC_MASK) {
+    const unsigned long long mask = (unsigned long long)w[3] | ((unsigned long long)w[4] << 32);
+    int bit = 0;
+    for (int ty = r.y0; ty < r.y1; ++ty)
+      for (int tx = r.x0; tx < r.x1; ++tx, ++bit)
+        if ((mask >> bit) & 1ull) emit(ty * gx + tx);
+  } else if (kind == BINREC_BANDS) {
+#pragma unroll 1
+    for (int b = 0; b < nb; ++b) {
+      const int lo = (int)(w[3 + b] & 0xFFFFu), hi = (int)(w[3 + b] >> 16);
+      if (!vertical)
+        for (int tx = lo; tx < hi; ++tx) emit((r.y0 + b) * gx + tx);
+      else
+        for (int ty = lo; ty < hi; ++ty) emit(ty * gx + r.x0 + b);
+    }
+  } else {
+    cover_tiles_in_rect(px, py, ca, cb, cc, t, r, gx, mode, emit);
+  }
 }
 
 }  // namespace gsb

@@ -84,7 +84,7 @@ constexpr int SH_ROW_F4 = 13;  // staged SH row: 48 floats padded to 52
 // padded to 52 floats: conflict-free 16-byte reads).  Every lane of the warp
 // takes part, so threads past P stay in the kernel with nothing to do.
 template <bool SH16>
-__global__ void __launch_bounds__(SH16 ? PF_SH16_THREADS : PF_THREADS)
+__global__ void __launch_bounds__(SH16 ? PF_SH16_THREADS : PF_THREADS, SH16 ? 8 : 1)
     preprocess_fwd_kernel(const gsb_preprocess_args a) {
   __shared__ float s_view[16], s_proj[16], s_cam[3];
   __shared__ float4 s_rows[SH16 ? PF_SH16_THREADS * SH_ROW_F4 : 1];
@@ -263,10 +263,13 @@ __global__ void __launch_bounds__(SH16 ? PF_SH16_THREADS : PF_THREADS)
         Rect br;
         float bt;
         coverage_setup(px, py, cov_a, cov_c, opacity, radius, gx, gy, br, bt);
-        tiles = cover_tiles_in_rect(px, py, con0, con1, con2, bt, br, gx, a.coverage_mode, NoEmit{});
-        if (a.bin_records && tiles > 0)
-          store_bin_record(reinterpret_cast<float4*>(a.bin_records) + (size_t)idx * 2, px, py, con0, con1,
-                           con2, bt, br);
+        unsigned brec[8];
+        tiles = coverage_record(px, py, con0, con1, con2, bt, br, a.coverage_mode, brec);
+        if (a.bin_records && tiles > 0) {
+          uint4* d = reinterpret_cast<uint4*>(a.bin_records) + (size_t)idx * 2;
+          d[0] = make_uint4(brec[0], brec[1], brec[2], brec[3]);
+          d[1] = make_uint4(brec[4], brec[5], brec[6], brec[7]);
+        }
       } else {
         cov_a = cov_b = cov_c = 0.0f;
       }

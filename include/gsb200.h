@@ -91,10 +91,12 @@ typedef struct {
   float* records;       /* (P,12) render records */
   float* cov3d_out;     /* (P,6) 3D covariance of the scale/rotation path, or NULL
                            (only the packed raw-compat geometry buffer needs it) */
-  float* bin_records;   /* (P,8) 16-byte aligned, or NULL: per Gaussian with tiles, the
-                           centre, conic, opacity threshold and clipped tile rect the
-                           binning emit needs (written only where tiles_touched > 0;
-                           needs both tile-grid dimensions below 65536) */
+  float* bin_records;   /* (P,8) 16-byte aligned, or NULL: per Gaussian with tiles, a
+                           32-byte record of its covered tiles (clipped rect plus the
+                           AccuTile interval of each band, or the conic_rect tile mask),
+                           written while counting so the binning emit only replays it
+                           (written only where tiles_touched > 0; needs both tile-grid
+                           dimensions below 65536) */
   int sparse_records;   /* 1: write render records only where radius > 0 (nothing reads
                            the others: render and the id-list backward skip them) */
 } gsb_preprocess_args;
@@ -150,8 +152,9 @@ typedef struct {
   void* workspace;
   size_t workspace_bytes;
   const float* bin_records;    /* (P,8) from gsb_preprocess_fwd, or NULL: with it the emit
-                                  reads one 32-byte record per Gaussian (radii, records,
-                                  conic_2d_inv and tiles_touched are then not read) */
+                                  reads one 32-byte record per Gaussian (radii, conic_2d_inv
+                                  and tiles_touched are then not read; records only for
+                                  footprints of more than 5 tile bands) */
   const long long* bin_status; /* status_out of gsb_bin_count (device; V is read from [2]) */
 } gsb_bin_sort_args;
 

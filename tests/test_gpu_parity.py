@@ -42,6 +42,12 @@ def _scene(name, dev):
     elif name == "cfg2_small_view":
         scene = wl.config2_scene(seed=3, n=60_000)
         view = wl.config2_view(seed=3, width=333, height=197)
+    elif name == "cfg2_big_footprints":
+        # scales x12: footprints of many tiles (AccuTile bands beyond what a
+        # binning record holds, conic_rect rects above 64 tiles)
+        scene = wl.config2_scene(seed=4, n=20_000)
+        scene.scales = scene.scales * 12.0
+        view = wl.config2_view(seed=4, width=333, height=197)
     else:
         raise KeyError(name)
     return scene, view
@@ -77,7 +83,7 @@ def _bits(a):
     return np.ascontiguousarray(a).view(np.uint32)
 
 
-@pytest.mark.parametrize("name", ["cfg1", "cfg2_200k", "cfg2_small_view"])
+@pytest.mark.parametrize("name", ["cfg1", "cfg2_200k", "cfg2_small_view", "cfg2_big_footprints"])
 @pytest.mark.parametrize("mode", [1, 0, 2])
 def test_preprocess_and_binning_bit_exact(cuda, name, mode):
     if name == "cfg2_200k" and mode != 1:
