@@ -335,6 +335,36 @@ def measure_small_configs(device):
     return out
 
 
+def measure_adam(trainer, peaks):
+    """The optimizer step that follows the all-reduce, on the bench's parameters and gradient buffer:
+    gswarp_b200.optim.FusedAdam (one pass, 28 B per element) against torch.optim.Adam (foreach)."""
+    import torch
+
+    from gswarp_b200.optim import FusedAdam
+
+    lrs = {"means": 1.6e-4, "scales": 5e-3, "rotations": 1e-3, "opacities": 2.5e-2, "sh_dc": 2.5e-3,
+           "sh_rest": 1.25e-4}
+    params = [p.detach() for p in trainer.params]
+    flat = trainer.flat
+    fa = FusedAdam(params, flat, lrs)
+    ms_fused = _event_ms(fa.step, 10, 3)
+    n = flat.numel()
+    gbs = 28.0 * n / (ms_fused * 1e-3) / 1e9
+    out = {"elements": n, "fused_ms": ms_fused, "fused_gbs": gbs,
+           "fused_frac_of_hbm": gbs / peaks.get("hbm_gbs", 6650.0)}
+    del fa
+    ref = [p.clone().requires_grad_(True) for p in params]
+    off = 0
+    for t in ref:
+        t.grad = flat[off:off + t.numel()].view_as(t)
+        off += t.numel()
+    opt = torch.optim.Adam([{"params": [t], "lr": 1e-3} for t in ref], lr=1e-3, eps=1e-15)
+    out["torch_adam_ms"] = _event_ms(opt.step, 5, 2)
+    del opt, ref
+    torch.cuda.empty_cache()
+    return out
+
+
 def cpu_baseline_sample(views, scene_cpu, band_rows=136):
     """Times the CPU oracle (all host threads) on one view of the workload:
     preprocess + binning of every Gaussian, then render, render backward, SSIM
@@ -535,6 +565,7 @@ def run_ours(args):
 
     extra = {}
     if rank == 0 and world == 1:
+        extra["optimizer"] = measure_adam(tr, peaks)
         del tr
         torch.cuda.empty_cache()
         if not args.no_cfg2:

@@ -24,7 +24,7 @@ GSB_ERR_OVERFLOW = -2
 GSB_ERR_CUDA = -3
 GSB_ERR_TIMEOUT = -4
 
-ABI_VERSION = 8
+ABI_VERSION = 9
 RECORD_FLOATS = 12
 GRAD_FLOATS = 12
 
@@ -103,7 +103,7 @@ class PreprocessBwdArgs(ctypes.Structure):
         ("accumulate", c_int),
         ("grad_means3d", vp), ("grad_means2d", vp), ("grad_scales", vp), ("grad_rotations", vp),
         ("grad_opacity", vp), ("grad_sh", vp), ("grad_colors", vp), ("grad_cov3d", vp),
-        ("ids", vp), ("num_ids", c_int), ("clear_grad_acc", c_int),
+        ("ids", vp), ("num_ids", c_int), ("clear_grad_acc", c_int), ("densify_grad_accum", vp),
     ]
 
 
@@ -139,6 +139,15 @@ class PhotoLossBwdArgs(ctypes.Structure):
     ]
 
 
+class AdamArgs(ctypes.Structure):
+    _fields_ = [
+        ("P", c_int), ("sh_coeffs", c_int), ("params", vp * 5),
+        ("grad", vp), ("exp_avg", vp), ("exp_avg_sq", vp),
+        ("lr", ctypes.c_double * 6), ("beta1", ctypes.c_double), ("beta2", ctypes.c_double),
+        ("eps", ctypes.c_double), ("step", c_int),
+    ]
+
+
 class KNNArgs(ctypes.Structure):
     _fields_ = [
         ("P", c_int), ("points", vp), ("out", vp), ("error_word", vp),
@@ -155,7 +164,7 @@ EXPORTED = (
     "gsb_bin_emit_sort", "gsb_render_fwd", "gsb_render_bwd", "gsb_preprocess_bwd",
     "gsb_ssim_partials_count", "gsb_ssim_fwd", "gsb_ssim_bwd", "gsb_knn_workspace_bytes",
     "gsb_knn", "gsb_selftest_threshold_log", "gsb_ssim_fwd_noalloc", "gsb_photo_loss_fwd",
-    "gsb_photo_loss_bwd",
+    "gsb_photo_loss_bwd", "gsb_adam_step", "gsb_densify_stats",
 )
 
 
@@ -182,6 +191,8 @@ def _declare(L) -> None:
     fn("gsb_ssim_bwd", c_int, [P(SSIMBwdArgs), vp])
     fn("gsb_photo_loss_fwd", c_int, [P(PhotoLossFwdArgs), vp])
     fn("gsb_photo_loss_bwd", c_int, [P(PhotoLossBwdArgs), vp])
+    fn("gsb_adam_step", c_int, [P(AdamArgs), vp])
+    fn("gsb_densify_stats", c_int, [c_int, vp, vp, vp, vp])
     fn("gsb_knn_workspace_bytes", ctypes.c_size_t, [c_int])
     fn("gsb_knn", c_int, [P(KNNArgs), vp])
     fn("gsb_selftest_threshold_log", c_int, [vp, vp, c_ll, vp])

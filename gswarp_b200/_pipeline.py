@@ -388,7 +388,8 @@ class PreprocessGrads:
 
 def preprocess_backward(g: Gaussians, cam: Camera, radii, records, grad_acc, grad_proj_2d, grad_conic_2d,
                         grad_conic_2d_inv, out: PreprocessGrads | None = None,
-                        ids: torch.Tensor | None = None, clear_grad_acc: bool = False) -> PreprocessGrads:
+                        ids: torch.Tensor | None = None, clear_grad_acc: bool = False,
+                        densify_grad_accum: torch.Tensor | None = None) -> PreprocessGrads:
     """Per-Gaussian backward.  With ``out`` given, gradients are added into
     its buffers (multi-view accumulation); otherwise fresh tensors are made.
     ``ids`` (accumulate mode only) restricts the work to those Gaussians --
@@ -436,6 +437,7 @@ def preprocess_backward(g: Gaussians, cam: Camera, radii, records, grad_acc, gra
     a.ids = _lib.ptr(ids) if ids is not None and ids.numel() else None
     a.num_ids = int(ids.numel()) if ids is not None else 0
     a.clear_grad_acc = int(clear_grad_acc)
+    a.densify_grad_accum = _lib.ptr(densify_grad_accum)
     if ids is not None and ids.numel() == 0:
         return out
     a.grad_means3d = _lib.ptr(out.grad_means3D)

@@ -617,6 +617,7 @@ __global__ void __launch_bounds__(SH16 ? PB_SH16_THREADS : PB_THREADS)
 #pragma unroll
     for (int k = 0; k < 6; ++k) a.grad_cov3d[gid * 6 + k] = acc ? oc[k] + gc3[k] : gc3[k];
   if (haso) a.grad_opacity[gid] = acc ? oo + rco[3] : rco[3];
+  if (a.densify_grad_accum) a.densify_grad_accum[gid] += sqrtf(rgx * rgx + rgy * rgy);
   if (a.clear_grad_acc) {
     // last, so the zero stores do not hold back any load above
     float4* w4 = const_cast<float4*>(ga4);

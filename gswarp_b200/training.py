@@ -99,7 +99,7 @@ class FusedViewStep:
     """
 
     def __init__(self, params: Sequence[torch.Tensor], settings: Sequence, l1_weight: float = 1.0,
-                 ssim_weight: float = 0.2, group=None):
+                 ssim_weight: float = 0.2, group=None, densify_stats: bool = False):
         if len(params) != 5:
             raise ValueError("params must be (means, scales, rotations, opacities, sh)")
         means, scales, rots, opac, sh = params
@@ -129,6 +129,14 @@ class FusedViewStep:
         self._side: torch.cuda.Stream | None = None
         # two streams in turn (overlapping consecutive views); False = one stream
         self.concurrent_views = True
+        # 3DGS densification statistics, accumulated per view until reset_densify_stats():
+        # xyz_gradient_accum += |d loss / d means2D (x, y)|, denom += 1 and max_radii2D = max(., radius)
+        # for every Gaussian with a radius in the view
+        self.densify_stats = densify_stats
+        if densify_stats:
+            self.xyz_gradient_accum = torch.zeros(P, dtype=torch.float32, device=dev)
+            self.denom = torch.zeros(P, dtype=torch.float32, device=dev)
+            self.max_radii2D = torch.zeros(P, dtype=torch.float32, device=dev)
 
     def _gaussians(self, rs) -> pl.Gaussians:
         means, scales, rots, opac, sh = self.params
@@ -177,7 +185,17 @@ class FusedViewStep:
         # reads each binned Gaussian's accumulator entry and zeroes it: the accumulator is all zero again
         # for the next view (render backward only touches binned Gaussians)
         pl.preprocess_backward(g, cam, pre.radii, pre.records, grad_acc, None, None, None, out=out, ids=binned.ids,
-                               clear_grad_acc=True)
+                               clear_grad_acc=True,
+                               densify_grad_accum=self.xyz_gradient_accum if self.densify_stats else None)
+        if self.densify_stats:
+            _lib.call("gsb_densify_stats", P, _lib.ptr(pre.radii), _lib.ptr(self.denom), _lib.ptr(self.max_radii2D),
+                      _lib.stream_handle(self.device))
+
+    def reset_densify_stats(self) -> None:
+        if self.densify_stats:
+            self.xyz_gradient_accum.zero_()
+            self.denom.zero_()
+            self.max_radii2D.zero_()
 
     def step(self, targets: Sequence[torch.Tensor]) -> torch.Tensor:
         """Runs every view, then the all-reduce.  Consecutive views go to two

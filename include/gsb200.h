@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define GSB_ABI_VERSION 8
+#define GSB_ABI_VERSION 9
 
 #define GSB_OK 0
 #define GSB_ERR_INVALID (-1)  /* bad argument: ValueError in Python          */
@@ -242,6 +242,8 @@ typedef struct {
   int clear_grad_acc;    /* 1: zero each processed Gaussian's grad_acc entry after reading it,
                             so a persistent accumulator is ready for the next view without a
                             full memset (the render backward only touches binned Gaussians) */
+  float* densify_grad_accum; /* optional (P): += |d loss / d means2D (x, y)| per processed
+                            Gaussian (3DGS add_densification_stats' gradient norm) */
 } gsb_preprocess_bwd_args;
 
 int gsb_preprocess_bwd(const gsb_preprocess_bwd_args* a, void* stream);
@@ -322,6 +324,31 @@ int gsb_photo_loss_bwd(const gsb_photo_loss_bwd_args* a, void* stream);
 int gsb_ssim_fwd_noalloc(int B, int C, int H, int W, int valid, float C1, float C2,
                          const float* img1, const float* img2, float* dm, float* loss,
                          void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Optimizer step after the training step's gradient all-reduce (B200       */
+/* addition; the reference leaves the optimizer to the training script).    */
+/* Fused Adam over the flat gradient buffer [means 3P | scales 3P |         */
+/* rotations 4P | opacities P | SH 3KP] with torch.optim.Adam's arithmetic  */
+/* (weight_decay 0, no amsgrad) and the six 3DGS learning-rate groups.      */
+/* ------------------------------------------------------------------------ */
+typedef struct {
+  int P, sh_coeffs;
+  float* params[5];       /* means (P,3), scales (P,3), rotations (P,4), opacities (P), sh (P,K,3) */
+  const float* grad;      /* flat, 11P + 3KP floats */
+  float* exp_avg;         /* flat, same layout */
+  float* exp_avg_sq;      /* flat, same layout */
+  double lr[6];           /* means, scales, rotations, opacities, SH DC (coefficient 0), SH rest */
+  double beta1, beta2, eps;
+  int step;               /* this update's step number, >= 1 (bias corrections) */
+} gsb_adam_args;
+
+int gsb_adam_step(const gsb_adam_args* a, void* stream);
+
+/* Densification statistics: for radius > 0, denom += 1 and
+ * max_radii = max(max_radii, radius) (3DGS add_densification_stats /
+ * max_radii2D); the gradient-norm sum comes from gsb_preprocess_bwd. */
+int gsb_densify_stats(int P, const int* radii, float* denom, float* max_radii, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* KNN initialiser.  Replaces distCUDA2 (gswarp/knn.py:264-410).             */
