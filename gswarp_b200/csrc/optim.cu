@@ -32,32 +32,51 @@ struct AdamScalars {
   float neg_step[6];  // -lr / bc1 per group
 };
 
+// 32-bit element indices (the host checks that the buffer holds fewer than
+// 2^32 elements); each thread handles ADAM_ITEMS elements ADAM_THREADS apart
+// so every load and store instruction of a warp is one coalesced run, and
+// all of a thread's loads are issued before its arithmetic.
 __global__ void __launch_bounds__(ADAM_THREADS) adam_kernel(const gsb_adam_args a, AdamScalars s,
-                                                           long long total) {
-  const long long P = a.P;
-  const long long seg_end[5] = {3 * P, 6 * P, 10 * P, 11 * P, total};
-  const long long base = ((long long)blockIdx.x * ADAM_THREADS * ADAM_ITEMS) + threadIdx.x;
+                                                           unsigned total) {
+  const unsigned P = (unsigned)a.P;
+  const unsigned e1 = 3u * P, e2 = 6u * P, e3 = 10u * P, e4 = 11u * P;
+  const unsigned row = 3u * (unsigned)a.sh_coeffs;
+  const unsigned base = blockIdx.x * (ADAM_THREADS * ADAM_ITEMS) + threadIdx.x;
+  float g[ADAM_ITEMS], m[ADAM_ITEMS], v[ADAM_ITEMS], pv[ADAM_ITEMS];
+  float* pp[ADAM_ITEMS];
+  int grp[ADAM_ITEMS];
 #pragma unroll
   for (int it = 0; it < ADAM_ITEMS; ++it) {
-    const long long e = base + (long long)it * ADAM_THREADS;
-    if (e >= total) return;
-    int seg = 0;
+    const unsigned e = base + it * ADAM_THREADS;
+    pp[it] = nullptr;
+    grp[it] = 0;
+    if (e < total) {
+      unsigned local;
+      int seg;
+      if (e < e1) { seg = 0; local = e; }
+      else if (e < e2) { seg = 1; local = e - e1; }
+      else if (e < e3) { seg = 2; local = e - e2; }
+      else if (e < e4) { seg = 3; local = e - e3; }
+      else { seg = 4; local = e - e4; }
+      grp[it] = seg == 4 ? (local % row < 3u ? 4 : 5) : seg;  // SH DC (coefficient 0) vs the rest
+      pp[it] = a.params[seg] + local;
+      g[it] = a.grad[e];
+      m[it] = a.exp_avg[e];
+      v[it] = a.exp_avg_sq[e];
+      pv[it] = *pp[it];
+    }
+  }
 #pragma unroll
-    for (int k = 0; k < 4; ++k) seg += e >= seg_end[k];
-    const long long local = e - (seg == 0 ? 0 : seg_end[seg - 1]);
-    float* p = a.params[seg] + local;
-    int group = seg;
-    if (seg == 4) group = (local % (3LL * a.sh_coeffs)) < 3 ? 4 : 5;  // SH DC vs the rest
-    const float g = a.grad[e];
-    float m = a.exp_avg[e];
-    float v = a.exp_avg_sq[e];
-    m = fmaf(s.w1, g - m, m);
-    v = v * s.b2;
-    v = fmaf(s.w2 * g, g, v);
-    const float denom = sqrtf(v) / s.bc2_sqrt + s.eps;
-    *p = fmaf(s.neg_step[group], m / denom, *p);
-    a.exp_avg[e] = m;
-    a.exp_avg_sq[e] = v;
+  for (int it = 0; it < ADAM_ITEMS; ++it) {
+    const unsigned e = base + it * ADAM_THREADS;
+    if (!pp[it]) continue;
+    float mm = fmaf(s.w1, g[it] - m[it], m[it]);
+    float vv = v[it] * s.b2;
+    vv = fmaf(s.w2 * g[it], g[it], vv);
+    const float denom = sqrtf(vv) / s.bc2_sqrt + s.eps;
+    *pp[it] = fmaf(s.neg_step[grp[it]], mm / denom, pv[it]);
+    a.exp_avg[e] = mm;
+    a.exp_avg_sq[e] = vv;
   }
 }
 
@@ -89,6 +108,10 @@ GSB_EXPORT int gsb_adam_step(const gsb_adam_args* a, void* stream) {
     }
   if (a->P == 0) return GSB_OK;
   const long long total = (long long)a->P * (11 + 3LL * a->sh_coeffs);
+  if (total >= (1ll << 32) - (long long)ADAM_THREADS * ADAM_ITEMS) {
+    set_error("gsb_adam_step: the flat buffer must hold fewer than 2^32 elements");
+    return GSB_ERR_INVALID;
+  }
   AdamScalars s;
   const double b1 = a->beta1, b2 = a->beta2;
   const double bc1 = 1.0 - std::pow(b1, (double)a->step);
@@ -101,7 +124,7 @@ GSB_EXPORT int gsb_adam_step(const gsb_adam_args* a, void* stream) {
   for (int k = 0; k < 6; ++k) s.neg_step[k] = (float)(-(a->lr[k] / bc1));
   const long long per_block = (long long)ADAM_THREADS * ADAM_ITEMS;
   const long long blocks = (total + per_block - 1) / per_block;
-  adam_kernel<<<(unsigned)blocks, ADAM_THREADS, 0, (cudaStream_t)stream>>>(*a, s, total);
+  adam_kernel<<<(unsigned)blocks, ADAM_THREADS, 0, (cudaStream_t)stream>>>(*a, s, (unsigned)total);
   return check_launch("gsb_adam_step");
 }
 
