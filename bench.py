@@ -335,6 +335,38 @@ def measure_small_configs(device):
     return out
 
 
+def measure_flow(device, steps, warmup):
+    """Config 2 through the flow rasterizer (top-K contributor outputs, K=20) against the standard one:
+    forward + backward of an L1 loss on the colour, through the public autograd APIs."""
+    import torch
+
+    import gswarp_b200.rasterizer as std
+    import gswarp_b200.rasterizer_flow as flow
+    from gswarp_b200 import workloads as wl
+
+    scene = wl.config2_scene(seed=0, n=1_000_000).to(device)
+    v = wl.config2_view(seed=0).to(device)
+    tgt = wl.target_image(0).to(device)
+    ps = [t.clone().requires_grad_(True) for t in (scene.means, scene.opacities, scene.sh, scene.scales,
+                                                    scene.rotations)]
+    m2d = torch.zeros_like(ps[0], requires_grad=True)
+    out = {"gaussians": 1_000_000, "top_k": flow.get_flow_topk()}
+    for name, mod in (("standard", std), ("flow", flow)):
+        rs = mod.GaussianRasterizationSettings(
+            image_height=v.height, image_width=v.width, tanfovx=v.tanfovx, tanfovy=v.tanfovy,
+            bg=torch.zeros(3, device=device), scale_modifier=1.0, viewmatrix=v.viewmatrix, projmatrix=v.projmatrix,
+            sh_degree=3, campos=v.campos, prefiltered=False)
+        r = mod.GaussianRasterizer(rs)
+
+        def one():
+            o = r(ps[0], m2d, ps[1], shs=ps[2], scales=ps[3], rotations=ps[4])
+            (o[0] - tgt).abs().mean().backward()
+
+        ms = _event_ms(one, steps, warmup)
+        out[name] = {"views_per_s": 1000.0 / ms, "ms_per_view": ms}
+    return out
+
+
 def measure_adam(trainer, peaks):
     """The optimizer step that follows the all-reduce, on the bench's parameters and gradient buffer:
     gswarp_b200.optim.FusedAdam (one pass, 28 B per element) against torch.optim.Adam (foreach)."""
@@ -571,6 +603,7 @@ def run_ours(args):
         if not args.no_cfg2:
             extra["config2_single_view"] = measure_cfg2(device, max(3, args.steps), max(3, args.warmup))
             extra["other_configs"] = measure_small_configs(device)
+            extra["flow_config2"] = measure_flow(device, max(3, args.steps), max(3, args.warmup))
         if not args.no_cpu_baseline:
             scene_cpu = wl.config2_scene(seed=0, n=args.gaussians)
             extra["cpu_baseline"] = cpu_baseline_sample([views[0]], scene_cpu)

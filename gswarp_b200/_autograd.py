@@ -27,8 +27,9 @@ def _camera(rs) -> pl.Camera:
 
 
 def run_forward(means3D, sh, colors_precomp, opacities, scales, rotations, cov3Ds_precomp, rs,
-                options: ExecutionOptions):
-    """Typed forward: returns (outputs tuple, Gaussians, Preprocessed, Binned, Rendered, Camera)."""
+                options: ExecutionOptions, top_k: int = 0):
+    """Typed forward: returns (Gaussians, Preprocessed, Binned, Rendered, Camera, background);
+    ``top_k > 0`` adds the flow render's auxiliary outputs to the Rendered."""
     if means3D.ndim != 2 or means3D.shape[1] != 3:
         raise ValueError("means3D must have dimensions (num_points, 3)")
     if getattr(rs, "prefiltered", False):
@@ -42,7 +43,7 @@ def run_forward(means3D, sh, colors_precomp, opacities, scales, rotations, cov3D
     with torch.cuda.device(dev):
         pre = pl.preprocess(g, cam, mode)
         binned = pl.binning(pre, cam, mode)
-        ren = pl.render(pre, binned, cam, bg, options.compute_depth)
+        ren = pl.render(pre, binned, cam, bg, options.compute_depth, top_k=top_k)
     return g, pre, binned, ren, cam, bg
 
 
@@ -84,10 +85,16 @@ def _grad_or_none(t):
 
 def run_backward(rs, options, num_rendered, means3D, sh, colors_precomp, opacities, scales, rotations,
                  cov3Ds_precomp, radii, records, point_list, ranges, n_contrib, alpha, grad_color, grad_depth,
-                 grad_alpha, grad_proj_2D, grad_conic_2D, grad_conic_2D_inv):
+                 grad_alpha, grad_proj_2D, grad_conic_2D, grad_conic_2D_inv, flow_grad: bool = False):
     """Returns the reference's 8-tuple (backward_ops.py:746): grad_means2D,
     grad_colors, grad_opacities, grad_means3D, grad_cov3D, grad_sh,
-    grad_scales, grad_rotations."""
+    grad_scales, grad_rotations.
+
+    ``flow_grad`` is the flow backend's ``enable_flow_grad``
+    (flow_ops.py:337-366): the render's screen-space and conic gradients are
+    first added into the proj_2D / conic_2D gradient inputs, which the
+    preprocess backward then combines with the render gradients again, as the
+    reference does."""
     P = means3D.shape[0]
     dev = means3D.device
     cam = _camera(rs)
@@ -114,6 +121,9 @@ def run_backward(rs, options, num_rendered, means3D, sh, colors_precomp, opaciti
                 gc = torch.zeros((NUM_CHANNELS, H, W), dtype=torch.float32, device=dev)
             grad_acc = pl.render_backward(records, binned, cam, bg, pl._f32(alpha), n_contrib, gc, gd, ga,
                                           options.compute_depth, P)
+        if flow_grad:
+            gp = (gp if gp is not None else torch.zeros((P, 2), dtype=torch.float32, device=dev)) + grad_acc[:, 0:2]
+            gk = (gk if gk is not None else torch.zeros((P, 3), dtype=torch.float32, device=dev)) + grad_acc[:, 4:7]
         pg = pl.preprocess_backward(g, cam, radii, records, grad_acc, gp, gk, gki)
     grad_colors = pg.grad_colors if g.colors is not None else torch.empty_like(colors_precomp)
     grad_opac = pg.grad_opacity.reshape(opacities.shape)

@@ -144,6 +144,10 @@ class Rendered:
     depth: torch.Tensor
     alpha: torch.Tensor
     n_contrib: torch.Tensor
+    # flow render auxiliary outputs (top_k > 0)
+    gs_per_pixel: torch.Tensor | None = None
+    weight_per_gs_pixel: torch.Tensor | None = None
+    x_mu: torch.Tensor | None = None
 
 
 def make_gaussians(means3D, opacities, scales, rotations, cov3D, sh, colors, scale_modifier, degree) -> Gaussians:
@@ -312,7 +316,10 @@ def binning(pre: Preprocessed, cam: Camera, coverage_mode: int, want_ids: bool =
     return Binned(R, point_list[:R], ranges, ids[:int(num_binned)] if ids is not None else None)
 
 
-def render(pre: Preprocessed, binned: Binned, cam: Camera, background: torch.Tensor, compute_depth: bool) -> Rendered:
+def render(pre: Preprocessed, binned: Binned, cam: Camera, background: torch.Tensor, compute_depth: bool,
+           top_k: int = 0) -> Rendered:
+    """Render forward; ``top_k > 0`` also fills the flow auxiliary outputs
+    (first ``top_k`` contributors per pixel: ids, weights, centre offsets)."""
     dev = pre.records.device
     H, W = cam.H, cam.W
     out = Rendered(
@@ -321,6 +328,10 @@ def render(pre: Preprocessed, binned: Binned, cam: Camera, background: torch.Ten
         alpha=torch.empty((1, H, W), dtype=torch.float32, device=dev),
         n_contrib=torch.empty(H * W, dtype=torch.int32, device=dev),
     )
+    if top_k > 0:
+        out.gs_per_pixel = torch.empty((top_k, H, W), dtype=torch.int32, device=dev)
+        out.weight_per_gs_pixel = torch.empty((top_k, H, W), dtype=torch.float32, device=dev)
+        out.x_mu = torch.empty((2, top_k, H, W), dtype=torch.float32, device=dev)
     a = _lib.RenderFwdArgs()
     a.W, a.H = W, H
     a.compute_depth = int(bool(compute_depth))
@@ -332,6 +343,10 @@ def render(pre: Preprocessed, binned: Binned, cam: Camera, background: torch.Ten
     a.out_depth = _lib.ptr(out.depth)
     a.out_alpha = _lib.ptr(out.alpha)
     a.n_contrib = _lib.ptr(out.n_contrib)
+    a.top_k = int(top_k) if top_k > 0 else 0
+    a.gs_per_pixel = _lib.ptr(out.gs_per_pixel)
+    a.weight_per_gs_pixel = _lib.ptr(out.weight_per_gs_pixel)
+    a.x_mu = _lib.ptr(out.x_mu)
     info = {"num_rendered": binned.num_rendered, "P": pre.records.shape[0], "kernels": 1}
     with _stage_timer("render_fwd", info):
         _lib.call("gsb_render_fwd", a, _lib.stream_handle(dev))

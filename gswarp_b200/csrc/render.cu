@@ -127,8 +127,13 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
-template <bool DEPTH>
+// AUX: also record the first top_k contributors of every pixel in
+// front-to-back order -- Gaussian id, compositing weight alpha * T and the
+// offset (dx, dy) = centre - pixel -- the flow render's auxiliary outputs
+// (flow_kernels.py:14-180); slots left empty are written -1 / 0 / 0.
+template <bool DEPTH, bool AUX>
 __global__ void __launch_bounds__(THREADS) render_fwd_kernel(const gsb_render_fwd_args a, int gx) {
+  __shared__ int s_id[AUX ? BATCH : 1];
   __shared__ float2 s_xy[BATCH];
   __shared__ float4 s_cf[BATCH];    // power coefficients, opacity in .w
   __shared__ float4 s_rgbd[BATCH];  // r, g, b, depth
@@ -145,8 +150,9 @@ __global__ void __launch_bounds__(THREADS) render_fwd_kernel(const gsb_render_fw
   const float bx0 = (float)(__shfl_sync(FULL, pxi, 0)), by0 = (float)(__shfl_sync(FULL, py0, 0));
   const float bx1 = bx0 + 7.0f, by1 = by0 + 7.0f;
   float fy[2], T[2], c0[2], c1[2], c2[2], wsum[2], dacc[2];
-  int last[2];
+  int last[2], nsucc[2] = {0, 0};
   bool inside[2], done[2];
+  const long long npix = (long long)a.W * a.H;
 #pragma unroll
   for (int p = 0; p < 2; ++p) {
     const int py = py0 + 4 * p;
@@ -165,6 +171,7 @@ __global__ void __launch_bounds__(THREADS) render_fwd_kernel(const gsb_render_fw
       const float4 q0 = __ldg(rec + (size_t)id * 3 + 0);
       const float4 q1 = __ldg(rec + (size_t)id * 3 + 1);
       const float4 q2 = __ldg(rec + (size_t)id * 3 + 2);
+      if (AUX) s_id[threadIdx.x] = id;
       s_xy[threadIdx.x] = make_float2(q0.x, q0.y);
       float4 cf = power_coefs(q0.z, q0.w, q1.x);
       cf.w = q1.y;
@@ -214,17 +221,34 @@ __global__ void __launch_bounds__(THREADS) render_fwd_kernel(const gsb_render_fw
         c2[p] += cd.z * contrib;
         wsum[p] += contrib;
         if (DEPTH) dacc[p] += cd.w * contrib;
+        if (AUX) {
+          if (nsucc[p] < a.top_k) {
+            const long long o = (long long)nsucc[p] * npix + (long long)(py0 + 4 * p) * a.W + pxi;
+            a.gs_per_pixel[o] = s_id[j];
+            a.weight_per_gs_pixel[o] = contrib;
+            a.x_mu[o] = dx;
+            a.x_mu[(long long)a.top_k * npix + o] = xy.y - fy[p];
+          }
+          ++nsucc[p];
+        }
         T[p] = test_T;
         last[p] = b - range.x + j + 1;
       }
       }
     }
   }
-  const long long npix = (long long)a.W * a.H;
 #pragma unroll
   for (int p = 0; p < 2; ++p) {
     if (!inside[p]) continue;
     const long long pix = (long long)(py0 + 4 * p) * a.W + pxi;
+    if (AUX)
+      for (int k = nsucc[p]; k < a.top_k; ++k) {
+        const long long o = (long long)k * npix + pix;
+        a.gs_per_pixel[o] = -1;
+        a.weight_per_gs_pixel[o] = 0.0f;
+        a.x_mu[o] = 0.0f;
+        a.x_mu[(long long)a.top_k * npix + o] = 0.0f;
+      }
     a.n_contrib[pix] = last[p];
     a.out_color[pix] = c0[p] + T[p] * a.background[0];
     a.out_color[npix + pix] = c1[p] + T[p] * a.background[1];
@@ -507,10 +531,17 @@ GSB_EXPORT int gsb_render_fwd(const gsb_render_fwd_args* a, void* stream) {
   }
   const int gx = div_up(a->W, BLOCK_X), gy = div_up(a->H, BLOCK_Y);
   cudaStream_t s = (cudaStream_t)stream;
+  const bool aux = a->top_k > 0;
+  if (aux && (!a->gs_per_pixel || !a->weight_per_gs_pixel || !a->x_mu)) {
+    set_error("gsb_render_fwd: top_k > 0 needs gs_per_pixel, weight_per_gs_pixel and x_mu");
+    return GSB_ERR_INVALID;
+  }
   if (a->compute_depth)
-    render_fwd_kernel<true><<<gx * gy, THREADS, 0, s>>>(*a, gx);
+    aux ? render_fwd_kernel<true, true><<<gx * gy, THREADS, 0, s>>>(*a, gx)
+        : render_fwd_kernel<true, false><<<gx * gy, THREADS, 0, s>>>(*a, gx);
   else
-    render_fwd_kernel<false><<<gx * gy, THREADS, 0, s>>>(*a, gx);
+    aux ? render_fwd_kernel<false, true><<<gx * gy, THREADS, 0, s>>>(*a, gx)
+        : render_fwd_kernel<false, false><<<gx * gy, THREADS, 0, s>>>(*a, gx);
   return check_launch("render_fwd_kernel");
 }
 

@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define GSB_ABI_VERSION 9
+#define GSB_ABI_VERSION 10
 
 #define GSB_OK 0
 #define GSB_ERR_INVALID (-1)  /* bad argument: ValueError in Python          */
@@ -176,6 +176,10 @@ typedef struct {
   float* out_depth;         /* (1,H,W) */
   float* out_alpha;         /* (1,H,W) */
   int* n_contrib;           /* (H*W) */
+  int top_k;                /* > 0: flow render auxiliary outputs (flow_kernels.py:14-180): */
+  int* gs_per_pixel;        /*   (K,H,W) ids of the first K contributors, -1 where none */
+  float* weight_per_gs_pixel; /* (K,H,W) their compositing weights alpha * T */
+  float* x_mu;              /*   (2,K,H,W) offsets centre - pixel (dx planes, then dy) */
 } gsb_render_fwd_args;
 
 int gsb_render_fwd(const gsb_render_fwd_args* a, void* stream);

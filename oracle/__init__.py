@@ -76,6 +76,8 @@ def _declare(L):
     L.or_render_fwd.restype = None
     L.or_render_fwd.argtypes = [c_int, c_int, _i32p, _i32p, _f32p, _f32p, _f32p, _f32p, _f32p, c_int,
                                 _f32p, _f32p, _f32p, _i32p]
+    L.or_render_flow_aux.restype = None
+    L.or_render_flow_aux.argtypes = [c_int, c_int, _i32p, _i32p, _f32p, _f32p, c_int, _i32p, _f32p, _f32p]
     L.or_render_bwd.restype = None
     L.or_render_bwd.argtypes = [c_int, c_int, c_int, _i32p, _i32p, _f32p, _f32p, _f32p, _f32p, _f32p,
                                 _f32p, _i32p, _f32p, _f32p, _f32p, c_int,
@@ -203,6 +205,18 @@ def render_fwd(W, H, ranges, point_list, xy, features, depths, conic_opacity, bg
     lib().or_render_fwd(W, H, _c(ranges, np.int32).reshape(-1), pl, _c(xy), _c(features), _c(depths),
                         _c(conic_opacity), _c(bg), int(bool(compute_depth)), color, depth, alpha, n_contrib)
     return color, depth, alpha, n_contrib
+
+
+def render_flow_aux(W, H, ranges, point_list, xy, conic_opacity, top_k):
+    """Top-K contributor outputs of the flow render: (gs_per_pixel (K,H,W) i32,
+    weight_per_gs_pixel (K,H,W), x_mu (2,K,H,W))."""
+    gs = np.zeros((top_k, H, W), np.int32)
+    wt = np.zeros((top_k, H, W), np.float32)
+    xm = np.zeros((2, top_k, H, W), np.float32)
+    pl = _c(point_list, np.int32) if len(point_list) else np.zeros(1, np.int32)
+    lib().or_render_flow_aux(W, H, _c(ranges, np.int32).reshape(-1), pl, _c(xy), _c(conic_opacity), int(top_k),
+                             gs, wt, xm)
+    return gs, wt, xm
 
 
 def render_bwd(W, H, P, ranges, point_list, xy, features, depths, conic_opacity, bg, out_alpha,

@@ -657,6 +657,65 @@ OR_EXPORT void or_render_fwd(int W, int H, const int* ranges, const int* point_l
 }
 
 // ---------------------------------------------------------------------------
+// Flow auxiliary outputs of the flow render (flow_kernels.py:14-180): the
+// same front-to-back loop as or_render_fwd; the first `top_k` Gaussians that
+// contribute to a pixel are recorded in order with their compositing weight
+// (alpha * T) and the offset (dx, dy) = centre - pixel.  Slots that stay
+// empty keep -1 / 0 / 0 (flow_ops.py:119-125).
+// ---------------------------------------------------------------------------
+OR_EXPORT void or_render_flow_aux(int W, int H, const int* ranges, const int* point_list, const float* xy,
+                                  const float* conic_opacity, int top_k, int* gs_per_pixel,
+                                  float* weight_per_gs_pixel, float* x_mu) {
+  const int grid_x = (W + BLOCK_X - 1) / BLOCK_X;
+  const int grid_y = (H + BLOCK_Y - 1) / BLOCK_Y;
+  const long long npix = (long long)W * H;
+  for (long long i = 0; i < (long long)top_k * npix; ++i) {
+    gs_per_pixel[i] = -1;
+    weight_per_gs_pixel[i] = 0.0f;
+    x_mu[i] = 0.0f;
+    x_mu[(long long)top_k * npix + i] = 0.0f;
+  }
+#pragma omp parallel for schedule(dynamic, 4)
+  for (int tile = 0; tile < grid_x * grid_y; ++tile) {
+    int tx = tile % grid_x, ty = tile / grid_x;
+    int start = ranges[2 * tile], end = ranges[2 * tile + 1];
+    for (int local = 0; local < BLOCK_X * BLOCK_Y; ++local) {
+      int pxi = tx * BLOCK_X + local % BLOCK_X;
+      int pyi = ty * BLOCK_Y + local / BLOCK_X;
+      if (pxi >= W || pyi >= H) continue;
+      long long pix = (long long)pyi * W + pxi;
+      float T = 1.0f;
+      int n_success = 0;
+      float fx = (float)pxi, fy = (float)pyi;
+      for (int k = start; k < end; ++k) {
+        int id = point_list[k];
+        const float* co = conic_opacity + id * 4;
+        float d_x = xy[id * 2] - fx;
+        float d_y = xy[id * 2 + 1] - fy;
+        float power = -0.5f * (co[0] * d_x * d_x + co[2] * d_y * d_y) - co[1] * d_x * d_y;
+        if (power <= 0.0f) {
+          float alpha = fmn(0.99f, co[3] * std::exp(power));
+          if (alpha >= (1.0f / 255.0f)) {
+            float test_T = T * (1.0f - alpha);
+            if (test_T < 0.0001f) break;
+            float contribution = alpha * T;
+            if (n_success < top_k) {
+              long long a = (long long)n_success * npix + pix;
+              gs_per_pixel[a] = id;
+              weight_per_gs_pixel[a] = contribution;
+              x_mu[a] = d_x;
+              x_mu[(long long)top_k * npix + a] = d_y;
+            }
+            n_success = n_success + 1;
+            T = test_T;
+          }
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Render backward (backward_kernels.py:538-707).  Per-pixel back-to-front
 // recurrence.  Per-Gaussian gradients are reduced in double, tile by tile in
 // tile order, so the oracle is deterministic.  grad_abs (optional, 10 per G)
