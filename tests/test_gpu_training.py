@@ -158,3 +158,23 @@ def test_fused_step_concurrent_views_match_serial(cuda):
     torch.cuda.synchronize()
     torch.testing.assert_close(la, lb, rtol=1e-6, atol=1e-7)
     assert float((b.grads.flat - ga).norm()) <= 1e-4 * float(ga.norm()) + 1e-7
+
+
+def test_fused_step_views_with_nothing_visible(cuda):
+    """A camera looking away from every Gaussian (no radius, no pairs) and a tiny image that is not a
+    multiple of the tile size: zero loss gradient contributions, finite losses, no error."""
+    params, settings, targets = _scene(cuda, 10_000, 1, 40, 23)
+    s0 = settings[0]
+    away = wl.look_at_view([0.0, 0.0, 30.0], [0.0, 0.0, 60.0], [0.0, 1.0, 0.0], 50.0, 40, 23)
+    s_away = s0._replace(viewmatrix=away.viewmatrix.to(cuda), projmatrix=away.projmatrix.to(cuda),
+                         campos=away.campos.to(cuda))
+    step = FusedViewStep([p.clone() for p in params], [s_away, s0], densify_stats=True)
+    losses = step.step([targets[0], targets[0]])
+    torch.cuda.synchronize()
+    assert torch.isfinite(losses).all()
+    assert torch.isfinite(step.grads.flat).all()
+    # the away view alone contributes nothing
+    only_away = FusedViewStep([p.clone() for p in params], [s_away])
+    only_away.step([targets[0]])
+    torch.cuda.synchronize()
+    assert not bool(only_away.grads.flat.any())
