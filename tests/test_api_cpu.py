@@ -115,3 +115,30 @@ def test_tuning_api_compat():
     assert gs.get_tuned_block_dim("render_forward") == 256
     gs.register_kernel_class("custom", 32)
     assert isinstance(gs.get_canonical_device("cpu"), str)
+
+
+def test_flow_options_are_call_scoped():
+    """gswarp runtime test_flow_option_is_scoped_with_the_same_snapshot (tests/test_runtime_options.py:98-109):
+    a per-call compute_flow_aux overrides the default for that call only."""
+    import torch
+
+    from gswarp_b200 import rasterizer_flow as flow
+
+    def settings(**kw):
+        return flow.GaussianRasterizationSettings(
+            image_height=4, image_width=4, tanfovx=1.0, tanfovy=1.0, bg=torch.zeros(3), scale_modifier=1.0,
+            viewmatrix=torch.eye(4), projmatrix=torch.eye(4), sh_degree=0, campos=torch.zeros(3),
+            prefiltered=False, **kw)
+
+    assert flow.get_compute_flow_aux() is True and flow.get_flow_topk() == 20
+    assert flow._active_topk(settings(compute_flow_aux=False)) == 0
+    assert flow._active_topk(settings()) == 20
+    flow.set_compute_flow_aux(False)
+    try:
+        assert flow._active_topk(settings()) == 0
+        assert flow._active_topk(settings(compute_flow_aux=True)) == 20
+    finally:
+        flow.set_compute_flow_aux(True)
+    assert settings().enable_flow_grad is True
+    with pytest.raises(ValueError):
+        flow.set_flow_topk(-3)
