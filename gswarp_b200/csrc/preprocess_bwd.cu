@@ -282,7 +282,7 @@ __device__ __forceinline__ void sh_backward_staged(const gsb_preprocess_bwd_args
 // user gradient (both only apply where radius > 0), so its contribution is
 // zero and it is skipped without touching memory.
 template <bool PRECOMP, bool SH16>
-__global__ void __launch_bounds__(SH16 ? PB_SH16_THREADS : PB_THREADS)
+__global__ void __launch_bounds__(SH16 ? PB_SH16_THREADS : PB_THREADS, SH16 ? 6 : 1)
     preprocess_bwd_kernel(const gsb_preprocess_bwd_args a) {
   __shared__ float s_view[16], s_proj[16], s_cam[3];
   __shared__ float s_rows[SH16 ? PB_SH16_THREADS * SH_ROW_F : 1];

@@ -132,7 +132,7 @@ __device__ __forceinline__ float ex2_approx(float x) {
 // offset (dx, dy) = centre - pixel -- the flow render's auxiliary outputs
 // (flow_kernels.py:14-180); slots left empty are written -1 / 0 / 0.
 template <bool DEPTH, bool AUX>
-__global__ void __launch_bounds__(THREADS) render_fwd_kernel(const gsb_render_fwd_args a, int gx) {
+__global__ void __launch_bounds__(THREADS, 10) render_fwd_kernel(const gsb_render_fwd_args a, int gx) {
   __shared__ int s_id[AUX ? BATCH : 1];
   __shared__ float2 s_xy[BATCH];
   __shared__ float4 s_cf[BATCH];    // power coefficients, opacity in .w
@@ -374,7 +374,7 @@ __device__ __forceinline__ bool bwd_pixel(BwdPixel& s, const float4 cf, float ax
 // DEPTH: compute_depth with a depth gradient given; GA: an alpha gradient
 // given.  Without them those terms are exactly zero and are not evaluated.
 template <bool DEPTH, bool GA>
-__global__ void __launch_bounds__(THREADS, 6) render_bwd_kernel(const gsb_render_bwd_args a, int gx) {
+__global__ void __launch_bounds__(THREADS, 8) render_bwd_kernel(const gsb_render_bwd_args a, int gx) {
   __shared__ int s_id[BATCH];
   __shared__ float2 s_xy[BATCH];
   __shared__ float4 s_cf[BATCH];    // power coefficients, opacity in .w
