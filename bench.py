@@ -56,6 +56,7 @@ def parse():
     p.add_argument("--no-cfg2", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-autograd", action="store_true", help="skip the drop-in autograd path comparison")
+    p.add_argument("--no-optimizer", action="store_true", help="skip the fused Adam measurement")
     return p.parse_args()
 
 
@@ -597,7 +598,8 @@ def run_ours(args):
 
     extra = {}
     if rank == 0 and world == 1:
-        extra["optimizer"] = measure_adam(tr, peaks)
+        if not args.no_optimizer:
+            extra["optimizer"] = measure_adam(tr, peaks)
         del tr
         torch.cuda.empty_cache()
         if not args.no_cfg2:

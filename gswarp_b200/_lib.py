@@ -24,7 +24,7 @@ GSB_ERR_OVERFLOW = -2
 GSB_ERR_CUDA = -3
 GSB_ERR_TIMEOUT = -4
 
-ABI_VERSION = 10
+ABI_VERSION = 11
 RECORD_FLOATS = 12
 GRAD_FLOATS = 12
 
@@ -46,7 +46,7 @@ class PreprocessArgs(ctypes.Structure):
         ("coverage_mode", c_int),
         ("radii", vp), ("proj_2d", vp), ("conic_2d", vp), ("conic_2d_inv", vp), ("depths", vp),
         ("tiles_touched", vp), ("records", vp), ("cov3d_out", vp), ("bin_records", vp),
-        ("sparse_records", c_int),
+        ("sparse_records", c_int), ("colors_clamp_signed", c_int),
     ]
 
 
@@ -105,6 +105,16 @@ class PreprocessBwdArgs(ctypes.Structure):
         ("grad_means3d", vp), ("grad_means2d", vp), ("grad_scales", vp), ("grad_rotations", vp),
         ("grad_opacity", vp), ("grad_sh", vp), ("grad_colors", vp), ("grad_cov3d", vp),
         ("ids", vp), ("num_ids", c_int), ("clear_grad_acc", c_int), ("densify_grad_accum", vp),
+        ("grad_colors_clamped", c_int),
+    ]
+
+
+class SHViewsArgs(ctypes.Structure):
+    _fields_ = [
+        ("P", c_int), ("num_views", c_int), ("sh_degree", c_int), ("sh_coeffs", c_int),
+        ("means", vp), ("sh", vp), ("campos", vp), ("colors", vp),
+        ("grad_colors", vp), ("clear_grad_colors", c_int), ("grad_sh", vp), ("grad_means3d", vp),
+        ("accumulate", c_int),
     ]
 
 
@@ -165,7 +175,8 @@ EXPORTED = (
     "gsb_bin_emit_sort", "gsb_render_fwd", "gsb_render_bwd", "gsb_preprocess_bwd",
     "gsb_ssim_partials_count", "gsb_ssim_fwd", "gsb_ssim_bwd", "gsb_knn_workspace_bytes",
     "gsb_knn", "gsb_selftest_threshold_log", "gsb_ssim_fwd_noalloc", "gsb_photo_loss_fwd",
-    "gsb_photo_loss_bwd", "gsb_adam_step", "gsb_densify_stats",
+    "gsb_photo_loss_bwd", "gsb_adam_step", "gsb_densify_stats", "gsb_sh_colors_views",
+    "gsb_sh_backward_views",
 )
 
 
@@ -194,6 +205,8 @@ def _declare(L) -> None:
     fn("gsb_photo_loss_bwd", c_int, [P(PhotoLossBwdArgs), vp])
     fn("gsb_adam_step", c_int, [P(AdamArgs), vp])
     fn("gsb_densify_stats", c_int, [c_int, vp, vp, vp, vp])
+    fn("gsb_sh_colors_views", c_int, [P(SHViewsArgs), vp])
+    fn("gsb_sh_backward_views", c_int, [P(SHViewsArgs), vp])
     fn("gsb_knn_workspace_bytes", ctypes.c_size_t, [c_int])
     fn("gsb_knn", c_int, [P(KNNArgs), vp])
     fn("gsb_selftest_threshold_log", c_int, [vp, vp, c_ll, vp])

@@ -185,13 +185,16 @@ MAX_TILE_GRID = 65535
 
 
 def preprocess(g: Gaussians, cam: Camera, coverage_mode: int, want_cov3d: bool = False,
-               bin_records: bool = True, sparse: bool = False) -> Preprocessed:
+               bin_records: bool = True, sparse: bool = False, colors_clamp_signed: bool = False) -> Preprocessed:
     """Runs the fused preprocess.  With ``bin_records`` (the default) it also
     writes the 32-byte per-Gaussian records the binning emit reads instead of
     gathering radii, render records, conic_2D_inv and tiles_touched.
     ``sparse`` (internal training step) skips what only the autograd outputs
     need: proj_2D / conic_2D / conic_2D_inv are not produced and render
-    records are written only for Gaussians with a radius."""
+    records are written only for Gaussians with a radius.
+    ``colors_clamp_signed``: ``g.colors`` comes from ``sh_colors_views``
+    (clamped channels stored as -0.0), so the records carry the SH path's
+    clamp bits."""
     P = g.P
     dev = g.means3D.device
     cov3d = None
@@ -242,6 +245,7 @@ def preprocess(g: Gaussians, cam: Camera, coverage_mode: int, want_cov3d: bool =
     a.cov3d_out = _lib.ptr(cov3d) if (cov3d is not None and g.cov3D is None) else None
     a.bin_records = _lib.ptr(out.bin_records)
     a.sparse_records = int(sparse)
+    a.colors_clamp_signed = int(colors_clamp_signed)
     with _stage_timer("preprocess_fwd", {"P": P, "kernels": 1}):
         _lib.call("gsb_preprocess_fwd", a, _lib.stream_handle(dev))
     return out
@@ -404,11 +408,14 @@ class PreprocessGrads:
 def preprocess_backward(g: Gaussians, cam: Camera, radii, records, grad_acc, grad_proj_2d, grad_conic_2d,
                         grad_conic_2d_inv, out: PreprocessGrads | None = None,
                         ids: torch.Tensor | None = None, clear_grad_acc: bool = False,
-                        densify_grad_accum: torch.Tensor | None = None) -> PreprocessGrads:
+                        densify_grad_accum: torch.Tensor | None = None,
+                        grad_colors_clamped: bool = False) -> PreprocessGrads:
     """Per-Gaussian backward.  With ``out`` given, gradients are added into
     its buffers (multi-view accumulation); otherwise fresh tensors are made.
     ``ids`` (accumulate mode only) restricts the work to those Gaussians --
-    the binned ids, when the only gradients are the render's."""
+    the binned ids, when the only gradients are the render's.
+    ``grad_colors_clamped``: the colour gradient goes through the forward's
+    clamp flags (the input of ``sh_backward_views``)."""
     if ids is not None and out is None:
         raise ValueError("an id list needs accumulation buffers (out=...)")
     P = g.P
@@ -453,6 +460,7 @@ def preprocess_backward(g: Gaussians, cam: Camera, radii, records, grad_acc, gra
     a.num_ids = int(ids.numel()) if ids is not None else 0
     a.clear_grad_acc = int(clear_grad_acc)
     a.densify_grad_accum = _lib.ptr(densify_grad_accum)
+    a.grad_colors_clamped = int(grad_colors_clamped)
     if ids is not None and ids.numel() == 0:
         return out
     a.grad_means3d = _lib.ptr(out.grad_means3D)
@@ -469,6 +477,55 @@ def preprocess_backward(g: Gaussians, cam: Camera, radii, records, grad_acc, gra
     if TIMING_ENABLED:
         info["visible"] = int(ids.numel()) if ids is not None else int((radii > 0).sum())
     return out
+
+
+def _sh_views_args(means: torch.Tensor, sh: torch.Tensor, degree: int, campos: torch.Tensor):
+    P = means.shape[0]
+    if sh.ndim != 3 or sh.shape[0] != P or sh.shape[2] != NUM_CHANNELS or not 1 <= sh.shape[1] <= 16:
+        raise ValueError("sh must be (P, K, 3) with 1 <= K <= 16")
+    if campos.ndim != 2 or campos.shape[1] != 3:
+        raise ValueError("campos must be (num_views, 3)")
+    a = _lib.SHViewsArgs()
+    a.P, a.num_views = P, campos.shape[0]
+    a.sh_degree, a.sh_coeffs = int(degree), sh.shape[1]
+    a.means, a.sh, a.campos = _lib.ptr(means), _lib.ptr(sh), _lib.ptr(campos)
+    return a
+
+
+def sh_colors_views(means: torch.Tensor, sh: torch.Tensor, degree: int, campos: torch.Tensor,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+    """(V,P,3) clamped SH colours of every Gaussian from each of the V
+    cameras in ``campos`` (V,3); clamped channels are -0.0."""
+    means, sh, campos = _f32(means), _f32(sh), _f32(campos)
+    a = _sh_views_args(means, sh, degree, campos)
+    shape = (campos.shape[0], means.shape[0], NUM_CHANNELS)
+    if out is None:
+        out = torch.empty(shape, dtype=torch.float32, device=means.device)
+    elif tuple(out.shape) != shape or out.dtype != torch.float32 or not out.is_contiguous():
+        raise ValueError(f"out must be contiguous fp32 {shape}")
+    a.colors = _lib.ptr(out)
+    with torch.cuda.device(means.device), _stage_timer("sh_colors", {"kernels": 1}):
+        _lib.call("gsb_sh_colors_views", a, _lib.stream_handle(means.device))
+    return out
+
+
+def sh_backward_views(means: torch.Tensor, sh: torch.Tensor, degree: int, campos: torch.Tensor,
+                      grad_colors: torch.Tensor, grad_sh: torch.Tensor, grad_means3D: torch.Tensor,
+                      accumulate: bool = False, clear_grad_colors: bool = True) -> None:
+    """SH gradient (stored into ``grad_sh``, or added with ``accumulate``) and
+    the view-direction term of the means gradient (added into
+    ``grad_means3D``) from the views' clamped colour gradients (V,P,3)."""
+    means, sh, campos = _f32(means), _f32(sh), _f32(campos)
+    a = _sh_views_args(means, sh, degree, campos)
+    P = means.shape[0]
+    for t, shape in ((grad_colors, (campos.shape[0], P, NUM_CHANNELS)), (grad_sh, tuple(sh.shape)),
+                     (grad_means3D, (P, 3))):
+        if tuple(t.shape) != shape or t.dtype != torch.float32 or not t.is_contiguous():
+            raise ValueError(f"gradient buffer must be contiguous fp32 {shape}")
+    a.grad_colors, a.grad_sh, a.grad_means3d = _lib.ptr(grad_colors), _lib.ptr(grad_sh), _lib.ptr(grad_means3D)
+    a.clear_grad_colors, a.accumulate = int(clear_grad_colors), int(accumulate)
+    with torch.cuda.device(means.device), _stage_timer("sh_backward", {"kernels": 1}):
+        _lib.call("gsb_sh_backward_views", a, _lib.stream_handle(means.device))
 
 
 def mark_visible(means3D: torch.Tensor, viewmatrix: torch.Tensor) -> torch.Tensor:

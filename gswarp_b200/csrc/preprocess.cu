@@ -15,6 +15,7 @@
 // kernels gather one Gaussian with three 16-byte loads.
 #include "gsb_common.cuh"
 #include "gsb_geometry.cuh"
+#include "gsb_shrows.cuh"
 
 namespace gsb {
 namespace {
@@ -73,6 +74,28 @@ __device__ __forceinline__ void eval_sh(const float (&sp)[48], int K, int degree
   }
 }
 
+// View-dependent colour of one SH row (zero-padded past K) seen from cam:
+// max(SH colour + 0.5, 0), returning the clamp bits (bit ch = channel ch
+// was clamped).  Every path that evaluates SH colours goes through here, so
+// the per-view preprocess and the multi-view colour kernel agree bit for bit.
+__device__ __forceinline__ unsigned sh_colour(const float (&shv)[48], int K, int degree, float p0, float p1,
+                                              float p2, float c0, float c1, float c2, float col[3]) {
+  const float dx = p0 - c0, dy = p1 - c1, dz = p2 - c2;
+  const float len_sq = dx * dx + dy * dy + dz * dz;
+  const float inv_len = 1.0f / sqrtf(fmx(len_sq, 1.0e-20f));
+  eval_sh(shv, K, degree, dx * inv_len, dy * inv_len, dz * inv_len, col);
+  unsigned clamp_bits = 0u;
+#pragma unroll
+  for (int ch = 0; ch < 3; ++ch) {
+    col[ch] = col[ch] + 0.5f;
+    if (col[ch] < 0.0f) {
+      col[ch] = 0.0f;
+      clamp_bits |= 1u << ch;
+    }
+  }
+  return clamp_bits;
+}
+
 constexpr int PF_THREADS = 256;
 constexpr int PF_SH16_THREADS = 128;
 constexpr int SH_ROW_F4 = 13;  // staged SH row: 48 floats padded to 52
@@ -83,9 +106,14 @@ constexpr int SH_ROW_F4 = 13;  // staged SH row: 48 floats padded to 52
 // survive culling -- and each thread evaluates its row from there (rows
 // padded to 52 floats: conflict-free 16-byte reads).  Every lane of the warp
 // takes part, so threads past P stay in the kernel with nothing to do.
-template <bool SH16>
-__global__ void __launch_bounds__(SH16 ? PF_SH16_THREADS : PF_THREADS, SH16 ? 8 : 1)
+// SH handling, a template parameter so that each variant carries only the
+// registers of its own colour path.
+enum ShMode { SHM_NONE = 0, SHM_ANY = 1, SHM_16 = 2 };
+
+template <int SHM>
+__global__ void __launch_bounds__(SHM == SHM_16 ? PF_SH16_THREADS : PF_THREADS, SHM == SHM_16 ? 8 : 1)
     preprocess_fwd_kernel(const gsb_preprocess_args a) {
+  constexpr bool SH16 = SHM == SHM_16;
   __shared__ float s_view[16], s_proj[16], s_cam[3];
   __shared__ float4 s_rows[SH16 ? PF_SH16_THREADS * SH_ROW_F4 : 1];
   if (threadIdx.x < 16) {
@@ -299,9 +327,6 @@ __global__ void __launch_bounds__(SH16 ? PF_SH16_THREADS : PF_THREADS, SH16 ? 8 
     }
     __syncwarp();
     if (need) {
-      const float dx = p0 - s_cam[0], dy = p1 - s_cam[1], dz = p2 - s_cam[2];
-      const float len_sq = dx * dx + dy * dy + dz * dz;
-      const float inv_len = 1.0f / sqrtf(fmx(len_sq, 1.0e-20f));
       float shv[48];
       const float4* row = rows + lane * SH_ROW_F4;
 #pragma unroll
@@ -312,15 +337,7 @@ __global__ void __launch_bounds__(SH16 ? PF_SH16_THREADS : PF_THREADS, SH16 ? 8 
         shv[q * 4 + 2] = t.z;
         shv[q * 4 + 3] = t.w;
       }
-      eval_sh(shv, 16, a.sh_degree, dx * inv_len, dy * inv_len, dz * inv_len, col);
-#pragma unroll
-      for (int ch = 0; ch < 3; ++ch) {
-        col[ch] = col[ch] + 0.5f;
-        if (col[ch] < 0.0f) {
-          col[ch] = 0.0f;
-          clamp_bits |= 1u << ch;
-        }
-      }
+      clamp_bits = sh_colour(shv, 16, a.sh_degree, p0, p1, p2, s_cam[0], s_cam[1], s_cam[2], col);
     }
     if (!live) return;
   } else if (radius > 0) {
@@ -328,10 +345,16 @@ __global__ void __launch_bounds__(SH16 ? PF_SH16_THREADS : PF_THREADS, SH16 ? 8 
       col[0] = a.colors_precomp[idx * 3 + 0];
       col[1] = a.colors_precomp[idx * 3 + 1];
       col[2] = a.colors_precomp[idx * 3 + 2];
-    } else if (a.sh) {
-      const float dx = p0 - s_cam[0], dy = p1 - s_cam[1], dz = p2 - s_cam[2];
-      const float len_sq = dx * dx + dy * dy + dz * dz;
-      const float inv_len = 1.0f / sqrtf(fmx(len_sq, 1.0e-20f));
+      if (a.colors_clamp_signed) {
+        // multi-view SH colours: -0.0 marks a clamped channel
+#pragma unroll
+        for (int ch = 0; ch < 3; ++ch)
+          if (signbit(col[ch])) {
+            col[ch] = 0.0f;
+            clamp_bits |= 1u << ch;
+          }
+      }
+    } else if (SHM == SHM_ANY && a.sh) {
       const float* sp = a.sh + (size_t)idx * a.sh_coeffs * 3;
       // The first 16 coefficients of the row, with 16-byte loads when the row
       // is an aligned 48-float record (SH degree 3).
@@ -351,15 +374,7 @@ __global__ void __launch_bounds__(SH16 ? PF_SH16_THREADS : PF_THREADS, SH16 ? 8 
 #pragma unroll
         for (int k = 0; k < 48; ++k) shv[k] = k < nsh ? __ldg(sp + k) : 0.0f;
       }
-      eval_sh(shv, a.sh_coeffs, a.sh_degree, dx * inv_len, dy * inv_len, dz * inv_len, col);
-#pragma unroll
-      for (int ch = 0; ch < 3; ++ch) {
-        col[ch] = col[ch] + 0.5f;
-        if (col[ch] < 0.0f) {
-          col[ch] = 0.0f;
-          clamp_bits |= 1u << ch;
-        }
-      }
+      clamp_bits = sh_colour(shv, a.sh_coeffs, a.sh_degree, p0, p1, p2, s_cam[0], s_cam[1], s_cam[2], col);
     }
   }
 
@@ -383,6 +398,40 @@ __global__ void __launch_bounds__(SH16 ? PF_SH16_THREADS : PF_THREADS, SH16 ? 8 
     rec[0] = make_float4(px, py, con0, con1);
     rec[1] = make_float4(con2, op_rec, depth, __uint_as_float(clamp_bits));
     rec[2] = make_float4(col[0], col[1], col[2], 0.0f);
+  }
+}
+
+// Multi-view SH colours: one thread per Gaussian, 128-thread CTAs.  Each
+// warp stages the SH rows of its 32 consecutive Gaussians (one contiguous
+// span of 32*K*3 floats) in shared memory with coalesced loads, each thread
+// copies its row to registers once and evaluates it from every camera.
+constexpr int SHV_THREADS = 128;
+constexpr int SHV_ROW_F = 49;  // 48 floats padded: per-thread scalar reads hit 32 banks
+
+__global__ void __launch_bounds__(SHV_THREADS) sh_colors_views_kernel(const gsb_sh_views_args a) {
+  __shared__ float s_rows[SHV_THREADS * SHV_ROW_F];
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  const int lane = threadIdx.x & 31;
+  const int base = idx - lane;
+  if (base >= a.P) return;  // whole warp past P
+  const int K = a.sh_coeffs, RF = K * 3;
+  float* rows = s_rows + (threadIdx.x & ~31) * SHV_ROW_F;
+  sh_rows_load<SHV_ROW_F>(rows, a.sh + (size_t)base * RF, RF, min(32, a.P - base), 0xffffffffu, lane);
+  __syncwarp();
+  if (idx >= a.P) return;
+  float shv[48];
+  const float* row = rows + lane * SHV_ROW_F;
+#pragma unroll
+  for (int e = 0; e < 48; ++e) shv[e] = e < RF ? row[e] : 0.0f;
+  const float p0 = a.means[idx * 3 + 0], p1 = a.means[idx * 3 + 1], p2 = a.means[idx * 3 + 2];
+  for (int v = 0; v < a.num_views; ++v) {
+    const float* cam = a.campos + v * 3;
+    float col[3];
+    const unsigned clamp_bits = sh_colour(shv, K, a.sh_degree, p0, p1, p2, __ldg(cam), __ldg(cam + 1),
+                                          __ldg(cam + 2), col);
+    float* out = a.colors + ((size_t)v * a.P + idx) * 3;
+#pragma unroll
+    for (int ch = 0; ch < 3; ++ch) out[ch] = ((clamp_bits >> ch) & 1u) ? -0.0f : col[ch];
   }
 }
 
@@ -438,11 +487,29 @@ GSB_EXPORT int gsb_preprocess_fwd(const gsb_preprocess_args* a, void* stream) {
   }
   const bool sh16 = a->sh && !a->colors_precomp && a->sh_coeffs == 16 &&
                     !(reinterpret_cast<uintptr_t>(a->sh) & 15);
+  cudaStream_t s = (cudaStream_t)stream;
   if (sh16)
-    preprocess_fwd_kernel<true><<<div_up(a->P, PF_SH16_THREADS), PF_SH16_THREADS, 0, (cudaStream_t)stream>>>(*a);
+    preprocess_fwd_kernel<SHM_16><<<div_up(a->P, PF_SH16_THREADS), PF_SH16_THREADS, 0, s>>>(*a);
+  else if (a->sh && !a->colors_precomp)
+    preprocess_fwd_kernel<SHM_ANY><<<div_up(a->P, PF_THREADS), PF_THREADS, 0, s>>>(*a);
   else
-    preprocess_fwd_kernel<false><<<div_up(a->P, PF_THREADS), PF_THREADS, 0, (cudaStream_t)stream>>>(*a);
+    preprocess_fwd_kernel<SHM_NONE><<<div_up(a->P, PF_THREADS), PF_THREADS, 0, s>>>(*a);
   return check_launch("preprocess_fwd_kernel");
+}
+
+GSB_EXPORT int gsb_sh_colors_views(const gsb_sh_views_args* a, void* stream) {
+  if (!a || a->P < 0 || a->num_views < 0 || a->sh_coeffs < 1 || a->sh_coeffs > 16 || a->sh_degree < 0 ||
+      a->sh_degree > 3) {
+    set_error("gsb_sh_colors_views: invalid sizes (P, num_views >= 0; 1 <= sh_coeffs <= 16; degree 0..3)");
+    return GSB_ERR_INVALID;
+  }
+  if (a->P == 0 || a->num_views == 0) return GSB_OK;
+  if (!a->means || !a->sh || !a->campos || !a->colors) {
+    set_error("gsb_sh_colors_views: null pointer argument");
+    return GSB_ERR_INVALID;
+  }
+  sh_colors_views_kernel<<<div_up(a->P, SHV_THREADS), SHV_THREADS, 0, (cudaStream_t)stream>>>(*a);
+  return check_launch("sh_colors_views_kernel");
 }
 
 GSB_EXPORT int gsb_mark_visible(int P, const float* means, const float* viewmatrix, uint8_t* out,

@@ -281,9 +281,14 @@ __device__ __forceinline__ void sh_backward_staged(const gsb_preprocess_bwd_args
 // In accumulate mode a Gaussian with radius 0 got no render gradient and no
 // user gradient (both only apply where radius > 0), so its contribution is
 // zero and it is skipped without touching memory.
-template <bool PRECOMP, bool SH16>
-__global__ void __launch_bounds__(SH16 ? PB_SH16_THREADS : PB_THREADS, SH16 ? 6 : 1)
+// SH handling, a template parameter so that each variant carries only the
+// registers of its own SH path.
+enum ShMode { SHM_NONE = 0, SHM_ANY = 1, SHM_16 = 2 };
+
+template <bool PRECOMP, int SHM>
+__global__ void __launch_bounds__(SHM == SHM_16 ? PB_SH16_THREADS : PB_THREADS, SHM == SHM_16 ? 6 : (SHM == SHM_NONE ? 3 : 1))
     preprocess_bwd_kernel(const gsb_preprocess_bwd_args a) {
+  constexpr bool SH16 = SHM == SHM_16;
   __shared__ float s_view[16], s_proj[16], s_cam[3];
   __shared__ float s_rows[SH16 ? PB_SH16_THREADS * SH_ROW_F : 1];
   if (threadIdx.x < 16) {
@@ -341,7 +346,7 @@ __global__ void __launch_bounds__(SH16 ? PB_SH16_THREADS : PB_THREADS, SH16 ? 6 
     sh_backward_staged(a, s_rows + (threadIdx.x & ~31) * SH_ROW_F, gid, work, need, mean, s_cam, g,
                        gsm);
     if (!work) return;
-  } else if (a.sh) {
+  } else if (SHM == SHM_ANY && a.sh) {
     const unsigned clamp_bits =
         __float_as_uint(reinterpret_cast<const float4*>(a.records)[(size_t)gid * 3 + 1].w);
     sh_backward(a, gid, mean, s_cam, rrgb, clamp_bits, gsm);
@@ -566,7 +571,7 @@ __global__ void __launch_bounds__(SH16 ? PB_SH16_THREADS : PB_THREADS, SH16 ? 6 
     }
   }
   float m0 = pm_x + gcm[0], m1 = pm_y + gcm[1], m2 = pm_z + gcm[2];
-  if (SH16 || a.sh) {
+  if (SH16 || (SHM == SHM_ANY && a.sh)) {
     m0 = m0 + gsm[0];
     m1 = m1 + gsm[1];
     m2 = m2 + gsm[2];
@@ -626,8 +631,19 @@ __global__ void __launch_bounds__(SH16 ? PB_SH16_THREADS : PB_THREADS, SH16 ? 6 
     w4[1] = z;
     w4[2] = z;
   }
-  if (a.grad_colors)
-    for (int k = 0; k < 3; ++k) store_or_add(a.grad_colors + gid * 3 + k, rrgb[k], acc);
+  if (a.grad_colors) {
+    // grad_colors_clamped: the gradient past the forward's clamp, the g the SH backward uses
+    const unsigned cb =
+        a.grad_colors_clamped ? __float_as_uint(reinterpret_cast<const float4*>(a.records)[(size_t)gid * 3 + 1].w)
+                              : 0u;
+    float gc[3];
+    sh_color_grad(rrgb, cb, gc);
+    float* gcp = a.grad_colors + gid * 3;
+    const float o0 = acc ? gcp[0] : 0.0f, o1 = acc ? gcp[1] : 0.0f, o2 = acc ? gcp[2] : 0.0f;
+    gcp[0] = acc ? o0 + gc[0] : gc[0];
+    gcp[1] = acc ? o1 + gc[1] : gc[1];
+    gcp[2] = acc ? o2 + gc[2] : gc[2];
+  }
 }
 
 }  // namespace
@@ -669,15 +685,21 @@ GSB_EXPORT int gsb_preprocess_bwd(const gsb_preprocess_bwd_args* a, void* stream
   if (sh16) {
     const int blocks = div_up(threads_needed, PB_SH16_THREADS);
     if (precomp)
-      preprocess_bwd_kernel<true, true><<<blocks, PB_SH16_THREADS, 0, s>>>(*a);
+      preprocess_bwd_kernel<true, SHM_16><<<blocks, PB_SH16_THREADS, 0, s>>>(*a);
     else
-      preprocess_bwd_kernel<false, true><<<blocks, PB_SH16_THREADS, 0, s>>>(*a);
+      preprocess_bwd_kernel<false, SHM_16><<<blocks, PB_SH16_THREADS, 0, s>>>(*a);
+  } else if (a->sh) {
+    const int blocks = div_up(threads_needed, PB_THREADS);
+    if (precomp)
+      preprocess_bwd_kernel<true, SHM_ANY><<<blocks, PB_THREADS, 0, s>>>(*a);
+    else
+      preprocess_bwd_kernel<false, SHM_ANY><<<blocks, PB_THREADS, 0, s>>>(*a);
   } else {
     const int blocks = div_up(threads_needed, PB_THREADS);
     if (precomp)
-      preprocess_bwd_kernel<true, false><<<blocks, PB_THREADS, 0, s>>>(*a);
+      preprocess_bwd_kernel<true, SHM_NONE><<<blocks, PB_THREADS, 0, s>>>(*a);
     else
-      preprocess_bwd_kernel<false, false><<<blocks, PB_THREADS, 0, s>>>(*a);
+      preprocess_bwd_kernel<false, SHM_NONE><<<blocks, PB_THREADS, 0, s>>>(*a);
   }
   return check_launch("preprocess_bwd_kernel");
 }

@@ -20,6 +20,16 @@ backward ADDING each view's gradients straight into the flat gradient buffer
 parameters' ``.grad``.  After the rank's views it takes part in one sum
 all-reduce of that buffer, as ``view_sharding.ViewShardedStep`` does.
 
+With more than one view (``batch_sh``, the default then), the SH work is
+done once per step instead of once per view: every view renders the same
+parameters, so one pass evaluates all the views' SH colours (reading each
+SH row once), the views' preprocess reads 12-byte colours instead of
+192-byte SH rows, their backward writes the clamped colour gradient, and
+one pass after the last view turns those into the SH gradient and the
+view-direction part of the means gradient.  Per view that removes one SH
+read in the forward and an SH read plus an SH-gradient read-modify-write in
+the backward for every visible Gaussian.
+
 Gradients equal the autograd path's up to the float summation order of the
 render backward's atomics (tests compare the two).
 """
@@ -99,7 +109,7 @@ class FusedViewStep:
     """
 
     def __init__(self, params: Sequence[torch.Tensor], settings: Sequence, l1_weight: float = 1.0,
-                 ssim_weight: float = 0.2, group=None, densify_stats: bool = False):
+                 ssim_weight: float = 0.2, group=None, densify_stats: bool = False, batch_sh: bool | None = None):
         if len(params) != 5:
             raise ValueError("params must be (means, scales, rotations, opacities, sh)")
         means, scales, rots, opac, sh = params
@@ -137,6 +147,21 @@ class FusedViewStep:
             self.xyz_gradient_accum = torch.zeros(P, dtype=torch.float32, device=dev)
             self.denom = torch.zeros(P, dtype=torch.float32, device=dev)
             self.max_radii2D = torch.zeros(P, dtype=torch.float32, device=dev)
+        # SH colours and SH gradients once per step (all views share the parameters and the SH degree)
+        degrees = {int(rs.sh_degree) for rs in self.settings}
+        can_batch = len(degrees) == 1 and 1 <= sh.shape[1] <= 16
+        if batch_sh is None:
+            batch_sh = can_batch and len(self.settings) > 1
+        elif batch_sh and not can_batch:
+            raise ValueError("batch_sh needs one SH degree for all views and at most 16 SH coefficients")
+        self.batch_sh = bool(batch_sh)
+        if self.batch_sh:
+            V = len(self.settings)
+            self._sh_degree = degrees.pop()
+            self._campos = torch.stack([c.campos.reshape(3) for c in self.cams]).contiguous()
+            self._colors = torch.empty((V, P, NUM_CHANNELS), dtype=torch.float32, device=dev)
+            # the SH backward resets what it reads, so this stays zero between steps
+            self._grad_colors = torch.zeros((V, P, NUM_CHANNELS), dtype=torch.float32, device=dev)
 
     def _gaussians(self, rs) -> pl.Gaussians:
         means, scales, rots, opac, sh = self.params
@@ -165,7 +190,9 @@ class FusedViewStep:
         if target.shape != (NUM_CHANNELS, cam.H, cam.W):
             raise ValueError(f"target {i} must have shape (3, {cam.H}, {cam.W})")
         tgt = self._target(i, target)
-        pre = pl.preprocess(g, cam, mode, sparse=True)
+        if self.batch_sh:
+            g.sh, g.colors = None, self._colors[i]
+        pre = pl.preprocess(g, cam, mode, sparse=True, colors_clamp_signed=self.batch_sh)
         binned = pl.binning(pre, cam, mode, want_ids=True)
         ren = pl.render(pre, binned, cam, bg, False)
         _, dm = photometric_loss_forward(ren.color, tgt, self.l1_weight, self.ssim_weight, out=self.losses[i])
@@ -178,15 +205,17 @@ class FusedViewStep:
                                       False, P, grad_acc=acc_buf)
         v_means, v_scales, v_rots, v_opac, v_sh = self.grads.views
         out = pl.PreprocessGrads(grad_means3D=v_means, grad_means2D=None, grad_opacity=v_opac,
-                                 grad_scales=v_scales, grad_rotations=v_rots, grad_cov3D=None, grad_sh=v_sh,
-                                 grad_colors=None)
+                                 grad_scales=v_scales, grad_rotations=v_rots, grad_cov3D=None,
+                                 grad_sh=None if self.batch_sh else v_sh,
+                                 grad_colors=self._grad_colors[i] if self.batch_sh else None)
         if before_accumulate is not None:
             torch.cuda.current_stream(self.device).wait_event(before_accumulate)
         # reads each binned Gaussian's accumulator entry and zeroes it: the accumulator is all zero again
         # for the next view (render backward only touches binned Gaussians)
         pl.preprocess_backward(g, cam, pre.radii, pre.records, grad_acc, None, None, None, out=out, ids=binned.ids,
                                clear_grad_acc=True,
-                               densify_grad_accum=self.xyz_gradient_accum if self.densify_stats else None)
+                               densify_grad_accum=self.xyz_gradient_accum if self.densify_stats else None,
+                               grad_colors_clamped=self.batch_sh)
         if self.densify_stats:
             _lib.call("gsb_densify_stats", P, _lib.ptr(pre.radii), _lib.ptr(self.denom), _lib.ptr(self.max_radii2D),
                       _lib.stream_handle(self.device))
@@ -210,7 +239,14 @@ class FusedViewStep:
             if self._side is None:
                 self._side = torch.cuda.Stream(self.device)
             streams = (main, self._side) if self.concurrent_views else (main, main)
-            self.grads.zero_()
+            means, _, _, _, sh = self.params
+            if self.batch_sh:
+                # the SH block is stored whole by the SH backward; only the rest needs zeroing
+                self.grads.flat[: self.grads.flat.numel() - sh.numel()].zero_()
+                self.grads.attach()
+                pl.sh_colors_views(means, sh, self._sh_degree, self._campos, out=self._colors)
+            else:
+                self.grads.zero_()
             ready = torch.cuda.Event()
             ready.record(main)
             self._side.wait_event(ready)  # zeroed buffer, targets and parameters visible to both streams
@@ -222,5 +258,8 @@ class FusedViewStep:
                     prev = torch.cuda.Event()
                     prev.record(s)
             main.wait_event(prev)
+            if self.batch_sh:
+                pl.sh_backward_views(means, sh, self._sh_degree, self._campos, self._grad_colors, self.grads.views[4],
+                                     self.grads.views[0])
             self.grads.all_reduce(self.group)
         return self.losses

@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define GSB_ABI_VERSION 10
+#define GSB_ABI_VERSION 11
 
 #define GSB_OK 0
 #define GSB_ERR_INVALID (-1)  /* bad argument: ValueError in Python          */
@@ -99,6 +99,10 @@ typedef struct {
                            dimensions below 65536) */
   int sparse_records;   /* 1: write render records only where radius > 0 (nothing reads
                            the others: render and the id-list backward skip them) */
+  int colors_clamp_signed; /* 1: colors_precomp holds SH colours from gsb_sh_colors_views:
+                           a channel stored as -0.0 was clamped at zero (its record clamp
+                           bit is set and its colour is +0.0), so the records equal those
+                           of the SH path bit for bit */
 } gsb_preprocess_args;
 
 int gsb_preprocess_fwd(const gsb_preprocess_args* a, void* stream);
@@ -248,9 +252,47 @@ typedef struct {
                             full memset (the render backward only touches binned Gaussians) */
   float* densify_grad_accum; /* optional (P): += |d loss / d means2D (x, y)| per processed
                             Gaussian (3DGS add_densification_stats' gradient norm) */
+  int grad_colors_clamped; /* 1: grad_colors receives the colour gradient through the
+                            forward's clamp (0 for the channels whose record clamp bit is
+                            set): the input gsb_sh_backward_views takes */
 } gsb_preprocess_bwd_args;
 
 int gsb_preprocess_bwd(const gsb_preprocess_bwd_args* a, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* SH colour over several views (B200 addition for multi-view steps).       */
+/* Every view of a data-parallel step renders the same Gaussians, so the   */
+/* SH rows (up to 192 B per Gaussian) are read once per step instead of    */
+/* once per view in the forward and three times per view in the backward:  */
+/* gsb_sh_colors_views writes each view's clamped SH colour                 */
+/* (preprocess_kernels.py:272-342; fed to gsb_preprocess_fwd with           */
+/* colors_clamp_signed), and gsb_sh_backward_views turns the views' colour */
+/* gradients (gsb_preprocess_bwd with grad_colors_clamped) into the SH      */
+/* gradient and the view-direction term of the means gradient              */
+/* (backward_kernels.py:297-536), summed over the views in view order.      */
+/* ------------------------------------------------------------------------ */
+typedef struct {
+  int P, num_views;
+  int sh_degree, sh_coeffs;    /* degree and K (1..16) */
+  const float* means;          /* (P,3) */
+  const float* sh;             /* (P,K,3) */
+  const float* campos;         /* (num_views,3), device */
+  /* gsb_sh_colors_views */
+  float* colors;               /* out (num_views,P,3): max(SH colour + 0.5, 0) of every
+                                  Gaussian from each camera; clamped channels are -0.0 */
+  /* gsb_sh_backward_views */
+  float* grad_colors;          /* (num_views,P,3) clamped colour gradients; entries that are
+                                  not zero are reset to zero after reading when
+                                  clear_grad_colors is set */
+  int clear_grad_colors;
+  float* grad_sh;              /* out (P,K,3): stored (every row, zero where no view
+                                  contributes), or added to when accumulate is set */
+  float* grad_means3d;         /* (P,3): the direction term is added */
+  int accumulate;
+} gsb_sh_views_args;
+
+int gsb_sh_colors_views(const gsb_sh_views_args* a, void* stream);
+int gsb_sh_backward_views(const gsb_sh_views_args* a, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* Fused SSIM.  Replaces FusedSSIMMap (gswarp/fused_ssim.py:1074-1150) and   */

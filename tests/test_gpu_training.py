@@ -94,11 +94,13 @@ def _autograd_step(params, settings, targets, w1, w2):
     return step.grads.flat, torch.stack(res.losses)
 
 
+@pytest.mark.parametrize("batch_sh", [True, False])
 @pytest.mark.parametrize("n,views,W,H", [(20_000, 3, 320, 192), (200_000, 2, 960, 544)])
-def test_fused_step_matches_autograd_step(cuda, n, views, W, H):
+def test_fused_step_matches_autograd_step(cuda, n, views, W, H, batch_sh):
     params, settings, targets = _scene(cuda, n, views, W, H)
     ref_flat, ref_losses = _autograd_step(params, settings, targets, 1.0, 0.2)
-    fused = FusedViewStep([p.clone() for p in params], settings, 1.0, 0.2)
+    fused = FusedViewStep([p.clone() for p in params], settings, 1.0, 0.2, batch_sh=batch_sh)
+    assert fused.batch_sh == batch_sh
     losses = fused.step(targets)
     torch.cuda.synchronize()
     torch.testing.assert_close(losses[:, 0], ref_losses, rtol=1e-5, atol=1e-6)
@@ -112,9 +114,11 @@ def test_fused_step_matches_autograd_step(cuda, n, views, W, H):
         a, b = got[off:off + k], ref_flat[off:off + k]
         assert float((a - b).norm()) <= 1e-4 * float(b.norm()) + 1e-7
         off += k
-    # the persistent render-gradient accumulator is left all zero for the next view
+    # the persistent render-gradient accumulator (and the per-view colour gradients) are left all zero
     for buf in fused._grad_acc:
         assert buf is None or not bool(buf.any())
+    if batch_sh:
+        assert not bool(fused._grad_colors.any())
     # a second step re-zeroes and re-accumulates (no doubling)
     fused.step(targets)
     assert float((fused.grads.flat - got).norm()) <= 1e-4 * float(got.norm()) + 1e-7
@@ -178,3 +182,104 @@ def test_fused_step_views_with_nothing_visible(cuda):
     only_away.step([targets[0]])
     torch.cuda.synchronize()
     assert not bool(only_away.grads.flat.any())
+
+
+def _sh_scene(dev, K, n=30_000, views=3, W=320, H=192):
+    params, settings, _ = _scene(dev, n, views, W, H)
+    sh = params[4]
+    if K != sh.shape[1]:
+        g = torch.Generator().manual_seed(K)
+        sh = (0.4 * torch.randn(sh.shape[0], K, 3, generator=g)).to(dev)
+        sh[:, 0] = params[4][:, 0]
+        params[4] = sh.contiguous()
+    return params, settings
+
+
+@pytest.mark.parametrize("degree,K", [(3, 16), (2, 9), (1, 16), (0, 1), (1, 4)])
+def test_sh_colors_views_give_the_sh_path_records(cuda, degree, K):
+    """Colours of every view from one multi-view pass, fed back as signed-clamp colours, give render
+    records (colour and clamp bits) identical to the per-view SH evaluation."""
+    from gswarp_b200 import _pipeline as pl
+    from gswarp_b200._autograd import _camera
+    params, settings = _sh_scene(cuda, K)
+    means, scales, rots, opac, sh = params
+    cams = [_camera(rs) for rs in settings]
+    campos = torch.stack([c.campos.reshape(3) for c in cams])
+    colors = pl.sh_colors_views(means, sh, degree, campos)
+    assert colors.shape == (len(cams), means.shape[0], 3)
+    clamped = 0
+    for v, cam in enumerate(cams):
+        g_sh = pl.make_gaussians(means, opac, scales, rots, None, sh, None, 1.0, degree)
+        g_col = pl.make_gaussians(means, opac, scales, rots, None, None, colors[v], 1.0, degree)
+        a = pl.preprocess(g_sh, cam, 1)
+        b = pl.preprocess(g_col, cam, 1, colors_clamp_signed=True)
+        assert torch.equal(a.radii, b.radii)
+        vis = a.radii > 0
+        assert int(vis.sum()) > 100
+        ra, rb = a.records[vis].view(torch.int32), b.records[vis].view(torch.int32)
+        assert torch.equal(ra, rb)
+        clamped += int((a.records[vis][:, 7].view(torch.int32) != 0).sum())
+    if degree > 0:
+        assert clamped > 0  # the clamp encoding is exercised
+
+
+@pytest.mark.parametrize("degree,K,views", [(3, 16, 3), (2, 9, 3), (1, 4, 3), (3, 16, 10)])
+def test_sh_backward_views_matches_per_view_sh_backward(cuda, degree, K, views):
+    """Stage isolation on the same render gradients: per-view SH backward accumulated view by view
+    against per-view clamped colour gradients + one multi-view SH backward (its own FMA arithmetic,
+    channels contracted first): equal within float rounding; the other gradients are untouched by
+    the split and stay bit-exact."""
+    from gswarp_b200 import _pipeline as pl
+    from gswarp_b200._autograd import _camera
+    from gswarp_b200.training import photometric_loss_backward, photometric_loss_forward
+    params, settings = _sh_scene(cuda, K, views=views)
+    means, scales, rots, opac, sh = params
+    P = means.shape[0]
+    cams = [_camera(rs) for rs in settings]
+    bg = torch.zeros(3, device=cuda)
+
+    def grads():
+        return pl.PreprocessGrads(
+            grad_means3D=torch.zeros(P, 3, device=cuda), grad_means2D=None, grad_opacity=torch.zeros(P, device=cuda),
+            grad_scales=torch.zeros(P, 3, device=cuda), grad_rotations=torch.zeros(P, 4, device=cuda),
+            grad_cov3D=None, grad_sh=torch.zeros(P, K, 3, device=cuda), grad_colors=None)
+
+    out_a, out_b = grads(), grads()
+    grad_sh_b = out_b.grad_sh
+    out_b.grad_sh = None
+    dcol = torch.zeros(len(cams), P, 3, device=cuda)
+    g_sh = pl.make_gaussians(means, opac, scales, rots, None, sh, None, 1.0, degree)
+    g_nosh = pl.make_gaussians(means, opac, scales, rots, None, None, None, 1.0, degree)
+    for v, cam in enumerate(cams):
+        pre = pl.preprocess(g_sh, cam, 1, sparse=True)
+        binned = pl.binning(pre, cam, 1, want_ids=True)
+        ren = pl.render(pre, binned, cam, bg, False)
+        tgt = wl.target_image(40 + v, cam.H, cam.W).to(cuda)
+        _, dm = photometric_loss_forward(ren.color, tgt)
+        gimg = photometric_loss_backward(ren.color, tgt, dm)
+        acc = pl.render_backward(pre.records, binned, cam, bg, ren.alpha, ren.n_contrib, gimg, None, None, False, P)
+        pl.preprocess_backward(g_sh, cam, pre.radii, pre.records, acc, None, None, None, out=out_a, ids=binned.ids)
+        out_b.grad_colors = dcol[v]
+        pl.preprocess_backward(g_nosh, cam, pre.radii, pre.records, acc, None, None, None, out=out_b,
+                               ids=binned.ids, grad_colors_clamped=True)
+    assert bool(dcol.any())
+    campos = torch.stack([c.campos.reshape(3) for c in cams])
+    pl.sh_backward_views(means, sh, degree, campos, dcol, grad_sh_b, out_b.grad_means3D)
+    torch.cuda.synchronize()
+    ref_sh = out_a.grad_sh
+    assert float((grad_sh_b - ref_sh).norm()) <= 1e-5 * float(ref_sh.norm())
+    torch.testing.assert_close(grad_sh_b, ref_sh, rtol=1e-4, atol=1e-5 * float(ref_sh.abs().max()))
+    assert torch.equal((grad_sh_b != 0).any(-1).any(-1), (ref_sh != 0).any(-1).any(-1))  # same rows touched
+    assert float(grad_sh_b.abs().sum()) > 0
+    for x, y in ((out_b.grad_scales, out_a.grad_scales), (out_b.grad_rotations, out_a.grad_rotations),
+                 (out_b.grad_opacity, out_a.grad_opacity)):
+        assert torch.equal(x, y)
+    ref = out_a.grad_means3D
+    assert float((out_b.grad_means3D - ref).norm()) <= 1e-5 * float(ref.norm())
+    assert not bool(dcol.any())  # read entries were reset
+    # accumulate mode adds onto what is there
+    extra = torch.full_like(grad_sh_b, 0.5)
+    dcol_again = torch.zeros_like(dcol)
+    pl.sh_backward_views(means, sh, degree, campos, dcol_again, extra, torch.zeros(P, 3, device=cuda),
+                         accumulate=True)
+    assert bool((extra == 0.5).all())
