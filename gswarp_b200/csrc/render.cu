@@ -17,8 +17,10 @@
 // per batch from the 48-byte render records (three 16-byte loads per
 // Gaussian); exp is one MUFU.EX2, 1/(1-alpha) one MUFU.RCP.  Backward: the
 // CTA walks its list from the CTA-wide maximum contributor down, each warp
-// skips positions above its own maximum, a warp vote skips Gaussians no lane
-// uses, and the ten gradient terms (already summed over the thread's two
+// skips positions above its own maximum, tests each Gaussian against the two
+// halves of its block (rows holding every lane's first / second pixel) so a
+// half it cannot reach is skipped warp-wide, a warp vote skips Gaussians no
+// lane uses, and the ten gradient terms (already summed over the thread's two
 // pixels) are reduced across the warp with a 12-shuffle transpose reduction
 // (instead of 10 x 5 butterfly shuffles); 10 lanes then issue one float atomic
 // each into the per-Gaussian accumulator.
@@ -64,10 +66,6 @@ __device__ __forceinline__ float4 alpha_box(float x, float y, float a, float b, 
   return make_float4(x - ex, x + ex, y - ey, y + ey);
 }
 
-__device__ __forceinline__ bool box_hits(const float4 b, float x0, float x1, float y0, float y1) {
-  return b.x <= x1 && b.y >= x0 && b.z <= y1 && b.w >= y0;
-}
-
 // Ellipse data for the exact block test: conic (a, b, c) and the culling
 // threshold on q = a dx^2 + 2b dx dy + c dy^2.  alpha >= 1/255 needs
 // q <= t = 2 ln(255 op); the test uses t * 1.02 + 0.05 (alpha 2.5% below the
@@ -101,6 +99,30 @@ __device__ __forceinline__ bool ellipse_hits(float cx, float cy, const float4 e,
     q = fminf(q, e.z * Y * Y + (2.0f * e.y * Y + e.x * dx) * dx);
   }
   return q <= e.w;
+}
+
+// Which halves of the warp's 8x8 block staged Gaussian g can reach: rows
+// y0..y0+3 hold every lane's first pixel, rows y0+4..y0+7 every lane's
+// second pixel, so a half the Gaussian misses is a pixel the whole warp can
+// skip.  Box test first, then the exact ellipse test per half.  (Used by the
+// backward, whose per-pixel work pays for the second test; the forward's
+// cheaper per-pixel work does not, and it tests the whole block once.)
+__device__ __forceinline__ void cull_halves(int g, int cnt, const float4* s_box, const float2* s_xy,
+                                            const float4* s_el, float x0, float x1, float y0, bool& top,
+                                            bool& bot) {
+  top = bot = false;
+  if (g < cnt) {
+    const float4 b = s_box[g];
+    const bool xs = b.x <= x1 && b.y >= x0;
+    top = xs && b.z <= y0 + 3.0f && b.w >= y0;
+    bot = xs && b.z <= y0 + 7.0f && b.w >= y0 + 4.0f;
+  }
+  if (__any_sync(FULL, top || bot) && (top || bot)) {
+    const float2 c = s_xy[g];
+    const float4 e = s_el[g];
+    if (top) top = ellipse_hits(c.x, c.y, e, x0, x1, y0, y0 + 3.0f);
+    if (bot) bot = ellipse_hits(c.x, c.y, e, x0, x1, y0 + 4.0f, y0 + 7.0f);
+  }
 }
 
 // Exponent of a Gaussian at pixel offset (dx, dy) in log2 units, from the
@@ -187,7 +209,11 @@ __global__ void __launch_bounds__(THREADS, 10) render_fwd_kernel(const gsb_rende
     for (int cb = 0; cb < cnt; cb += 32) {
       if (__all_sync(FULL, done[0] && done[1])) break;
       const int g = cb + lane;
-      bool hit = g < cnt && box_hits(s_box[g], bx0, bx1, by0, by1);
+      bool hit = false;
+      if (g < cnt) {
+        const float4 bb = s_box[g];
+        hit = bb.x <= bx1 && bb.y >= bx0 && bb.z <= by1 && bb.w >= by0;
+      }
       if (__any_sync(FULL, hit) && hit) {
         const float2 cxy = s_xy[g];
         hit = ellipse_hits(cxy.x, cxy.y, s_el[g], bx0, bx1, by0, by1);
@@ -443,7 +469,7 @@ __global__ void __launch_bounds__(THREADS, 8) render_bwd_kernel(const gsb_render
   }
   const float fx = (float)pxi;
   const float bx0 = (float)(__shfl_sync(FULL, pxi, 0)), by0 = (float)(__shfl_sync(FULL, py0, 0));
-  const float bx1 = bx0 + 7.0f, by1 = by0 + 7.0f;
+  const float bx1 = bx0 + 7.0f;
 
   for (int hi = cta_max; hi > 0; hi -= BATCH) {
     const int lo = max(0, hi - BATCH);
@@ -468,29 +494,30 @@ __global__ void __launch_bounds__(THREADS, 8) render_bwd_kernel(const gsb_render
     // Lanes test staged Gaussians against the warp's 8x8 block; the warp
     // visits only the hits below its own maximum, back to front.
     for (int cb = ((top - lo - 1) >> 5) << 5; cb >= 0 && top > lo; cb -= 32) {
-      const int g = cb + lane;
-      bool hit = g < top - lo && box_hits(s_box[g], bx0, bx1, by0, by1);
-      if (__any_sync(FULL, hit) && hit) {
-        const float2 cxy = s_xy[g];
-        hit = ellipse_hits(cxy.x, cxy.y, s_el[g], bx0, bx1, by0, by1);
-      }
-      unsigned hits = __ballot_sync(FULL, hit);
+      bool ht, hb;
+      cull_halves(cb + lane, top - lo, s_box, s_xy, s_el, bx0, bx1, by0, ht, hb);
+      const unsigned top_h = __ballot_sync(FULL, ht), bot_h = __ballot_sync(FULL, hb);
+      unsigned hits = top_h | bot_h;
       while (hits) {
-      const int j = cb + 31 - __clz(hits);
-      hits &= ~(1u << (j - cb));
+      const int bit = 31 - __clz(hits);
+      const int j = cb + bit;
+      hits &= ~(1u << bit);
       const int pos = lo + j;
       BwdSums m = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
       bool contrib = false;
       float dx = 0.0f;
-      if (pos < px[0].lc || pos < px[1].lc) {
+      // a half the Gaussian cannot reach has alpha < 1/255 at every pixel: no state change to skip
+      const bool e0 = ((top_h >> bit) & 1u) && pos < px[0].lc;
+      const bool e1 = ((bot_h >> bit) & 1u) && pos < px[1].lc;
+      if (e0 || e1) {
         const float2 xy = s_xy[j];
         const float4 cf = s_cf[j];
         const float4 cd = s_rgbd[j];
         dx = xy.x - fx;
         float ax, bx;
         column_terms(cf, dx, ax, bx);
-        if (pos < px[0].lc) contrib |= bwd_pixel<DEPTH, GA>(px[0], cf, ax, bx, xy.y, cd, has_bg, m);
-        if (pos < px[1].lc) contrib |= bwd_pixel<DEPTH, GA>(px[1], cf, ax, bx, xy.y, cd, has_bg, m);
+        if (e0) contrib |= bwd_pixel<DEPTH, GA>(px[0], cf, ax, bx, xy.y, cd, has_bg, m);
+        if (e1) contrib |= bwd_pixel<DEPTH, GA>(px[1], cf, ax, bx, xy.y, cd, has_bg, m);
       }
       if (__any_sync(FULL, contrib)) {
         const float4 con = s_con[j];

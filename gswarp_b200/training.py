@@ -135,10 +135,10 @@ class FusedViewStep:
         self.device = dev
         self.losses = torch.zeros((len(self.settings), 3), dtype=torch.float32, device=dev)
         self._staging: dict[int, torch.Tensor] = {}
-        self._grad_acc: list[torch.Tensor | None] = [None, None]
-        self._side: torch.cuda.Stream | None = None
-        # two streams in turn (overlapping consecutive views); False = one stream
-        self.concurrent_views = True
+        self._grad_acc: list[torch.Tensor | None] = []
+        self._side: list[torch.cuda.Stream] = []
+        # consecutive views go to this many streams in turn (overlapping them); 1 = one stream
+        self.num_streams = 2
         # 3DGS densification statistics, accumulated per view until reset_densify_stats():
         # xyz_gradient_accum += |d loss / d means2D (x, y)|, denom += 1 and max_radii2D = max(., radius)
         # for every Gaussian with a radius in the view
@@ -162,6 +162,14 @@ class FusedViewStep:
             self._colors = torch.empty((V, P, NUM_CHANNELS), dtype=torch.float32, device=dev)
             # the SH backward resets what it reads, so this stays zero between steps
             self._grad_colors = torch.zeros((V, P, NUM_CHANNELS), dtype=torch.float32, device=dev)
+
+    @property
+    def concurrent_views(self) -> bool:
+        return self.num_streams > 1
+
+    @concurrent_views.setter
+    def concurrent_views(self, on: bool) -> None:
+        self.num_streams = 2 if on else 1
 
     def _gaussians(self, rs) -> pl.Gaussians:
         means, scales, rots, opac, sh = self.params
@@ -197,6 +205,8 @@ class FusedViewStep:
         ren = pl.render(pre, binned, cam, bg, False)
         _, dm = photometric_loss_forward(ren.color, tgt, self.l1_weight, self.ssim_weight, out=self.losses[i])
         grad_img = photometric_loss_backward(ren.color, tgt, dm, self.l1_weight, self.ssim_weight)
+        while len(self._grad_acc) <= lane:
+            self._grad_acc.append(None)
         acc_buf = self._grad_acc[lane]
         if acc_buf is None or acc_buf.shape[0] != P:
             acc_buf = torch.zeros((P, _lib.GRAD_FLOATS), dtype=torch.float32, device=self.device)
@@ -227,18 +237,19 @@ class FusedViewStep:
             self.max_radii2D.zero_()
 
     def step(self, targets: Sequence[torch.Tensor]) -> torch.Tensor:
-        """Runs every view, then the all-reduce.  Consecutive views go to two
-        streams in turn, so one view's compute-bound render kernels overlap
-        the next view's memory- and latency-bound preprocess and binning;
-        the accumulations into the flat gradient buffer stay in view order
-        (each waits for the previous one)."""
+        """Runs every view, then the all-reduce.  Consecutive views go to
+        ``num_streams`` streams in turn, so one view's compute-bound render
+        kernels overlap the next view's memory- and latency-bound preprocess
+        and binning; the accumulations into the flat gradient buffer stay in
+        view order (each waits for the previous one)."""
         if len(targets) != len(self.settings):
             raise ValueError(f"expected {len(self.settings)} targets, got {len(targets)}")
+        n_streams = max(1, int(self.num_streams))
         with torch.cuda.device(self.device):
             main = torch.cuda.current_stream(self.device)
-            if self._side is None:
-                self._side = torch.cuda.Stream(self.device)
-            streams = (main, self._side) if self.concurrent_views else (main, main)
+            while len(self._side) < n_streams - 1:
+                self._side.append(torch.cuda.Stream(self.device))
+            streams = [main] + self._side[: n_streams - 1]
             means, _, _, _, sh = self.params
             if self.batch_sh:
                 # the SH block is stored whole by the SH backward; only the rest needs zeroing
@@ -249,14 +260,16 @@ class FusedViewStep:
                 self.grads.zero_()
             ready = torch.cuda.Event()
             ready.record(main)
-            self._side.wait_event(ready)  # zeroed buffer, targets and parameters visible to both streams
+            for side in streams[1:]:
+                side.wait_event(ready)  # zeroed buffer, targets and parameters visible to every stream
             prev = None
             for i, t in enumerate(targets):
-                s = streams[i % 2]
+                s = streams[i % n_streams]
                 with torch.cuda.stream(s):
-                    self.view(i, t, before_accumulate=prev, lane=i % 2)
+                    self.view(i, t, before_accumulate=prev, lane=i % n_streams)
                     prev = torch.cuda.Event()
                     prev.record(s)
+            # the last view's event follows every earlier one (each view's accumulation waits for the previous)
             main.wait_event(prev)
             if self.batch_sh:
                 pl.sh_backward_views(means, sh, self._sh_degree, self._campos, self._grad_colors, self.grads.views[4],
