@@ -446,13 +446,14 @@ def cpu_baseline_sample(views, scene_cpu, band_rows=136):
 
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of each kernel at the default
-# workload (6M Gaussians, 1920x1080, first view), from a 1-pass ncu capture of
-# `python bench.py --steps 1 --warmup 1 --no-e2e --no-cfg2 --no-cpu-baseline --no-autograd`.
+# workload (6M Gaussians, 1920x1080, first view of the training step), from a 1-pass ncu capture of
+# `python bench.py --steps 1 --warmup 1 --no-e2e --no-autograd --no-cfg2 --no-cpu-baseline --no-optimizer`.
 MEASURED_TRAFFIC = {
-    "render_bwd": 262.66e6 + 32.25e6,
-    "render_fwd": 163.15e6 + 31.17e6,
-    "preprocess_bwd": 1.43e9 + 348.69e6,
-    "preprocess_fwd": 1.06e9 + 349.14e6,
+    "render_bwd": 262.64e6 + 31.48e6,
+    "render_fwd": 163.58e6 + 31.18e6,
+    "preprocess_bwd": 1136.76e6 + 450.03e6,
+    "preprocess_fwd": 379.93e6 + 336.40e6,
+    "sh_colors": 1224.03e6 + 544.70e6,
 }
 
 
