@@ -6,9 +6,10 @@
 // (:831-874) / _bwd_h_scalar_valid (:878-935) + _bwd_v_tiled (:985-1067) /
 // _bwd_v (:938-981).  The reference runs each direction as two kernels with
 // four (forward) or three (backward) full-size intermediate maps in HBM; here
-// each direction is ONE kernel per 32x16 output tile: the input tile plus a
+// each direction is ONE kernel per 32x40 output tile: the input tile plus a
 // 5-pixel halo is staged in shared memory, the horizontal pass writes shared
-// memory only, and the vertical pass produces the outputs.  Forward writes
+// memory only, and the vertical pass produces the outputs; both passes slide
+// their 11-tap windows over values held in registers.  Forward writes
 // only what backward needs (dm0, dm1, dm2) plus one partial SSIM sum per CTA;
 // a last tiny kernel turns the partial sums into the mean.
 //
@@ -20,11 +21,25 @@
 namespace gsb {
 namespace {
 
-constexpr int TX = 32, TY = 16;
+constexpr int TX = 32, TY = 40;
 constexpr int HALO = 5;
 constexpr int RX = TX + 2 * HALO;  // 42
-constexpr int RY = TY + 2 * HALO;  // 26
+constexpr int RY = TY + 2 * HALO;  // 50
 constexpr int THREADS = 256;
+// Register blocking: a thread runs the horizontal pass over RH consecutive
+// outputs of one row (its 11-tap windows slide over RH + 10 values held in
+// registers) and the vertical pass over RV consecutive outputs of one column,
+// so each staged value is read from shared memory about once per thread
+// instead of once per tap.  Row strides are odd: the warps' accesses hit 32
+// different banks.
+constexpr int RH = 8;
+constexpr int HSEG = TX / RH;         // row segments: 4
+constexpr int H_ITEMS = RY * HSEG;    // 200 horizontal work items
+constexpr int RV = 5;
+constexpr int VSEG = TY / RV;         // column segments: 8
+static_assert(TX * VSEG == THREADS, "one vertical work item per thread");
+static_assert(H_ITEMS <= THREADS, "one horizontal work item per thread at most");
+constexpr int STAGE_ITERS = (RY * RX + THREADS - 1) / THREADS;  // staged values per thread: 9
 
 __constant__ float GW[11] = {0.001028380123898387f, 0.0075987582094967365f,
                              0.036000773310661316f,  0.10936068743467331f,
@@ -53,77 +68,109 @@ __global__ void __launch_bounds__(THREADS) ssim_fwd_kernel(const gsb_ssim_fwd_ar
   const float* img1 = a.img1 + pbase;
   const float* img2 = a.img2 + pbase;
 
-  for (int i = threadIdx.x; i < RY * RX; i += THREADS) {
-    const int r = i / RX, c = i % RX;
-    const int gy = y0 - HALO + r, gxp = x0 - HALO + c;
-    float v1 = 0.0f, v2 = 0.0f;
-    if (gy >= 0 && gy < H && gxp >= 0 && gxp < W) {
-      v1 = __ldg(img1 + (size_t)gy * W + gxp);
-      v2 = __ldg(img2 + (size_t)gy * W + gxp);
-    }
-    s_x[r][c] = v1;
-    s_y[r][c] = v2;
-  }
-  __syncthreads();
-  // Horizontal pass (fused_ssim.py:477-511): symmetric tap pairs, then centre.
-  for (int i = threadIdx.x; i < RY * TX; i += THREADS) {
-    const int r = i / TX, c = i % TX;
-    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+  // Staging: all of a thread's loads are issued before its shared-memory
+  // stores, so their latencies overlap instead of adding up.
+  {
+    float v1[STAGE_ITERS], v2[STAGE_ITERS];
 #pragma unroll
-    for (int k = 0; k < 5; ++k) {
-      const float g = GW[k];
-      const float v1l = s_x[r][c + k], v2l = s_y[r][c + k];
-      const float v1r = s_x[r][c + 10 - k], v2r = s_y[r][c + 10 - k];
-      a0 += g * (v1l + v1r);
-      a1 += g * (v2l + v2r);
-      a2 += g * (v1l * v1l + v2l * v2l + v1r * v1r + v2r * v2r);
-      a3 += g * (v1l * v2l + v1r * v2r);
-    }
-    const float v1c = s_x[r][c + 5], v2c = s_y[r][c + 5];
-    a0 += GW[5] * v1c;
-    a1 += GW[5] * v2c;
-    a2 += GW[5] * (v1c * v1c + v2c * v2c);
-    a3 += GW[5] * v1c * v2c;
-    s_h[0][r][c] = a0;
-    s_h[1][r][c] = a1;
-    s_h[2][r][c] = a2;
-    s_h[3][r][c] = a3;
-  }
-  __syncthreads();
-  float local_sum = 0.0f, local_l1 = 0.0f;
-  const size_t npix = (size_t)a.B * a.C * H * W;
-  for (int i = threadIdx.x; i < TX * TY; i += THREADS) {
-    const int r = i / TX, c = i % TX;
-    const int gy = y0 + r, gxp = x0 + c;
-    if (gy >= H || gxp >= W) continue;
-    if (a.valid && (gy < 5 || gy >= H - 5 || gxp < 5 || gxp >= W - 5)) continue;
-    float s4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-    for (int k = 0; k < 5; ++k) {
-      const float g = GW[k];
-#pragma unroll
-      for (int m = 0; m < 4; ++m) {
-        const float top = s_h[m][r + k][c], bot = s_h[m][r + 10 - k][c];
-        if (a.valid) {
-          s4[m] += g * (top + bot);
-        } else {
-          s4[m] += g * top;
-          s4[m] += g * bot;
-        }
+    for (int it = 0; it < STAGE_ITERS; ++it) {
+      const int i = threadIdx.x + it * THREADS;
+      const int r = i / RX, c = i % RX;
+      const int gy = y0 - HALO + r, gxp = x0 - HALO + c;
+      v1[it] = v2[it] = 0.0f;
+      if (i < RY * RX && gy >= 0 && gy < H && gxp >= 0 && gxp < W) {
+        v1[it] = __ldg(img1 + (size_t)gy * W + gxp);
+        v2[it] = __ldg(img2 + (size_t)gy * W + gxp);
       }
     }
 #pragma unroll
-    for (int m = 0; m < 4; ++m) s4[m] += GW[5] * s_h[m][r + 5][c];
-    const float mu1 = s4[0], mu2 = s4[1];
+    for (int it = 0; it < STAGE_ITERS; ++it) {
+      const int i = threadIdx.x + it * THREADS;
+      if (i < RY * RX) {
+        s_x[i / RX][i % RX] = v1[it];
+        s_y[i / RX][i % RX] = v2[it];
+      }
+    }
+  }
+  __syncthreads();
+  // Horizontal pass (fused_ssim.py:477-511): symmetric tap pairs, then centre.
+  if (threadIdx.x < H_ITEMS) {
+    const int r = threadIdx.x / HSEG, c0 = (threadIdx.x % HSEG) * RH;
+    float xv[RH + 10], yv[RH + 10];
+#pragma unroll
+    for (int q = 0; q < RH + 10; ++q) {
+      xv[q] = s_x[r][c0 + q];
+      yv[q] = s_y[r][c0 + q];
+    }
+#pragma unroll
+    for (int j = 0; j < RH; ++j) {
+      float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+#pragma unroll
+      for (int k = 0; k < 5; ++k) {
+        const float g = GW[k];
+        const float v1l = xv[j + k], v2l = yv[j + k];
+        const float v1r = xv[j + 10 - k], v2r = yv[j + 10 - k];
+        a0 += g * (v1l + v1r);
+        a1 += g * (v2l + v2r);
+        a2 += g * (v1l * v1l + v2l * v2l + v1r * v1r + v2r * v2r);
+        a3 += g * (v1l * v2l + v1r * v2r);
+      }
+      const float v1c = xv[j + 5], v2c = yv[j + 5];
+      a0 += GW[5] * v1c;
+      a1 += GW[5] * v2c;
+      a2 += GW[5] * (v1c * v1c + v2c * v2c);
+      a3 += GW[5] * v1c * v2c;
+      s_h[0][r][c0 + j] = a0;
+      s_h[1][r][c0 + j] = a1;
+      s_h[2][r][c0 + j] = a2;
+      s_h[3][r][c0 + j] = a3;
+    }
+  }
+  __syncthreads();
+  // Vertical pass: column c, rows r0 .. r0 + RV - 1 of the tile.
+  const int c = threadIdx.x % TX, r0 = (threadIdx.x / TX) * RV;
+  float s4[RV][4];
+#pragma unroll
+  for (int m = 0; m < 4; ++m) {
+    float w[RV + 10];
+#pragma unroll
+    for (int q = 0; q < RV + 10; ++q) w[q] = s_h[m][r0 + q][c];
+#pragma unroll
+    for (int j = 0; j < RV; ++j) {
+      float acc = 0.0f;
+#pragma unroll
+      for (int k = 0; k < 5; ++k) {
+        const float g = GW[k];
+        const float top = w[j + k], bot = w[j + 10 - k];
+        if (a.valid) {
+          acc += g * (top + bot);
+        } else {
+          acc += g * top;
+          acc += g * bot;
+        }
+      }
+      acc += GW[5] * w[j + 5];
+      s4[j][m] = acc;
+    }
+  }
+  float local_sum = 0.0f, local_l1 = 0.0f;
+  const size_t npix = (size_t)a.B * a.C * H * W;
+  const int gxp = x0 + c;
+#pragma unroll
+  for (int j = 0; j < RV; ++j) {
+    const int gy = y0 + r0 + j;
+    if (gy >= H || gxp >= W) continue;
+    if (a.valid && (gy < 5 || gy >= H - 5 || gxp < 5 || gxp >= W - 5)) continue;
+    const float mu1 = s4[j][0], mu2 = s4[j][1];
     const float mu1_sq = mu1 * mu1, mu2_sq = mu2 * mu2, mu1mu2 = mu1 * mu2;
     const float Av = mu1_sq + mu2_sq + a.C1;
-    const float Bv = s4[2] - mu1_sq - mu2_sq + a.C2;
+    const float Bv = s4[j][2] - mu1_sq - mu2_sq + a.C2;
     const float Cv = 2.0f * mu1mu2 + a.C1;
-    const float Dv = 2.0f * (s4[3] - mu1mu2) + a.C2;
+    const float Dv = 2.0f * (s4[j][3] - mu1mu2) + a.C2;
     const float rA = 1.0f / Av, rB = 1.0f / Bv, rAB = rA * rB;
     const float m = Cv * Dv * rAB;
     local_sum += m;
-    if (WITH_L1) local_l1 += fabsf(s_x[r + HALO][c + HALO] - s_y[r + HALO][c + HALO]);
+    if (WITH_L1) local_l1 += fabsf(s_x[r0 + j + HALO][c + HALO] - s_y[r0 + j + HALO][c + HALO]);
     if (a.dm) {
       const size_t o = pbase + (size_t)gy * W + gxp;
       a.dm[o] = 2.0f * (mu2 * (Dv - Cv) * rAB + mu1 * m * (rB - rA));
@@ -189,65 +236,81 @@ __global__ void __launch_bounds__(THREADS) ssim_bwd_kernel(const gsb_ssim_bwd_ar
   const float scale = inv_n * (WITH_L1 ? upstream_host : a.upstream[0]);
   const int lo_y = a.valid ? 5 : 0, hi_y = a.valid ? H - 5 : H;
   const int lo_x = a.valid ? 5 : 0, hi_x = a.valid ? W - 5 : W;
-  for (int i = threadIdx.x; i < RY * RX; i += THREADS) {
-    const int r = i / RX, c = i % RX;
-    const int gy = y0 - HALO + r, gxp = x0 - HALO + c;
-    float d0 = 0.0f, d1 = 0.0f, d2 = 0.0f;
-    if (gy >= lo_y && gy < hi_y && gxp >= lo_x && gxp < hi_x) {
-      const size_t o = pbase + (size_t)gy * W + gxp;
-      d0 = __ldg(a.dm + o);
-      d1 = __ldg(a.dm + npix + o);
-      d2 = __ldg(a.dm + 2 * npix + o);
-    }
-    s_dm[0][r][c] = d0;
-    s_dm[1][r][c] = d1;
-    s_dm[2][r][c] = d2;
-  }
-  __syncthreads();
-  // Horizontal pass of dm * (upstream / N) (fused_ssim.py:844-868).
-  for (int i = threadIdx.x; i < RY * TX; i += THREADS) {
-    const int r = i / TX, c = i % TX;
-    float t0 = 0.0f, t1 = 0.0f, t2 = 0.0f;
+  {
+    float d[3][STAGE_ITERS];
 #pragma unroll
-    for (int k = 0; k < 5; ++k) {
-      const float gs = GW[k] * scale;
-      t0 += gs * s_dm[0][r][c + k];
-      t1 += gs * s_dm[1][r][c + k];
-      t2 += gs * s_dm[2][r][c + k];
-      t0 += gs * s_dm[0][r][c + 10 - k];
-      t1 += gs * s_dm[1][r][c + 10 - k];
-      t2 += gs * s_dm[2][r][c + 10 - k];
+    for (int it = 0; it < STAGE_ITERS; ++it) {
+      const int i = threadIdx.x + it * THREADS;
+      const int r = i / RX, c = i % RX;
+      const int gy = y0 - HALO + r, gxp = x0 - HALO + c;
+      d[0][it] = d[1][it] = d[2][it] = 0.0f;
+      if (i < RY * RX && gy >= lo_y && gy < hi_y && gxp >= lo_x && gxp < hi_x) {
+        const size_t o = pbase + (size_t)gy * W + gxp;
+        d[0][it] = __ldg(a.dm + o);
+        d[1][it] = __ldg(a.dm + npix + o);
+        d[2][it] = __ldg(a.dm + 2 * npix + o);
+      }
     }
-    const float gs = GW[5] * scale;
-    t0 += gs * s_dm[0][r][c + 5];
-    t1 += gs * s_dm[1][r][c + 5];
-    t2 += gs * s_dm[2][r][c + 5];
-    s_t[0][r][c] = t0;
-    s_t[1][r][c] = t1;
-    s_t[2][r][c] = t2;
+#pragma unroll
+    for (int it = 0; it < STAGE_ITERS; ++it) {
+      const int i = threadIdx.x + it * THREADS;
+      if (i < RY * RX)
+#pragma unroll
+        for (int m = 0; m < 3; ++m) s_dm[m][i / RX][i % RX] = d[m][it];
+    }
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < TX * TY; i += THREADS) {
-    const int r = i / TX, c = i % TX;
-    const int gy = y0 + r, gxp = x0 + c;
+  // Horizontal pass of dm * (upstream / N) (fused_ssim.py:844-868), one map at a time.
+  if (threadIdx.x < H_ITEMS) {
+    const int r = threadIdx.x / HSEG, c0 = (threadIdx.x % HSEG) * RH;
+#pragma unroll
+    for (int m = 0; m < 3; ++m) {
+      float dv[RH + 10];
+#pragma unroll
+      for (int q = 0; q < RH + 10; ++q) dv[q] = s_dm[m][r][c0 + q];
+#pragma unroll
+      for (int j = 0; j < RH; ++j) {
+        float t = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 5; ++k) {
+          const float gs = GW[k] * scale;
+          t += gs * dv[j + k];
+          t += gs * dv[j + 10 - k];
+        }
+        t += GW[5] * scale * dv[j + 5];
+        s_t[m][r][c0 + j] = t;
+      }
+    }
+  }
+  __syncthreads();
+  const int c = threadIdx.x % TX, r0 = (threadIdx.x / TX) * RV;
+  float acc3[RV][3];
+#pragma unroll
+  for (int m = 0; m < 3; ++m) {
+    float w[RV + 10];
+#pragma unroll
+    for (int q = 0; q < RV + 10; ++q) w[q] = s_t[m][r0 + q][c];
+#pragma unroll
+    for (int j = 0; j < RV; ++j) {
+      float acc = 0.0f;
+#pragma unroll
+      for (int k = 0; k < 5; ++k) {
+        const float g = GW[k];
+        acc += g * w[j + k];
+        acc += g * w[j + 10 - k];
+      }
+      acc += GW[5] * w[j + 5];
+      acc3[j][m] = acc;
+    }
+  }
+  const int gxp = x0 + c;
+#pragma unroll
+  for (int j = 0; j < RV; ++j) {
+    const int gy = y0 + r0 + j;
     if (gy >= H || gxp >= W) continue;
-    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f;
-#pragma unroll
-    for (int k = 0; k < 5; ++k) {
-      const float g = GW[k];
-      a0 += g * s_t[0][r + k][c];
-      a1 += g * s_t[1][r + k][c];
-      a2 += g * s_t[2][r + k][c];
-      a0 += g * s_t[0][r + 10 - k][c];
-      a1 += g * s_t[1][r + 10 - k][c];
-      a2 += g * s_t[2][r + 10 - k][c];
-    }
-    a0 += GW[5] * s_t[0][r + 5][c];
-    a1 += GW[5] * s_t[1][r + 5][c];
-    a2 += GW[5] * s_t[2][r + 5][c];
     const size_t o = pbase + (size_t)gy * W + gxp;
     const float x1 = __ldg(a.img1 + o), x2 = __ldg(a.img2 + o);
-    float gv = a0 + 2.0f * x1 * a1 + x2 * a2;
+    float gv = acc3[j][0] + 2.0f * x1 * acc3[j][1] + x2 * acc3[j][2];
     if (WITH_L1) {
       const float d = x1 - x2;
       gv = gv + (d > 0.0f ? l1_scale : (d < 0.0f ? -l1_scale : 0.0f));
@@ -420,13 +483,13 @@ GSB_EXPORT int gsb_photo_loss_bwd(const gsb_photo_loss_bwd_args* a, void* stream
 // cudaMalloc/cudaFree round trip (cudaFree synchronizes the device) is not
 // acceptable.  This entry point computes the same mean SSIM (and, if `dm` is
 // given, the same dm maps) as gsb_ssim_fwd but keeps its only scratch -- one
-// partial sum per 32x16 output tile -- in a fixed device array that lives in
+// partial sum per 32x40 output tile -- in a fixed device array that lives in
 // this library for as long as it is loaded (256 KiB on every GPU that loads
 // it), so it allocates nothing.
 //
 // Limits and sharing rules:
-//  * at most GSB_SSIM_NOALLOC_MAX_PARTIALS tiles, i.e. B*C*ceil(H/16)*
-//    ceil(W/32) <= 65536 (four 3x1080x1920 images need 48,960); larger
+//  * at most GSB_SSIM_NOALLOC_MAX_PARTIALS tiles, i.e. B*C*ceil(H/40)*
+//    ceil(W/32) <= 65536 (four 3x1080x1920 images need 19,440); larger
 //    inputs are rejected with GSB_ERR_INVALID;
 //  * every call on a device shares the one array and it keeps the last
 //    call's partial sums; each call writes every slot it later reads, so
@@ -487,7 +550,7 @@ GSB_EXPORT int gsb_ssim_fwd_noalloc(int B, int C, int H, int W, int valid, float
   const long long blocks = (long long)B * C * tx * ty;
   if (blocks > NOALLOC_MAX_PARTIALS) {
     set_error("gsb_ssim_fwd_noalloc: %lld output tiles exceed the fixed scratch of %d "
-              "(B*C*ceil(H/16)*ceil(W/32) must be <= %d); use gsb_ssim_fwd with a workspace",
+              "(B*C*ceil(H/40)*ceil(W/32) must be <= %d); use gsb_ssim_fwd with a workspace",
               blocks, NOALLOC_MAX_PARTIALS, NOALLOC_MAX_PARTIALS);
     return GSB_ERR_INVALID;
   }

@@ -361,7 +361,7 @@ int gsb_photo_loss_bwd(const gsb_photo_loss_bwd_args* a, void* stream);
  * without a device allocator, or a loop that cannot afford a cudaMalloc /
  * cudaFree round trip).  Same result as gsb_ssim_fwd (mean SSIM into *loss,
  * dm maps if dm is non-NULL), but its scratch is a fixed 256 KiB device array
- * inside the library, so B*C*ceil(H/16)*ceil(W/32) must not exceed
+ * inside the library, so B*C*ceil(H/40)*ceil(W/32) must not exceed
  * GSB_SSIM_NOALLOC_MAX_PARTIALS (larger inputs return GSB_ERR_INVALID).
  * All calls on a device share that array: calls whose kernels overlap on the
  * GPU race.  The first call on a device looks up the array's address; make

@@ -38,7 +38,7 @@ def test_workspace_queries_are_host_only():
     assert 0 < a < b
     assert L.gsb_bin_sort_workspace_bytes(10_000_000, 1920, 1080) > 10_000_000 * 12
     assert L.gsb_knn_workspace_bytes(2_000_000) > 2_000_000 * 28
-    assert L.gsb_ssim_partials_count(4, 3, 1080, 1920) == 12 * 60 * 68
+    assert L.gsb_ssim_partials_count(4, 3, 1080, 1920) == 12 * 60 * 27
 
 
 def test_invalid_arguments_map_to_value_error():

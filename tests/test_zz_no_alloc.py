@@ -79,7 +79,7 @@ def test_noalloc_rejects_inputs_beyond_its_fixed_scratch():
     dev = torch.device("cuda:0")
     fn = _declare(_lib.load())
     x = torch.zeros(1, device=dev)
-    # 8 x 3 x 1088 x 2048 images need 8*3*68*64 = 104,448 tiles > 65,536
-    st = fn(8, 3, 1088, 2048, 0, C1, C2, _lib.ptr(x), _lib.ptr(x), None, _lib.ptr(x), _lib.stream_handle(dev))
+    # 16 x 3 x 2048 x 2048 images need 16*3*52*64 = 159,744 tiles > 65,536
+    st = fn(16, 3, 2048, 2048, 0, C1, C2, _lib.ptr(x), _lib.ptr(x), None, _lib.ptr(x), _lib.stream_handle(dev))
     assert st == _lib.GSB_ERR_INVALID
     assert b"fixed scratch" in _lib.load().gsb_last_error()
