@@ -24,7 +24,7 @@ GSB_ERR_OVERFLOW = -2
 GSB_ERR_CUDA = -3
 GSB_ERR_TIMEOUT = -4
 
-ABI_VERSION = 11
+ABI_VERSION = 12
 RECORD_FLOATS = 12
 GRAD_FLOATS = 12
 
@@ -114,7 +114,7 @@ class SHViewsArgs(ctypes.Structure):
         ("P", c_int), ("num_views", c_int), ("sh_degree", c_int), ("sh_coeffs", c_int),
         ("means", vp), ("sh", vp), ("campos", vp), ("colors", vp),
         ("grad_colors", vp), ("clear_grad_colors", c_int), ("grad_sh", vp), ("grad_means3d", vp),
-        ("accumulate", c_int),
+        ("accumulate", c_int), ("begin", c_int), ("end", c_int),
     ]
 
 

@@ -511,10 +511,12 @@ def sh_colors_views(means: torch.Tensor, sh: torch.Tensor, degree: int, campos: 
 
 def sh_backward_views(means: torch.Tensor, sh: torch.Tensor, degree: int, campos: torch.Tensor,
                       grad_colors: torch.Tensor, grad_sh: torch.Tensor, grad_means3D: torch.Tensor,
-                      accumulate: bool = False, clear_grad_colors: bool = True) -> None:
+                      accumulate: bool = False, clear_grad_colors: bool = True, begin: int = 0,
+                      end: int | None = None) -> None:
     """SH gradient (stored into ``grad_sh``, or added with ``accumulate``) and
     the view-direction term of the means gradient (added into
-    ``grad_means3D``) from the views' clamped colour gradients (V,P,3)."""
+    ``grad_means3D``) from the views' clamped colour gradients (V,P,3), for
+    the Gaussians [begin, end) (all by default)."""
     means, sh, campos = _f32(means), _f32(sh), _f32(campos)
     a = _sh_views_args(means, sh, degree, campos)
     P = means.shape[0]
@@ -524,6 +526,12 @@ def sh_backward_views(means: torch.Tensor, sh: torch.Tensor, degree: int, campos
             raise ValueError(f"gradient buffer must be contiguous fp32 {shape}")
     a.grad_colors, a.grad_sh, a.grad_means3d = _lib.ptr(grad_colors), _lib.ptr(grad_sh), _lib.ptr(grad_means3D)
     a.clear_grad_colors, a.accumulate = int(clear_grad_colors), int(accumulate)
+    end = P if end is None else int(end)
+    if not 0 <= begin <= end <= P:
+        raise ValueError(f"need 0 <= begin <= end <= {P}")
+    if begin == end:
+        return
+    a.begin, a.end = int(begin), end
     with torch.cuda.device(means.device), _stage_timer("sh_backward", {"kernels": 1}):
         _lib.call("gsb_sh_backward_views", a, _lib.stream_handle(means.device))
 

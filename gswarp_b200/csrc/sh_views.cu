@@ -107,14 +107,17 @@ template <int USED>
 __global__ void __launch_bounds__(SHV_THREADS, 4) sh_backward_views_kernel(const gsb_sh_views_args a) {
   __shared__ float s_rows[SHV_THREADS * SHV_ROW_F];
   __shared__ float s_g[WARPS][VCHUNK][96];
-  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  // Gaussians [first, last): the warps start at `first` (a multiple of 32
+  // is not required: rows are addressed from the warp's own base).
+  const int first = a.begin, last = a.end;
+  const int idx = first + blockIdx.x * blockDim.x + threadIdx.x;
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int base = idx - lane;
-  if (base >= a.P) return;  // whole warp past P
-  const bool live = idx < a.P;
+  if (base >= last) return;  // whole warp past the range
+  const bool live = idx < last;
   const int K = a.sh_coeffs, RF = K * 3;
-  const int rows_here = min(32, a.P - base);
+  const int rows_here = min(32, last - base);
   const int n_here = rows_here * 3;
   float* rows = s_rows + warp * SHV_ROW_F * 32;
   const size_t plane = (size_t)a.P * 3;
@@ -225,18 +228,25 @@ GSB_EXPORT int gsb_sh_backward_views(const gsb_sh_views_args* a, void* stream) {
     set_error("gsb_sh_backward_views: null pointer argument");
     return GSB_ERR_INVALID;
   }
+  gsb_sh_views_args r = *a;
+  if (r.begin == 0 && r.end == 0) r.end = r.P;
+  if (r.begin < 0 || r.end > r.P || r.begin > r.end) {
+    set_error("gsb_sh_backward_views: need 0 <= begin <= end <= P");
+    return GSB_ERR_INVALID;
+  }
+  if (r.begin == r.end) return GSB_OK;
   // coefficients the degree uses (degree and K both bound it)
   int used = 1;
   if (a->sh_degree > 0 && a->sh_coeffs > 3) used = 4;
   if (a->sh_degree > 1 && a->sh_coeffs > 8) used = 9;
   if (a->sh_degree > 2 && a->sh_coeffs > 15) used = 16;
-  const int blocks = div_up(a->P, SHV_THREADS);
+  const int blocks = div_up(r.end - r.begin, SHV_THREADS);
   cudaStream_t s = (cudaStream_t)stream;
   switch (used) {
-    case 1: sh_backward_views_kernel<1><<<blocks, SHV_THREADS, 0, s>>>(*a); break;
-    case 4: sh_backward_views_kernel<4><<<blocks, SHV_THREADS, 0, s>>>(*a); break;
-    case 9: sh_backward_views_kernel<9><<<blocks, SHV_THREADS, 0, s>>>(*a); break;
-    default: sh_backward_views_kernel<16><<<blocks, SHV_THREADS, 0, s>>>(*a); break;
+    case 1: sh_backward_views_kernel<1><<<blocks, SHV_THREADS, 0, s>>>(r); break;
+    case 4: sh_backward_views_kernel<4><<<blocks, SHV_THREADS, 0, s>>>(r); break;
+    case 9: sh_backward_views_kernel<9><<<blocks, SHV_THREADS, 0, s>>>(r); break;
+    default: sh_backward_views_kernel<16><<<blocks, SHV_THREADS, 0, s>>>(r); break;
   }
   return check_launch("sh_backward_views_kernel");
 }

@@ -94,6 +94,11 @@ def photometric_loss_backward(img: torch.Tensor, target: torch.Tensor, dm: torch
     return g
 
 
+def _distributed(group) -> bool:
+    return (torch.distributed.is_available() and torch.distributed.is_initialized()
+            and torch.distributed.get_world_size(group) > 1)
+
+
 class FusedViewStep:
     """One data-parallel training step over this rank's views, fused.
 
@@ -139,6 +144,9 @@ class FusedViewStep:
         self._side: list[torch.cuda.Stream] = []
         # consecutive views go to this many streams in turn (overlapping them); 1 = one stream
         self.num_streams = 2
+        # with a process group and multi-view SH: Gaussian ranges whose SH gradients are all-reduced
+        # while the next range's SH backward runs
+        self.reduce_chunks = 4
         # 3DGS densification statistics, accumulated per view until reset_densify_stats():
         # xyz_gradient_accum += |d loss / d means2D (x, y)|, denom += 1 and max_radii2D = max(., radius)
         # for every Gaussian with a radius in the view
@@ -271,8 +279,35 @@ class FusedViewStep:
                     prev.record(s)
             # the last view's event follows every earlier one (each view's accumulation waits for the previous)
             main.wait_event(prev)
-            if self.batch_sh:
+            if not self.batch_sh:
+                self.grads.all_reduce(self.group)
+            elif not _distributed(self.group):
                 pl.sh_backward_views(means, sh, self._sh_degree, self._campos, self._grad_colors, self.grads.views[4],
                                      self.grads.views[0])
-            self.grads.all_reduce(self.group)
+            else:
+                self._sh_backward_and_reduce(means, sh)
         return self.losses
+
+    def _sh_backward_and_reduce(self, means: torch.Tensor, sh: torch.Tensor) -> None:
+        """SH backward in ranges of Gaussians, each range's SH gradient
+        all-reduced (on NCCL's stream) while the next range is computed; the
+        rest of the buffer (means, scales, rotations, opacities: complete
+        after the last view, except the means' direction term, which the SH
+        backward adds) goes last.  The sums are elementwise, so the result
+        equals one all-reduce of the whole buffer."""
+        P = means.shape[0]
+        flat = self.grads.flat
+        sh_off = flat.numel() - sh.numel()
+        row = sh.numel() // max(P, 1)
+        chunks = max(1, min(self.reduce_chunks, P))
+        works = []
+        for c in range(chunks):
+            b, e = P * c // chunks, P * (c + 1) // chunks
+            pl.sh_backward_views(means, sh, self._sh_degree, self._campos, self._grad_colors, self.grads.views[4],
+                                 self.grads.views[0], begin=b, end=e)
+            if e > b:
+                works.append(torch.distributed.all_reduce(flat[sh_off + b * row: sh_off + e * row], group=self.group,
+                                                          async_op=True))
+        works.append(torch.distributed.all_reduce(flat[:sh_off], group=self.group, async_op=True))
+        for w in works:
+            w.wait()

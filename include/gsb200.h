@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define GSB_ABI_VERSION 11
+#define GSB_ABI_VERSION 12
 
 #define GSB_OK 0
 #define GSB_ERR_INVALID (-1)  /* bad argument: ValueError in Python          */
@@ -289,6 +289,9 @@ typedef struct {
                                   contributes), or added to when accumulate is set */
   float* grad_means3d;         /* (P,3): the direction term is added */
   int accumulate;
+  int begin, end;              /* gsb_sh_backward_views: the Gaussians [begin, end) only
+                                  (0, 0 = all P), so a caller can start reducing one range
+                                  across GPUs while the next is computed */
 } gsb_sh_views_args;
 
 int gsb_sh_colors_views(const gsb_sh_views_args* a, void* stream);
