@@ -167,20 +167,22 @@ __global__ void __launch_bounds__(THREADS, 4) onesweep_kernel(
     key[i] = valid ? keys_in[pos] : 0xFFFFFFFFu;
     rank[i] = valid ? 0u : 0xFFFFFFFFu;  // invalid marker
   }
-  // Stable warp-local ranking: round i holds 32 consecutive keys.
+  // Stable warp-local ranking: round i holds 32 consecutive keys.  The
+  // lowest lane of each digit group adds the group's size to the warp's
+  // counter with a shared atomic and hands the old count to its peers: no
+  // read-then-write chain between rounds (shared atomics of one warp to one
+  // address take effect in issue order, so rounds keep their order).
+  const unsigned lt = lanemask_lt();
 #pragma unroll
   for (int i = 0; i < ITEMS; ++i) {
     const bool valid = rank[i] != 0xFFFFFFFFu;
     const unsigned d = valid ? (key[i] >> shift) & (RADIX - 1) : (unsigned)RADIX;
     const unsigned peers = digit_peers(d);
+    const int leader = __ffs(peers) - 1;
     unsigned old = 0;
-    if (valid) {
-      old = s_warp_hist[warp][d];
-      rank[i] = old + __popc(peers & lanemask_lt());
-    }
-    __syncwarp();
-    if (valid && lane == __ffs(peers) - 1) s_warp_hist[warp][d] = old + __popc(peers);
-    __syncwarp();
+    if (valid && lane == leader) old = atomicAdd(&s_warp_hist[warp][d], (unsigned)__popc(peers));
+    old = __shfl_sync(0xffffffffu, old, leader);
+    if (valid) rank[i] = old + __popc(peers & lt);
   }
   __syncthreads();
 
