@@ -84,18 +84,37 @@ __device__ __forceinline__ bool conic_rect_intersects(float px, float py, float 
   return q_min <= threshold + COVERAGE_Q_EPSILON;
 }
 
-// math_kernels.py:242-303: AccuTile tile interval of one band.
-__device__ __forceinline__ void band_interval(float pu, float pv, float cuu, float cuv, float cvv,
-                                              float threshold, int tile_v, int block_u,
-                                              int block_v, int rect_u_min, int rect_u_max,
-                                              int& lo, int& hi) {
-  float det = cuu * cvv - cuv * cuv;
-  if (cuu <= 0.0f || cvv <= 0.0f || det <= DET_EPSILON) {
+// math_kernels.py:242-303: AccuTile tile interval of one band.  The terms
+// that do not depend on the band (determinant, padded threshold, the
+// ellipse's u-extent and the v at its u-extremes) are computed once per
+// Gaussian by band_setup, with the same expressions, so every band sees the
+// same bits as a per-band evaluation.
+struct BandSetup {
+  bool degenerate;
+  float det, ts, extent_u, v_at_min_u, v_at_max_u;
+};
+
+__device__ __forceinline__ BandSetup band_setup(float cuu, float cuv, float cvv, float threshold) {
+  BandSetup b;
+  b.det = cuu * cvv - cuv * cuv;
+  b.degenerate = cuu <= 0.0f || cvv <= 0.0f || b.det <= DET_EPSILON;
+  b.ts = threshold + COVERAGE_Q_EPSILON;
+  // unused (and possibly not finite) when degenerate
+  b.extent_u = sqrtf(fmx(b.ts * cvv / b.det, 0.0f));
+  b.v_at_min_u = cuv * b.extent_u / cvv;
+  b.v_at_max_u = -cuv * b.extent_u / cvv;
+  return b;
+}
+
+__device__ __forceinline__ void band_interval(float pu, float pv, float cuu, float cuv, const BandSetup& bs,
+                                              int tile_v, int block_u, int block_v, int rect_u_min,
+                                              int rect_u_max, int& lo, int& hi) {
+  if (bs.degenerate) {
     lo = rect_u_min;
     hi = rect_u_max;
     return;
   }
-  float ts = threshold + COVERAGE_Q_EPSILON;
+  const float det = bs.det, ts = bs.ts;
   float v0 = (float)(tile_v * block_v) - pv;
   float v1 = (float)(tile_v * block_v + block_v - 1) - pv;
   float u_min = FLT_BIG, u_max = -FLT_BIG;
@@ -116,15 +135,13 @@ __device__ __forceinline__ void band_interval(float pu, float pv, float cuu, flo
     u_max = fmx(u_max, center + half);
     found = true;
   }
-  float extent_u = sqrtf(fmx(ts * cvv / det, 0.0f));
-  float v_at_min_u = cuv * extent_u / cvv;
-  if (v_at_min_u >= v0 - COVERAGE_Q_EPSILON && v_at_min_u <= v1 + COVERAGE_Q_EPSILON) {
+  const float extent_u = bs.extent_u;
+  if (bs.v_at_min_u >= v0 - COVERAGE_Q_EPSILON && bs.v_at_min_u <= v1 + COVERAGE_Q_EPSILON) {
     u_min = fmn(u_min, -extent_u);
     u_max = fmx(u_max, -extent_u);
     found = true;
   }
-  float v_at_max_u = -cuv * extent_u / cvv;
-  if (v_at_max_u >= v0 - COVERAGE_Q_EPSILON && v_at_max_u <= v1 + COVERAGE_Q_EPSILON) {
+  if (bs.v_at_max_u >= v0 - COVERAGE_Q_EPSILON && bs.v_at_max_u <= v1 + COVERAGE_Q_EPSILON) {
     u_min = fmn(u_min, extent_u);
     u_max = fmx(u_max, extent_u);
     found = true;
@@ -186,16 +203,18 @@ __device__ __forceinline__ int cover_tiles_in_rect(float px, float py, float ca,
     return count;
   }
   if (span_y <= span_x) {
+    const BandSetup bs = band_setup(ca, cb, cc, t);
     for (int ty = r.y0; ty < r.y1; ++ty) {
       int lo, hi;
-      band_interval(px, py, ca, cb, cc, t, ty, BLOCK_X, BLOCK_Y, r.x0, r.x1, lo, hi);
+      band_interval(px, py, ca, cb, bs, ty, BLOCK_X, BLOCK_Y, r.x0, r.x1, lo, hi);
       count += imx(0, hi - lo);
       for (int tx = lo; tx < hi; ++tx) emit(ty * gx + tx);
     }
   } else {
+    const BandSetup bs = band_setup(cc, cb, ca, t);
     for (int tx = r.x0; tx < r.x1; ++tx) {
       int lo, hi;
-      band_interval(py, px, cc, cb, ca, t, tx, BLOCK_Y, BLOCK_X, r.y0, r.y1, lo, hi);
+      band_interval(py, px, cc, cb, bs, tx, BLOCK_Y, BLOCK_X, r.y0, r.y1, lo, hi);
       count += imx(0, hi - lo);
       for (int ty = lo; ty < hi; ++ty) emit(ty * gx + tx);
     }
@@ -261,12 +280,13 @@ __device__ __forceinline__ int coverage_record(float px, float py, float ca, flo
   const int nb = vertical ? span_x : span_y;
   const bool fits = nb <= BINREC_MAX_BANDS;
   w[2] = (fits ? BINREC_BANDS : BINREC_SWEEP) | (vertical ? 4u : 0u) | ((unsigned)nb << 8);
+  const BandSetup bs = vertical ? band_setup(cc, cb, ca, t) : band_setup(ca, cb, cc, t);
   for (int b = 0; b < nb; ++b) {
     int lo, hi;
     if (!vertical)
-      band_interval(px, py, ca, cb, cc, t, r.y0 + b, BLOCK_X, BLOCK_Y, r.x0, r.x1, lo, hi);
+      band_interval(px, py, ca, cb, bs, r.y0 + b, BLOCK_X, BLOCK_Y, r.x0, r.x1, lo, hi);
     else
-      band_interval(py, px, cc, cb, ca, t, r.x0 + b, BLOCK_Y, BLOCK_X, r.y0, r.y1, lo, hi);
+      band_interval(py, px, cc, cb, bs, r.x0 + b, BLOCK_Y, BLOCK_X, r.y0, r.y1, lo, hi);
     count += imx(0, hi - lo);
     if (fits && b < BINREC_MAX_BANDS) w[3 + b] = (unsigned)lo | ((unsigned)hi << 16);
   }
