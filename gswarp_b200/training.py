@@ -140,6 +140,8 @@ class FusedViewStep:
         self.device = dev
         self.losses = torch.zeros((len(self.settings), 3), dtype=torch.float32, device=dev)
         self._staging: dict[int, torch.Tensor] = {}
+        self._target_ready: dict[int, torch.cuda.Event] = {}
+        self._copy_stream: torch.cuda.Stream | None = None
         self._grad_acc: list[torch.Tensor | None] = []
         self._side: list[torch.cuda.Stream] = []
         # consecutive views go to this many streams in turn (overlapping them); 1 = one stream
@@ -183,15 +185,39 @@ class FusedViewStep:
         means, scales, rots, opac, sh = self.params
         return pl.make_gaussians(means, opac, scales, rots, None, sh, None, rs.scale_modifier, rs.sh_degree)
 
-    def _target(self, i: int, t: torch.Tensor) -> torch.Tensor:
-        if t.device == self.device:
-            return pl._f32(t)
+    def _staging_buffer(self, i: int, t: torch.Tensor) -> torch.Tensor:
         buf = self._staging.get(i)
         if buf is None or buf.shape != t.shape:
             buf = torch.empty(t.shape, dtype=torch.float32, device=self.device)
             self._staging[i] = buf
-        buf.copy_(t, non_blocking=True)
         return buf
+
+    def _upload_targets(self, targets: Sequence[torch.Tensor], main: torch.cuda.Stream) -> None:
+        """Host targets are copied on a copy stream at the start of the step,
+        each with an event that only its view's loss waits for, so the copies
+        overlap the views' preprocess, binning and render."""
+        if all(t.device == self.device for t in targets):
+            return
+        if self._copy_stream is None:
+            self._copy_stream = torch.cuda.Stream(self.device)
+        self._copy_stream.wait_stream(main)  # the previous step is done with the staging buffers
+        with torch.cuda.stream(self._copy_stream):
+            for i, t in enumerate(targets):
+                if t.device == self.device:
+                    continue
+                self._staging_buffer(i, t).copy_(t, non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(self._copy_stream)
+                self._target_ready[i] = ev
+
+    def _target(self, i: int, t: torch.Tensor) -> tuple[torch.Tensor, torch.cuda.Event | None]:
+        if t.device == self.device:
+            return pl._f32(t), None
+        ready = self._target_ready.pop(i, None)
+        buf = self._staging_buffer(i, t)
+        if ready is None:  # not uploaded by step(): copy in stream order
+            buf.copy_(t, non_blocking=True)
+        return buf, ready
 
     def view(self, i: int, target: torch.Tensor, before_accumulate: torch.cuda.Event | None = None,
              lane: int = 0) -> None:
@@ -205,12 +231,14 @@ class FusedViewStep:
         P = g.P
         if target.shape != (NUM_CHANNELS, cam.H, cam.W):
             raise ValueError(f"target {i} must have shape (3, {cam.H}, {cam.W})")
-        tgt = self._target(i, target)
+        tgt, tgt_ready = self._target(i, target)
         if self.batch_sh:
             g.sh, g.colors = None, self._colors[i]
         pre = pl.preprocess(g, cam, mode, sparse=True, colors_clamp_signed=self.batch_sh)
         binned = pl.binning(pre, cam, mode, want_ids=True)
         ren = pl.render(pre, binned, cam, bg, False)
+        if tgt_ready is not None:
+            torch.cuda.current_stream(self.device).wait_event(tgt_ready)
         _, dm = photometric_loss_forward(ren.color, tgt, self.l1_weight, self.ssim_weight, out=self.losses[i])
         grad_img = photometric_loss_backward(ren.color, tgt, dm, self.l1_weight, self.ssim_weight)
         while len(self._grad_acc) <= lane:
@@ -266,6 +294,7 @@ class FusedViewStep:
                 pl.sh_colors_views(means, sh, self._sh_degree, self._campos, out=self._colors)
             else:
                 self.grads.zero_()
+            self._upload_targets(targets, main)
             ready = torch.cuda.Event()
             ready.record(main)
             for side in streams[1:]:
