@@ -28,162 +28,192 @@ constexpr int SCAN_THREADS = 256;
 constexpr int SCAN_ITEMS = 16;
 constexpr int SCAN_TILE = SCAN_THREADS * SCAN_ITEMS;  // 4096
 
-// Per 4096-Gaussian block: how many have tiles (tiles_touched > 0).
-__global__ void __launch_bounds__(SCAN_THREADS) vis_count_kernel(int P, const int* __restrict__ tiles_touched,
-                                                                 long long* __restrict__ block_sums) {
-  __shared__ int s[SCAN_THREADS / 32];
-  const long long base = (long long)blockIdx.x * SCAN_TILE;
-  int acc = 0;
+constexpr int SCAN_WARPS = SCAN_THREADS / 32;
+
+// Decoupled look-back over one 62-bit value per tile, run by one warp: the
+// warp reads 32 predecessors' status words at once, sums back to the nearest
+// inclusive one and publishes this tile's inclusive value.  Tiles are claimed
+// in launch order (atomic counter), so every tile waited on belongs to a
+// running CTA; each spin is nevertheless bounded (SPIN_LIMIT): a timeout sets
+// ERR_LOOKBACK_TIMEOUT and counts the slot as an inclusive zero, so the walk
+// ends.  Returns the exclusive prefix (in every lane).
+__device__ long long warp_lookback(unsigned long long* status, int tile, long long agg, long long* err) {
+  using radix::FLAG_AGG;
+  using radix::FLAG_INC;
+  using radix::VALUE_MASK;
+  const int lane = threadIdx.x & 31;
+  if (lane == 0)
+    radix::st_volatile(status + tile, (tile == 0 ? FLAG_INC : FLAG_AGG) | (unsigned long long)agg);
+  long long excl = 0;
+  if (tile > 0) {
+    int t = tile - 1;
+    while (true) {
+      const int my = t - lane;
+      unsigned long long v = FLAG_INC;  // before tile 0: an inclusive zero
+      if (my >= 0) {
+        v = radix::ld_volatile(status + my);
+        int spins = 0;
+        while ((v & ~VALUE_MASK) == 0 && ++spins < SPIN_LIMIT) v = radix::ld_volatile(status + my);
+        if ((v & ~VALUE_MASK) == 0) {
+          atomicOr((unsigned long long*)err, (unsigned long long)ERR_LOOKBACK_TIMEOUT);
+          v = FLAG_INC;
+        }
+      }
+      const unsigned inc = __ballot_sync(0xffffffffu, (v & ~VALUE_MASK) == FLAG_INC);
+      const int stop = inc ? __ffs(inc) - 1 : 31;  // nearest inclusive predecessor
+      long long val = lane <= stop ? (long long)(v & VALUE_MASK) : 0;
 #pragma unroll
-  for (int i = 0; i < SCAN_ITEMS; ++i) {
-    const long long r = base + i * SCAN_THREADS + threadIdx.x;
-    if (r < P) acc += tiles_touched[r] > 0;
+      for (int o = 16; o > 0; o >>= 1) val += __shfl_xor_sync(0xffffffffu, val, o);
+      excl += val;
+      if (inc) break;
+      t -= 32;
+    }
+    if (lane == 0) radix::st_volatile(status + tile, FLAG_INC | (unsigned long long)(excl + agg));
   }
-  acc = __reduce_add_sync(0xffffffffu, acc);
-  if ((threadIdx.x & 31) == 0) s[threadIdx.x >> 5] = acc;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    long long t = 0;
-    for (int w = 0; w < SCAN_THREADS / 32; ++w) t += s[w];
-    block_sums[blockIdx.x] = t;
-  }
+  return excl;
 }
 
-// Order-preserving compaction of the Gaussians with tiles: keys = depth
-// float bits, vals = point index, in index order (so the stable depth sort
-// breaks depth ties by index).  block_prefix = exclusive block offsets.
-__global__ void __launch_bounds__(SCAN_THREADS) vis_compact_kernel(
+// Order-preserving compaction of the Gaussians with tiles in one pass:
+// keys = depth float bits, vals = point index, in index order (so the stable
+// depth sort breaks depth ties by index).  A CTA takes 4096 consecutive
+// Gaussians as 16 chunks of 256; positions inside the CTA come from per-warp
+// ballots, the CTA's offset from the look-back.  The last tile writes the
+// count V.
+__global__ void __launch_bounds__(SCAN_THREADS) compact_kernel(
     int P, const float* __restrict__ depths, const int* __restrict__ tiles_touched,
-    const long long* __restrict__ block_prefix, unsigned* __restrict__ keys, unsigned* __restrict__ vals,
-    int* __restrict__ ids_out) {
-  __shared__ int s_warp[SCAN_THREADS / 32];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const long long base = (long long)blockIdx.x * SCAN_TILE;
-  // Chunk i covers SCAN_THREADS consecutive indices; warps take them in order.
-  long long out = block_prefix[blockIdx.x];
-#pragma unroll 1
-  for (int i = 0; i < SCAN_ITEMS; ++i) {
-    const long long r = base + i * SCAN_THREADS + threadIdx.x;
-    const bool keep = r < P && tiles_touched[r] > 0;
-    const unsigned m = __ballot_sync(0xffffffffu, keep);
-    if (lane == 0) s_warp[warp] = __popc(m);
-    __syncthreads();
-    int before = 0, total = 0;
+    unsigned long long* __restrict__ status, unsigned* __restrict__ counter, unsigned* __restrict__ keys,
+    unsigned* __restrict__ vals, int* __restrict__ ids_out, long long* __restrict__ count_out,
+    int* __restrict__ count_int, long long* __restrict__ err) {
+  __shared__ int s_tile;
+  __shared__ int s_pre[SCAN_ITEMS * SCAN_WARPS];
+  __shared__ int s_wsum[SCAN_WARPS];
+  __shared__ long long s_excl;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) s_tile = (int)atomicAdd(counter, 1u);
+  __syncthreads();
+  const int tile = s_tile;
+  const long long base = (long long)tile * SCAN_TILE;
+  unsigned m[SCAN_ITEMS];
 #pragma unroll
-    for (int w = 0; w < SCAN_THREADS / 32; ++w) {
-      const int c = s_warp[w];
-      before += w < warp ? c : 0;
-      total += c;
-    }
-    if (keep) {
-      const long long o = out + before + __popc(m & lanemask_lt());
+  for (int i = 0; i < SCAN_ITEMS; ++i) {
+    const long long r = base + i * SCAN_THREADS + tid;
+    m[i] = __ballot_sync(0xffffffffu, r < P && tiles_touched[r] > 0);
+    if (lane == 0) s_pre[i * SCAN_WARPS + warp] = __popc(m[i]);
+  }
+  __syncthreads();
+  // exclusive prefix over the (chunk, warp) counts in index order
+  const int v = tid < SCAN_ITEMS * SCAN_WARPS ? s_pre[tid] : 0;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) s_wsum[warp] = x;
+  __syncthreads();
+  int wpre = 0, total = 0;
+#pragma unroll
+  for (int w = 0; w < SCAN_WARPS; ++w) {
+    wpre += w < warp ? s_wsum[w] : 0;
+    total += s_wsum[w];
+  }
+  if (tid < SCAN_ITEMS * SCAN_WARPS) s_pre[tid] = wpre + x - v;
+  if (warp == 0) {
+    const long long e = warp_lookback(status, tile, total, err);
+    if (lane == 0) s_excl = e;
+  }
+  __syncthreads();
+  const long long excl = s_excl;
+  const unsigned lt = lanemask_lt();
+#pragma unroll
+  for (int i = 0; i < SCAN_ITEMS; ++i) {
+    if ((m[i] >> lane) & 1u) {
+      const long long r = base + i * SCAN_THREADS + tid;
+      const long long o = excl + s_pre[i * SCAN_WARPS + warp] + __popc(m[i] & lt);
       keys[o] = __float_as_uint(depths[r]);
       vals[o] = (unsigned)r;
       if (ids_out) ids_out[o] = (int)r;
     }
-    out += total;
-    __syncthreads();
+  }
+  if (tile == (int)gridDim.x - 1 && tid == 0) {
+    count_out[0] = excl + total;
+    *count_int = (int)(excl + total);
   }
 }
 
-// Block sums (int64) of tiles_touched gathered in depth order.
-__global__ void __launch_bounds__(SCAN_THREADS) scan_reduce_kernel(
+// Inclusive scan of tiles_touched in depth order in one pass:
+// offsets[r] = sum_{q<=r} tiles[order[q]] over the first n = *n_dev entries.
+// Ids are read coalesced, the counts gathered, and each thread scans 16
+// consecutive counts through shared memory (padded: conflict-free); the
+// CTA's offset comes from the look-back; the tile holding the last entry
+// writes the int64 total.
+__global__ void __launch_bounds__(SCAN_THREADS) depth_scan_kernel(
     const int* __restrict__ n_dev, const int* __restrict__ order, const int* __restrict__ tiles_touched,
-    long long* __restrict__ block_sums) {
-  __shared__ long long s[SCAN_THREADS / 32];
-  const int P = *n_dev;
-  const long long base = (long long)blockIdx.x * SCAN_TILE;
-  long long acc = 0;
+    unsigned long long* __restrict__ status, unsigned* __restrict__ counter, int* __restrict__ offsets,
+    long long* __restrict__ total_out, long long* __restrict__ err) {
+  constexpr int PAD = SCAN_TILE + SCAN_TILE / 16;
+  __shared__ int s_c[PAD];
+  __shared__ long long s_wsum[SCAN_WARPS];
+  __shared__ long long s_excl;
+  __shared__ int s_tile;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int n = *n_dev;
+  if (tid == 0) s_tile = (int)atomicAdd(counter, 1u);
+  __syncthreads();
+  const int tile = s_tile;
+  const long long base = (long long)tile * SCAN_TILE;
+  if (base >= n) return;  // every later tile lies past n as well: nobody waits on this one
+  int c[SCAN_ITEMS];
 #pragma unroll
   for (int i = 0; i < SCAN_ITEMS; ++i) {
-    const long long r = base + i * SCAN_THREADS + threadIdx.x;
-    if (r < P) acc += tiles_touched[order[r]];
+    const long long r = base + i * SCAN_THREADS + tid;
+    c[i] = r < n ? order[r] : -1;
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-  if ((threadIdx.x & 31) == 0) s[threadIdx.x >> 5] = acc;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    long long t = 0;
-    for (int w = 0; w < SCAN_THREADS / 32; ++w) t += s[w];
-    block_sums[blockIdx.x] = t;
-  }
-}
-
-// Exclusive scan of the block sums in one CTA; writes the total (and, if
-// total_int is given, the total as an int for device-side counts).
-__global__ void __launch_bounds__(1024) scan_blocks_kernel(int nblocks,
-                                                           long long* __restrict__ block_sums,
-                                                           long long* __restrict__ status_out,
-                                                           int* __restrict__ total_int) {
-  __shared__ long long s_carry;
-  __shared__ long long s_warp[32];
-  if (threadIdx.x == 0) s_carry = 0;
-  __syncthreads();
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int base = 0; base < nblocks; base += 1024) {
-    const int i = base + threadIdx.x;
-    const long long v = i < nblocks ? block_sums[i] : 0;
-    long long x = v;
+  for (int i = 0; i < SCAN_ITEMS; ++i) c[i] = c[i] >= 0 ? tiles_touched[c[i]] : 0;
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const long long y = __shfl_up_sync(0xffffffffu, x, o);
-      if (lane >= o) x += y;
-    }
-    if (lane == 31) s_warp[warp] = x;
-    __syncthreads();
-    long long wpre = 0, tot = 0;
-    for (int w = 0; w < 32; ++w) {
-      const long long t = s_warp[w];
-      if (w < warp) wpre += t;
-      tot += t;
-    }
-    if (i < nblocks) block_sums[i] = s_carry + wpre + x - v;
-    __syncthreads();
-    if (threadIdx.x == 0) s_carry += tot;
-    __syncthreads();
+  for (int i = 0; i < SCAN_ITEMS; ++i) {
+    const int l = i * SCAN_THREADS + tid;
+    s_c[l + l / 16] = c[i];
   }
-  if (threadIdx.x == 0) {
-    status_out[0] = s_carry;
-    if (total_int) *total_int = (int)s_carry;
-  }
-}
-
-// Inclusive scan in depth order: offsets[r] = sum_{q<=r} tiles[order[q]].
-__global__ void __launch_bounds__(SCAN_THREADS) scan_downsweep_kernel(
-    const int* __restrict__ n_dev, const int* __restrict__ order, const int* __restrict__ tiles_touched,
-    const long long* __restrict__ block_prefix, int* __restrict__ offsets) {
-  __shared__ long long s_warp[SCAN_THREADS / 32];
-  const int P = *n_dev;
-  if ((long long)blockIdx.x * SCAN_TILE >= P) return;
-  const long long base = (long long)blockIdx.x * SCAN_TILE;
-  // Thread t owns the SCAN_ITEMS consecutive ranks [base + t*ITEMS, ...).
-  long long v[SCAN_ITEMS];
+  __syncthreads();
   long long run = 0;
+  long long mine[SCAN_ITEMS];
 #pragma unroll
   for (int i = 0; i < SCAN_ITEMS; ++i) {
-    const long long r = base + (long long)threadIdx.x * SCAN_ITEMS + i;
-    const long long c = r < P ? tiles_touched[order[r]] : 0;
-    run += c;
-    v[i] = run;
+    run += s_c[tid * 17 + i];  // local index tid*16 + i, padded
+    mine[i] = run;
   }
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   long long x = run;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const long long y = __shfl_up_sync(0xffffffffu, x, o);
     if (lane >= o) x += y;
   }
-  if (lane == 31) s_warp[warp] = x;
+  if (lane == 31) s_wsum[warp] = x;
   __syncthreads();
-  long long wpre = 0;
-  for (int w = 0; w < warp; ++w) wpre += s_warp[w];
-  const long long excl = block_prefix[blockIdx.x] + wpre + x - run;
+  long long wpre = 0, total = 0;
+#pragma unroll
+  for (int w = 0; w < SCAN_WARPS; ++w) {
+    wpre += w < warp ? s_wsum[w] : 0;
+    total += s_wsum[w];
+  }
+  if (warp == 0) {
+    const long long e = warp_lookback(status, tile, total, err);
+    if (lane == 0) s_excl = e;
+  }
+  __syncthreads();
+  const long long pre = s_excl + wpre + x - run;
+#pragma unroll
+  for (int i = 0; i < SCAN_ITEMS; ++i) s_c[tid * 17 + i] = (int)(pre + mine[i]);
+  __syncthreads();
 #pragma unroll
   for (int i = 0; i < SCAN_ITEMS; ++i) {
-    const long long r = base + (long long)threadIdx.x * SCAN_ITEMS + i;
-    if (r < P) offsets[r] = (int)(excl + v[i]);
+    const int l = i * SCAN_THREADS + tid;
+    const long long r = base + l;
+    if (r < n) offsets[r] = s_c[l + l / 16];
   }
+  if (base + SCAN_TILE >= n && tid == 0) *total_out = s_excl + total;
 }
 
 struct EmitPairs {
@@ -290,8 +320,8 @@ GSB_EXPORT size_t gsb_bin_count_workspace_bytes(int P) {
   const size_t n = (size_t)(P > 0 ? P : 1);
   size_t b = 0;
   b += align256(n * 4) * 3;  // keys, keys_alt, vals_alt
-  b += align256((size_t)div_up((long long)n, SCAN_TILE) * 8);
-  b += 256;                  // device count of Gaussians with tiles
+  b += align256((size_t)div_up((long long)n, SCAN_TILE) * 8) * 2;  // look-back status of the two scans
+  b += 256;                  // device count of Gaussians with tiles, tile counters
   b += radix::scratch_bytes((long long)n, 4);
   return b + 256;
 }
@@ -324,21 +354,25 @@ GSB_EXPORT int gsb_bin_count(const gsb_bin_count_args* a, void* stream) {
   unsigned* vals_alt = (unsigned*)w;
   w += align256((size_t)P * 4);
   const int nblocks = div_up(P, SCAN_TILE);
-  long long* block_sums = (long long*)w;
-  w += align256((size_t)nblocks * 8);
+  const size_t status_bytes = align256((size_t)nblocks * 8);
+  unsigned long long* status_c = (unsigned long long*)w;
+  unsigned long long* status_s = (unsigned long long*)(w + status_bytes);
+  w += 2 * status_bytes;
   int* n_vis = (int*)w;
+  unsigned* counters = (unsigned*)(w + 16);  // [0] compaction, [1] scan
   w += 256;
   void* sort_scratch = w;
 
   long long* err = a->status_out + 1;
-  cudaMemsetAsync(err, 0, sizeof(long long), s);
+  // look-back status words and tile counters start at zero; so do the pair
+  // total and the error word (V is always written)
+  cudaMemsetAsync(status_c, 0, 2 * status_bytes + 256, s);
+  cudaMemsetAsync(a->status_out, 0, 2 * sizeof(long long), s);
   // 1. order-preserving compaction of the Gaussians with tiles (count V into
   //    status_out[2] and n_vis); only they take part in the depth sort.
   unsigned* vals0 = (unsigned*)a->depth_order;
-  vis_count_kernel<<<nblocks, SCAN_THREADS, 0, s>>>(P, a->tiles_touched, block_sums);
-  scan_blocks_kernel<<<1, 1024, 0, s>>>(nblocks, block_sums, a->status_out + 2, n_vis);
-  vis_compact_kernel<<<nblocks, SCAN_THREADS, 0, s>>>(P, a->depths, a->tiles_touched, block_sums, keys, vals0,
-                                                      a->binned_ids);
+  compact_kernel<<<nblocks, SCAN_THREADS, 0, s>>>(P, a->depths, a->tiles_touched, status_c, counters, keys, vals0,
+                                                  a->binned_ids, a->status_out + 2, n_vis, err);
   // 2. stable sort of the V (depth bits, index) pairs.
   unsigned* kb[2] = {keys, keys_alt};
   unsigned* vb[2] = {vals0, vals_alt};
@@ -347,10 +381,8 @@ GSB_EXPORT int gsb_bin_count(const gsb_bin_count_args* a, void* stream) {
     cudaMemcpyAsync(a->depth_order, vals_alt, (size_t)P * 4, cudaMemcpyDeviceToDevice, s);
   }
   // 3. inclusive scan of tiles_touched in depth order; pair total -> status_out[0].
-  scan_reduce_kernel<<<nblocks, SCAN_THREADS, 0, s>>>(n_vis, a->depth_order, a->tiles_touched, block_sums);
-  scan_blocks_kernel<<<1, 1024, 0, s>>>(nblocks, block_sums, a->status_out, nullptr);
-  scan_downsweep_kernel<<<nblocks, SCAN_THREADS, 0, s>>>(n_vis, a->depth_order, a->tiles_touched,
-                                                         block_sums, a->point_offsets);
+  depth_scan_kernel<<<nblocks, SCAN_THREADS, 0, s>>>(n_vis, a->depth_order, a->tiles_touched, status_s, counters + 1,
+                                                     a->point_offsets, a->status_out, err);
   return check_launch("gsb_bin_count");
 }
 
