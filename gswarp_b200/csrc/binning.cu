@@ -286,24 +286,18 @@ __global__ void __launch_bounds__(256) emit_kernel(
   if (e.k != n) atomicOr((unsigned long long*)err, (unsigned long long)ERR_EMIT_MISMATCH);
 }
 
-__global__ void ranges_kernel(long long R, const unsigned* __restrict__ keys,
-                              int* __restrict__ ranges) {
-  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= R) return;
-  const unsigned cur = keys[i];
-  if (i == 0) {
-    ranges[cur * 2] = 0;
-  } else {
-    const unsigned prev = keys[i - 1];
-    if (cur != prev) {
-      ranges[prev * 2 + 1] = (int)i;
-      ranges[cur * 2] = (int)i;
-    }
-  }
-  if (i == R - 1) ranges[cur * 2 + 1] = (int)R;
-}
 
 inline size_t align256(size_t b) { return (b + 255) & ~(size_t)255; }
+
+// Ranges when the sort has no pass to write them: a single tile (every key
+// is 0) or a single pair.
+__global__ void single_range_kernel(const unsigned* __restrict__ keys, int R, int* __restrict__ ranges) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) {
+    const unsigned k = keys[0];
+    ranges[2 * (size_t)k] = 0;
+    ranges[2 * (size_t)k + 1] = R;
+  }
+}
 
 inline int tile_sort_passes(int tiles) {
   if (tiles <= 1) return 0;
@@ -452,7 +446,12 @@ GSB_EXPORT int gsb_bin_emit_sort(const gsb_bin_sort_args* a, void* stream) {
     emit_kernel<<<div_up(a->P, 256), 256, 0, s>>>(
         a->bin_status + 2, gx, gy, a->coverage_mode, a->depth_order, a->point_offsets, a->tiles_touched, a->radii,
         reinterpret_cast<const float4*>(a->records), a->conic_2d_inv, kb[0], vb[0], a->error_word);
-  const int where = radix::sort_pairs(kb, vb, R, nullptr, passes, sort_scratch, a->error_word, s);
-  ranges_kernel<<<div_up(R, 256), 256, 0, s>>>(R, kb[where], a->ranges);
+  // the last pass also writes the per-tile ranges (the array was zeroed above)
+  if (passes == 0 || R <= 1) {
+    // nothing to sort: the emitted order is the sorted order
+    if (vb[0] != pl) cudaMemcpyAsync(pl, vb[0], (size_t)R * 4, cudaMemcpyDeviceToDevice, s);
+    single_range_kernel<<<1, 32, 0, s>>>(kb[0], (int)R, a->ranges);
+  } else
+    radix::sort_pairs(kb, vb, R, nullptr, passes, sort_scratch, a->error_word, s, a->ranges, tiles);
   return check_launch("gsb_bin_emit_sort");
 }

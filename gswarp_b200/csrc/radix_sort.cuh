@@ -139,7 +139,7 @@ __global__ void __launch_bounds__(THREADS, 4) onesweep_kernel(
     unsigned* __restrict__ keys_out, unsigned* __restrict__ vals_out, int n_host,
     const int* __restrict__ n_dev, int shift,
     const unsigned* __restrict__ bin_base, unsigned long long* __restrict__ lookback,
-    unsigned* __restrict__ tile_counter, long long* __restrict__ err) {
+    unsigned* __restrict__ tile_counter, long long* __restrict__ err, int* __restrict__ ranges) {
   __shared__ unsigned s_keys[TILE_KEYS];
   __shared__ unsigned s_vals[HAS_VALS ? TILE_KEYS : 1];
   __shared__ unsigned s_warp_hist[WARPS][RADIX];
@@ -271,8 +271,23 @@ __global__ void __launch_bounds__(THREADS, 4) onesweep_kernel(
     if (dst < (unsigned)n) {
       keys_out[dst] = k;
       if (HAS_VALS) vals_out[dst] = s_vals[j];
+      if (ranges) {
+        // Last pass: the staged tile is sorted by the whole key, so a key
+        // whose neighbour in the tile differs is the tile's first / last
+        // occurrence of it.  The key's global [start, end) is the min / max
+        // over the tiles that hold it: end by atomicMax, start as n - start
+        // by atomicMax (both fields start at zero, so keys that never occur
+        // stay (0, 0)); ranges_fixup_kernel turns n - start back into start.
+        if (j == 0 || s_keys[j - 1] != k) atomicMax(ranges + 2 * (size_t)k, n - (int)dst);
+        if (j == tile_n - 1 || s_keys[j + 1] != k) atomicMax(ranges + 2 * (size_t)k + 1, (int)dst + 1);
+      }
     }
   }
+}
+
+__global__ void ranges_fixup_kernel(int keys, int n, int* __restrict__ ranges) {
+  const int k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k < keys && ranges[2 * k + 1] > 0) ranges[2 * k] = n - ranges[2 * k];
 }
 
 // Workspace layout for sorting n pairs with `passes` 8-bit passes.
@@ -320,8 +335,12 @@ __host__ inline SortScratch carve_scratch(void* base, long long n, int passes) {
 // Returns the index (0/1) of the buffer pair that holds the result.
 // vals may be null (keys only).  With n_dev non-null the count is read on
 // the device (at most n, which sizes the grids and the scratch).
+// With `ranges` (and n_dev null) the last pass also writes, for every key
+// value below range_keys, its [start, end) in the sorted output into the
+// zero-initialised int2 array `ranges` ((0, 0) for absent keys).
 __host__ inline int sort_pairs(unsigned* k[2], unsigned* v[2], long long n, const int* n_dev, int passes,
-                               void* scratch, long long* err, cudaStream_t stream) {
+                               void* scratch, long long* err, cudaStream_t stream, int* ranges = nullptr,
+                               int range_keys = 0) {
   if ((n <= 1 && !n_dev) || n <= 0 || passes == 0) return 0;
   SortScratch s = carve_scratch(scratch, n, passes);
   cudaMemsetAsync(s.hist, 0, s.zero_bytes, stream);
@@ -332,17 +351,20 @@ __host__ inline int sort_pairs(unsigned* k[2], unsigned* v[2], long long n, cons
   int cur = 0;
   for (int p = 0; p < passes; ++p) {
     unsigned long long* lb = s.lookback + (size_t)p * tiles * RADIX;
+    int* rg = (p == passes - 1 && !n_dev) ? ranges : nullptr;
     if (v[0]) {
       onesweep_kernel<true><<<tiles, THREADS, 0, stream>>>(
           k[cur], v[cur], k[cur ^ 1], v[cur ^ 1], (int)n, n_dev, p * RADIX_BITS, s.bin_base + p * RADIX,
-          lb, s.counters + p, err);
+          lb, s.counters + p, err, rg);
     } else {
       onesweep_kernel<false><<<tiles, THREADS, 0, stream>>>(
           k[cur], nullptr, k[cur ^ 1], nullptr, (int)n, n_dev, p * RADIX_BITS, s.bin_base + p * RADIX,
-          lb, s.counters + p, err);
+          lb, s.counters + p, err, rg);
     }
     cur ^= 1;
   }
+  if (ranges && !n_dev && range_keys > 0)
+    ranges_fixup_kernel<<<(range_keys + 255) / 256, 256, 0, stream>>>(range_keys, (int)n, ranges);
   return cur;
 }
 

@@ -48,6 +48,15 @@ def _scene(name, dev):
         scene = wl.config2_scene(seed=4, n=20_000)
         scene.scales = scene.scales * 12.0
         view = wl.config2_view(seed=4, width=333, height=197)
+    elif name == "single_tile":
+        # a 16x16 image: one tile, so the tile sort has no pass
+        scene, _ = wl.config1_scene(seed=1, n=300)
+        view = wl.look_at_view([0.0, 0.0, -3.0], [0.0, 0.0, 0.0], [0.0, -1.0, 0.0], 60.0, 16, 16)
+    elif name == "single_pair":
+        # one small Gaussian inside one tile of a 4x3-tile image: a single (tile, point) pair
+        scene = wl.Scene(torch.tensor([[0.4, 0.0, 0.0]]), torch.full((1, 3), 0.002),
+                         torch.tensor([[1.0, 0.0, 0.0, 0.0]]), torch.tensor([[0.9]]), torch.full((1, 1, 3), 0.3), 0)
+        view = wl.look_at_view([0.0, 0.0, -3.0], [0.0, 0.0, 0.0], [0.0, -1.0, 0.0], 60.0, 64, 48)
     else:
         raise KeyError(name)
     return scene, view
@@ -83,11 +92,12 @@ def _bits(a):
     return np.ascontiguousarray(a).view(np.uint32)
 
 
-@pytest.mark.parametrize("name", ["cfg1", "cfg2_200k", "cfg2_small_view", "cfg2_big_footprints"])
+@pytest.mark.parametrize("name", ["cfg1", "cfg2_200k", "cfg2_small_view", "cfg2_big_footprints", "single_tile",
+                                  "single_pair"])
 @pytest.mark.parametrize("mode", [1, 0, 2])
 def test_preprocess_and_binning_bit_exact(cuda, name, mode):
-    if name == "cfg2_200k" and mode != 1:
-        pytest.skip("large case checked in the default AccuTile mode only")
+    if name in ("cfg2_200k", "single_tile", "single_pair") and mode != 1:
+        pytest.skip("checked in the default AccuTile mode only")
     scene, view = _scene(name, cuda)
     ref = _oracle_pre(scene, view, mode)
     g, cam, pre = _gpu_pre(scene, view, cuda, mode)
@@ -114,6 +124,8 @@ def test_preprocess_and_binning_bit_exact(cuda, name, mode):
         binned = pl.binning(pre, cam, mode)
         torch.cuda.synchronize()
         assert binned.num_rendered == len(ref_pl)
+        if name == "single_pair":
+            assert len(ref_pl) == 1
         np.testing.assert_array_equal(_np(binned.point_list), ref_pl)
         np.testing.assert_array_equal(_np(binned.ranges), ref_ranges)
 
