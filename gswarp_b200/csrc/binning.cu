@@ -232,37 +232,127 @@ struct EmitPairs {
   }
 };
 
-// Emit from the 32-byte binning records written by preprocess: one random
-// 32-byte read per Gaussian, then the recorded tiles are written out (the
-// AccuTile arithmetic is not repeated, except for the rare records with more
-// than BINREC_MAX_BANDS bands, which re-run the sweep from the render
-// record).  The pair count is the difference of adjacent inclusive offsets
-// (both coalesced).
-__global__ void __launch_bounds__(256) emit_binrec_kernel(
+// Emit from the 32-byte binning records written by preprocess, one warp per
+// 32 consecutive depth-ordered Gaussians.  Each lane reads its Gaussian's
+// record (one random 32-byte read) and pair count (the difference of
+// adjacent inclusive offsets), the warp scans the counts, and then the lanes
+// take consecutive pairs of the warp -- the owning Gaussian found by binary
+// search over the warp's prefix, the tile decoded from its record -- so every
+// store is coalesced and no lane waits for the warp's largest footprint.
+// Records with more than BINREC_MAX_BANDS bands re-run the sweep from the
+// render record per lane afterwards.  A record whose tile count differs from
+// the pair count raises ERR_EMIT_MISMATCH (and emits no more than the count).
+struct EmitLane {
+  unsigned w[8];
+  int pre, start, point;
+};
+
+__device__ __forceinline__ int record_count(const unsigned (&w)[8]) {
+  const int x0 = (int)(w[0] & 0xFFFFu), y0 = (int)(w[0] >> 16);
+  const int x1 = (int)(w[1] & 0xFFFFu), y1 = (int)(w[1] >> 16);
+  const unsigned kind = w[2] & 3u;
+  if (kind == BINREC_RECT) return (x1 - x0) * (y1 - y0);
+  if (kind == BINREC_MASK) return __popc(w[3]) + __popc(w[4]);
+  int c = 0;
+  const int nb = (int)((w[2] >> 8) & 0xFFu);
+  for (int b = 0; b < nb && b < BINREC_MAX_BANDS; ++b) c += imx(0, (int)(w[3 + b] >> 16) - (int)(w[3 + b] & 0xFFFFu));
+  return c;
+}
+
+// Tile of the idx-th pair of a (non-sweep) record, in cover_tiles_in_rect's order.
+__device__ __forceinline__ int record_tile(const unsigned* w, int idx, int gx) {
+  const int x0 = (int)(w[0] & 0xFFFFu), y0 = (int)(w[0] >> 16);
+  const int x1 = (int)(w[1] & 0xFFFFu);
+  const unsigned kind = w[2] & 3u;
+  const int width = x1 - x0;
+  if (kind == BINREC_RECT) {
+    const int row = idx / width;
+    return (y0 + row) * gx + x0 + (idx - row * width);
+  }
+  if (kind == BINREC_MASK) {
+    const int lo = __popc(w[3]);
+    const int bit = idx < lo ? __fns(w[3], 0, idx + 1) : 32 + __fns(w[4], 0, idx - lo + 1);
+    const int row = bit / width;
+    return (y0 + row) * gx + x0 + (bit - row * width);
+  }
+  const bool vertical = (w[2] >> 2) & 1u;
+  const int nb = (int)((w[2] >> 8) & 0xFFu);
+  for (int b = 0; b < nb; ++b) {
+    const int lo = (int)(w[3 + b] & 0xFFFFu), hi = (int)(w[3 + b] >> 16);
+    const int len = imx(0, hi - lo);
+    if (idx < len) return vertical ? (lo + idx) * gx + x0 + b : (y0 + b) * gx + lo + idx;
+    idx -= len;
+  }
+  return 0;  // unreachable: idx < record_count
+}
+
+constexpr int EMIT_THREADS = 256;
+
+__global__ void __launch_bounds__(EMIT_THREADS) emit_binrec_kernel(
     const long long* __restrict__ n_dev, int gx, int mode, const int* __restrict__ order,
     const int* __restrict__ offsets, const uint4* __restrict__ bin_records, const float4* __restrict__ records,
     unsigned* __restrict__ keys, unsigned* __restrict__ vals, long long* __restrict__ err) {
-  const int r = blockIdx.x * blockDim.x + threadIdx.x;
-  if (r >= *n_dev) return;
-  const int end = offsets[r];
-  const int n = end - (r > 0 ? offsets[r - 1] : 0);
-  if (n <= 0) return;
-  const int p = order[r];
-  const uint4 a = __ldg(bin_records + (size_t)p * 2), b = __ldg(bin_records + (size_t)p * 2 + 1);
-  const unsigned w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-  float px = 0.0f, py = 0.0f, ca = 0.0f, cb = 0.0f, cc = 0.0f, t = 0.0f;
-  if ((w[2] & 3u) == BINREC_SWEEP) {
-    const float4 q0 = __ldg(records + (size_t)p * 3), q1 = __ldg(records + (size_t)p * 3 + 1);
-    px = q0.x;
-    py = q0.y;
-    ca = q0.z;
-    cb = q0.w;
-    cc = q1.x;
-    t = opacity_threshold(q1.y);
+  __shared__ EmitLane s_lane[EMIT_THREADS];
+  const int lane = threadIdx.x & 31;
+  const long long nv = *n_dev;
+  const long long warp_first = ((long long)blockIdx.x * EMIT_THREADS + (threadIdx.x & ~31));
+  if (warp_first >= nv) return;  // whole warp past the binned Gaussians
+  const int r = (int)(warp_first + lane);
+  EmitLane& me = s_lane[threadIdx.x];
+  int n = 0, point = 0, start = 0;
+  unsigned w[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+  if (r < nv) {
+    const int end = offsets[r];
+    n = end - (r > 0 ? offsets[r - 1] : 0);
+    start = end - n;
+    if (n > 0) {
+      point = order[r];
+      const uint4 a = __ldg(bin_records + (size_t)point * 2), b = __ldg(bin_records + (size_t)point * 2 + 1);
+      w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
+      w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
+    }
   }
-  EmitPairs e{keys, vals, (long long)end - n, n, p, 0};
-  emit_record(w, gx, mode, px, py, ca, cb, cc, t, e);
-  if (e.k != n) atomicOr((unsigned long long*)err, (unsigned long long)ERR_EMIT_MISMATCH);
+  const bool sweep = n > 0 && (w[2] & 3u) == BINREC_SWEEP;
+  int ncoop = 0;
+  if (n > 0 && !sweep) {
+    const int c = record_count(w);
+    if (c != n) atomicOr((unsigned long long*)err, (unsigned long long)ERR_EMIT_MISMATCH);
+    ncoop = min(c, n);
+  }
+  // warp exclusive scan of the cooperative counts
+  int x = ncoop;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  const int total = __shfl_sync(0xffffffffu, x, 31);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) me.w[k] = w[k];
+  me.pre = x - ncoop;
+  me.start = start;
+  me.point = point;
+  __syncwarp();
+  const EmitLane* wl = s_lane + (threadIdx.x & ~31);
+  for (int q = lane; q < total; q += 32) {
+    // owner: the last lane whose prefix is <= q (a lane after the owner starts past q; lanes
+    // without pairs before it have lower indices)
+    int o = 0;
+#pragma unroll
+    for (int step = 16; step > 0; step >>= 1)
+      if (wl[o + step].pre <= q) o += step;
+    const int idx = q - wl[o].pre;
+    const int pos = wl[o].start + idx;
+    keys[pos] = (unsigned)record_tile(wl[o].w, idx, gx);
+    vals[pos] = (unsigned)wl[o].point;
+  }
+  if (sweep) {
+    const float4 q0 = __ldg(records + (size_t)point * 3), q1 = __ldg(records + (size_t)point * 3 + 1);
+    const float t = opacity_threshold(q1.y);
+    EmitPairs e{keys, vals, (long long)start, n, point, 0};
+    emit_record(w, gx, mode, q0.x, q0.y, q0.z, q0.w, q1.x, t, e);
+    if (e.k != n) atomicOr((unsigned long long*)err, (unsigned long long)ERR_EMIT_MISMATCH);
+  }
 }
 
 __global__ void __launch_bounds__(256) emit_kernel(
@@ -438,7 +528,7 @@ GSB_EXPORT int gsb_bin_emit_sort(const gsb_bin_sort_args* a, void* stream) {
     vb[1] = pl;
   }
   if (binrec)
-    emit_binrec_kernel<<<div_up(a->P, 256), 256, 0, s>>>(
+    emit_binrec_kernel<<<div_up(a->P, EMIT_THREADS), EMIT_THREADS, 0, s>>>(
         a->bin_status + 2, gx, a->coverage_mode, a->depth_order, a->point_offsets,
         reinterpret_cast<const uint4*>(a->bin_records), reinterpret_cast<const float4*>(a->records), kb[0],
         vb[0], a->error_word);
