@@ -283,7 +283,8 @@ def binning(pre: Preprocessed, cam: Camera, coverage_mode: int, want_ids: bool =
     a.status_out = _lib.ptr(status)
     a.workspace = _lib.ptr(ws)
     a.workspace_bytes = ws_bytes
-    with _stage_timer("bin_count", {"P": P, "kernels": 12}):
+    # compaction, depth-key histogram + bin bases, 4 depth passes, depth-ordered scan
+    with _stage_timer("bin_count", {"P": P, "kernels": 8}):
         _lib.call("gsb_bin_count", a, stream)
     sticky = sticky_error_word(dev)
     total, err, num_binned, sticky_bits = torch.cat([status, sticky]).tolist()
@@ -315,7 +316,11 @@ def binning(pre: Preprocessed, cam: Camera, coverage_mode: int, want_ids: bool =
     b.workspace_bytes = ws2.numel()
     b.bin_records = _lib.ptr(pre.bin_records)
     b.bin_status = _lib.ptr(status)
-    with _stage_timer("bin_emit_sort", {"P": P, "num_rendered": R, "kernels": 7}):
+    # emit, then either the tile sort (histogram + bin bases, one pass per 8 bits of the tile
+    # id, ranges fix-up) or, with one tile or one pair, the single-range kernel
+    passes = ((gx * gy - 1).bit_length() + 7) // 8 if gx * gy > 1 else 0
+    kernels = 0 if R == 0 else (2 if passes == 0 or R <= 1 else 4 + passes)
+    with _stage_timer("bin_emit_sort", {"P": P, "num_rendered": R, "kernels": kernels}):
         _lib.call("gsb_bin_emit_sort", b, stream)
     return Binned(R, point_list[:R], ranges, ids[:int(num_binned)] if ids is not None else None)
 
