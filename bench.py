@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark: 3DGS forward+backward views/sec at 1080p through gswarp_b200.
 
-Workload (weak scaling): 6,000,000 Gaussians with the
+Workload (benchmark configuration 5, weak scaling): 6,000,000 Gaussians with the
 config-2 distributions (SH degree 3), cameras on a radius-12 ring at random
 elevations, 1920x1080.  Each GPU renders 8 views per step; each view does
 forward, loss = L1 + 0.2 * (1 - SSIM) against a seeded target, backward; the
@@ -258,7 +258,7 @@ def kernel_profile(trainer, steps=2):
 
 
 def measure_cfg2(device, steps, warmup):
-    """Single view: 1M Gaussians SH3 1080p, fwd+bwd raster + L1 + SSIM."""
+    """Single view, benchmark configuration 2: 1M Gaussians SH3 1080p, fwd+bwd raster + L1 + SSIM."""
     import torch
 
     import gswarp_b200 as gs
@@ -294,7 +294,7 @@ def _event_ms(fn, reps, warmup):
 
 
 def measure_small_configs(device):
-    """BASELINE configs 1, 3 and 4 through the public API (device-resident
+    """Benchmark configurations 1, 3 and 4 through the public API (device-resident
     inputs, CUDA events, mean over repetitions after warm-up)."""
     import torch
 
