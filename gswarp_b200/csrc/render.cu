@@ -228,20 +228,29 @@ __global__ void __launch_bounds__(THREADS, 10) render_fwd_kernel(const gsb_rende
       const float dx = xy.x - fx;
       float ax, bx;
       column_terms(cf, dx, ax, bx);
+      // Both pixels' exponent, alpha and transmittance run straight through
+      // (two independent instruction streams); only the short updates below
+      // depend on the per-pixel decisions.
+      float alph[2], testT[2];
+      bool ok[2];
 #pragma unroll
       for (int p = 0; p < 2; ++p) {
-        if (done[p]) continue;
         const float power2 = power2_of(cf, ax, bx, xy.y - fy[p]);
-        if (power2 > 0.0f) continue;
-        const float alpha = fminf(0.99f, cf.w * ex2_approx(power2));
-        if (alpha < (1.0f / 255.0f)) continue;
-        const float test_T = T[p] * (1.0f - alpha);
+        alph[p] = fminf(0.99f, cf.w * ex2_approx(power2));
+        testT[p] = T[p] * (1.0f - alph[p]);
+        ok[p] = !done[p] && !(power2 > 0.0f) && !(alph[p] < (1.0f / 255.0f));
+      }
+      const float4 cd = s_rgbd[j];
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        if (!ok[p]) continue;
+        const float alpha = alph[p];
+        const float test_T = testT[p];
         if (test_T < 0.0001f) {
           done[p] = true;
           continue;
         }
         const float contrib = alpha * T[p];
-        const float4 cd = s_rgbd[j];
         c0[p] += cd.x * contrib;
         c1[p] += cd.y * contrib;
         c2[p] += cd.z * contrib;
@@ -355,46 +364,58 @@ struct BwdSums {
 
 // One pixel's contribution of the Gaussian at this position (3DGS
 // recurrences accum_rec / last_alpha / last_color, backward_kernels.py:
-// 637-671).  Returns whether the pixel contributed.
+// 637-671).  Returns whether the pixel contributed.  The arithmetic runs
+// straight through (no early return) and only the state updates depend on
+// whether the pixel contributes, so the two pixels of a thread form two
+// independent instruction streams the scheduler can interleave; for a
+// contributing pixel every value is the same expression as before.
 template <bool DEPTH, bool GA>
-__device__ __forceinline__ bool bwd_pixel(BwdPixel& s, const float4 cf, float ax, float bx, float y,
+__device__ __forceinline__ bool bwd_pixel(BwdPixel& s, bool e, const float4 cf, float ax, float bx, float y,
                                           const float4 cd, bool has_bg, BwdSums& m) {
   const float dy = y - s.fy;
   const float power2 = power2_of(cf, ax, bx, dy);
-  if (power2 > 0.0f) return false;
   const float G = ex2_approx(power2);
   const float alpha = fminf(0.99f, cf.w * G);
-  if (alpha < (1.0f / 255.0f)) return false;
+  const bool ok = e && !(power2 > 0.0f) && !(alpha < (1.0f / 255.0f));
   // alpha <= 0.99, so 1 - alpha >= 0.01 (the reference's 1e-5 floor never binds)
   const float inv_oma = fast_rcp(1.0f - alpha);
-  s.T = s.T * inv_oma;
-  const float dchannel = alpha * s.T;
+  const float T = s.T * inv_oma;
+  const float dchannel = alpha * T;
   const float cg = cd.x * s.g0 + cd.y * s.g1 + cd.z * s.g2;
-  s.S = __fmaf_rn(s.la, s.lcg - s.S, s.S);
-  s.lcg = cg;
-  float dL_dopa = cg - s.S;
-  m.dcol0 += dchannel * s.g0;
-  m.dcol1 += dchannel * s.g1;
-  m.dcol2 += dchannel * s.g2;
+  const float S = __fmaf_rn(s.la, s.lcg - s.S, s.S);
+  float dL_dopa = cg - S;
+  float adr = 0.0f, aar = 0.0f;
   if (DEPTH) {
-    s.adr = __fmaf_rn(s.la, s.ld - s.adr, s.adr);
-    s.ld = cd.w;
-    dL_dopa += (cd.w - s.adr) * s.gd;
-    m.ddepth += dchannel * s.gd;
+    adr = __fmaf_rn(s.la, s.ld - s.adr, s.adr);
+    dL_dopa += (cd.w - adr) * s.gd;
   }
   if (GA) {
-    s.aar = s.la + (1.0f - s.la) * s.aar;
-    dL_dopa += (1.0f - s.aar) * s.ga;
+    aar = s.la + (1.0f - s.la) * s.aar;
+    dL_dopa += (1.0f - aar) * s.ga;
   }
-  dL_dopa *= s.T;
-  s.la = alpha;
+  dL_dopa *= T;
   if (has_bg) dL_dopa += (-s.T_final * inv_oma) * s.bg_dot;
   const float u = G * dL_dopa;
   const float uy = u * dy;
-  m.U += u;
-  m.UY += uy;
-  m.UYY = __fmaf_rn(uy, dy, m.UYY);
-  return true;
+  if (ok) {
+    s.T = T;
+    s.S = S;
+    s.lcg = cg;
+    s.la = alpha;
+    if (DEPTH) {
+      s.adr = adr;
+      s.ld = cd.w;
+      m.ddepth += dchannel * s.gd;
+    }
+    if (GA) s.aar = aar;
+    m.dcol0 += dchannel * s.g0;
+    m.dcol1 += dchannel * s.g1;
+    m.dcol2 += dchannel * s.g2;
+    m.U += u;
+    m.UY += uy;
+    m.UYY = __fmaf_rn(uy, dy, m.UYY);
+  }
+  return ok;
 }
 
 // DEPTH: compute_depth with a depth gradient given; GA: an alpha gradient
@@ -516,8 +537,9 @@ __global__ void __launch_bounds__(THREADS, 8) render_bwd_kernel(const gsb_render
         dx = xy.x - fx;
         float ax, bx;
         column_terms(cf, dx, ax, bx);
-        if (e0) contrib |= bwd_pixel<DEPTH, GA>(px[0], cf, ax, bx, xy.y, cd, has_bg, m);
-        if (e1) contrib |= bwd_pixel<DEPTH, GA>(px[1], cf, ax, bx, xy.y, cd, has_bg, m);
+        const bool c0 = bwd_pixel<DEPTH, GA>(px[0], e0, cf, ax, bx, xy.y, cd, has_bg, m);
+        const bool c1 = bwd_pixel<DEPTH, GA>(px[1], e1, cf, ax, bx, xy.y, cd, has_bg, m);
+        contrib = c0 || c1;
       }
       if (__any_sync(FULL, contrib)) {
         const float4 con = s_con[j];
