@@ -24,7 +24,7 @@ GSB_ERR_OVERFLOW = -2
 GSB_ERR_CUDA = -3
 GSB_ERR_TIMEOUT = -4
 
-ABI_VERSION = 12
+ABI_VERSION = 13
 RECORD_FLOATS = 12
 GRAD_FLOATS = 12
 
@@ -78,6 +78,7 @@ class RenderFwdArgs(ctypes.Structure):
         ("ranges", vp), ("point_list", vp), ("records", vp), ("background", vp),
         ("out_color", vp), ("out_depth", vp), ("out_alpha", vp), ("n_contrib", vp),
         ("top_k", c_int), ("gs_per_pixel", vp), ("weight_per_gs_pixel", vp), ("x_mu", vp),
+        ("aux_scratch", vp),
     ]
 
 

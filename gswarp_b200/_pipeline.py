@@ -326,9 +326,11 @@ def binning(pre: Preprocessed, cam: Camera, coverage_mode: int, want_ids: bool =
 
 
 def render(pre: Preprocessed, binned: Binned, cam: Camera, background: torch.Tensor, compute_depth: bool,
-           top_k: int = 0) -> Rendered:
+           top_k: int = 0, split_aux: bool = True) -> Rendered:
     """Render forward; ``top_k > 0`` also fills the flow auxiliary outputs
-    (first ``top_k`` contributors per pixel: ids, weights, centre offsets)."""
+    (first ``top_k`` contributors per pixel: ids, weights, centre offsets),
+    through a 16-byte-record scratch and a split kernel (``split_aux``) or
+    written directly by the render."""
     dev = pre.records.device
     H, W = cam.H, cam.W
     out = Rendered(
@@ -337,10 +339,13 @@ def render(pre: Preprocessed, binned: Binned, cam: Camera, background: torch.Ten
         alpha=torch.empty((1, H, W), dtype=torch.float32, device=dev),
         n_contrib=torch.empty(H * W, dtype=torch.int32, device=dev),
     )
+    aux_scratch = None
     if top_k > 0:
         out.gs_per_pixel = torch.empty((top_k, H, W), dtype=torch.int32, device=dev)
         out.weight_per_gs_pixel = torch.empty((top_k, H, W), dtype=torch.float32, device=dev)
         out.x_mu = torch.empty((2, top_k, H, W), dtype=torch.float32, device=dev)
+        if split_aux:  # one 16-byte record per slot, split into the three outputs by a second kernel
+            aux_scratch = torch.empty((top_k, H, W, 4), dtype=torch.float32, device=dev)
     a = _lib.RenderFwdArgs()
     a.W, a.H = W, H
     a.compute_depth = int(bool(compute_depth))
@@ -356,7 +361,9 @@ def render(pre: Preprocessed, binned: Binned, cam: Camera, background: torch.Ten
     a.gs_per_pixel = _lib.ptr(out.gs_per_pixel)
     a.weight_per_gs_pixel = _lib.ptr(out.weight_per_gs_pixel)
     a.x_mu = _lib.ptr(out.x_mu)
-    info = {"num_rendered": binned.num_rendered, "P": pre.records.shape[0], "kernels": 1}
+    a.aux_scratch = _lib.ptr(aux_scratch)
+    info = {"num_rendered": binned.num_rendered, "P": pre.records.shape[0],
+            "kernels": 2 if aux_scratch is not None else 1}
     with _stage_timer("render_fwd", info):
         _lib.call("gsb_render_fwd", a, _lib.stream_handle(dev))
     if TIMING_ENABLED:

@@ -259,10 +259,15 @@ __global__ void __launch_bounds__(THREADS, 10) render_fwd_kernel(const gsb_rende
         if (AUX) {
           if (nsucc[p] < a.top_k) {
             const long long o = (long long)nsucc[p] * npix + (long long)(py0 + 4 * p) * a.W + pxi;
-            a.gs_per_pixel[o] = s_id[j];
-            a.weight_per_gs_pixel[o] = contrib;
-            a.x_mu[o] = dx;
-            a.x_mu[(long long)a.top_k * npix + o] = xy.y - fy[p];
+            if (a.aux_scratch) {
+              reinterpret_cast<float4*>(a.aux_scratch)[o] =
+                  make_float4(__int_as_float(s_id[j]), contrib, dx, xy.y - fy[p]);
+            } else {
+              a.gs_per_pixel[o] = s_id[j];
+              a.weight_per_gs_pixel[o] = contrib;
+              a.x_mu[o] = dx;
+              a.x_mu[(long long)a.top_k * npix + o] = xy.y - fy[p];
+            }
           }
           ++nsucc[p];
         }
@@ -279,10 +284,14 @@ __global__ void __launch_bounds__(THREADS, 10) render_fwd_kernel(const gsb_rende
     if (AUX)
       for (int k = nsucc[p]; k < a.top_k; ++k) {
         const long long o = (long long)k * npix + pix;
-        a.gs_per_pixel[o] = -1;
-        a.weight_per_gs_pixel[o] = 0.0f;
-        a.x_mu[o] = 0.0f;
-        a.x_mu[(long long)a.top_k * npix + o] = 0.0f;
+        if (a.aux_scratch) {
+          reinterpret_cast<float4*>(a.aux_scratch)[o] = make_float4(__int_as_float(-1), 0.0f, 0.0f, 0.0f);
+        } else {
+          a.gs_per_pixel[o] = -1;
+          a.weight_per_gs_pixel[o] = 0.0f;
+          a.x_mu[o] = 0.0f;
+          a.x_mu[(long long)a.top_k * npix + o] = 0.0f;
+        }
       }
     a.n_contrib[pix] = last[p];
     a.out_color[pix] = c0[p] + T[p] * a.background[0];
@@ -291,6 +300,20 @@ __global__ void __launch_bounds__(THREADS, 10) render_fwd_kernel(const gsb_rende
     a.out_alpha[pix] = wsum[p];
     a.out_depth[pix] = dacc[p];
   }
+}
+
+// Splits the (K,H,W) 16-byte slot records into the flow outputs: one thread
+// per (slot, pixel), coalesced loads and stores.
+__global__ void flow_aux_split_kernel(long long n, long long kn, const float4* __restrict__ scratch,
+                                      int* __restrict__ ids, float* __restrict__ weights,
+                                      float* __restrict__ x_mu) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float4 r = scratch[i];
+  ids[i] = __float_as_int(r.x);
+  weights[i] = r.y;
+  x_mu[i] = r.z;
+  x_mu[kn + i] = r.w;
 }
 
 // Transpose reduction of ten per-lane values over a warp (12 shuffles).
@@ -585,12 +608,21 @@ GSB_EXPORT int gsb_render_fwd(const gsb_render_fwd_args* a, void* stream) {
     set_error("gsb_render_fwd: top_k > 0 needs gs_per_pixel, weight_per_gs_pixel and x_mu");
     return GSB_ERR_INVALID;
   }
+  if (aux && a->aux_scratch && (reinterpret_cast<uintptr_t>(a->aux_scratch) & 15)) {
+    set_error("gsb_render_fwd: aux_scratch needs 16-byte alignment");
+    return GSB_ERR_INVALID;
+  }
   if (a->compute_depth)
     aux ? render_fwd_kernel<true, true><<<gx * gy, THREADS, 0, s>>>(*a, gx)
         : render_fwd_kernel<true, false><<<gx * gy, THREADS, 0, s>>>(*a, gx);
   else
     aux ? render_fwd_kernel<false, true><<<gx * gy, THREADS, 0, s>>>(*a, gx)
         : render_fwd_kernel<false, false><<<gx * gy, THREADS, 0, s>>>(*a, gx);
+  if (aux && a->aux_scratch) {
+    const long long kn = (long long)a->top_k * a->W * a->H;
+    flow_aux_split_kernel<<<(unsigned)((kn + 255) / 256), 256, 0, s>>>(
+        kn, kn, reinterpret_cast<const float4*>(a->aux_scratch), a->gs_per_pixel, a->weight_per_gs_pixel, a->x_mu);
+  }
   return check_launch("render_fwd_kernel");
 }
 

@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define GSB_ABI_VERSION 12
+#define GSB_ABI_VERSION 13
 
 #define GSB_OK 0
 #define GSB_ERR_INVALID (-1)  /* bad argument: ValueError in Python          */
@@ -184,6 +184,11 @@ typedef struct {
   int* gs_per_pixel;        /*   (K,H,W) ids of the first K contributors, -1 where none */
   float* weight_per_gs_pixel; /* (K,H,W) their compositing weights alpha * T */
   float* x_mu;              /*   (2,K,H,W) offsets centre - pixel (dx planes, then dy) */
+  float* aux_scratch;       /* optional (K,H,W,4) floats, 16-byte aligned: the render writes each
+                               slot as one 16-byte (id, weight, dx, dy) record here, and a second
+                               kernel splits the records into the three outputs with coalesced
+                               stores (a quarter of the store transactions of writing the
+                               outputs directly); NULL: the outputs are written directly */
 } gsb_render_fwd_args;
 
 int gsb_render_fwd(const gsb_render_fwd_args* a, void* stream);

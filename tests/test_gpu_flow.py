@@ -126,3 +126,22 @@ def test_flow_backward(cuda):
                      (ps_t[4].grad, want.grad_rotations)):
         assert float((got - ref).norm()) <= 1e-3 * float(ref.norm()) + 1e-9
     assert float((ps_t[0].grad - ps_std[0].grad).norm()) > 1e-3 * float(ps_std[0].grad.norm())
+
+
+def test_flow_aux_direct_and_split_writes_agree(cuda):
+    """The render writes the top-K slots either straight into the three outputs or as 16-byte records that a
+    second kernel splits; both give the same outputs bit for bit."""
+    scene, view, s, kw = _setup("cfg2_small_view", cuda)
+    g = pl.make_gaussians(s.means, s.opacities, s.scales, s.rotations, None, s.sh, None, 1.0, scene.sh_degree)
+    cam = pl.Camera(W=view.width, H=view.height, tanfovx=view.tanfovx, tanfovy=view.tanfovy,
+                    viewmatrix=kw["viewmatrix"], projmatrix=kw["projmatrix"], campos=kw["campos"])
+    pre = pl.preprocess(g, cam, 1)
+    binned = pl.binning(pre, cam, 1)
+    split = pl.render(pre, binned, cam, kw["bg"], True, top_k=12, split_aux=True)
+    direct = pl.render(pre, binned, cam, kw["bg"], True, top_k=12, split_aux=False)
+    torch.cuda.synchronize()
+    assert torch.equal(split.gs_per_pixel, direct.gs_per_pixel)
+    assert torch.equal(split.weight_per_gs_pixel.view(torch.int32), direct.weight_per_gs_pixel.view(torch.int32))
+    assert torch.equal(split.x_mu.view(torch.int32), direct.x_mu.view(torch.int32))
+    assert torch.equal(split.color, direct.color)
+    assert bool((split.gs_per_pixel >= 0).any()) and bool((split.gs_per_pixel < 0).any())
