@@ -96,11 +96,14 @@ __global__ void __launch_bounds__(THREADS) ssim_fwd_kernel(const gsb_ssim_fwd_ar
   // Horizontal pass (fused_ssim.py:477-511): symmetric tap pairs, then centre.
   if (threadIdx.x < H_ITEMS) {
     const int r = threadIdx.x / HSEG, c0 = (threadIdx.x % HSEG) * RH;
-    float xv[RH + 10], yv[RH + 10];
+    // x^2 + y^2 and x*y once per window value (each is used by up to 11 outputs)
+    float xv[RH + 10], yv[RH + 10], sq[RH + 10], xy[RH + 10];
 #pragma unroll
     for (int q = 0; q < RH + 10; ++q) {
       xv[q] = s_x[r][c0 + q];
       yv[q] = s_y[r][c0 + q];
+      sq[q] = xv[q] * xv[q] + yv[q] * yv[q];
+      xy[q] = xv[q] * yv[q];
     }
 #pragma unroll
     for (int j = 0; j < RH; ++j) {
@@ -108,18 +111,16 @@ __global__ void __launch_bounds__(THREADS) ssim_fwd_kernel(const gsb_ssim_fwd_ar
 #pragma unroll
       for (int k = 0; k < 5; ++k) {
         const float g = GW[k];
-        const float v1l = xv[j + k], v2l = yv[j + k];
-        const float v1r = xv[j + 10 - k], v2r = yv[j + 10 - k];
-        a0 += g * (v1l + v1r);
-        a1 += g * (v2l + v2r);
-        a2 += g * (v1l * v1l + v2l * v2l + v1r * v1r + v2r * v2r);
-        a3 += g * (v1l * v2l + v1r * v2r);
+        const int l = j + k, rr = j + 10 - k;
+        a0 += g * (xv[l] + xv[rr]);
+        a1 += g * (yv[l] + yv[rr]);
+        a2 += g * (sq[l] + sq[rr]);
+        a3 += g * (xy[l] + xy[rr]);
       }
-      const float v1c = xv[j + 5], v2c = yv[j + 5];
-      a0 += GW[5] * v1c;
-      a1 += GW[5] * v2c;
-      a2 += GW[5] * (v1c * v1c + v2c * v2c);
-      a3 += GW[5] * v1c * v2c;
+      a0 += GW[5] * xv[j + 5];
+      a1 += GW[5] * yv[j + 5];
+      a2 += GW[5] * sq[j + 5];
+      a3 += GW[5] * xy[j + 5];
       s_h[0][r][c0 + j] = a0;
       s_h[1][r][c0 + j] = a1;
       s_h[2][r][c0 + j] = a2;
