@@ -212,17 +212,15 @@ __device__ __forceinline__ float boxbox_dist(const float* a, const float* b) {
   return d[0] * d[0] + d[1] * d[1] + d[2] * d[2];
 }
 
+// Inserts d into the sorted three smallest (b0 <= b1 <= b2): a compare-exchange
+// chain, branch-free; the kept values (ties included) are the ones a
+// shift-insertion keeps, in the same order.
 __device__ __forceinline__ void push3(float d, float& b0, float& b1, float& b2) {
-  if (d < b0) {
-    b2 = b1;
-    b1 = b0;
-    b0 = d;
-  } else if (d < b1) {
-    b2 = b1;
-    b1 = d;
-  } else if (d < b2) {
-    b2 = d;
-  }
+  const float c0 = fmaxf(b0, d);
+  b0 = fminf(b0, d);
+  const float c1 = fmaxf(b1, c0);
+  b1 = fminf(b1, c0);
+  b2 = fminf(b2, c1);
 }
 
 __device__ __forceinline__ float warp_max(float v) {
@@ -231,43 +229,106 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
-// Scan leaf L for the lanes with `need`: lane j holds the leaf's point j and
-// broadcasts it; the query's own index is skipped.
-__device__ __forceinline__ void scan_leaf(int L, int P, int my_idx, bool need, float px, float py, float pz,
+// Candidate leaf L against every lane's query point: the warp stages the
+// leaf's points in shared memory (one 16-byte slot per lane), then each lane
+// reads them back by broadcast.  OWN: L is the query's own leaf, whose point
+// at the lane's own position is skipped (as a +big distance, which top-3
+// never keeps).
+template <bool OWN>
+__device__ __forceinline__ void scan_leaf(int L, int P, bool need, float px, float py, float pz,
                                           const float* __restrict__ sx, const float* __restrict__ sy,
-                                          const float* __restrict__ sz, float& b0, float& b1, float& b2) {
+                                          const float* __restrict__ sz, float4* s_pts, float& b0, float& b1,
+                                          float& b2) {
+  const int lane = threadIdx.x & 31;
+  const int c = L * LEAF + lane;
+  __syncwarp();  // the previous leaf's readers are done with s_pts
+  s_pts[lane] = c < P ? make_float4(sx[c], sy[c], sz[c], 0.0f) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  __syncwarp();
+  if (!need) return;
+  const int n = min(LEAF, P - L * LEAF);
+#pragma unroll 4
+  for (int k = 0; k < n; ++k) {
+    const float4 q = s_pts[k];
+    const float dx = px - q.x, dy = py - q.y, dz = pz - q.z;
+    float d = dx * dx + dy * dy + dz * dz;
+    if (OWN && k == lane) d = FLT_BIG_K;
+    push3(d, b0, b1, b2);
+  }
+}
+
+// Candidate leaf L for the few lanes in needmask (not the query's own leaf):
+// candidate-parallel instead of query-parallel.  For each needing lane q,
+// every lane computes q's distance to its own candidate (same operands, same
+// order as scan_leaf), three warp minimum reductions take the three smallest
+// (ties kept: one lane removed per round) and q pushes them into its top
+// three -- the same three smallest values as pushing all 32.  Cheaper than
+// the 32-step scan when only a few lanes need the leaf (sparse regions, where
+// a few far query points otherwise make the warp scan many distant leaves).
+constexpr int SPARSE_LANES = 8;
+
+__device__ __forceinline__ float warp_min(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fminf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ void scan_leaf_sparse(int L, int P, unsigned needmask, float px, float py, float pz,
+                                                 const float* __restrict__ sx, const float* __restrict__ sy,
+                                                 const float* __restrict__ sz, float& b0, float& b1, float& b2) {
   const int lane = threadIdx.x & 31;
   const int c = L * LEAF + lane;
   const bool cv = c < P;
   const float cx = cv ? sx[c] : 0.0f, cy = cv ? sy[c] : 0.0f, cz = cv ? sz[c] : 0.0f;
-  const int n = min(LEAF, P - L * LEAF);
-  for (int k = 0; k < n; ++k) {
-    const float qx = __shfl_sync(0xffffffffu, cx, k);
-    const float qy = __shfl_sync(0xffffffffu, cy, k);
-    const float qz = __shfl_sync(0xffffffffu, cz, k);
-    if (need && L * LEAF + k != my_idx) {
-      const float dx = px - qx, dy = py - qy, dz = pz - qz;
-      push3(dx * dx + dy * dy + dz * dz, b0, b1, b2);
+  while (needmask) {
+    const int q = __ffs(needmask) - 1;
+    needmask &= needmask - 1;
+    const float qx = __shfl_sync(0xffffffffu, px, q), qy = __shfl_sync(0xffffffffu, py, q);
+    const float qz = __shfl_sync(0xffffffffu, pz, q), qb2 = __shfl_sync(0xffffffffu, b2, q);
+    float d = FLT_BIG_K;
+    if (cv) {
+      const float dx = qx - cx, dy = qy - cy, dz = qz - cz;
+      d = dx * dx + dy * dy + dz * dz;
+    }
+    float m[3];
+#pragma unroll
+    for (int r = 0; r < 3; ++r) {
+      m[r] = warp_min(d);
+      if (r == 0 && !(m[0] < qb2)) break;  // nothing below q's third-best: no change
+      // drop one lane holding the minimum (a tie keeps its other copies)
+      const unsigned at = __ballot_sync(0xffffffffu, d == m[r]);
+      if (lane == __ffs(at) - 1) d = FLT_BIG_K;
+      if (r == 0) {
+        m[1] = m[2] = FLT_BIG_K;
+      }
+    }
+    if (lane == q && m[0] < qb2) {
+      push3(m[0], b0, b1, b2);
+      push3(m[1], b0, b1, b2);
+      push3(m[2], b0, b1, b2);
     }
   }
 }
 
 // One warp per query leaf.  Boxes: leaves (nl), parents (np), grandparents (ng).
-__global__ void __launch_bounds__(256) search_kernel(int P, int nl, int np, int ng, const float* __restrict__ sx,
+__global__ void __launch_bounds__(256, 4) search_kernel(int P, int nl, int np, int ng, const float* __restrict__ sx,
                                                      const float* __restrict__ sy, const float* __restrict__ sz,
                                                      const float* __restrict__ leaf_b, const float* __restrict__ par_b,
                                                      const float* __restrict__ gp_b,
                                                      const unsigned* __restrict__ order, float* __restrict__ out) {
+  __shared__ float4 s_leaf[256 / 32][32];
   const int lane = threadIdx.x & 31;
   const int qleaf = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
   if (qleaf >= nl) return;  // whole warp
+  float4* s_pts = s_leaf[threadIdx.x >> 5];
   const int my_idx = qleaf * LEAF + lane;
   const bool valid = my_idx < P;
   const float px = valid ? sx[my_idx] : 0.0f, py = valid ? sy[my_idx] : 0.0f, pz = valid ? sz[my_idx] : 0.0f;
   float b0 = FLT_BIG_K, b1 = FLT_BIG_K, b2 = FLT_BIG_K;
   // 1. the query's own leaf (its Morton neighbours): a first third-best.
-  scan_leaf(qleaf, P, my_idx, valid, px, py, pz, sx, sy, sz, b0, b1, b2);
-  const float* qb = leaf_b + (size_t)qleaf * 6;  // the warp's query AABB
+  scan_leaf<true>(qleaf, P, valid, px, py, pz, sx, sy, sz, s_pts, b0, b1, b2);
+  float qb[6];  // the warp's query AABB
+#pragma unroll
+  for (int k = 0; k < 6; ++k) qb[k] = leaf_b[(size_t)qleaf * 6 + k];
   // 2. two walks over grandparents -> parents -> leaves, 32 boxes tested at a
   // time against the warp's query AABB: the first visits only leaves whose
   // box overlaps the query AABB (the local neighbourhood, which brings every
@@ -287,19 +348,33 @@ __global__ void __launch_bounds__(256) search_kernel(int P, int nl, int np, int 
         const int pp = g * 32 + __ffs(pmask) - 1;
         pmask &= pmask - 1;
         if (pass == 1) mb2 = warp_max(valid ? b2 : 0.0f);
+        // lane j holds leaf pp*32+j's box; the per-point test below takes it
+        // by shuffle instead of a dependent load per visited leaf (a query
+        // leaf spanning a Morton discontinuity overlaps thousands of leaves)
         const int lidx = pp * 32 + lane;
+        float lb[6];
+#pragma unroll
+        for (int k = 0; k < 6; ++k) lb[k] = lidx < nl ? leaf_b[(size_t)lidx * 6 + k] : 0.0f;
         bool lneed = false;
         if (lidx < nl && lidx != qleaf) {
-          const float d = boxbox_dist(qb, leaf_b + (size_t)lidx * 6);
+          const float d = boxbox_dist(qb, lb);
           lneed = pass == 0 ? d == 0.0f : (d > 0.0f && d <= mb2);
         }
         unsigned lmask = __ballot_sync(0xffffffffu, lneed);
         while (lmask) {
-          const int L = pp * 32 + __ffs(lmask) - 1;
+          const int j = __ffs(lmask) - 1;
+          const int L = pp * 32 + j;
           lmask &= lmask - 1;
-          const bool need = valid && !(box_dist(leaf_b + (size_t)L * 6, px, py, pz) > b2);
-          if (!__any_sync(0xffffffffu, need)) continue;
-          scan_leaf(L, P, my_idx, need, px, py, pz, sx, sy, sz, b0, b1, b2);
+          float cb[6];
+#pragma unroll
+          for (int k = 0; k < 6; ++k) cb[k] = __shfl_sync(0xffffffffu, lb[k], j);
+          const bool need = valid && !(box_dist(cb, px, py, pz) > b2);
+          const unsigned needmask = __ballot_sync(0xffffffffu, need);
+          if (!needmask) continue;
+          if (__popc(needmask) <= SPARSE_LANES)
+            scan_leaf_sparse(L, P, needmask, px, py, pz, sx, sy, sz, b0, b1, b2);
+          else
+            scan_leaf<false>(L, P, need, px, py, pz, sx, sy, sz, s_pts, b0, b1, b2);
         }
       }
     }
