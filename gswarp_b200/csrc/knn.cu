@@ -309,6 +309,21 @@ __device__ __forceinline__ void scan_leaf_sparse(int L, int P, unsigned needmask
   }
 }
 
+// Visits candidate leaf L (not the query's own) for the lanes whose lower
+// bound to its box (cb, the same on every lane) does not exceed their third-best.
+__device__ __forceinline__ void visit_leaf(int L, const float (&cb)[6], int P, bool valid, float px, float py,
+                                           float pz, const float* __restrict__ sx, const float* __restrict__ sy,
+                                           const float* __restrict__ sz, float4* s_pts, float& b0, float& b1,
+                                           float& b2) {
+  const bool need = valid && !(box_dist(cb, px, py, pz) > b2);
+  const unsigned needmask = __ballot_sync(0xffffffffu, need);
+  if (!needmask) return;
+  if (__popc(needmask) <= SPARSE_LANES)
+    scan_leaf_sparse(L, P, needmask, px, py, pz, sx, sy, sz, b0, b1, b2);
+  else
+    scan_leaf<false>(L, P, need, px, py, pz, sx, sy, sz, s_pts, b0, b1, b2);
+}
+
 // One warp per query leaf.  Boxes: leaves (nl), parents (np), grandparents (ng).
 __global__ void __launch_bounds__(256, 4) search_kernel(int P, int nl, int np, int ng, const float* __restrict__ sx,
                                                      const float* __restrict__ sy, const float* __restrict__ sz,
@@ -326,10 +341,23 @@ __global__ void __launch_bounds__(256, 4) search_kernel(int P, int nl, int np, i
   float b0 = FLT_BIG_K, b1 = FLT_BIG_K, b2 = FLT_BIG_K;
   // 1. the query's own leaf (its Morton neighbours): a first third-best.
   scan_leaf<true>(qleaf, P, valid, px, py, pz, sx, sy, sz, s_pts, b0, b1, b2);
+  // 2. the two Morton-adjacent leaves: a query leaf that spans a jump of the
+  // Morton curve holds the tail of one region and the head of another, whose
+  // points continue in these two leaves, so every lane gets a close
+  // third-best before the walks (which then skip both leaves).
+#pragma unroll
+  for (int side = -1; side <= 1; side += 2) {
+    const int L = qleaf + side;
+    if (L < 0 || L >= nl) continue;
+    float cb[6];
+#pragma unroll
+    for (int k = 0; k < 6; ++k) cb[k] = leaf_b[(size_t)L * 6 + k];
+    visit_leaf(L, cb, P, valid, px, py, pz, sx, sy, sz, s_pts, b0, b1, b2);
+  }
   float qb[6];  // the warp's query AABB
 #pragma unroll
   for (int k = 0; k < 6; ++k) qb[k] = leaf_b[(size_t)qleaf * 6 + k];
-  // 2. two walks over grandparents -> parents -> leaves, 32 boxes tested at a
+  // 3. two walks over grandparents -> parents -> leaves, 32 boxes tested at a
   // time against the warp's query AABB: the first visits only leaves whose
   // box overlaps the query AABB (the local neighbourhood, which brings every
   // lane's third-best down quickly), the second every other leaf that its
@@ -337,16 +365,39 @@ __global__ void __launch_bounds__(256, 4) search_kernel(int P, int nl, int np, i
   // second walk skips exactly the leaves the first one visited.
   const int own_par = qleaf / 32, own_gp = own_par / 32;
   for (int pass = 0; pass < 2; ++pass) {
+    // grandparent distances to the query AABB, 32 at a time (lane k holds
+    // grandparent 32*chunk + k), taken by shuffle in the visiting order
+    int chunk = -1;
+    float dg = 0.0f;
     for (int gi = 0; gi < ng; ++gi) {
       const int g = gi == 0 ? own_gp : (gi <= own_gp ? gi - 1 : gi);
+      if ((g >> 5) != chunk) {
+        chunk = g >> 5;
+        const int t = chunk * 32 + lane;
+        float tb[6];
+#pragma unroll
+        for (int k = 0; k < 6; ++k) tb[k] = t < ng ? gp_b[(size_t)t * 6 + k] : 0.0f;
+        dg = boxbox_dist(qb, tb);
+      }
       float mb2 = pass == 0 ? 0.0f : warp_max(valid ? b2 : 0.0f);
-      if (boxbox_dist(qb, gp_b + (size_t)g * 6) > mb2) continue;
+      if (__shfl_sync(0xffffffffu, dg, g & 31) > mb2) continue;
       const int pidx = g * 32 + lane;
-      unsigned pmask =
-          __ballot_sync(0xffffffffu, pidx < np && boxbox_dist(qb, par_b + (size_t)pidx * 6) <= mb2);
+      float pbx[6];
+#pragma unroll
+      for (int k = 0; k < 6; ++k) pbx[k] = pidx < np ? par_b[(size_t)pidx * 6 + k] : 0.0f;
+      unsigned pmask = __ballot_sync(0xffffffffu, pidx < np && boxbox_dist(qb, pbx) <= mb2);
       while (pmask) {
-        const int pp = g * 32 + __ffs(pmask) - 1;
+        const int pj = __ffs(pmask) - 1;
+        const int pp = g * 32 + pj;
         pmask &= pmask - 1;
+        // skip the parent when no lane's own bound reaches its box: no leaf
+        // inside it can then be needed, now or later (third-bests only shrink)
+        {
+          float cb[6];
+#pragma unroll
+          for (int k = 0; k < 6; ++k) cb[k] = __shfl_sync(0xffffffffu, pbx[k], pj);
+          if (!__any_sync(0xffffffffu, valid && !(box_dist(cb, px, py, pz) > b2))) continue;
+        }
         if (pass == 1) mb2 = warp_max(valid ? b2 : 0.0f);
         // lane j holds leaf pp*32+j's box; the per-point test below takes it
         // by shuffle instead of a dependent load per visited leaf (a query
@@ -356,7 +407,7 @@ __global__ void __launch_bounds__(256, 4) search_kernel(int P, int nl, int np, i
 #pragma unroll
         for (int k = 0; k < 6; ++k) lb[k] = lidx < nl ? leaf_b[(size_t)lidx * 6 + k] : 0.0f;
         bool lneed = false;
-        if (lidx < nl && lidx != qleaf) {
+        if (lidx < nl && (lidx < qleaf - 1 || lidx > qleaf + 1)) {
           const float d = boxbox_dist(qb, lb);
           lneed = pass == 0 ? d == 0.0f : (d > 0.0f && d <= mb2);
         }
@@ -368,13 +419,7 @@ __global__ void __launch_bounds__(256, 4) search_kernel(int P, int nl, int np, i
           float cb[6];
 #pragma unroll
           for (int k = 0; k < 6; ++k) cb[k] = __shfl_sync(0xffffffffu, lb[k], j);
-          const bool need = valid && !(box_dist(cb, px, py, pz) > b2);
-          const unsigned needmask = __ballot_sync(0xffffffffu, need);
-          if (!needmask) continue;
-          if (__popc(needmask) <= SPARSE_LANES)
-            scan_leaf_sparse(L, P, needmask, px, py, pz, sx, sy, sz, b0, b1, b2);
-          else
-            scan_leaf<false>(L, P, need, px, py, pz, sx, sy, sz, s_pts, b0, b1, b2);
+          visit_leaf(L, cb, P, valid, px, py, pz, sx, sy, sz, s_pts, b0, b1, b2);
         }
       }
     }
