@@ -71,17 +71,21 @@ __global__ void __launch_bounds__(256) bounds_partial_kernel(int P, const float*
 // and round to float32 like the reference's wp.float32(...) kernel arguments.
 __global__ void bounds_final_kernel(int nparts, const float* __restrict__ part,
                                     float* __restrict__ bounds) {
-  if (threadIdx.x != 0) return;
-  float lo[3], hi[3];
-  for (int c = 0; c < 3; ++c) {
-    lo[c] = part[c];
-    hi[c] = part[3 + c];
-  }
-  for (int b = 1; b < nparts; ++b)
+  // one warp: lanes take the partials strided, then a shuffle min/max
+  // (minimum and maximum do not depend on the order)
+  const int lane = threadIdx.x & 31;
+  float lo[3] = {FLT_BIG_K, FLT_BIG_K, FLT_BIG_K}, hi[3] = {-FLT_BIG_K, -FLT_BIG_K, -FLT_BIG_K};
+  for (int b = lane; b < nparts; b += 32)
     for (int c = 0; c < 3; ++c) {
       lo[c] = fminf(lo[c], part[b * 6 + c]);
       hi[c] = fmaxf(hi[c], part[b * 6 + 3 + c]);
     }
+  for (int c = 0; c < 3; ++c)
+    for (int o = 16; o > 0; o >>= 1) {
+      lo[c] = fminf(lo[c], __shfl_xor_sync(0xffffffffu, lo[c], o));
+      hi[c] = fmaxf(hi[c], __shfl_xor_sync(0xffffffffu, hi[c], o));
+    }
+  if (lane != 0) return;
   for (int c = 0; c < 3; ++c) {
     const double l = lo[c];
     double h = hi[c];

@@ -130,8 +130,8 @@ __device__ __forceinline__ void cull_halves(int g, int cnt, const float4* s_box,
 //   power2 = cf.x dx^2 + (cf.z dy + cf.y dx) dy = log2(e) * (-(a dx^2 + c dy^2)/2 - b dx dy),
 // so exp(power) = ex2(power2).  ax = cf.x dx^2 and bx = cf.y dx are shared by
 // the thread's two pixels (same column).  Forward and backward evaluate it
-// through this one function with explicit FMAs, so they make the same
-// alpha decisions bit for bit.
+// through power2_of2 with explicit FMAs, so they make the same alpha
+// decisions bit for bit.
 __device__ __forceinline__ float4 power_coefs(float a, float b, float c) {
   const float L2E = 1.4426950408889634f;
   return make_float4(-0.5f * L2E * a, -L2E * b, -0.5f * L2E * c, 0.0f);
@@ -140,9 +140,16 @@ __device__ __forceinline__ void column_terms(const float4 cf, float dx, float& a
   ax = __fmul_rn(__fmul_rn(cf.x, dx), dx);
   bx = __fmul_rn(cf.y, dx);
 }
-__device__ __forceinline__ float power2_of(const float4 cf, float ax, float bx, float dy) {
-  return __fmaf_rn(__fmaf_rn(cf.z, dy, bx), dy, ax);
+// The exponent for the thread's two pixels (dy = (dy0, dy1)) as one packed
+// stream: per component fma(fma(cf.z, dy, bx), dy, ax), each rounded once.
+__device__ __forceinline__ float2 power2_of2(const float4 cf, float ax, float bx, float2 dy) {
+  return __ffma2_rn(__ffma2_rn(make_float2(cf.z, cf.z), dy, make_float2(bx, bx)), dy, make_float2(ax, ax));
 }
+// 1 - v per component, rounded once (fma(v, -1, 1) is the subtraction).
+__device__ __forceinline__ float2 one_minus2(float2 v) {
+  return __ffma2_rn(v, make_float2(-1.0f, -1.0f), make_float2(1.0f, 1.0f));
+}
+__device__ __forceinline__ float half_of(float2 v, int p) { return p ? v.y : v.x; }
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -171,8 +178,13 @@ __global__ void __launch_bounds__(THREADS, 10) render_fwd_kernel(const gsb_rende
   // the warp's 8x8 pixel block
   const float bx0 = (float)(__shfl_sync(FULL, pxi, 0)), by0 = (float)(__shfl_sync(FULL, py0, 0));
   const float bx1 = bx0 + 7.0f, by1 = by0 + 7.0f;
-  float fy[2], T[2], c0[2], c1[2], c2[2], wsum[2], dacc[2];
-  int last[2], nsucc[2] = {0, 0};
+  // The thread's two pixels (same column, rows py0 and py0 + 4) share every
+  // Gaussian operand, so their arithmetic runs as packed f32x2 operations
+  // (__ffma2_rn / __fmul2_rn / __fadd2_rn: per component the same IEEE
+  // round-to-nearest results as the scalar __fmaf_rn / __fmul_rn / __fadd_rn).
+  float fy[2];
+  float2 T = make_float2(1.0f, 1.0f), c0 = make_float2(0.0f, 0.0f), c1 = c0, c2 = c0, wsum = c0, dacc = c0;
+  int last[2] = {0, 0}, nsucc[2] = {0, 0};
   bool inside[2], done[2];
   const long long npix = (long long)a.W * a.H;
 #pragma unroll
@@ -181,10 +193,8 @@ __global__ void __launch_bounds__(THREADS, 10) render_fwd_kernel(const gsb_rende
     fy[p] = (float)py;
     inside[p] = pxi < a.W && py < a.H;
     done[p] = !inside[p];
-    T[p] = 1.0f;
-    c0[p] = c1[p] = c2[p] = wsum[p] = dacc[p] = 0.0f;
-    last[p] = 0;
   }
+  const float2 nfy = make_float2(-fy[0], -fy[1]);
   for (int b = range.x; b < range.y; b += BATCH) {
     if (__syncthreads_count(done[0] && done[1]) == THREADS) break;
     const int i = b + threadIdx.x;
@@ -229,33 +239,38 @@ __global__ void __launch_bounds__(THREADS, 10) render_fwd_kernel(const gsb_rende
       float ax, bx;
       column_terms(cf, dx, ax, bx);
       // Both pixels' exponent, alpha and transmittance run straight through
-      // (two independent instruction streams); only the short updates below
-      // depend on the per-pixel decisions.
-      float alph[2], testT[2];
-      bool ok[2];
-#pragma unroll
-      for (int p = 0; p < 2; ++p) {
-        const float power2 = power2_of(cf, ax, bx, xy.y - fy[p]);
-        alph[p] = fminf(0.99f, cf.w * ex2_approx(power2));
-        testT[p] = T[p] * (1.0f - alph[p]);
-        ok[p] = !done[p] && !(power2 > 0.0f) && !(alph[p] < (1.0f / 255.0f));
-      }
+      // as one packed stream; the per-pixel decisions only select.
+      const float2 dy = __fadd2_rn(make_float2(xy.y, xy.y), nfy);
+      const float2 pw = power2_of2(cf, ax, bx, dy);
+      float2 al = __fmul2_rn(make_float2(cf.w, cf.w), make_float2(ex2_approx(pw.x), ex2_approx(pw.y)));
+      al.x = fminf(0.99f, al.x);
+      al.y = fminf(0.99f, al.y);
+      const float2 tt = __fmul2_rn(T, one_minus2(al));
+      const bool ok0 = !done[0] && !(pw.x > 0.0f) && !(al.x < (1.0f / 255.0f));
+      const bool ok1 = !done[1] && !(pw.y > 0.0f) && !(al.y < (1.0f / 255.0f));
+      // a pixel whose transmittance would drop below 1e-4 stops before this Gaussian
+      const bool st0 = ok0 && tt.x < 0.0001f, st1 = ok1 && tt.y < 0.0001f;
+      const bool acc[2] = {ok0 && !st0, ok1 && !st1};
+      done[0] = done[0] || st0;
+      done[1] = done[1] || st1;
+      float2 cm = __fmul2_rn(al, T);  // alpha * T, zero where the pixel does not take the Gaussian
+      cm.x = acc[0] ? cm.x : 0.0f;
+      cm.y = acc[1] ? cm.y : 0.0f;
       const float4 cd = s_rgbd[j];
+      c0 = __ffma2_rn(make_float2(cd.x, cd.x), cm, c0);
+      c1 = __ffma2_rn(make_float2(cd.y, cd.y), cm, c1);
+      c2 = __ffma2_rn(make_float2(cd.z, cd.z), cm, c2);
+      wsum = __fadd2_rn(wsum, cm);
+      if (DEPTH) dacc = __ffma2_rn(make_float2(cd.w, cd.w), cm, dacc);
+      T.x = acc[0] ? tt.x : T.x;
+      T.y = acc[1] ? tt.y : T.y;
+      const int idx = b - range.x + j + 1;
+      last[0] = acc[0] ? idx : last[0];
+      last[1] = acc[1] ? idx : last[1];
 #pragma unroll
       for (int p = 0; p < 2; ++p) {
-        if (!ok[p]) continue;
-        const float alpha = alph[p];
-        const float test_T = testT[p];
-        if (test_T < 0.0001f) {
-          done[p] = true;
-          continue;
-        }
-        const float contrib = alpha * T[p];
-        c0[p] += cd.x * contrib;
-        c1[p] += cd.y * contrib;
-        c2[p] += cd.z * contrib;
-        wsum[p] += contrib;
-        if (DEPTH) dacc[p] += cd.w * contrib;
+        if (!acc[p]) continue;
+        const float contrib = p ? cm.y : cm.x;
         if (AUX) {
           if (nsucc[p] < a.top_k) {
             const long long o = (long long)nsucc[p] * npix + (long long)(py0 + 4 * p) * a.W + pxi;
@@ -271,8 +286,6 @@ __global__ void __launch_bounds__(THREADS, 10) render_fwd_kernel(const gsb_rende
           }
           ++nsucc[p];
         }
-        T[p] = test_T;
-        last[p] = b - range.x + j + 1;
       }
       }
     }
@@ -293,12 +306,13 @@ __global__ void __launch_bounds__(THREADS, 10) render_fwd_kernel(const gsb_rende
           a.x_mu[(long long)a.top_k * npix + o] = 0.0f;
         }
       }
+    const float Tp = half_of(T, p);
     a.n_contrib[pix] = last[p];
-    a.out_color[pix] = c0[p] + T[p] * a.background[0];
-    a.out_color[npix + pix] = c1[p] + T[p] * a.background[1];
-    a.out_color[2 * npix + pix] = c2[p] + T[p] * a.background[2];
-    a.out_alpha[pix] = wsum[p];
-    a.out_depth[pix] = dacc[p];
+    a.out_color[pix] = half_of(c0, p) + Tp * a.background[0];
+    a.out_color[npix + pix] = half_of(c1, p) + Tp * a.background[1];
+    a.out_color[2 * npix + pix] = half_of(c2, p) + Tp * a.background[2];
+    a.out_alpha[pix] = half_of(wsum, p);
+    a.out_depth[pix] = half_of(dacc, p);
   }
 }
 
@@ -362,15 +376,20 @@ __device__ __forceinline__ int warp_reduce10(const float (&v)[10], float& out) {
   return off < 0 ? -1 : (b4 ? 5 : 0) + off;
 }
 
-// Back-to-front state of one pixel (backward_kernels.py:606-625).
-// The colour part of accum_rec only enters dL/dalpha through its dot
-// product with the pixel's colour gradient g, so the state keeps that dot
-// product S = accum_rec . g (same recurrence, S' = la lcg + (1 - la) S with
-// lcg = last_color . g) instead of the three channels.
-struct BwdPixel {
-  int lc;
-  float fy, T, T_final, g0, g1, g2, gd, ga, bg_dot;
-  float S, lcg, adr, aar, la, ld;
+// Back-to-front state of the thread's two pixels (backward_kernels.py:
+// 606-625), one f32x2 component per pixel.  The colour part of accum_rec
+// only enters dL/dalpha through its dot product with the pixel's colour
+// gradient g, so the state keeps that dot product S = accum_rec . g.  The
+// reference advances accum_rec / last_alpha / last_color lazily, at the next
+// contributing Gaussian; here S (and the depth / alpha accumulators) advance
+// eagerly at the end of each contributing Gaussian -- the same operands in
+// the same expression, so the same values -- which leaves no last_* state:
+// with alpha masked to zero where a pixel does not take the Gaussian, the
+// update fma(0, ., S) leaves S unchanged and needs no per-pixel select.
+struct BwdPair {
+  int lc0, lc1;
+  float2 nfy, T, nTf, g0, g1, g2, gd, ga, bg_dot;
+  float2 S, adr, aar;
 };
 
 // Gradient sums of one Gaussian over the thread's pixels.  The per-pixel
@@ -385,60 +404,55 @@ struct BwdSums {
   float U, UY, UYY, dcol0, dcol1, dcol2, ddepth;
 };
 
-// One pixel's contribution of the Gaussian at this position (3DGS
+// The two pixels' contributions of the Gaussian at this position (3DGS
 // recurrences accum_rec / last_alpha / last_color, backward_kernels.py:
-// 637-671).  Returns whether the pixel contributed.  The arithmetic runs
-// straight through (no early return) and only the state updates depend on
-// whether the pixel contributes, so the two pixels of a thread form two
-// independent instruction streams the scheduler can interleave; for a
-// contributing pixel every value is the same expression as before.
+// 637-671), written to m; c0 / c1 tell whether each pixel contributed.  The
+// arithmetic runs straight through as one packed stream (both pixels share
+// the Gaussian's operands); the per-pixel decisions only mask alpha and G.
+// For a contributing pixel every value is the same expression as a scalar
+// evaluation of that pixel.
 template <bool DEPTH, bool GA>
-__device__ __forceinline__ bool bwd_pixel(BwdPixel& s, bool e, const float4 cf, float ax, float bx, float y,
-                                          const float4 cd, bool has_bg, BwdSums& m) {
-  const float dy = y - s.fy;
-  const float power2 = power2_of(cf, ax, bx, dy);
-  const float G = ex2_approx(power2);
-  const float alpha = fminf(0.99f, cf.w * G);
-  const bool ok = e && !(power2 > 0.0f) && !(alpha < (1.0f / 255.0f));
+__device__ __forceinline__ void bwd_pair(BwdPair& s, bool e0, bool e1, const float4 cf, float ax, float bx,
+                                         float y, const float4 cd, bool has_bg, BwdSums& m, bool& c0, bool& c1) {
+  const float2 neg1 = make_float2(-1.0f, -1.0f);
+  const float2 dy = __fadd2_rn(make_float2(y, y), s.nfy);
+  const float2 pw = power2_of2(cf, ax, bx, dy);
+  const float2 G = make_float2(ex2_approx(pw.x), ex2_approx(pw.y));
+  float2 al = __fmul2_rn(make_float2(cf.w, cf.w), G);
+  al.x = fminf(0.99f, al.x);
+  al.y = fminf(0.99f, al.y);
+  c0 = e0 && !(pw.x > 0.0f) && !(al.x < (1.0f / 255.0f));
+  c1 = e1 && !(pw.y > 0.0f) && !(al.y < (1.0f / 255.0f));
+  const float2 am = make_float2(c0 ? al.x : 0.0f, c1 ? al.y : 0.0f);
   // alpha <= 0.99, so 1 - alpha >= 0.01 (the reference's 1e-5 floor never binds)
-  const float inv_oma = fast_rcp(1.0f - alpha);
-  const float T = s.T * inv_oma;
-  const float dchannel = alpha * T;
-  const float cg = cd.x * s.g0 + cd.y * s.g1 + cd.z * s.g2;
-  const float S = __fmaf_rn(s.la, s.lcg - s.S, s.S);
-  float dL_dopa = cg - S;
-  float adr = 0.0f, aar = 0.0f;
-  if (DEPTH) {
-    adr = __fmaf_rn(s.la, s.ld - s.adr, s.adr);
-    dL_dopa += (cd.w - adr) * s.gd;
-  }
-  if (GA) {
-    aar = s.la + (1.0f - s.la) * s.aar;
-    dL_dopa += (1.0f - aar) * s.ga;
-  }
-  dL_dopa *= T;
-  if (has_bg) dL_dopa += (-s.T_final * inv_oma) * s.bg_dot;
-  const float u = G * dL_dopa;
-  const float uy = u * dy;
-  if (ok) {
-    s.T = T;
-    s.S = S;
-    s.lcg = cg;
-    s.la = alpha;
-    if (DEPTH) {
-      s.adr = adr;
-      s.ld = cd.w;
-      m.ddepth += dchannel * s.gd;
-    }
-    if (GA) s.aar = aar;
-    m.dcol0 += dchannel * s.g0;
-    m.dcol1 += dchannel * s.g1;
-    m.dcol2 += dchannel * s.g2;
-    m.U += u;
-    m.UY += uy;
-    m.UYY = __fmaf_rn(uy, dy, m.UYY);
-  }
-  return ok;
+  const float2 oma = one_minus2(am);
+  const float2 inv = make_float2(fast_rcp(oma.x), fast_rcp(oma.y));
+  const float2 T = __fmul2_rn(s.T, inv);
+  const float2 dch = __fmul2_rn(am, T);
+  const float2 cg = __ffma2_rn(make_float2(cd.z, cd.z), s.g2,
+                               __ffma2_rn(make_float2(cd.y, cd.y), s.g1, __fmul2_rn(make_float2(cd.x, cd.x), s.g0)));
+  float2 dL = __ffma2_rn(s.S, neg1, cg);  // cg - S
+  const float2 cdw = make_float2(cd.w, cd.w);
+  if (DEPTH) dL = __ffma2_rn(__ffma2_rn(s.adr, neg1, cdw), s.gd, dL);
+  if (GA) dL = __ffma2_rn(one_minus2(s.aar), s.ga, dL);
+  dL = __fmul2_rn(dL, T);
+  if (has_bg) dL = __ffma2_rn(__fmul2_rn(s.nTf, inv), s.bg_dot, dL);
+  const float2 u = __fmul2_rn(make_float2(c0 ? G.x : 0.0f, c1 ? G.y : 0.0f), dL);
+  const float2 uy = __fmul2_rn(u, dy);
+  // state: transmittance behind the next Gaussian, accumulators advanced eagerly
+  s.T.x = c0 ? T.x : s.T.x;
+  s.T.y = c1 ? T.y : s.T.y;
+  s.S = __ffma2_rn(am, __ffma2_rn(s.S, neg1, cg), s.S);
+  if (DEPTH) s.adr = __ffma2_rn(am, __ffma2_rn(s.adr, neg1, cdw), s.adr);
+  if (GA) s.aar = __ffma2_rn(one_minus2(am), s.aar, am);
+  // the Gaussian's sums over the two pixels, accumulated as pixel 0 then pixel 1
+  m.U = u.x + u.y;
+  m.UY = uy.x + uy.y;
+  m.UYY = __fmaf_rn(uy.y, dy.y, __fmul_rn(uy.x, dy.x));
+  m.dcol0 = __fmaf_rn(dch.y, s.g0.y, __fmul_rn(dch.x, s.g0.x));
+  m.dcol1 = __fmaf_rn(dch.y, s.g1.y, __fmul_rn(dch.x, s.g1.x));
+  m.dcol2 = __fmaf_rn(dch.y, s.g2.y, __fmul_rn(dch.x, s.g2.x));
+  if (DEPTH) m.ddepth = __fmaf_rn(dch.y, s.gd.y, __fmul_rn(dch.x, s.gd.x));
 }
 
 // DEPTH: compute_depth with a depth gradient given; GA: an alpha gradient
@@ -463,29 +477,39 @@ __global__ void __launch_bounds__(THREADS, 8) render_bwd_kernel(const gsb_render
   const long long npix = (long long)a.W * a.H;
   const bool has_bg = a.background[0] != 0.0f || a.background[1] != 0.0f || a.background[2] != 0.0f;
 
-  BwdPixel px[2];
+  BwdPair px;
+  px.lc0 = px.lc1 = 0;
+  float Tf[2], g0[2], g1[2], g2[2], gd[2], ga[2];
 #pragma unroll
   for (int p = 0; p < 2; ++p) {
-    BwdPixel& s = px[p];
     const int py = py0 + 4 * p;
-    s.fy = (float)py;
-    s.lc = 0;
-    s.T_final = s.g0 = s.g1 = s.g2 = s.gd = s.ga = s.bg_dot = 0.0f;
+    int lc = 0;
+    Tf[p] = g0[p] = g1[p] = g2[p] = gd[p] = ga[p] = 0.0f;
     if (pxi < a.W && py < a.H && n > 0) {
       const long long pix = (long long)py * a.W + pxi;
-      s.lc = a.n_contrib[pix];
-      s.T_final = 1.0f - a.out_alpha[pix];
-      s.g0 = a.grad_color[pix];
-      s.g1 = a.grad_color[npix + pix];
-      s.g2 = a.grad_color[2 * npix + pix];
-      if (DEPTH) s.gd = a.grad_depth[pix];
-      if (GA) s.ga = a.grad_alpha[pix];
-      s.bg_dot = a.background[0] * s.g0 + a.background[1] * s.g1 + a.background[2] * s.g2;
+      lc = a.n_contrib[pix];
+      Tf[p] = 1.0f - a.out_alpha[pix];
+      g0[p] = a.grad_color[pix];
+      g1[p] = a.grad_color[npix + pix];
+      g2[p] = a.grad_color[2 * npix + pix];
+      if (DEPTH) gd[p] = a.grad_depth[pix];
+      if (GA) ga[p] = a.grad_alpha[pix];
     }
-    s.T = s.T_final;
-    s.S = s.lcg = s.adr = s.aar = s.la = s.ld = 0.0f;
+    if (p) px.lc1 = lc;
+    else px.lc0 = lc;
   }
-  const int warp_max = __reduce_max_sync(FULL, max(px[0].lc, px[1].lc));
+  px.nfy = make_float2(-(float)py0, -(float)(py0 + 4));
+  px.T = make_float2(Tf[0], Tf[1]);
+  px.nTf = make_float2(-Tf[0], -Tf[1]);
+  px.g0 = make_float2(g0[0], g0[1]);
+  px.g1 = make_float2(g1[0], g1[1]);
+  px.g2 = make_float2(g2[0], g2[1]);
+  px.gd = make_float2(gd[0], gd[1]);
+  px.ga = make_float2(ga[0], ga[1]);
+  px.bg_dot = make_float2(a.background[0] * g0[0] + a.background[1] * g1[0] + a.background[2] * g2[0],
+                          a.background[0] * g0[1] + a.background[1] * g1[1] + a.background[2] * g2[1]);
+  px.S = px.adr = px.aar = make_float2(0.0f, 0.0f);
+  const int warp_max = __reduce_max_sync(FULL, max(px.lc0, px.lc1));
   if (lane == 0) s_max[warp] = warp_max;
   __syncthreads();
   int cta_max = 0;
@@ -551,8 +575,8 @@ __global__ void __launch_bounds__(THREADS, 8) render_bwd_kernel(const gsb_render
       bool contrib = false;
       float dx = 0.0f;
       // a half the Gaussian cannot reach has alpha < 1/255 at every pixel: no state change to skip
-      const bool e0 = ((top_h >> bit) & 1u) && pos < px[0].lc;
-      const bool e1 = ((bot_h >> bit) & 1u) && pos < px[1].lc;
+      const bool e0 = ((top_h >> bit) & 1u) && pos < px.lc0;
+      const bool e1 = ((bot_h >> bit) & 1u) && pos < px.lc1;
       if (e0 || e1) {
         const float2 xy = s_xy[j];
         const float4 cf = s_cf[j];
@@ -560,8 +584,8 @@ __global__ void __launch_bounds__(THREADS, 8) render_bwd_kernel(const gsb_render
         dx = xy.x - fx;
         float ax, bx;
         column_terms(cf, dx, ax, bx);
-        const bool c0 = bwd_pixel<DEPTH, GA>(px[0], e0, cf, ax, bx, xy.y, cd, has_bg, m);
-        const bool c1 = bwd_pixel<DEPTH, GA>(px[1], e1, cf, ax, bx, xy.y, cd, has_bg, m);
+        bool c0, c1;
+        bwd_pair<DEPTH, GA>(px, e0, e1, cf, ax, bx, xy.y, cd, has_bg, m, c0, c1);
         contrib = c0 || c1;
       }
       if (__any_sync(FULL, contrib)) {
