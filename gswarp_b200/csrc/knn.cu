@@ -369,22 +369,11 @@ __global__ void __launch_bounds__(256, 4) search_kernel(int P, int nl, int np, i
   // second walk skips exactly the leaves the first one visited.
   const int own_par = qleaf / 32, own_gp = own_par / 32;
   for (int pass = 0; pass < 2; ++pass) {
-    // grandparent distances to the query AABB, 32 at a time (lane k holds
-    // grandparent 32*chunk + k), taken by shuffle in the visiting order
-    int chunk = -1;
-    float dg = 0.0f;
-    for (int gi = 0; gi < ng; ++gi) {
-      const int g = gi == 0 ? own_gp : (gi <= own_gp ? gi - 1 : gi);
-      if ((g >> 5) != chunk) {
-        chunk = g >> 5;
-        const int t = chunk * 32 + lane;
-        float tb[6];
-#pragma unroll
-        for (int k = 0; k < 6; ++k) tb[k] = t < ng ? gp_b[(size_t)t * 6 + k] : 0.0f;
-        dg = boxbox_dist(qb, tb);
-      }
+    // Grandparent g at box-box distance dgg from the query AABB: its parents,
+    // then their leaves, that the pass's bound admits.
+    auto visit_gp = [&](int g, float dgg) {
       float mb2 = pass == 0 ? 0.0f : warp_max(valid ? b2 : 0.0f);
-      if (__shfl_sync(0xffffffffu, dg, g & 31) > mb2) continue;
+      if (dgg > mb2) return;
       const int pidx = g * 32 + lane;
       float pbx[6];
 #pragma unroll
@@ -425,6 +414,30 @@ __global__ void __launch_bounds__(256, 4) search_kernel(int P, int nl, int np, i
           for (int k = 0; k < 6; ++k) cb[k] = __shfl_sync(0xffffffffu, lb[k], j);
           visit_leaf(L, cb, P, valid, px, py, pz, sx, sy, sz, s_pts, b0, b1, b2);
         }
+      }
+    };
+    // the query's own grandparent first, then the others in index order:
+    // 32 grandparent distances per load (lane k holds grandparent 32c + k),
+    // a ballot of those the bound admits at the chunk's start (a superset:
+    // bounds only shrink, and visit_gp re-tests with the current one)
+    {
+      float tb[6];
+#pragma unroll
+      for (int k = 0; k < 6; ++k) tb[k] = gp_b[(size_t)own_gp * 6 + k];
+      visit_gp(own_gp, boxbox_dist(qb, tb));
+    }
+    for (int c = 0; c * 32 < ng; ++c) {
+      const int t = c * 32 + lane;
+      float tb[6];
+#pragma unroll
+      for (int k = 0; k < 6; ++k) tb[k] = t < ng ? gp_b[(size_t)t * 6 + k] : 0.0f;
+      const float dg = boxbox_dist(qb, tb);
+      const float mb2c = pass == 0 ? 0.0f : warp_max(valid ? b2 : 0.0f);
+      unsigned gmask = __ballot_sync(0xffffffffu, t < ng && t != own_gp && dg <= mb2c);
+      while (gmask) {
+        const int bit = __ffs(gmask) - 1;
+        gmask &= gmask - 1;
+        visit_gp(c * 32 + bit, __shfl_sync(0xffffffffu, dg, bit));
       }
     }
   }
