@@ -53,9 +53,8 @@ __constant__ float GW[11] = {0.001028380123898387f, 0.0075987582094967365f,
 template <bool WITH_L1>
 __global__ void __launch_bounds__(THREADS) ssim_fwd_kernel(const gsb_ssim_fwd_args a, int tiles_x,
                                                            int tiles_y) {
-  __shared__ float s_x[RY][RX + 1];
-  __shared__ float s_y[RY][RX + 1];
-  __shared__ float s_h[4][RY][TX + 1];
+  __shared__ float2 s_p[RY][RX + 1];      // (img1, img2)
+  __shared__ float2 s_h[2][RY][TX + 1];   // horizontal sums: (x, y) and (x^2 + y^2, x y)
   __shared__ float s_red[THREADS / 32];
   __shared__ float s_red_l1[THREADS / 32];
   const int H = a.H, W = a.W;
@@ -86,45 +85,37 @@ __global__ void __launch_bounds__(THREADS) ssim_fwd_kernel(const gsb_ssim_fwd_ar
 #pragma unroll
     for (int it = 0; it < STAGE_ITERS; ++it) {
       const int i = threadIdx.x + it * THREADS;
-      if (i < RY * RX) {
-        s_x[i / RX][i % RX] = v1[it];
-        s_y[i / RX][i % RX] = v2[it];
-      }
+      if (i < RY * RX) s_p[i / RX][i % RX] = make_float2(v1[it], v2[it]);
     }
   }
   __syncthreads();
   // Horizontal pass (fused_ssim.py:477-511): symmetric tap pairs, then centre.
+  // The four filtered quantities go as two packed f32x2 pairs, (x, y) and
+  // (x^2 + y^2, x y): the same taps and weights, per component the same
+  // round-to-nearest results as four scalar chains.  Consecutive lanes take
+  // consecutive rows (odd row stride: conflict-free 8-byte accesses).
   if (threadIdx.x < H_ITEMS) {
-    const int r = threadIdx.x / HSEG, c0 = (threadIdx.x % HSEG) * RH;
+    const int r = threadIdx.x % RY, c0 = (threadIdx.x / RY) * RH;
     // x^2 + y^2 and x*y once per window value (each is used by up to 11 outputs)
-    float xv[RH + 10], yv[RH + 10], sq[RH + 10], xy[RH + 10];
+    float2 p[RH + 10], sq[RH + 10];
 #pragma unroll
     for (int q = 0; q < RH + 10; ++q) {
-      xv[q] = s_x[r][c0 + q];
-      yv[q] = s_y[r][c0 + q];
-      sq[q] = xv[q] * xv[q] + yv[q] * yv[q];
-      xy[q] = xv[q] * yv[q];
+      p[q] = s_p[r][c0 + q];
+      sq[q] = make_float2(p[q].x * p[q].x + p[q].y * p[q].y, p[q].x * p[q].y);
     }
 #pragma unroll
     for (int j = 0; j < RH; ++j) {
-      float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+      float2 a01 = make_float2(0.0f, 0.0f), a23 = a01;
 #pragma unroll
       for (int k = 0; k < 5; ++k) {
-        const float g = GW[k];
+        const float2 g = make_float2(GW[k], GW[k]);
         const int l = j + k, rr = j + 10 - k;
-        a0 += g * (xv[l] + xv[rr]);
-        a1 += g * (yv[l] + yv[rr]);
-        a2 += g * (sq[l] + sq[rr]);
-        a3 += g * (xy[l] + xy[rr]);
+        a01 = __ffma2_rn(g, __fadd2_rn(p[l], p[rr]), a01);
+        a23 = __ffma2_rn(g, __fadd2_rn(sq[l], sq[rr]), a23);
       }
-      a0 += GW[5] * xv[j + 5];
-      a1 += GW[5] * yv[j + 5];
-      a2 += GW[5] * sq[j + 5];
-      a3 += GW[5] * xy[j + 5];
-      s_h[0][r][c0 + j] = a0;
-      s_h[1][r][c0 + j] = a1;
-      s_h[2][r][c0 + j] = a2;
-      s_h[3][r][c0 + j] = a3;
+      const float2 g5 = make_float2(GW[5], GW[5]);
+      s_h[0][r][c0 + j] = __ffma2_rn(g5, p[j + 5], a01);
+      s_h[1][r][c0 + j] = __ffma2_rn(g5, sq[j + 5], a23);
     }
   }
   __syncthreads();
@@ -132,26 +123,27 @@ __global__ void __launch_bounds__(THREADS) ssim_fwd_kernel(const gsb_ssim_fwd_ar
   const int c = threadIdx.x % TX, r0 = (threadIdx.x / TX) * RV;
   float s4[RV][4];
 #pragma unroll
-  for (int m = 0; m < 4; ++m) {
-    float w[RV + 10];
+  for (int m = 0; m < 2; ++m) {
+    float2 w[RV + 10];
 #pragma unroll
     for (int q = 0; q < RV + 10; ++q) w[q] = s_h[m][r0 + q][c];
 #pragma unroll
     for (int j = 0; j < RV; ++j) {
-      float acc = 0.0f;
+      float2 acc = make_float2(0.0f, 0.0f);
 #pragma unroll
       for (int k = 0; k < 5; ++k) {
-        const float g = GW[k];
-        const float top = w[j + k], bot = w[j + 10 - k];
+        const float2 g = make_float2(GW[k], GW[k]);
+        const float2 top = w[j + k], bot = w[j + 10 - k];
         if (a.valid) {
-          acc += g * (top + bot);
+          acc = __ffma2_rn(g, __fadd2_rn(top, bot), acc);
         } else {
-          acc += g * top;
-          acc += g * bot;
+          acc = __ffma2_rn(g, top, acc);
+          acc = __ffma2_rn(g, bot, acc);
         }
       }
-      acc += GW[5] * w[j + 5];
-      s4[j][m] = acc;
+      acc = __ffma2_rn(make_float2(GW[5], GW[5]), w[j + 5], acc);
+      s4[j][2 * m] = acc.x;
+      s4[j][2 * m + 1] = acc.y;
     }
   }
   float local_sum = 0.0f, local_l1 = 0.0f;
@@ -171,7 +163,10 @@ __global__ void __launch_bounds__(THREADS) ssim_fwd_kernel(const gsb_ssim_fwd_ar
     const float rA = 1.0f / Av, rB = 1.0f / Bv, rAB = rA * rB;
     const float m = Cv * Dv * rAB;
     local_sum += m;
-    if (WITH_L1) local_l1 += fabsf(s_x[r0 + j + HALO][c + HALO] - s_y[r0 + j + HALO][c + HALO]);
+    if (WITH_L1) {
+      const float2 v = s_p[r0 + j + HALO][c + HALO];
+      local_l1 += fabsf(v.x - v.y);
+    }
     if (a.dm) {
       const size_t o = pbase + (size_t)gy * W + gxp;
       a.dm[o] = 2.0f * (mu2 * (Dv - Cv) * rAB + mu1 * m * (rB - rA));
@@ -224,8 +219,11 @@ template <bool WITH_L1>
 __global__ void __launch_bounds__(THREADS) ssim_bwd_kernel(const gsb_ssim_bwd_args a, int tiles_x,
                                                            int tiles_y, float inv_n, float upstream_host,
                                                            float l1_scale) {
-  __shared__ float s_dm[3][RY][RX + 1];
-  __shared__ float s_t[3][RY][TX + 1];
+  // maps 0 and 1 as packed f32x2 pairs, map 2 alone
+  __shared__ float2 s_dm01[RY][RX + 1];
+  __shared__ float s_dm2[RY][RX + 1];
+  __shared__ float2 s_t01[RY][TX + 1];
+  __shared__ float s_t2[RY][TX + 1];
   const int H = a.H, W = a.W;
   const int tile = blockIdx.x;
   const int tx = tile % tiles_x;
@@ -255,20 +253,41 @@ __global__ void __launch_bounds__(THREADS) ssim_bwd_kernel(const gsb_ssim_bwd_ar
 #pragma unroll
     for (int it = 0; it < STAGE_ITERS; ++it) {
       const int i = threadIdx.x + it * THREADS;
-      if (i < RY * RX)
-#pragma unroll
-        for (int m = 0; m < 3; ++m) s_dm[m][i / RX][i % RX] = d[m][it];
+      if (i < RY * RX) {
+        s_dm01[i / RX][i % RX] = make_float2(d[0][it], d[1][it]);
+        s_dm2[i / RX][i % RX] = d[2][it];
+      }
     }
   }
   __syncthreads();
-  // Horizontal pass of dm * (upstream / N) (fused_ssim.py:844-868), one map at a time.
+  // Horizontal pass of dm * (upstream / N) (fused_ssim.py:844-868): maps 0
+  // and 1 as one packed f32x2 chain (per component the scalar chain's
+  // round-to-nearest results), then map 2.  Consecutive lanes take
+  // consecutive rows.
   if (threadIdx.x < H_ITEMS) {
-    const int r = threadIdx.x / HSEG, c0 = (threadIdx.x % HSEG) * RH;
+    const int r = threadIdx.x % RY, c0 = (threadIdx.x / RY) * RH;
+    {
+      float2 dv[RH + 10];
 #pragma unroll
-    for (int m = 0; m < 3; ++m) {
+      for (int q = 0; q < RH + 10; ++q) dv[q] = s_dm01[r][c0 + q];
+#pragma unroll
+      for (int j = 0; j < RH; ++j) {
+        float2 t = make_float2(0.0f, 0.0f);
+#pragma unroll
+        for (int k = 0; k < 5; ++k) {
+          const float gs = GW[k] * scale;
+          const float2 g = make_float2(gs, gs);
+          t = __ffma2_rn(g, dv[j + k], t);
+          t = __ffma2_rn(g, dv[j + 10 - k], t);
+        }
+        const float g5 = GW[5] * scale;
+        s_t01[r][c0 + j] = __ffma2_rn(make_float2(g5, g5), dv[j + 5], t);
+      }
+    }
+    {
       float dv[RH + 10];
 #pragma unroll
-      for (int q = 0; q < RH + 10; ++q) dv[q] = s_dm[m][r][c0 + q];
+      for (int q = 0; q < RH + 10; ++q) dv[q] = s_dm2[r][c0 + q];
 #pragma unroll
       for (int j = 0; j < RH; ++j) {
         float t = 0.0f;
@@ -279,18 +298,35 @@ __global__ void __launch_bounds__(THREADS) ssim_bwd_kernel(const gsb_ssim_bwd_ar
           t += gs * dv[j + 10 - k];
         }
         t += GW[5] * scale * dv[j + 5];
-        s_t[m][r][c0 + j] = t;
+        s_t2[r][c0 + j] = t;
       }
     }
   }
   __syncthreads();
   const int c = threadIdx.x % TX, r0 = (threadIdx.x / TX) * RV;
   float acc3[RV][3];
+  {
+    float2 w[RV + 10];
 #pragma unroll
-  for (int m = 0; m < 3; ++m) {
+    for (int q = 0; q < RV + 10; ++q) w[q] = s_t01[r0 + q][c];
+#pragma unroll
+    for (int j = 0; j < RV; ++j) {
+      float2 acc = make_float2(0.0f, 0.0f);
+#pragma unroll
+      for (int k = 0; k < 5; ++k) {
+        const float2 g = make_float2(GW[k], GW[k]);
+        acc = __ffma2_rn(g, w[j + k], acc);
+        acc = __ffma2_rn(g, w[j + 10 - k], acc);
+      }
+      acc = __ffma2_rn(make_float2(GW[5], GW[5]), w[j + 5], acc);
+      acc3[j][0] = acc.x;
+      acc3[j][1] = acc.y;
+    }
+  }
+  {
     float w[RV + 10];
 #pragma unroll
-    for (int q = 0; q < RV + 10; ++q) w[q] = s_t[m][r0 + q][c];
+    for (int q = 0; q < RV + 10; ++q) w[q] = s_t2[r0 + q][c];
 #pragma unroll
     for (int j = 0; j < RV; ++j) {
       float acc = 0.0f;
@@ -301,7 +337,7 @@ __global__ void __launch_bounds__(THREADS) ssim_bwd_kernel(const gsb_ssim_bwd_ar
         acc += g * w[j + 10 - k];
       }
       acc += GW[5] * w[j + 5];
-      acc3[j][m] = acc;
+      acc3[j][2] = acc;
     }
   }
   const int gxp = x0 + c;

@@ -65,7 +65,7 @@ def test_fused_ssim_inference_mode(cuda):
     assert abs(float(l) - ref) <= 2e-6
 
 
-@pytest.mark.parametrize("n", [4, 5, 1023, 1024, 1025, 50_000])
+@pytest.mark.parametrize("n", [4, 5, 33, 64, 65, 96, 1023, 1024, 1025, 50_000])
 def test_knn_bit_exact(cuda, n):
     pts = wl.config4_points(seed=n, n=max(n, 4))[:n].contiguous()
     got = gs.distCUDA2(pts.to(cuda)).cpu().numpy()
@@ -81,6 +81,24 @@ def test_knn_degenerate_and_duplicates(cuda):
     dup = torch.cat([flat, flat[:100]])
     for pts in (flat, dup):
         got = gs.distCUDA2(pts.to(cuda)).cpu().numpy()
+        want, _ = oracle.knn(pts.numpy())
+        np.testing.assert_array_equal(got, want)
+
+
+def test_knn_ties_and_sparse_outliers(cuda):
+    """Exact distance ties (an integer grid: every interior point has six
+    neighbours at distance 1) and a dense cluster with a few far outliers
+    (query leaves whose bounds stay large, so candidate leaves are needed by
+    only a few lanes): bit-exact against brute force."""
+    g = torch.arange(15, dtype=torch.float32)
+    grid = torch.stack(torch.meshgrid(g, g, g, indexing="ij"), -1).reshape(-1, 3)
+    gen = torch.Generator().manual_seed(7)
+    cluster = torch.randn(3000, 3, generator=gen) * 0.05
+    outliers = (torch.rand(24, 3, generator=gen) * 2.0 - 1.0) * 50.0
+    mixed = torch.cat([cluster, outliers])[torch.randperm(3024, generator=gen)].contiguous()
+    for pts in (grid, mixed):
+        got = gs.distCUDA2(pts.to(cuda)).cpu().numpy()
+        np.testing.assert_array_equal(got, oracle.knn_bruteforce(pts.numpy()))
         want, _ = oracle.knn(pts.numpy())
         np.testing.assert_array_equal(got, want)
 
