@@ -94,6 +94,24 @@ def photometric_loss_backward(img: torch.Tensor, target: torch.Tensor, dm: torch
     return g
 
 
+def reduction_plan(P: int, means_numel: int, sh_numel: int, total: int, chunks: int):
+    """Issue order of the multi-view step's all-reduces over the flat gradient
+    buffer ``[means | scales | rotations | opacities | SH]`` (``total``
+    floats): first the block complete after the last view (scales,
+    rotations, opacities), then one SH slice per Gaussian range ``[b, e)`` of
+    the SH backward, then the means (to which the SH backward adds).  Returns
+    ``(first, [((b, e), (lo, hi)), ...], last)`` with slices as ``(lo, hi)``;
+    together they cover ``[0, total)`` once."""
+    sh_off = total - sh_numel
+    row = sh_numel // max(P, 1)
+    n = max(1, min(chunks, P))
+    ranges = []
+    for c in range(n):
+        b, e = P * c // n, P * (c + 1) // n
+        ranges.append(((b, e), (sh_off + b * row, sh_off + e * row)))
+    return (means_numel, sh_off), ranges, (0, means_numel)
+
+
 def _distributed(group) -> bool:
     return (torch.distributed.is_available() and torch.distributed.is_initialized()
             and torch.distributed.get_world_size(group) > 1)
@@ -318,25 +336,22 @@ class FusedViewStep:
         return self.losses
 
     def _sh_backward_and_reduce(self, means: torch.Tensor, sh: torch.Tensor) -> None:
-        """SH backward in ranges of Gaussians, each range's SH gradient
-        all-reduced (on NCCL's stream) while the next range is computed; the
-        rest of the buffer (means, scales, rotations, opacities: complete
-        after the last view, except the means' direction term, which the SH
-        backward adds) goes last.  The sums are elementwise, so the result
-        equals one all-reduce of the whole buffer."""
+        """All-reduces (on NCCL's stream) while the SH backward runs: first the
+        scales, rotations and opacities (complete after the last view), then
+        the SH gradient range by range, each while the next range is
+        computed, and the means last (the SH backward adds their
+        view-direction term).  The sums are elementwise, so the result equals
+        one all-reduce of the whole buffer."""
         P = means.shape[0]
         flat = self.grads.flat
-        sh_off = flat.numel() - sh.numel()
-        row = sh.numel() // max(P, 1)
-        chunks = max(1, min(self.reduce_chunks, P))
-        works = []
-        for c in range(chunks):
-            b, e = P * c // chunks, P * (c + 1) // chunks
+        first, ranges, last = reduction_plan(P, self.grads.views[0].numel(), sh.numel(), flat.numel(),
+                                             self.reduce_chunks)
+        works = [torch.distributed.all_reduce(flat[first[0]:first[1]], group=self.group, async_op=True)]
+        for (b, e), (lo, hi) in ranges:
             pl.sh_backward_views(means, sh, self._sh_degree, self._campos, self._grad_colors, self.grads.views[4],
                                  self.grads.views[0], begin=b, end=e)
-            if e > b:
-                works.append(torch.distributed.all_reduce(flat[sh_off + b * row: sh_off + e * row], group=self.group,
-                                                          async_op=True))
-        works.append(torch.distributed.all_reduce(flat[:sh_off], group=self.group, async_op=True))
+            if hi > lo:
+                works.append(torch.distributed.all_reduce(flat[lo:hi], group=self.group, async_op=True))
+        works.append(torch.distributed.all_reduce(flat[last[0]:last[1]], group=self.group, async_op=True))
         for w in works:
             w.wait()
