@@ -1,9 +1,9 @@
 """Two-GPU training step (needs at least two GPUs; skipped otherwise).
 
 Two NCCL ranks, each rendering its own views of the same scene.  The
-multi-view-SH step reduces the SH gradient in Gaussian ranges, each
-all-reduced while the next range's SH backward runs, and the rest of the
-buffer last; the result must equal (up to the render backward's atomic
+multi-view-SH step all-reduces the scales, rotations and opacities first,
+then the SH gradient in Gaussian ranges, each while the next range's SH
+backward runs, and the means last; the result must equal (up to the render backward's atomic
 summation order) the per-view-SH step's single all-reduce of the whole
 buffer, and the sum of the ranks' local gradients."""
 
