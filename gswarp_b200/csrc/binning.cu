@@ -288,7 +288,7 @@ __device__ __forceinline__ int record_tile(const unsigned* w, int idx, int gx) {
 
 constexpr int EMIT_THREADS = 256;
 
-__global__ void __launch_bounds__(EMIT_THREADS) emit_binrec_kernel(
+__global__ void __launch_bounds__(EMIT_THREADS, 8) emit_binrec_kernel(
     const long long* __restrict__ n_dev, int gx, int mode, const int* __restrict__ order,
     const int* __restrict__ offsets, const uint4* __restrict__ bin_records, const float4* __restrict__ records,
     unsigned* __restrict__ keys, unsigned* __restrict__ vals, long long* __restrict__ err) {
