@@ -180,8 +180,10 @@ __global__ void __launch_bounds__(THREADS, 10) render_fwd_kernel(const gsb_rende
   const float bx1 = bx0 + 7.0f, by1 = by0 + 7.0f;
   // The thread's two pixels (same column, rows py0 and py0 + 4) share every
   // Gaussian operand, so their arithmetic runs as packed f32x2 operations
-  // (__ffma2_rn / __fmul2_rn / __fadd2_rn: per component the same IEEE
-  // round-to-nearest results as the scalar __fmaf_rn / __fmul_rn / __fadd_rn).
+  // (__ffma2_rn / __fmul2_rn / __fadd2_rn: each rounds per component like
+  // the scalar __fmaf_rn / __fmul_rn / __fadd_rn; as with scalar code in this
+  // unit, the compiler may contract a packed multiply feeding a packed add
+  // into one fused operation, so results match a scalar build to rounding).
   float fy[2];
   float2 T = make_float2(1.0f, 1.0f), c0 = make_float2(0.0f, 0.0f), c1 = c0, c2 = c0, wsum = c0, dacc = c0;
   int last[2] = {0, 0}, nsucc[2] = {0, 0};

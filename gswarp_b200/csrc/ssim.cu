@@ -91,8 +91,8 @@ __global__ void __launch_bounds__(THREADS) ssim_fwd_kernel(const gsb_ssim_fwd_ar
   __syncthreads();
   // Horizontal pass (fused_ssim.py:477-511): symmetric tap pairs, then centre.
   // The four filtered quantities go as two packed f32x2 pairs, (x, y) and
-  // (x^2 + y^2, x y): the same taps and weights, per component the same
-  // round-to-nearest results as four scalar chains.  Consecutive lanes take
+  // (x^2 + y^2, x y): per component the same taps, weights and fused
+  // multiply-adds as four scalar chains.  Consecutive lanes take
   // consecutive rows (odd row stride: conflict-free 8-byte accesses).
   if (threadIdx.x < H_ITEMS) {
     const int r = threadIdx.x % RY, c0 = (threadIdx.x / RY) * RH;
@@ -262,7 +262,7 @@ __global__ void __launch_bounds__(THREADS) ssim_bwd_kernel(const gsb_ssim_bwd_ar
   __syncthreads();
   // Horizontal pass of dm * (upstream / N) (fused_ssim.py:844-868): maps 0
   // and 1 as one packed f32x2 chain (per component the scalar chain's
-  // round-to-nearest results), then map 2.  Consecutive lanes take
+  // fused multiply-adds), then map 2.  Consecutive lanes take
   // consecutive rows.
   if (threadIdx.x < H_ITEMS) {
     const int r = threadIdx.x % RY, c0 = (threadIdx.x / RY) * RH;
