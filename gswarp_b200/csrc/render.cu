@@ -412,7 +412,7 @@ struct BwdSums {
 // arithmetic runs straight through as one packed stream (both pixels share
 // the Gaussian's operands); the per-pixel decisions only mask alpha and G.
 // For a contributing pixel every value is the same expression as a scalar
-// evaluation of that pixel.
+// evaluation of that pixel (up to which multiply-adds the compiler fuses).
 template <bool DEPTH, bool GA>
 __device__ __forceinline__ void bwd_pair(BwdPair& s, bool e0, bool e1, const float4 cf, float ax, float bx,
                                          float y, const float4 cd, bool has_bg, BwdSums& m, bool& c0, bool& c1) {
