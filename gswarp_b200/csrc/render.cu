@@ -181,9 +181,8 @@ __global__ void __launch_bounds__(THREADS, 10) render_fwd_kernel(const gsb_rende
   // The thread's two pixels (same column, rows py0 and py0 + 4) share every
   // Gaussian operand, so their arithmetic runs as packed f32x2 operations
   // (__ffma2_rn / __fmul2_rn / __fadd2_rn: each rounds per component like
-  // the scalar __fmaf_rn / __fmul_rn / __fadd_rn; as with scalar code in this
-  // unit, the compiler may contract a packed multiply feeding a packed add
-  // into one fused operation, so results match a scalar build to rounding).
+  // the scalar __fmaf_rn / __fmul_rn / __fadd_rn; composed packed expressions
+  // are not guaranteed to match a scalar build bit for bit, only to rounding).
   float fy[2];
   float2 T = make_float2(1.0f, 1.0f), c0 = make_float2(0.0f, 0.0f), c1 = c0, c2 = c0, wsum = c0, dacc = c0;
   int last[2] = {0, 0}, nsucc[2] = {0, 0};
@@ -412,7 +411,7 @@ struct BwdSums {
 // arithmetic runs straight through as one packed stream (both pixels share
 // the Gaussian's operands); the per-pixel decisions only mask alpha and G.
 // For a contributing pixel every value is the same expression as a scalar
-// evaluation of that pixel (up to which multiply-adds the compiler fuses).
+// evaluation of that pixel, to rounding.
 template <bool DEPTH, bool GA>
 __device__ __forceinline__ void bwd_pair(BwdPair& s, bool e0, bool e1, const float4 cf, float ax, float bx,
                                          float y, const float4 cd, bool has_bg, BwdSums& m, bool& c0, bool& c1) {
