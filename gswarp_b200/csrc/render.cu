@@ -181,8 +181,9 @@ __global__ void __launch_bounds__(THREADS, 10) render_fwd_kernel(const gsb_rende
   // The thread's two pixels (same column, rows py0 and py0 + 4) share every
   // Gaussian operand, so their arithmetic runs as packed f32x2 operations
   // (__ffma2_rn / __fmul2_rn / __fadd2_rn: each rounds per component like
-  // the scalar __fmaf_rn / __fmul_rn / __fadd_rn; composed packed expressions
-  // are not guaranteed to match a scalar build bit for bit, only to rounding).
+  // the scalar __fmaf_rn / __fmul_rn / __fadd_rn, but the compiler may fuse
+  // a packed multiply into the add it feeds, so composed expressions match a
+  // scalar build to rounding, not bit for bit).
   float fy[2];
   float2 T = make_float2(1.0f, 1.0f), c0 = make_float2(0.0f, 0.0f), c1 = c0, c2 = c0, wsum = c0, dacc = c0;
   int last[2] = {0, 0}, nsucc[2] = {0, 0};
