@@ -1,104 +1,33 @@
-"""Tile-coverage contract (mirrors gswarp/_internal/coverage.py:1-151).
+"""Tile-coverage policy of the rasterizer.
 
-A method declares its footprint semantics; ``resolve_tile_coverage_mode``
-maps the public policy ("auto", "snugbox", "accutile_sweep", "conic_rect")
-to one concrete kernel mode.  Baseline 3DGS declares the CUDA-compatible
-screen-conic contract, so "auto" resolves to AccuTile (kernel mode id 1).
+The public policy names are those of gswarp's ``set_tile_coverage_mode``:
+"auto", "snugbox", "accutile_sweep" and "conic_rect".  The kernels take an
+integer mode (``GSB_COVERAGE_*`` in include/gsb200.h): 0 SnugBox, 1 AccuTile
+band sweep, 2 per-tile conic/rectangle test.  This package serves one method,
+baseline 3DGS, whose screen-space conic footprint admits every exact mode;
+for it gswarp resolves "auto" to the AccuTile sweep
+(gswarp/_internal/coverage.py:94-110), and so does ``kernel_mode``.
 """
 
 from __future__ import annotations
 
-from dataclasses import dataclass
-
-TILE_COVERAGE_MODES = ("auto", "snugbox", "accutile_sweep", "conic_rect")
-CONCRETE_TILE_COVERAGE_MODES = ("snugbox", "accutile_sweep", "conic_rect")
-
-FOOTPRINT_SCREEN_CONIC = "screen_conic"
-FOOTPRINT_AXIS_ALIGNED = "axis_aligned"
-FOOTPRINT_RAY_SPLAT = "ray_splat"
-FOOTPRINT_CUSTOM = "custom"
-FOOTPRINTS = (FOOTPRINT_SCREEN_CONIC, FOOTPRINT_AXIS_ALIGNED, FOOTPRINT_RAY_SPLAT, FOOTPRINT_CUSTOM)
-
-SUPPORT_CUDA_3SIGMA_CLAMPED = "cuda_3sigma_clamped"
-SUPPORT_ALPHA_CUTOFF = "alpha_cutoff"
-SUPPORT_CUSTOM = "custom"
-SUPPORT_POLICIES = (SUPPORT_CUDA_3SIGMA_CLAMPED, SUPPORT_ALPHA_CUTOFF, SUPPORT_CUSTOM)
-
-SAMPLE_PIXEL_CENTERS = "pixel_centers"
-SAMPLE_CONTINUOUS = "continuous"
-SAMPLE_CUSTOM = "custom"
-SAMPLE_DOMAINS = (SAMPLE_PIXEL_CENTERS, SAMPLE_CONTINUOUS, SAMPLE_CUSTOM)
-
-EXACT_POLICY_CUDA_COMPAT_CONIC = "cuda_compat_screen_conic"
-
-_MODE_IDS = {"snugbox": 0, "accutile_sweep": 1, "conic_rect": 2}
+KERNEL_MODE = {"snugbox": 0, "accutile_sweep": 1, "conic_rect": 2}
+AUTO = "accutile_sweep"
+POLICIES = ("auto", *KERNEL_MODE)
 
 
-@dataclass(frozen=True, slots=True)
-class CoverageContract:
-    footprint: str
-    support: str
-    sample_domain: str
-    exact_policy: str | None = None
-
-    def __post_init__(self) -> None:
-        if self.footprint not in FOOTPRINTS:
-            raise ValueError(f"unknown coverage footprint: {self.footprint!r}")
-        if self.support not in SUPPORT_POLICIES:
-            raise ValueError(f"unknown coverage support policy: {self.support!r}")
-        if self.sample_domain not in SAMPLE_DOMAINS:
-            raise ValueError(f"unknown coverage sample domain: {self.sample_domain!r}")
-        if self.exact_policy not in (None, EXACT_POLICY_CUDA_COMPAT_CONIC):
-            raise ValueError(f"unknown exact coverage policy: {self.exact_policy!r}")
-        if self.exact_policy == EXACT_POLICY_CUDA_COMPAT_CONIC and (
-            self.footprint != FOOTPRINT_SCREEN_CONIC
-            or self.support != SUPPORT_CUDA_3SIGMA_CLAMPED
-            or self.sample_domain != SAMPLE_PIXEL_CENTERS
-        ):
-            raise ValueError(
-                "cuda-compatible exact coverage requires a screen conic, "
-                "CUDA 3-sigma support, and pixel-center sampling"
-            )
+def check_policy(policy: str) -> str:
+    """``policy`` if it is a public policy name, else gswarp's ValueError."""
+    if policy not in POLICIES:
+        raise ValueError("mode must be one of " + ", ".join(repr(p) for p in POLICIES))
+    return policy
 
 
-BASELINE_3DGS_COVERAGE = CoverageContract(
-    footprint=FOOTPRINT_SCREEN_CONIC,
-    support=SUPPORT_CUDA_3SIGMA_CLAMPED,
-    sample_domain=SAMPLE_PIXEL_CENTERS,
-    exact_policy=EXACT_POLICY_CUDA_COMPAT_CONIC,
-)
-CONSERVATIVE_COVERAGE = CoverageContract(
-    footprint=FOOTPRINT_CUSTOM, support=SUPPORT_CUSTOM, sample_domain=SAMPLE_CUSTOM
-)
+def concrete(policy: str) -> str:
+    """The mode a policy runs as ("auto" -> "accutile_sweep")."""
+    return AUTO if check_policy(policy) == "auto" else policy
 
 
-def normalize_tile_coverage_mode(mode: str) -> str:
-    if mode not in TILE_COVERAGE_MODES:
-        choices = ", ".join(repr(v) for v in TILE_COVERAGE_MODES)
-        raise ValueError(f"mode must be one of {choices}")
-    return mode
-
-
-def resolve_tile_coverage_mode(mode: str, contract: CoverageContract) -> str:
-    mode = normalize_tile_coverage_mode(mode)
-    if contract.exact_policy == EXACT_POLICY_CUDA_COMPAT_CONIC:
-        return "accutile_sweep" if mode == "auto" else mode
-    if mode == "auto":
-        return "snugbox"
-    if mode != "snugbox":
-        raise ValueError(
-            f"tile coverage mode {mode!r} requires exact policy "
-            f"{EXACT_POLICY_CUDA_COMPAT_CONIC!r}; method declares {contract!r}"
-        )
-    return mode
-
-
-def tile_coverage_mode_id(mode: str) -> int:
-    mode = normalize_tile_coverage_mode(mode)
-    if mode == "auto":
-        raise ValueError("auto tile coverage must be resolved before kernel dispatch")
-    return _MODE_IDS[mode]
-
-
-def resolve_tile_coverage_mode_id(mode: str, contract: CoverageContract) -> int:
-    return tile_coverage_mode_id(resolve_tile_coverage_mode(mode, contract))
+def kernel_mode(policy: str) -> int:
+    """The kernels' integer mode for a public policy."""
+    return KERNEL_MODE[concrete(policy)]

@@ -16,7 +16,7 @@ from dataclasses import dataclass
 import torch
 
 from . import _lib
-from ._coverage import BASELINE_3DGS_COVERAGE, resolve_tile_coverage_mode_id
+from . import _coverage
 from ._runtime import BLOCK_X, BLOCK_Y, ExecutionOptions
 
 NUM_CHANNELS = 3
@@ -58,6 +58,24 @@ def sticky_error_word(device: torch.device) -> torch.Tensor:
         t = torch.zeros(1, dtype=torch.int64, device=device)
         _STICKY[idx] = t
     return t
+
+
+def _device_error(bits: int) -> RuntimeError:
+    return RuntimeError(f"gswarp_b200 device error word {int(bits):#x} "
+                        "(bounded wait timed out or binning mismatch)")
+
+
+def raise_device_errors(device: torch.device) -> None:
+    """Reads the sticky error word of ``device`` (a synchronisation of the
+    current stream) and raises if a kernel flagged an error since the last
+    check; the word is cleared before raising.  Binning checks it at its own
+    host read of the pair count, which covers every earlier call; this
+    covers the calls after it (the emit and sort of the last binning)."""
+    sticky = sticky_error_word(device)
+    bits = int(sticky.item())
+    if bits:
+        sticky.zero_()
+        raise _device_error(bits)
 
 
 def _f32(t: torch.Tensor) -> torch.Tensor:
@@ -176,8 +194,7 @@ def make_gaussians(means3D, opacities, scales, rotations, cov3D, sh, colors, sca
 
 
 def coverage_mode_id(options: ExecutionOptions | None) -> int:
-    mode = "auto" if options is None else options.tile_coverage_mode
-    return resolve_tile_coverage_mode_id(mode, BASELINE_3DGS_COVERAGE)
+    return _coverage.kernel_mode("auto" if options is None else options.tile_coverage_mode)
 
 
 BIN_RECORD_FLOATS = 8
@@ -290,7 +307,7 @@ def binning(pre: Preprocessed, cam: Camera, coverage_mode: int, want_ids: bool =
     total, err, num_binned, sticky_bits = torch.cat([status, sticky]).tolist()
     if err or sticky_bits:
         sticky.zero_()
-        raise RuntimeError(f"gswarp_b200 device error word {int(err) | int(sticky_bits):#x} (bounded wait timed out or binning mismatch)")
+        raise _device_error(int(err) | int(sticky_bits))
     if total < 0 or total > MAX_BINNING_PAIRS:
         raise OverflowError(
             "binning tile-reference count exceeds signed int32; reduce Gaussian footprint or image size"

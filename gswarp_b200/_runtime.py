@@ -20,7 +20,7 @@ from typing import Any
 
 import torch
 
-from ._coverage import normalize_tile_coverage_mode
+from . import _coverage
 
 BLOCK_X = 16
 BLOCK_Y = 16
@@ -36,18 +36,14 @@ _COMPUTE_DEPTH = os.environ.get("GSWARP_COMPUTE_DEPTH", "1") != "0"
 _AUTO_TUNE_ENABLED = True
 _AUTO_TUNE_VERBOSE = True
 
-# Fixed launch shapes of the sm_100a kernels (threads per CTA).
-KERNEL_BLOCK_DIMS = {
-    "preprocess": 256,
-    "binning_emit": 256,
-    "radix_sort": 256,
-    "render_forward": 256,
-    "render_backward": 256,
-    "backward_preprocess": 256,
-    "ssim_fwd": 256,
-    "ssim_bwd": 256,
-    "knn_search": 256,
-}
+# Kernel classes whose launch shapes the native library reports
+# (gsb_block_dim): the sm_100a shapes are fixed at compile time.
+KERNEL_CLASSES = (
+    "preprocess", "preprocess_sh16", "sh_colors_views", "binning_scan", "binning_emit", "radix_sort",
+    "render_forward", "render_backward", "backward_preprocess", "backward_preprocess_sh16", "sh_backward_views",
+    "ssim_fwd", "ssim_bwd", "ssim_fwd_h", "ssim_fwd_v", "ssim_bwd_h", "ssim_bwd_v", "knn_morton", "knn_gather",
+    "knn_box_minmax", "knn_box_dist", "knn_search", "adam",
+)
 _REGISTERED_KERNEL_CLASSES: dict[str, tuple[int, str]] = {}
 
 
@@ -117,7 +113,7 @@ def get_tile_coverage_mode() -> str:
 
 def set_tile_coverage_mode(mode: str) -> None:
     global _TILE_COVERAGE_MODE
-    _TILE_COVERAGE_MODE = normalize_tile_coverage_mode(mode)
+    _TILE_COVERAGE_MODE = _coverage.check_policy(mode)
 
 
 def get_compute_depth() -> bool:
@@ -141,8 +137,6 @@ def set_runtime_auto_tuning(enabled: bool = True, verbose: bool = True) -> None:
 
 def resolve_execution_options(raster_settings) -> ExecutionOptions:
     """Merge global defaults and per-call settings (runtime_context.py:12-36)."""
-    from ._coverage import BASELINE_3DGS_COVERAGE, resolve_tile_coverage_mode
-
     backward_mode = getattr(raster_settings, "backward_mode", None)
     sort_mode = getattr(raster_settings, "binning_sort_mode", None)
     if backward_mode is not None and backward_mode != "manual":
@@ -152,7 +146,7 @@ def resolve_execution_options(raster_settings) -> ExecutionOptions:
     return ExecutionOptions(
         backward_mode=_BACKWARD_MODE if backward_mode is None else backward_mode,
         binning_sort_mode=_BINNING_SORT_MODE if sort_mode is None else sort_mode,
-        tile_coverage_mode=resolve_tile_coverage_mode(_TILE_COVERAGE_MODE, BASELINE_3DGS_COVERAGE),
+        tile_coverage_mode=_coverage.concrete(_TILE_COVERAGE_MODE),
         compute_depth=_COMPUTE_DEPTH,
         auto_tune=bool(getattr(raster_settings, "auto_tune", True)),
         auto_tune_verbose=bool(getattr(raster_settings, "auto_tune_verbose", True)),
@@ -178,7 +172,14 @@ def register_kernel_class(name: str, registers_per_thread: int, family: str = "c
 
 
 def get_tuned_block_dim(kernel_class: str, device=None) -> int:
-    return KERNEL_BLOCK_DIMS.get(kernel_class, 256)
+    """Threads per CTA the native library launches for ``kernel_class``
+    (the reference returns its tuned block_dim, or 256 when it has none,
+    gswarp/_tuning.py:342-375); a class the library does not launch gets
+    the reference's default of 256."""
+    from . import _lib
+
+    n = int(_lib.load().gsb_block_dim(str(kernel_class).encode()))
+    return n if n > 0 else 256
 
 
 def get_default_parameter_info() -> dict[str, dict[str, Any]]:
@@ -206,7 +207,7 @@ def initialize_runtime_tuning(device=None, verbose: bool = True) -> dict[str, An
     key = str(d)
     rep = _TUNING_REPORTS.get(key)
     if rep is None:
-        rep = {"device": key, "kernel_block_dims": dict(KERNEL_BLOCK_DIMS), "backend": "gswarp_b200 sm_100a"}
+        rep = {"device": key, "kernel_block_dims": {k: get_tuned_block_dim(k) for k in KERNEL_CLASSES}, "backend": "gswarp_b200 sm_100a"}
         if d.type == "cuda" and torch.cuda.is_available():
             p = torch.cuda.get_device_properties(d)
             rep.update(name=p.name, sm_count=p.multi_processor_count,

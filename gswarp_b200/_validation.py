@@ -1,5 +1,12 @@
-"""Public input validation (same contract and messages as
-gswarp/_internal/api/validation.py:46-202)."""
+"""Validation of the rasterizer's public inputs.
+
+The exception type (ValueError), the wording of every message and the
+order in which the checks fire are gswarp's drop-in contract
+(gswarp/_internal/api/validation.py:46-202); ``tests/test_validation_cpu.py``
+pins them.  Here the contract is written down as
+data -- which arguments are tensors, where each must live, what shape it must
+have -- and one small checker walks it.
+"""
 
 from __future__ import annotations
 
@@ -9,6 +16,7 @@ from typing import NamedTuple
 import torch
 
 INT32_MAX = 2**31 - 1
+N = "N"  # the Gaussian count in a shape spec
 
 
 class GaussianInputs(NamedTuple):
@@ -19,127 +27,126 @@ class GaussianInputs(NamedTuple):
     cov3D_precomp: torch.Tensor
 
 
-def _tensor(name, value):
-    if not isinstance(value, torch.Tensor):
-        raise ValueError(f"{name} must be a torch.Tensor")
-    return value
+class _Spec(NamedTuple):
+    """One tensor argument: its public name and its shape (N = the Gaussian
+    count, None = any size); ``shape=None`` checks placement only."""
+    name: str
+    shape: tuple | None
 
 
-def _f32_on(name, value, device):
-    if value.device != device:
-        raise ValueError(f"{name} must be on {device}, got {value.device}")
-    if value.dtype != torch.float32:
-        raise ValueError(f"{name} must have dtype torch.float32, got {value.dtype}")
+# Settings fields, in contract order: scalar fields, then tensors.
+_SETTING_SCALARS = ("image_height", "image_width", "tanfovx", "tanfovy", "scale_modifier", "sh_degree")
+_SETTING_TENSORS = (_Spec("bg", (3,)), _Spec("viewmatrix", (4, 4)), _Spec("projmatrix", (4, 4)),
+                    _Spec("campos", (3,)))
+# Optional Gaussian attributes (empty tensor = absent), in contract order.
+_OPTIONAL = (_Spec("sh", None), _Spec("colors_precomp", (N, 3)), _Spec("scales", (N, 3)),
+             _Spec("rotations", (N, 4)), _Spec("cov3Ds_precomp", (N, 6)))
 
 
-def _shape(name, value, shape):
-    if value.ndim != len(shape) or any(e is not None and a != e for a, e in zip(value.shape, shape)):
-        expected = tuple("N" if e is None else e for e in shape)
-        raise ValueError(f"{name} must have shape {expected}, got {tuple(value.shape)}")
+def _on_cuda(t: torch.Tensor) -> bool:
+    return t.is_cuda
 
 
-def _finite(name, value):
-    if value.numel() != 0 and not bool(torch.isfinite(value).all()):
-        raise ValueError(f"{name} contains NaN or Inf values")
+def _fail(msg: str):
+    raise ValueError(msg)
+
+
+def _is_tensor(name: str, value) -> torch.Tensor:
+    return value if isinstance(value, torch.Tensor) else _fail(f"{name} must be a torch.Tensor")
+
+
+def _placed(name: str, t: torch.Tensor, device: torch.device) -> None:
+    if t.device != device:
+        _fail(f"{name} must be on {device}, got {t.device}")
+    if t.dtype != torch.float32:
+        _fail(f"{name} must have dtype torch.float32, got {t.dtype}")
+
+
+def _shaped(name: str, t: torch.Tensor, shape: tuple, n: int | None = None) -> None:
+    want = tuple(n if (d == N and n is not None) else (None if d == N else d) for d in shape)
+    if t.ndim != len(want) or any(w is not None and a != w for a, w in zip(t.shape, want)):
+        shown = tuple(N if w is None else w for w in want)
+        _fail(f"{name} must have shape {shown}, got {tuple(t.shape)}")
+
+
+def _check(name: str, t: torch.Tensor, device: torch.device, shape: tuple | None = None, n: int | None = None):
+    _placed(name, t, device)
+    if shape is not None:
+        _shaped(name, t, shape, n)
 
 
 def validate_rasterizer_inputs(means3D, means2D, sh, colors_precomp, opacities, scales, rotations,
                                cov3Ds_precomp, raster_settings) -> None:
-    means3D = _tensor("means3D", means3D)
-    means2D = _tensor("means2D", means2D)
-    opacities = _tensor("opacities", opacities)
-    if not means3D.is_cuda:
-        raise ValueError("means3D must be a CUDA tensor")
+    """Raises ValueError on the first violated contract, in gswarp's order."""
+    means3D, means2D, opacities = (_is_tensor(k, v) for k, v in
+                                   (("means3D", means3D), ("means2D", means2D), ("opacities", opacities)))
+    if not _on_cuda(means3D):
+        _fail("means3D must be a CUDA tensor")
     device = means3D.device
-    _f32_on("means3D", means3D, device)
-    _shape("means3D", means3D, (None, 3))
+    _check("means3D", means3D, device, (N, 3))
     n = means3D.shape[0]
     if n > INT32_MAX:
-        raise ValueError("the Gaussian count must fit in a signed 32-bit index")
-    _f32_on("means2D", means2D, device)
-    _shape("means2D", means2D, (n, 3))
-    _f32_on("opacities", opacities, device)
+        _fail("the Gaussian count must fit in a signed 32-bit index")
+    _check("means2D", means2D, device, (N, 3), n)
+    _check("opacities", opacities, device)
     if opacities.numel() != n:
-        raise ValueError(f"opacities must contain one value per Gaussian ({n}), got {opacities.numel()}")
+        _fail(f"opacities must contain one value per Gaussian ({n}), got {opacities.numel()}")
+
     try:
-        H = raster_settings.image_height
-        W = raster_settings.image_width
-        tanfovx = raster_settings.tanfovx
-        tanfovy = raster_settings.tanfovy
-        scale_modifier = raster_settings.scale_modifier
-        sh_degree = raster_settings.sh_degree
-        bg = _tensor("raster_settings.bg", raster_settings.bg)
-        view = _tensor("raster_settings.viewmatrix", raster_settings.viewmatrix)
-        proj = _tensor("raster_settings.projmatrix", raster_settings.projmatrix)
-        campos = _tensor("raster_settings.campos", raster_settings.campos)
+        H, W, tanfovx, tanfovy, scale_modifier, sh_degree = (getattr(raster_settings, f) for f in _SETTING_SCALARS)
+        tensors = [_is_tensor(f"raster_settings.{s.name}", getattr(raster_settings, s.name)) for s in _SETTING_TENSORS]
     except AttributeError as exc:
         raise ValueError("raster_settings is missing a required field") from exc
-    if not isinstance(H, int) or not isinstance(W, int) or H <= 0 or W <= 0:
-        raise ValueError("image_height and image_width must be positive integers")
+    if not (isinstance(H, int) and isinstance(W, int) and H > 0 and W > 0):
+        _fail("image_height and image_width must be positive integers")
     if H * W > INT32_MAX:
-        raise ValueError("image_height * image_width must fit in a signed 32-bit index")
+        _fail("image_height * image_width must fit in a signed 32-bit index")
     if not all(math.isfinite(float(v)) and float(v) > 0.0 for v in (tanfovx, tanfovy, scale_modifier)):
-        raise ValueError("tanfovx, tanfovy, and scale_modifier must be finite and positive")
+        _fail("tanfovx, tanfovy, and scale_modifier must be finite and positive")
     if not isinstance(sh_degree, int) or sh_degree < 0:
-        raise ValueError("sh_degree must be a non-negative integer")
-    for name, value, shape in (("raster_settings.bg", bg, (3,)), ("raster_settings.viewmatrix", view, (4, 4)),
-                               ("raster_settings.projmatrix", proj, (4, 4)), ("raster_settings.campos", campos, (3,))):
-        _f32_on(name, value, device)
-        _shape(name, value, shape)
-    optional = {"sh": sh, "colors_precomp": colors_precomp, "scales": scales, "rotations": rotations,
-                "cov3Ds_precomp": cov3Ds_precomp}
-    for name, value in optional.items():
-        value = _tensor(name, value)
-        if value.numel() != 0:
-            _f32_on(name, value, device)
-    has_sh = sh.numel() != 0
-    has_colors = colors_precomp.numel() != 0
-    has_scales = scales.numel() != 0
-    has_rot = rotations.numel() != 0
-    has_cov = cov3Ds_precomp.numel() != 0
-    if n != 0 and has_sh == has_colors:
-        raise ValueError("provide exactly one of sh or colors_precomp")
-    if n != 0 and has_scales != has_rot:
-        raise ValueError("provide exactly one of scales/rotations or cov3Ds_precomp")
-    if n != 0 and (has_scales or has_rot) == has_cov:
-        raise ValueError("provide exactly one of scales/rotations or cov3Ds_precomp")
-    if has_colors:
-        _shape("colors_precomp", colors_precomp, (n, 3))
-    if has_scales:
-        _shape("scales", scales, (n, 3))
-    if has_rot:
-        _shape("rotations", rotations, (n, 4))
-    if has_cov:
-        _shape("cov3Ds_precomp", cov3Ds_precomp, (n, 6))
-    if has_sh:
-        if sh.numel() % (n * 3) != 0:
-            raise ValueError("sh must contain a whole number of RGB coefficients per Gaussian")
-        if sh.numel() // (n * 3) < (sh_degree + 1) ** 2:
-            raise ValueError("sh does not contain enough coefficients for sh_degree")
+        _fail("sh_degree must be a non-negative integer")
+    for spec, t in zip(_SETTING_TENSORS, tensors):
+        _check(f"raster_settings.{spec.name}", t, device, spec.shape)
+
+    given = dict(zip((s.name for s in _OPTIONAL), (sh, colors_precomp, scales, rotations, cov3Ds_precomp)))
+    for spec in _OPTIONAL:
+        t = given[spec.name] = _is_tensor(spec.name, given[spec.name])
+        if t.numel():
+            _placed(spec.name, t, device)
+    has = {k: t.numel() != 0 for k, t in given.items()}
+    if n and has["sh"] == has["colors_precomp"]:
+        _fail("provide exactly one of sh or colors_precomp")
+    if n and (has["scales"] != has["rotations"] or (has["scales"] or has["rotations"]) == has["cov3Ds_precomp"]):
+        _fail("provide exactly one of scales/rotations or cov3Ds_precomp")
+    for spec in _OPTIONAL[1:]:
+        if has[spec.name]:
+            _shaped(spec.name, given[spec.name], spec.shape, n)
+    if has["sh"]:
+        per_gaussian, rem = divmod(given["sh"].numel(), n * 3)
+        if rem:
+            _fail("sh must contain a whole number of RGB coefficients per Gaussian")
+        if per_gaussian < (sh_degree + 1) ** 2:
+            _fail("sh does not contain enough coefficients for sh_degree")
+
     if getattr(raster_settings, "debug", False):
-        for name, value in (("means3D", means3D), ("means2D", means2D), ("opacities", opacities),
-                            ("raster_settings.bg", bg), ("raster_settings.viewmatrix", view),
-                            ("raster_settings.projmatrix", proj), ("raster_settings.campos", campos),
-                            *optional.items()):
-            _finite(name, value)
+        named = [("means3D", means3D), ("means2D", means2D), ("opacities", opacities)]
+        named += [(f"raster_settings.{s.name}", t) for s, t in zip(_SETTING_TENSORS, tensors)]
+        for name, t in named + list(given.items()):
+            if t.numel() and not bool(torch.isfinite(t).all()):
+                _fail(f"{name} contains NaN or Inf values")
 
 
 def normalize_gaussian_inputs(*, dc, shs, colors_precomp, scales, rotations, cov3D_precomp) -> GaussianInputs:
-    if dc is not None and shs is not None:
-        shs = torch.cat([dc, shs], dim=1)
-    elif dc is not None:
-        shs = dc
-    if (shs is None and colors_precomp is None) or (shs is not None and colors_precomp is not None):
-        raise ValueError("provide exactly one of shs or colors_precomp")
-    if ((scales is None or rotations is None) and cov3D_precomp is None) or (
-        (scales is not None or rotations is not None) and cov3D_precomp is not None
-    ):
-        raise ValueError("provide exactly one of scales/rotations or cov3D_precomp")
+    """Folds ``dc`` into the SH coefficients (dc first) and turns absent
+    inputs into empty tensors, after the exactly-one checks of
+    gswarp/_internal/api/validation.py:162-202."""
+    if dc is not None:
+        shs = dc if shs is None else torch.cat([dc, shs], dim=1)
+    if (shs is None) == (colors_precomp is None):
+        _fail("provide exactly one of shs or colors_precomp")
+    pair = (scales is not None, rotations is not None)
+    if (not all(pair) and cov3D_precomp is None) or (any(pair) and cov3D_precomp is not None):
+        _fail("provide exactly one of scales/rotations or cov3D_precomp")
     empty = torch.Tensor([])
-    return GaussianInputs(
-        shs=empty if shs is None else shs,
-        colors_precomp=empty if colors_precomp is None else colors_precomp,
-        scales=empty if scales is None else scales,
-        rotations=empty if rotations is None else rotations,
-        cov3D_precomp=empty if cov3D_precomp is None else cov3D_precomp,
-    )
+    return GaussianInputs(*(empty if t is None else t for t in (shs, colors_precomp, scales, rotations,
+                                                                   cov3D_precomp)))

@@ -24,7 +24,7 @@
 namespace gsb {
 namespace {
 
-constexpr int SCAN_THREADS = 256;
+constexpr int SCAN_THREADS = launch::BINNING_SCAN;
 constexpr int SCAN_ITEMS = 16;
 constexpr int SCAN_TILE = SCAN_THREADS * SCAN_ITEMS;  // 4096
 
@@ -242,6 +242,20 @@ struct EmitPairs {
 // Records with more than BINREC_MAX_BANDS bands re-run the sweep from the
 // render record per lane afterwards.  A record whose tile count differs from
 // the pair count raises ERR_EMIT_MISMATCH (and emits no more than the count).
+// Slots of the pair count that a mismatching record does not fill get the
+// key EMIT_FILL_KEY (no tile: above every tile id, so the ranges pass skips
+// it) and the Gaussian's own id, so nothing downstream reads an
+// uninitialised key or point id.
+constexpr unsigned EMIT_FILL_KEY = 0xFFFFFFFFu;
+
+__device__ __forceinline__ void emit_fill(unsigned* keys, unsigned* vals, long long start, int from, int n,
+                                          int point) {
+  for (int k = from; k < n; ++k) {
+    keys[start + k] = EMIT_FILL_KEY;
+    vals[start + k] = (unsigned)point;
+  }
+}
+
 struct EmitLane {
   unsigned w[8];
   int pre, start, point;
@@ -286,7 +300,7 @@ __device__ __forceinline__ int record_tile(const unsigned* w, int idx, int gx) {
   return 0;  // unreachable: idx < record_count
 }
 
-constexpr int EMIT_THREADS = 256;
+constexpr int EMIT_THREADS = launch::BINNING_EMIT;
 
 __global__ void __launch_bounds__(EMIT_THREADS, 8) emit_binrec_kernel(
     const long long* __restrict__ n_dev, int gx, int mode, const int* __restrict__ order,
@@ -346,12 +360,14 @@ __global__ void __launch_bounds__(EMIT_THREADS, 8) emit_binrec_kernel(
     keys[pos] = (unsigned)record_tile(wl[o].w, idx, gx);
     vals[pos] = (unsigned)wl[o].point;
   }
+  if (n > 0 && !sweep && ncoop < n) emit_fill(keys, vals, start, ncoop, n, point);
   if (sweep) {
     const float4 q0 = __ldg(records + (size_t)point * 3), q1 = __ldg(records + (size_t)point * 3 + 1);
     const float t = opacity_threshold(q1.y);
     EmitPairs e{keys, vals, (long long)start, n, point, 0};
     emit_record(w, gx, mode, q0.x, q0.y, q0.z, q0.w, q1.x, t, e);
     if (e.k != n) atomicOr((unsigned long long*)err, (unsigned long long)ERR_EMIT_MISMATCH);
+    if (e.k < n) emit_fill(keys, vals, start, e.k, n, point);
   }
 }
 
@@ -364,16 +380,20 @@ __global__ void __launch_bounds__(256) emit_kernel(
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= *n_dev) return;
   const int p = order[r];
-  const int n = tiles_touched[p];
+  // the slots are the ones the offsets give this Gaussian (as in the record
+  // path); a coverage that produces another count is flagged and filled
+  const int end = offsets[r];
+  const int n = end - (r > 0 ? offsets[r - 1] : 0);
   if (n <= 0) return;
   const int radius = radii[p];
   const float4 q0 = records[(size_t)p * 3 + 0];
   const float4 q1 = records[(size_t)p * 3 + 1];
   const float cov_a = conic_2d_inv[(size_t)p * 3 + 0];
   const float cov_c = conic_2d_inv[(size_t)p * 3 + 2];
-  EmitPairs e{keys, vals, (long long)offsets[r] - n, n, p, 0};
+  EmitPairs e{keys, vals, (long long)end - n, n, p, 0};
   cover_tiles(q0.x, q0.y, cov_a, cov_c, q0.z, q0.w, q1.x, q1.y, radius, gx, gy, mode, e);
   if (e.k != n) atomicOr((unsigned long long*)err, (unsigned long long)ERR_EMIT_MISMATCH);
+  if (e.k < n) emit_fill(keys, vals, e.start, e.k, n, p);
 }
 
 
@@ -381,9 +401,10 @@ inline size_t align256(size_t b) { return (b + 255) & ~(size_t)255; }
 
 // Ranges when the sort has no pass to write them: a single tile (every key
 // is 0) or a single pair.
-__global__ void single_range_kernel(const unsigned* __restrict__ keys, int R, int* __restrict__ ranges) {
+__global__ void single_range_kernel(const unsigned* __restrict__ keys, int R, int tiles, int* __restrict__ ranges) {
   if (threadIdx.x == 0 && blockIdx.x == 0) {
     const unsigned k = keys[0];
+    if (k >= (unsigned)tiles) return;  // an emit fill key (mismatch flagged): no range
     ranges[2 * (size_t)k] = 0;
     ranges[2 * (size_t)k + 1] = R;
   }
@@ -540,7 +561,7 @@ GSB_EXPORT int gsb_bin_emit_sort(const gsb_bin_sort_args* a, void* stream) {
   if (passes == 0 || R <= 1) {
     // nothing to sort: the emitted order is the sorted order
     if (vb[0] != pl) cudaMemcpyAsync(pl, vb[0], (size_t)R * 4, cudaMemcpyDeviceToDevice, s);
-    single_range_kernel<<<1, 32, 0, s>>>(kb[0], (int)R, a->ranges);
+    single_range_kernel<<<1, 32, 0, s>>>(kb[0], (int)R, tiles, a->ranges);
   } else
     radix::sort_pairs(kb, vb, R, nullptr, passes, sort_scratch, a->error_word, s, a->ranges, tiles);
   return check_launch("gsb_bin_emit_sort");

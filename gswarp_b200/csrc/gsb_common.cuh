@@ -9,6 +9,7 @@
 #include <string>
 
 #include "../../include/gsb200.h"
+#include "gsb_launch.cuh"
 
 #define GSB_EXPORT extern "C" __attribute__((visibility("default")))
 

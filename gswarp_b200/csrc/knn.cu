@@ -31,9 +31,10 @@ namespace gsb {
 namespace {
 
 constexpr int BOUNDS_BLOCKS = 296;
+constexpr int KT = launch::KNN;  // threads per CTA of every KNN kernel but the final bounds reduction
 constexpr float FLT_BIG_K = 3.402823466e38f;
 
-__global__ void __launch_bounds__(256) bounds_partial_kernel(int P, const float* __restrict__ pts,
+__global__ void __launch_bounds__(KT) bounds_partial_kernel(int P, const float* __restrict__ pts,
                                                              float* __restrict__ part) {
   float lo[3] = {FLT_BIG_K, FLT_BIG_K, FLT_BIG_K}, hi[3] = {-FLT_BIG_K, -FLT_BIG_K, -FLT_BIG_K};
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < P; i += gridDim.x * blockDim.x) {
@@ -44,7 +45,7 @@ __global__ void __launch_bounds__(256) bounds_partial_kernel(int P, const float*
       hi[c] = fmaxf(hi[c], v);
     }
   }
-  __shared__ float s[6][8];
+  __shared__ float s[6][KT / 32];
 #pragma unroll
   for (int c = 0; c < 3; ++c) {
 #pragma unroll
@@ -61,7 +62,7 @@ __global__ void __launch_bounds__(256) bounds_partial_kernel(int P, const float*
   __syncthreads();
   if (threadIdx.x < 6) {
     float r = s[threadIdx.x][0];
-    for (int w = 1; w < 8; ++w)
+    for (int w = 1; w < KT / 32; ++w)
       r = threadIdx.x < 3 ? fminf(r, s[threadIdx.x][w]) : fmaxf(r, s[threadIdx.x][w]);
     part[blockIdx.x * 6 + threadIdx.x] = r;
   }
@@ -122,7 +123,7 @@ constexpr int LEAF = 32;  // points per leaf (one per lane); 32 leaves per paren
 
 // Thread per sorted point: gather the sorted SoA; each warp (= one leaf of
 // 32 consecutive sorted points) reduces its AABB.
-__global__ void __launch_bounds__(256) gather_leaf_kernel(int P, const float* __restrict__ pts,
+__global__ void __launch_bounds__(KT) gather_leaf_kernel(int P, const float* __restrict__ pts,
                                                           const unsigned* __restrict__ order,
                                                           float* __restrict__ sx, float* __restrict__ sy,
                                                           float* __restrict__ sz, float* __restrict__ leaf_boxes) {
@@ -159,7 +160,7 @@ __global__ void __launch_bounds__(256) gather_leaf_kernel(int P, const float* __
 }
 
 // Warp per parent box: AABB of up to 32 child boxes.
-__global__ void __launch_bounds__(256) reduce_boxes_kernel(int nchild, const float* __restrict__ child,
+__global__ void __launch_bounds__(KT) reduce_boxes_kernel(int nchild, const float* __restrict__ child,
                                                            float* __restrict__ parent) {
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   const int par = t / 32, lane = threadIdx.x & 31;
@@ -329,12 +330,12 @@ __device__ __forceinline__ void visit_leaf(int L, const float (&cb)[6], int P, b
 }
 
 // One warp per query leaf.  Boxes: leaves (nl), parents (np), grandparents (ng).
-__global__ void __launch_bounds__(256, 4) search_kernel(int P, int nl, int np, int ng, const float* __restrict__ sx,
+__global__ void __launch_bounds__(KT, 4) search_kernel(int P, int nl, int np, int ng, const float* __restrict__ sx,
                                                      const float* __restrict__ sy, const float* __restrict__ sz,
                                                      const float* __restrict__ leaf_b, const float* __restrict__ par_b,
                                                      const float* __restrict__ gp_b,
                                                      const unsigned* __restrict__ order, float* __restrict__ out) {
-  __shared__ float4 s_leaf[256 / 32][32];
+  __shared__ float4 s_leaf[KT / 32][32];
   const int lane = threadIdx.x & 31;
   const int qleaf = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
   if (qleaf >= nl) return;  // whole warp
@@ -491,17 +492,17 @@ GSB_EXPORT int gsb_knn(const gsb_knn_args* a, void* stream) {
   float* bounds = (float*)take(256);
   void* scratch = w;
 
-  bounds_partial_kernel<<<BOUNDS_BLOCKS, 256, 0, s>>>(P, a->points, part);
+  bounds_partial_kernel<<<BOUNDS_BLOCKS, KT, 0, s>>>(P, a->points, part);
   bounds_final_kernel<<<1, 32, 0, s>>>(BOUNDS_BLOCKS, part, bounds);
-  morton_kernel<<<div_up(P, 256), 256, 0, s>>>(P, a->points, bounds, codes, idx);
+  morton_kernel<<<div_up(P, KT), KT, 0, s>>>(P, a->points, bounds, codes, idx);
   unsigned* kb[2] = {codes, codes_alt};
   unsigned* vb[2] = {idx, idx_alt};
   const int where = radix::sort_pairs(kb, vb, P, nullptr, 4, scratch, a->error_word, s);
   const unsigned* order = vb[where];
-  gather_leaf_kernel<<<div_up((long long)nl * LEAF, 256), 256, 0, s>>>(P, a->points, order, sx, sy, sz, leaf_b);
-  reduce_boxes_kernel<<<div_up((long long)np * 32, 256), 256, 0, s>>>(nl, leaf_b, par_b);
-  reduce_boxes_kernel<<<div_up((long long)ng * 32, 256), 256, 0, s>>>(np, par_b, gp_b);
-  search_kernel<<<div_up((long long)nl * 32, 256), 256, 0, s>>>(P, nl, np, ng, sx, sy, sz, leaf_b, par_b, gp_b,
+  gather_leaf_kernel<<<div_up((long long)nl * LEAF, KT), KT, 0, s>>>(P, a->points, order, sx, sy, sz, leaf_b);
+  reduce_boxes_kernel<<<div_up((long long)np * 32, KT), KT, 0, s>>>(nl, leaf_b, par_b);
+  reduce_boxes_kernel<<<div_up((long long)ng * 32, KT), KT, 0, s>>>(np, par_b, gp_b);
+  search_kernel<<<div_up((long long)nl * 32, KT), KT, 0, s>>>(P, nl, np, ng, sx, sy, sz, leaf_b, par_b, gp_b,
                                                                 order, a->out);
   return check_launch("gsb_knn");
 }

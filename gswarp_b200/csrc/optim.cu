@@ -24,7 +24,7 @@
 namespace gsb {
 namespace {
 
-constexpr int ADAM_THREADS = 256;
+constexpr int ADAM_THREADS = launch::ADAM;
 constexpr int ADAM_ITEMS = 4;
 
 struct AdamScalars {
@@ -134,6 +134,6 @@ GSB_EXPORT int gsb_densify_stats(int P, const int* radii, float* denom, float* m
     return GSB_ERR_INVALID;
   }
   if (P == 0) return GSB_OK;
-  densify_stats_kernel<<<div_up(P, 256), 256, 0, (cudaStream_t)stream>>>(P, radii, denom, max_radii);
+  densify_stats_kernel<<<div_up(P, ADAM_THREADS), ADAM_THREADS, 0, (cudaStream_t)stream>>>(P, radii, denom, max_radii);
   return check_launch("gsb_densify_stats");
 }

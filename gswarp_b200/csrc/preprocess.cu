@@ -96,8 +96,8 @@ __device__ __forceinline__ unsigned sh_colour(const float (&shv)[48], int K, int
   return clamp_bits;
 }
 
-constexpr int PF_THREADS = 256;
-constexpr int PF_SH16_THREADS = 128;
+constexpr int PF_THREADS = launch::PREPROCESS;
+constexpr int PF_SH16_THREADS = launch::PREPROCESS_SH16;
 constexpr int SH_ROW_F4 = 13;  // staged SH row: 48 floats padded to 52
 
 // SH16: (P,16,3) SH rows, 16-byte aligned.  Each warp then moves the SH rows
@@ -405,7 +405,7 @@ __global__ void __launch_bounds__(SHM == SHM_16 ? PF_SH16_THREADS : PF_THREADS, 
 // warp stages the SH rows of its 32 consecutive Gaussians (one contiguous
 // span of 32*K*3 floats) in shared memory with coalesced loads, each thread
 // copies its row to registers once and evaluates it from every camera.
-constexpr int SHV_THREADS = 128;
+constexpr int SHV_THREADS = launch::SH_COLORS_VIEWS;
 constexpr int SHV_ROW_F = 49;  // 48 floats padded: per-thread scalar reads hit 32 banks
 
 __global__ void __launch_bounds__(SHV_THREADS) sh_colors_views_kernel(const gsb_sh_views_args a) {

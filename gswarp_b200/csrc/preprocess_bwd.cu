@@ -196,8 +196,8 @@ __device__ void sh_backward(const gsb_preprocess_bwd_args& a, int idx, const flo
 // accesses of a warp hit 32 different banks).  Arithmetic is the same
 // sh_core as the per-thread path.
 constexpr int SH_ROW_F = 49;
-constexpr int PB_THREADS = 256;
-constexpr int PB_SH16_THREADS = 128;
+constexpr int PB_THREADS = launch::PREPROCESS_BWD;
+constexpr int PB_SH16_THREADS = launch::PREPROCESS_BWD_SH16;
 
 __device__ __forceinline__ void sh_backward_staged(const gsb_preprocess_bwd_args& a, float* rows, int my_idx,
                                                    bool work, bool need, const float mean[3],

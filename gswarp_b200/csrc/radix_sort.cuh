@@ -27,7 +27,7 @@ namespace {
 
 constexpr int RADIX_BITS = 8;
 constexpr int RADIX = 1 << RADIX_BITS;
-constexpr int THREADS = 256;
+constexpr int THREADS = launch::RADIX_SORT;
 constexpr int WARPS = THREADS / 32;
 constexpr int ITEMS = 15;
 constexpr int TILE_KEYS = THREADS * ITEMS;  // 3840
@@ -139,7 +139,8 @@ __global__ void __launch_bounds__(THREADS, 4) onesweep_kernel(
     unsigned* __restrict__ keys_out, unsigned* __restrict__ vals_out, int n_host,
     const int* __restrict__ n_dev, int shift,
     const unsigned* __restrict__ bin_base, unsigned long long* __restrict__ lookback,
-    unsigned* __restrict__ tile_counter, long long* __restrict__ err, int* __restrict__ ranges) {
+    unsigned* __restrict__ tile_counter, long long* __restrict__ err, int* __restrict__ ranges,
+    int range_keys) {
   __shared__ unsigned s_keys[TILE_KEYS];
   __shared__ unsigned s_vals[HAS_VALS ? TILE_KEYS : 1];
   __shared__ unsigned s_warp_hist[WARPS][RADIX];
@@ -278,8 +279,12 @@ __global__ void __launch_bounds__(THREADS, 4) onesweep_kernel(
         // over the tiles that hold it: end by atomicMax, start as n - start
         // by atomicMax (both fields start at zero, so keys that never occur
         // stay (0, 0)); ranges_fixup_kernel turns n - start back into start.
-        if (j == 0 || s_keys[j - 1] != k) atomicMax(ranges + 2 * (size_t)k, n - (int)dst);
-        if (j == tile_n - 1 || s_keys[j + 1] != k) atomicMax(ranges + 2 * (size_t)k + 1, (int)dst + 1);
+        // Keys at or above range_keys (the emit's fill for pairs it could not
+        // produce, flagged in the error word) have no range slot.
+        if (k < (unsigned)range_keys) {
+          if (j == 0 || s_keys[j - 1] != k) atomicMax(ranges + 2 * (size_t)k, n - (int)dst);
+          if (j == tile_n - 1 || s_keys[j + 1] != k) atomicMax(ranges + 2 * (size_t)k + 1, (int)dst + 1);
+        }
       }
     }
   }
@@ -355,11 +360,11 @@ __host__ inline int sort_pairs(unsigned* k[2], unsigned* v[2], long long n, cons
     if (v[0]) {
       onesweep_kernel<true><<<tiles, THREADS, 0, stream>>>(
           k[cur], v[cur], k[cur ^ 1], v[cur ^ 1], (int)n, n_dev, p * RADIX_BITS, s.bin_base + p * RADIX,
-          lb, s.counters + p, err, rg);
+          lb, s.counters + p, err, rg, range_keys);
     } else {
       onesweep_kernel<false><<<tiles, THREADS, 0, stream>>>(
           k[cur], nullptr, k[cur ^ 1], nullptr, (int)n, n_dev, p * RADIX_BITS, s.bin_base + p * RADIX,
-          lb, s.counters + p, err, rg);
+          lb, s.counters + p, err, rg, range_keys);
     }
     cur ^= 1;
   }

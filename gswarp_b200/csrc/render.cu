@@ -29,7 +29,7 @@
 namespace gsb {
 namespace {
 
-constexpr int THREADS = 128;
+constexpr int THREADS = launch::RENDER;
 constexpr int BATCH = 128;
 constexpr unsigned FULL = 0xffffffffu;
 

@@ -32,7 +32,7 @@ constexpr float C3_0 = -0.5900435899266435f, C3_1 = 2.890611442640554f, C3_2 = -
                 C3_3 = 0.3731763325901154f, C3_4 = -0.4570457994644658f, C3_5 = 1.445305721320277f,
                 C3_6 = -0.5900435899266435f;
 
-constexpr int SHV_THREADS = 128;
+constexpr int SHV_THREADS = launch::SH_BACKWARD_VIEWS;
 constexpr int SHV_ROW_F = 49;  // 48 floats padded: per-thread scalar reads of a warp hit 32 banks
 
 // Adds one view's contribution: accum[3k+c] += Y_k g_c for the USED

@@ -25,7 +25,7 @@ constexpr int TX = 32, TY = 40;
 constexpr int HALO = 5;
 constexpr int RX = TX + 2 * HALO;  // 42
 constexpr int RY = TY + 2 * HALO;  // 50
-constexpr int THREADS = 256;
+constexpr int THREADS = launch::SSIM;
 // Register blocking: a thread runs the horizontal pass over RH consecutive
 // outputs of one row (its 11-tap windows slide over RH + 10 values held in
 // registers) and the vertical pass over RV consecutive outputs of one column,
@@ -532,10 +532,13 @@ GSB_EXPORT int gsb_photo_loss_bwd(const gsb_photo_loss_bwd_args* a, void* stream
 //    call's partial sums; each call writes every slot it later reads, so
 //    nothing has to start at zero, but two calls whose kernels overlap on
 //    the GPU (different streams without ordering) race on the array;
-//  * the array's device address is looked up once per device, on the first
-//    call made with that device current; make that first call before any
-//    stream capture begins.
+//  * the array's device address is looked up once per device and CUDA
+//    context, on the first call made with that device current (and again
+//    after the context is replaced, e.g. by cudaDeviceReset); make the first
+//    call on a device before any stream capture begins.
 // ---------------------------------------------------------------------------
+#include <cuda.h>
+
 #include <mutex>
 
 namespace gsb {
@@ -543,11 +546,43 @@ namespace {
 constexpr int NOALLOC_MAX_PARTIALS = GSB_SSIM_NOALLOC_MAX_PARTIALS;
 static __device__ __align__(256) float g_noalloc_partials[NOALLOC_MAX_PARTIALS];
 constexpr int NOALLOC_MAX_DEVICES = 64;
-float* g_noalloc_ptr[NOALLOC_MAX_DEVICES] = {};
+struct NoallocSlot {
+  unsigned long long ctx_id;  // context the address belongs to (0: unknown)
+  float* ptr;
+};
+NoallocSlot g_noalloc_slot[NOALLOC_MAX_DEVICES] = {};
 std::mutex g_noalloc_mutex;
 
-// Device address of the fixed scratch array on the current device (looked
-// up once per device).
+// Unique id of the calling thread's current CUDA context (driver
+// cuCtxGetCurrent + cuCtxGetId, fetched through the runtime so the library
+// does not link libcuda); 0 when it cannot be told, in which case the
+// address is looked up again on every call.
+unsigned long long current_context_id() {
+  using GetCurrent = CUresult (*)(CUcontext*);
+  using GetId = CUresult (*)(CUcontext, unsigned long long*);
+  static GetCurrent get_current = nullptr;
+  static GetId get_id = nullptr;
+  static bool resolved = false;
+  if (!resolved) {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = (GetCurrent)f;
+    f = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = (GetId)f;
+    resolved = true;
+  }
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || !ctx || get_id(ctx, &id) != CUDA_SUCCESS)
+    return 0;
+  return id;
+}
+
+// Device address of the fixed scratch array on the current device.
 int noalloc_scratch(float** out) {
   int dev = -1;
   cudaError_t e = cudaGetDevice(&dev);
@@ -556,16 +591,21 @@ int noalloc_scratch(float** out) {
     return GSB_ERR_CUDA;
   }
   std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-  if (!g_noalloc_ptr[dev]) {
+  NoallocSlot& slot = g_noalloc_slot[dev];
+  const unsigned long long ctx = current_context_id();
+  if (!slot.ptr || ctx == 0 || ctx != slot.ctx_id) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_partials);
     if (e != cudaSuccess || !p) {
       set_error("gsb_ssim_fwd_noalloc: cudaGetSymbolAddress failed (%s)", cudaGetErrorString(e));
+      slot = NoallocSlot{};
       return GSB_ERR_CUDA;
     }
-    g_noalloc_ptr[dev] = (float*)p;
+    slot.ptr = (float*)p;
+    // the lookup makes the device's context current if it was not yet
+    slot.ctx_id = ctx ? ctx : current_context_id();
   }
-  *out = g_noalloc_ptr[dev];
+  *out = slot.ptr;
   return GSB_OK;
 }
 }  // namespace

@@ -128,7 +128,9 @@ class FusedViewStep:
     the step -- and returns the per-view [loss, L1, SSIM] rows as a (V,3)
     device tensor.  Gradients are in ``self.grads`` (one flat buffer; its
     blocks are the parameters' ``.grad``) and are all-reduced across the
-    process group when one is initialised.
+    process group when one is initialised.  The step ends with one host read
+    of the device error word (a synchronisation), so an error flagged by any
+    of its kernels raises ``RuntimeError`` from this call.
     """
 
     def __init__(self, params: Sequence[torch.Tensor], settings: Sequence, l1_weight: float = 1.0,
@@ -333,6 +335,9 @@ class FusedViewStep:
                                      self.grads.views[0])
             else:
                 self._sh_backward_and_reduce(means, sh)
+            # errors flagged by the last view's emit and sort (earlier views' are read by the next
+            # view's binning): raised by this call, before anyone uses its gradients
+            pl.raise_device_errors(self.device)
         return self.losses
 
     def _sh_backward_and_reduce(self, means: torch.Tensor, sh: torch.Tensor) -> None:

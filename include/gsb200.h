@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define GSB_ABI_VERSION 13
+#define GSB_ABI_VERSION 14
 
 #define GSB_OK 0
 #define GSB_ERR_INVALID (-1)  /* bad argument: ValueError in Python          */
@@ -56,6 +56,17 @@ extern "C" {
 
 int gsb_abi_version(void);
 const char* gsb_last_error(void);
+
+/* Threads per CTA that the library launches for a kernel class (0 for an
+ * unknown name).  Stands in for get_tuned_block_dim (gswarp/_tuning.py:342):
+ * the sm_100a launch shapes are fixed at compile time, and this reports the
+ * shapes actually launched.  Classes: preprocess, preprocess_sh16,
+ * sh_colors_views, binning_scan, binning_emit, radix_sort, render_forward,
+ * render_backward, backward_preprocess, backward_preprocess_sh16,
+ * sh_backward_views, ssim_fwd, ssim_bwd (and the reference's ssim_fwd_h,
+ * ssim_fwd_v, ssim_bwd_h, ssim_bwd_v), knn_morton, knn_gather,
+ * knn_box_minmax, knn_box_dist, knn_search, adam. */
+int gsb_block_dim(const char* kernel_class);
 
 /* ------------------------------------------------------------------------ */
 /* Preprocess forward.  Replaces preprocess_gaussians                        */
@@ -372,8 +383,9 @@ int gsb_photo_loss_bwd(const gsb_photo_loss_bwd_args* a, void* stream);
  * inside the library, so B*C*ceil(H/40)*ceil(W/32) must not exceed
  * GSB_SSIM_NOALLOC_MAX_PARTIALS (larger inputs return GSB_ERR_INVALID).
  * All calls on a device share that array: calls whose kernels overlap on the
- * GPU race.  The first call on a device looks up the array's address; make
- * it before any stream capture begins. */
+ * GPU race.  The first call on a device looks up the array's address (again
+ * after the device's context is replaced, e.g. by cudaDeviceReset); make it
+ * before any stream capture begins. */
 #define GSB_SSIM_NOALLOC_MAX_PARTIALS 65536
 int gsb_ssim_fwd_noalloc(int B, int C, int H, int W, int valid, float C1, float C2,
                          const float* img1, const float* img2, float* dm, float* loss,

@@ -55,20 +55,17 @@ def test_fused_ssim_validation():
 
 
 def test_coverage_policy_resolution():
-    axis = cov.CoverageContract(footprint=cov.FOOTPRINT_AXIS_ALIGNED, support=cov.SUPPORT_ALPHA_CUTOFF,
-                                sample_domain=cov.SAMPLE_PIXEL_CENTERS)
-    assert cov.resolve_tile_coverage_mode("auto", cov.CONSERVATIVE_COVERAGE) == "snugbox"
-    assert cov.resolve_tile_coverage_mode("auto", axis) == "snugbox"
-    with pytest.raises(ValueError, match="cuda_compat_screen_conic"):
-        cov.resolve_tile_coverage_mode("conic_rect", cov.CONSERVATIVE_COVERAGE)
-    assert cov.resolve_tile_coverage_mode("auto", cov.BASELINE_3DGS_COVERAGE) == "accutile_sweep"
-    assert cov.tile_coverage_mode_id("accutile_sweep") == 1
-    assert cov.resolve_tile_coverage_mode_id("auto", cov.BASELINE_3DGS_COVERAGE) == 1
-    with pytest.raises(ValueError, match="resolved"):
-        cov.tile_coverage_mode_id("auto")
-    with pytest.raises(ValueError, match="footprint"):
-        cov.CoverageContract(footprint="typo", support=cov.SUPPORT_ALPHA_CUTOFF,
-                             sample_domain=cov.SAMPLE_PIXEL_CENTERS)
+    """gswarp's coverage policy contract for baseline 3DGS
+    (tests/test_tile_coverage.py:189-231, coverage.py:80-110): "auto" runs the
+    AccuTile sweep, the concrete names map to kernel modes 0/1/2, anything
+    else is a ValueError listing the four names."""
+    assert cov.POLICIES == ("auto", "snugbox", "accutile_sweep", "conic_rect")
+    assert cov.concrete("auto") == "accutile_sweep"
+    assert [cov.kernel_mode(m) for m in cov.POLICIES] == [1, 0, 1, 2]
+    with pytest.raises(ValueError, match="mode must be one of 'auto', 'snugbox', 'accutile_sweep', 'conic_rect'"):
+        cov.kernel_mode("bogus")
+    with pytest.raises(ValueError, match="mode must be one of"):
+        cov.check_policy("AUTO")
 
 
 def test_runtime_setters_and_snapshot():
@@ -112,8 +109,10 @@ def test_rasterizer_rejects_cpu_inputs():
 
 
 def test_tuning_api_compat():
-    assert gs.get_tuned_block_dim("render_forward") == 256
+    # the render kernels launch 128-thread CTAs (16x16 tile, two pixels per thread)
+    assert gs.get_tuned_block_dim("render_forward") == 128
     gs.register_kernel_class("custom", 32)
+    assert gs.get_tuned_block_dim("custom") == 256
     assert isinstance(gs.get_canonical_device("cpu"), str)
 
 
