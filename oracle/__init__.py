@@ -75,13 +75,13 @@ def _declare(L):
                              vp, c_ll, _i32p, vp]
     L.or_render_fwd.restype = None
     L.or_render_fwd.argtypes = [c_int, c_int, _i32p, _i32p, _f32p, _f32p, _f32p, _f32p, _f32p, c_int,
-                                _f32p, _f32p, _f32p, _i32p]
+                                _f32p, _f32p, _f32p, _i32p, vp, vp]
     L.or_render_flow_aux.restype = None
     L.or_render_flow_aux.argtypes = [c_int, c_int, _i32p, _i32p, _f32p, _f32p, c_int, _i32p, _f32p, _f32p]
     L.or_render_bwd.restype = None
     L.or_render_bwd.argtypes = [c_int, c_int, c_int, _i32p, _i32p, _f32p, _f32p, _f32p, _f32p, _f32p,
                                 _f32p, _i32p, _f32p, _f32p, _f32p, c_int,
-                                _f32p, _f32p, _f32p, _f32p, vp]
+                                _f32p, _f32p, _f32p, _f32p, vp, vp, c_float, vp]
     L.or_preprocess_bwd.restype = None
     L.or_preprocess_bwd.argtypes = (
         [c_int, _f32p, _i32p, vp, vp, c_float, vp, _f32p, _f32p] + [c_float] * 4
@@ -195,15 +195,25 @@ def binning(pre, W, H, mode=1):
     return point_list[:total], ranges, keys[:total]
 
 
-def render_fwd(W, H, ranges, point_list, xy, features, depths, conic_opacity, bg, compute_depth=True):
+def render_fwd(W, H, ranges, point_list, xy, features, depths, conic_opacity, bg, compute_depth=True,
+               with_margin=False):
+    """(color, depth, alpha, n_contrib), plus with ``with_margin`` two (H, W)
+    arrays: the per-pixel smallest relative margin of the pixel's thresholded
+    decisions (exponent sign, alpha >= 1/255, T*(1-alpha) < 1e-4) and the
+    largest absolute size of the exponent's terms among the pairs it blends."""
     npix = W * H
     color = np.zeros((3, H, W), np.float32)
     depth = np.zeros((1, H, W), np.float32)
     alpha = np.zeros((1, H, W), np.float32)
     n_contrib = np.zeros(npix, np.int32)
+    margin = np.ones((H, W), np.float32) if with_margin else None
+    cond = np.zeros((H, W), np.float32) if with_margin else None
     pl = _c(point_list, np.int32) if len(point_list) else np.zeros(1, np.int32)
     lib().or_render_fwd(W, H, _c(ranges, np.int32).reshape(-1), pl, _c(xy), _c(features), _c(depths),
-                        _c(conic_opacity), _c(bg), int(bool(compute_depth)), color, depth, alpha, n_contrib)
+                        _c(conic_opacity), _c(bg), int(bool(compute_depth)), color, depth, alpha, n_contrib,
+                        _opt(margin), _opt(cond))
+    if with_margin:
+        return color, depth, alpha, n_contrib, margin, cond
     return color, depth, alpha, n_contrib
 
 
@@ -220,20 +230,34 @@ def render_flow_aux(W, H, ranges, point_list, xy, conic_opacity, top_k):
 
 
 def render_bwd(W, H, P, ranges, point_list, xy, features, depths, conic_opacity, bg, out_alpha,
-               n_contrib, grad_color, grad_depth, grad_alpha, compute_depth=True, with_abs=False):
+               n_contrib, grad_color, grad_depth, grad_alpha, compute_depth=True, with_abs=False,
+               with_margin=False, flag_eps=None):
+    """Per-Gaussian render gradients; ``with_abs`` adds "abs" (P, 10), the
+    sum of |term| per gradient component (xy 2, depth, conic 4, rgb 3);
+    ``with_margin`` adds "margin" (H, W), the smallest relative margin of the
+    decisions the backward re-evaluates (exponent sign, alpha >= 1/255) over
+    each pixel's contributors; ``flag_eps`` adds "flagged_abs" (P, 10), the
+    part of "abs" that comes from pixels whose margin is below flag_eps."""
     g_xy = np.zeros((P, 2), np.float32)
     g_d = np.zeros(P, np.float32)
     g_co = np.zeros((P, 4), np.float32)
     g_rgb = np.zeros((P, 3), np.float32)
     g_abs = np.zeros((P, 10), np.float64) if with_abs else None
+    margin = np.ones((H, W), np.float32) if with_margin else None
+    flagged = np.zeros((P, 10), np.float64) if flag_eps is not None else None
     pl = _c(point_list, np.int32) if len(point_list) else np.zeros(1, np.int32)
     lib().or_render_bwd(W, H, P, _c(ranges, np.int32).reshape(-1), pl, _c(xy), _c(features), _c(depths),
                         _c(conic_opacity), _c(bg), _c(out_alpha).reshape(-1), _c(n_contrib, np.int32),
                         _c(grad_color).reshape(-1), _c(grad_depth).reshape(-1), _c(grad_alpha).reshape(-1),
-                        int(bool(compute_depth)), g_xy, g_d, g_co, g_rgb, _opt(g_abs))
+                        int(bool(compute_depth)), g_xy, g_d, g_co, g_rgb, _opt(g_abs), _opt(margin),
+                        float(flag_eps or 0.0), _opt(flagged))
     out = dict(grad_xy=g_xy, grad_depth=g_d, grad_conic_opacity=g_co, grad_rgb=g_rgb)
     if with_abs:
         out["abs"] = g_abs
+    if with_margin:
+        out["margin"] = margin
+    if flag_eps is not None:
+        out["flagged_abs"] = flagged
     return out
 
 

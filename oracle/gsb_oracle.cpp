@@ -600,14 +600,36 @@ OR_EXPORT long long or_binning(int P, const float* xy, const int* radii, const f
   return total;
 }
 
+// Relative distance of a pixel's thresholded decisions from their thresholds
+// (test instrumentation, not part of the reference's arithmetic): the sign
+// test of the exponent against the size of its terms, alpha >= 1/255 and
+// T*(1-alpha) < 1e-4.  An implementation whose exp or exponent rounding
+// differs by a relative d can decide a pair differently only where this is
+// below about d.
+inline float power_scale(float a, float b, float c, float dx, float dy) {
+  return 0.5f * (std::fabs(a) * dx * dx + std::fabs(c) * dy * dy) + std::fabs(b * dx * dy);
+}
+inline float power_margin(float power, float a, float b, float c, float dx, float dy) {
+  const float scale = power_scale(a, b, c, dx, dy);
+  return scale > 0.0f ? std::fabs(power) / scale : 1.0f;
+}
+inline float alpha_margin(float alpha) { return std::fabs(alpha - 1.0f / 255.0f) * 255.0f; }
+inline float trans_margin(float test_T) { return std::fabs(test_T - 0.0001f) * 10000.0f; }
+
 // ---------------------------------------------------------------------------
 // Render forward (render_kernels.py:15-147).  Integer pixel coordinates,
 // front-to-back, stop when T*(1-alpha) < 1e-4 without adding that pair.
+// margin (optional, per pixel): the smallest decision margin of the pairs the
+// pixel evaluates (see power_margin); cond (optional, per pixel): the largest
+// power_scale of the pairs it blends -- the absolute size of the terms whose
+// sum is the exponent, so rounding differences in the exponent are of order
+// eps * cond.
 // ---------------------------------------------------------------------------
 OR_EXPORT void or_render_fwd(int W, int H, const int* ranges, const int* point_list,
                              const float* xy, const float* features, const float* depths,
                              const float* conic_opacity, const float* bg, int compute_depth,
-                             float* out_color, float* out_depth, float* out_alpha, int* n_contrib) {
+                             float* out_color, float* out_depth, float* out_alpha, int* n_contrib,
+                             float* margin, float* cond) {
   const int grid_x = (W + BLOCK_X - 1) / BLOCK_X;
   const int grid_y = (H + BLOCK_Y - 1) / BLOCK_Y;
   const long long npix = (long long)W * H;
@@ -623,6 +645,7 @@ OR_EXPORT void or_render_fwd(int W, int H, const int* ranges, const int* point_l
       float T = 1.0f, c0 = 0, c1 = 0, c2 = 0, wsum = 0, dacc = 0;
       int contributor = 0, last = 0;
       float fx = (float)pxi, fy = (float)pyi;
+      float m = 1.0f, cd = 0.0f;
       for (int k = start; k < end; ++k) {
         contributor = contributor + 1;
         int id = point_list[k];
@@ -630,12 +653,16 @@ OR_EXPORT void or_render_fwd(int W, int H, const int* ranges, const int* point_l
         float d_x = xy[id * 2] - fx;
         float d_y = xy[id * 2 + 1] - fy;
         float power = -0.5f * (co[0] * d_x * d_x + co[2] * d_y * d_y) - co[1] * d_x * d_y;
+        if (margin) m = fmn(m, power_margin(power, co[0], co[1], co[2], d_x, d_y));
         if (power <= 0.0f) {
           float alpha = fmn(0.99f, co[3] * std::exp(power));
+          if (margin) m = fmn(m, alpha_margin(alpha));
           if (alpha >= (1.0f / 255.0f)) {
             float test_T = T * (1.0f - alpha);
+            if (margin) m = fmn(m, trans_margin(test_T));
             if (test_T < 0.0001f) break;
             float contribution = alpha * T;
+            if (cond) cd = fmx(cd, power_scale(co[0], co[1], co[2], d_x, d_y));
             c0 = c0 + features[id * 3 + 0] * contribution;
             c1 = c1 + features[id * 3 + 1] * contribution;
             c2 = c2 + features[id * 3 + 2] * contribution;
@@ -647,6 +674,8 @@ OR_EXPORT void or_render_fwd(int W, int H, const int* ranges, const int* point_l
         }
       }
       n_contrib[pix] = last;
+      if (margin) margin[pix] = m;
+      if (cond) cond[pix] = cd;
       out_color[pix] = c0 + T * bg[0];
       out_color[npix + pix] = c1 + T * bg[1];
       out_color[2 * npix + pix] = c2 + T * bg[2];
@@ -720,7 +749,11 @@ OR_EXPORT void or_render_flow_aux(int W, int H, const int* ranges, const int* po
 // recurrence.  Per-Gaussian gradients are reduced in double, tile by tile in
 // tile order, so the oracle is deterministic.  grad_abs (optional, 10 per G)
 // receives the sum of |term| of every accumulated contribution, for
-// condition-aware comparison against float atomics.
+// condition-aware comparison against float atomics.  Test instrumentation
+// (optional): margin, per pixel, the smallest decision margin of the pairs
+// the backward re-evaluates; flagged_abs (10 per G), the sum of |term| of the
+// contributions from pixels whose margin is below flag_eps -- the part of a
+// gradient that another exp implementation may decide differently.
 // Output layout per Gaussian: grad_xy[2], grad_depth[1], grad_co[4], grad_rgb[3].
 // ---------------------------------------------------------------------------
 OR_EXPORT void or_render_bwd(int W, int H, int P, const int* ranges, const int* point_list,
@@ -729,14 +762,15 @@ OR_EXPORT void or_render_bwd(int W, int H, int P, const int* ranges, const int* 
                              const int* n_contrib, const float* grad_color,
                              const float* grad_depth, const float* grad_alpha, int compute_depth,
                              float* grad_xy, float* grad_depths, float* grad_co, float* grad_rgb,
-                             double* grad_abs) {
+                             double* grad_abs, float* margin, float flag_eps, double* flagged_abs) {
   const int grid_x = (W + BLOCK_X - 1) / BLOCK_X;
   const int grid_y = (H + BLOCK_Y - 1) / BLOCK_Y;
   const int ntile = grid_x * grid_y;
   const long long npix = (long long)W * H;
   const float ddelx_dx = 0.5f * (float)W;
   const float ddely_dy = 0.5f * (float)H;
-  // per tile: list of (gaussian, 10 sums, 10 abs sums)
+  // per tile: list of (gaussian, 10 sums, 10 abs sums, 10 abs sums from flagged pixels)
+  constexpr int ACC = 30;
   std::vector<std::vector<double>> tile_acc(ntile);
 #pragma omp parallel for schedule(dynamic, 4)
   for (int tile = 0; tile < ntile; ++tile) {
@@ -745,13 +779,29 @@ OR_EXPORT void or_render_bwd(int W, int H, int P, const int* ranges, const int* 
     int n = end - start;
     if (n <= 0) continue;
     std::vector<double>& acc = tile_acc[tile];
-    acc.assign((size_t)n * 20, 0.0);
+    acc.assign((size_t)n * ACC, 0.0);
     for (int local = 0; local < BLOCK_X * BLOCK_Y; ++local) {
       int pxi = tx * BLOCK_X + local % BLOCK_X;
       int pyi = ty * BLOCK_Y + local / BLOCK_X;
       if (pxi >= W || pyi >= H) continue;
       long long pix = (long long)pyi * W + pxi;
       int lc = n_contrib[pix];
+      // with flagged_abs: this pixel's decision margin first (same decisions as below)
+      bool flagged = false;
+      if (flagged_abs) {
+        float pm = 1.0f;
+        for (int pos = lc - 1; pos >= 0; --pos) {
+          int id = point_list[start + pos];
+          const float* co = conic_opacity + id * 4;
+          float d_x = xy[id * 2] - (float)pxi;
+          float d_y = xy[id * 2 + 1] - (float)pyi;
+          float power = -0.5f * (co[0] * d_x * d_x + co[2] * d_y * d_y) - co[1] * d_x * d_y;
+          pm = fmn(pm, power_margin(power, co[0], co[1], co[2], d_x, d_y));
+          if (power > 0.0f) continue;
+          pm = fmn(pm, alpha_margin(fmn(0.99f, co[3] * std::exp(power))));
+        }
+        flagged = pm < flag_eps;
+      }
       float T_final = 1.0f - out_alpha[pix];
       float T = T_final;
       float g0 = grad_color[pix], g1 = grad_color[npix + pix], g2 = grad_color[2 * npix + pix];
@@ -760,38 +810,50 @@ OR_EXPORT void or_render_bwd(int W, int H, int P, const int* ranges, const int* 
       float bg_dot = bg[0] * g0 + bg[1] * g1 + bg[2] * g2;
       float ar0 = 0, ar1 = 0, ar2 = 0, adr = 0, aar = 0, la = 0, lc0 = 0, lc1 = 0, lc2 = 0, ld = 0;
       float fx = (float)pxi, fy = (float)pyi;
+      float m = 1.0f;
       for (int pos = lc - 1; pos >= 0; --pos) {
         int id = point_list[start + pos];
         const float* co = conic_opacity + id * 4;
         float d_x = xy[id * 2] - fx;
         float d_y = xy[id * 2 + 1] - fy;
         float power = -0.5f * (co[0] * d_x * d_x + co[2] * d_y * d_y) - co[1] * d_x * d_y;
-        if (power > 0.0f) continue;
+        const float pmg = power_margin(power, co[0], co[1], co[2], d_x, d_y);
+        if (margin) m = fmn(m, pmg);
+        // In a flagged pixel, a pair skipped by a decision within flag_eps of
+        // its threshold may be taken by another exp implementation: its terms
+        // are evaluated as if taken and counted in flagged_abs only (the
+        // pixel's state is not advanced).
+        if (power > 0.0f && !(flagged && pmg < flag_eps)) continue;
         float G = std::exp(power);
         float alpha = fmn(0.99f, co[3] * std::exp(power));
-        if (!(alpha >= (1.0f / 255.0f))) continue;
+        if (margin) m = fmn(m, alpha_margin(alpha));
+        const bool take = power <= 0.0f && alpha >= (1.0f / 255.0f);
+        if (!take && !(flagged && (pmg < flag_eps || alpha_margin(alpha) < flag_eps))) continue;
+        // working copy of the back-to-front state, committed when the pair is taken
+        float nT = T, nar0 = ar0, nar1 = ar1, nar2 = ar2, nadr = adr, naar = aar, nla = la, nld = ld;
+        float nlc0 = lc0, nlc1 = lc1, nlc2 = lc2;
         float oma = fmx(1.0f - alpha, ONE_MINUS_ALPHA_MIN);
-        T = T / oma;
-        float dchannel = alpha * T;
+        nT = nT / oma;
+        float dchannel = alpha * nT;
         float cr = features[id * 3], cg = features[id * 3 + 1], cb = features[id * 3 + 2];
-        ar0 = la * lc0 + (1.0f - la) * ar0;
-        ar1 = la * lc1 + (1.0f - la) * ar1;
-        ar2 = la * lc2 + (1.0f - la) * ar2;
-        lc0 = cr; lc1 = cg; lc2 = cb;
-        float dL_dopa = (cr - ar0) * g0 + (cg - ar1) * g1 + (cb - ar2) * g2;
+        nar0 = nla * nlc0 + (1.0f - nla) * nar0;
+        nar1 = nla * nlc1 + (1.0f - nla) * nar1;
+        nar2 = nla * nlc2 + (1.0f - nla) * nar2;
+        nlc0 = cr; nlc1 = cg; nlc2 = cb;
+        float dL_dopa = (cr - nar0) * g0 + (cg - nar1) * g1 + (cb - nar2) * g2;
         float gf0 = dchannel * g0, gf1 = dchannel * g1, gf2 = dchannel * g2;
         float gdep = 0.0f;
         if (compute_depth) {
           float dv = depths[id];
-          adr = la * ld + (1.0f - la) * adr;
-          ld = dv;
-          dL_dopa = dL_dopa + (dv - adr) * gd;
+          nadr = nla * nld + (1.0f - nla) * nadr;
+          nld = dv;
+          dL_dopa = dL_dopa + (dv - nadr) * gd;
           gdep = dchannel * gd;
         }
-        aar = la + (1.0f - la) * aar;
-        dL_dopa = dL_dopa + (1.0f - aar) * ga;
-        dL_dopa = dL_dopa * T;
-        la = alpha;
+        naar = nla + (1.0f - nla) * naar;
+        dL_dopa = dL_dopa + (1.0f - naar) * ga;
+        dL_dopa = dL_dopa * nT;
+        nla = alpha;
         dL_dopa = dL_dopa + (-T_final / oma) * bg_dot;
         float dL_dG = co[3] * dL_dopa;
         float gdx = G * d_x, gdy = G * d_y;
@@ -806,25 +868,35 @@ OR_EXPORT void or_render_bwd(int W, int H, int P, const int* ranges, const int* 
         v[5] = -0.5f * gdy * d_y * dL_dG;
         v[6] = G * dL_dopa;
         v[7] = gf0; v[8] = gf1; v[9] = gf2;
-        double* a = &acc[(size_t)pos * 20];
+        double* a = &acc[(size_t)pos * ACC];
+        if (!take) {
+          for (int k = 0; k < 10; ++k) a[20 + k] += std::fabs((double)v[k]);
+          continue;
+        }
+        T = nT; ar0 = nar0; ar1 = nar1; ar2 = nar2; adr = nadr; aar = naar; la = nla; ld = nld;
+        lc0 = nlc0; lc1 = nlc1; lc2 = nlc2;
         for (int k = 0; k < 10; ++k) {
           a[k] += (double)v[k];
           a[10 + k] += std::fabs((double)v[k]);
+          if (flagged) a[20 + k] += std::fabs((double)v[k]);
         }
       }
+      if (margin) margin[pix] = m;
     }
   }
   std::vector<double> sum((size_t)P * 10, 0.0), abs_sum((size_t)P * 10, 0.0);
+  if (flagged_abs) std::fill(flagged_abs, flagged_abs + (size_t)P * 10, 0.0);
   for (int tile = 0; tile < ntile; ++tile) {
     const std::vector<double>& acc = tile_acc[tile];
     if (acc.empty()) continue;
     int start = ranges[2 * tile];
-    int n = (int)(acc.size() / 20);
+    int n = (int)(acc.size() / ACC);
     for (int pos = 0; pos < n; ++pos) {
       int id = point_list[start + pos];
       for (int k = 0; k < 10; ++k) {
-        sum[(size_t)id * 10 + k] += acc[(size_t)pos * 20 + k];
-        abs_sum[(size_t)id * 10 + k] += acc[(size_t)pos * 20 + 10 + k];
+        sum[(size_t)id * 10 + k] += acc[(size_t)pos * ACC + k];
+        abs_sum[(size_t)id * 10 + k] += acc[(size_t)pos * ACC + 10 + k];
+        if (flagged_abs) flagged_abs[(size_t)id * 10 + k] += acc[(size_t)pos * ACC + 20 + k];
       }
     }
   }

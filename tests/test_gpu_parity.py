@@ -6,13 +6,11 @@ stage fed identical inputs:
   binary32 expressions without contraction);
 * binning: point list and tile ranges bit-exact (canonical order
   (tile, depth bits, point index));
-* render forward: colour/alpha/depth within rtol 1e-4 / atol 1e-5 and
-  n_contrib equal, except at pixels where an alpha-threshold decision sits
-  within float rounding of 1/255 or 1e-4 (the kernel uses the hardware exp);
-  such pixels are bounded in number and in effect;
-* render backward: per-Gaussian gradients within rtol 1e-4 of the oracle's
-  float64 reduction plus the float32 rounding bound of the summation
-  (atomics reorder it), on the same forward state;
+* render forward and backward: the margin rule of tests/render_parity.py --
+  rtol 1e-4 / atol 1e-5 everywhere except at pixels whose thresholded
+  decisions sit within 1e-5 (relative) of their thresholds, with no other
+  exceptions; gradients may exceed their tolerance only by what such pixels
+  contribute;
 * preprocess backward: bit-exact given the same render gradients.
 """
 
@@ -21,6 +19,7 @@ import pytest
 import torch
 
 import oracle
+import render_parity as rp
 from gswarp_b200 import _pipeline as pl
 from gswarp_b200 import workloads as wl
 
@@ -158,32 +157,19 @@ def _render_case(name, dev):
     bg = torch.tensor([0.1, 0.2, 0.3], device=dev)
     ren = pl.render(pre, binned, cam, bg, True)
     torch.cuda.synchronize()
-    rec = _np(pre.records)
-    inputs = dict(ranges=_np(binned.ranges), point_list=_np(binned.point_list), xy=rec[:, 0:2].copy(),
-                  features=rec[:, 8:11].copy(), depths=rec[:, 6].copy(),
-                  conic_opacity=np.concatenate([rec[:, 2:4], rec[:, 4:6]], 1).copy(), bg=_np(bg))
+    inputs = rp.forward_inputs(_np(pre.records), _np(binned.ranges), _np(binned.point_list), _np(bg))
     return scene, view, g, cam, pre, binned, ren, bg, inputs
 
 
-def _frac_bad(got, ref, atol=1e-5, rtol=1e-4):
-    return float(np.mean(np.abs(got - ref) > atol + rtol * np.abs(ref)))
-
-
-@pytest.mark.parametrize("name", ["cfg1", "cfg2_200k"])
+@pytest.mark.parametrize("name", ["cfg1", "cfg2_200k", "cfg2_small_view", "cfg2_big_footprints"])
 def test_render_forward_matches_oracle(cuda, name):
     scene, view, g, cam, pre, binned, ren, bg, inp = _render_case(name, cuda)
     W, H = view.width, view.height
-    col, dep, alp, nc = oracle.render_fwd(W, H, inp["ranges"], inp["point_list"], inp["xy"], inp["features"],
-                                          inp["depths"], inp["conic_opacity"], inp["bg"], True)
-    gnc = _np(ren.n_contrib)
-    assert np.mean(gnc != nc) <= 1e-3
-    for got, ref in ((_np(ren.color), col), (_np(ren.alpha), alp), (_np(ren.depth), dep)):
-        assert _frac_bad(got, ref) <= 2e-3
-        assert np.max(np.abs(got - ref)) <= 0.05 * max(1.0, float(np.abs(ref).max()))
+    _, _, alp, _ = rp.check_forward(W, H, inp, _np(ren.color), _np(ren.depth), _np(ren.alpha), _np(ren.n_contrib))
     assert float(alp.mean()) > 0.01
 
 
-@pytest.mark.parametrize("name", ["cfg1", "cfg2_200k"])
+@pytest.mark.parametrize("name", ["cfg1", "cfg2_200k", "cfg2_small_view", "cfg2_big_footprints"])
 def test_render_backward_matches_oracle(cuda, name):
     scene, view, g, cam, pre, binned, ren, bg, inp = _render_case(name, cuda)
     W, H, P = view.width, view.height, scene.n
@@ -194,21 +180,8 @@ def test_render_backward_matches_oracle(cuda, name):
     grad_acc = pl.render_backward(pre.records, binned, cam, bg, ren.alpha, ren.n_contrib, gcol.to(cuda),
                                   gdep.to(cuda), galp.to(cuda), True, P)
     torch.cuda.synchronize()
-    ref = oracle.render_bwd(W, H, P, inp["ranges"], inp["point_list"], inp["xy"], inp["features"], inp["depths"],
-                            inp["conic_opacity"], inp["bg"], _np(ren.alpha), _np(ren.n_contrib), gcol.numpy(),
-                            gdep.numpy(), galp.numpy(), True, with_abs=True)
-    ga = _np(grad_acc)
-    got = np.concatenate([ga[:, 0:3], ga[:, 4:8], ga[:, 8:11]], 1)
-    want = np.concatenate([ref["grad_xy"], ref["grad_depth"][:, None], ref["grad_conic_opacity"], ref["grad_rgb"]], 1)
-    absum = ref["abs"]
-    # float32 summation bound for the reordered atomics + per-term rounding
-    tol = 1e-4 * np.abs(want) + 2e-6 * absum + 1e-7
-    bad = np.abs(got - want) > tol
-    assert bad.mean() <= 5e-3, f"{bad.sum()} of {bad.size} gradient entries outside tolerance"
-    for k in range(10):
-        num = np.linalg.norm(got[:, k] - want[:, k])
-        den = np.linalg.norm(want[:, k]) + 1e-30
-        assert num / den <= 2e-3, (k, num / den)
+    rp.check_backward(W, H, P, inp, _np(ren.alpha), _np(ren.n_contrib), gcol.numpy(), gdep.numpy(), galp.numpy(),
+                      rp.gpu_grads(_np(grad_acc)))
 
 
 @pytest.mark.parametrize("name", ["cfg1", "cfg2_200k"])
