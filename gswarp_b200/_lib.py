@@ -24,7 +24,7 @@ GSB_ERR_OVERFLOW = -2
 GSB_ERR_CUDA = -3
 GSB_ERR_TIMEOUT = -4
 
-ABI_VERSION = 14
+ABI_VERSION = 15
 RECORD_FLOATS = 12
 GRAD_FLOATS = 12
 
@@ -177,7 +177,7 @@ EXPORTED = (
     "gsb_ssim_partials_count", "gsb_ssim_fwd", "gsb_ssim_bwd", "gsb_knn_workspace_bytes",
     "gsb_knn", "gsb_selftest_threshold_log", "gsb_ssim_fwd_noalloc", "gsb_photo_loss_fwd",
     "gsb_photo_loss_bwd", "gsb_adam_step", "gsb_densify_stats", "gsb_sh_colors_views",
-    "gsb_sh_backward_views", "gsb_block_dim",
+    "gsb_sh_backward_views", "gsb_block_dim", "gsb_peak_fp32", "gsb_peak_ex2", "gsb_peak_work",
 )
 
 
@@ -191,6 +191,9 @@ def _declare(L) -> None:
     fn("gsb_abi_version", c_int, [])
     fn("gsb_last_error", ctypes.c_char_p, [])
     fn("gsb_block_dim", c_int, [ctypes.c_char_p])
+    fn("gsb_peak_fp32", c_int, [c_int, c_int, vp, vp])
+    fn("gsb_peak_ex2", c_int, [c_int, c_int, vp, vp])
+    fn("gsb_peak_work", c_ll, [c_int, c_int, c_int])
     fn("gsb_preprocess_fwd", c_int, [P(PreprocessArgs), vp])
     fn("gsb_mark_visible", c_int, [c_int, vp, vp, vp, vp])
     fn("gsb_bin_count_workspace_bytes", ctypes.c_size_t, [c_int])

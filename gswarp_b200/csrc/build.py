@@ -28,7 +28,7 @@ COMMON = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-fvisibility=hi
 # Units that must reproduce the oracle's IEEE binary32 arithmetic exactly.
 NO_FMA = {"preprocess.cu", "binning.cu", "preprocess_bwd.cu", "knn.cu"}
 SOURCES = ["capi.cu", "preprocess.cu", "binning.cu", "render.cu", "preprocess_bwd.cu", "sh_views.cu",
-           "ssim.cu", "knn.cu", "optim.cu"]
+           "ssim.cu", "knn.cu", "optim.cu", "peaks.cu"]
 
 
 def nvcc() -> str:

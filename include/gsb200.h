@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define GSB_ABI_VERSION 14
+#define GSB_ABI_VERSION 15
 
 #define GSB_OK 0
 #define GSB_ERR_INVALID (-1)  /* bad argument: ValueError in Python          */
@@ -67,6 +67,16 @@ const char* gsb_last_error(void);
  * ssim_fwd_v, ssim_bwd_h, ssim_bwd_v), knn_morton, knn_gather,
  * knn_box_minmax, knn_box_dist, knn_search, adam. */
 int gsb_block_dim(const char* kernel_class);
+
+/* Measurement microkernels (no counterpart in the reference; used by the
+ * benchmark for the compute roofline of the render kernels).  gsb_peak_fp32
+ * runs packed f32x2 fused multiply-adds, gsb_peak_ex2 MUFU ex2.approx, in
+ * `blocks` CTAs of independent chains for `iters` iterations; `out` (blocks
+ * floats) only keeps the results live.  gsb_peak_work returns one launch's
+ * FLOP (which = 0) or ex2 evaluations (which = 1). */
+int gsb_peak_fp32(int blocks, int iters, float* out, void* stream);
+int gsb_peak_ex2(int blocks, int iters, float* out, void* stream);
+long long gsb_peak_work(int which, int blocks, int iters);
 
 /* ------------------------------------------------------------------------ */
 /* Preprocess forward.  Replaces preprocess_gaussians                        */

@@ -104,6 +104,8 @@ def _declare(L):
     L.or_knn_bruteforce.argtypes = [c_int, _f32p, _f32p]
     L.or_num_threads.restype = c_int
     L.or_num_threads.argtypes = []
+    L.or_set_num_threads.restype = None
+    L.or_set_num_threads.argtypes = [c_int]
 
 
 def _c(a, dtype=np.float32):
@@ -112,6 +114,13 @@ def _c(a, dtype=np.float32):
 
 def num_threads() -> int:
     return int(lib().or_num_threads())
+
+
+def set_num_threads(n: int) -> int:
+    """Sets the oracle's OpenMP thread count (overriding OMP_NUM_THREADS) and
+    returns the count now in effect."""
+    lib().or_set_num_threads(int(n))
+    return num_threads()
 
 
 def count_tiles(px, py, cov_aa, cov_cc, ca, cb, cc, opacity, radius, grid_x, grid_y, mode=1) -> int:

@@ -41,6 +41,7 @@
 
 #ifdef _OPENMP
 #include <omp.h>
+#include <parallel/algorithm>
 #endif
 
 #define OR_EXPORT extern "C" __attribute__((visibility("default")))
@@ -565,26 +566,37 @@ OR_EXPORT long long or_binning(int P, const float* xy, const int* radii, const f
   const int grid_x = (W + BLOCK_X - 1) / BLOCK_X;
   const int grid_y = (H + BLOCK_Y - 1) / BLOCK_Y;
   const int T = grid_x * grid_y;
-  long long total = 0;
-  for (int i = 0; i < P; ++i) total += tiles_touched[i];
+  // pair slots of each Gaussian: exclusive prefix sum of tiles_touched
+  std::vector<long long> offset((size_t)P + 1, 0);
+  for (int i = 0; i < P; ++i) offset[i + 1] = offset[i] + tiles_touched[i];
+  const long long total = offset[P];
   if (cap < total) return total;
   struct Pair { uint32_t tile; uint32_t depth; uint32_t idx; };
-  std::vector<Pair> pairs;
-  pairs.reserve((size_t)total);
-  std::vector<int> e;
-  for (int i = 0; i < P; ++i) {
-    if (radii[i] <= 0) continue;
-    e.clear();
-    const float* co = conic_opacity + i * 4;
-    const float* cv = conic_2d_inv + i * 3;
-    cover_tiles(xy[i * 2], xy[i * 2 + 1], cv[0], cv[2], co[0], co[1], co[2], co[3], radii[i],
-                grid_x, grid_y, mode, &e);
-    uint32_t db;
-    std::memcpy(&db, &depths[i], 4);
-    for (int t : e) pairs.push_back(Pair{(uint32_t)t, db, (uint32_t)i});
+  std::vector<Pair> pairs((size_t)total);
+  int mismatch = 0;
+#pragma omp parallel reduction(| : mismatch)
+  {
+    std::vector<int> e;
+#pragma omp for schedule(dynamic, 4096)
+    for (int i = 0; i < P; ++i) {
+      if (radii[i] <= 0) continue;
+      e.clear();
+      const float* co = conic_opacity + i * 4;
+      const float* cv = conic_2d_inv + i * 3;
+      cover_tiles(xy[i * 2], xy[i * 2 + 1], cv[0], cv[2], co[0], co[1], co[2], co[3], radii[i],
+                  grid_x, grid_y, mode, &e);
+      if ((long long)e.size() != tiles_touched[i]) {
+        mismatch = 1;
+        continue;
+      }
+      uint32_t db;
+      std::memcpy(&db, &depths[i], 4);
+      for (size_t k = 0; k < e.size(); ++k) pairs[(size_t)offset[i] + k] = Pair{(uint32_t)e[k], db, (uint32_t)i};
+    }
   }
-  if ((long long)pairs.size() != total) return -1;  // count/emit disagreement
-  std::sort(pairs.begin(), pairs.end(), [](const Pair& a, const Pair& b) {
+  if (mismatch) return -1;  // count/emit disagreement
+  // (tile, depth bits, index) is a total order on the pairs: any correct sort gives the same list
+  __gnu_parallel::sort(pairs.begin(), pairs.end(), [](const Pair& a, const Pair& b) {
     if (a.tile != b.tile) return a.tile < b.tile;
     if (a.depth != b.depth) return a.depth < b.depth;
     return a.idx < b.idx;
@@ -769,17 +781,26 @@ OR_EXPORT void or_render_bwd(int W, int H, int P, const int* ranges, const int* 
   const long long npix = (long long)W * H;
   const float ddelx_dx = 0.5f * (float)W;
   const float ddely_dy = 0.5f * (float)H;
-  // per tile: list of (gaussian, 10 sums, 10 abs sums, 10 abs sums from flagged pixels)
-  constexpr int ACC = 30;
-  std::vector<std::vector<double>> tile_acc(ntile);
+  // per tile and list position: 10 sums, then (if asked for) 10 sums of |term| and 10 sums of
+  // |term| from flagged pixels
+  const int OFF_ABS = 10, OFF_FLAG = grad_abs ? 20 : 10;
+  const int ACC = 10 + (grad_abs ? 10 : 0) + (flagged_abs ? 10 : 0);
+  // One slot of ACC doubles per entry of the point list (tile lists are
+  // contiguous in it), in a grow-only buffer kept across calls; each tile's
+  // slots are zeroed by the thread that fills them.
+  long long R = 0;
+  for (int tile = 0; tile < ntile; ++tile) R = std::max<long long>(R, ranges[2 * tile + 1]);
+  static std::vector<double> g_acc;
+  if (g_acc.size() < (size_t)R * ACC) g_acc.resize((size_t)R * ACC);
+  double* const acc_all = g_acc.data();
 #pragma omp parallel for schedule(dynamic, 4)
   for (int tile = 0; tile < ntile; ++tile) {
     int tx = tile % grid_x, ty = tile / grid_x;
     int start = ranges[2 * tile], end = ranges[2 * tile + 1];
     int n = end - start;
     if (n <= 0) continue;
-    std::vector<double>& acc = tile_acc[tile];
-    acc.assign((size_t)n * ACC, 0.0);
+    double* const acc = acc_all + (size_t)start * ACC;
+    std::fill(acc, acc + (size_t)n * ACC, 0.0);
     for (int local = 0; local < BLOCK_X * BLOCK_Y; ++local) {
       int pxi = tx * BLOCK_X + local % BLOCK_X;
       int pyi = ty * BLOCK_Y + local / BLOCK_X;
@@ -817,15 +838,17 @@ OR_EXPORT void or_render_bwd(int W, int H, int P, const int* ranges, const int* 
         float d_x = xy[id * 2] - fx;
         float d_y = xy[id * 2 + 1] - fy;
         float power = -0.5f * (co[0] * d_x * d_x + co[2] * d_y * d_y) - co[1] * d_x * d_y;
-        const float pmg = power_margin(power, co[0], co[1], co[2], d_x, d_y);
+        const float pmg = (margin || flagged) ? power_margin(power, co[0], co[1], co[2], d_x, d_y) : 1.0f;
         if (margin) m = fmn(m, pmg);
         // In a flagged pixel, a pair skipped by a decision within flag_eps of
         // its threshold may be taken by another exp implementation: its terms
         // are evaluated as if taken and counted in flagged_abs only (the
         // pixel's state is not advanced).
         if (power > 0.0f && !(flagged && pmg < flag_eps)) continue;
+        // G = exp(power) and alpha = min(0.99, op * exp(power)) (backward_kernels.py:629-630):
+        // one evaluation serves both, the same value
         float G = std::exp(power);
-        float alpha = fmn(0.99f, co[3] * std::exp(power));
+        float alpha = fmn(0.99f, co[3] * G);
         if (margin) m = fmn(m, alpha_margin(alpha));
         const bool take = power <= 0.0f && alpha >= (1.0f / 255.0f);
         if (!take && !(flagged && (pmg < flag_eps || alpha_margin(alpha) < flag_eps))) continue;
@@ -868,35 +891,50 @@ OR_EXPORT void or_render_bwd(int W, int H, int P, const int* ranges, const int* 
         v[5] = -0.5f * gdy * d_y * dL_dG;
         v[6] = G * dL_dopa;
         v[7] = gf0; v[8] = gf1; v[9] = gf2;
-        double* a = &acc[(size_t)pos * ACC];
+        double* a = acc + (size_t)pos * ACC;
         if (!take) {
-          for (int k = 0; k < 10; ++k) a[20 + k] += std::fabs((double)v[k]);
+          for (int k = 0; k < 10; ++k) a[OFF_FLAG + k] += std::fabs((double)v[k]);
           continue;
         }
         T = nT; ar0 = nar0; ar1 = nar1; ar2 = nar2; adr = nadr; aar = naar; la = nla; ld = nld;
         lc0 = nlc0; lc1 = nlc1; lc2 = nlc2;
-        for (int k = 0; k < 10; ++k) {
-          a[k] += (double)v[k];
-          a[10 + k] += std::fabs((double)v[k]);
-          if (flagged) a[20 + k] += std::fabs((double)v[k]);
-        }
+        for (int k = 0; k < 10; ++k) a[k] += (double)v[k];
+        if (grad_abs)
+          for (int k = 0; k < 10; ++k) a[OFF_ABS + k] += std::fabs((double)v[k]);
+        if (flagged)
+          for (int k = 0; k < 10; ++k) a[OFF_FLAG + k] += std::fabs((double)v[k]);
       }
       if (margin) margin[pix] = m;
     }
   }
-  std::vector<double> sum((size_t)P * 10, 0.0), abs_sum((size_t)P * 10, 0.0);
-  if (flagged_abs) std::fill(flagged_abs, flagged_abs + (size_t)P * 10, 0.0);
-  for (int tile = 0; tile < ntile; ++tile) {
-    const std::vector<double>& acc = tile_acc[tile];
-    if (acc.empty()) continue;
-    int start = ranges[2 * tile];
-    int n = (int)(acc.size() / ACC);
-    for (int pos = 0; pos < n; ++pos) {
-      int id = point_list[start + pos];
-      for (int k = 0; k < 10; ++k) {
-        sum[(size_t)id * 10 + k] += acc[(size_t)pos * ACC + k];
-        abs_sum[(size_t)id * 10 + k] += acc[(size_t)pos * ACC + 10 + k];
-        if (flagged_abs) flagged_abs[(size_t)id * 10 + k] += acc[(size_t)pos * ACC + 20 + k];
+  // Per-Gaussian totals, tile by tile in tile order (deterministic); each thread owns a range of
+  // Gaussian ids and walks the whole list.
+  static std::vector<double> g_sum, g_abs;
+  if (g_sum.size() < (size_t)P * 10) g_sum.resize((size_t)P * 10);
+  if (grad_abs && g_abs.size() < (size_t)P * 10) g_abs.resize((size_t)P * 10);
+  double* const sum = g_sum.data();
+  double* const abs_sum = g_abs.data();
+#pragma omp parallel
+  {
+    const int nth = omp_get_num_threads(), th = omp_get_thread_num();
+    const long long lo_id = (long long)P * th / nth, hi_id = (long long)P * (th + 1) / nth;
+    std::fill(sum + lo_id * 10, sum + hi_id * 10, 0.0);
+    if (grad_abs) std::fill(abs_sum + lo_id * 10, abs_sum + hi_id * 10, 0.0);
+    if (flagged_abs) std::fill(flagged_abs + lo_id * 10, flagged_abs + hi_id * 10, 0.0);
+    for (int tile = 0; tile < ntile; ++tile) {
+      const int start = ranges[2 * tile];
+      const int n = ranges[2 * tile + 1] - start;
+      if (n <= 0) continue;
+      const double* const acc = acc_all + (size_t)start * ACC;
+      for (int pos = 0; pos < n; ++pos) {
+        const int id = point_list[start + pos];
+        if (id < lo_id || id >= hi_id) continue;
+        const double* a = &acc[(size_t)pos * ACC];
+        for (int k = 0; k < 10; ++k) sum[(size_t)id * 10 + k] += a[k];
+        if (grad_abs)
+          for (int k = 0; k < 10; ++k) abs_sum[(size_t)id * 10 + k] += a[OFF_ABS + k];
+        if (flagged_abs)
+          for (int k = 0; k < 10; ++k) flagged_abs[(size_t)id * 10 + k] += a[OFF_FLAG + k];
       }
     }
   }
@@ -1650,5 +1688,15 @@ OR_EXPORT int or_num_threads() {
   return omp_get_max_threads();
 #else
   return 1;
+#endif
+}
+
+// Thread count of the following parallel regions (overrides OMP_NUM_THREADS,
+// which launchers such as torchrun set to 1).
+OR_EXPORT void or_set_num_threads(int n) {
+#ifdef _OPENMP
+  if (n > 0) omp_set_num_threads(n);
+#else
+  (void)n;
 #endif
 }
