@@ -21,6 +21,8 @@ __global__ void __launch_bounds__(PEAK_THREADS) fp32_peak_kernel(int iters, floa
   for (int k = 0; k < CHAINS; ++k) a[k] = make_float2(seed + threadIdx.x * 1e-3f + k, seed - k * 1e-3f);
   const float2 m = make_float2(0.9999999f, 0.9999998f);
   const float2 c = make_float2(1.0e-7f, 2.0e-7f);
+  // unrolled so the loop counter and branch are a small share of the issue slots
+#pragma unroll 16
   for (int i = 0; i < iters; ++i) {
 #pragma unroll
     for (int k = 0; k < CHAINS; ++k) a[k] = __ffma2_rn(a[k], m, c);
@@ -42,6 +44,7 @@ __global__ void __launch_bounds__(PEAK_THREADS) ex2_peak_kernel(int iters, float
   float a[CHAINS];
 #pragma unroll
   for (int k = 0; k < CHAINS; ++k) a[k] = seed + threadIdx.x * 1e-4f + k * 1e-3f;
+#pragma unroll 16
   for (int i = 0; i < iters; ++i) {
 #pragma unroll
     for (int k = 0; k < CHAINS; ++k) a[k] = ex2_approx_ftz(-a[k]);

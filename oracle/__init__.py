@@ -81,7 +81,7 @@ def _declare(L):
     L.or_render_bwd.restype = None
     L.or_render_bwd.argtypes = [c_int, c_int, c_int, _i32p, _i32p, _f32p, _f32p, _f32p, _f32p, _f32p,
                                 _f32p, _i32p, _f32p, _f32p, _f32p, c_int,
-                                _f32p, _f32p, _f32p, _f32p, vp, vp, c_float, vp]
+                                _f32p, _f32p, _f32p, _f32p, vp, vp, c_float, vp, vp]
     L.or_preprocess_bwd.restype = None
     L.or_preprocess_bwd.argtypes = (
         [c_int, _f32p, _i32p, vp, vp, c_float, vp, _f32p, _f32p] + [c_float] * 4
@@ -242,7 +242,9 @@ def render_bwd(W, H, P, ranges, point_list, xy, features, depths, conic_opacity,
                n_contrib, grad_color, grad_depth, grad_alpha, compute_depth=True, with_abs=False,
                with_margin=False, flag_eps=None):
     """Per-Gaussian render gradients; ``with_abs`` adds "abs" (P, 10), the
-    sum of |term| per gradient component (xy 2, depth, conic 4, rgb 3);
+    sum of |term| per gradient component (xy 2, depth, conic 4, rgb 3), and
+    "cond_abs" (P, 10), the sum of |term| times the absolute size of the
+    term's exponent terms (its sensitivity to rounding in the exponent);
     ``with_margin`` adds "margin" (H, W), the smallest relative margin of the
     decisions the backward re-evaluates (exponent sign, alpha >= 1/255) over
     each pixel's contributors; ``flag_eps`` adds "flagged_abs" (P, 10), the
@@ -254,15 +256,17 @@ def render_bwd(W, H, P, ranges, point_list, xy, features, depths, conic_opacity,
     g_abs = np.zeros((P, 10), np.float64) if with_abs else None
     margin = np.ones((H, W), np.float32) if with_margin else None
     flagged = np.zeros((P, 10), np.float64) if flag_eps is not None else None
+    cond = np.zeros((P, 10), np.float64) if with_abs else None
     pl = _c(point_list, np.int32) if len(point_list) else np.zeros(1, np.int32)
     lib().or_render_bwd(W, H, P, _c(ranges, np.int32).reshape(-1), pl, _c(xy), _c(features), _c(depths),
                         _c(conic_opacity), _c(bg), _c(out_alpha).reshape(-1), _c(n_contrib, np.int32),
                         _c(grad_color).reshape(-1), _c(grad_depth).reshape(-1), _c(grad_alpha).reshape(-1),
                         int(bool(compute_depth)), g_xy, g_d, g_co, g_rgb, _opt(g_abs), _opt(margin),
-                        float(flag_eps or 0.0), _opt(flagged))
+                        float(flag_eps or 0.0), _opt(flagged), _opt(cond))
     out = dict(grad_xy=g_xy, grad_depth=g_d, grad_conic_opacity=g_co, grad_rgb=g_rgb)
     if with_abs:
         out["abs"] = g_abs
+        out["cond_abs"] = cond
     if with_margin:
         out["margin"] = margin
     if flag_eps is not None:

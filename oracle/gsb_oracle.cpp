@@ -765,7 +765,10 @@ OR_EXPORT void or_render_flow_aux(int W, int H, const int* ranges, const int* po
 // (optional): margin, per pixel, the smallest decision margin of the pairs
 // the backward re-evaluates; flagged_abs (10 per G), the sum of |term| of the
 // contributions from pixels whose margin is below flag_eps -- the part of a
-// gradient that another exp implementation may decide differently.
+// gradient that another exp implementation may decide differently; cond_abs
+// (10 per G), the sum of |term| * power_scale over the taken pairs -- each
+// term's sensitivity to rounding in its exponent, which is of order eps times
+// the size of the exponent's terms.
 // Output layout per Gaussian: grad_xy[2], grad_depth[1], grad_co[4], grad_rgb[3].
 // ---------------------------------------------------------------------------
 OR_EXPORT void or_render_bwd(int W, int H, int P, const int* ranges, const int* point_list,
@@ -774,7 +777,8 @@ OR_EXPORT void or_render_bwd(int W, int H, int P, const int* ranges, const int* 
                              const int* n_contrib, const float* grad_color,
                              const float* grad_depth, const float* grad_alpha, int compute_depth,
                              float* grad_xy, float* grad_depths, float* grad_co, float* grad_rgb,
-                             double* grad_abs, float* margin, float flag_eps, double* flagged_abs) {
+                             double* grad_abs, float* margin, float flag_eps, double* flagged_abs,
+                             double* cond_abs) {
   const int grid_x = (W + BLOCK_X - 1) / BLOCK_X;
   const int grid_y = (H + BLOCK_Y - 1) / BLOCK_Y;
   const int ntile = grid_x * grid_y;
@@ -783,8 +787,9 @@ OR_EXPORT void or_render_bwd(int W, int H, int P, const int* ranges, const int* 
   const float ddely_dy = 0.5f * (float)H;
   // per tile and list position: 10 sums, then (if asked for) 10 sums of |term| and 10 sums of
   // |term| from flagged pixels
-  const int OFF_ABS = 10, OFF_FLAG = grad_abs ? 20 : 10;
-  const int ACC = 10 + (grad_abs ? 10 : 0) + (flagged_abs ? 10 : 0);
+  const int OFF_ABS = 10, OFF_COND = grad_abs ? 20 : 10;
+  const int OFF_FLAG = OFF_COND + (cond_abs ? 10 : 0);
+  const int ACC = OFF_FLAG + (flagged_abs ? 10 : 0);
   // One slot of ACC doubles per entry of the point list (tile lists are
   // contiguous in it), in a grow-only buffer kept across calls; each tile's
   // slots are zeroed by the thread that fills them.
@@ -901,6 +906,10 @@ OR_EXPORT void or_render_bwd(int W, int H, int P, const int* ranges, const int* 
         for (int k = 0; k < 10; ++k) a[k] += (double)v[k];
         if (grad_abs)
           for (int k = 0; k < 10; ++k) a[OFF_ABS + k] += std::fabs((double)v[k]);
+        if (cond_abs) {
+          const double sc = power_scale(co[0], co[1], co[2], d_x, d_y);
+          for (int k = 0; k < 10; ++k) a[OFF_COND + k] += std::fabs((double)v[k]) * sc;
+        }
         if (flagged)
           for (int k = 0; k < 10; ++k) a[OFF_FLAG + k] += std::fabs((double)v[k]);
       }
@@ -912,6 +921,7 @@ OR_EXPORT void or_render_bwd(int W, int H, int P, const int* ranges, const int* 
   static std::vector<double> g_sum, g_abs;
   if (g_sum.size() < (size_t)P * 10) g_sum.resize((size_t)P * 10);
   if (grad_abs && g_abs.size() < (size_t)P * 10) g_abs.resize((size_t)P * 10);
+  // cond_abs is summed straight into the caller's array
   double* const sum = g_sum.data();
   double* const abs_sum = g_abs.data();
 #pragma omp parallel
@@ -921,6 +931,7 @@ OR_EXPORT void or_render_bwd(int W, int H, int P, const int* ranges, const int* 
     std::fill(sum + lo_id * 10, sum + hi_id * 10, 0.0);
     if (grad_abs) std::fill(abs_sum + lo_id * 10, abs_sum + hi_id * 10, 0.0);
     if (flagged_abs) std::fill(flagged_abs + lo_id * 10, flagged_abs + hi_id * 10, 0.0);
+    if (cond_abs) std::fill(cond_abs + lo_id * 10, cond_abs + hi_id * 10, 0.0);
     for (int tile = 0; tile < ntile; ++tile) {
       const int start = ranges[2 * tile];
       const int n = ranges[2 * tile + 1] - start;
@@ -935,6 +946,8 @@ OR_EXPORT void or_render_bwd(int W, int H, int P, const int* ranges, const int* 
           for (int k = 0; k < 10; ++k) abs_sum[(size_t)id * 10 + k] += a[OFF_ABS + k];
         if (flagged_abs)
           for (int k = 0; k < 10; ++k) flagged_abs[(size_t)id * 10 + k] += a[OFF_FLAG + k];
+        if (cond_abs)
+          for (int k = 0; k < 10; ++k) cond_abs[(size_t)id * 10 + k] += a[OFF_COND + k];
       }
     }
   }
