@@ -57,6 +57,8 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-autograd", action="store_true", help="skip the drop-in autograd path comparison")
     p.add_argument("--no-optimizer", action="store_true", help="skip the fused Adam measurement")
+    p.add_argument("--path", default="fused", choices=["fused", "autograd"],
+                   help="the measured path: the fused training step, or the drop-in autograd path alone")
     return p.parse_args()
 
 
@@ -849,7 +851,7 @@ def run_ours(args):
     V = len(views)
     targets_dev = [wl.target_image(rank * V + i, args.height, args.width).to(device) for i in range(V)]
     targets_host = [t.cpu().pin_memory() for t in targets_dev] if not args.no_e2e else None
-    tr = Trainer(scene, views, targets_dev, targets_host, world, device)
+    tr = Trainer(scene, views, targets_dev, targets_host, world, device, path=args.path)
 
     # device-resident timing with clock sampling
     sampler = ClockSampler(local)
@@ -868,7 +870,7 @@ def run_ours(args):
 
     # the drop-in autograd path on the same workload, for comparison
     autograd_api = None
-    if not args.no_autograd:
+    if not args.no_autograd and args.path == "fused":
         autograd_api = measure_autograd(args, scene, views, targets_dev, targets_host, world, device, views_total)
 
     prof = kernel_profile(tr, steps=1)
@@ -909,8 +911,9 @@ def run_ours(args):
                        "l2": "inputs larger than L2 (6M-Gaussian scene, 1.4 GB of parameters)"},
             "clocks": clocks,
             "e2e": e2e,
-            "path": "gswarp_b200.training.FusedViewStep (C ABI stages, fused photometric loss, preprocess "
-                    "backward accumulating into the flat gradient buffer)",
+            "path": ("gswarp_b200.training.FusedViewStep (C ABI stages, fused photometric loss, preprocess "
+                     "backward accumulating into the flat gradient buffer)" if args.path == "fused" else
+                     "GaussianRasterizer + fused_ssim under autograd, ViewShardedStep"),
             "autograd_api": autograd_api,
             "gpu_launches": launches * args.steps,
             "roofline": rl,

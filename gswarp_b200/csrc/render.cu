@@ -10,20 +10,25 @@
 // last_color (and depth) terms, gradients of xy (scaled by W/2, H/2), conic,
 // opacity, colour and depth.
 //
-// B200 design (both directions): one 128-thread CTA per 16x16 tile; each
-// thread owns TWO pixels (rows y and y+4 of its warp's 8x8 block), so every
-// Gaussian staged in shared memory is read once per two pixels and the
-// per-(warp, Gaussian) control work covers 64 pixels.  Gaussians are staged
+// B200 design.  Forward: one 128-thread CTA per 16x16 tile; each thread owns
+// TWO pixels (rows y and y+4 of its warp's 8x8 block), so every Gaussian
+// staged in shared memory is read once per two pixels and the per-(warp,
+// Gaussian) control work covers 64 pixels.  Backward: one 64-thread CTA per
+// tile; each warp owns an 8x16 column block and each thread FOUR pixels (rows
+// y, y+4, y+8, y+12) as two packed pairs, so the per-(warp, Gaussian) work
+// that does not scale with pixels -- culling, operand loads, the 10-term warp
+// reduction and the atomics -- covers 128 pixels (a Gaussian that reaches
+// both 8x8 blocks of a column costs one hit, not two).  Both stage Gaussians
 // per batch from the 48-byte render records (three 16-byte loads per
 // Gaussian); exp is one MUFU.EX2, 1/(1-alpha) one MUFU.RCP.  Backward: the
 // CTA walks its list from the CTA-wide maximum contributor down, each warp
-// skips positions above its own maximum, tests each Gaussian against the two
-// halves of its block (rows holding every lane's first / second pixel) so a
-// half it cannot reach is skipped warp-wide, a warp vote skips Gaussians no
-// lane uses, and the ten gradient terms (already summed over the thread's two
-// pixels) are reduced across the warp with a 12-shuffle transpose reduction
-// (instead of 10 x 5 butterfly shuffles); 10 lanes then issue one float atomic
-// each into the per-Gaussian accumulator.
+// skips positions above its own maximum, tests each Gaussian against the four
+// 8x4 quarters of its block (each quarter holds one pixel slot of every lane)
+// so a quarter it cannot reach is skipped warp-wide, a warp vote skips
+// Gaussians no lane uses, and the ten gradient terms (already summed over the
+// thread's pixels) are reduced across the warp with a 12-shuffle transpose
+// reduction (instead of 10 x 5 butterfly shuffles); 10 lanes then issue one
+// float atomic each into the per-Gaussian accumulator.
 #include "gsb_common.cuh"
 
 namespace gsb {
@@ -457,10 +462,64 @@ __device__ __forceinline__ void bwd_pair(BwdPair& s, bool e0, bool e1, const flo
   if (DEPTH) m.ddepth = __fmaf_rn(dch.y, s.gd.y, __fmul_rn(dch.x, s.gd.x));
 }
 
+// Backward launch shape: two warps per 16x16 tile, each owning an 8-column x
+// 16-row block with FOUR pixels per thread (rows r, r+4, r+8, r+12 of its
+// column), run as two packed f32x2 pairs that share every Gaussian operand
+// (the column offset dx included).  Against a warp per 8x8 block, a Gaussian
+// that covers both blocks of a column costs one hit -- one cull, one
+// operand load, one 10-term warp reduction and one set of atomics -- for
+// twice the pixels; culling stays at 8x4 granularity (each quarter of the
+// block holds one pixel slot of every lane, so a quarter the Gaussian cannot
+// reach is skipped warp-wide).
+constexpr int BWD_THREADS = 64;
+
+// The thread's column and first row (slot k is row py0 + 4k).
+__device__ __forceinline__ void bwd_pixels_of(int tile, int gx, int& px, int& py0) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tx = tile % gx, ty = tile / gx;
+  px = tx * BLOCK_X + warp * 8 + (lane & 7);
+  py0 = ty * BLOCK_Y + (lane >> 3);
+}
+
+// Which quarters (rows y0+4k .. y0+4k+3, k = 0..3) of the warp's 8x16 block
+// staged Gaussian g can reach: box test, then the exact ellipse test per
+// quarter (same tests as the forward's block test, same widened threshold).
+__device__ __forceinline__ unsigned cull_quarters(int g, int cnt, const float4* s_box, const float2* s_xy,
+                                                  const float4* s_el, float x0, float x1, float y0) {
+  unsigned q = 0;
+  if (g < cnt) {
+    const float4 b = s_box[g];
+    if (b.x <= x1 && b.y >= x0) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        if (b.z <= y0 + 4.0f * k + 3.0f && b.w >= y0 + 4.0f * k) q |= 1u << k;
+    }
+  }
+  if (__any_sync(FULL, q != 0) && q) {
+    const float2 c = s_xy[g];
+    const float4 e = s_el[g];
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      if ((q >> k) & 1u && !ellipse_hits(c.x, c.y, e, x0, x1, y0 + 4.0f * k, y0 + 4.0f * k + 3.0f))
+        q &= ~(1u << k);
+  }
+  return q;
+}
+
+__device__ __forceinline__ void add_sums(BwdSums& m, const BwdSums& o, bool depth) {
+  m.U += o.U;
+  m.UY += o.UY;
+  m.UYY += o.UYY;
+  m.dcol0 += o.dcol0;
+  m.dcol1 += o.dcol1;
+  m.dcol2 += o.dcol2;
+  if (depth) m.ddepth += o.ddepth;
+}
+
 // DEPTH: compute_depth with a depth gradient given; GA: an alpha gradient
 // given.  Without them those terms are exactly zero and are not evaluated.
 template <bool DEPTH, bool GA>
-__global__ void __launch_bounds__(THREADS, 8) render_bwd_kernel(const gsb_render_bwd_args a, int gx) {
+__global__ void __launch_bounds__(BWD_THREADS, 11) render_bwd_kernel(const gsb_render_bwd_args a, int gx) {
   __shared__ int s_id[BATCH];
   __shared__ float2 s_xy[BATCH];
   __shared__ float4 s_cf[BATCH];    // power coefficients, opacity in .w
@@ -468,55 +527,60 @@ __global__ void __launch_bounds__(THREADS, 8) render_bwd_kernel(const gsb_render
   __shared__ float4 s_rgbd[BATCH];
   __shared__ float4 s_box[BATCH];
   __shared__ float4 s_el[BATCH];
-  __shared__ int s_max[THREADS / 32];
+  __shared__ int s_max[BWD_THREADS / 32];
   const int tile = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int pxi, py0;
-  pixels_of(tile, gx, pxi, py0);
+  bwd_pixels_of(tile, gx, pxi, py0);
   const int2 range = reinterpret_cast<const int2*>(a.ranges)[tile];
   const int n = range.y - range.x;
   const float4* rec = reinterpret_cast<const float4*>(a.records);
   const long long npix = (long long)a.W * a.H;
   const bool has_bg = a.background[0] != 0.0f || a.background[1] != 0.0f || a.background[2] != 0.0f;
 
-  BwdPair px;
-  px.lc0 = px.lc1 = 0;
-  float Tf[2], g0[2], g1[2], g2[2], gd[2], ga[2];
+  // pair 0: slots 0 and 1 (rows py0, py0 + 4); pair 1: slots 2 and 3 (rows py0 + 8, py0 + 12)
+  BwdPair px[2];
+  int lc_max = 0;
 #pragma unroll
-  for (int p = 0; p < 2; ++p) {
-    const int py = py0 + 4 * p;
-    int lc = 0;
-    Tf[p] = g0[p] = g1[p] = g2[p] = gd[p] = ga[p] = 0.0f;
-    if (pxi < a.W && py < a.H && n > 0) {
-      const long long pix = (long long)py * a.W + pxi;
-      lc = a.n_contrib[pix];
-      Tf[p] = 1.0f - a.out_alpha[pix];
-      g0[p] = a.grad_color[pix];
-      g1[p] = a.grad_color[npix + pix];
-      g2[p] = a.grad_color[2 * npix + pix];
-      if (DEPTH) gd[p] = a.grad_depth[pix];
-      if (GA) ga[p] = a.grad_alpha[pix];
+  for (int h = 0; h < 2; ++h) {
+    float Tf[2], g0[2], g1[2], g2[2], gd[2], ga[2];
+    int lc[2];
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+      const int py = py0 + 8 * h + 4 * p;
+      lc[p] = 0;
+      Tf[p] = g0[p] = g1[p] = g2[p] = gd[p] = ga[p] = 0.0f;
+      if (pxi < a.W && py < a.H && n > 0) {
+        const long long pix = (long long)py * a.W + pxi;
+        lc[p] = a.n_contrib[pix];
+        Tf[p] = 1.0f - a.out_alpha[pix];
+        g0[p] = a.grad_color[pix];
+        g1[p] = a.grad_color[npix + pix];
+        g2[p] = a.grad_color[2 * npix + pix];
+        if (DEPTH) gd[p] = a.grad_depth[pix];
+        if (GA) ga[p] = a.grad_alpha[pix];
+      }
     }
-    if (p) px.lc1 = lc;
-    else px.lc0 = lc;
+    BwdPair& s = px[h];
+    s.lc0 = lc[0];
+    s.lc1 = lc[1];
+    lc_max = max(lc_max, max(lc[0], lc[1]));
+    s.nfy = make_float2(-(float)(py0 + 8 * h), -(float)(py0 + 8 * h + 4));
+    s.T = make_float2(Tf[0], Tf[1]);
+    s.nTf = make_float2(-Tf[0], -Tf[1]);
+    s.g0 = make_float2(g0[0], g0[1]);
+    s.g1 = make_float2(g1[0], g1[1]);
+    s.g2 = make_float2(g2[0], g2[1]);
+    s.gd = make_float2(gd[0], gd[1]);
+    s.ga = make_float2(ga[0], ga[1]);
+    s.bg_dot = make_float2(a.background[0] * g0[0] + a.background[1] * g1[0] + a.background[2] * g2[0],
+                           a.background[0] * g0[1] + a.background[1] * g1[1] + a.background[2] * g2[1]);
+    s.S = s.adr = s.aar = make_float2(0.0f, 0.0f);
   }
-  px.nfy = make_float2(-(float)py0, -(float)(py0 + 4));
-  px.T = make_float2(Tf[0], Tf[1]);
-  px.nTf = make_float2(-Tf[0], -Tf[1]);
-  px.g0 = make_float2(g0[0], g0[1]);
-  px.g1 = make_float2(g1[0], g1[1]);
-  px.g2 = make_float2(g2[0], g2[1]);
-  px.gd = make_float2(gd[0], gd[1]);
-  px.ga = make_float2(ga[0], ga[1]);
-  px.bg_dot = make_float2(a.background[0] * g0[0] + a.background[1] * g1[0] + a.background[2] * g2[0],
-                          a.background[0] * g0[1] + a.background[1] * g1[1] + a.background[2] * g2[1]);
-  px.S = px.adr = px.aar = make_float2(0.0f, 0.0f);
-  const int warp_max = __reduce_max_sync(FULL, max(px.lc0, px.lc1));
+  const int warp_max = __reduce_max_sync(FULL, lc_max);
   if (lane == 0) s_max[warp] = warp_max;
   __syncthreads();
-  int cta_max = 0;
-#pragma unroll
-  for (int w = 0; w < THREADS / 32; ++w) cta_max = max(cta_max, s_max[w]);
+  int cta_max = max(s_max[0], s_max[1]);
   cta_max = min(cta_max, n);  // n_contrib never exceeds the tile's list
   if (cta_max <= 0) return;
 
@@ -544,7 +608,7 @@ __global__ void __launch_bounds__(THREADS, 8) render_bwd_kernel(const gsb_render
   for (int hi = cta_max; hi > 0; hi -= BATCH) {
     const int lo = max(0, hi - BATCH);
     __syncthreads();
-    for (int k = threadIdx.x; k < hi - lo; k += THREADS) {
+    for (int k = threadIdx.x; k < hi - lo; k += BWD_THREADS) {
       const int id = a.point_list[range.x + lo + k];
       const float4 q0 = __ldg(rec + (size_t)id * 3 + 0);
       const float4 q1 = __ldg(rec + (size_t)id * 3 + 1);
@@ -561,56 +625,66 @@ __global__ void __launch_bounds__(THREADS, 8) render_bwd_kernel(const gsb_render
     }
     __syncthreads();
     const int top = min(hi, warp_max);
-    // Lanes test staged Gaussians against the warp's 8x8 block; the warp
+    // Lanes test staged Gaussians against the warp's four quarters; the warp
     // visits only the hits below its own maximum, back to front.
     for (int cb = ((top - lo - 1) >> 5) << 5; cb >= 0 && top > lo; cb -= 32) {
-      bool ht, hb;
-      cull_halves(cb + lane, top - lo, s_box, s_xy, s_el, bx0, bx1, by0, ht, hb);
-      const unsigned top_h = __ballot_sync(FULL, ht), bot_h = __ballot_sync(FULL, hb);
-      unsigned hits = top_h | bot_h;
+      const unsigned q = cull_quarters(cb + lane, top - lo, s_box, s_xy, s_el, bx0, bx1, by0);
+      const unsigned m0 = __ballot_sync(FULL, q & 1u), m1 = __ballot_sync(FULL, q & 2u);
+      const unsigned m2 = __ballot_sync(FULL, q & 4u), m3 = __ballot_sync(FULL, q & 8u);
+      unsigned hits = m0 | m1 | m2 | m3;
       while (hits) {
-      const int bit = 31 - __clz(hits);
-      const int j = cb + bit;
-      hits &= ~(1u << bit);
-      const int pos = lo + j;
-      BwdSums m = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
-      bool contrib = false;
-      float dx = 0.0f;
-      // a half the Gaussian cannot reach has alpha < 1/255 at every pixel: no state change to skip
-      const bool e0 = ((top_h >> bit) & 1u) && pos < px.lc0;
-      const bool e1 = ((bot_h >> bit) & 1u) && pos < px.lc1;
-      if (e0 || e1) {
-        const float2 xy = s_xy[j];
-        const float4 cf = s_cf[j];
-        const float4 cd = s_rgbd[j];
-        dx = xy.x - fx;
-        float ax, bx;
-        column_terms(cf, dx, ax, bx);
-        bool c0, c1;
-        bwd_pair<DEPTH, GA>(px, e0, e1, cf, ax, bx, xy.y, cd, has_bg, m, c0, c1);
-        contrib = c0 || c1;
-      }
-      if (__any_sync(FULL, contrib)) {
-        const float4 con = s_con[j];
-        const float dxU = dx * m.U;
-        float v[10];
-        v[0] = con.x * dxU + con.y * m.UY;   // x: times -op W/2
-        v[1] = con.z * m.UY + con.y * dxU;   // y: times -op H/2
-        v[2] = m.ddepth;
-        v[3] = dx * dxU;                     // conic a: times -op/2
-        v[4] = dx * m.UY;                    // conic b: times -op/2
-        v[5] = m.UYY;                        // conic c: times -op/2
-        v[6] = m.U;                          // opacity
-        v[7] = m.dcol0;
-        v[8] = m.dcol1;
-        v[9] = m.dcol2;
-        float sum;
-        warp_reduce10(v, sum);
-        if (my_writer) {
-          const float scale = fmaf(s_cf[j].w, my_mul_op, my_mul_one);
-          atomicAdd(a.grad_acc + (size_t)s_id[j] * GSB_GRAD_FLOATS + my_off, sum * scale);
+        const int bit = 31 - __clz(hits);
+        const int j = cb + bit;
+        hits &= ~(1u << bit);
+        const int pos = lo + j;
+        // a quarter the Gaussian cannot reach has alpha < 1/255 at every pixel: no state change to skip
+        const bool e0 = ((m0 >> bit) & 1u) && pos < px[0].lc0;
+        const bool e1 = ((m1 >> bit) & 1u) && pos < px[0].lc1;
+        const bool e2 = ((m2 >> bit) & 1u) && pos < px[1].lc0;
+        const bool e3 = ((m3 >> bit) & 1u) && pos < px[1].lc1;
+        BwdSums m = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+        bool contrib = false;
+        float dx = 0.0f;
+        if (e0 || e1 || e2 || e3) {
+          const float2 xy = s_xy[j];
+          const float4 cf = s_cf[j];
+          const float4 cd = s_rgbd[j];
+          dx = xy.x - fx;
+          float ax, bx;
+          column_terms(cf, dx, ax, bx);
+          bool c0, c1;
+          if (e0 || e1) {
+            bwd_pair<DEPTH, GA>(px[0], e0, e1, cf, ax, bx, xy.y, cd, has_bg, m, c0, c1);
+            contrib = c0 || c1;
+          }
+          if (e2 || e3) {
+            BwdSums m2s;
+            bwd_pair<DEPTH, GA>(px[1], e2, e3, cf, ax, bx, xy.y, cd, has_bg, m2s, c0, c1);
+            add_sums(m, m2s, DEPTH);
+            contrib = contrib || c0 || c1;
+          }
         }
-      }
+        if (__any_sync(FULL, contrib)) {
+          const float4 con = s_con[j];
+          const float dxU = dx * m.U;
+          float v[10];
+          v[0] = con.x * dxU + con.y * m.UY;   // x: times -op W/2
+          v[1] = con.z * m.UY + con.y * dxU;   // y: times -op H/2
+          v[2] = m.ddepth;
+          v[3] = dx * dxU;                     // conic a: times -op/2
+          v[4] = dx * m.UY;                    // conic b: times -op/2
+          v[5] = m.UYY;                        // conic c: times -op/2
+          v[6] = m.U;                          // opacity
+          v[7] = m.dcol0;
+          v[8] = m.dcol1;
+          v[9] = m.dcol2;
+          float sum;
+          warp_reduce10(v, sum);
+          if (my_writer) {
+            const float scale = fmaf(s_cf[j].w, my_mul_op, my_mul_one);
+            atomicAdd(a.grad_acc + (size_t)s_id[j] * GSB_GRAD_FLOATS + my_off, sum * scale);
+          }
+        }
       }
     }
   }
@@ -665,12 +739,12 @@ GSB_EXPORT int gsb_render_bwd(const gsb_render_bwd_args* a, void* stream) {
   const bool ga = a->grad_alpha != nullptr;
   const int blocks = gx * gy;
   if (depth && ga)
-    render_bwd_kernel<true, true><<<blocks, THREADS, 0, s>>>(*a, gx);
+    render_bwd_kernel<true, true><<<blocks, BWD_THREADS, 0, s>>>(*a, gx);
   else if (depth)
-    render_bwd_kernel<true, false><<<blocks, THREADS, 0, s>>>(*a, gx);
+    render_bwd_kernel<true, false><<<blocks, BWD_THREADS, 0, s>>>(*a, gx);
   else if (ga)
-    render_bwd_kernel<false, true><<<blocks, THREADS, 0, s>>>(*a, gx);
+    render_bwd_kernel<false, true><<<blocks, BWD_THREADS, 0, s>>>(*a, gx);
   else
-    render_bwd_kernel<false, false><<<blocks, THREADS, 0, s>>>(*a, gx);
+    render_bwd_kernel<false, false><<<blocks, BWD_THREADS, 0, s>>>(*a, gx);
   return check_launch("render_bwd_kernel");
 }
