@@ -24,7 +24,7 @@ GSB_ERR_OVERFLOW = -2
 GSB_ERR_CUDA = -3
 GSB_ERR_TIMEOUT = -4
 
-ABI_VERSION = 15
+ABI_VERSION = 16
 RECORD_FLOATS = 12
 GRAD_FLOATS = 12
 

@@ -434,6 +434,52 @@ class PreprocessGrads:
     grad_colors: torch.Tensor | None
 
 
+def preprocess_backward_args(g: Gaussians, cam: Camera, radii, records, grad_acc, grad_proj_2d, grad_conic_2d,
+                             grad_conic_2d_inv, out: "PreprocessGrads", accumulate: bool,
+                             ids: torch.Tensor | None = None, clear_grad_acc: bool = False,
+                             densify_grad_accum: torch.Tensor | None = None,
+                             grad_colors_clamped: bool = False) -> "_lib.PreprocessBwdArgs":
+    """The argument block of one ``gsb_preprocess_bwd`` call (see
+    ``preprocess_backward``); a caller that runs the same view over several
+    id slices changes only ``ids`` / ``num_ids`` between calls."""
+    a = _lib.PreprocessBwdArgs()
+    a.P, a.W, a.H = g.P, cam.W, cam.H
+    a.means = _lib.ptr(g.means3D)
+    a.radii = _lib.ptr(radii)
+    a.scales = _lib.ptr(g.scales)
+    a.rotations = _lib.ptr(g.rotations)
+    a.cov3d_precomp = _lib.ptr(g.cov3D)
+    a.scale_modifier = g.scale_modifier
+    a.viewmatrix = _lib.ptr(cam.viewmatrix)
+    a.projmatrix = _lib.ptr(cam.projmatrix)
+    a.campos = _lib.ptr(cam.campos)
+    a.tanfovx, a.tanfovy = float(cam.tanfovx), float(cam.tanfovy)
+    a.focal_x, a.focal_y = cam.focal_x, cam.focal_y
+    a.sh = _lib.ptr(g.sh)
+    a.sh_degree = g.degree
+    a.sh_coeffs = g.sh.shape[1] if g.sh is not None else 0
+    a.records = _lib.ptr(records)
+    a.grad_acc = _lib.ptr(grad_acc)
+    a.grad_proj_2d = _lib.ptr(grad_proj_2d)
+    a.grad_conic_2d = _lib.ptr(grad_conic_2d)
+    a.grad_conic_2d_inv = _lib.ptr(grad_conic_2d_inv)
+    a.accumulate = int(accumulate)
+    a.ids = _lib.ptr(ids) if ids is not None and ids.numel() else None
+    a.num_ids = int(ids.numel()) if ids is not None else 0
+    a.clear_grad_acc = int(clear_grad_acc)
+    a.densify_grad_accum = _lib.ptr(densify_grad_accum)
+    a.grad_colors_clamped = int(grad_colors_clamped)
+    a.grad_means3d = _lib.ptr(out.grad_means3D)
+    a.grad_means2d = _lib.ptr(out.grad_means2D)
+    a.grad_scales = _lib.ptr(out.grad_scales)
+    a.grad_rotations = _lib.ptr(out.grad_rotations)
+    a.grad_opacity = _lib.ptr(out.grad_opacity)
+    a.grad_sh = _lib.ptr(out.grad_sh)
+    a.grad_colors = _lib.ptr(out.grad_colors)
+    a.grad_cov3d = _lib.ptr(out.grad_cov3D)
+    return a
+
+
 def preprocess_backward(g: Gaussians, cam: Camera, radii, records, grad_acc, grad_proj_2d, grad_conic_2d,
                         grad_conic_2d_inv, out: PreprocessGrads | None = None,
                         ids: torch.Tensor | None = None, clear_grad_acc: bool = False,
@@ -463,43 +509,10 @@ def preprocess_backward(g: Gaussians, cam: Camera, radii, records, grad_acc, gra
         )
     if P == 0:
         return out
-    a = _lib.PreprocessBwdArgs()
-    a.P, a.W, a.H = P, cam.W, cam.H
-    a.means = _lib.ptr(g.means3D)
-    a.radii = _lib.ptr(radii)
-    a.scales = _lib.ptr(g.scales)
-    a.rotations = _lib.ptr(g.rotations)
-    a.cov3d_precomp = _lib.ptr(g.cov3D)
-    a.scale_modifier = g.scale_modifier
-    a.viewmatrix = _lib.ptr(cam.viewmatrix)
-    a.projmatrix = _lib.ptr(cam.projmatrix)
-    a.campos = _lib.ptr(cam.campos)
-    a.tanfovx, a.tanfovy = float(cam.tanfovx), float(cam.tanfovy)
-    a.focal_x, a.focal_y = cam.focal_x, cam.focal_y
-    a.sh = _lib.ptr(g.sh)
-    a.sh_degree = g.degree
-    a.sh_coeffs = g.sh.shape[1] if g.sh is not None else 0
-    a.records = _lib.ptr(records)
-    a.grad_acc = _lib.ptr(grad_acc)
-    a.grad_proj_2d = _lib.ptr(grad_proj_2d)
-    a.grad_conic_2d = _lib.ptr(grad_conic_2d)
-    a.grad_conic_2d_inv = _lib.ptr(grad_conic_2d_inv)
-    a.accumulate = int(acc)
-    a.ids = _lib.ptr(ids) if ids is not None and ids.numel() else None
-    a.num_ids = int(ids.numel()) if ids is not None else 0
-    a.clear_grad_acc = int(clear_grad_acc)
-    a.densify_grad_accum = _lib.ptr(densify_grad_accum)
-    a.grad_colors_clamped = int(grad_colors_clamped)
+    a = preprocess_backward_args(g, cam, radii, records, grad_acc, grad_proj_2d, grad_conic_2d, grad_conic_2d_inv,
+                                 out, acc, ids, clear_grad_acc, densify_grad_accum, grad_colors_clamped)
     if ids is not None and ids.numel() == 0:
         return out
-    a.grad_means3d = _lib.ptr(out.grad_means3D)
-    a.grad_means2d = _lib.ptr(out.grad_means2D)
-    a.grad_scales = _lib.ptr(out.grad_scales)
-    a.grad_rotations = _lib.ptr(out.grad_rotations)
-    a.grad_opacity = _lib.ptr(out.grad_opacity)
-    a.grad_sh = _lib.ptr(out.grad_sh)
-    a.grad_colors = _lib.ptr(out.grad_colors)
-    a.grad_cov3d = _lib.ptr(out.grad_cov3D)
     info = {"P": P, "kernels": 1, "accumulate": acc}
     with _stage_timer("preprocess_bwd", info):
         _lib.call("gsb_preprocess_bwd", a, _lib.stream_handle(dev))

@@ -49,7 +49,7 @@ GSB_EXPORT int gsb_block_dim(const char* kernel_class) {
       {"binning_emit", BINNING_EMIT},
       {"radix_sort", RADIX_SORT},
       {"render_forward", RENDER},
-      {"render_backward", RENDER},
+      {"render_backward", RENDER_BWD},
       {"backward_preprocess", PREPROCESS_BWD},
       {"backward_preprocess_sh16", PREPROCESS_BWD_SH16},
       {"sh_backward_views", SH_BACKWARD_VIEWS},

@@ -275,6 +275,141 @@ __device__ __forceinline__ void sh_backward_staged(const gsb_preprocess_bwd_args
   __syncwarp();
 }
 
+// backward_kernels.py:89-112 (scale/rotation path): the screen-space
+// gradient (gxy0, gxy1) through the projection of the mean, plus the term of
+// the view-depth gradient rgd; returns the mean's view-space depth.
+__device__ __forceinline__ float proj_mean_grad(const float* pr, const float* vf, const float mean[3], float gxy0,
+                                                float gxy1, float rgd, float pm[3]) {
+  const float hom_x = pr[0] * mean[0] + pr[4] * mean[1] + pr[8] * mean[2] + pr[12];
+  const float hom_y = pr[1] * mean[0] + pr[5] * mean[1] + pr[9] * mean[2] + pr[13];
+  const float hom_w = pr[3] * mean[0] + pr[7] * mean[1] + pr[11] * mean[2] + pr[15];
+  const float inv_w = 1.0f / (hom_w + 1.0e-7f);
+  const float inv_w2 = inv_w * inv_w;
+  const float gh = hom_x * gxy0 + hom_y * gxy1;
+  pm[0] = inv_w * (pr[0] * gxy0 + pr[1] * gxy1) - pr[3] * inv_w2 * gh;
+  pm[1] = inv_w * (pr[4] * gxy0 + pr[5] * gxy1) - pr[7] * inv_w2 * gh;
+  pm[2] = inv_w * (pr[8] * gxy0 + pr[9] * gxy1) - pr[11] * inv_w2 * gh;
+  const float zz = vf[2] * mean[0] + vf[6] * mean[1] + vf[10] * mean[2] + vf[14];
+  pm[0] = pm[0] + (vf[2] - vf[3] * zz) * rgd;
+  pm[1] = pm[1] + (vf[6] - vf[7] * zz) * rgd;
+  pm[2] = pm[2] + (vf[10] - vf[11] * zz) * rgd;
+  return zz;
+}
+
+// backward_kernels.py:124-287 (scale/rotation path, radius > 0): the
+// conic gradient tc (render + user conic_2D gradient) and the user conic_2D_inv
+// gradient gi through the EWA covariance to the mean (gcm), the scales (gs)
+// and the rotation (gr); (x, y, z) is the mean in view space.
+__device__ __forceinline__ void cov_scale_rot_grads(const float* vf, float x, float y, float z, float limx,
+                                                    float limy, float focal_x, float focal_y,
+                                                    float scale_modifier, const float sc_in[3], float4 rot_in,
+                                                    float tc0, float tc1, float tc2, float gi0, float gi1,
+                                                    float gi2, float gcm[3], float gs[3], float gr[4]) {
+  const float w00 = vf[0], w01 = vf[1], w02 = vf[2], w10 = vf[4], w11 = vf[5], w12 = vf[6];
+  const float w20 = vf[8], w21 = vf[9], w22 = vf[10];
+  const float tz_inv = 1.0f / (z + 1.0e-7f);
+  const float txtz = x * tz_inv, tytz = y * tz_inv;
+  float x_mul = 1.0f, y_mul = 1.0f;
+  if (txtz < -limx || txtz > limx) x_mul = 0.0f;
+  if (tytz < -limy || tytz > limy) y_mul = 0.0f;
+  const float tx = fclamp(txtz, -limx, limx), ty = fclamp(tytz, -limy, limy);
+  const float j00 = focal_x * tz_inv;
+  const float j02 = -j00 * tx;
+  const float j11 = focal_y * tz_inv;
+  const float j12 = -j11 * ty;
+  const float t00 = w00 * j00 + w02 * j02, t10 = w10 * j00 + w12 * j02,
+              t20 = w20 * j00 + w22 * j02;
+  const float t01 = w01 * j11 + w02 * j12, t11 = w11 * j11 + w12 * j12,
+              t21 = w21 * j11 + w22 * j12;
+  const float s0 = sc_in[0] * scale_modifier;
+  const float s1 = sc_in[1] * scale_modifier;
+  const float s2 = sc_in[2] * scale_modifier;
+  const float4 q = rot_in;
+  const float rr = q.x, xq = q.y, yq = q.z, zq = q.w;
+  const float r00 = 1.0f - 2.0f * (yq * yq + zq * zq);
+  const float r01 = 2.0f * (xq * yq + rr * zq);
+  const float r02 = 2.0f * (xq * zq - rr * yq);
+  const float r10 = 2.0f * (xq * yq - rr * zq);
+  const float r11 = 1.0f - 2.0f * (xq * xq + zq * zq);
+  const float r12 = 2.0f * (yq * zq + rr * xq);
+  const float r20 = 2.0f * (xq * zq + rr * yq);
+  const float r21 = 2.0f * (yq * zq - rr * xq);
+  const float r22 = 1.0f - 2.0f * (xq * xq + yq * yq);
+  const float m00 = s0 * r00, m01 = s0 * r01, m02 = s0 * r02;
+  const float m10 = s1 * r10, m11 = s1 * r11, m12 = s1 * r12;
+  const float m20 = s2 * r20, m21 = s2 * r21, m22 = s2 * r22;
+  const float v00 = m00 * m00 + m10 * m10 + m20 * m20;
+  const float v01 = m00 * m01 + m10 * m11 + m20 * m21;
+  const float v02 = m00 * m02 + m10 * m12 + m20 * m22;
+  const float v11 = m01 * m01 + m11 * m11 + m21 * m21;
+  const float v12 = m01 * m02 + m11 * m12 + m21 * m22;
+  const float v22 = m02 * m02 + m12 * m12 + m22 * m22;
+  const float vt0x = v00 * t00 + v01 * t10 + v02 * t20;
+  const float vt0y = v01 * t00 + v11 * t10 + v12 * t20;
+  const float vt0z = v02 * t00 + v12 * t10 + v22 * t20;
+  const float vt1x = v00 * t01 + v01 * t11 + v02 * t21;
+  const float vt1y = v01 * t01 + v11 * t11 + v12 * t21;
+  const float vt1z = v02 * t01 + v12 * t11 + v22 * t21;
+  const float filt = 0.0f;
+  const float aa = t00 * vt0x + t10 * vt0y + t20 * vt0z + 0.3f + filt;
+  const float bb = t00 * vt1x + t10 * vt1y + t20 * vt1z;
+  const float cc = t01 * vt1x + t11 * vt1y + t21 * vt1z + 0.3f + filt;
+  const float denom = aa * cc - bb * bb;
+  const float denom2inv = 1.0f / (denom * denom + 1.0e-7f);
+  float dL_da = denom2inv * (-cc * cc * tc0 + 2.0f * bb * cc * tc1 - bb * bb * tc2);
+  float dL_dc = denom2inv * (-aa * aa * tc2 + 2.0f * aa * bb * tc1 - bb * bb * tc0);
+  float dL_db = denom2inv * 2.0f * (bb * cc * tc0 - (aa * cc + bb * bb) * tc1 + aa * bb * tc2);
+  dL_da = dL_da + gi0;
+  dL_db = dL_db + gi1;
+  dL_dc = dL_dc + gi2;
+  const float gc0 = t00 * t00 * dL_da + t00 * t01 * dL_db + t01 * t01 * dL_dc;
+  const float gc3v = t10 * t10 * dL_da + t10 * t11 * dL_db + t11 * t11 * dL_dc;
+  const float gc5 = t20 * t20 * dL_da + t20 * t21 * dL_db + t21 * t21 * dL_dc;
+  const float gc1 = 2.0f * t00 * t10 * dL_da + (t00 * t11 + t01 * t10) * dL_db + 2.0f * t01 * t11 * dL_dc;
+  const float gc2 = 2.0f * t00 * t20 * dL_da + (t00 * t21 + t01 * t20) * dL_db + 2.0f * t01 * t21 * dL_dc;
+  const float gc4 = 2.0f * t10 * t20 * dL_da + (t10 * t21 + t11 * t20) * dL_db + 2.0f * t11 * t21 * dL_dc;
+  const float dT00 = 2.0f * vt0x * dL_da + vt1x * dL_db;
+  const float dT01 = 2.0f * vt0y * dL_da + vt1y * dL_db;
+  const float dT02 = 2.0f * vt0z * dL_da + vt1z * dL_db;
+  const float dT10 = vt0x * dL_db + 2.0f * vt1x * dL_dc;
+  const float dT11 = vt0y * dL_db + 2.0f * vt1y * dL_dc;
+  const float dT12 = vt0z * dL_db + 2.0f * vt1z * dL_dc;
+  const float dJ00 = w00 * dT00 + w10 * dT01 + w20 * dT02;
+  const float dJ02 = w02 * dT00 + w12 * dT01 + w22 * dT02;
+  const float dJ11 = w01 * dT10 + w11 * dT11 + w21 * dT12;
+  const float dJ12 = w02 * dT10 + w12 * dT11 + w22 * dT12;
+  const float dL_dtx = x_mul * -j00 * tz_inv * dJ02;
+  const float dL_dty = y_mul * -j11 * tz_inv * dJ12;
+  const float dL_dtz = -(j00 * dJ00 + j11 * dJ11 + 2.0f * j02 * dJ02 + 2.0f * j12 * dJ12) * tz_inv;
+  gcm[0] = w00 * dL_dtx + w01 * dL_dty + w02 * dL_dtz;
+  gcm[1] = w10 * dL_dtx + w11 * dL_dty + w12 * dL_dtz;
+  gcm[2] = w20 * dL_dtx + w21 * dL_dty + w22 * dL_dtz;
+  const float sg00 = gc0, sg01 = 0.5f * gc1, sg02 = 0.5f * gc2, sg11 = gc3v, sg12 = 0.5f * gc4,
+              sg22 = gc5;
+  const float dM00 = 2.0f * (m00 * sg00 + m01 * sg01 + m02 * sg02);
+  const float dM01 = 2.0f * (m00 * sg01 + m01 * sg11 + m02 * sg12);
+  const float dM02 = 2.0f * (m00 * sg02 + m01 * sg12 + m02 * sg22);
+  const float dM10 = 2.0f * (m10 * sg00 + m11 * sg01 + m12 * sg02);
+  const float dM11 = 2.0f * (m10 * sg01 + m11 * sg11 + m12 * sg12);
+  const float dM12 = 2.0f * (m10 * sg02 + m11 * sg12 + m12 * sg22);
+  const float dM20 = 2.0f * (m20 * sg00 + m21 * sg01 + m22 * sg02);
+  const float dM21 = 2.0f * (m20 * sg01 + m21 * sg11 + m22 * sg12);
+  const float dM22 = 2.0f * (m20 * sg02 + m21 * sg12 + m22 * sg22);
+  gs[0] = scale_modifier * (dM00 * r00 + dM01 * r01 + dM02 * r02);
+  gs[1] = scale_modifier * (dM10 * r10 + dM11 * r11 + dM12 * r12);
+  gs[2] = scale_modifier * (dM20 * r20 + dM21 * r21 + dM22 * r22);
+  const float dR00 = dM00 * s0, dR01 = dM01 * s0, dR02 = dM02 * s0;
+  const float dR10 = dM10 * s1, dR11 = dM11 * s1, dR12 = dM12 * s1;
+  const float dR20 = dM20 * s2, dR21 = dM21 * s2, dR22 = dM22 * s2;
+  gr[0] = 2.0f * zq * (dR01 - dR10) + 2.0f * yq * (dR20 - dR02) + 2.0f * xq * (dR12 - dR21);
+  gr[1] = 2.0f * yq * (dR10 + dR01) + 2.0f * zq * (dR20 + dR02) + 2.0f * rr * (dR12 - dR21) -
+          4.0f * xq * (dR22 + dR11);
+  gr[2] = 2.0f * xq * (dR10 + dR01) + 2.0f * rr * (dR20 - dR02) + 2.0f * zq * (dR12 + dR21) -
+          4.0f * yq * (dR22 + dR00);
+  gr[3] = 2.0f * rr * (dR01 - dR10) + 2.0f * xq * (dR20 + dR02) + 2.0f * yq * (dR12 + dR21) -
+          4.0f * zq * (dR11 + dR00);
+}
+
 // SH16: SH rows of exactly 16 coefficients, 16-byte aligned, handled by
 // sh_backward_staged (every lane of a warp takes part, so lanes past P or
 // without work stay in the kernel and only skip their loads and stores).
@@ -359,30 +494,30 @@ __global__ void __launch_bounds__(SHM == SHM_16 ? PB_SH16_THREADS : PB_THREADS, 
     gxy0 = gxy0 + a.grad_proj_2d[gid * 2];
     gxy1 = gxy1 + a.grad_proj_2d[gid * 2 + 1];
   }
-  const float hom_x = pr[0] * mean[0] + pr[4] * mean[1] + pr[8] * mean[2] + pr[12];
-  const float hom_y = pr[1] * mean[0] + pr[5] * mean[1] + pr[9] * mean[2] + pr[13];
-  const float hom_w = pr[3] * mean[0] + pr[7] * mean[1] + pr[11] * mean[2] + pr[15];
-  const float inv_w = 1.0f / (hom_w + 1.0e-7f);
   float pm_x, pm_y, pm_z;
+  float zz;
   if (!PRECOMP) {
-    // backward_kernels.py:89-112
-    const float inv_w2 = inv_w * inv_w;
-    const float gh = hom_x * gxy0 + hom_y * gxy1;
-    pm_x = inv_w * (pr[0] * gxy0 + pr[1] * gxy1) - pr[3] * inv_w2 * gh;
-    pm_y = inv_w * (pr[4] * gxy0 + pr[5] * gxy1) - pr[7] * inv_w2 * gh;
-    pm_z = inv_w * (pr[8] * gxy0 + pr[9] * gxy1) - pr[11] * inv_w2 * gh;
+    float pm[3];
+    zz = proj_mean_grad(pr, vf, mean, gxy0, gxy1, rgd, pm);
+    pm_x = pm[0];
+    pm_y = pm[1];
+    pm_z = pm[2];
   } else {
     // backward_kernels.py:853-866
+    const float hom_x = pr[0] * mean[0] + pr[4] * mean[1] + pr[8] * mean[2] + pr[12];
+    const float hom_y = pr[1] * mean[0] + pr[5] * mean[1] + pr[9] * mean[2] + pr[13];
+    const float hom_w = pr[3] * mean[0] + pr[7] * mean[1] + pr[11] * mean[2] + pr[15];
+    const float inv_w = 1.0f / (hom_w + 1.0e-7f);
     const float mul1 = hom_x * inv_w * inv_w;
     const float mul2 = hom_y * inv_w * inv_w;
     pm_x = (pr[0] * inv_w - pr[3] * mul1) * gxy0 + (pr[1] * inv_w - pr[3] * mul2) * gxy1;
     pm_y = (pr[4] * inv_w - pr[7] * mul1) * gxy0 + (pr[5] * inv_w - pr[7] * mul2) * gxy1;
     pm_z = (pr[8] * inv_w - pr[11] * mul1) * gxy0 + (pr[9] * inv_w - pr[11] * mul2) * gxy1;
+    zz = vf[2] * mean[0] + vf[6] * mean[1] + vf[10] * mean[2] + vf[14];
+    pm_x = pm_x + (vf[2] - vf[3] * zz) * rgd;
+    pm_y = pm_y + (vf[6] - vf[7] * zz) * rgd;
+    pm_z = pm_z + (vf[10] - vf[11] * zz) * rgd;
   }
-  const float zz = vf[2] * mean[0] + vf[6] * mean[1] + vf[10] * mean[2] + vf[14];
-  pm_x = pm_x + (vf[2] - vf[3] * zz) * rgd;
-  pm_y = pm_y + (vf[6] - vf[7] * zz) * rgd;
-  pm_z = pm_z + (vf[10] - vf[11] * zz) * rgd;
 
   float gcm[3] = {0.0f, 0.0f, 0.0f};
   float gs[3] = {0.0f, 0.0f, 0.0f}, gr[4] = {0.0f, 0.0f, 0.0f, 0.0f};
@@ -404,108 +539,8 @@ __global__ void __launch_bounds__(SHM == SHM_16 ? PB_SH16_THREADS : PB_THREADS, 
     const float gi1 = gkv ? gkv[1] : 0.0f;
     const float gi2 = gkv ? gkv[2] : 0.0f;
     if (!PRECOMP) {
-      // backward_kernels.py:124-287
-      const float tz_inv = 1.0f / (z + 1.0e-7f);
-      const float txtz = x * tz_inv, tytz = y * tz_inv;
-      float x_mul = 1.0f, y_mul = 1.0f;
-      if (txtz < -limx || txtz > limx) x_mul = 0.0f;
-      if (tytz < -limy || tytz > limy) y_mul = 0.0f;
-      const float tx = fclamp(txtz, -limx, limx), ty = fclamp(tytz, -limy, limy);
-      const float j00 = a.focal_x * tz_inv;
-      const float j02 = -j00 * tx;
-      const float j11 = a.focal_y * tz_inv;
-      const float j12 = -j11 * ty;
-      const float t00 = w00 * j00 + w02 * j02, t10 = w10 * j00 + w12 * j02,
-                  t20 = w20 * j00 + w22 * j02;
-      const float t01 = w01 * j11 + w02 * j12, t11 = w11 * j11 + w12 * j12,
-                  t21 = w21 * j11 + w22 * j12;
-      const float s0 = sc_in[0] * a.scale_modifier;
-      const float s1 = sc_in[1] * a.scale_modifier;
-      const float s2 = sc_in[2] * a.scale_modifier;
-      const float4 q = rot_in;
-      const float rr = q.x, xq = q.y, yq = q.z, zq = q.w;
-      const float r00 = 1.0f - 2.0f * (yq * yq + zq * zq);
-      const float r01 = 2.0f * (xq * yq + rr * zq);
-      const float r02 = 2.0f * (xq * zq - rr * yq);
-      const float r10 = 2.0f * (xq * yq - rr * zq);
-      const float r11 = 1.0f - 2.0f * (xq * xq + zq * zq);
-      const float r12 = 2.0f * (yq * zq + rr * xq);
-      const float r20 = 2.0f * (xq * zq + rr * yq);
-      const float r21 = 2.0f * (yq * zq - rr * xq);
-      const float r22 = 1.0f - 2.0f * (xq * xq + yq * yq);
-      const float m00 = s0 * r00, m01 = s0 * r01, m02 = s0 * r02;
-      const float m10 = s1 * r10, m11 = s1 * r11, m12 = s1 * r12;
-      const float m20 = s2 * r20, m21 = s2 * r21, m22 = s2 * r22;
-      const float v00 = m00 * m00 + m10 * m10 + m20 * m20;
-      const float v01 = m00 * m01 + m10 * m11 + m20 * m21;
-      const float v02 = m00 * m02 + m10 * m12 + m20 * m22;
-      const float v11 = m01 * m01 + m11 * m11 + m21 * m21;
-      const float v12 = m01 * m02 + m11 * m12 + m21 * m22;
-      const float v22 = m02 * m02 + m12 * m12 + m22 * m22;
-      const float vt0x = v00 * t00 + v01 * t10 + v02 * t20;
-      const float vt0y = v01 * t00 + v11 * t10 + v12 * t20;
-      const float vt0z = v02 * t00 + v12 * t10 + v22 * t20;
-      const float vt1x = v00 * t01 + v01 * t11 + v02 * t21;
-      const float vt1y = v01 * t01 + v11 * t11 + v12 * t21;
-      const float vt1z = v02 * t01 + v12 * t11 + v22 * t21;
-      const float filt = 0.0f;
-      const float aa = t00 * vt0x + t10 * vt0y + t20 * vt0z + 0.3f + filt;
-      const float bb = t00 * vt1x + t10 * vt1y + t20 * vt1z;
-      const float cc = t01 * vt1x + t11 * vt1y + t21 * vt1z + 0.3f + filt;
-      const float denom = aa * cc - bb * bb;
-      const float denom2inv = 1.0f / (denom * denom + 1.0e-7f);
-      float dL_da = denom2inv * (-cc * cc * tc0 + 2.0f * bb * cc * tc1 - bb * bb * tc2);
-      float dL_dc = denom2inv * (-aa * aa * tc2 + 2.0f * aa * bb * tc1 - bb * bb * tc0);
-      float dL_db = denom2inv * 2.0f * (bb * cc * tc0 - (aa * cc + bb * bb) * tc1 + aa * bb * tc2);
-      dL_da = dL_da + gi0;
-      dL_db = dL_db + gi1;
-      dL_dc = dL_dc + gi2;
-      const float gc0 = t00 * t00 * dL_da + t00 * t01 * dL_db + t01 * t01 * dL_dc;
-      const float gc3v = t10 * t10 * dL_da + t10 * t11 * dL_db + t11 * t11 * dL_dc;
-      const float gc5 = t20 * t20 * dL_da + t20 * t21 * dL_db + t21 * t21 * dL_dc;
-      const float gc1 = 2.0f * t00 * t10 * dL_da + (t00 * t11 + t01 * t10) * dL_db + 2.0f * t01 * t11 * dL_dc;
-      const float gc2 = 2.0f * t00 * t20 * dL_da + (t00 * t21 + t01 * t20) * dL_db + 2.0f * t01 * t21 * dL_dc;
-      const float gc4 = 2.0f * t10 * t20 * dL_da + (t10 * t21 + t11 * t20) * dL_db + 2.0f * t11 * t21 * dL_dc;
-      const float dT00 = 2.0f * vt0x * dL_da + vt1x * dL_db;
-      const float dT01 = 2.0f * vt0y * dL_da + vt1y * dL_db;
-      const float dT02 = 2.0f * vt0z * dL_da + vt1z * dL_db;
-      const float dT10 = vt0x * dL_db + 2.0f * vt1x * dL_dc;
-      const float dT11 = vt0y * dL_db + 2.0f * vt1y * dL_dc;
-      const float dT12 = vt0z * dL_db + 2.0f * vt1z * dL_dc;
-      const float dJ00 = w00 * dT00 + w10 * dT01 + w20 * dT02;
-      const float dJ02 = w02 * dT00 + w12 * dT01 + w22 * dT02;
-      const float dJ11 = w01 * dT10 + w11 * dT11 + w21 * dT12;
-      const float dJ12 = w02 * dT10 + w12 * dT11 + w22 * dT12;
-      const float dL_dtx = x_mul * -j00 * tz_inv * dJ02;
-      const float dL_dty = y_mul * -j11 * tz_inv * dJ12;
-      const float dL_dtz = -(j00 * dJ00 + j11 * dJ11 + 2.0f * j02 * dJ02 + 2.0f * j12 * dJ12) * tz_inv;
-      gcm[0] = w00 * dL_dtx + w01 * dL_dty + w02 * dL_dtz;
-      gcm[1] = w10 * dL_dtx + w11 * dL_dty + w12 * dL_dtz;
-      gcm[2] = w20 * dL_dtx + w21 * dL_dty + w22 * dL_dtz;
-      const float sg00 = gc0, sg01 = 0.5f * gc1, sg02 = 0.5f * gc2, sg11 = gc3v, sg12 = 0.5f * gc4,
-                  sg22 = gc5;
-      const float dM00 = 2.0f * (m00 * sg00 + m01 * sg01 + m02 * sg02);
-      const float dM01 = 2.0f * (m00 * sg01 + m01 * sg11 + m02 * sg12);
-      const float dM02 = 2.0f * (m00 * sg02 + m01 * sg12 + m02 * sg22);
-      const float dM10 = 2.0f * (m10 * sg00 + m11 * sg01 + m12 * sg02);
-      const float dM11 = 2.0f * (m10 * sg01 + m11 * sg11 + m12 * sg12);
-      const float dM12 = 2.0f * (m10 * sg02 + m11 * sg12 + m12 * sg22);
-      const float dM20 = 2.0f * (m20 * sg00 + m21 * sg01 + m22 * sg02);
-      const float dM21 = 2.0f * (m20 * sg01 + m21 * sg11 + m22 * sg12);
-      const float dM22 = 2.0f * (m20 * sg02 + m21 * sg12 + m22 * sg22);
-      gs[0] = a.scale_modifier * (dM00 * r00 + dM01 * r01 + dM02 * r02);
-      gs[1] = a.scale_modifier * (dM10 * r10 + dM11 * r11 + dM12 * r12);
-      gs[2] = a.scale_modifier * (dM20 * r20 + dM21 * r21 + dM22 * r22);
-      const float dR00 = dM00 * s0, dR01 = dM01 * s0, dR02 = dM02 * s0;
-      const float dR10 = dM10 * s1, dR11 = dM11 * s1, dR12 = dM12 * s1;
-      const float dR20 = dM20 * s2, dR21 = dM21 * s2, dR22 = dM22 * s2;
-      gr[0] = 2.0f * zq * (dR01 - dR10) + 2.0f * yq * (dR20 - dR02) + 2.0f * xq * (dR12 - dR21);
-      gr[1] = 2.0f * yq * (dR10 + dR01) + 2.0f * zq * (dR20 + dR02) + 2.0f * rr * (dR12 - dR21) -
-              4.0f * xq * (dR22 + dR11);
-      gr[2] = 2.0f * xq * (dR10 + dR01) + 2.0f * rr * (dR20 - dR02) + 2.0f * zq * (dR12 + dR21) -
-              4.0f * yq * (dR22 + dR00);
-      gr[3] = 2.0f * rr * (dR01 - dR10) + 2.0f * xq * (dR20 + dR02) + 2.0f * yq * (dR12 + dR21) -
-              4.0f * zq * (dR11 + dR00);
+      cov_scale_rot_grads(vf, x, y, z, limx, limy, a.focal_x, a.focal_y, a.scale_modifier, sc_in, rot_in, tc0,
+                          tc1, tc2, gi0, gi1, gi2, gcm, gs, gr);
     } else {
       // backward_kernels.py:731-840
       const float* c3 = a.cov3d_precomp + (size_t)gid * 6;

@@ -471,7 +471,7 @@ __device__ __forceinline__ void bwd_pair(BwdPair& s, bool e0, bool e1, const flo
 // twice the pixels; culling stays at 8x4 granularity (each quarter of the
 // block holds one pixel slot of every lane, so a quarter the Gaussian cannot
 // reach is skipped warp-wide).
-constexpr int BWD_THREADS = 64;
+constexpr int BWD_THREADS = launch::RENDER_BWD;
 
 // The thread's column and first row (slot k is row py0 + 4k).
 __device__ __forceinline__ void bwd_pixels_of(int tile, int gx, int& px, int& py0) {

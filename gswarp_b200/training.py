@@ -30,12 +30,27 @@ view-direction part of the means gradient.  Per view that removes one SH
 read in the forward and an SH read plus an SH-gradient read-modify-write in
 the backward for every visible Gaussian.
 
+With a process group the multi-view step also reorders the backward, so
+that the exchange overlaps computation instead of starting after it: each
+view stops after its render backward (into its own 48-byte-per-Gaussian
+accumulator), and the views' preprocess backward then runs one Gaussian
+range at a time -- per range, every view's accumulating preprocess backward
+over its binned ids inside the range (the same kernel and the same
+per-Gaussian order of additions as view by view, so the same bits), then
+the SH backward of the range.  A finished range is final, so its all-reduce
+runs on NCCL's stream while the next range is computed.  On one GPU the
+view-by-view order is kept: there each view's preprocess backward overlaps
+the next view's forward on the other stream, which the range order gives
+up.
+
 Gradients equal the autograd path's up to the float summation order of the
 render backward's atomics (tests compare the two).
 """
 
 from __future__ import annotations
 
+import ctypes
+from dataclasses import dataclass
 from typing import Sequence
 
 import torch
@@ -94,27 +109,40 @@ def photometric_loss_backward(img: torch.Tensor, target: torch.Tensor, dm: torch
     return g
 
 
-def reduction_plan(P: int, means_numel: int, sh_numel: int, total: int, chunks: int):
-    """Issue order of the multi-view step's all-reduces over the flat gradient
-    buffer ``[means | scales | rotations | opacities | SH]`` (``total``
-    floats): first the block complete after the last view (scales,
-    rotations, opacities), then one SH slice per Gaussian range ``[b, e)`` of
-    the SH backward, then the means (to which the SH backward adds).  Returns
-    ``(first, [((b, e), (lo, hi)), ...], last)`` with slices as ``(lo, hi)``;
-    together they cover ``[0, total)`` once."""
-    sh_off = total - sh_numel
-    row = sh_numel // max(P, 1)
-    n = max(1, min(chunks, P))
-    ranges = []
-    for c in range(n):
-        b, e = P * c // n, P * (c + 1) // n
-        ranges.append(((b, e), (sh_off + b * row, sh_off + e * row)))
-    return (means_numel, sh_off), ranges, (0, means_numel)
+def backward_ranges(P: int, chunks: int) -> list[tuple[int, int]]:
+    """The Gaussian ranges ``[b, e)`` the multi-view backward works through
+    one after another: ``min(chunks, P)`` ranges of near-equal size, in
+    order, covering ``[0, P)`` once (none for P = 0)."""
+    n = max(1, min(int(chunks), P))
+    return [(P * c // n, P * (c + 1) // n) for c in range(n)] if P > 0 else []
+
+
+def range_slices(P: int, block_floats: Sequence[int], b: int, e: int) -> list[tuple[int, int]]:
+    """Slices ``(lo, hi)`` of the flat gradient buffer that hold the
+    Gaussians ``[b, e)``: the buffer is SoA blocks of ``block_floats[k]``
+    floats per Gaussian (``(3, 3, 4, 1, 48)`` for means, scales, rotations,
+    opacities and SH at degree 3), one slice per block."""
+    out, off = [], 0
+    for f in block_floats:
+        out.append((off + f * b, off + f * e))
+        off += f * P
+    return out
 
 
 def _distributed(group) -> bool:
     return (torch.distributed.is_available() and torch.distributed.is_initialized()
             and torch.distributed.get_world_size(group) > 1)
+
+
+@dataclass(slots=True)
+class _ViewState:
+    """What the range-ordered preprocess backward reads of one view."""
+    gaussians: pl.Gaussians
+    cam: pl.Camera
+    radii: torch.Tensor
+    records: torch.Tensor
+    ids: torch.Tensor
+    grad_acc: torch.Tensor
 
 
 class FusedViewStep:
@@ -166,9 +194,13 @@ class FusedViewStep:
         self._side: list[torch.cuda.Stream] = []
         # consecutive views go to this many streams in turn (overlapping them); 1 = one stream
         self.num_streams = 2
-        # with a process group and multi-view SH: Gaussian ranges whose SH gradients are all-reduced
-        # while the next range's SH backward runs
-        self.reduce_chunks = 4
+        # multi-view SH: the views' preprocess and SH backward run after the last view's render
+        # backward, one Gaussian range at a time, and each range is all-reduced (with a process group)
+        # while the next one is computed
+        self.backward_chunks = 8
+        # range-ordered backward: None = when a process group is in use (on one GPU the per-view
+        # preprocess backward overlaps the next view's forward on the other stream instead)
+        self.range_backward: bool | None = None
         # 3DGS densification statistics, accumulated per view until reset_densify_stats():
         # xyz_gradient_accum += |d loss / d means2D (x, y)|, denom += 1 and max_radii2D = max(., radius)
         # for every Gaussian with a radius in the view
@@ -179,11 +211,13 @@ class FusedViewStep:
             self.max_radii2D = torch.zeros(P, dtype=torch.float32, device=dev)
         # SH colours and SH gradients once per step (all views share the parameters and the SH degree)
         degrees = {int(rs.sh_degree) for rs in self.settings}
-        can_batch = len(degrees) == 1 and 1 <= sh.shape[1] <= 16
+        can_batch = len(degrees) == 1 and 1 <= sh.shape[1] <= 16 and \
+            len({float(rs.scale_modifier) for rs in self.settings}) == 1
         if batch_sh is None:
             batch_sh = can_batch and len(self.settings) > 1
         elif batch_sh and not can_batch:
-            raise ValueError("batch_sh needs one SH degree for all views and at most 16 SH coefficients")
+            raise ValueError("batch_sh needs one SH degree and scale modifier for all views and at most 16 "
+                             "SH coefficients")
         self.batch_sh = bool(batch_sh)
         if self.batch_sh:
             V = len(self.settings)
@@ -192,6 +226,10 @@ class FusedViewStep:
             self._colors = torch.empty((V, P, NUM_CHANNELS), dtype=torch.float32, device=dev)
             # the SH backward resets what it reads, so this stays zero between steps
             self._grad_colors = torch.zeros((V, P, NUM_CHANNELS), dtype=torch.float32, device=dev)
+            self._scale_modifier = float(self.settings[0].scale_modifier)
+        # one render-gradient accumulator per view for the range-ordered backward (the multi-view
+        # preprocess backward zeroes what it reads, so they stay zero between steps)
+        self._view_grad_acc: torch.Tensor | None = None
 
     @property
     def concurrent_views(self) -> bool:
@@ -286,6 +324,30 @@ class FusedViewStep:
             _lib.call("gsb_densify_stats", P, _lib.ptr(pre.radii), _lib.ptr(self.denom), _lib.ptr(self.max_radii2D),
                       _lib.stream_handle(self.device))
 
+    def view_render_grads(self, i: int, target: torch.Tensor, grad_acc: torch.Tensor) -> _ViewState:
+        """Multi-view SH, first half of view ``i`` on the current stream:
+        forward, loss, loss backward and render backward into ``grad_acc``
+        (the view's own zeroed (P, 12) accumulator).  Returns what the
+        range-ordered preprocess backward of the step reads of this view."""
+        rs, cam, mode, bg = self.settings[i], self.cams[i], self.modes[i], self.bgs[i]
+        g = self._gaussians(rs)
+        P = g.P
+        if target.shape != (NUM_CHANNELS, cam.H, cam.W):
+            raise ValueError(f"target {i} must have shape (3, {cam.H}, {cam.W})")
+        tgt, tgt_ready = self._target(i, target)
+        g.sh, g.colors = None, self._colors[i]
+        pre = pl.preprocess(g, cam, mode, sparse=True, colors_clamp_signed=True)
+        binned = pl.binning(pre, cam, mode, want_ids=True)
+        ren = pl.render(pre, binned, cam, bg, False)
+        if tgt_ready is not None:
+            torch.cuda.current_stream(self.device).wait_event(tgt_ready)
+        _, dm = photometric_loss_forward(ren.color, tgt, self.l1_weight, self.ssim_weight, out=self.losses[i])
+        grad_img = photometric_loss_backward(ren.color, tgt, dm, self.l1_weight, self.ssim_weight)
+        pl.render_backward(pre.records, binned, cam, bg, ren.alpha, ren.n_contrib, grad_img, None, None, False, P,
+                           grad_acc=grad_acc)
+        return _ViewState(gaussians=g, cam=cam, radii=pre.radii, records=pre.records, ids=binned.ids,
+                          grad_acc=grad_acc)
+
     def reset_densify_stats(self) -> None:
         if self.densify_stats:
             self.xyz_gradient_accum.zero_()
@@ -296,8 +358,14 @@ class FusedViewStep:
         """Runs every view, then the all-reduce.  Consecutive views go to
         ``num_streams`` streams in turn, so one view's compute-bound render
         kernels overlap the next view's memory- and latency-bound preprocess
-        and binning; the accumulations into the flat gradient buffer stay in
-        view order (each waits for the previous one)."""
+        and binning.  Each view finishes its own backward, the accumulations
+        into the flat gradient buffer in view order (each waits for the
+        previous one), then the multi-view SH backward and the all-reduce
+        run; or, range-ordered (``range_backward``; by default when a
+        process group is in use), every view stops after its render backward
+        (each into its own accumulator) and the preprocess and SH backward of
+        all views run afterwards on this stream, Gaussian range by Gaussian
+        range, each range all-reduced while the next is computed."""
         if len(targets) != len(self.settings):
             raise ValueError(f"expected {len(self.settings)} targets, got {len(targets)}")
         n_streams = max(1, int(self.num_streams))
@@ -314,49 +382,105 @@ class FusedViewStep:
                 pl.sh_colors_views(means, sh, self._sh_degree, self._campos, out=self._colors)
             else:
                 self.grads.zero_()
+            P, V = means.shape[0], len(targets)
+            ranged = self.batch_sh and (self.range_backward if self.range_backward is not None
+                                        else _distributed(self.group))
+            if ranged and (self._view_grad_acc is None or self._view_grad_acc.shape[:2] != (V, P)):
+                self._view_grad_acc = torch.zeros((V, P, _lib.GRAD_FLOATS), dtype=torch.float32, device=self.device)
             self._upload_targets(targets, main)
             ready = torch.cuda.Event()
             ready.record(main)
             for side in streams[1:]:
-                side.wait_event(ready)  # zeroed buffer, targets and parameters visible to every stream
-            prev = None
-            for i, t in enumerate(targets):
-                s = streams[i % n_streams]
-                with torch.cuda.stream(s):
-                    self.view(i, t, before_accumulate=prev, lane=i % n_streams)
-                    prev = torch.cuda.Event()
-                    prev.record(s)
-            # the last view's event follows every earlier one (each view's accumulation waits for the previous)
-            main.wait_event(prev)
-            if not self.batch_sh:
-                self.grads.all_reduce(self.group)
-            elif not _distributed(self.group):
-                pl.sh_backward_views(means, sh, self._sh_degree, self._campos, self._grad_colors, self.grads.views[4],
-                                     self.grads.views[0])
+                side.wait_event(ready)  # zeroed buffers, targets and parameters visible to every stream
+            if ranged:
+                states = []
+                for i, t in enumerate(targets):
+                    s = streams[i % n_streams]
+                    with torch.cuda.stream(s):
+                        st = self.view_render_grads(i, t, self._view_grad_acc[i])
+                        if s is not main:
+                            for buf in (st.radii, st.records, st.ids):
+                                buf.record_stream(main)
+                        states.append(st)
+                for side in streams[1:]:
+                    done = torch.cuda.Event()
+                    done.record(side)
+                    main.wait_event(done)
+                self._ranged_backward(states)
             else:
-                self._sh_backward_and_reduce(means, sh)
+                prev = None
+                for i, t in enumerate(targets):
+                    s = streams[i % n_streams]
+                    with torch.cuda.stream(s):
+                        self.view(i, t, before_accumulate=prev, lane=i % n_streams)
+                        prev = torch.cuda.Event()
+                        prev.record(s)
+                # the last view's event follows every earlier one (each view's accumulation waits for the
+                # previous)
+                main.wait_event(prev)
+                if self.batch_sh:
+                    pl.sh_backward_views(means, sh, self._sh_degree, self._campos, self._grad_colors,
+                                         self.grads.views[4], self.grads.views[0])
+                self.grads.all_reduce(self.group)
             # errors flagged by the last view's emit and sort (earlier views' are read by the next
             # view's binning): raised by this call, before anyone uses its gradients
             pl.raise_device_errors(self.device)
         return self.losses
 
-    def _sh_backward_and_reduce(self, means: torch.Tensor, sh: torch.Tensor) -> None:
-        """All-reduces (on NCCL's stream) while the SH backward runs: first the
-        scales, rotations and opacities (complete after the last view), then
-        the SH gradient range by range, each while the next range is
-        computed, and the means last (the SH backward adds their
-        view-direction term).  The sums are elementwise, so the result equals
-        one all-reduce of the whole buffer."""
+    def _ranged_backward(self, states: list) -> None:
+        """The second half of a multi-view step, on the current stream, one
+        Gaussian range after another: every view's preprocess backward over
+        its binned ids inside the range (accumulated into the flat buffer in
+        view order, as view by view), then the SH backward of the range
+        (stores the SH rows, adds the view-direction term to the means).
+        With a process group each finished range is all-reduced on NCCL's
+        stream while the next range is computed; the sums are elementwise,
+        so the result equals one all-reduce of the whole buffer.  Finding
+        the ranges' bounds in the views' id lists costs one host read."""
+        means, _, _, _, sh = self.params
         P = means.shape[0]
         flat = self.grads.flat
-        first, ranges, last = reduction_plan(P, self.grads.views[0].numel(), sh.numel(), flat.numel(),
-                                             self.reduce_chunks)
-        works = [torch.distributed.all_reduce(flat[first[0]:first[1]], group=self.group, async_op=True)]
-        for (b, e), (lo, hi) in ranges:
-            pl.sh_backward_views(means, sh, self._sh_degree, self._campos, self._grad_colors, self.grads.views[4],
-                                 self.grads.views[0], begin=b, end=e)
-            if hi > lo:
-                works.append(torch.distributed.all_reduce(flat[lo:hi], group=self.group, async_op=True))
-        works.append(torch.distributed.all_reduce(flat[last[0]:last[1]], group=self.group, async_op=True))
+        v_means, v_scales, v_rots, v_opac, v_sh = self.grads.views
+        blocks = [v.numel() // P if P else 0 for v in self.grads.views]
+        ranges = backward_ranges(P, self.backward_chunks)
+        if not ranges:
+            return
+        bounds = torch.tensor([b for b, _ in ranges] + [P], dtype=torch.int32, device=self.device)
+        splits = torch.stack([torch.searchsorted(st.ids, bounds) for st in states]).tolist()
+        if self.densify_stats:
+            for st in states:
+                _lib.call("gsb_densify_stats", P, _lib.ptr(st.radii), _lib.ptr(self.denom),
+                          _lib.ptr(self.max_radii2D), _lib.stream_handle(self.device))
+        # one argument block per view; per range only the id slice changes
+        args = []
+        for v, st in enumerate(states):
+            out = pl.PreprocessGrads(grad_means3D=v_means, grad_means2D=None, grad_opacity=v_opac,
+                                     grad_scales=v_scales, grad_rotations=v_rots, grad_cov3D=None, grad_sh=None,
+                                     grad_colors=self._grad_colors[v])
+            args.append(pl.preprocess_backward_args(
+                st.gaussians, st.cam, st.radii, st.records, st.grad_acc, None, None, None, out, True, ids=st.ids,
+                clear_grad_acc=True, densify_grad_accum=self.xyz_gradient_accum if self.densify_stats else None,
+                grad_colors_clamped=True))
+        L = _lib.load()
+        stream = _lib.stream_handle(self.device)
+        dist = _distributed(self.group)
+        works = []
+        for r, (b, e) in enumerate(ranges):
+            for v, st in enumerate(states):
+                lo, hi = splits[v][r], splits[v][r + 1]
+                if hi <= lo:
+                    continue
+                a = args[v]
+                a.ids = st.ids.data_ptr() + 4 * lo
+                a.num_ids = hi - lo
+                with pl._stage_timer("preprocess_bwd", {"P": P, "kernels": 1, "accumulate": True,
+                                                        "visible": hi - lo}):
+                    _lib.check(L.gsb_preprocess_bwd(ctypes.byref(a), stream), "gsb_preprocess_bwd")
+            pl.sh_backward_views(means, sh, self._sh_degree, self._campos, self._grad_colors, v_sh, v_means,
+                                 begin=b, end=e)
+            if dist:
+                for lo, hi in range_slices(P, blocks, b, e):
+                    if hi > lo:
+                        works.append(torch.distributed.all_reduce(flat[lo:hi], group=self.group, async_op=True))
         for w in works:
             w.wait()

@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define GSB_ABI_VERSION 15
+#define GSB_ABI_VERSION 16
 
 #define GSB_OK 0
 #define GSB_ERR_INVALID (-1)  /* bad argument: ValueError in Python          */

@@ -109,8 +109,10 @@ def test_rasterizer_rejects_cpu_inputs():
 
 
 def test_tuning_api_compat():
-    # the render kernels launch 128-thread CTAs (16x16 tile, two pixels per thread)
+    # the render forward launches 128-thread CTAs (16x16 tile, two pixels per thread), the
+    # backward 64-thread CTAs (four pixels per thread)
     assert gs.get_tuned_block_dim("render_forward") == 128
+    assert gs.get_tuned_block_dim("render_backward") == 64
     gs.register_kernel_class("custom", 32)
     assert gs.get_tuned_block_dim("custom") == 256
     assert isinstance(gs.get_canonical_device("cpu"), str)

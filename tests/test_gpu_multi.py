@@ -1,11 +1,11 @@
 """Two-GPU training step (needs at least two GPUs; skipped otherwise).
 
 Two NCCL ranks, each rendering its own views of the same scene.  The
-multi-view-SH step all-reduces the scales, rotations and opacities first,
-then the SH gradient in Gaussian ranges, each while the next range's SH
-backward runs, and the means last; the result must equal (up to the render backward's atomic
-summation order) the per-view-SH step's single all-reduce of the whole
-buffer, and the sum of the ranks' local gradients."""
+multi-view-SH step computes the per-Gaussian backward one Gaussian range at
+a time and all-reduces each finished range while the next one is computed;
+the result must equal (up to the render backward's atomic summation order)
+the per-view-SH step's single all-reduce of the whole buffer, and the sum of
+the ranks' local gradients."""
 
 import os
 import socket
@@ -58,7 +58,7 @@ def _worker(rank: int, world: int, port: int) -> None:
         sizes = [p.numel() for p in params]
 
         overlapped = FusedViewStep([p.clone() for p in params], settings, batch_sh=True)
-        overlapped.reduce_chunks = 3
+        overlapped.backward_chunks = 3
         overlapped.step(targets)
         plain = FusedViewStep([p.clone() for p in params], settings, batch_sh=False)
         plain.step(targets)

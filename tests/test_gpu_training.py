@@ -124,6 +124,66 @@ def test_fused_step_matches_autograd_step(cuda, n, views, W, H, batch_sh):
     assert float((fused.grads.flat - got).norm()) <= 1e-4 * float(got.norm()) + 1e-7
 
 
+@pytest.mark.parametrize("n,views,W,H", [(20_000, 3, 320, 192), (200_000, 2, 960, 544)])
+def test_range_ordered_step_matches_autograd_step(cuda, n, views, W, H):
+    """The range-ordered multi-view step (the default with a process group),
+    forced on one GPU, against the autograd path; its per-view
+    accumulators are left zero and a second step does not double."""
+    params, settings, targets = _scene(cuda, n, views, W, H)
+    ref_flat, ref_losses = _autograd_step(params, settings, targets, 1.0, 0.2)
+    fused = FusedViewStep([p.clone() for p in params], settings, 1.0, 0.2)
+    fused.range_backward = True
+    fused.backward_chunks = 3
+    losses = fused.step(targets)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(losses[:, 0], ref_losses, rtol=1e-5, atol=1e-6)
+    got = fused.grads.flat.clone()
+    off = 0
+    for p in params:
+        k = p.numel()
+        a, b = got[off:off + k], ref_flat[off:off + k]
+        assert float((a - b).norm()) <= 1e-4 * float(b.norm()) + 1e-7
+        off += k
+    assert not bool(fused._view_grad_acc.any()) and not bool(fused._grad_colors.any())
+    fused.step(targets)
+    assert float((fused.grads.flat - got).norm()) <= 1e-4 * float(got.norm()) + 1e-7
+
+
+@pytest.mark.parametrize("chunks", [2, 5, 64])
+def test_range_ordered_backward_is_independent_of_the_ranges(cuda, chunks):
+    """The multi-view step's second half over Gaussian ranges: fed the same
+    render gradients, any split into ranges gives the bits of one range
+    (every view's accumulating preprocess backward over its whole id list,
+    in view order, then the SH backward), and leaves the per-view render
+    accumulators and colour gradients zero."""
+    from gswarp_b200 import _pipeline as pl
+
+    params, settings, targets = _scene(cuda, 30_000, 3, 256, 160)
+    step = FusedViewStep([p.clone() for p in params], settings, densify_stats=True)
+    assert step.batch_sh
+    means, _, _, _, sh = step.params
+    P = means.shape[0]
+    step._view_grad_acc = torch.zeros((3, P, 12), device=cuda)
+    pl.sh_colors_views(means, sh, 3, step._campos, out=step._colors)
+    states = [step.view_render_grads(i, t, step._view_grad_acc[i]) for i, t in enumerate(targets)]
+    saved = step._view_grad_acc.clone()
+    results = []
+    for n in (1, chunks):
+        step._view_grad_acc.copy_(saved)
+        step.grads.flat.fill_(0.0)
+        step.reset_densify_stats()
+        step.backward_chunks = n
+        step._ranged_backward(states)
+        torch.cuda.synchronize()
+        results.append([t.clone() for t in (step.grads.flat, step.xyz_gradient_accum, step.denom,
+                                            step.max_radii2D)])
+        assert not bool(step._view_grad_acc.any())
+        assert not bool(step._grad_colors.any())
+    assert float(results[0][0].abs().sum()) > 0 and float(results[0][2].sum()) > 0
+    for a, b in zip(*results):
+        assert torch.equal(a, b)
+
+
 def test_fused_step_host_targets_match_device_targets(cuda):
     params, settings, targets = _scene(cuda, 20_000, 2, 256, 128)
     host = [t.cpu().pin_memory() for t in targets]

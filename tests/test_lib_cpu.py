@@ -79,13 +79,13 @@ def test_block_dims_are_the_launched_shapes():
 
     src = (Path(__file__).resolve().parents[1] / "gswarp_b200" / "csrc" / "gsb_launch.cuh").read_text()
     consts = {m.group(1): int(m.group(2)) for m in _re.finditer(r"constexpr int (\w+) = (\d+);", src)}
-    expect = {"render_forward": consts["RENDER"], "render_backward": consts["RENDER"],
+    expect = {"render_forward": consts["RENDER"], "render_backward": consts["RENDER_BWD"],
               "preprocess": consts["PREPROCESS"], "preprocess_sh16": consts["PREPROCESS_SH16"],
               "backward_preprocess_sh16": consts["PREPROCESS_BWD_SH16"], "ssim_fwd_h": consts["SSIM"],
               "knn_box_dist": consts["KNN"], "radix_sort": consts["RADIX_SORT"]}
     for name, n in expect.items():
         assert _runtime.get_tuned_block_dim(name) == n, name
-    assert _runtime.get_tuned_block_dim("render_backward") == 128
+    assert _runtime.get_tuned_block_dim("render_backward") == 64
     for name in _runtime.KERNEL_CLASSES:
         assert _lib.load().gsb_block_dim(name.encode()) > 0, name
     assert _lib.load().gsb_block_dim(b"no_such_kernel") == 0

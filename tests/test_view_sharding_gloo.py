@@ -51,23 +51,25 @@ def test_shard_views_partitions_all_views():
         shard_views(8, 2, 2)
 
 
-def test_reduction_plan_covers_the_buffer_once():
-    """The multi-view step's overlapped all-reduces: the complete blocks
-    first, SH ranges in Gaussian order, means last; disjoint and exhaustive."""
-    from gswarp_b200.training import reduction_plan
+def test_backward_ranges_and_slices_cover_the_buffer_once():
+    """The multi-view step's range-ordered backward: Gaussian ranges in
+    order, covering [0, P) once, and per range one slice per SoA block of
+    the flat gradient buffer; over all ranges the slices are disjoint and
+    cover the buffer exactly."""
+    from gswarp_b200.training import backward_ranges, range_slices
 
+    blocks = (3, 3, 4, 1, 48)
     for P in (1, 2, 37, 1000, 6_000_001):
-        for chunks in (1, 3, 4, 64):
-            total = P * 59
-            first, ranges, last = reduction_plan(P, 3 * P, 48 * P, total, chunks)
-            assert first == (3 * P, 11 * P) and last == (0, 3 * P)
-            slices = [first] + [sl for _, sl in ranges] + [last]
-            covered = sorted(slices)
-            assert covered[0][0] == 0 and covered[-1][1] == total
-            assert all(a[1] == b[0] for a, b in zip(covered, covered[1:]))
-            assert [g for g, _ in ranges][0][0] == 0 and ranges[-1][0][1] == P
-            assert all(r0[0][1] == r1[0][0] for r0, r1 in zip(ranges, ranges[1:]))
+        for chunks in (1, 3, 8, 64):
+            ranges = backward_ranges(P, chunks)
             assert len(ranges) == max(1, min(chunks, P))
+            assert ranges[0][0] == 0 and ranges[-1][1] == P
+            assert all(r0[1] == r1[0] and r0[0] < r0[1] for r0, r1 in zip(ranges, ranges[1:]))
+            slices = sorted(sl for b, e in ranges for sl in range_slices(P, blocks, b, e))
+            assert slices[0][0] == 0 and slices[-1][1] == 59 * P
+            assert all(a[1] == b[0] for a, b in zip(slices, slices[1:]))
+    assert backward_ranges(0, 8) == []
+    assert range_slices(10, blocks, 2, 5) == [(6, 15), (36, 45), (68, 80), (102, 105), (206, 350)]
 
 
 def test_gradient_buffer_accumulates_in_place():
