@@ -59,6 +59,8 @@ def parse():
     p.add_argument("--no-optimizer", action="store_true", help="skip the fused Adam measurement")
     p.add_argument("--path", default="fused", choices=["fused", "autograd"],
                    help="the measured path: the fused training step, or the drop-in autograd path alone")
+    p.add_argument("--backward-order", default="auto", choices=["auto", "views", "ranges"],
+                   help="fused step: per-view backward, range-ordered backward, or auto (ranges with N > 1)")
     return p.parse_args()
 
 
@@ -713,6 +715,25 @@ def measure_allreduce(flat, world: int, reps: int = 5) -> dict:
         str(x) for x in torch.cuda.nccl.version()), "env": env or "NCCL defaults"}
 
 
+def nccl_algorithms(path) -> dict | str:
+    """Algorithm, protocol and channels NCCL chose per all-reduce size, from
+    its tuning log lines ("AllReduce: <bytes> Bytes -> Algo <a> proto <p>
+    channel{Lo..Hi}={lo..hi}")."""
+    import re
+
+    if not path or not os.path.exists(path):
+        return "not recorded (NCCL debug output configured by the caller)"
+    pat = re.compile(r"AllReduce: (\d+) Bytes -> Algo (\w+) proto (\w+) channel\{Lo\.\.Hi\}=\{(\d+)\.\.(\d+)\}")
+    seen = {}
+    with open(path, errors="replace") as f:
+        for line in f:
+            m = pat.search(line)
+            if m:
+                seen[int(m.group(1))] = f"{m.group(2)}/{m.group(3)}/{int(m.group(5)) - int(m.group(4)) + 1}ch"
+    big = sorted(seen, reverse=True)[:8]
+    return {str(k): seen[k] for k in big} or "no tuning lines"
+
+
 def dp_check(device, rank: int, world: int) -> dict:
     """Correctness of the data-parallel step on this job's ranks (outside the
     timed region): each rank renders its own 2 views of a 30K-Gaussian scene;
@@ -834,7 +855,12 @@ def run_ours(args):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
+    nccl_log = None
     if world > 1:
+        if "NCCL_DEBUG_FILE" not in os.environ and os.environ.get("NCCL_DEBUG", "").upper() not in ("INFO", "TRACE"):
+            # NCCL's tuning lines (to a file) name the algorithm and protocol of every collective
+            nccl_log = f"/tmp/gsb_bench_nccl.{os.getpid()}.log"
+            os.environ.update(NCCL_DEBUG="INFO", NCCL_DEBUG_SUBSYS="TUNING", NCCL_DEBUG_FILE=nccl_log)
         torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
     from gswarp_b200 import workloads as wl
     from gswarp_b200 import _pipeline
@@ -852,6 +878,8 @@ def run_ours(args):
     targets_dev = [wl.target_image(rank * V + i, args.height, args.width).to(device) for i in range(V)]
     targets_host = [t.cpu().pin_memory() for t in targets_dev] if not args.no_e2e else None
     tr = Trainer(scene, views, targets_dev, targets_host, world, device, path=args.path)
+    if args.path == "fused" and args.backward_order != "auto":
+        tr.fused.range_backward = args.backward_order == "ranges"
 
     # device-resident timing with clock sampling
     sampler = ClockSampler(local)
@@ -873,6 +901,8 @@ def run_ours(args):
     if not args.no_autograd and args.path == "fused":
         autograd_api = measure_autograd(args, scene, views, targets_dev, targets_host, world, device, views_total)
 
+    tr_ranged = args.path == "fused" and tr.fused.batch_sh and (
+        tr.fused.range_backward if tr.fused.range_backward is not None else world > 1)
     prof = kernel_profile(tr, steps=1)
     launches = sum(v["kernels"] for v in prof.values())
     default = (args.gaussians, args.width, args.height) == (6_000_000, 1920, 1080)
@@ -885,6 +915,7 @@ def run_ours(args):
     extra = {}
     if world > 1:
         extra["allreduce"] = measure_allreduce(tr.flat, world)
+        extra["allreduce"]["nccl_algorithms"] = nccl_algorithms(nccl_log)
         extra["dp_check"] = dp_check(device, rank, world)
     if rank == 0 and world == 1:
         if not args.no_optimizer:
@@ -914,6 +945,7 @@ def run_ours(args):
             "path": ("gswarp_b200.training.FusedViewStep (C ABI stages, fused photometric loss, preprocess "
                      "backward accumulating into the flat gradient buffer)" if args.path == "fused" else
                      "GaussianRasterizer + fused_ssim under autograd, ViewShardedStep"),
+            "backward_order": (("ranges" if tr_ranged else "views") if args.path == "fused" else None),
             "autograd_api": autograd_api,
             "gpu_launches": launches * args.steps,
             "roofline": rl,

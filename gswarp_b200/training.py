@@ -201,6 +201,10 @@ class FusedViewStep:
         # range-ordered backward: None = when a process group is in use (on one GPU the per-view
         # preprocess backward overlaps the next view's forward on the other stream instead)
         self.range_backward: bool | None = None
+        # view-by-view order with a process group: 0 = SH backward, then one all-reduce of the buffer;
+        # n > 0 = the blocks complete after the last view are all-reduced while the SH backward runs in
+        # n Gaussian ranges, each range's SH rows while the next is computed, the means last
+        self.sh_reduce_chunks = 0
         # 3DGS densification statistics, accumulated per view until reset_densify_stats():
         # xyz_gradient_accum += |d loss / d means2D (x, y)|, denom += 1 and max_radii2D = max(., radius)
         # for every Gaussian with a radius in the view
@@ -418,14 +422,39 @@ class FusedViewStep:
                 # the last view's event follows every earlier one (each view's accumulation waits for the
                 # previous)
                 main.wait_event(prev)
-                if self.batch_sh:
-                    pl.sh_backward_views(means, sh, self._sh_degree, self._campos, self._grad_colors,
-                                         self.grads.views[4], self.grads.views[0])
-                self.grads.all_reduce(self.group)
+                if self.batch_sh and _distributed(self.group) and self.sh_reduce_chunks > 0:
+                    self._sh_backward_and_reduce()
+                else:
+                    if self.batch_sh:
+                        pl.sh_backward_views(means, sh, self._sh_degree, self._campos, self._grad_colors,
+                                             self.grads.views[4], self.grads.views[0])
+                    self.grads.all_reduce(self.group)
             # errors flagged by the last view's emit and sort (earlier views' are read by the next
             # view's binning): raised by this call, before anyone uses its gradients
             pl.raise_device_errors(self.device)
         return self.losses
+
+    def _sh_backward_and_reduce(self) -> None:
+        """All-reduces (on NCCL's stream) while the SH backward runs: first the
+        scales, rotations and opacities (complete after the last view), then
+        the SH rows range by range, each while the next range is computed,
+        and the means last (the SH backward adds their view-direction term).
+        The sums are elementwise, so the result equals one all-reduce of the
+        whole buffer."""
+        means, _, _, _, sh = self.params
+        P = means.shape[0]
+        flat = self.grads.flat
+        blocks = [v.numel() // P if P else 0 for v in self.grads.views]
+        whole = range_slices(P, blocks, 0, P)
+        works = [torch.distributed.all_reduce(flat[whole[1][0]:whole[3][1]], group=self.group, async_op=True)]
+        for b, e in backward_ranges(P, self.sh_reduce_chunks):
+            pl.sh_backward_views(means, sh, self._sh_degree, self._campos, self._grad_colors, self.grads.views[4],
+                                 self.grads.views[0], begin=b, end=e)
+            lo, hi = range_slices(P, blocks, b, e)[4]
+            works.append(torch.distributed.all_reduce(flat[lo:hi], group=self.group, async_op=True))
+        works.append(torch.distributed.all_reduce(flat[whole[0][0]:whole[0][1]], group=self.group, async_op=True))
+        for w in works:
+            w.wait()
 
     def _ranged_backward(self, states: list) -> None:
         """The second half of a multi-view step, on the current stream, one

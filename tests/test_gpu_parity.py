@@ -47,6 +47,14 @@ def _scene(name, dev):
         scene = wl.config2_scene(seed=4, n=20_000)
         scene.scales = scene.scales * 12.0
         view = wl.config2_view(seed=4, width=333, height=197)
+    elif name == "crowded_tiles":
+        # 12 tiles holding up to ~30K pairs each (the per-tile depth sort's
+        # long-segment path, several chunks) and 2,000 Gaussians sharing the
+        # depth bits of others (ties broken by point index)
+        scene = wl.config2_scene(seed=6, n=30_000)
+        scene.scales = scene.scales * 8.0
+        scene.means[-2000:] = scene.means[:2000] + torch.tensor([0.01, -0.01, 0.0])
+        view = wl.look_at_view([0.0, 0.0, -14.0], [0.0, 0.0, 0.0], [0.0, -1.0, 0.0], 40.0, 64, 48)
     elif name == "single_tile":
         # a 16x16 image: one tile, so the tile sort has no pass
         scene, _ = wl.config1_scene(seed=1, n=300)
@@ -91,8 +99,8 @@ def _bits(a):
     return np.ascontiguousarray(a).view(np.uint32)
 
 
-@pytest.mark.parametrize("name", ["cfg1", "cfg2_200k", "cfg2_small_view", "cfg2_big_footprints", "single_tile",
-                                  "single_pair"])
+@pytest.mark.parametrize("name", ["cfg1", "cfg2_200k", "cfg2_small_view", "cfg2_big_footprints", "crowded_tiles",
+                                  "single_tile", "single_pair"])
 @pytest.mark.parametrize("mode", [1, 0, 2])
 def test_preprocess_and_binning_bit_exact(cuda, name, mode):
     if name in ("cfg2_200k", "single_tile", "single_pair") and mode != 1:
