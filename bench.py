@@ -59,8 +59,8 @@ def parse():
     p.add_argument("--no-optimizer", action="store_true", help="skip the fused Adam measurement")
     p.add_argument("--path", default="fused", choices=["fused", "autograd"],
                    help="the measured path: the fused training step, or the drop-in autograd path alone")
-    p.add_argument("--backward-order", default="auto", choices=["auto", "views", "ranges"],
-                   help="fused step: per-view backward, range-ordered backward, or auto (ranges with N > 1)")
+    p.add_argument("--backward-order", default="views", choices=["views", "ranges"],
+                   help="fused step: per-view backward (default) or the range-ordered backward")
     return p.parse_args()
 
 
@@ -878,7 +878,7 @@ def run_ours(args):
     targets_dev = [wl.target_image(rank * V + i, args.height, args.width).to(device) for i in range(V)]
     targets_host = [t.cpu().pin_memory() for t in targets_dev] if not args.no_e2e else None
     tr = Trainer(scene, views, targets_dev, targets_host, world, device, path=args.path)
-    if args.path == "fused" and args.backward_order != "auto":
+    if args.path == "fused":
         tr.fused.range_backward = args.backward_order == "ranges"
 
     # device-resident timing with clock sampling
@@ -901,8 +901,7 @@ def run_ours(args):
     if not args.no_autograd and args.path == "fused":
         autograd_api = measure_autograd(args, scene, views, targets_dev, targets_host, world, device, views_total)
 
-    tr_ranged = args.path == "fused" and tr.fused.batch_sh and (
-        tr.fused.range_backward if tr.fused.range_backward is not None else world > 1)
+    tr_ranged = args.path == "fused" and tr.fused.batch_sh and bool(tr.fused.range_backward)
     prof = kernel_profile(tr, steps=1)
     launches = sum(v["kernels"] for v in prof.values())
     default = (args.gaussians, args.width, args.height) == (6_000_000, 1920, 1080)

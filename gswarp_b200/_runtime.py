@@ -40,7 +40,7 @@ _AUTO_TUNE_VERBOSE = True
 # (gsb_block_dim): the sm_100a shapes are fixed at compile time.
 KERNEL_CLASSES = (
     "preprocess", "preprocess_sh16", "sh_colors_views", "binning_scan", "binning_emit", "radix_sort",
-    "render_forward", "render_backward", "backward_preprocess", "backward_preprocess_sh16", "sh_backward_views",
+    "render_forward", "render_backward", "render_backward_small_grid", "backward_preprocess", "backward_preprocess_sh16", "sh_backward_views",
     "ssim_fwd", "ssim_bwd", "ssim_fwd_h", "ssim_fwd_v", "ssim_bwd_h", "ssim_bwd_v", "knn_morton", "knn_gather",
     "knn_box_minmax", "knn_box_dist", "knn_search", "adam",
 )

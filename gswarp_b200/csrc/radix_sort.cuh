@@ -1,18 +1,19 @@
 // radix_sort.cuh -- stable LSD radix sort of (uint32 key, uint32 value) pairs.
 //
 // Replaces Warp's wp.utils.radix_sort_pairs (called from gswarp
-// memory.py:571-600 and knn.py:337-341) with a reduce-then-scan design for
-// sm_100a, 8 key bits a pass:
-//   1. one histogram kernel computes the digit histograms of every pass in a
-//      single read of the keys (per-warp shared sub-histograms);
+// memory.py:571-600 and knn.py:337-341) with a single-pass-per-digit
+// ("onesweep") design for sm_100a:
+//   1. one histogram kernel computes the 8-bit digit histograms of every
+//      pass in a single read of the keys (warp-aggregated shared atomics);
 //   2. a tiny kernel turns them into per-pass bin bases;
-//   3. each pass: a count kernel writes every 3840-key tile's digit counts,
-//      a scan kernel (a CTA per digit) turns them into the tiles' output
-//      offsets, and a scatter kernel ranks each tile's keys stably per warp
-//      (per-bit ballots), stages the tile in digit order in shared memory
-//      and writes it out in runs.
-// No CTA waits on another (the offsets are known before the scatter starts),
-// at the cost of reading the keys once more per pass.
+//   3. each pass is ONE kernel: a CTA claims the next 3840-key tile through
+//      an atomic counter, ranks its keys stably per warp (per-bit ballots),
+//      publishes its per-digit counts, resolves its global offsets by
+//      decoupled look-back over the preceding tiles, stages the tile in
+//      digit order in shared memory and writes it out in runs.
+// Tiles are claimed in launch order, so every tile a CTA waits on belongs to
+// a CTA that is already running; each look-back spin is nevertheless bounded
+// (SPIN_LIMIT) and reports ERR_LOOKBACK_TIMEOUT instead of hanging.
 #pragma once
 
 #include <algorithm>
@@ -31,6 +32,7 @@ constexpr int WARPS = THREADS / 32;
 constexpr int ITEMS = 15;
 constexpr int TILE_KEYS = THREADS * ITEMS;  // 3840
 constexpr int MAX_PASSES = 4;
+constexpr int LOOKBACK_WINDOW = 4;
 constexpr int HIST_ITEMS = 8;
 
 constexpr unsigned long long FLAG_AGG = 1ull << 62;
@@ -131,73 +133,31 @@ __global__ void __launch_bounds__(THREADS) bin_base_kernel(const unsigned* __res
   bin_base[p * RADIX + threadIdx.x] = block_exclusive_scan(c, s_warp, nullptr);
 }
 
-// Pass step 1: every tile's digit counts, digit-major (counts[d * tiles + t]),
-// zero for tiles past the element count.
-__global__ void __launch_bounds__(THREADS) tile_count_kernel(const unsigned* __restrict__ keys, int n_host,
-                                                             const int* __restrict__ n_dev, int shift,
-                                                             unsigned* __restrict__ counts, int tiles) {
-  __shared__ unsigned s_count[RADIX];
-  const int tid = threadIdx.x;
-  const int n = n_dev ? *n_dev : n_host;
-  s_count[tid] = 0u;
-  __syncthreads();
-  const long long base = (long long)blockIdx.x * TILE_KEYS;
-  unsigned key[ITEMS];
-#pragma unroll
-  for (int i = 0; i < ITEMS; ++i) {
-    const long long pos = base + i * THREADS + tid;
-    key[i] = pos < n ? __ldg(keys + pos) : 0u;
-  }
-#pragma unroll
-  for (int i = 0; i < ITEMS; ++i)
-    if (base + i * THREADS + tid < n) atomicAdd(&s_count[(key[i] >> shift) & (RADIX - 1)], 1u);
-  __syncthreads();
-  counts[(size_t)tid * tiles + blockIdx.x] = s_count[tid];
-}
-
-// Pass step 2: one CTA per digit turns its row of tile counts into the
-// tiles' global output offsets for that digit: the digit's base (all keys of
-// smaller digits) plus an exclusive scan over the tiles, in place.
-__global__ void __launch_bounds__(THREADS) tile_offset_kernel(unsigned* __restrict__ counts, int tiles,
-                                                              const unsigned* __restrict__ bin_base) {
-  __shared__ unsigned s_warp[WARPS];
-  unsigned* row = counts + (size_t)blockIdx.x * tiles;
-  unsigned carry = bin_base[blockIdx.x];
-  for (int t0 = 0; t0 < tiles; t0 += THREADS) {
-    const int t = t0 + threadIdx.x;
-    const unsigned c = t < tiles ? row[t] : 0u;
-    unsigned total;
-    const unsigned ex = block_exclusive_scan(c, s_warp, &total);
-    if (t < tiles) row[t] = carry + ex;
-    carry += total;
-  }
-}
-
-// Pass step 3: a CTA per tile ranks its keys stably per warp (per-bit
-// ballots, the rounds of a warp holding consecutive keys), stages the tile in
-// digit order in shared memory and writes it out in runs at the offsets of
-// step 2.  No tile waits on another.
 template <bool HAS_VALS>
-__global__ void __launch_bounds__(THREADS, 4) scatter_kernel(
+__global__ void __launch_bounds__(THREADS, 4) onesweep_kernel(
     const unsigned* __restrict__ keys_in, const unsigned* __restrict__ vals_in,
     unsigned* __restrict__ keys_out, unsigned* __restrict__ vals_out, int n_host,
-    const int* __restrict__ n_dev, int shift, const unsigned* __restrict__ offsets, int tiles,
-    int* __restrict__ ranges, int range_keys) {
+    const int* __restrict__ n_dev, int shift,
+    const unsigned* __restrict__ bin_base, unsigned long long* __restrict__ lookback,
+    unsigned* __restrict__ tile_counter, long long* __restrict__ err, int* __restrict__ ranges,
+    int range_keys) {
   __shared__ unsigned s_keys[TILE_KEYS];
   __shared__ unsigned s_vals[HAS_VALS ? TILE_KEYS : 1];
   __shared__ unsigned s_warp_hist[WARPS][RADIX];
   __shared__ unsigned s_digit_start[RADIX];
   __shared__ unsigned s_global[RADIX];
   __shared__ unsigned s_scan[WARPS];
+  __shared__ int s_tile;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  // With a device-side count the grid is sized for the upper bound.
+  // With a device-side count the grid is sized for the upper bound; CTAs
+  // that claim a tile past the end leave (no later tile waits on them).
   const int n = n_dev ? *n_dev : n_host;
-  const int tile = blockIdx.x;
-  if ((long long)tile * TILE_KEYS >= n) return;
+  if (tid == 0) s_tile = (int)atomicAdd(tile_counter, 1u);
   for (int i = tid; i < WARPS * RADIX; i += THREADS) (&s_warp_hist[0][0])[i] = 0u;
-  s_global[tid] = offsets[(size_t)tid * tiles + tile];
   __syncthreads();
+  const int tile = s_tile;
+  if ((long long)tile * TILE_KEYS >= n) return;
   const long long base = (long long)tile * TILE_KEYS + (long long)warp * (ITEMS * 32);
 
   unsigned key[ITEMS], rank[ITEMS];
@@ -235,10 +195,13 @@ __global__ void __launch_bounds__(THREADS, 4) scatter_kernel(
     s_warp_hist[w][tid] = total;
     total += c;
   }
+  unsigned long long* my_slot = lookback + (size_t)tile * RADIX + tid;
+  st_volatile(my_slot, (tile == 0 ? FLAG_INC : FLAG_AGG) | (unsigned long long)total);
   s_digit_start[tid] = block_exclusive_scan(total, s_scan, nullptr);
   __syncthreads();
 
-  // Stage the tile in digit order; values are read here, not earlier.
+  // Stage the tile in digit order (before the look-back, so the key and rank
+  // registers are free while it waits); values are read here, not earlier.
 #pragma unroll
   for (int i = 0; i < ITEMS; ++i) {
     if (rank[i] != 0xFFFFFFFFu) {
@@ -258,6 +221,45 @@ __global__ void __launch_bounds__(THREADS, 4) scatter_kernel(
     for (int i = 0; i < ITEMS; ++i)
       if (rank[i] != 0xFFFFFFFFu) s_vals[rank[i]] = val[i];
   }
+
+  // Decoupled look-back over a window of LOOKBACK_WINDOW predecessors at a
+  // time: the window's status words are loaded together (one memory round
+  // trip per window instead of one per tile), then consumed nearest first,
+  // adding aggregates until an inclusive prefix is found.  A slot that is not
+  // published yet is re-read (bounded) before the walk moves past it.
+  unsigned long long excl = 0;
+  if (tile > 0) {
+    int t = tile - 1;
+    int spins = 0;
+    bool done = false;
+    while (!done) {
+      unsigned long long w[LOOKBACK_WINDOW];
+#pragma unroll
+      for (int k = 0; k < LOOKBACK_WINDOW; ++k)
+        w[k] = t - k >= 0 ? ld_volatile(lookback + (size_t)(t - k) * RADIX + tid) : FLAG_INC;
+#pragma unroll
+      for (int k = 0; k < LOOKBACK_WINDOW; ++k) {
+        if (done) break;
+        unsigned long long v = w[k];
+        while ((v & ~VALUE_MASK) == 0) {
+          if (++spins > SPIN_LIMIT) {
+            atomicOr((unsigned long long*)err, (unsigned long long)ERR_LOOKBACK_TIMEOUT);
+            break;
+          }
+          v = ld_volatile(lookback + (size_t)(t - k) * RADIX + tid);
+        }
+        if ((v & ~VALUE_MASK) == 0) {  // timed out: give up, error already flagged
+          done = true;
+          break;
+        }
+        if (t - k >= 0) excl += v & VALUE_MASK;
+        if ((v & ~VALUE_MASK) == FLAG_INC || t - k <= 0) done = true;
+      }
+      t -= LOOKBACK_WINDOW;
+    }
+    st_volatile(my_slot, FLAG_INC | (excl + total));
+  }
+  s_global[tid] = bin_base[tid] + (unsigned)excl;
   __syncthreads();
   const long long tile_base = (long long)tile * TILE_KEYS;
   const int tile_n = (int)min((long long)TILE_KEYS, (long long)n - tile_base);
@@ -265,8 +267,8 @@ __global__ void __launch_bounds__(THREADS, 4) scatter_kernel(
     const unsigned k = s_keys[j];
     const unsigned d = (k >> shift) & (RADIX - 1);
     const unsigned dst = s_global[d] + (unsigned)j - s_digit_start[d];
-    // dst < n whenever the counts and the keys agree (the test keeps any
-    // write inside the output)
+    // dst < n whenever the histogram and look-back agree; the test keeps a
+    // timed-out look-back (flagged above) from writing out of bounds.
     if (dst < (unsigned)n) {
       keys_out[dst] = k;
       if (HAS_VALS) vals_out[dst] = s_vals[j];
@@ -295,10 +297,11 @@ __global__ void ranges_fixup_kernel(int keys, int n, int* __restrict__ ranges) {
 
 // Workspace layout for sorting n pairs with `passes` 8-bit passes.
 struct SortScratch {
-  unsigned* hist;      // passes*256
-  unsigned* bin_base;  // passes*256
-  unsigned* counts;    // 256*tiles, reused by every pass
-  size_t zero_bytes;   // bytes to clear from `hist` on
+  unsigned* hist;                  // passes*256
+  unsigned* bin_base;              // passes*256
+  unsigned* counters;              // passes
+  unsigned long long* lookback;    // passes*tiles*256
+  size_t zero_bytes;               // bytes to clear from `hist` on
 };
 
 __host__ inline int num_tiles(long long n) { return (int)((n + TILE_KEYS - 1) / TILE_KEYS); }
@@ -306,24 +309,29 @@ __host__ inline int num_tiles(long long n) { return (int)((n + TILE_KEYS - 1) / 
 __host__ inline size_t scratch_bytes(long long n, int passes) {
   const size_t tiles = (size_t)num_tiles(n > 0 ? n : 1);
   size_t b = 0;
-  b += (size_t)passes * RADIX * 4;  // hist
-  b += (size_t)passes * RADIX * 4;  // bin_base
+  b += (size_t)passes * RADIX * 4;   // hist
+  b += (size_t)passes * RADIX * 4;   // bin_base
+  b += 256;                          // counters (padded)
   b = (b + 255) & ~(size_t)255;
-  b += (size_t)RADIX * tiles * 4;   // tile counts / offsets
+  b += (size_t)passes * tiles * RADIX * 8;
   return b + 256;
 }
 
 __host__ inline SortScratch carve_scratch(void* base, long long n, int passes) {
+  const size_t tiles = (size_t)num_tiles(n > 0 ? n : 1);
   char* p = (char*)(((uintptr_t)base + 255) & ~(uintptr_t)255);
   SortScratch s;
+  char* start = p;
   s.hist = (unsigned*)p;
   p += (size_t)passes * RADIX * 4;
   s.bin_base = (unsigned*)p;
   p += (size_t)passes * RADIX * 4;
-  s.zero_bytes = (size_t)passes * RADIX * 4;
+  s.counters = (unsigned*)p;
+  p += 256;
   p = (char*)(((uintptr_t)p + 255) & ~(uintptr_t)255);
-  s.counts = (unsigned*)p;
-  (void)n;
+  s.lookback = (unsigned long long*)p;
+  p += (size_t)passes * tiles * RADIX * 8;
+  s.zero_bytes = (size_t)(p - start);
   return s;
 }
 
@@ -334,13 +342,10 @@ __host__ inline SortScratch carve_scratch(void* base, long long n, int passes) {
 // the device (at most n, which sizes the grids and the scratch).
 // With `ranges` (and n_dev null) the last pass also writes, for every key
 // value below range_keys, its [start, end) in the sorted output into the
-// zero-initialised int2 array `ranges` ((0, 0) for absent keys).  `err` is
-// kept for the callers' error plumbing; no step of the sort waits on
-// another tile, so none can time out.
+// zero-initialised int2 array `ranges` ((0, 0) for absent keys).
 __host__ inline int sort_pairs(unsigned* k[2], unsigned* v[2], long long n, const int* n_dev, int passes,
                                void* scratch, long long* err, cudaStream_t stream, int* ranges = nullptr,
                                int range_keys = 0) {
-  (void)err;
   if ((n <= 1 && !n_dev) || n <= 0 || passes == 0) return 0;
   SortScratch s = carve_scratch(scratch, n, passes);
   cudaMemsetAsync(s.hist, 0, s.zero_bytes, stream);
@@ -350,15 +355,16 @@ __host__ inline int sort_pairs(unsigned* k[2], unsigned* v[2], long long n, cons
   const int tiles = num_tiles(n);
   int cur = 0;
   for (int p = 0; p < passes; ++p) {
+    unsigned long long* lb = s.lookback + (size_t)p * tiles * RADIX;
     int* rg = (p == passes - 1 && !n_dev) ? ranges : nullptr;
-    tile_count_kernel<<<tiles, THREADS, 0, stream>>>(k[cur], (int)n, n_dev, p * RADIX_BITS, s.counts, tiles);
-    tile_offset_kernel<<<RADIX, THREADS, 0, stream>>>(s.counts, tiles, s.bin_base + p * RADIX);
     if (v[0]) {
-      scatter_kernel<true><<<tiles, THREADS, 0, stream>>>(k[cur], v[cur], k[cur ^ 1], v[cur ^ 1], (int)n, n_dev,
-                                                          p * RADIX_BITS, s.counts, tiles, rg, range_keys);
+      onesweep_kernel<true><<<tiles, THREADS, 0, stream>>>(
+          k[cur], v[cur], k[cur ^ 1], v[cur ^ 1], (int)n, n_dev, p * RADIX_BITS, s.bin_base + p * RADIX,
+          lb, s.counters + p, err, rg, range_keys);
     } else {
-      scatter_kernel<false><<<tiles, THREADS, 0, stream>>>(k[cur], nullptr, k[cur ^ 1], nullptr, (int)n, n_dev,
-                                                           p * RADIX_BITS, s.counts, tiles, rg, range_keys);
+      onesweep_kernel<false><<<tiles, THREADS, 0, stream>>>(
+          k[cur], nullptr, k[cur ^ 1], nullptr, (int)n, n_dev, p * RADIX_BITS, s.bin_base + p * RADIX,
+          lb, s.counters + p, err, rg, range_keys);
     }
     cur ^= 1;
   }

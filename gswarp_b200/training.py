@@ -30,18 +30,19 @@ view-direction part of the means gradient.  Per view that removes one SH
 read in the forward and an SH read plus an SH-gradient read-modify-write in
 the backward for every visible Gaussian.
 
-With a process group the multi-view step also reorders the backward, so
-that the exchange overlaps computation instead of starting after it: each
-view stops after its render backward (into its own 48-byte-per-Gaussian
+With a process group the multi-view step all-reduces the blocks that are
+complete after the last view while the SH backward runs, and the SH rows
+range by range as they are produced (``sh_reduce_chunks``).  A
+range-ordered backward (``range_backward``) is also available: each view
+stops after its render backward (into its own 48-byte-per-Gaussian
 accumulator), and the views' preprocess backward then runs one Gaussian
 range at a time -- per range, every view's accumulating preprocess backward
 over its binned ids inside the range (the same kernel and the same
 per-Gaussian order of additions as view by view, so the same bits), then
-the SH backward of the range.  A finished range is final, so its all-reduce
-runs on NCCL's stream while the next range is computed.  On one GPU the
-view-by-view order is kept: there each view's preprocess backward overlaps
-the next view's forward on the other stream, which the range order gives
-up.
+the SH backward of the range -- so that each finished range is all-reduced
+while the next is computed.  It is off by default: it gives up the overlap
+of each view's preprocess backward with the next view's forward, and on 2
+GPUs that cost as much as the exchange it hid.
 
 Gradients equal the autograd path's up to the float summation order of the
 render backward's atomics (tests compare the two).
@@ -198,13 +199,14 @@ class FusedViewStep:
         # backward, one Gaussian range at a time, and each range is all-reduced (with a process group)
         # while the next one is computed
         self.backward_chunks = 8
-        # range-ordered backward: None = when a process group is in use (on one GPU the per-view
-        # preprocess backward overlaps the next view's forward on the other stream instead)
-        self.range_backward: bool | None = None
+        # range-ordered backward (multi-view SH only): off by default -- the per-view preprocess
+        # backward overlaps the next view's forward on the other stream, which the range order gives up,
+        # and on 2 GPUs the exchange it overlaps did not pay for that (25.5 ms per step either way)
+        self.range_backward = False
         # view-by-view order with a process group: 0 = SH backward, then one all-reduce of the buffer;
         # n > 0 = the blocks complete after the last view are all-reduced while the SH backward runs in
         # n Gaussian ranges, each range's SH rows while the next is computed, the means last
-        self.sh_reduce_chunks = 0
+        self.sh_reduce_chunks = 4
         # 3DGS densification statistics, accumulated per view until reset_densify_stats():
         # xyz_gradient_accum += |d loss / d means2D (x, y)|, denom += 1 and max_radii2D = max(., radius)
         # for every Gaussian with a radius in the view
@@ -365,8 +367,7 @@ class FusedViewStep:
         and binning.  Each view finishes its own backward, the accumulations
         into the flat gradient buffer in view order (each waits for the
         previous one), then the multi-view SH backward and the all-reduce
-        run; or, range-ordered (``range_backward``; by default when a
-        process group is in use), every view stops after its render backward
+        run; or, range-ordered (``range_backward``), every view stops after its render backward
         (each into its own accumulator) and the preprocess and SH backward of
         all views run afterwards on this stream, Gaussian range by Gaussian
         range, each range all-reduced while the next is computed."""
@@ -387,8 +388,7 @@ class FusedViewStep:
             else:
                 self.grads.zero_()
             P, V = means.shape[0], len(targets)
-            ranged = self.batch_sh and (self.range_backward if self.range_backward is not None
-                                        else _distributed(self.group))
+            ranged = self.batch_sh and bool(self.range_backward)
             if ranged and (self._view_grad_acc is None or self._view_grad_acc.shape[:2] != (V, P)):
                 self._view_grad_acc = torch.zeros((V, P, _lib.GRAD_FLOATS), dtype=torch.float32, device=self.device)
             self._upload_targets(targets, main)

@@ -1,11 +1,13 @@
 """Two-GPU training step (needs at least two GPUs; skipped otherwise).
 
 Two NCCL ranks, each rendering its own views of the same scene.  The
-multi-view-SH step computes the per-Gaussian backward one Gaussian range at
-a time and all-reduces each finished range while the next one is computed;
-the result must equal (up to the render backward's atomic summation order)
-the per-view-SH step's single all-reduce of the whole buffer, and the sum of
-the ranks' local gradients."""
+multi-view-SH step all-reduces the blocks complete after the last view while
+the SH backward runs, the SH rows range by range and the means last; the
+range-ordered variant computes the per-Gaussian backward one Gaussian range
+at a time and all-reduces each finished range while the next one is
+computed.  Both must equal (up to the render backward's atomic summation
+order) the per-view-SH step's single all-reduce of the whole buffer, and the
+sum of the ranks' local gradients."""
 
 import os
 import socket
@@ -58,8 +60,12 @@ def _worker(rank: int, world: int, port: int) -> None:
         sizes = [p.numel() for p in params]
 
         overlapped = FusedViewStep([p.clone() for p in params], settings, batch_sh=True)
-        overlapped.backward_chunks = 3
+        overlapped.sh_reduce_chunks = 3
         overlapped.step(targets)
+        ranged = FusedViewStep([p.clone() for p in params], settings, batch_sh=True)
+        ranged.range_backward = True
+        ranged.backward_chunks = 3
+        ranged.step(targets)
         plain = FusedViewStep([p.clone() for p in params], settings, batch_sh=False)
         plain.step(targets)
         local = FusedViewStep([p.clone() for p in params], settings, batch_sh=True, group=singles[rank])
@@ -72,6 +78,7 @@ def _worker(rank: int, world: int, port: int) -> None:
         assert float((got - local.grads.flat).norm()) > 1e-3 * float(got.norm())  # the other rank contributed
         _close(got, plain.grads.flat, sizes)
         _close(got, summed, sizes)
+        _close(ranged.grads.flat, summed, sizes)
         # every rank holds the same reduced buffer
         first = got.clone()
         dist.broadcast(first, src=0)

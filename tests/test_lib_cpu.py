@@ -80,6 +80,7 @@ def test_block_dims_are_the_launched_shapes():
     src = (Path(__file__).resolve().parents[1] / "gswarp_b200" / "csrc" / "gsb_launch.cuh").read_text()
     consts = {m.group(1): int(m.group(2)) for m in _re.finditer(r"constexpr int (\w+) = (\d+);", src)}
     expect = {"render_forward": consts["RENDER"], "render_backward": consts["RENDER_BWD"],
+              "render_backward_small_grid": consts["RENDER"],
               "preprocess": consts["PREPROCESS"], "preprocess_sh16": consts["PREPROCESS_SH16"],
               "backward_preprocess_sh16": consts["PREPROCESS_BWD_SH16"], "ssim_fwd_h": consts["SSIM"],
               "knn_box_dist": consts["KNN"], "radix_sort": consts["RADIX_SORT"]}
