@@ -421,9 +421,23 @@ struct BwdSums {
 // the Gaussian's operands); the per-pixel decisions only mask alpha and G.
 // For a contributing pixel every value is the same expression as a scalar
 // evaluation of that pixel, to rounding.
+// One Gaussian at this position applied to a pixel pair back to front (3DGS
+// recurrences accum_rec / last_alpha / last_color, backward_kernels.py:
+// 637-671): updates the pair's state and returns the per-pixel terms the
+// gradient sums are made of; c0 / c1 tell whether each pixel contributed.
+// The arithmetic runs straight through as one packed stream (both pixels
+// share the Gaussian's operands); the per-pixel decisions only mask alpha
+// and G.  For a contributing pixel every value is the same expression as a
+// scalar evaluation of that pixel, to rounding.  A pixel that does not take
+// the Gaussian gets zero terms and an unchanged state.
+struct PairTerms {
+  float2 u, uy, dy, dch;
+};
+
 template <bool DEPTH, bool GA>
-__device__ __forceinline__ void bwd_pair(BwdPair& s, bool e0, bool e1, const float4 cf, float ax, float bx,
-                                         float y, const float4 cd, bool has_bg, BwdSums& m, bool& c0, bool& c1) {
+__device__ __forceinline__ PairTerms bwd_pair_core(BwdPair& s, bool e0, bool e1, const float4 cf, float ax,
+                                                   float bx, float y, const float4 cd, bool has_bg, bool& c0,
+                                                   bool& c1) {
   const float2 neg1 = make_float2(-1.0f, -1.0f);
   const float2 dy = __fadd2_rn(make_float2(y, y), s.nfy);
   const float2 pw = power2_of2(cf, ax, bx, dy);
@@ -455,14 +469,62 @@ __device__ __forceinline__ void bwd_pair(BwdPair& s, bool e0, bool e1, const flo
   s.S = __ffma2_rn(am, __ffma2_rn(s.S, neg1, cg), s.S);
   if (DEPTH) s.adr = __ffma2_rn(am, __ffma2_rn(s.adr, neg1, cdw), s.adr);
   if (GA) s.aar = __ffma2_rn(one_minus2(am), s.aar, am);
-  // the Gaussian's sums over the two pixels, accumulated as pixel 0 then pixel 1
-  m.U = u.x + u.y;
-  m.UY = uy.x + uy.y;
-  m.UYY = __fmaf_rn(uy.y, dy.y, __fmul_rn(uy.x, dy.x));
-  m.dcol0 = __fmaf_rn(dch.y, s.g0.y, __fmul_rn(dch.x, s.g0.x));
-  m.dcol1 = __fmaf_rn(dch.y, s.g1.y, __fmul_rn(dch.x, s.g1.x));
-  m.dcol2 = __fmaf_rn(dch.y, s.g2.y, __fmul_rn(dch.x, s.g2.x));
-  if (DEPTH) m.ddepth = __fmaf_rn(dch.y, s.gd.y, __fmul_rn(dch.x, s.gd.x));
+  return PairTerms{u, uy, dy, dch};
+}
+
+
+// The pair's sums (BwdSums), accumulated as pixel 0 then pixel 1.
+template <bool DEPTH, bool GA>
+__device__ __forceinline__ void bwd_pair(BwdPair& s, bool e0, bool e1, const float4 cf, float ax, float bx,
+                                         float y, const float4 cd, bool has_bg, BwdSums& m, bool& c0, bool& c1) {
+  const PairTerms t = bwd_pair_core<DEPTH, GA>(s, e0, e1, cf, ax, bx, y, cd, has_bg, c0, c1);
+  m.U = t.u.x + t.u.y;
+  m.UY = t.uy.x + t.uy.y;
+  m.UYY = __fmaf_rn(t.uy.y, t.dy.y, __fmul_rn(t.uy.x, t.dy.x));
+  m.dcol0 = __fmaf_rn(t.dch.y, s.g0.y, __fmul_rn(t.dch.x, s.g0.x));
+  m.dcol1 = __fmaf_rn(t.dch.y, s.g1.y, __fmul_rn(t.dch.x, s.g1.x));
+  m.dcol2 = __fmaf_rn(t.dch.y, s.g2.y, __fmul_rn(t.dch.x, s.g2.x));
+  if (DEPTH) m.ddepth = __fmaf_rn(t.dch.y, s.gd.y, __fmul_rn(t.dch.x, s.gd.x));
+}
+
+// Sums of several pairs kept per pixel slot (packed): the first pair stores
+// its terms, later pairs add theirs, and one horizontal add per sum ends the
+// hit -- for two pairs 16 instructions where two BwdSums and their addition
+// take 26.
+struct BwdSums2 {
+  float2 U, UY, UYY, d0, d1, d2, dd;
+};
+
+template <bool DEPTH, bool FIRST>
+__device__ __forceinline__ void sums2_add(BwdSums2& m, const PairTerms& t, const BwdPair& s) {
+  if (FIRST) {
+    m.U = t.u;
+    m.UY = t.uy;
+    m.UYY = __fmul2_rn(t.uy, t.dy);
+    m.d0 = __fmul2_rn(t.dch, s.g0);
+    m.d1 = __fmul2_rn(t.dch, s.g1);
+    m.d2 = __fmul2_rn(t.dch, s.g2);
+    if (DEPTH) m.dd = __fmul2_rn(t.dch, s.gd);
+  } else {
+    m.U = __fadd2_rn(m.U, t.u);
+    m.UY = __fadd2_rn(m.UY, t.uy);
+    m.UYY = __ffma2_rn(t.uy, t.dy, m.UYY);
+    m.d0 = __ffma2_rn(t.dch, s.g0, m.d0);
+    m.d1 = __ffma2_rn(t.dch, s.g1, m.d1);
+    m.d2 = __ffma2_rn(t.dch, s.g2, m.d2);
+    if (DEPTH) m.dd = __ffma2_rn(t.dch, s.gd, m.dd);
+  }
+}
+
+template <bool DEPTH>
+__device__ __forceinline__ void sums2_reduce(const BwdSums2& m2, BwdSums& m) {
+  m.U = m2.U.x + m2.U.y;
+  m.UY = m2.UY.x + m2.UY.y;
+  m.UYY = m2.UYY.x + m2.UYY.y;
+  m.dcol0 = m2.d0.x + m2.d0.y;
+  m.dcol1 = m2.d1.x + m2.d1.y;
+  m.dcol2 = m2.d2.x + m2.d2.y;
+  if (DEPTH) m.ddepth = m2.dd.x + m2.dd.y;
 }
 
 // Backward launch shape: two warps per 16x16 tile, each owning an 8-column x
@@ -512,16 +574,6 @@ __device__ __forceinline__ unsigned cull_quarters(int g, int cnt, const float4* 
         q &= ~(1u << k);
   }
   return q;
-}
-
-__device__ __forceinline__ void add_sums(BwdSums& m, const BwdSums& o, bool depth) {
-  m.U += o.U;
-  m.UY += o.UY;
-  m.UYY += o.UYY;
-  m.dcol0 += o.dcol0;
-  m.dcol1 += o.dcol1;
-  m.dcol2 += o.dcol2;
-  if (depth) m.ddepth += o.ddepth;
 }
 
 // DEPTH: compute_depth with a depth gradient given; GA: an alpha gradient
@@ -653,7 +705,10 @@ __global__ void __launch_bounds__(BWD_THREADS, 11) render_bwd_tile2_kernel(const
         BwdSums m = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
         bool contrib = false;
         float dx = 0.0f;
-        if (e0 || e1 || e2 || e3) {
+        // which pairs the warp runs (warp-uniform; a lane whose pixels do not
+        // take the Gaussian gets zero terms and keeps its state)
+        const bool P0 = __any_sync(FULL, e0 || e1), P1 = __any_sync(FULL, e2 || e3);
+        if (P0 || P1) {
           const float2 xy = s_xy[j];
           const float4 cf = s_cf[j];
           const float4 cd = s_rgbd[j];
@@ -661,16 +716,22 @@ __global__ void __launch_bounds__(BWD_THREADS, 11) render_bwd_tile2_kernel(const
           float ax, bx;
           column_terms(cf, dx, ax, bx);
           bool c0, c1;
-          if (e0 || e1) {
-            bwd_pair<DEPTH, GA>(px[0], e0, e1, cf, ax, bx, xy.y, cd, has_bg, m, c0, c1);
+          BwdSums2 m2;
+          if (P0) {
+            const PairTerms t0 = bwd_pair_core<DEPTH, GA>(px[0], e0, e1, cf, ax, bx, xy.y, cd, has_bg, c0, c1);
             contrib = c0 || c1;
+            sums2_add<DEPTH, true>(m2, t0, px[0]);
+            if (P1) {
+              const PairTerms t1 = bwd_pair_core<DEPTH, GA>(px[1], e2, e3, cf, ax, bx, xy.y, cd, has_bg, c0, c1);
+              contrib = contrib || c0 || c1;
+              sums2_add<DEPTH, false>(m2, t1, px[1]);
+            }
+          } else {
+            const PairTerms t1 = bwd_pair_core<DEPTH, GA>(px[1], e2, e3, cf, ax, bx, xy.y, cd, has_bg, c0, c1);
+            contrib = c0 || c1;
+            sums2_add<DEPTH, true>(m2, t1, px[1]);
           }
-          if (e2 || e3) {
-            BwdSums m2s;
-            bwd_pair<DEPTH, GA>(px[1], e2, e3, cf, ax, bx, xy.y, cd, has_bg, m2s, c0, c1);
-            add_sums(m, m2s, DEPTH);
-            contrib = contrib || c0 || c1;
-          }
+          sums2_reduce<DEPTH>(m2, m);
         }
         if (__any_sync(FULL, contrib)) {
           const float4 con = s_con[j];
