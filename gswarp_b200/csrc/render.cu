@@ -25,9 +25,9 @@
 // per batch from the 48-byte render records (three 16-byte loads per
 // Gaussian); exp is one MUFU.EX2, 1/(1-alpha) one MUFU.RCP.  Backward: the
 // CTA walks its list from the CTA-wide maximum contributor down, each warp
-// skips positions above its own maximum, tests each Gaussian against the four
-// 8x4 quarters of its block (each quarter holds one pixel slot of every lane)
-// so a quarter it cannot reach is skipped warp-wide, a warp vote skips
+// skips positions above its own maximum, tests each Gaussian against the
+// halves of its block that hold whole pixel pairs (so a pair the Gaussian
+// cannot reach is skipped warp-wide), a warp vote skips
 // Gaussians no lane uses, and the ten gradient terms (already summed over the
 // thread's pixels) are reduced across the warp with a 12-shuffle transpose
 // reduction (instead of 10 x 5 butterfly shuffles); 10 lanes then issue one
@@ -533,9 +533,10 @@ __device__ __forceinline__ void sums2_reduce(const BwdSums2& m2, BwdSums& m) {
 // (the column offset dx included).  Against a warp per 8x8 block, a Gaussian
 // that covers both blocks of a column costs one hit -- one cull, one
 // operand load, one 10-term warp reduction and one set of atomics -- for
-// twice the pixels; culling stays at 8x4 granularity (each quarter of the
-// block holds one pixel slot of every lane, so a quarter the Gaussian cannot
-// reach is skipped warp-wide).
+// twice the pixels.  Culling is per 8x8 half (the rows of one pixel pair of
+// every lane): a half the Gaussian cannot reach is a pair the warp skips;
+// testing the four 8x4 quarters instead only masked pixels the per-pixel
+// alpha test rejects anyway, and cost 4% more time.
 constexpr int BWD_THREADS = launch::RENDER_BWD;
 // Grids of at least this many tiles use the two-warp kernel (more pixels per
 // hit); smaller ones the four-warp kernel (a shorter heaviest tile): at
@@ -551,29 +552,27 @@ __device__ __forceinline__ void bwd_pixels_of(int tile, int gx, int& px, int& py
   py0 = ty * BLOCK_Y + (lane >> 3);
 }
 
-// Which quarters (rows y0+4k .. y0+4k+3, k = 0..3) of the warp's 8x16 block
+// Which 8x8 halves (rows y0..y0+7, y0+8..y0+15) of the warp's 8x16 block
 // staged Gaussian g can reach: box test, then the exact ellipse test per
-// quarter (same tests as the forward's block test, same widened threshold).
-__device__ __forceinline__ unsigned cull_quarters(int g, int cnt, const float4* s_box, const float2* s_xy,
-                                                  const float4* s_el, float x0, float x1, float y0) {
-  unsigned q = 0;
+// half (the forward's block test, same widened threshold).  A half decides
+// whether its pixel pair runs; a pixel inside a reached half that the
+// Gaussian does not reach fails the per-pixel alpha test and is left as is.
+__device__ __forceinline__ void cull_halves8(int g, int cnt, const float4* s_box, const float2* s_xy,
+                                             const float4* s_el, float x0, float x1, float y0, bool& top,
+                                             bool& bot) {
+  top = bot = false;
   if (g < cnt) {
     const float4 b = s_box[g];
-    if (b.x <= x1 && b.y >= x0) {
-#pragma unroll
-      for (int k = 0; k < 4; ++k)
-        if (b.z <= y0 + 4.0f * k + 3.0f && b.w >= y0 + 4.0f * k) q |= 1u << k;
-    }
+    const bool xs = b.x <= x1 && b.y >= x0;
+    top = xs && b.z <= y0 + 7.0f && b.w >= y0;
+    bot = xs && b.z <= y0 + 15.0f && b.w >= y0 + 8.0f;
   }
-  if (__any_sync(FULL, q != 0) && q) {
+  if (__any_sync(FULL, top || bot) && (top || bot)) {
     const float2 c = s_xy[g];
     const float4 e = s_el[g];
-#pragma unroll
-    for (int k = 0; k < 4; ++k)
-      if ((q >> k) & 1u && !ellipse_hits(c.x, c.y, e, x0, x1, y0 + 4.0f * k, y0 + 4.0f * k + 3.0f))
-        q &= ~(1u << k);
+    if (top) top = ellipse_hits(c.x, c.y, e, x0, x1, y0, y0 + 7.0f);
+    if (bot) bot = ellipse_hits(c.x, c.y, e, x0, x1, y0 + 8.0f, y0 + 15.0f);
   }
-  return q;
 }
 
 // DEPTH: compute_depth with a depth gradient given; GA: an alpha gradient
@@ -685,19 +684,20 @@ __global__ void __launch_bounds__(BWD_THREADS, 11) render_bwd_tile2_kernel(const
     }
     __syncthreads();
     const int top = min(hi, warp_max);
-    // Lanes test staged Gaussians against the warp's four quarters; the warp
+    // Lanes test staged Gaussians against the warp's two 8x8 halves; the warp
     // visits only the hits below its own maximum, back to front.
     for (int cb = ((top - lo - 1) >> 5) << 5; cb >= 0 && top > lo; cb -= 32) {
-      const unsigned q = cull_quarters(cb + lane, top - lo, s_box, s_xy, s_el, bx0, bx1, by0);
-      const unsigned m0 = __ballot_sync(FULL, q & 1u), m1 = __ballot_sync(FULL, q & 2u);
-      const unsigned m2 = __ballot_sync(FULL, q & 4u), m3 = __ballot_sync(FULL, q & 8u);
-      unsigned hits = m0 | m1 | m2 | m3;
+      bool h_top, h_bot;
+      cull_halves8(cb + lane, top - lo, s_box, s_xy, s_el, bx0, bx1, by0, h_top, h_bot);
+      const unsigned m0 = __ballot_sync(FULL, h_top), m2 = __ballot_sync(FULL, h_bot);
+      const unsigned m1 = m0, m3 = m2;
+      unsigned hits = m0 | m2;
       while (hits) {
         const int bit = 31 - __clz(hits);
         const int j = cb + bit;
         hits &= ~(1u << bit);
         const int pos = lo + j;
-        // a quarter the Gaussian cannot reach has alpha < 1/255 at every pixel: no state change to skip
+        // a half the Gaussian cannot reach has alpha < 1/255 at every pixel: no state change to skip
         const bool e0 = ((m0 >> bit) & 1u) && pos < px[0].lc0;
         const bool e1 = ((m1 >> bit) & 1u) && pos < px[0].lc1;
         const bool e2 = ((m2 >> bit) & 1u) && pos < px[1].lc0;
