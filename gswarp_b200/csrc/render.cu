@@ -737,9 +737,10 @@ __global__ void __launch_bounds__(BWD_THREADS, 11) render_bwd_tile2_kernel(const
 
 // Backward for grids of few tiles: one 128-thread CTA per tile, each warp an
 // 8x8 block, each thread two pixels (rows y, y+4) as one packed pair, culled
-// per block (−3% on an 800x800 view against a test per 8x4 half).  When the grid holds fewer tiles than the GPU holds CTAs,
-// the kernel lasts as long as its heaviest tile, and four warps per tile
-// finish it sooner than two.  DEPTH: compute_depth with a depth gradient
+// per block (3% faster on an 800x800 view than a test per 8x4 half).  When
+// the grid holds fewer tiles than the GPU holds CTAs, the kernel lasts as
+// long as its heaviest tile, and four warps per tile finish it sooner than
+// two.  DEPTH: compute_depth with a depth gradient
 // given; GA: an alpha gradient given.  Without them those terms are exactly
 // zero and are not evaluated.
 template <bool DEPTH, bool GA>
