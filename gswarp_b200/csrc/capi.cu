@@ -50,7 +50,7 @@ GSB_EXPORT int gsb_block_dim(const char* kernel_class) {
       {"radix_sort", RADIX_SORT},
       {"render_forward", RENDER},
       {"render_backward", RENDER_BWD},
-      {"render_backward_small_grid", RENDER},  // grids of fewer than 4,096 tiles
+      {"render_backward_small_grid", RENDER},  // grids of fewer than 6,000 tiles
       {"backward_preprocess", PREPROCESS_BWD},
       {"backward_preprocess_sh16", PREPROCESS_BWD_SH16},
       {"sh_backward_views", SH_BACKWARD_VIEWS},

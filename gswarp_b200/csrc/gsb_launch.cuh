@@ -13,7 +13,7 @@ constexpr int BINNING_SCAN = 256;        // compact_kernel, depth_scan_kernel
 constexpr int BINNING_EMIT = 256;        // emit_binrec_kernel, emit_kernel
 constexpr int RADIX_SORT = 256;          // histogram_kernel, onesweep_kernel, bin_base_kernel
 constexpr int RENDER = 128;              // render_fwd_kernel, render_bwd_tile4_kernel (16x16 tile, 2 px/thread)
-constexpr int RENDER_BWD = 64;           // render_bwd_tile2_kernel (16x16 tile, 4 px/thread; grids of >= 4,096 tiles)
+constexpr int RENDER_BWD = 64;           // render_bwd_tile2_kernel (16x16 tile, 4 px/thread; grids of >= 6,000 tiles)
 constexpr int PREPROCESS_BWD = 256;      // preprocess_bwd_kernel, no SH or SH rows of any width
 constexpr int PREPROCESS_BWD_SH16 = 128; // preprocess_bwd_kernel with (P,16,3) SH rows staged per warp
 constexpr int SH_BACKWARD_VIEWS = 128;   // sh_backward_views_kernel

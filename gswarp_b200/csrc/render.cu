@@ -13,7 +13,7 @@
 // B200 design.  Forward: one 128-thread CTA per 16x16 tile; each thread owns
 // TWO pixels (rows y and y+4 of its warp's 8x8 block), so every Gaussian
 // staged in shared memory is read once per two pixels and the per-(warp,
-// Gaussian) control work covers 64 pixels.  Backward, on grids of 4,096
+// Gaussian) control work covers 64 pixels.  Backward, on grids of 6,000
 // tiles or more: one 64-thread CTA per tile; each warp owns an 8x16 column
 // block and each thread FOUR pixels (rows y, y+4, y+8, y+12) as two packed
 // pairs, so the per-(warp, Gaussian) work that does not scale with pixels --
@@ -515,10 +515,12 @@ __device__ __forceinline__ void sums2_reduce(const BwdSums2& m2, BwdSums& m) {
 // alpha test rejects anyway, and cost 4% more time.
 constexpr int BWD_THREADS = launch::RENDER_BWD;
 // Grids of at least this many tiles use the two-warp kernel (more pixels per
-// hit); smaller ones the four-warp kernel (a shorter heaviest tile): at
-// 1920x1080 (8,160 tiles) the former is 5% faster, at 800x800 (2,500 tiles)
-// the latter 18%.
-constexpr int BWD_TILE2_MIN_TILES = 4096;
+// hit); smaller ones the four-warp kernel (a shorter heaviest tile).  Render
+// backward, 1M / 3M / 6M Gaussians, two-warp against four-warp kernel (ms):
+// 1245x825 (4,056 tiles) 0.63/0.61, 0.86/0.83, 0.85/0.83; 1600x1063 (6,700)
+// 0.76/0.74, 1.04/1.05, 1.02/1.05; 1920x1080 (8,160) 0.75/0.78, 1.05/1.11,
+// 1.04/1.11; 2560x1440 (14,400) 0.98/1.08, 1.40/1.55, 1.40/1.56.
+constexpr int BWD_TILE2_MIN_TILES = 6000;
 
 // The thread's column and first row (slot k is row py0 + 4k).
 __device__ __forceinline__ void bwd_pixels_of(int tile, int gx, int& px, int& py0) {

@@ -62,8 +62,8 @@ const char* gsb_last_error(void);
  * the sm_100a launch shapes are fixed at compile time, and this reports the
  * shapes actually launched.  Classes: preprocess, preprocess_sh16,
  * sh_colors_views, binning_scan, binning_emit, radix_sort, render_forward,
- * render_backward (grids of 4,096 tiles and more), render_backward_small_grid, backward_preprocess, backward_preprocess_sh16,
- * sh_backward_views, ssim_fwd, ssim_bwd (and the reference's ssim_fwd_h,
+ * render_backward (grids of 6,000 tiles and more), render_backward_small_grid,
+ * backward_preprocess, backward_preprocess_sh16, sh_backward_views, ssim_fwd, ssim_bwd (and the reference's ssim_fwd_h,
  * ssim_fwd_v, ssim_bwd_h, ssim_bwd_v), knn_morton, knn_gather,
  * knn_box_minmax, knn_box_dist, knn_search, adam. */
 int gsb_block_dim(const char* kernel_class);
