@@ -362,6 +362,54 @@ __device__ __forceinline__ int warp_reduce10(const float (&v)[10], float& out) {
   return off < 0 ? -1 : (b4 ? 5 : 0) + off;
 }
 
+// One halving stage of a transpose reduction: lanes whose `bit` is clear keep
+// the first ceil(N/2) values and send the rest (zero-padded), lanes whose bit
+// is set keep the rest and send the first, to the lane `xmask` apart.
+template <int N>
+__device__ __forceinline__ void halve(const float (&in)[N], float (&out)[(N + 1) / 2], bool bit, int xmask) {
+  constexpr int H = (N + 1) / 2;
+#pragma unroll
+  for (int k = 0; k < H; ++k) {
+    const float lo = in[k];
+    const float hi = (k + H < N) ? in[k + H] : 0.0f;
+    const float send = bit ? lo : hi;
+    const float keep = bit ? hi : lo;
+    out[k] = keep + __shfl_xor_sync(FULL, send, xmask);
+  }
+}
+
+// Transpose reduction of twenty per-lane values over a warp (21 shuffles,
+// against 24 for two ten-value reductions): on return each of the values'
+// warp totals sits in one lane; the returned index is the value held
+// (0..19), or -1 for the twelve lanes left with padding.
+__device__ __forceinline__ int warp_reduce20(const float (&v)[20], float& out) {
+  const int lane = threadIdx.x & 31;
+  float a[10], b[5], c[3], d[2], e[1];
+  halve<20>(v, a, lane & 16, 16);
+  halve<10>(a, b, lane & 8, 8);
+  halve<5>(b, c, lane & 4, 4);
+  halve<3>(c, d, lane & 2, 2);
+  halve<2>(d, e, lane & 1, 1);
+  out = e[0];
+  // the original index of the kept value: each stage halves the slots and
+  // keeps the upper half (offset ceil(slots/2)) where the lane's bit is set;
+  // real values fill the lowest slots, so n counts those still held
+  int idx = 0, n = 20, slots = 20;
+  const int bits[5] = {lane & 16, lane & 8, lane & 4, lane & 2, lane & 1};
+#pragma unroll
+  for (int st = 0; st < 5; ++st) {
+    const int h = (slots + 1) / 2;
+    if (bits[st]) {
+      idx += h;
+      n -= h;
+    } else {
+      n = n < h ? n : h;
+    }
+    slots = h;
+  }
+  return n >= 1 ? idx : -1;
+}
+
 // Back-to-front state of the thread's two pixels (backward_kernels.py:
 // 606-625), one f32x2 component per pixel.  The colour part of accum_rec
 // only enters dL/dalpha through its dot product with the pixel's colour
@@ -638,6 +686,23 @@ __global__ void __launch_bounds__(BWD_THREADS, 11) render_bwd_tile2_kernel(const
     my_mul_op = slot == 0 ? -half_w : slot == 1 ? -half_h : (slot >= 3 && slot <= 5) ? -0.5f : 0.0f;
     my_mul_one = (slot == 2 || slot >= 6) ? 1.0f : 0.0f;
   }
+  // the same for the twenty-value reduction of two hits (values 10..19: the second hit)
+  bool my_writer20, my_second20;
+  int my_off20;
+  float my_mul_op20, my_mul_one20;
+  {
+    float dummy[20];
+#pragma unroll
+    for (int k = 0; k < 20; ++k) dummy[k] = 0.0f;
+    float unused;
+    const int idx = warp_reduce20(dummy, unused);
+    const int slot = idx >= 10 ? idx - 10 : idx;
+    my_second20 = idx >= 10;
+    my_writer20 = idx >= 0 && (DEPTH || slot != 2);
+    my_off20 = slot < 3 ? slot : slot + 1;
+    my_mul_op20 = slot == 0 ? -half_w : slot == 1 ? -half_h : (slot >= 3 && slot <= 5) ? -0.5f : 0.0f;
+    my_mul_one20 = (slot == 2 || slot >= 6) ? 1.0f : 0.0f;
+  }
   const float fx = (float)pxi;
   const float bx0 = (float)(__shfl_sync(FULL, pxi, 0)), by0 = (float)(__shfl_sync(FULL, py0, 0));
   const float bx1 = bx0 + 7.0f;
@@ -668,68 +733,99 @@ __global__ void __launch_bounds__(BWD_THREADS, 11) render_bwd_tile2_kernel(const
       bool h_top, h_bot;
       cull_halves8(cb + lane, top - lo, s_box, s_xy, s_el, bx0, bx1, by0, h_top, h_bot);
       const unsigned m0 = __ballot_sync(FULL, h_top), m2 = __ballot_sync(FULL, h_bot);
-      const unsigned m1 = m0, m3 = m2;
       unsigned hits = m0 | m2;
-      while (hits) {
-        const int bit = 31 - __clz(hits);
+      // The hit at `bit`: the warp's pairs it reaches run back to front; its ten
+      // gradient terms land in v.  Returns whether any lane contributed.
+      auto eval_hit = [&](int bit, float (&v)[10]) -> bool {
         const int j = cb + bit;
-        hits &= ~(1u << bit);
         const int pos = lo + j;
         // a half the Gaussian cannot reach has alpha < 1/255 at every pixel: no state change to skip
         const bool e0 = ((m0 >> bit) & 1u) && pos < px[0].lc0;
-        const bool e1 = ((m1 >> bit) & 1u) && pos < px[0].lc1;
+        const bool e1 = ((m0 >> bit) & 1u) && pos < px[0].lc1;
         const bool e2 = ((m2 >> bit) & 1u) && pos < px[1].lc0;
-        const bool e3 = ((m3 >> bit) & 1u) && pos < px[1].lc1;
-        BwdSums m = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
-        bool contrib = false;
-        float dx = 0.0f;
+        const bool e3 = ((m2 >> bit) & 1u) && pos < px[1].lc1;
         // which pairs the warp runs (warp-uniform; a lane whose pixels do not
         // take the Gaussian gets zero terms and keeps its state)
         const bool P0 = __any_sync(FULL, e0 || e1), P1 = __any_sync(FULL, e2 || e3);
-        if (P0 || P1) {
-          const float2 xy = s_xy[j];
-          const float4 cf = s_cf[j];
-          const float4 cd = s_rgbd[j];
-          dx = xy.x - fx;
-          float ax, bx;
-          column_terms(cf, dx, ax, bx);
-          bool c0, c1;
-          BwdSums2 m2;
-          if (P0) {
-            const PairTerms t0 = bwd_pair_core<DEPTH, GA>(px[0], e0, e1, cf, ax, bx, xy.y, cd, has_bg, c0, c1);
-            contrib = c0 || c1;
-            sums2_add<DEPTH, true>(m2, t0, px[0]);
-            if (P1) {
-              const PairTerms t1 = bwd_pair_core<DEPTH, GA>(px[1], e2, e3, cf, ax, bx, xy.y, cd, has_bg, c0, c1);
-              contrib = contrib || c0 || c1;
-              sums2_add<DEPTH, false>(m2, t1, px[1]);
-            }
-          } else {
+        if (!(P0 || P1)) return false;
+        const float2 xy = s_xy[j];
+        const float4 cf = s_cf[j];
+        const float4 cd = s_rgbd[j];
+        const float dx = xy.x - fx;
+        float ax, bx;
+        column_terms(cf, dx, ax, bx);
+        bool c0, c1, contrib;
+        BwdSums2 m2;
+        if (P0) {
+          const PairTerms t0 = bwd_pair_core<DEPTH, GA>(px[0], e0, e1, cf, ax, bx, xy.y, cd, has_bg, c0, c1);
+          contrib = c0 || c1;
+          sums2_add<DEPTH, true>(m2, t0, px[0]);
+          if (P1) {
             const PairTerms t1 = bwd_pair_core<DEPTH, GA>(px[1], e2, e3, cf, ax, bx, xy.y, cd, has_bg, c0, c1);
-            contrib = c0 || c1;
-            sums2_add<DEPTH, true>(m2, t1, px[1]);
+            contrib = contrib || c0 || c1;
+            sums2_add<DEPTH, false>(m2, t1, px[1]);
           }
-          sums2_reduce<DEPTH>(m2, m);
+        } else {
+          const PairTerms t1 = bwd_pair_core<DEPTH, GA>(px[1], e2, e3, cf, ax, bx, xy.y, cd, has_bg, c0, c1);
+          contrib = c0 || c1;
+          sums2_add<DEPTH, true>(m2, t1, px[1]);
         }
-        if (__any_sync(FULL, contrib)) {
-          const float4 con = s_con[j];
-          const float dxU = dx * m.U;
-          float v[10];
-          v[0] = con.x * dxU + con.y * m.UY;   // x: times -op W/2
-          v[1] = con.z * m.UY + con.y * dxU;   // y: times -op H/2
-          v[2] = m.ddepth;
-          v[3] = dx * dxU;                     // conic a: times -op/2
-          v[4] = dx * m.UY;                    // conic b: times -op/2
-          v[5] = m.UYY;                        // conic c: times -op/2
-          v[6] = m.U;                          // opacity
-          v[7] = m.dcol0;
-          v[8] = m.dcol1;
-          v[9] = m.dcol2;
+        if (!__any_sync(FULL, contrib)) return false;
+        BwdSums m;
+        sums2_reduce<DEPTH>(m2, m);
+        if (!DEPTH) m.ddepth = 0.0f;
+        const float4 con = s_con[j];
+        const float dxU = dx * m.U;
+        v[0] = con.x * dxU + con.y * m.UY;   // x: times -op W/2
+        v[1] = con.z * m.UY + con.y * dxU;   // y: times -op H/2
+        v[2] = m.ddepth;
+        v[3] = dx * dxU;                     // conic a: times -op/2
+        v[4] = dx * m.UY;                    // conic b: times -op/2
+        v[5] = m.UYY;                        // conic c: times -op/2
+        v[6] = m.U;                          // opacity
+        v[7] = m.dcol0;
+        v[8] = m.dcol1;
+        v[9] = m.dcol2;
+        return true;
+      };
+      // Contributing hits are reduced two at a time (one 20-value transpose
+      // reduction instead of two 10-value ones); an unpaired last one alone.
+      while (hits) {
+        const int bitA = 31 - __clz(hits);
+        hits &= ~(1u << bitA);
+        float vA[10];
+        if (!eval_hit(bitA, vA)) continue;
+        int bitB = -1;
+        float vB[10];
+        while (hits) {
+          const int bit = 31 - __clz(hits);
+          hits &= ~(1u << bit);
+          if (eval_hit(bit, vB)) {
+            bitB = bit;
+            break;
+          }
+        }
+        const int jA = cb + bitA;
+        if (bitB >= 0) {
+          float v20[20];
+#pragma unroll
+          for (int k = 0; k < 10; ++k) {
+            v20[k] = vA[k];
+            v20[10 + k] = vB[k];
+          }
           float sum;
-          warp_reduce10(v, sum);
+          warp_reduce20(v20, sum);
+          if (my_writer20) {
+            const int jj = my_second20 ? cb + bitB : jA;
+            const float scale = fmaf(s_cf[jj].w, my_mul_op20, my_mul_one20);
+            atomicAdd(a.grad_acc + (size_t)s_id[jj] * GSB_GRAD_FLOATS + my_off20, sum * scale);
+          }
+        } else {
+          float sum;
+          warp_reduce10(vA, sum);
           if (my_writer) {
-            const float scale = fmaf(s_cf[j].w, my_mul_op, my_mul_one);
-            atomicAdd(a.grad_acc + (size_t)s_id[j] * GSB_GRAD_FLOATS + my_off, sum * scale);
+            const float scale = fmaf(s_cf[jA].w, my_mul_op, my_mul_one);
+            atomicAdd(a.grad_acc + (size_t)s_id[jA] * GSB_GRAD_FLOATS + my_off, sum * scale);
           }
         }
       }
