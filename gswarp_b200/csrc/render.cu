@@ -919,6 +919,23 @@ __global__ void __launch_bounds__(THREADS, 8) render_bwd_tile4_kernel(const gsb_
     my_mul_op = slot == 0 ? -half_w : slot == 1 ? -half_h : (slot >= 3 && slot <= 5) ? -0.5f : 0.0f;
     my_mul_one = (slot == 2 || slot >= 6) ? 1.0f : 0.0f;
   }
+  // the same for the twenty-value reduction of two hits (values 10..19: the second hit)
+  bool my_writer20, my_second20;
+  int my_off20;
+  float my_mul_op20, my_mul_one20;
+  {
+    float dummy[20];
+#pragma unroll
+    for (int k = 0; k < 20; ++k) dummy[k] = 0.0f;
+    float unused;
+    const int idx = warp_reduce20(dummy, unused);
+    const int slot = idx >= 10 ? idx - 10 : idx;
+    my_second20 = idx >= 10;
+    my_writer20 = idx >= 0 && (DEPTH || slot != 2);
+    my_off20 = slot < 3 ? slot : slot + 1;
+    my_mul_op20 = slot == 0 ? -half_w : slot == 1 ? -half_h : (slot >= 3 && slot <= 5) ? -0.5f : 0.0f;
+    my_mul_one20 = (slot == 2 || slot >= 6) ? 1.0f : 0.0f;
+  }
   const float fx = (float)pxi;
   const float bx0 = (float)(__shfl_sync(FULL, pxi, 0)), by0 = (float)(__shfl_sync(FULL, py0, 0));
   const float bx1 = bx0 + 7.0f;
@@ -957,32 +974,31 @@ __global__ void __launch_bounds__(THREADS, 8) render_bwd_tile4_kernel(const gsb_
       if (__any_sync(FULL, hit) && hit) hit = ellipse_hits(s_xy[g].x, s_xy[g].y, s_el[g], bx0, bx1, by0, by0 + 7.0f);
       const unsigned top_h = __ballot_sync(FULL, hit), bot_h = top_h;
       unsigned hits = top_h;
-      while (hits) {
-      const int bit = 31 - __clz(hits);
-      const int j = cb + bit;
-      hits &= ~(1u << bit);
-      const int pos = lo + j;
-      BwdSums m = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
-      bool contrib = false;
-      float dx = 0.0f;
-      // a half the Gaussian cannot reach has alpha < 1/255 at every pixel: no state change to skip
-      const bool e0 = ((top_h >> bit) & 1u) && pos < px.lc0;
-      const bool e1 = ((bot_h >> bit) & 1u) && pos < px.lc1;
-      if (e0 || e1) {
-        const float2 xy = s_xy[j];
-        const float4 cf = s_cf[j];
-        const float4 cd = s_rgbd[j];
-        dx = xy.x - fx;
-        float ax, bx;
-        column_terms(cf, dx, ax, bx);
-        bool c0, c1;
-        bwd_pair<DEPTH, GA>(px, e0, e1, cf, ax, bx, xy.y, cd, has_bg, m, c0, c1);
-        contrib = c0 || c1;
-      }
-      if (__any_sync(FULL, contrib)) {
+      // The hit at `bit`: this lane's pixels that take it run back to front;
+      // its ten gradient terms land in v.  Returns whether any lane contributed.
+      auto eval_hit = [&](int bit, float (&v)[10]) -> bool {
+        const int j = cb + bit;
+        const int pos = lo + j;
+        BwdSums m = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+        bool contrib = false;
+        float dx = 0.0f;
+        // a half the Gaussian cannot reach has alpha < 1/255 at every pixel: no state change to skip
+        const bool e0 = ((top_h >> bit) & 1u) && pos < px.lc0;
+        const bool e1 = ((bot_h >> bit) & 1u) && pos < px.lc1;
+        if (e0 || e1) {
+          const float2 xy = s_xy[j];
+          const float4 cf = s_cf[j];
+          const float4 cd = s_rgbd[j];
+          dx = xy.x - fx;
+          float ax, bx;
+          column_terms(cf, dx, ax, bx);
+          bool c0, c1;
+          bwd_pair<DEPTH, GA>(px, e0, e1, cf, ax, bx, xy.y, cd, has_bg, m, c0, c1);
+          contrib = c0 || c1;
+        }
+        if (!__any_sync(FULL, contrib)) return false;
         const float4 con = s_con[j];
         const float dxU = dx * m.U;
-        float v[10];
         v[0] = con.x * dxU + con.y * m.UY;   // x: times -op W/2
         v[1] = con.z * m.UY + con.y * dxU;   // y: times -op H/2
         v[2] = m.ddepth;
@@ -993,13 +1009,47 @@ __global__ void __launch_bounds__(THREADS, 8) render_bwd_tile4_kernel(const gsb_
         v[7] = m.dcol0;
         v[8] = m.dcol1;
         v[9] = m.dcol2;
-        float sum;
-        warp_reduce10(v, sum);
-        if (my_writer) {
-          const float scale = fmaf(s_cf[j].w, my_mul_op, my_mul_one);
-          atomicAdd(a.grad_acc + (size_t)s_id[j] * GSB_GRAD_FLOATS + my_off, sum * scale);
+        return true;
+      };
+      // contributing hits are reduced two at a time, an unpaired last one alone
+      while (hits) {
+        const int bitA = 31 - __clz(hits);
+        hits &= ~(1u << bitA);
+        float vA[10];
+        if (!eval_hit(bitA, vA)) continue;
+        int bitB = -1;
+        float vB[10];
+        while (hits) {
+          const int bit = 31 - __clz(hits);
+          hits &= ~(1u << bit);
+          if (eval_hit(bit, vB)) {
+            bitB = bit;
+            break;
+          }
         }
-      }
+        const int jA = cb + bitA;
+        if (bitB >= 0) {
+          float v20[20];
+#pragma unroll
+          for (int k = 0; k < 10; ++k) {
+            v20[k] = vA[k];
+            v20[10 + k] = vB[k];
+          }
+          float sum;
+          warp_reduce20(v20, sum);
+          if (my_writer20) {
+            const int jj = my_second20 ? cb + bitB : jA;
+            const float scale = fmaf(s_cf[jj].w, my_mul_op20, my_mul_one20);
+            atomicAdd(a.grad_acc + (size_t)s_id[jj] * GSB_GRAD_FLOATS + my_off20, sum * scale);
+          }
+        } else {
+          float sum;
+          warp_reduce10(vA, sum);
+          if (my_writer) {
+            const float scale = fmaf(s_cf[jA].w, my_mul_op, my_mul_one);
+            atomicAdd(a.grad_acc + (size_t)s_id[jA] * GSB_GRAD_FLOATS + my_off, sum * scale);
+          }
+        }
       }
     }
   }
