@@ -364,37 +364,49 @@ __device__ __forceinline__ int warp_reduce10(const float (&v)[10], float& out) {
 
 // One halving stage of a transpose reduction: lanes whose `bit` is clear keep
 // the first ceil(N/2) values and send the rest (zero-padded), lanes whose bit
-// is set keep the rest and send the first, to the lane `xmask` apart.
+// is set keep the rest and send the first, to the lane `xmask` apart.  The
+// adds run two outputs per packed f32x2 add (per component the scalar sum).
 template <int N>
 __device__ __forceinline__ void halve(const float (&in)[N], float (&out)[(N + 1) / 2], bool bit, int xmask) {
   constexpr int H = (N + 1) / 2;
+  float keep[H], recv[H];
 #pragma unroll
   for (int k = 0; k < H; ++k) {
     const float lo = in[k];
     const float hi = (k + H < N) ? in[k + H] : 0.0f;
-    const float send = bit ? lo : hi;
-    const float keep = bit ? hi : lo;
-    out[k] = keep + __shfl_xor_sync(FULL, send, xmask);
+    keep[k] = bit ? hi : lo;
+    recv[k] = __shfl_xor_sync(FULL, bit ? lo : hi, xmask);
   }
+#pragma unroll
+  for (int k = 0; k + 1 < H; k += 2) {
+    const float2 sum = __fadd2_rn(make_float2(keep[k], keep[k + 1]), make_float2(recv[k], recv[k + 1]));
+    out[k] = sum.x;
+    out[k + 1] = sum.y;
+  }
+  if (H & 1) out[H - 1] = keep[H - 1] + recv[H - 1];
 }
 
-// Transpose reduction of twenty per-lane values over a warp (21 shuffles,
-// against 24 for two ten-value reductions): on return each of the values'
-// warp totals sits in one lane; the returned index is the value held
-// (0..19), or -1 for the twelve lanes left with padding.
-__device__ __forceinline__ int warp_reduce20(const float (&v)[20], float& out) {
+// Transpose reduction of N (17..32) per-lane values over a warp in five
+// halving stages (N + 2 shuffles or fewer; two ten-value reductions take 24):
+// on return each value's warp total sits in one lane; the returned index is
+// the value held (0..N-1), or -1 for the lanes left with padding.
+template <int N>
+__device__ __forceinline__ int warp_reduce_n(const float (&v)[N], float& out) {
+  static_assert(N > 16 && N <= 32, "five halving stages");
+  constexpr int N1 = (N + 1) / 2, N2 = (N1 + 1) / 2, N3 = (N2 + 1) / 2, N4 = (N3 + 1) / 2;
+  static_assert(N4 == 2, "five halving stages end in one value");
   const int lane = threadIdx.x & 31;
-  float a[10], b[5], c[3], d[2], e[1];
-  halve<20>(v, a, lane & 16, 16);
-  halve<10>(a, b, lane & 8, 8);
-  halve<5>(b, c, lane & 4, 4);
-  halve<3>(c, d, lane & 2, 2);
-  halve<2>(d, e, lane & 1, 1);
+  float a[N1], b[N2], c[N3], d[N4], e[1];
+  halve<N>(v, a, lane & 16, 16);
+  halve<N1>(a, b, lane & 8, 8);
+  halve<N2>(b, c, lane & 4, 4);
+  halve<N3>(c, d, lane & 2, 2);
+  halve<N4>(d, e, lane & 1, 1);
   out = e[0];
   // the original index of the kept value: each stage halves the slots and
   // keeps the upper half (offset ceil(slots/2)) where the lane's bit is set;
   // real values fill the lowest slots, so n counts those still held
-  int idx = 0, n = 20, slots = 20;
+  int idx = 0, n = N, slots = N;
   const int bits[5] = {lane & 16, lane & 8, lane & 4, lane & 2, lane & 1};
 #pragma unroll
   for (int st = 0; st < 5; ++st) {
@@ -409,6 +421,11 @@ __device__ __forceinline__ int warp_reduce20(const float (&v)[20], float& out) {
   }
   return n >= 1 ? idx : -1;
 }
+
+// Gradient terms per hit in the paired reduction: all ten, or without the
+// depth term (index 2) when no depth gradient is asked for.
+template <bool DEPTH>
+__device__ __forceinline__ int pair_term_slot(int t) { return (DEPTH || t < 2) ? t : t + 1; }
 
 // Back-to-front state of the thread's two pixels (backward_kernels.py:
 // 606-625), one f32x2 component per pixel.  The colour part of accum_rec
@@ -686,19 +703,21 @@ __global__ void __launch_bounds__(BWD_THREADS, 11) render_bwd_tile2_kernel(const
     my_mul_op = slot == 0 ? -half_w : slot == 1 ? -half_h : (slot >= 3 && slot <= 5) ? -0.5f : 0.0f;
     my_mul_one = (slot == 2 || slot >= 6) ? 1.0f : 0.0f;
   }
-  // the same for the twenty-value reduction of two hits (values 10..19: the second hit)
+  // the same for the paired reduction of two hits (the first hit's terms,
+  // then the second's)
+  constexpr int PT = DEPTH ? 10 : 9;
   bool my_writer20, my_second20;
   int my_off20;
   float my_mul_op20, my_mul_one20;
   {
-    float dummy[20];
+    float dummy[2 * PT];
 #pragma unroll
-    for (int k = 0; k < 20; ++k) dummy[k] = 0.0f;
+    for (int k = 0; k < 2 * PT; ++k) dummy[k] = 0.0f;
     float unused;
-    const int idx = warp_reduce20(dummy, unused);
-    const int slot = idx >= 10 ? idx - 10 : idx;
-    my_second20 = idx >= 10;
-    my_writer20 = idx >= 0 && (DEPTH || slot != 2);
+    const int idx = warp_reduce_n<2 * PT>(dummy, unused);
+    my_second20 = idx >= PT;
+    const int slot = pair_term_slot<DEPTH>(my_second20 ? idx - PT : idx);
+    my_writer20 = idx >= 0;
     my_off20 = slot < 3 ? slot : slot + 1;
     my_mul_op20 = slot == 0 ? -half_w : slot == 1 ? -half_h : (slot >= 3 && slot <= 5) ? -0.5f : 0.0f;
     my_mul_one20 = (slot == 2 || slot >= 6) ? 1.0f : 0.0f;
@@ -807,14 +826,14 @@ __global__ void __launch_bounds__(BWD_THREADS, 11) render_bwd_tile2_kernel(const
         }
         const int jA = cb + bitA;
         if (bitB >= 0) {
-          float v20[20];
+          float v2[2 * PT];
 #pragma unroll
-          for (int k = 0; k < 10; ++k) {
-            v20[k] = vA[k];
-            v20[10 + k] = vB[k];
+          for (int k = 0; k < PT; ++k) {
+            v2[k] = vA[pair_term_slot<DEPTH>(k)];
+            v2[PT + k] = vB[pair_term_slot<DEPTH>(k)];
           }
           float sum;
-          warp_reduce20(v20, sum);
+          warp_reduce_n<2 * PT>(v2, sum);
           if (my_writer20) {
             const int jj = my_second20 ? cb + bitB : jA;
             const float scale = fmaf(s_cf[jj].w, my_mul_op20, my_mul_one20);
@@ -919,19 +938,21 @@ __global__ void __launch_bounds__(THREADS, 8) render_bwd_tile4_kernel(const gsb_
     my_mul_op = slot == 0 ? -half_w : slot == 1 ? -half_h : (slot >= 3 && slot <= 5) ? -0.5f : 0.0f;
     my_mul_one = (slot == 2 || slot >= 6) ? 1.0f : 0.0f;
   }
-  // the same for the twenty-value reduction of two hits (values 10..19: the second hit)
+  // the same for the paired reduction of two hits (the first hit's terms,
+  // then the second's)
+  constexpr int PT = DEPTH ? 10 : 9;
   bool my_writer20, my_second20;
   int my_off20;
   float my_mul_op20, my_mul_one20;
   {
-    float dummy[20];
+    float dummy[2 * PT];
 #pragma unroll
-    for (int k = 0; k < 20; ++k) dummy[k] = 0.0f;
+    for (int k = 0; k < 2 * PT; ++k) dummy[k] = 0.0f;
     float unused;
-    const int idx = warp_reduce20(dummy, unused);
-    const int slot = idx >= 10 ? idx - 10 : idx;
-    my_second20 = idx >= 10;
-    my_writer20 = idx >= 0 && (DEPTH || slot != 2);
+    const int idx = warp_reduce_n<2 * PT>(dummy, unused);
+    my_second20 = idx >= PT;
+    const int slot = pair_term_slot<DEPTH>(my_second20 ? idx - PT : idx);
+    my_writer20 = idx >= 0;
     my_off20 = slot < 3 ? slot : slot + 1;
     my_mul_op20 = slot == 0 ? -half_w : slot == 1 ? -half_h : (slot >= 3 && slot <= 5) ? -0.5f : 0.0f;
     my_mul_one20 = (slot == 2 || slot >= 6) ? 1.0f : 0.0f;
@@ -1029,14 +1050,14 @@ __global__ void __launch_bounds__(THREADS, 8) render_bwd_tile4_kernel(const gsb_
         }
         const int jA = cb + bitA;
         if (bitB >= 0) {
-          float v20[20];
+          float v2[2 * PT];
 #pragma unroll
-          for (int k = 0; k < 10; ++k) {
-            v20[k] = vA[k];
-            v20[10 + k] = vB[k];
+          for (int k = 0; k < PT; ++k) {
+            v2[k] = vA[pair_term_slot<DEPTH>(k)];
+            v2[PT + k] = vB[pair_term_slot<DEPTH>(k)];
           }
           float sum;
-          warp_reduce20(v20, sum);
+          warp_reduce_n<2 * PT>(v2, sum);
           if (my_writer20) {
             const int jj = my_second20 ? cb + bitB : jA;
             const float scale = fmaf(s_cf[jj].w, my_mul_op20, my_mul_one20);
