@@ -526,21 +526,37 @@ MEASURED_TRAFFIC = {
 }
 
 
-# Algorithmic work per stage and view (fixed formulas; fp32/int32 = 4 B): N Gaussians, R tile-Gaussian
-# pairs, E pixel-Gaussian pairs up to each pixel's last contributor, T tiles, P_px pixels, M = 3 * P_px
-# SSIM elements.  Bytes are the minimum each stage must move through HBM; render FLOP per pair are the
-# reference's per-pair arithmetic (28 forward, 70 backward) with one ex2 each; SSIM 336 FLOP per element.
-def stage_work(stage: str, N: int, R: int, E: int, T: int, P_px: int) -> dict:
+# Algorithmic work per stage and view (fixed formulas; fp32/int32 = 4 B): N Gaussians, V of them binned (with
+# tiles), R tile-Gaussian pairs, E pixel-Gaussian pairs up to each pixel's last contributor, T tiles, P_px
+# pixels, M = 3 * P_px SSIM elements, `views` views per step.  Bytes are the minimum each stage must move
+# through HBM; render FLOP per pair are the reference's per-pair arithmetic (28 forward, 70 backward) with one
+# ex2 each; SSIM 336 FLOP per element.
+# The fused multi-view step (fused=True): preprocess reads mean + opacity of every Gaussian and writes its
+# radius, depth and tile count (28 B); a binned Gaussian also reads scale, rotation and its SH colour (40 B)
+# and writes its render and binning records (80 B); the step's SH colour pass reads each SH row and mean once
+# (204 B per step) and writes a colour per view (12 B).  Preprocess backward, per binned Gaussian: id, radius,
+# mean, scale, rotation and clamp bits in (48 B), the render-gradient accumulator read and cleared (96 B), the
+# 11 gradient floats of the flat buffer and the view's 3 colour-gradient floats read and written (112 B); the
+# step's SH backward reads each SH row, mean and the views' colour gradients and writes the SH gradient and
+# the means gradient (420 B per step over its views, plus 24 B per view for the colour gradients).
+# The per-view autograd path (fused=False) evaluates SH and writes dense gradients for every Gaussian.
+def stage_work(stage: str, N: int, R: int, E: int, T: int, P_px: int, V: int | None = None, views: int = 1,
+               fused: bool = True) -> dict:
     M = 3 * P_px
+    V = N if V is None else V
+    if fused:
+        pre_fwd = 28 * N + 120 * V + (204.0 / views + 12) * N
+        pre_bwd = 260 * V + (420.0 / views + 24) * N
+    else:
+        pre_fwd, pre_bwd = 316 * N, 528 * N
     return {
-        # means, scales, rotations, opacity, SH rows in; radii, proj, conic, conic_inv, render payload, tiles out
-        "preprocess_fwd": {"bytes": 316 * N},
+        "preprocess_fwd": {"bytes": pre_fwd},
         # scan (8N) + emit (12R) + sort lower bound (24R) + point list (8R) + ranges (8T)
         "binning": {"bytes": 8 * N + 44 * R + 8 * T},
         "render_fwd": {"bytes": 44 * R + 24 * P_px, "flop": 28 * E, "ex2": E},
         "ssim_l1": {"bytes": 20 * M, "flop": 336 * M},
-        "render_bwd": {"bytes": 44 * R + 28 * P_px + 40 * N, "flop": 70 * E, "ex2": E},
-        "preprocess_bwd": {"bytes": 528 * N},
+        "render_bwd": {"bytes": 44 * R + 28 * P_px + 40 * V, "flop": 70 * E, "ex2": E},
+        "preprocess_bwd": {"bytes": pre_bwd},
     }[stage]
 
 
@@ -569,7 +585,7 @@ def roofline(prof, peaks, compute, pixels, N, tiles, workload_is_default=False):
     stage = {"bin_count": "binning", "bin_emit_sort": "binning", "loss_fwd": "ssim_l1",
              "loss_bwd": "ssim_l1"}.get(name, name)
     try:
-        work = stage_work(stage, V if stage == "render_bwd" else N, R, E, tiles, pixels)
+        work = stage_work(stage, N, R, E, tiles, pixels, V=V)
     except KeyError:
         return {"kernel": name, "mean_launch_ms": rec["mean_ms"], "note": "no algorithmic model for this stage"}
     t_bound, bound = bound_time(work, peaks, compute)
@@ -597,7 +613,7 @@ def roofline(prof, peaks, compute, pixels, N, tiles, workload_is_default=False):
     return out
 
 
-def step_roofline(prof, peaks, compute, N, pixels, tiles, views, ms_per_step, world, ar_gbs=770.0):
+def step_roofline(prof, peaks, compute, N, pixels, tiles, views, ms_per_step, world, ar_gbs=770.0, fused=True):
     """Per-view roofline of the whole step: the sum over its stages of
     max(bytes / HBM, FLOP / FP32, ex2 / MUFU) (stage_work, with each view's
     measured R and E), plus at N > 1 the all-reduce's per-GPU ring traffic
@@ -615,7 +631,7 @@ def step_roofline(prof, peaks, compute, N, pixels, tiles, views, ms_per_step, wo
         V = rb[k].get("binned", N)
         t = 0.0
         for st in ("preprocess_fwd", "binning", "render_fwd", "ssim_l1", "render_bwd", "preprocess_bwd"):
-            tt, b = bound_time(stage_work(st, V if st == "render_bwd" else N, R, E, tiles, pixels), peaks, compute)
+            tt, b = bound_time(stage_work(st, N, R, E, tiles, pixels, V=V, views=views, fused=fused), peaks, compute)
             stages.setdefault(st, []).append((tt, b))
             t += tt
         per_view.append(t)
@@ -909,7 +925,8 @@ def run_ours(args):
     pixels = args.width * args.height
     tiles = ((args.width + 15) // 16) * ((args.height + 15) // 16)
     rl = roofline(prof, peaks, compute, pixels, scene.n, tiles, workload_is_default=default)
-    step_rl = step_roofline(prof, peaks, compute, scene.n, pixels, tiles, V, ms / args.steps, world)
+    step_rl = step_roofline(prof, peaks, compute, scene.n, pixels, tiles, V, ms / args.steps, world,
+                            fused=args.path == "fused")
 
     extra = {}
     if world > 1:

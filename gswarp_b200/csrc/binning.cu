@@ -410,11 +410,9 @@ __global__ void single_range_kernel(const unsigned* __restrict__ keys, int R, in
   }
 }
 
-inline int tile_sort_passes(int tiles) {
-  if (tiles <= 1) return 0;
-  int bits = 32 - __builtin_clz((unsigned)(tiles - 1));
-  return (bits + radix::RADIX_BITS - 1) / radix::RADIX_BITS;
-}
+// Significant bits of a tile id (0 for a single tile) and the sort passes they take.
+inline int tile_key_bits(int tiles) { return tiles <= 1 ? 0 : 32 - __builtin_clz((unsigned)(tiles - 1)); }
+inline int tile_sort_passes(int tiles) { return radix::passes_for_bits(tile_key_bits(tiles)); }
 
 }  // namespace
 }  // namespace gsb
@@ -481,7 +479,7 @@ GSB_EXPORT int gsb_bin_count(const gsb_bin_count_args* a, void* stream) {
   // 2. stable sort of the V (depth bits, index) pairs.
   unsigned* kb[2] = {keys, keys_alt};
   unsigned* vb[2] = {vals0, vals_alt};
-  const int where = radix::sort_pairs(kb, vb, P, n_vis, 4, sort_scratch, err, s);
+  const int where = radix::sort_pairs(kb, vb, P, n_vis, 32, sort_scratch, err, s);
   if (where != 0) {  // 4 passes always end in buffer 0; kept for safety
     cudaMemcpyAsync(a->depth_order, vals_alt, (size_t)P * 4, cudaMemcpyDeviceToDevice, s);
   }
@@ -563,6 +561,6 @@ GSB_EXPORT int gsb_bin_emit_sort(const gsb_bin_sort_args* a, void* stream) {
     if (vb[0] != pl) cudaMemcpyAsync(pl, vb[0], (size_t)R * 4, cudaMemcpyDeviceToDevice, s);
     single_range_kernel<<<1, 32, 0, s>>>(kb[0], (int)R, tiles, a->ranges);
   } else
-    radix::sort_pairs(kb, vb, R, nullptr, passes, sort_scratch, a->error_word, s, a->ranges, tiles);
+    radix::sort_pairs(kb, vb, R, nullptr, tile_key_bits(tiles), sort_scratch, a->error_word, s, a->ranges, tiles);
   return check_launch("gsb_bin_emit_sort");
 }

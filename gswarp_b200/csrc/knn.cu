@@ -497,7 +497,7 @@ GSB_EXPORT int gsb_knn(const gsb_knn_args* a, void* stream) {
   morton_kernel<<<div_up(P, KT), KT, 0, s>>>(P, a->points, bounds, codes, idx);
   unsigned* kb[2] = {codes, codes_alt};
   unsigned* vb[2] = {idx, idx_alt};
-  const int where = radix::sort_pairs(kb, vb, P, nullptr, 4, scratch, a->error_word, s);
+  const int where = radix::sort_pairs(kb, vb, P, nullptr, 30, scratch, a->error_word, s);  // 30-bit Morton codes
   const unsigned* order = vb[where];
   gather_leaf_kernel<<<div_up((long long)nl * LEAF, KT), KT, 0, s>>>(P, a->points, order, sx, sy, sz, leaf_b);
   reduce_boxes_kernel<<<div_up((long long)np * 32, KT), KT, 0, s>>>(nl, leaf_b, par_b);

@@ -420,6 +420,33 @@ __device__ __forceinline__ void cov_scale_rot_grads(const float* vf, float x, fl
 // registers of its own SH path.
 enum ShMode { SHM_NONE = 0, SHM_ANY = 1, SHM_16 = 2 };
 
+__device__ __forceinline__ void prefetch_line(const void* p) {
+  asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
+}
+
+// Accumulate mode: the thread's memory is requested as soon as its id is
+// known.  Its inputs would otherwise wait for the radius load, and the old
+// gradient values for the whole computation (they are read just before the
+// stores), each a further round trip to DRAM; prefetched lines turn those
+// later loads into cache hits without holding registers across the
+// computation.  The 48-byte accumulator can straddle two 128-byte lines.
+__device__ __forceinline__ void prefetch_rows(const gsb_preprocess_bwd_args& a, int gid) {
+  const size_t g = (size_t)gid;
+  prefetch_line(a.means + g * 3);
+  prefetch_line(a.grad_acc + g * 12);
+  prefetch_line(a.grad_acc + g * 12 + 11);
+  if (a.scales) prefetch_line(a.scales + g * 3);
+  if (a.rotations) prefetch_line(a.rotations + g * 4);
+  prefetch_line(a.grad_means3d + g * 3);
+  if (a.grad_scales) prefetch_line(a.grad_scales + g * 3);
+  if (a.grad_rotations) prefetch_line(a.grad_rotations + g * 4);
+  if (a.grad_opacity) prefetch_line(a.grad_opacity + g);
+  if (a.grad_colors) {
+    prefetch_line(a.grad_colors + g * 3);
+    if (a.grad_colors_clamped) prefetch_line(a.records + g * 12 + 7);
+  }
+}
+
 template <bool PRECOMP, int SHM>
 __global__ void __launch_bounds__(SHM == SHM_16 ? PB_SH16_THREADS : PB_THREADS, SHM == SHM_16 ? 6 : (SHM == SHM_NONE ? 3 : 1))
     preprocess_bwd_kernel(const gsb_preprocess_bwd_args a) {
@@ -439,6 +466,7 @@ __global__ void __launch_bounds__(SHM == SHM_16 ? PB_SH16_THREADS : PB_THREADS, 
   // otherwise thread t handles Gaussian t.
   const bool live = a.ids ? tid < a.num_ids : tid < a.P;
   const int gid = a.ids ? (live ? a.ids[tid] : 0) : tid;
+  if (!SH16 && acc && live) prefetch_rows(a, gid);
   const int rad = live ? a.radii[gid] : 0;
   const bool work = live && (!acc || rad > 0);
   if (!SH16 && !work) return;

@@ -7,10 +7,14 @@
 //      pass in a single read of the keys (warp-aggregated shared atomics);
 //   2. a tiny kernel turns them into per-pass bin bases;
 //   3. each pass is ONE kernel: a CTA claims the next 3840-key tile through
-//      an atomic counter, ranks its keys stably per warp (per-bit ballots),
-//      publishes its per-digit counts, resolves its global offsets by
-//      decoupled look-back over the preceding tiles, stages the tile in
-//      digit order in shared memory and writes it out in runs.
+//      an atomic counter, ranks its keys stably per warp (one ballot per
+//      digit bit), publishes its per-digit counts, resolves its global
+//      offsets by decoupled look-back over the preceding tiles, stages the
+//      tile in digit order in shared memory and writes it out in runs.
+// The caller states how many low key bits are significant: every pass takes
+// 8 of them except the last, which takes what is left (a 13-bit tile id
+// sorts in an 8-bit and a 5-bit pass), and the last pass writes only the
+// values (and the key ranges) -- no caller reads the sorted keys.
 // Tiles are claimed in launch order, so every tile a CTA waits on belongs to
 // a CTA that is already running; each look-back spin is nevertheless bounded
 // (SPIN_LIMIT) and reports ERR_LOOKBACK_TIMEOUT instead of hanging.
@@ -48,13 +52,13 @@ __device__ __forceinline__ void st_volatile(unsigned long long* p, unsigned long
   asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
-// Lanes of the warp whose 9-bit value d (an 8-bit digit, or RADIX for "no
-// key") equals this lane's: nine ballots, one per bit (cheaper on sm_100a
-// than a match.any over 32 distinct values).
+// Lanes of the warp whose BITS-bit digit d equals this lane's: one ballot
+// per bit (cheaper on sm_100a than a match.any over 32 distinct values).
+template <int BITS>
 __device__ __forceinline__ unsigned digit_peers(unsigned d) {
   unsigned peers = 0xffffffffu;
 #pragma unroll
-  for (int b = 0; b <= RADIX_BITS; ++b) {
+  for (int b = 0; b < BITS; ++b) {
     const bool bit = (d >> b) & 1u;
     const unsigned m = __ballot_sync(0xffffffffu, bit);
     peers &= bit ? m : ~m;
@@ -93,7 +97,8 @@ __device__ __forceinline__ unsigned block_exclusive_scan(unsigned v, unsigned* s
 // loaded before any is counted.
 __global__ void __launch_bounds__(THREADS) histogram_kernel(const unsigned* __restrict__ keys,
                                                             int n_host, const int* __restrict__ n_dev,
-                                                            int passes, unsigned* __restrict__ hist) {
+                                                            int passes, unsigned last_mask,
+                                                            unsigned* __restrict__ hist) {
   const int n = n_dev ? *n_dev : n_host;
   __shared__ unsigned s_hist[WARPS][MAX_PASSES][RADIX];
   for (int i = threadIdx.x; i < WARPS * MAX_PASSES * RADIX; i += THREADS) (&s_hist[0][0][0])[i] = 0u;
@@ -112,7 +117,8 @@ __global__ void __launch_bounds__(THREADS) histogram_kernel(const unsigned* __re
     for (int it = 0; it < HIST_ITEMS; ++it) {
       if (base + it * 32 + lane < n) {
         for (int p = 0; p < passes; ++p)
-          atomicAdd(&s_hist[warp][p][(kv[it] >> (p * RADIX_BITS)) & (RADIX - 1)], 1u);
+          atomicAdd(&s_hist[warp][p][(kv[it] >> (p * RADIX_BITS)) & (p == passes - 1 ? last_mask : RADIX - 1)],
+                    1u);
       }
     }
   }
@@ -133,7 +139,9 @@ __global__ void __launch_bounds__(THREADS) bin_base_kernel(const unsigned* __res
   bin_base[p * RADIX + threadIdx.x] = block_exclusive_scan(c, s_warp, nullptr);
 }
 
-template <bool HAS_VALS>
+// One pass over the digit of BITS bits at `shift`.  keys_out may be null
+// (the last pass: only values and ranges are wanted).
+template <int BITS>
 __global__ void __launch_bounds__(THREADS, 4) onesweep_kernel(
     const unsigned* __restrict__ keys_in, const unsigned* __restrict__ vals_in,
     unsigned* __restrict__ keys_out, unsigned* __restrict__ vals_out, int n_host,
@@ -142,13 +150,15 @@ __global__ void __launch_bounds__(THREADS, 4) onesweep_kernel(
     unsigned* __restrict__ tile_counter, long long* __restrict__ err, int* __restrict__ ranges,
     int range_keys) {
   __shared__ unsigned s_keys[TILE_KEYS];
-  __shared__ unsigned s_vals[HAS_VALS ? TILE_KEYS : 1];
+  __shared__ unsigned s_vals[TILE_KEYS];
   __shared__ unsigned s_warp_hist[WARPS][RADIX];
   __shared__ unsigned s_digit_start[RADIX];
   __shared__ unsigned s_global[RADIX];
   __shared__ unsigned s_scan[WARPS];
   __shared__ int s_tile;
 
+  constexpr unsigned MASK = (1u << BITS) - 1u;
+  constexpr int NB = 1 << BITS;  // digits in use; threads tid >= NB own none
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   // With a device-side count the grid is sized for the upper bound; CTAs
   // that claim a tile past the end leave (no later tile waits on them).
@@ -160,13 +170,17 @@ __global__ void __launch_bounds__(THREADS, 4) onesweep_kernel(
   if ((long long)tile * TILE_KEYS >= n) return;
   const long long base = (long long)tile * TILE_KEYS + (long long)warp * (ITEMS * 32);
 
+  // Positions past n (only in the last tile) hold the key 0xFFFFFFFF, whose
+  // digit is the largest, and are ranked like the others: a warp's missing
+  // positions follow all of its valid ones and only later warps have more,
+  // so they stage after every valid key of the tile, at [tile_n, TILE_KEYS),
+  // where nothing reads them.  Their counts enter the last tile's published
+  // totals, which no tile reads (tiles look back only at earlier ones).
   unsigned key[ITEMS], rank[ITEMS];
 #pragma unroll
   for (int i = 0; i < ITEMS; ++i) {
     const long long pos = base + i * 32 + lane;
-    const bool valid = pos < n;
-    key[i] = valid ? keys_in[pos] : 0xFFFFFFFFu;
-    rank[i] = valid ? 0u : 0xFFFFFFFFu;  // invalid marker
+    key[i] = pos < n ? keys_in[pos] : 0xFFFFFFFFu;
   }
   // Stable warp-local ranking: round i holds 32 consecutive keys.  The
   // lowest lane of each digit group adds the group's size to the warp's
@@ -176,14 +190,13 @@ __global__ void __launch_bounds__(THREADS, 4) onesweep_kernel(
   const unsigned lt = lanemask_lt();
 #pragma unroll
   for (int i = 0; i < ITEMS; ++i) {
-    const bool valid = rank[i] != 0xFFFFFFFFu;
-    const unsigned d = valid ? (key[i] >> shift) & (RADIX - 1) : (unsigned)RADIX;
-    const unsigned peers = digit_peers(d);
+    const unsigned d = (key[i] >> shift) & MASK;
+    const unsigned peers = digit_peers<BITS>(d);
     const int leader = __ffs(peers) - 1;
     unsigned old = 0;
-    if (valid && lane == leader) old = atomicAdd(&s_warp_hist[warp][d], (unsigned)__popc(peers));
+    if (lane == leader) old = atomicAdd(&s_warp_hist[warp][d], (unsigned)__popc(peers));
     old = __shfl_sync(0xffffffffu, old, leader);
-    if (valid) rank[i] = old + __popc(peers & lt);
+    rank[i] = old + __popc(peers & lt);
   }
   __syncthreads();
 
@@ -196,7 +209,7 @@ __global__ void __launch_bounds__(THREADS, 4) onesweep_kernel(
     total += c;
   }
   unsigned long long* my_slot = lookback + (size_t)tile * RADIX + tid;
-  st_volatile(my_slot, (tile == 0 ? FLAG_INC : FLAG_AGG) | (unsigned long long)total);
+  if (tid < NB) st_volatile(my_slot, (tile == 0 ? FLAG_INC : FLAG_AGG) | (unsigned long long)total);
   s_digit_start[tid] = block_exclusive_scan(total, s_scan, nullptr);
   __syncthreads();
 
@@ -204,22 +217,19 @@ __global__ void __launch_bounds__(THREADS, 4) onesweep_kernel(
   // registers are free while it waits); values are read here, not earlier.
 #pragma unroll
   for (int i = 0; i < ITEMS; ++i) {
-    if (rank[i] != 0xFFFFFFFFu) {
-      const unsigned d = (key[i] >> shift) & (RADIX - 1);
-      rank[i] += s_digit_start[d] + s_warp_hist[warp][d];
-      s_keys[rank[i]] = key[i];
-    }
+    const unsigned d = (key[i] >> shift) & MASK;
+    rank[i] += s_digit_start[d] + s_warp_hist[warp][d];
+    s_keys[rank[i]] = key[i];
   }
-  if (HAS_VALS) {
+  {
     unsigned val[ITEMS];
 #pragma unroll
     for (int i = 0; i < ITEMS; ++i) {
       const long long pos = base + i * 32 + lane;
-      val[i] = rank[i] != 0xFFFFFFFFu ? vals_in[pos] : 0u;
+      val[i] = pos < n ? vals_in[pos] : 0u;
     }
 #pragma unroll
-    for (int i = 0; i < ITEMS; ++i)
-      if (rank[i] != 0xFFFFFFFFu) s_vals[rank[i]] = val[i];
+    for (int i = 0; i < ITEMS; ++i) s_vals[rank[i]] = val[i];
   }
 
   // Decoupled look-back over a window of LOOKBACK_WINDOW predecessors at a
@@ -228,7 +238,7 @@ __global__ void __launch_bounds__(THREADS, 4) onesweep_kernel(
   // adding aggregates until an inclusive prefix is found.  A slot that is not
   // published yet is re-read (bounded) before the walk moves past it.
   unsigned long long excl = 0;
-  if (tile > 0) {
+  if (tile > 0 && tid < NB) {
     int t = tile - 1;
     int spins = 0;
     bool done = false;
@@ -265,13 +275,13 @@ __global__ void __launch_bounds__(THREADS, 4) onesweep_kernel(
   const int tile_n = (int)min((long long)TILE_KEYS, (long long)n - tile_base);
   for (int j = tid; j < tile_n; j += THREADS) {
     const unsigned k = s_keys[j];
-    const unsigned d = (k >> shift) & (RADIX - 1);
+    const unsigned d = (k >> shift) & MASK;
     const unsigned dst = s_global[d] + (unsigned)j - s_digit_start[d];
     // dst < n whenever the histogram and look-back agree; the test keeps a
     // timed-out look-back (flagged above) from writing out of bounds.
     if (dst < (unsigned)n) {
-      keys_out[dst] = k;
-      if (HAS_VALS) vals_out[dst] = s_vals[j];
+      if (keys_out) keys_out[dst] = k;
+      vals_out[dst] = s_vals[j];
       if (ranges) {
         // Last pass: the staged tile is sorted by the whole key, so a key
         // whose neighbour in the tile differs is the tile's first / last
@@ -335,36 +345,60 @@ __host__ inline SortScratch carve_scratch(void* base, long long n, int passes) {
   return s;
 }
 
-// Sorts n pairs by the low `passes*8` key bits.  Buffers ping-pong:
-// pass 0 reads (k[0],v[0]) and writes (k[1],v[1]), pass 1 the reverse, ...
-// Returns the index (0/1) of the buffer pair that holds the result.
-// vals may be null (keys only).  With n_dev non-null the count is read on
+// Passes needed for keys of `key_bits` significant low bits.
+__host__ inline int passes_for_bits(int key_bits) { return (key_bits + RADIX_BITS - 1) / RADIX_BITS; }
+
+template <int BITS>
+__host__ inline void launch_pass(int tiles, cudaStream_t stream, const unsigned* ki, const unsigned* vi,
+                                 unsigned* ko, unsigned* vo, int n, const int* n_dev, int shift,
+                                 const unsigned* base, unsigned long long* lb, unsigned* counter, long long* err,
+                                 int* rg, int range_keys) {
+  onesweep_kernel<BITS><<<tiles, THREADS, 0, stream>>>(ki, vi, ko, vo, n, n_dev, shift, base, lb, counter, err, rg,
+                                                       range_keys);
+}
+
+// Sorts n pairs by the low `key_bits` (1..32) key bits (higher bits are
+// ignored).  Buffers ping-pong: pass 0 reads (k[0],v[0]) and writes
+// (k[1],v[1]), pass 1 the reverse, ...  Returns the index (0/1) of the
+// buffer pair that holds the sorted values; the last pass does not write
+// keys, so the sorted keys are not kept.  With n_dev non-null the count is read on
 // the device (at most n, which sizes the grids and the scratch).
 // With `ranges` (and n_dev null) the last pass also writes, for every key
 // value below range_keys, its [start, end) in the sorted output into the
 // zero-initialised int2 array `ranges` ((0, 0) for absent keys).
-__host__ inline int sort_pairs(unsigned* k[2], unsigned* v[2], long long n, const int* n_dev, int passes,
+__host__ inline int sort_pairs(unsigned* k[2], unsigned* v[2], long long n, const int* n_dev, int key_bits,
                                void* scratch, long long* err, cudaStream_t stream, int* ranges = nullptr,
                                int range_keys = 0) {
+  const int passes = passes_for_bits(key_bits);
   if ((n <= 1 && !n_dev) || n <= 0 || passes == 0) return 0;
+  const int last_bits = key_bits - RADIX_BITS * (passes - 1);
   SortScratch s = carve_scratch(scratch, n, passes);
   cudaMemsetAsync(s.hist, 0, s.zero_bytes, stream);
   const int hist_blocks = (int)std::min<long long>(148 * 4, (n + THREADS * 8 - 1) / (THREADS * 8));
-  histogram_kernel<<<std::max(hist_blocks, 1), THREADS, 0, stream>>>(k[0], (int)n, n_dev, passes, s.hist);
+  histogram_kernel<<<std::max(hist_blocks, 1), THREADS, 0, stream>>>(k[0], (int)n, n_dev, passes,
+                                                                      (1u << last_bits) - 1u, s.hist);
   bin_base_kernel<<<passes, THREADS, 0, stream>>>(s.hist, s.bin_base);
   const int tiles = num_tiles(n);
   int cur = 0;
   for (int p = 0; p < passes; ++p) {
     unsigned long long* lb = s.lookback + (size_t)p * tiles * RADIX;
-    int* rg = (p == passes - 1 && !n_dev) ? ranges : nullptr;
-    if (v[0]) {
-      onesweep_kernel<true><<<tiles, THREADS, 0, stream>>>(
-          k[cur], v[cur], k[cur ^ 1], v[cur ^ 1], (int)n, n_dev, p * RADIX_BITS, s.bin_base + p * RADIX,
-          lb, s.counters + p, err, rg, range_keys);
-    } else {
-      onesweep_kernel<false><<<tiles, THREADS, 0, stream>>>(
-          k[cur], nullptr, k[cur ^ 1], nullptr, (int)n, n_dev, p * RADIX_BITS, s.bin_base + p * RADIX,
-          lb, s.counters + p, err, rg, range_keys);
+    const bool last = p == passes - 1;
+    int* rg = (last && !n_dev) ? ranges : nullptr;
+    unsigned* ko = last ? nullptr : k[cur ^ 1];
+    const unsigned* vi = v[cur];
+    unsigned* vo = v[cur ^ 1];
+    const int bits = last ? last_bits : RADIX_BITS;
+    const unsigned* base = s.bin_base + p * RADIX;
+    const int sh = p * RADIX_BITS;
+    switch (bits) {
+      case 1: launch_pass<1>(tiles, stream, k[cur], vi, ko, vo, (int)n, n_dev, sh, base, lb, s.counters + p, err, rg, range_keys); break;
+      case 2: launch_pass<2>(tiles, stream, k[cur], vi, ko, vo, (int)n, n_dev, sh, base, lb, s.counters + p, err, rg, range_keys); break;
+      case 3: launch_pass<3>(tiles, stream, k[cur], vi, ko, vo, (int)n, n_dev, sh, base, lb, s.counters + p, err, rg, range_keys); break;
+      case 4: launch_pass<4>(tiles, stream, k[cur], vi, ko, vo, (int)n, n_dev, sh, base, lb, s.counters + p, err, rg, range_keys); break;
+      case 5: launch_pass<5>(tiles, stream, k[cur], vi, ko, vo, (int)n, n_dev, sh, base, lb, s.counters + p, err, rg, range_keys); break;
+      case 6: launch_pass<6>(tiles, stream, k[cur], vi, ko, vo, (int)n, n_dev, sh, base, lb, s.counters + p, err, rg, range_keys); break;
+      case 7: launch_pass<7>(tiles, stream, k[cur], vi, ko, vo, (int)n, n_dev, sh, base, lb, s.counters + p, err, rg, range_keys); break;
+      default: launch_pass<8>(tiles, stream, k[cur], vi, ko, vo, (int)n, n_dev, sh, base, lb, s.counters + p, err, rg, range_keys); break;
     }
     cur ^= 1;
   }

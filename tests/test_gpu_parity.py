@@ -137,6 +137,23 @@ def test_preprocess_and_binning_bit_exact(cuda, name, mode):
         np.testing.assert_array_equal(_np(binned.ranges), ref_ranges)
 
 
+@pytest.mark.parametrize("width", [16, 32, 48, 80, 176, 272, 528, 1040, 2064])
+def test_tile_sort_every_last_digit_width(cuda, width):
+    """Tile grids of 2 to 258 tiles: the tile sort's last pass takes 1 to 8
+    key bits (258 tiles: an 8-bit pass and a 1-bit pass); the point list and
+    the ranges stay bit-exact."""
+    scene, _ = wl.config1_scene(seed=7, n=4000)
+    view = wl.look_at_view([0.0, 0.0, -2.5], [0.0, 0.0, 0.0], [0.0, -1.0, 0.0], 70.0, width, 32)
+    ref = _oracle_pre(scene, view)
+    _, cam, pre = _gpu_pre(scene, view, cuda)
+    ref_pl, ref_ranges, _ = oracle.binning(ref, view.width, view.height, 1)
+    binned = pl.binning(pre, cam, 1)
+    torch.cuda.synchronize()
+    assert binned.num_rendered == len(ref_pl) > 0
+    np.testing.assert_array_equal(_np(binned.point_list), ref_pl)
+    np.testing.assert_array_equal(_np(binned.ranges), ref_ranges)
+
+
 def test_sparse_preprocess_matches_dense(cuda):
     """The training step's sparse preprocess gives the same radii, counts,
     depths, binning records and (where radius > 0) render records."""
