@@ -58,6 +58,25 @@ class GradientBuffer:
         self.flat.zero_()
         self.attach()
 
+    def detach(self) -> None:
+        """Unset every parameter's ``.grad``: the next backward stores its
+        gradients as fresh tensors instead of adding them into the buffer."""
+        for p in self.params:
+            p.grad = None
+
+    def take(self) -> None:
+        """After one backward since :meth:`detach`: copy each parameter's
+        ``.grad`` into its block (zero for a parameter that received none) and
+        attach the blocks again.  The buffer then holds that backward's
+        gradients -- one copy, where zeroing the buffer and accumulating into
+        it reads and writes it twice more."""
+        for p, v in zip(self.params, self.views):
+            if p.grad is None:
+                v.zero_()
+            elif p.grad.data_ptr() != v.data_ptr():
+                v.copy_(p.grad)
+        self.attach()
+
     def all_reduce(self, group=None) -> None:
         if torch.distributed.is_available() and torch.distributed.is_initialized():
             if torch.distributed.get_world_size(group) > 1:
@@ -90,11 +109,21 @@ class ViewShardedStep:
         self.group = group
 
     def step(self) -> StepResult:
-        self.grads.zero_()
         losses = []
-        for i in self.view_indices:
+        if not self.view_indices:
+            self.grads.zero_()
+        for n, i in enumerate(self.view_indices):
             loss = self.view_fn(i)
-            loss.backward()
+            if n == 0:
+                # the first view's gradients are copied into the buffer rather
+                # than added to a zero-filled one
+                self.grads.detach()
+                try:
+                    loss.backward()
+                finally:
+                    self.grads.take()
+            else:
+                loss.backward()
             losses.append(loss.detach())
         self.grads.all_reduce(self.group)
         return StepResult(losses=losses, views=len(self.view_indices))

@@ -88,6 +88,30 @@ def test_gradient_buffer_accumulates_in_place():
     torch.testing.assert_close(step.grads.flat, expect, rtol=1e-5, atol=1e-5)
 
 
+def test_first_view_without_a_gradient_leaves_a_zero_block():
+    """The first view's gradients are copied into the buffer: a parameter the
+    first view does not use gets a zero block (no stale values from the
+    previous step), and later views add into the attached blocks."""
+    params = _params()
+
+    def loss(v):
+        full = _view_loss(params, v)
+        return full if v > 0 else (params[0] * 2.0).sum()
+
+    step = ViewShardedStep(params, range(3), loss)
+    step.grads.flat.fill_(7.0)  # stale contents must not survive the step
+    step.step()
+    expect = []
+    for k in range(5):
+        e = sum(_view_weights(v)[k] for v in (1, 2)).reshape(-1) + 2 * 0.02 * params[k].detach().reshape(-1)
+        if k == 0:
+            e = e + 2.0
+        expect.append(e)
+    torch.testing.assert_close(step.grads.flat, torch.cat(expect), rtol=1e-5, atol=1e-5)
+    for p, v in zip(params, step.grads.views):
+        assert p.grad.data_ptr() == v.data_ptr()
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
