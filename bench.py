@@ -61,6 +61,8 @@ def parse():
                    help="the measured path: the fused training step, or the drop-in autograd path alone")
     p.add_argument("--backward-order", default="views", choices=["views", "ranges"],
                    help="fused step: per-view backward (default) or the range-ordered backward")
+    p.add_argument("--deferred-views", type=int, default=None,
+                   help="fused step: the last K views finish range by range (default: the library's)")
     return p.parse_args()
 
 
@@ -896,6 +898,8 @@ def run_ours(args):
     tr = Trainer(scene, views, targets_dev, targets_host, world, device, path=args.path)
     if args.path == "fused":
         tr.fused.range_backward = args.backward_order == "ranges"
+        if args.deferred_views is not None:
+            tr.fused.deferred_views = args.deferred_views
 
     # device-resident timing with clock sampling
     sampler = ClockSampler(local)
@@ -918,6 +922,8 @@ def run_ours(args):
         autograd_api = measure_autograd(args, scene, views, targets_dev, targets_host, world, device, views_total)
 
     tr_ranged = args.path == "fused" and tr.fused.batch_sh and bool(tr.fused.range_backward)
+    tr_deferred = (V if tr_ranged else min(V, int(tr.fused.deferred_views))) \
+        if args.path == "fused" and tr.fused.batch_sh else 0
     prof = kernel_profile(tr, steps=1)
     launches = sum(v["kernels"] for v in prof.values())
     default = (args.gaussians, args.width, args.height) == (6_000_000, 1920, 1080)
@@ -962,6 +968,7 @@ def run_ours(args):
                      "backward accumulating into the flat gradient buffer)" if args.path == "fused" else
                      "GaussianRasterizer + fused_ssim under autograd, ViewShardedStep"),
             "backward_order": (("ranges" if tr_ranged else "views") if args.path == "fused" else None),
+            "deferred_views": tr_deferred,
             "autograd_api": autograd_api,
             "gpu_launches": launches * args.steps,
             "roofline": rl,

@@ -203,6 +203,11 @@ class FusedViewStep:
         # backward overlaps the next view's forward on the other stream, which the range order gives up,
         # and on 2 GPUs the exchange it overlaps did not pay for that (25.5 ms per step either way)
         self.range_backward = False
+        # a partial range order (multi-view SH only): the first V - deferred_views views run view by
+        # view, the last deferred_views stop after their render backward and finish range by range as
+        # above (range_backward set = every view deferred); the additions into the flat buffer keep
+        # view order either way, so every setting gives the same bits
+        self.deferred_views = 0
         # view-by-view order with a process group: 0 = SH backward, then one all-reduce of the buffer;
         # n > 0 = the blocks complete after the last view are all-reduced while the SH backward runs in
         # n Gaussian ranges, each range's SH rows while the next is computed, the means last
@@ -367,9 +372,10 @@ class FusedViewStep:
         and binning.  Each view finishes its own backward, the accumulations
         into the flat gradient buffer in view order (each waits for the
         previous one), then the multi-view SH backward and the all-reduce
-        run; or, range-ordered (``range_backward``), every view stops after its render backward
-        (each into its own accumulator) and the preprocess and SH backward of
-        all views run afterwards on this stream, Gaussian range by Gaussian
+        run; or, range-ordered (``range_backward``, or the last
+        ``deferred_views`` views), those views stop after their render
+        backward (each into its own accumulator) and their preprocess and the
+        SH backward run afterwards on this stream, Gaussian range by Gaussian
         range, each range all-reduced while the next is computed."""
         if len(targets) != len(self.settings):
             raise ValueError(f"expected {len(self.settings)} targets, got {len(targets)}")
@@ -388,24 +394,36 @@ class FusedViewStep:
             else:
                 self.grads.zero_()
             P, V = means.shape[0], len(targets)
-            ranged = self.batch_sh and bool(self.range_backward)
-            if ranged and (self._view_grad_acc is None or self._view_grad_acc.shape[:2] != (V, P)):
-                self._view_grad_acc = torch.zeros((V, P, _lib.GRAD_FLOATS), dtype=torch.float32, device=self.device)
+            deferred = 0
+            if self.batch_sh:
+                deferred = V if self.range_backward else max(0, min(V, int(self.deferred_views)))
+            ranged = deferred > 0
+            if ranged and (self._view_grad_acc is None or self._view_grad_acc.shape[:2] != (deferred, P)):
+                self._view_grad_acc = torch.zeros((deferred, P, _lib.GRAD_FLOATS), dtype=torch.float32,
+                                                  device=self.device)
             self._upload_targets(targets, main)
             ready = torch.cuda.Event()
             ready.record(main)
             for side in streams[1:]:
                 side.wait_event(ready)  # zeroed buffers, targets and parameters visible to every stream
             if ranged:
-                states = []
-                for i, t in enumerate(targets):
+                first = V - deferred
+                prev = None
+                for i in range(first):
                     s = streams[i % n_streams]
                     with torch.cuda.stream(s):
-                        st = self.view_render_grads(i, t, self._view_grad_acc[i])
+                        self.view(i, targets[i], before_accumulate=prev, lane=i % n_streams)
+                        prev = torch.cuda.Event()
+                        prev.record(s)
+                states = []
+                for i in range(first, V):
+                    s = streams[i % n_streams]
+                    with torch.cuda.stream(s):
+                        st = self.view_render_grads(i, targets[i], self._view_grad_acc[i - first])
                         if s is not main:
                             for buf in (st.radii, st.records, st.ids):
                                 buf.record_stream(main)
-                        states.append(st)
+                        states.append((i, st))
                 for side in streams[1:]:
                     done = torch.cuda.Event()
                     done.record(side)
@@ -458,9 +476,11 @@ class FusedViewStep:
 
     def _ranged_backward(self, states: list) -> None:
         """The second half of a multi-view step, on the current stream, one
-        Gaussian range after another: every view's preprocess backward over
-        its binned ids inside the range (accumulated into the flat buffer in
-        view order, as view by view), then the SH backward of the range
+        Gaussian range after another: every deferred view's (``states``:
+        (view index, state) pairs, in view order, after the views that ran
+        view by view) preprocess backward over its binned ids inside the range
+        (accumulated into the flat buffer in view order, as view by view),
+        then the SH backward of the range
         (stores the SH rows, adds the view-direction term to the means).
         With a process group each finished range is all-reduced on NCCL's
         stream while the next range is computed; the sums are elementwise,
@@ -475,14 +495,14 @@ class FusedViewStep:
         if not ranges:
             return
         bounds = torch.tensor([b for b, _ in ranges] + [P], dtype=torch.int32, device=self.device)
-        splits = torch.stack([torch.searchsorted(st.ids, bounds) for st in states]).tolist()
+        splits = torch.stack([torch.searchsorted(st.ids, bounds) for _, st in states]).tolist()
         if self.densify_stats:
-            for st in states:
+            for _, st in states:
                 _lib.call("gsb_densify_stats", P, _lib.ptr(st.radii), _lib.ptr(self.denom),
                           _lib.ptr(self.max_radii2D), _lib.stream_handle(self.device))
         # one argument block per view; per range only the id slice changes
         args = []
-        for v, st in enumerate(states):
+        for v, st in states:
             out = pl.PreprocessGrads(grad_means3D=v_means, grad_means2D=None, grad_opacity=v_opac,
                                      grad_scales=v_scales, grad_rotations=v_rots, grad_cov3D=None, grad_sh=None,
                                      grad_colors=self._grad_colors[v])
@@ -495,11 +515,11 @@ class FusedViewStep:
         dist = _distributed(self.group)
         works = []
         for r, (b, e) in enumerate(ranges):
-            for v, st in enumerate(states):
-                lo, hi = splits[v][r], splits[v][r + 1]
+            for k, (_, st) in enumerate(states):
+                lo, hi = splits[k][r], splits[k][r + 1]
                 if hi <= lo:
                     continue
-                a = args[v]
+                a = args[k]
                 a.ids = st.ids.data_ptr() + 4 * lo
                 a.num_ids = hi - lo
                 with pl._stage_timer("preprocess_bwd", {"P": P, "kernels": 1, "accumulate": True,

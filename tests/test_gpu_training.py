@@ -124,15 +124,20 @@ def test_fused_step_matches_autograd_step(cuda, n, views, W, H, batch_sh):
     assert float((fused.grads.flat - got).norm()) <= 1e-4 * float(got.norm()) + 1e-7
 
 
+@pytest.mark.parametrize("deferred", ["all", 1])
 @pytest.mark.parametrize("n,views,W,H", [(20_000, 3, 320, 192), (200_000, 2, 960, 544)])
-def test_range_ordered_step_matches_autograd_step(cuda, n, views, W, H):
-    """The range-ordered multi-view step (the default with a process group),
-    forced on one GPU, against the autograd path; its per-view
-    accumulators are left zero and a second step does not double."""
+def test_range_ordered_step_matches_autograd_step(cuda, n, views, W, H, deferred):
+    """The range-ordered multi-view step -- every view deferred, or only the
+    last one (the earlier views run view by view) -- on one GPU, against the
+    autograd path; its per-view accumulators are left zero and a second step
+    does not double."""
     params, settings, targets = _scene(cuda, n, views, W, H)
     ref_flat, ref_losses = _autograd_step(params, settings, targets, 1.0, 0.2)
     fused = FusedViewStep([p.clone() for p in params], settings, 1.0, 0.2)
-    fused.range_backward = True
+    if deferred == "all":
+        fused.range_backward = True
+    else:
+        fused.deferred_views = deferred
     fused.backward_chunks = 3
     losses = fused.step(targets)
     torch.cuda.synchronize()
@@ -173,7 +178,7 @@ def test_range_ordered_backward_is_independent_of_the_ranges(cuda, chunks):
         step.grads.flat.fill_(0.0)
         step.reset_densify_stats()
         step.backward_chunks = n
-        step._ranged_backward(states)
+        step._ranged_backward(list(enumerate(states)))
         torch.cuda.synchronize()
         results.append([t.clone() for t in (step.grads.flat, step.xyz_gradient_accum, step.denom,
                                             step.max_radii2D)])
