@@ -110,6 +110,8 @@ constexpr int SH_ROW_F4 = 13;  // staged SH row: 48 floats padded to 52
 // registers of its own colour path.
 enum ShMode { SHM_NONE = 0, SHM_ANY = 1, SHM_16 = 2 };
 
+__device__ __forceinline__ void prefetch_l1(const void* p) { asm volatile("prefetch.global.L1 [%0];" ::"l"(p)); }
+
 template <int SHM>
 __global__ void __launch_bounds__(SHM == SHM_16 ? PF_SH16_THREADS : PF_THREADS, SHM == SHM_16 ? 8 : 1)
     preprocess_fwd_kernel(const gsb_preprocess_args a) {
@@ -127,6 +129,14 @@ __global__ void __launch_bounds__(SHM == SHM_16 ? PF_SH16_THREADS : PF_THREADS, 
   const bool live = idx < a.P;
   if (!SH16 && !live) return;
   const int li = live ? idx : 0;  // in-bounds index for the loads of lanes past P
+  // The scale / rotation loads wait for the near-plane test and the colour
+  // load for the whole projection and coverage count: their lines are
+  // requested now, together with the mean's.
+  if (live) {
+    if (a.scales) prefetch_l1(a.scales + (size_t)idx * 3);
+    if (a.rotations) prefetch_l1(a.rotations + (size_t)idx * 4);
+    if (a.colors_precomp) prefetch_l1(a.colors_precomp + (size_t)idx * 3);
+  }
   const float* v = s_view;
   const float* pr = s_proj;
   const int gx = (a.W + BLOCK_X - 1) / BLOCK_X;

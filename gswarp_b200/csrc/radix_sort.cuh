@@ -269,14 +269,15 @@ __global__ void __launch_bounds__(THREADS, 4) onesweep_kernel(
     }
     st_volatile(my_slot, FLAG_INC | (excl + total));
   }
-  s_global[tid] = bin_base[tid] + (unsigned)excl;
+  // staged position j of digit d goes to s_global[d] + j (unsigned wrap-around)
+  s_global[tid] = bin_base[tid] + (unsigned)excl - s_digit_start[tid];
   __syncthreads();
   const long long tile_base = (long long)tile * TILE_KEYS;
   const int tile_n = (int)min((long long)TILE_KEYS, (long long)n - tile_base);
   for (int j = tid; j < tile_n; j += THREADS) {
     const unsigned k = s_keys[j];
     const unsigned d = (k >> shift) & MASK;
-    const unsigned dst = s_global[d] + (unsigned)j - s_digit_start[d];
+    const unsigned dst = s_global[d] + (unsigned)j;
     // dst < n whenever the histogram and look-back agree; the test keeps a
     // timed-out look-back (flagged above) from writing out of bounds.
     if (dst < (unsigned)n) {
