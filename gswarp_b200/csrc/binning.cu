@@ -316,11 +316,13 @@ __global__ void __launch_bounds__(EMIT_THREADS, 8) emit_binrec_kernel(
   int n = 0, point = 0, start = 0;
   unsigned w[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
   if (r < nv) {
+    // the id is read with the offsets (not after them): one round trip less
+    // before the record load
+    point = order[r];
     const int end = offsets[r];
     n = end - (r > 0 ? offsets[r - 1] : 0);
     start = end - n;
     if (n > 0) {
-      point = order[r];
       const uint4 a = __ldg(bin_records + (size_t)point * 2), b = __ldg(bin_records + (size_t)point * 2 + 1);
       w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
       w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
