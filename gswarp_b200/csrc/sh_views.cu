@@ -122,6 +122,21 @@ __global__ void __launch_bounds__(SHV_THREADS, 4) sh_backward_views_kernel(const
   float* rows = s_rows + warp * SHV_ROW_F * 32;
   const size_t plane = (size_t)a.P * 3;
   float(*sg)[96] = s_g[warp];
+  // The SH rows are loaded only after the colour gradients are staged, and
+  // the means gradient is read back at the end: their lines are requested
+  // now (the warp's rows are one contiguous span).
+  {
+    const float* span = a.sh + (size_t)base * RF;
+    const int nf = rows_here * RF;
+    // one address per 128 bytes and the span's last float (a misaligned
+    // start leaves a partial line at the end); all inside the span
+    for (int l = lane; l * 32 < nf; l += 32) asm volatile("prefetch.global.L2 [%0];" ::"l"(span + (size_t)l * 32));
+    if (lane == 31) asm volatile("prefetch.global.L2 [%0];" ::"l"(span + (nf - 1)));
+    if (live) {
+      asm volatile("prefetch.global.L1 [%0];" ::"l"(a.means + (size_t)idx * 3));
+      asm volatile("prefetch.global.L1 [%0];" ::"l"(a.grad_means3d + (size_t)idx * 3));
+    }
+  }
 
   // One chunk of views' colour gradients into shared memory.  Every load is
   // issued before any reset store: the compiler cannot tell the views' planes
