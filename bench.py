@@ -520,11 +520,11 @@ def cpu_baseline_sample(args, views_timed: int = 2) -> dict:
 # workload (6M Gaussians, 1920x1080, first view of the training step), from a 1-pass ncu capture of
 # `python bench.py --steps 1 --warmup 1 --no-e2e --no-autograd --no-cfg2 --no-cpu-baseline --no-optimizer`.
 MEASURED_TRAFFIC = {
-    "render_bwd": 262.64e6 + 31.48e6,
-    "render_fwd": 163.58e6 + 31.18e6,
-    "preprocess_bwd": 1136.76e6 + 450.03e6,
-    "preprocess_fwd": 379.93e6 + 336.40e6,
-    "sh_colors": 1224.03e6 + 544.70e6,
+    "render_bwd": 262.87e6 + 33.48e6,
+    "render_fwd": 163.27e6 + 31.64e6,
+    "preprocess_bwd": 1140.62e6 + 451.03e6,
+    "preprocess_fwd": 380.36e6 + 331.54e6,
+    "sh_colors": 1224.03e6 + 544.67e6,
 }
 
 
