@@ -136,6 +136,11 @@ __global__ void __launch_bounds__(SHM == SHM_16 ? PF_SH16_THREADS : PF_THREADS, 
     if (a.scales) prefetch_l1(a.scales + (size_t)idx * 3);
     if (a.rotations) prefetch_l1(a.rotations + (size_t)idx * 4);
     if (a.colors_precomp) prefetch_l1(a.colors_precomp + (size_t)idx * 3);
+    // the warp stages SH rows only after the projection tells which survive
+    if (SH16 && a.sh && !a.colors_precomp) {
+      prefetch_l1(a.sh + (size_t)idx * 48);
+      prefetch_l1(a.sh + (size_t)idx * 48 + 47);
+    }
   }
   const float* v = s_view;
   const float* pr = s_proj;

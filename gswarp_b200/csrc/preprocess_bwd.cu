@@ -424,6 +424,18 @@ __device__ __forceinline__ void prefetch_line(const void* p) {
   asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
 }
 
+// Store mode (the autograd path, every Gaussian): the inputs are requested
+// with the radius instead of after it.
+__device__ __forceinline__ void prefetch_inputs(const gsb_preprocess_bwd_args& a, int gid) {
+  const size_t g = (size_t)gid;
+  prefetch_line(a.means + g * 3);
+  prefetch_line(a.grad_acc + g * 12);
+  prefetch_line(a.grad_acc + g * 12 + 11);
+  if (a.scales) prefetch_line(a.scales + g * 3);
+  if (a.rotations) prefetch_line(a.rotations + g * 4);
+  prefetch_line(a.records + g * 12 + 7);
+}
+
 // Accumulate mode: the thread's memory is requested as soon as its id is
 // known.  Its inputs would otherwise wait for the radius load, and the old
 // gradient values for the whole computation (they are read just before the
@@ -467,7 +479,13 @@ __global__ void __launch_bounds__(SHM == SHM_16 ? PB_SH16_THREADS : PB_THREADS, 
   const bool live = a.ids ? tid < a.num_ids : tid < a.P;
   const int gid = a.ids ? (live ? a.ids[tid] : 0) : tid;
   if (!SH16 && acc && live) prefetch_rows(a, gid);
+  if (!acc && live) prefetch_inputs(a, gid);
   const int rad = live ? a.radii[gid] : 0;
+  if (SH16 && live && rad > 0) {
+    // the SH row is staged only after the render gradient and clamp bits are read
+    prefetch_line(a.sh + (size_t)gid * 48);
+    prefetch_line(a.sh + (size_t)gid * 48 + 47);
+  }
   const bool work = live && (!acc || rad > 0);
   if (!SH16 && !work) return;
   const float* pr = s_proj;
