@@ -192,6 +192,8 @@ class Trainer:
         else:
             self.means2d = torch.zeros_like(self.means, requires_grad=True)
             self.stage_tgt = [torch.empty_like(t) for t in targets_dev] if targets_host else None
+            self.copy_stream = torch.cuda.Stream(device) if targets_host else None
+            self.tgt_ready = [None] * len(views)
             self.e2e = False
             self.dp = ViewShardedStep(self.params, range(len(views)), self._view_loss)
             self.flat = self.dp.grads.flat
@@ -200,7 +202,7 @@ class Trainer:
         gs = self.gs
         if self.e2e:
             tgt = self.stage_tgt[i]
-            tgt.copy_(self.targets_host[i], non_blocking=True)
+            self.torch.cuda.current_stream(self.device).wait_event(self.tgt_ready[i])
         else:
             tgt = self.targets_dev[i]
         self.means2d.grad = None
@@ -215,6 +217,17 @@ class Trainer:
             losses = self.fused.step(self.targets_host if e2e else self.targets_dev)[:, 0]
         else:
             self.e2e = e2e
+            if e2e:
+                # every view's target is copied from pinned host memory on a copy stream at the start of
+                # the step, each view waiting only for its own copy (the fused path does the same)
+                torch = self.torch
+                self.copy_stream.wait_stream(torch.cuda.current_stream(self.device))
+                with torch.cuda.stream(self.copy_stream):
+                    for i, t in enumerate(self.targets_host):
+                        self.stage_tgt[i].copy_(t, non_blocking=True)
+                        ev = torch.cuda.Event()
+                        ev.record(self.copy_stream)
+                        self.tgt_ready[i] = ev
             losses = self.torch.stack(self.dp.step().losses)
         if e2e:
             self.loss_host.copy_(losses, non_blocking=True)
