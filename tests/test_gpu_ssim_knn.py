@@ -103,6 +103,16 @@ def test_knn_ties_and_sparse_outliers(cuda):
         np.testing.assert_array_equal(got, want)
 
 
+@pytest.mark.parametrize("bad", [float("nan"), float("inf"), -float("inf")])
+def test_knn_rejects_non_finite_points(cuda, bad):
+    """A NaN or an Inf anywhere in the points raises ValueError with the
+    reference's message (knn.py:297-298), before any kernel runs."""
+    pts = wl.config4_points(seed=3, n=5000)
+    pts[4321, 2] = bad
+    with pytest.raises(ValueError, match="NaN or Inf"):
+        gs.distCUDA2(pts.to(cuda))
+
+
 def test_knn_config4_subset(cuda):
     pts = wl.config4_points(seed=0, n=300_000)
     got = gs.distCUDA2(pts.to(cuda)).cpu().numpy()
