@@ -65,7 +65,9 @@ def test_fused_ssim_inference_mode(cuda):
     assert abs(float(l) - ref) <= 2e-6
 
 
-@pytest.mark.parametrize("n", [4, 5, 33, 64, 65, 96, 1023, 1024, 1025, 50_000])
+# 3840 / 7680 / 7681: one and two whole sort tiles of 3,840 keys and one key more (the last tile holding
+# positions past the end)
+@pytest.mark.parametrize("n", [4, 5, 33, 64, 65, 96, 1023, 1024, 1025, 3840, 7680, 7681, 50_000])
 def test_knn_bit_exact(cuda, n):
     pts = wl.config4_points(seed=n, n=max(n, 4))[:n].contiguous()
     got = gs.distCUDA2(pts.to(cuda)).cpu().numpy()
